@@ -1,0 +1,125 @@
+"""ctypes binding of the C ABI in include/asdsl_b200.h (libasdsl_b200.so).
+
+The shared library is built in-tree (``__graft_entry__.build()`` or
+``python -m asdsl_b200.build``) next to this file.  There is no fallback: if the
+library or a CUDA device is missing, every native call raises RuntimeError, as
+the reference does when its native extension is absent
+(asdsl/kernels/gemv_q4.py:373-374).
+
+Status codes map onto the reference's exception classes:
+std::invalid_argument -> ValueError, std::out_of_range -> IndexError,
+anything else -> RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libasdsl_b200.so")
+
+OK, EINVAL, ERANGE, ECUDA, ENCCL, ETIMEOUT, ENOMEM = range(7)
+
+FMT_PREQ2, FMT_PREQ, FMT_Q4_128, FMT_S256 = 0, 1, 2, 3
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+_SZ = ctypes.c_size_t
+
+# name -> argtypes (restype is int unless listed in _RESTYPES)
+_SIGS = {
+    "asdsl_b200_version": [],
+    "asdsl_b200_last_error": [],
+    "asdsl_b200_device_status": [_P, _I],
+    "asdsl_b200_quantize_activation": [_P, _P, _P, _P, _I, _I, _P],
+    "asdsl_b200_gemv_preq2_fused": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_gemv_preq2": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_gemv_q4_32_preq": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_gemv_q4_32_preq_fused": [_P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_gemv_q4_128": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_gemv_q4_128_fused": [_P, _P, _P, _I, _I, _P],
+    "asdsl_b200_gemv_q4_s256": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_gemv_q4km": [_P, _P, _P, _I, _I, _P],
+    "asdsl_b200_gemv_q4_packed": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "asdsl_b200_gemv_q4_unpacked": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_matmul_batch_q4": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "asdsl_b200_argmax_scratch_bytes": [],
+    "asdsl_b200_gemv_argmax": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P],
+    "asdsl_b200_gateup_silu": [_I, _P, _P, _P, _P, _I, _I, _P],
+}
+_RESTYPES = {
+    "asdsl_b200_version": ctypes.c_char_p,
+    "asdsl_b200_last_error": ctypes.c_char_p,
+    "asdsl_b200_argmax_scratch_bytes": _SZ,
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def exported_symbols() -> list[str]:
+    """Every symbol the C ABI header declares (used by the load test)."""
+    return list(_SIGS) + list(EXTRA_SIGS)
+
+
+# entry points registered by other modules (engine, sharding) before load()
+EXTRA_SIGS: dict[str, tuple[list, object]] = {}
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load libasdsl_b200.so once and type every exported symbol."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise RuntimeError(
+                f"asdsl_b200 native library not built ({p} missing); run __graft_entry__.build()"
+            )
+        lib = ctypes.CDLL(p)
+        for name, argtypes in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = _RESTYPES.get(name, _I)
+        for name, (argtypes, restype) in EXTRA_SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().asdsl_b200_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str = "") -> None:
+    """Raise the exception class the reference would raise for this status."""
+    if rc == OK:
+        return
+    msg = last_error() or what
+    if rc == EINVAL:
+        raise ValueError(msg)
+    if rc == ERANGE:
+        raise IndexError(msg)
+    if rc == ETIMEOUT:
+        raise TimeoutError(msg)
+    raise RuntimeError(msg)
+
+
+def call(name: str, *args) -> int:
+    rc = getattr(load(), name)(*args)
+    check(rc, name)
+    return rc
+
+
+def device_status(clear: bool = True) -> int:
+    """Status bits set by kernels whose bounded waits gave up (0 = healthy)."""
+    v = ctypes.c_uint(0)
+    check(load().asdsl_b200_device_status(ctypes.byref(v), 1 if clear else 0))
+    return int(v.value)

@@ -1,0 +1,127 @@
+"""One decoder layer's projection set on the device (the C0.1 byte mix):
+
+    qkv  = W_qkv  x      preq2 gs 32   (unified_engine.cpp:1411-1413)
+    o    = W_o    x      preq2 gs 32   (:1487-1489)
+    h    = silu(W_gate x) * (W_up x)   Q4_128, fused in one kernel (:1532-1538 + :836-857)
+    y    = W_down h      Q4_128        (:1592-1598)
+
+Weights live in HBM for the object's lifetime; ``step`` enqueues the four
+kernels on torch's current stream (capturable in a CUDA graph), ``forward``
+is the host-buffer call a user makes (x in, outputs out, copies included).
+``build_c1_host`` reproduces the reference's C0.1 weight pipeline for the
+benchmark: gs-32 asymmetric quantization with the clip search, then
+dequantize and requantize to Q4_128 for gate_up/down
+(experiments/phi4_cpu_run.py:3482-3517).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from asdsl_b200 import _lib
+from asdsl_b200.quantization import core, repack
+
+FMT_PREQ2, FMT_Q4_128 = 0, 2
+
+
+class LayerProjections:
+    def __init__(self, qkv_meta, qkv_quant, o_meta, o_quant, gate_up_q4_128, down_q4_128, hidden: int,
+                 qkv_rows: int, q_dim: int, inter: int):
+        dev = torch.device("cuda", torch.cuda.current_device())
+
+        def up(a):
+            return a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+        self.qkv_meta, self.qkv_quant = up(qkv_meta), up(qkv_quant)
+        self.o_meta, self.o_quant = up(o_meta), up(o_quant)
+        self.gu, self.dn = up(gate_up_q4_128), up(down_q4_128)
+        self.H, self.QKV, self.QD, self.I = hidden, qkv_rows, q_dim, inter
+        self.qkv_out = torch.empty(qkv_rows, dtype=torch.float32, device=dev)
+        self.o_out = torch.empty(hidden, dtype=torch.float32, device=dev)
+        self.h = torch.empty(inter, dtype=torch.float32, device=dev)
+        self.y = torch.empty(hidden, dtype=torch.float32, device=dev)
+        self._x = torch.empty(hidden, dtype=torch.float32, device=dev)
+        self._pin_x = torch.empty(hidden, dtype=torch.float32, pin_memory=True)
+        n_out = qkv_rows + 2 * hidden
+        self._pin_out = torch.empty(n_out, dtype=torch.float32, pin_memory=True)
+        self._out_cat = torch.empty(n_out, dtype=torch.float32, device=dev)
+
+    @property
+    def weight_bytes(self) -> int:
+        return sum(t.numel() for t in (self.qkv_meta, self.qkv_quant, self.o_meta, self.o_quant, self.gu, self.dn))
+
+    @property
+    def algorithmic_bytes(self) -> int:
+        """Packed weights + fp32 activations in + fp32 results out of each GEMV
+        (the reference's GB/s definition without its A8 overhead term,
+        benchmarks/kernel_bench_compare.py:46-52)."""
+        act = 4 * (self.H + self.QKV) + 4 * (self.QD + self.H) + 4 * (self.H + self.I) + 4 * (self.I + self.H)
+        return self.weight_bytes + act
+
+    def step(self, x: torch.Tensor, stream_ptr=None) -> int:
+        """Enqueue the 4 kernels; returns the number of launches."""
+        s = stream_ptr if stream_ptr is not None else (torch.cuda.current_stream().cuda_stream or None)
+        L = _lib.load()
+        _lib.check(L.asdsl_b200_gemv_preq2_fused(self.qkv_meta.data_ptr(), self.qkv_quant.data_ptr(), x.data_ptr(),
+                                                 self.qkv_out.data_ptr(), self.QKV, self.H, 32, s))
+        _lib.check(L.asdsl_b200_gemv_preq2_fused(self.o_meta.data_ptr(), self.o_quant.data_ptr(), x.data_ptr(),
+                                                 self.o_out.data_ptr(), self.H, self.QD, 32, s))
+        _lib.check(L.asdsl_b200_gateup_silu(FMT_Q4_128, self.gu.data_ptr(), None, x.data_ptr(), self.h.data_ptr(),
+                                            self.I, self.H, s))
+        _lib.check(L.asdsl_b200_gemv_q4_128_fused(self.dn.data_ptr(), self.h.data_ptr(), self.y.data_ptr(), self.H,
+                                                  self.I, s))
+        return 4
+
+    def forward(self, x_host: np.ndarray) -> dict:
+        """Host buffers in and out: pinned H2D of x, the step, one D2H of the results."""
+        self._pin_x.numpy()[:] = x_host
+        self._x.copy_(self._pin_x, non_blocking=True)
+        self.step(self._x)
+        n1, n2 = self.QKV, self.QKV + self.H
+        self._out_cat[:n1].copy_(self.qkv_out)
+        self._out_cat[n1:n2].copy_(self.o_out)
+        self._out_cat[n2:].copy_(self.y)
+        self._pin_out.copy_(self._out_cat, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        o = self._pin_out.numpy()
+        return {"qkv": o[:n1].copy(), "o": o[n1:n2].copy(), "y": o[n2:].copy()}
+
+    def clone(self) -> "LayerProjections":
+        """Same weights at new device addresses (L2-rotation copies for benchmarking)."""
+        return LayerProjections(self.qkv_meta.clone(), self.qkv_quant.clone(), self.o_meta.clone(),
+                                self.o_quant.clone(), self.gu.clone(), self.dn.clone(), self.H, self.QKV, self.QD,
+                                self.I)
+
+
+C1 = dict(hidden=3072, qkv_rows=5120, q_dim=3072, inter=8192)
+
+
+def build_c1_host(seed: int = 1, cfg: dict = C1) -> dict:
+    """Config 1's weights and activation from one seeded generator: W_qkv, W_o, W_gate_up,
+    W_down ~ N(0, 0.02) drawn in that order, then x ~ N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    H, QKV, QD, I = cfg["hidden"], cfg["qkv_rows"], cfg["q_dim"], cfg["inter"]
+    out = {}
+    for name, (rows, cols) in (("qkv", (QKV, H)), ("o", (H, QD))):
+        w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+        qt = core.quantize_weights(w, 4, 32, False, True)
+        sc, bi = core.scales_biases_f32(qt)
+        flat = repack.blocks_to_flat(repack.repack_asymmetric_to_q4_32_blocks(qt.data, sc, bi, rows, cols, 32))
+        out[name + "_meta"], out[name + "_quant"] = repack.repack_preq_blocks_to_preq2(flat, rows, cols)
+    for name, (rows, cols) in (("gate_up", (2 * I, H)), ("down", (H, I))):
+        w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+        qt = core.quantize_weights(w, 4, 32, False, True)
+        sc, bi = core.scales_biases_f32(qt)
+        wdq = core.dequant_packed_projection(qt.data, sc, bi, rows, cols, 32)
+        out[name + "_q4_128"] = repack.repack_fp32_to_q4_128_blocks(wdq, rows, cols)
+    out["x"] = rng.standard_normal(H).astype(np.float32)
+    out["cfg"] = dict(cfg)
+    return out
+
+
+def from_host(host: dict) -> LayerProjections:
+    c = host["cfg"]
+    return LayerProjections(host["qkv_meta"], host["qkv_quant"], host["o_meta"], host["o_quant"],
+                            host["gate_up_q4_128"], host["down_q4_128"], c["hidden"], c["qkv_rows"], c["q_dim"],
+                            c["inter"])

@@ -1,0 +1,362 @@
+// asdsl_b200.cu -- the C ABI of the B200-native ASDSL decode hot path.
+//
+// Single translation unit: the kernel headers are included here so that the
+// library needs no relocatable device code.  Every exported function is
+// declared in include/asdsl_b200.h with the reference interface it replaces.
+#include "../../include/asdsl_b200.h"
+
+#include "launch.cuh"
+
+using namespace asdsl;
+
+namespace {
+
+constexpr int kMaxK = 20480;  // reference thread_local A8 scratch (gemv_preq2_avx2.cpp:315-316)
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------------------
+// standalone A8 (quantize_activation_avx2): one warp per group, any group size
+// ---------------------------------------------------------------------------
+__global__ void k_quantize_activation(const float* __restrict__ x, int8_t* __restrict__ xq, float* __restrict__ xs,
+                                      int32_t* __restrict__ xsum, int K, int gs) {
+    const int wpb = blockDim.x >> 5;
+    const int g = blockIdx.x * wpb + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int ng = K / gs;
+    if (g >= ng) return;
+    const float* xg = x + static_cast<long long>(g) * gs;
+    float amax = 0.0f;
+    for (int j = lane; j < gs; j += 32) amax = fmaxf(amax, fabsf(xg[j]));
+    amax = warp_max(amax);
+    int8_t* q = xq + static_cast<long long>(g) * gs;
+    int s = 0;
+    if (amax < 1e-9f) {
+        for (int j = lane; j < gs; j += 32) q[j] = 0;
+        if (lane == 0) xs[g] = 1.0f;
+    } else {
+        const float inv = __fdiv_rn(127.0f, amax);
+        for (int j = lane; j < gs; j += 32) {
+            const int c = a8_code(xg[j], inv);
+            q[j] = static_cast<int8_t>(c);
+            s += c;
+        }
+        if (lane == 0) xs[g] = __fmul_rn(amax, inv127f());
+    }
+    s = warp_sum_i(s);
+    if (xsum && lane == 0) xsum[g] = s;
+}
+
+// ---------------------------------------------------------------------------
+// unpacked (one code per byte) fp32-activation GEMV: warp per row, lane per group
+// (gemv_q4_avx2.cpp:755-806; a compatibility path, not the decode hot path)
+// ---------------------------------------------------------------------------
+__global__ void k_gemv_unpacked(const uint8_t* __restrict__ w, const float* __restrict__ x,
+                                const float* __restrict__ scales, const float* __restrict__ biases,
+                                float* __restrict__ y, int M, int K, int gs) {
+    const int wpb = blockDim.x >> 5;
+    const int row = blockIdx.x * wpb + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const int ng = K / gs;
+    const uint8_t* wr = w + static_cast<long long>(row) * K;
+    float acc = 0.0f;
+    for (int g = lane; g < ng; g += 32) {
+        float d = 0.0f, sx = 0.0f;
+        for (int j = 0; j < gs; ++j) {
+            const float xv = x[g * gs + j];
+            d = __fmaf_rn(static_cast<float>(wr[g * gs + j]), xv, d);
+            sx = __fadd_rn(sx, xv);
+        }
+        const long long gi = static_cast<long long>(row) * ng + g;
+        acc += __fmaf_rn(d, scales[gi], __fmul_rn(biases[gi], sx));
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[row] = acc;
+}
+
+int check_k(int K, int gs, const char* fn) {
+    if (gs <= 0 || K <= 0) return set_error(kEinval, std::string(fn) + ": invalid dimensions");
+    if (K % gs != 0) return set_error(kEinval, std::string(fn) + ": in_features must be divisible by group_size");
+    if (K > kMaxK) return set_error(kEinval, std::string(fn) + ": n_groups exceeds buffer");
+    return kOk;
+}
+
+// preq2 streams: quant (band units) + meta (4 rows per band)
+inline void preq2_streams(StreamIn* s, const uint8_t* meta, const uint8_t* quant, long long M, long long K) {
+    const long long ng = K / 32;
+    const long long nb = (M + 3) / 4;
+    s[0] = StreamIn{quant, ng * 64, nb * ng * 64};
+    s[1] = StreamIn{meta, ng * 16, M * ng * 4};
+}
+
+GemvArgs base_args(int M, int K, int gs) {
+    GemvArgs ga;
+    std::memset(&ga, 0, sizeof(ga));
+    ga.M = M;
+    ga.K = K;
+    ga.gs = gs;
+    return ga;
+}
+
+}  // namespace
+
+// ===========================================================================
+// exported C ABI
+// ===========================================================================
+extern "C" {
+
+const char* asdsl_b200_version(void) { return "asdsl-b200 0.1 (sm_100a)"; }
+
+const char* asdsl_b200_last_error(void) { return last_error_msg().c_str(); }
+
+int asdsl_b200_device_status(unsigned int* status, int clear) {
+    if (!status) return set_error(kEinval, "asdsl_b200_device_status: null pointer");
+    ASDSL_CUDA(cudaDeviceSynchronize());
+    unsigned int v = 0;
+    ASDSL_CUDA(cudaMemcpyFromSymbol(&v, g_status_word, sizeof(v)));
+    *status = v;
+    if (clear) {
+        const unsigned int z = 0;
+        ASDSL_CUDA(cudaMemcpyToSymbol(g_status_word, &z, sizeof(z)));
+    }
+    return kOk;
+}
+
+int asdsl_b200_quantize_activation(const float* x, int8_t* xq, float* xs, int32_t* xsum, int K, int gs,
+                                   void* stream) {
+    if (!x || !xq || !xs) return set_error(kEinval, "quantize_activation: null pointer");
+    if (gs <= 0 || K < 0) return set_error(kEinval, "quantize_activation: invalid dimensions");
+    const int ng = K / gs;
+    if (ng == 0) return kOk;
+    const int wpb = 8;
+    k_quantize_activation<<<(ng + wpb - 1) / wpb, wpb * 32, 0, as_stream(stream)>>>(x, xq, xs, xsum, K, gs);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_gemv_preq2_fused(const uint8_t* meta, const uint8_t* quant, const float* x, float* y, int M, int K,
+                                int gs, void* stream) {
+    if (!meta || !quant || !x || !y) return set_error(kEinval, "gemv_preq2_fused_avx2: null pointer");
+    if (gs != 32) return set_error(kEinval, "gemv_preq2_fused_avx2: group_size must be 32");
+    if (int rc = check_k(K, gs, "gemv_preq2_fused_avx2")) return rc;
+    if (M < 0) return set_error(kEinval, "gemv_preq2_fused_avx2: invalid dimensions");
+    StreamIn s[2];
+    preq2_streams(s, meta, quant, M, K);
+    GemvArgs ga = base_args(M, K, 32);
+    ga.x = x;
+    ga.y = y;
+    return launch_stream_gemv<kFmtPreq2, kProA8, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_preq2(const uint8_t* meta, const uint8_t* quant, const int8_t* xq, const float* xs, float* y,
+                          int M, int K, int gs, void* stream) {
+    if (!meta || !quant || !xq || !xs || !y) return set_error(kEinval, "gemv_preq2_avx2: null pointer");
+    if (gs != 32) return set_error(kEinval, "gemv_preq2_avx2: group_size must be 32");
+    if (int rc = check_k(K, gs, "gemv_preq2_avx2")) return rc;
+    if (M < 0) return set_error(kEinval, "gemv_preq2_avx2: invalid dimensions");
+    StreamIn s[2];
+    preq2_streams(s, meta, quant, M, K);
+    GemvArgs ga = base_args(M, K, 32);
+    ga.xq = xq;
+    ga.xs_in = xs;
+    ga.y = y;
+    return launch_stream_gemv<kFmtPreq2, kProQ8, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_q4_32_preq(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K,
+                               int gs, void* stream) {
+    if (!blocks || !xq || !xs || !y) return set_error(kEinval, "gemv_q4_32_preq_avx2: null input pointer");
+    if (M <= 0 || K <= 0 || gs <= 0) return set_error(kEinval, "gemv_q4_32_preq_avx2: invalid dimensions");
+    if (K % gs) return set_error(kEinval, "gemv_q4_32_preq_avx2: in_features must be divisible by group_size");
+    if (gs != 32) return set_error(kEinval, "gemv_q4_32_preq_avx2: group_size must be 32");
+    if (K / gs > 640) return set_error(kEinval, "gemv_q4_32_preq_avx2: n_groups exceeds buffer");
+    const long long ng = K / 32;
+    StreamIn s[1] = {{blocks, ng * 20, static_cast<long long>(M) * ng * 20}};
+    GemvArgs ga = base_args(M, K, 32);
+    ga.xq = xq;
+    ga.xs_in = xs;
+    ga.y = y;
+    return launch_stream_gemv<kFmtPreq, kProQ8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_q4_32_preq_fused(const uint8_t* blocks, const float* x, float* y, int M, int K, int gs,
+                                     void* stream) {
+    if (!blocks || !x || !y) return set_error(kEinval, "gemv_q4_32_preq_fused_avx2: null input pointer");
+    if (gs != 32) return set_error(kEinval, "gemv_q4_32_preq_fused_avx2: group_size must be 32");
+    if (M <= 0 || K <= 0) return set_error(kEinval, "gemv_q4_32_preq_fused_avx2: invalid dimensions");
+    if (int rc = check_k(K, gs, "gemv_q4_32_preq_fused_avx2")) return rc;
+    const long long ng = K / 32;
+    StreamIn s[1] = {{blocks, ng * 20, static_cast<long long>(M) * ng * 20}};
+    GemvArgs ga = base_args(M, K, 32);
+    ga.x = x;
+    ga.y = y;
+    return launch_stream_gemv<kFmtPreq, kProA8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_q4_128(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K, int gs,
+                           void* stream) {
+    if (!blocks || !xq || !xs || !y) return set_error(kEinval, "gemv_q4_128_preq_avx2: null pointer");
+    if (gs != 128) return set_error(kEinval, "gemv_q4_128_preq_avx2: group_size must be 128");
+    if (K <= 0 || K % 128) return set_error(kEinval, "gemv_q4_128_preq_avx2: in_features must be divisible by 128");
+    if (K > 17920) return set_error(kEinval, "gemv_q4_128_preq_avx2: in_features exceeds 17920");
+    if (M < 0) return set_error(kEinval, "gemv_q4_128_preq_avx2: invalid dimensions");
+    const long long ng = K / 128;
+    StreamIn s[1] = {{blocks, ng * 66, static_cast<long long>(M) * ng * 66}};
+    GemvArgs ga = base_args(M, K, 128);
+    ga.xq = xq;
+    ga.xs_in = xs;
+    ga.y = y;
+    return launch_stream_gemv<kFmtQ4_128, kProQ8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_q4_128_fused(const uint8_t* blocks, const float* x, float* y, int M, int K, void* stream) {
+    if (!blocks || !x || !y) return set_error(kEinval, "gemv_q4_128_fused: null pointer");
+    if (K <= 0 || K % 128) return set_error(kEinval, "gemv_q4_128_fused: in_features must be divisible by 128");
+    if (K > 17920) return set_error(kEinval, "gemv_q4_128_fused: in_features exceeds 17920");
+    if (M < 0) return set_error(kEinval, "gemv_q4_128_fused: invalid dimensions");
+    const long long ng = K / 128;
+    StreamIn s[1] = {{blocks, ng * 66, static_cast<long long>(M) * ng * 66}};
+    GemvArgs ga = base_args(M, K, 128);
+    ga.x = x;
+    ga.y = y;
+    return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_q4_s256(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K, int gs,
+                            void* stream) {
+    if (!blocks || !xq || !xs || !y) return set_error(kEinval, "gemv_q4_s256: null pointer");
+    if (gs != 32) return set_error(kEinval, "gemv_q4_s256: group_size must be 32");
+    if (K <= 0 || K % 256) return set_error(kEinval, "gemv_q4_s256: in_features must be divisible by 256");
+    if (K > 17920) return set_error(kEinval, "gemv_q4_s256: in_features exceeds 17920");
+    if (M < 0) return set_error(kEinval, "gemv_q4_s256: invalid dimensions");
+    const long long nsb = K / 256;
+    StreamIn s[1] = {{blocks, nsb * 144, static_cast<long long>(M) * nsb * 144}};
+    GemvArgs ga = base_args(M, K, 32);
+    ga.xq = xq;
+    ga.xs_in = xs;
+    ga.y = y;
+    return launch_stream_gemv<kFmtS256, kProQ8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_q4km(const uint8_t* w, const float* x, float* y, int M, int K, void* stream) {
+    if (K <= 0 || M <= 0) return kOk;  // the reference returns without work (gemv_q4_avx2.cpp:364-366)
+    if (!w || !x || !y) return set_error(kEinval, "gemv_q4km_q8_avx2: null pointer");
+    if (K % 256) return set_error(kEinval, "in_features must be divisible by 256 for Q4_K_M");
+    if (K > kMaxK) return set_error(kEinval, "gemv_q4km_q8_avx2: in_features too large");
+    const long long nb = K / 256;
+    StreamIn s[1] = {{w, nb * 144, static_cast<long long>(M) * nb * 144}};
+    GemvArgs ga = base_args(M, K, 32);
+    ga.x = x;
+    ga.y = y;
+    return launch_stream_gemv<kFmtQ4K, kProQ4K, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gemv_q4_packed(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                              int M, int K, int gs, int batch, void* stream) {
+    if (!w || !x || !scales || !biases || !y) return set_error(kEinval, "gemv_q4_packed: null pointer");
+    if (M <= 0 || K <= 0 || gs <= 0) return set_error(kEinval, "M, K, group_size must be positive");
+    if (batch < 1) return set_error(kEinval, "batch must be >= 1");
+    if (K % 2) return set_error(kEinval, "K must be even for 4-bit packing");
+    if (K % gs) return set_error(kEinval, "K must be divisible by group_size");
+    if (gs % 8) return set_error(kEinval, "group_size must be a multiple of 8 for AVX2 vectorization");
+    if (K > 32768) return set_error(kEinval, "gemv_q4_packed: in_features too large");
+    const long long ng = K / gs;
+    StreamIn s[3] = {{w, K / 2, static_cast<long long>(M) * (K / 2)},
+                     {scales, ng * 4, static_cast<long long>(M) * ng * 4},
+                     {biases, ng * 4, static_cast<long long>(M) * ng * 4}};
+    for (int b = 0; b < batch; ++b) {
+        GemvArgs ga = base_args(M, K, gs);
+        ga.x = x + static_cast<long long>(b) * K;
+        ga.y = y + static_cast<long long>(b) * M;
+        int rc = launch_stream_gemv<kFmtPacked, kProF32, kEpiStore>(s, 3, M, 0, ga, as_stream(stream));
+        if (rc) return rc;
+    }
+    return kOk;
+}
+
+int asdsl_b200_gemv_q4_unpacked(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                                int M, int K, int gs, void* stream) {
+    if (!w || !x || !scales || !biases || !y) return set_error(kEinval, "gemv_q4_unpacked: null pointer");
+    if (M <= 0 || K <= 0 || gs <= 0) return set_error(kEinval, "M, K, group_size must be positive");
+    if (K % 2) return set_error(kEinval, "K must be even for 4-bit packing");
+    if (K % gs) return set_error(kEinval, "K must be divisible by group_size");
+    if (gs % 8) return set_error(kEinval, "group_size must be a multiple of 8 for AVX2 vectorization");
+    const int wpb = 8;
+    k_gemv_unpacked<<<(M + wpb - 1) / wpb, wpb * 32, 0, as_stream(stream)>>>(w, x, scales, biases, y, M, K, gs);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_matmul_batch_q4(const uint8_t* w, const float* scales, const float* biases, const float* X, float* Y,
+                               int M, int K, int B, int gs, void* stream) {
+    return asdsl_b200_gemv_q4_packed(w, X, scales, biases, Y, M, K, gs, B, stream);
+}
+
+size_t asdsl_b200_argmax_scratch_bytes(void) { return 256 + 2 * 4 * 1024; }
+
+int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y, float* out_val,
+                           int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes, int M, int K,
+                           void* stream) {
+    if (!w0 || !x || !out_val || !out_idx || !scratch) return set_error(kEinval, "gemv_argmax: null pointer");
+    if (scratch_bytes < asdsl_b200_argmax_scratch_bytes()) return set_error(kEinval, "gemv_argmax: scratch too small");
+    if (M <= 0) return set_error(kEinval, "gemv_argmax: invalid dimensions");
+    if (sm_count() > 1024) return set_error(kEinval, "gemv_argmax: too many SMs for the scratch layout");
+    uint8_t* sc = static_cast<uint8_t*>(scratch);
+    GemvArgs ga;
+    StreamIn s[2];
+    if (fmt == ASDSL_B200_FMT_PREQ2) {
+        if (!w1) return set_error(kEinval, "gemv_argmax: null pointer");
+        if (int rc = check_k(K, 32, "gemv_argmax")) return rc;
+        preq2_streams(s, w0, w1, M, K);
+        ga = base_args(M, K, 32);
+    } else if (fmt == ASDSL_B200_FMT_Q4_128) {
+        if (K <= 0 || K % 128 || K > 17920) return set_error(kEinval, "gemv_argmax: in_features must be k*128 <= 17920");
+        const long long ng = K / 128;
+        s[0] = StreamIn{w0, ng * 66, static_cast<long long>(M) * ng * 66};
+        ga = base_args(M, K, 128);
+    } else {
+        return set_error(kEinval, "gemv_argmax: unsupported weight format");
+    }
+    ga.x = x;
+    ga.y = y;
+    ga.counter = reinterpret_cast<unsigned int*>(sc);
+    ga.part_val = reinterpret_cast<float*>(sc + 256);
+    ga.part_idx = reinterpret_cast<int*>(sc + 256 + 4 * 1024);
+    ga.out_val = out_val;
+    ga.out_idx = out_idx;
+    ga.row_base = row_base;
+    if (fmt == ASDSL_B200_FMT_PREQ2)
+        return launch_stream_gemv<kFmtPreq2, kProA8, kEpiArgmax>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+    return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiArgmax>(s, 1, M, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* h, int I, int K,
+                           void* stream) {
+    if (!w0 || !x || !h) return set_error(kEinval, "gateup_silu: null pointer");
+    if (I <= 0) return set_error(kEinval, "gateup_silu: invalid dimensions");
+    GemvArgs ga;
+    StreamIn s[2];
+    if (fmt == ASDSL_B200_FMT_PREQ2) {
+        if (!w1) return set_error(kEinval, "gateup_silu: null pointer");
+        if (I % 4) return set_error(kEinval, "gateup_silu: intermediate size must be a multiple of 4 for preq2");
+        if (int rc = check_k(K, 32, "gateup_silu")) return rc;
+        preq2_streams(s, w0, w1, 2LL * I, K);
+        ga = base_args(I, K, 32);
+        ga.x = x;
+        ga.h = h;
+        return launch_stream_gemv<kFmtPreq2, kProA8, kEpiSilu>(s, 2, I / 4, I / 4, ga, as_stream(stream));
+    }
+    if (fmt == ASDSL_B200_FMT_Q4_128) {
+        if (K <= 0 || K % 128 || K > 17920) return set_error(kEinval, "gateup_silu: in_features must be k*128 <= 17920");
+        const long long ng = K / 128;
+        s[0] = StreamIn{w0, ng * 66, 2LL * I * ng * 66};
+        ga = base_args(I, K, 128);
+        ga.x = x;
+        ga.h = h;
+        return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiSilu>(s, 1, I, I, ga, as_stream(stream));
+    }
+    return set_error(kEinval, "gateup_silu: unsupported weight format");
+}
+
+}  // extern "C"

@@ -1,0 +1,383 @@
+"""Benchmark of the B200 W4A8 decode hot path.
+
+Default workload (N=1): BASELINE config 1 -- one Phi-4-mini-shape decoder layer's
+projection set at batch 1 (qkv 5120x3072 + o 3072x3072 preq2 gs32, gate_up
+16384x3072 + down 3072x8192 Q4_128, SiLU*up fused between), seed 1, through the
+reference's C0.1 weight pipeline.  A step = the four fused kernels over one
+activation vector.  Metric: W4 GEMV HBM GB/s (algorithmic bytes / time).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N>1 (torchrun) every rank runs its own replica of the step on its own GPU
+(weak scaling, no data-path collective); value = all ranks' bytes / max-over-ranks
+time.  --impl reference times the reference's own AVX2/OpenMP kernels (compiled
+from its sources into oracle/_ref) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "asdsl-framework_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "W4 GEMV HBM GB/s (one Phi-4-mini layer projection set, batch 1)"
+NOMINAL_HBM_GBS = 8000.0
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic(name: str):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(name)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples of one GPU during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [t.strip() for t in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU arm: the reference's own kernels (oracle/_ref) on the host cores
+# ---------------------------------------------------------------------------
+def cpu_layer_step_runner(host: dict):
+    """Returns (callable running one config-1 step on the reference's CPU kernels, kind, cores)."""
+    import numpy as np
+
+    from oracle.oracle import Oracle, RefKernels, ref_lib_path
+
+    c = host["cfg"]
+    H, QKV, QD, I = c["hidden"], c["qkv_rows"], c["q_dim"], c["inter"]
+    orc = Oracle()
+    if ref_lib_path():
+        rk, kind = RefKernels(), "reference"
+    else:
+        rk, kind = None, "port"
+
+    def step():
+        x = host["x"]
+        if rk is not None:
+            qkv = rk.gemv_preq2_fused(host["qkv_meta"], host["qkv_quant"], x, QKV, H)
+            o = rk.gemv_preq2_fused(host["o_meta"], host["o_quant"], x, H, QD)
+            xq, xs = rk.quantize_activation(x, 128)
+            gu = rk.gemv_q4_128_q8(host["gate_up_q4_128"], xq, xs, 2 * I, H)
+            h = orc.swiglu(gu[:I], gu[I:])
+            hq, hs = rk.quantize_activation(h, 128)
+            y = rk.gemv_q4_128_q8(host["down_q4_128"], hq, hs, H, I)
+        else:
+            qkv = orc.gemv_preq2_fused(host["qkv_meta"], host["qkv_quant"], x, QKV, H)
+            o = orc.gemv_preq2_fused(host["o_meta"], host["o_quant"], x, H, QD)
+            gu = orc.gemv_q4_128_fused(host["gate_up_q4_128"], x, 2 * I, H)
+            h = orc.swiglu(gu[:I], gu[I:])
+            y = orc.gemv_q4_128_fused(host["down_q4_128"], h, H, I)
+        return qkv, o, y
+
+    del np
+    return step, kind
+
+
+def time_cpu(step, budget_s: float, min_steps: int = 3, max_steps: int = 10**6):
+    step()  # warm (page-in, OpenMP pool)
+    n, t0 = 0, time.perf_counter()
+    while n < max_steps and (n < min_steps or time.perf_counter() - t0 < budget_s):
+        step()
+        n += 1
+    return n, time.perf_counter() - t0
+
+
+def run_reference(args, host, bytes_per_step):
+    step, kind = cpu_layer_step_runner(host)
+    for _ in range(max(args.warmup, 0)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    gbs = bytes_per_step * args.steps / dt / 1e9
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4 x s8 -> f32 (W4A8)", "data": "synthetic",
+        "config": {"workload": "c1_layer_projection_set", "seed": 1, "global_batch": 1, "cpu_threads": cores},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": f"{args.steps} full config-1 layer steps on the host cores"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--copies", type=int, default=4, help="weight copies rotated to defeat L2 (> 126 MB total)")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline sampling")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cores = os.cpu_count() or 1
+        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        from asdsl_b200.layer import build_c1_host
+
+        host = build_c1_host(1)
+        wb = sum(host[k].nbytes for k in ("qkv_meta", "qkv_quant", "o_meta", "o_quant", "gate_up_q4_128",
+                                          "down_q4_128"))
+        c = host["cfg"]
+        act = 4 * (c["hidden"] + c["qkv_rows"]) + 4 * (c["q_dim"] + c["hidden"]) + 8 * (c["hidden"] + c["inter"])
+        print(json.dumps(run_reference(args, host, wb + act)), flush=True)
+        return
+
+    import numpy as np
+    import torch
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev_index = torch.cuda.current_device()
+
+    from asdsl_b200 import _lib
+    from asdsl_b200.build import build_library
+    from asdsl_b200.layer import build_c1_host, from_host
+
+    if rank == 0:
+        build_library()
+    if world > 1:
+        dist.barrier()
+    _lib.load()
+
+    host = build_c1_host(1)
+    base = from_host(host)
+    layers = [base] + [base.clone() for _ in range(max(args.copies, 1) - 1)]
+    bytes_per_step = base.algorithmic_bytes
+    x = torch.from_numpy(host["x"]).cuda()
+    stream = torch.cuda.Stream()
+
+    # correctness gate before timing (CPU oracle on the same bytes)
+    from oracle.oracle import Oracle, build as build_oracle, rel_err
+
+    if rank == 0 and not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+        build_oracle()
+    if world > 1:
+        dist.barrier()
+    with torch.cuda.stream(stream):
+        base.step(x)
+    stream.synchronize()
+    orc = Oracle()
+    c = host["cfg"]
+    ref_y_gu = orc.gemv_q4_128_fused(host["gate_up_q4_128"], host["x"], 2 * c["inter"], c["hidden"])
+    ref_h = orc.swiglu(ref_y_gu[: c["inter"]], ref_y_gu[c["inter"]:])
+    ref_y = orc.gemv_q4_128_fused(host["down_q4_128"], ref_h, c["hidden"], c["inter"])
+    err = rel_err(base.y.cpu().numpy(), ref_y)
+    if err > 1e-3:
+        raise SystemExit(f"bench: GPU result mismatch vs oracle ({err})")
+
+    # one CUDA graph per weight copy; replay round-robin
+    graphs = []
+    for L in layers:
+        with torch.cuda.stream(stream):
+            L.step(x)  # warm + set kernel attributes before capture
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            L.step(x)
+        graphs.append(g)
+    launches_per_step = 4
+
+    for i in range(args.warmup):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev_index) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                graphs[i % len(graphs)].replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * bytes_per_step / (ms_step * 1e-3) / 1e9
+
+    # dominant kernel alone (gate_up + SiLU, Q4_128): per-launch duration over rotated copies
+    dom_iters = 200
+    lib = _lib.load()
+    s_ptr = stream.cuda_stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(10):
+        L = layers[i % len(layers)]
+        lib.asdsl_b200_gateup_silu(2, L.gu.data_ptr(), None, x.data_ptr(), L.h.data_ptr(), L.I, L.H, s_ptr)
+    e0.record(stream)
+    for i in range(dom_iters):
+        L = layers[i % len(layers)]
+        lib.asdsl_b200_gateup_silu(2, L.gu.data_ptr(), None, x.data_ptr(), L.h.data_ptr(), L.I, L.H, s_ptr)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dom_ms = e0.elapsed_time(e1) / dom_iters
+    dom_bytes = base.gu.numel() + 4 * (base.H + base.I)
+    peak, peak_kind = _peaks()
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+
+    # e2e through the public host-buffer API (pinned H2D of x, D2H of all outputs)
+    e2e_steps = min(args.steps, 200)
+    for _ in range(3):
+        base.forward(host["x"])
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(e2e_steps):
+        base.forward(host["x"])
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = world * bytes_per_step / (e2e_ms * 1e-3) / 1e9
+    assert _lib.device_status(clear=True) == 0, "a kernel reported a bounded-wait timeout"
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        step, kind = cpu_layer_step_runner(host)
+        n, dt = time_cpu(step, args.cpu_budget)
+        cpu = {"value": round(bytes_per_step * n / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+               "sample": f"{n} full config-1 layer steps ({dt:.1f} s) on the host cores, OpenMP threads = cores"}
+
+    if rank == 0:
+        clocks = clk.summary()
+        out = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "u4 x s8 -> f32 (W4A8)",
+            "data": "synthetic",
+            "config": {"workload": "c1_layer_projection_set", "seed": 1, "global_batch": 1,
+                       "bytes_per_step": bytes_per_step, "weight_copies_rotated": len(layers),
+                       "l2": f"rotating {len(layers)} weight copies ({len(layers) * base.weight_bytes / 1e6:.0f} MB > 126 MB L2)",
+                       "parallelism": f"replica x{world}", "frac_of_8TBs": round(value / world / NOMINAL_HBM_GBS, 4)},
+            "roofline": {"bound": "hbm", "kernel": "k_stream_gemv<Q4_128, A8, SiLU> (gate_up 16384x3072 + SiLU)",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": _traffic("gateup_silu_q4_128_c1"),
+                         "launch_us": round(dom_ms * 1e3, 3), "bytes_per_launch": dom_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * base.H,
+                    "d2h_bytes_per_step": 4 * (base.QKV + 2 * base.H), "ms_per_step": round(e2e_ms, 5)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(out), flush=True)
+    for g in graphs:
+        del g
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,139 @@
+/*
+ * asdsl_b200.h -- C ABI of the B200-native ASDSL W4A8 decode hot path.
+ *
+ * Every entry point takes plain pointers and sizes.  Unless a comment says
+ * otherwise, array arguments are DEVICE pointers (cudaMalloc / torch CUDA
+ * storage) that are 16-byte aligned, and work is enqueued on `stream`
+ * (a cudaStream_t passed as void*; NULL = the legacy default stream) without
+ * synchronizing.  Functions return ASDSL_B200_OK or an error code; the message
+ * of the last error on the calling thread is returned by asdsl_b200_last_error().
+ *
+ * Each declaration cites the reference interface it replaces
+ * (aarushk09/asdsl-framework, paths relative to the repository root).
+ * Reference-side bindings are shown in INTEGRATION.md.
+ */
+#ifndef ASDSL_B200_H
+#define ASDSL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes: the reference's exception classes map onto them
+ * (std::invalid_argument -> EINVAL, std::out_of_range -> ERANGE) */
+#define ASDSL_B200_OK 0
+#define ASDSL_B200_EINVAL 1   /* bad argument (ValueError) */
+#define ASDSL_B200_ERANGE 2   /* index out of range (IndexError) */
+#define ASDSL_B200_ECUDA 3    /* CUDA runtime error (RuntimeError) */
+#define ASDSL_B200_ENCCL 4    /* NCCL error (RuntimeError) */
+#define ASDSL_B200_ETIMEOUT 5 /* a bounded device-side wait gave up */
+#define ASDSL_B200_ENOMEM 6   /* device allocation failed */
+
+/* weight formats accepted by asdsl_b200_gemv_w4a8 */
+#define ASDSL_B200_FMT_PREQ2 0  /* meta [M][K/32][4] + quant [ceil(M/4)][K/32][64] (repack_preq2.py:22-46) */
+#define ASDSL_B200_FMT_PREQ 1   /* [M][K/32][20] blocks (repack_q4_32.py:63-102) */
+#define ASDSL_B200_FMT_Q4_128 2 /* [M][K/128][66] blocks (repack_q4_128.py:34-92) */
+#define ASDSL_B200_FMT_S256 3   /* [M][K/256][144] blocks (gemv_q4_s256.cpp:1-17) */
+
+const char* asdsl_b200_version(void);
+const char* asdsl_b200_last_error(void);
+
+/* Reads (and with clear != 0 resets) the current device's status word: bits
+ * set by kernels whose bounded waits gave up.  Synchronizes the device. */
+int asdsl_b200_device_status(unsigned int* status, int clear);
+
+/* A8 activation quantization.
+ * Replaces quantize_activation_avx2 (asdsl/kernels/native/gemv_q4_preq_restored.cpp:505-549;
+ * binding asdsl/kernels/native/gemv_q4_avx2.cpp:1352-1365).
+ * x[K] fp32 -> xq[K] int8, xs[K/gs] fp32; xsum[K/gs] int32 (optional, may be NULL). */
+int asdsl_b200_quantize_activation(const float* x, int8_t* xq, float* xs, int32_t* xsum, int in_features,
+                                   int group_size, void* stream);
+
+/* preq2 W4A8 GEMV with fused A8 (gs 32).
+ * Replaces gemv_preq2_fused_avx2 (asdsl/kernels/native/gemv_preq2_avx2.cpp:301-319;
+ * binding gemv_q4_avx2.cpp:1405-1420). */
+int asdsl_b200_gemv_preq2_fused(const uint8_t* meta, const uint8_t* quant, const float* x, float* y,
+                                int out_features, int in_features, int group_size, void* stream);
+
+/* preq2 W4A8 GEMV on caller-quantized activations.
+ * Replaces gemv_preq2_avx2 (asdsl/kernels/native/gemv_preq2_avx2.cpp:321-337). */
+int asdsl_b200_gemv_preq2(const uint8_t* meta, const uint8_t* quant, const int8_t* x_q8, const float* x_scales,
+                          float* y, int out_features, int in_features, int group_size, void* stream);
+
+/* preq (20-byte block) W4A8 GEMV on caller-quantized activations.
+ * Replaces gemv_q4_32_preq_avx2 (asdsl/kernels/native/gemv_q4_preq_restored.cpp:551-577). */
+int asdsl_b200_gemv_q4_32_preq(const uint8_t* blocks, const int8_t* x_q8, const float* x_scales, float* y,
+                               int out_features, int in_features, int group_size, void* stream);
+
+/* preq W4A8 GEMV with fused A8.
+ * Replaces gemv_q4_32_preq_fused_avx2 / _4row / _8row / _g4fused_4row
+ * (asdsl/kernels/native/gemv_q4_preq_restored.cpp:579-669). */
+int asdsl_b200_gemv_q4_32_preq_fused(const uint8_t* blocks, const float* x, float* y, int out_features,
+                                     int in_features, int group_size, void* stream);
+
+/* Q4_128 symmetric W4A8 GEMV on caller-quantized activations (gs 128).
+ * Replaces gemv_q4_128_preq_avx2 (asdsl/kernels/native/gemv_q4_128.cpp:94-257;
+ * binding gemv_q4_avx2.cpp:1422-1437). */
+int asdsl_b200_gemv_q4_128(const uint8_t* blocks, const int8_t* x_q8, const float* x_scales, float* y,
+                           int out_features, int in_features, int group_size, void* stream);
+
+/* Q4_128 GEMV with fused A8 at gs 128: quantize_activation_avx2(..., 128) followed
+ * by gemv_q4_128_preq_avx2, as the engine's C0.1 branches do
+ * (asdsl/kernels/native/unified_engine.cpp:1532-1538, :1592-1598). */
+int asdsl_b200_gemv_q4_128_fused(const uint8_t* blocks, const float* x, float* y, int out_features,
+                                 int in_features, void* stream);
+
+/* Q4_S256 W4A8 GEMV on caller-quantized activations (activation gs 32).
+ * Replaces gemv_q4_s256_preq_avx2 (asdsl/kernels/native/gemv_q4_s256.cpp:83-209). */
+int asdsl_b200_gemv_q4_s256(const uint8_t* blocks, const int8_t* x_q8, const float* x_scales, float* y,
+                            int out_features, int in_features, int group_size, void* stream);
+
+/* Q4_K (reference interpretation: fp16 d, fp16 dmin, 16 6-bit LE values, 8x16 nibble bytes)
+ * GEMV with its own A8.  Replaces gemv_q4km_q8_avx2 (asdsl/kernels/native/gemv_q4_avx2.cpp:357-420;
+ * binding :1318-1348). */
+int asdsl_b200_gemv_q4km(const uint8_t* weights_q4km, const float* x, float* y, int out_features,
+                         int in_features, void* stream);
+
+/* fp32-activation packed W4 GEMV, `batch` independent activation rows x[batch][K] -> y[batch][M].
+ * Replaces gemv_q4_packed_impl_v2 and its binding py_gemv_q4_packed
+ * (asdsl/kernels/native/gemv_q4_avx2.cpp:665-749, :1084-1126). */
+int asdsl_b200_gemv_q4_packed(const uint8_t* w_packed, const float* x, const float* scales, const float* biases,
+                              float* y, int M, int K, int group_size, int batch, void* stream);
+
+/* fp32-activation GEMV on unpacked (one code per byte) weights.
+ * Replaces gemv_q4_unpacked_impl (asdsl/kernels/native/gemv_q4_avx2.cpp:755-806). */
+int asdsl_b200_gemv_q4_unpacked(const uint8_t* w, const float* x, const float* scales, const float* biases,
+                                float* y, int M, int K, int group_size, void* stream);
+
+/* Batched fp32-activation packed GEMV, Y[B][M] = W x X[B][K]^T.
+ * Replaces matmul_batch_q4_impl (asdsl/kernels/native/gemv_q4_avx2.cpp:950-1021). */
+int asdsl_b200_matmul_batch_q4(const uint8_t* w_packed, const float* scales, const float* biases,
+                               const float* X_batch, float* Y_batch, int M, int K, int B, int group_size,
+                               void* stream);
+
+/* Bytes of device scratch the fused-argmax GEMVs need (zero-filled once by the caller;
+ * the kernels leave it re-armed). */
+size_t asdsl_b200_argmax_scratch_bytes(void);
+
+/* lm_head GEMV with fused first-max argmax (fused A8; fmt PREQ2 at gs 32 or Q4_128 at gs 128).
+ * Writes logits to y (may be NULL) and the maximum / its global row index (row_base + local row)
+ * to out_val[0] / out_idx[0].  Replaces the engine's lm_head GEMV + argmax_f32_avx2
+ * (asdsl/kernels/native/unified_engine.cpp:1628-1644 and :207-233). */
+int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
+                           float* out_val, int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes,
+                           int out_features, int in_features, void* stream);
+
+/* Fused gate_up GEMV + SiLU(gate)*up: rows [0, I) are gate, [I, 2I) are up, h[i] = silu(gate_i)*up_i
+ * with the reference's fast_exp.  fmt PREQ2 (w0 = meta, w1 = quant) or Q4_128 (w0 = blocks).
+ * Replaces the gate_up GEMV + swiglu_inplace pair (asdsl/kernels/native/unified_engine.cpp:1539-1570,
+ * :836-857). */
+int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* h,
+                           int intermediate, int in_features, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ASDSL_B200_H */

@@ -1,0 +1,78 @@
+"""The C ABI library: it loads, exports every symbol include/asdsl_b200.h declares,
+and rejects bad arguments with the reference's exception classes -- all without a
+GPU (no compute call is made).  CPU only."""
+
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    names = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            names |= set(re.findall(r"\b(asdsl_b200_\w+)\s*\(", text))
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from asdsl_b200 import _lib
+    from asdsl_b200.build import build_library
+
+    build_library()
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    from asdsl_b200 import _lib
+
+    declared = _declared_symbols()
+    assert declared, "no declarations found"
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared but not exported"
+    # and the Python binding types every one of them
+    assert set(declared) <= set(_lib.exported_symbols())
+
+
+def test_version_and_scratch(lib):
+    assert b"sm_100a" in lib.asdsl_b200_version()
+    assert lib.asdsl_b200_argmax_scratch_bytes() >= 256
+
+
+def test_argument_errors_map_to_reference_exceptions(lib):
+    from asdsl_b200 import _lib
+
+    # null pointers / bad group sizes are rejected on the host before any CUDA call
+    with pytest.raises(ValueError, match="null pointer"):
+        _lib.call("asdsl_b200_gemv_preq2_fused", None, None, None, None, 16, 64, 32, None)
+    with pytest.raises(ValueError, match="group_size must be 32"):
+        _lib.call("asdsl_b200_gemv_preq2_fused", 16, 16, 16, 16, 16, 64, 64, None)
+    with pytest.raises(ValueError, match="group_size must be 128"):
+        _lib.call("asdsl_b200_gemv_q4_128", 16, 16, 16, 16, 16, 256, 32, None)
+    with pytest.raises(ValueError, match="divisible by 256"):
+        _lib.call("asdsl_b200_gemv_q4km", 16, 16, 16, 4, 100, None)
+    with pytest.raises(ValueError, match="n_groups exceeds buffer"):
+        _lib.call("asdsl_b200_gemv_q4_32_preq", 16, 16, 16, 16, 4, 32 * 641, 32, None)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        _lib.call("asdsl_b200_gemv_q4_packed", 16, 16, 16, 16, 16, 4, 36, 12, 1, None)
+    # Q4_K with empty shapes returns without work, like the reference
+    assert _lib.call("asdsl_b200_gemv_q4km", None, None, None, 0, 256, None) == 0
+
+
+def test_python_api_fails_loudly_without_gpu():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from asdsl_b200.kernels import gemv_q4_packed, has_native_kernel
+
+    assert not has_native_kernel()
+    with pytest.raises(RuntimeError):
+        gemv_q4_packed(np.zeros(32, np.uint8), np.zeros(64, np.float32), np.ones(2, np.float32),
+                       np.zeros(2, np.float32), 1, 64, 32)
