@@ -22,7 +22,7 @@ LIB_PATH = os.path.join(_HERE, "libasdsl_b200.so")
 
 OK, EINVAL, ERANGE, ECUDA, ENCCL, ETIMEOUT, ENOMEM = range(7)
 
-FMT_PREQ2, FMT_PREQ, FMT_Q4_128, FMT_S256 = 0, 1, 2, 3
+FMT_PREQ2, FMT_PREQ, FMT_Q4_128, FMT_S256, FMT_Q4_128_BANDED = 0, 1, 2, 3, 4
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -34,6 +34,7 @@ _SIGS = {
     "asdsl_b200_version": [],
     "asdsl_b200_last_error": [],
     "asdsl_b200_device_status": [_P, _I],
+    "asdsl_b200_set_launch_policy": [_I, _I],
     "asdsl_b200_quantize_activation": [_P, _P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_preq2_fused": [_P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_gemv_preq2": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
@@ -47,6 +48,8 @@ _SIGS = {
     "asdsl_b200_gemv_q4_unpacked": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_matmul_batch_q4": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "asdsl_b200_argmax_scratch_bytes": [],
+    "asdsl_b200_relayout_q4_128": [_P, _P, _P, _I, _I, _P],
+    "asdsl_b200_gemv_q4_128_banded": [_P, _P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_argmax": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P],
     "asdsl_b200_gateup_silu": [_I, _P, _P, _P, _P, _I, _I, _P],
 }

@@ -1,9 +1,11 @@
-"""One decoder layer's projection set on the device (the C0.1 byte mix):
+"""One decoder layer's projection set on the device (the C0.1 byte mix), run as
+the dependent chain a decode step runs:
 
-    qkv  = W_qkv  x      preq2 gs 32   (unified_engine.cpp:1411-1413)
-    o    = W_o    x      preq2 gs 32   (:1487-1489)
-    h    = silu(W_gate x) * (W_up x)   Q4_128, fused in one kernel (:1532-1538 + :836-857)
-    y    = W_down h      Q4_128        (:1592-1598)
+    qkv  = W_qkv  x            preq2 gs 32   (unified_engine.cpp:1411-1413)
+    o    = W_o    qkv[:q_dim]  preq2 gs 32   (:1487-1489; the q slice stands in for
+                                              the attention output, which config 1 omits)
+    h    = silu(W_gate o) * (W_up o)   Q4_128, fused in one kernel (:1532-1538 + :836-857)
+    y    = W_down h            Q4_128        (:1592-1598)
 
 Weights live in HBM for the object's lifetime; ``step`` enqueues the four
 kernels on torch's current stream (capturable in a CUDA graph), ``forward``
@@ -22,7 +24,17 @@ import torch
 from asdsl_b200 import _lib
 from asdsl_b200.quantization import core, repack
 
-FMT_PREQ2, FMT_Q4_128 = 0, 2
+FMT_PREQ2, FMT_Q4_128, FMT_Q4_128_BANDED = 0, 2, 4
+
+
+def relayout_q4_128(blocks: torch.Tensor, rows: int, cols: int):
+    """Device re-layout of Q4_128 blocks into (quant, scales) bands (asdsl_b200_relayout_q4_128)."""
+    nb, ng = (rows + 3) // 4, cols // 128
+    q = torch.empty(nb * ng * 256, dtype=torch.uint8, device=blocks.device)
+    s = torch.empty(nb * ng * 8, dtype=torch.uint8, device=blocks.device)
+    _lib.call("asdsl_b200_relayout_q4_128", blocks.data_ptr(), q.data_ptr(), s.data_ptr(), rows, cols,
+              torch.cuda.current_stream().cuda_stream or None)
+    return q, s
 
 
 class LayerProjections:
@@ -35,8 +47,14 @@ class LayerProjections:
 
         self.qkv_meta, self.qkv_quant = up(qkv_meta), up(qkv_quant)
         self.o_meta, self.o_quant = up(o_meta), up(o_quant)
-        self.gu, self.dn = up(gate_up_q4_128), up(down_q4_128)
         self.H, self.QKV, self.QD, self.I = hidden, qkv_rows, q_dim, inter
+        # Q4_128 blocks -> banded device layout (bit-exact byte moves, done once)
+        if isinstance(gate_up_q4_128, tuple):
+            self.gu_q, self.gu_s = gate_up_q4_128
+            self.dn_q, self.dn_s = down_q4_128
+        else:
+            self.gu_q, self.gu_s = relayout_q4_128(up(gate_up_q4_128), 2 * inter, hidden)
+            self.dn_q, self.dn_s = relayout_q4_128(up(down_q4_128), hidden, inter)
         self.qkv_out = torch.empty(qkv_rows, dtype=torch.float32, device=dev)
         self.o_out = torch.empty(hidden, dtype=torch.float32, device=dev)
         self.h = torch.empty(inter, dtype=torch.float32, device=dev)
@@ -49,7 +67,8 @@ class LayerProjections:
 
     @property
     def weight_bytes(self) -> int:
-        return sum(t.numel() for t in (self.qkv_meta, self.qkv_quant, self.o_meta, self.o_quant, self.gu, self.dn))
+        return sum(t.numel() for t in (self.qkv_meta, self.qkv_quant, self.o_meta, self.o_quant, self.gu_q, self.gu_s,
+                                       self.dn_q, self.dn_s))
 
     @property
     def algorithmic_bytes(self) -> int:
@@ -65,12 +84,12 @@ class LayerProjections:
         L = _lib.load()
         _lib.check(L.asdsl_b200_gemv_preq2_fused(self.qkv_meta.data_ptr(), self.qkv_quant.data_ptr(), x.data_ptr(),
                                                  self.qkv_out.data_ptr(), self.QKV, self.H, 32, s))
-        _lib.check(L.asdsl_b200_gemv_preq2_fused(self.o_meta.data_ptr(), self.o_quant.data_ptr(), x.data_ptr(),
-                                                 self.o_out.data_ptr(), self.H, self.QD, 32, s))
-        _lib.check(L.asdsl_b200_gateup_silu(FMT_Q4_128, self.gu.data_ptr(), None, x.data_ptr(), self.h.data_ptr(),
-                                            self.I, self.H, s))
-        _lib.check(L.asdsl_b200_gemv_q4_128_fused(self.dn.data_ptr(), self.h.data_ptr(), self.y.data_ptr(), self.H,
-                                                  self.I, s))
+        _lib.check(L.asdsl_b200_gemv_preq2_fused(self.o_meta.data_ptr(), self.o_quant.data_ptr(),
+                                                 self.qkv_out.data_ptr(), self.o_out.data_ptr(), self.H, self.QD, 32, s))
+        _lib.check(L.asdsl_b200_gateup_silu(FMT_Q4_128_BANDED, self.gu_q.data_ptr(), self.gu_s.data_ptr(),
+                                            self.o_out.data_ptr(), self.h.data_ptr(), self.I, self.H, s))
+        _lib.check(L.asdsl_b200_gemv_q4_128_banded(self.dn_q.data_ptr(), self.dn_s.data_ptr(), self.h.data_ptr(),
+                                                   self.y.data_ptr(), self.H, self.I, s))
         return 4
 
     def forward(self, x_host: np.ndarray) -> dict:
@@ -90,8 +109,8 @@ class LayerProjections:
     def clone(self) -> "LayerProjections":
         """Same weights at new device addresses (L2-rotation copies for benchmarking)."""
         return LayerProjections(self.qkv_meta.clone(), self.qkv_quant.clone(), self.o_meta.clone(),
-                                self.o_quant.clone(), self.gu.clone(), self.dn.clone(), self.H, self.QKV, self.QD,
-                                self.I)
+                                self.o_quant.clone(), (self.gu_q.clone(), self.gu_s.clone()),
+                                (self.dn_q.clone(), self.dn_s.clone()), self.H, self.QKV, self.QD, self.I)
 
 
 C1 = dict(hidden=3072, qkv_rows=5120, q_dim=3072, inter=8192)
@@ -125,3 +144,15 @@ def from_host(host: dict) -> LayerProjections:
     return LayerProjections(host["qkv_meta"], host["qkv_quant"], host["o_meta"], host["o_quant"],
                             host["gate_up_q4_128"], host["down_q4_128"], c["hidden"], c["qkv_rows"], c["q_dim"],
                             c["inter"])
+
+
+def layer_reference(orc, host: dict) -> dict:
+    """The same chain on the CPU oracle (test / bench checker only)."""
+    c = host["cfg"]
+    H, QKV, QD, I = c["hidden"], c["qkv_rows"], c["q_dim"], c["inter"]
+    qkv = orc.gemv_preq2_fused(host["qkv_meta"], host["qkv_quant"], host["x"], QKV, H)
+    o = orc.gemv_preq2_fused(host["o_meta"], host["o_quant"], qkv[:QD], H, QD)
+    gu = orc.gemv_q4_128_fused(host["gate_up_q4_128"], o, 2 * I, H)
+    h = orc.swiglu(gu[:I], gu[I:])
+    y = orc.gemv_q4_128_fused(host["down_q4_128"], h, H, I)
+    return {"qkv": qkv, "o": o, "y": y}

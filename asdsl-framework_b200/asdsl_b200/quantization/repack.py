@@ -145,3 +145,18 @@ def repack_asymmetric_to_q4_128_blocks(packed, scales, biases, rows: int, cols: 
     zero32 = (-bi64 / sc64).astype(np.float32).reshape(rows, ng, 1)
     w = (q - zero32) * sc64.astype(np.float32).reshape(rows, ng, 1)
     return _q4_128_from_f32_rows(w)
+
+
+def q4_128_to_banded(blocks, rows: int, cols: int):
+    """Host form of the device re-layout of Q4_128 blocks (asdsl_b200_relayout_q4_128):
+    quant [ceil(rows/4)][cols/128][4][64] nibble bytes + scales [ceil(rows/4)][cols/128][4] fp16,
+    rows past `rows` zero-filled.  Pure byte moves."""
+    ng = cols // 128
+    nb = (rows + 3) // 4
+    b = np.asarray(blocks, dtype=np.uint8).reshape(rows, ng, 66)
+    pad = np.zeros((nb * 4, ng, 66), dtype=np.uint8)
+    pad[:rows] = b
+    pad = pad.reshape(nb, 4, ng, 66).transpose(0, 2, 1, 3)
+    quant = np.ascontiguousarray(pad[..., 2:]).reshape(-1)
+    scales = np.ascontiguousarray(pad[..., 0:2]).reshape(-1)
+    return quant, scales

@@ -90,6 +90,26 @@ inline void preq2_streams(StreamIn* s, const uint8_t* meta, const uint8_t* quant
     s[1] = StreamIn{meta, ng * 16, M * ng * 4};
 }
 
+LaunchOpts rows_opt(long long row_bytes) {
+    LaunchOpts o;
+    o.row_bytes = static_cast<int>(row_bytes);
+    return o;
+}
+
+// banded Q4_128 streams: quant [nb][ng][4][64] + scales [nb][ng][4] fp16 (band units)
+inline void q128b_streams(StreamIn* s, const uint8_t* quant, const uint8_t* scales, long long M, long long K) {
+    const long long ng = K / 128;
+    const long long nb = (M + 3) / 4;
+    s[0] = StreamIn{quant, ng * 256, nb * ng * 256};
+    s[1] = StreamIn{scales, ng * 8, nb * ng * 8};
+}
+
+int check_k128(int K, const char* fn) {
+    if (K <= 0 || K % 128) return set_error(kEinval, std::string(fn) + ": in_features must be divisible by 128");
+    if (K > 17920) return set_error(kEinval, std::string(fn) + ": in_features exceeds 17920");
+    return kOk;
+}
+
 GemvArgs base_args(int M, int K, int gs) {
     GemvArgs ga;
     std::memset(&ga, 0, sizeof(ga));
@@ -109,6 +129,14 @@ extern "C" {
 const char* asdsl_b200_version(void) { return "asdsl-b200 0.1 (sm_100a)"; }
 
 const char* asdsl_b200_last_error(void) { return last_error_msg().c_str(); }
+
+int asdsl_b200_set_launch_policy(int ctas_per_sm, int use_pdl) {
+    if (ctas_per_sm < 1 || ctas_per_sm > kCtasPerSm)
+        return set_error(kEinval, "set_launch_policy: ctas_per_sm must be in [1, " + std::to_string(kCtasPerSm) + "]");
+    launch_policy().ctas_per_sm = ctas_per_sm;
+    launch_policy().pdl = use_pdl ? 1 : 0;
+    return kOk;
+}
 
 int asdsl_b200_device_status(unsigned int* status, int clear) {
     if (!status) return set_error(kEinval, "asdsl_b200_device_status: null pointer");
@@ -172,12 +200,13 @@ int asdsl_b200_gemv_q4_32_preq(const uint8_t* blocks, const int8_t* xq, const fl
     if (gs != 32) return set_error(kEinval, "gemv_q4_32_preq_avx2: group_size must be 32");
     if (K / gs > 640) return set_error(kEinval, "gemv_q4_32_preq_avx2: n_groups exceeds buffer");
     const long long ng = K / 32;
-    StreamIn s[1] = {{blocks, ng * 20, static_cast<long long>(M) * ng * 20}};
+    StreamIn s[1] = {{blocks, 4 * ng * 20, static_cast<long long>(M) * ng * 20}};
     GemvArgs ga = base_args(M, K, 32);
     ga.xq = xq;
     ga.xs_in = xs;
     ga.y = y;
-    return launch_stream_gemv<kFmtPreq, kProQ8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+    return launch_stream_gemv<kFmtPreq, kProQ8, kEpiStore>(s, 1, (M + 3) / 4, 0, ga, as_stream(stream),
+                                                           rows_opt(ng * 20));
 }
 
 int asdsl_b200_gemv_q4_32_preq_fused(const uint8_t* blocks, const float* x, float* y, int M, int K, int gs,
@@ -187,11 +216,12 @@ int asdsl_b200_gemv_q4_32_preq_fused(const uint8_t* blocks, const float* x, floa
     if (M <= 0 || K <= 0) return set_error(kEinval, "gemv_q4_32_preq_fused_avx2: invalid dimensions");
     if (int rc = check_k(K, gs, "gemv_q4_32_preq_fused_avx2")) return rc;
     const long long ng = K / 32;
-    StreamIn s[1] = {{blocks, ng * 20, static_cast<long long>(M) * ng * 20}};
+    StreamIn s[1] = {{blocks, 4 * ng * 20, static_cast<long long>(M) * ng * 20}};
     GemvArgs ga = base_args(M, K, 32);
     ga.x = x;
     ga.y = y;
-    return launch_stream_gemv<kFmtPreq, kProA8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+    return launch_stream_gemv<kFmtPreq, kProA8, kEpiStore>(s, 1, (M + 3) / 4, 0, ga, as_stream(stream),
+                                                           rows_opt(ng * 20));
 }
 
 int asdsl_b200_gemv_q4_128(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K, int gs,
@@ -202,12 +232,13 @@ int asdsl_b200_gemv_q4_128(const uint8_t* blocks, const int8_t* xq, const float*
     if (K > 17920) return set_error(kEinval, "gemv_q4_128_preq_avx2: in_features exceeds 17920");
     if (M < 0) return set_error(kEinval, "gemv_q4_128_preq_avx2: invalid dimensions");
     const long long ng = K / 128;
-    StreamIn s[1] = {{blocks, ng * 66, static_cast<long long>(M) * ng * 66}};
+    StreamIn s[1] = {{blocks, 4 * ng * 66, static_cast<long long>(M) * ng * 66}};
     GemvArgs ga = base_args(M, K, 128);
     ga.xq = xq;
     ga.xs_in = xs;
     ga.y = y;
-    return launch_stream_gemv<kFmtQ4_128, kProQ8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+    return launch_stream_gemv<kFmtQ4_128, kProQ8, kEpiStore>(s, 1, (M + 3) / 4, 0, ga, as_stream(stream),
+                                                             rows_opt(ng * 66));
 }
 
 int asdsl_b200_gemv_q4_128_fused(const uint8_t* blocks, const float* x, float* y, int M, int K, void* stream) {
@@ -216,11 +247,12 @@ int asdsl_b200_gemv_q4_128_fused(const uint8_t* blocks, const float* x, float* y
     if (K > 17920) return set_error(kEinval, "gemv_q4_128_fused: in_features exceeds 17920");
     if (M < 0) return set_error(kEinval, "gemv_q4_128_fused: invalid dimensions");
     const long long ng = K / 128;
-    StreamIn s[1] = {{blocks, ng * 66, static_cast<long long>(M) * ng * 66}};
+    StreamIn s[1] = {{blocks, 4 * ng * 66, static_cast<long long>(M) * ng * 66}};
     GemvArgs ga = base_args(M, K, 128);
     ga.x = x;
     ga.y = y;
-    return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+    return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiStore>(s, 1, (M + 3) / 4, 0, ga, as_stream(stream),
+                                                             rows_opt(ng * 66));
 }
 
 int asdsl_b200_gemv_q4_s256(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K, int gs,
@@ -231,12 +263,13 @@ int asdsl_b200_gemv_q4_s256(const uint8_t* blocks, const int8_t* xq, const float
     if (K > 17920) return set_error(kEinval, "gemv_q4_s256: in_features exceeds 17920");
     if (M < 0) return set_error(kEinval, "gemv_q4_s256: invalid dimensions");
     const long long nsb = K / 256;
-    StreamIn s[1] = {{blocks, nsb * 144, static_cast<long long>(M) * nsb * 144}};
+    StreamIn s[1] = {{blocks, 4 * nsb * 144, static_cast<long long>(M) * nsb * 144}};
     GemvArgs ga = base_args(M, K, 32);
     ga.xq = xq;
     ga.xs_in = xs;
     ga.y = y;
-    return launch_stream_gemv<kFmtS256, kProQ8, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+    return launch_stream_gemv<kFmtS256, kProQ8, kEpiStore>(s, 1, (M + 3) / 4, 0, ga, as_stream(stream),
+                                                           rows_opt(nsb * 144));
 }
 
 int asdsl_b200_gemv_q4km(const uint8_t* w, const float* x, float* y, int M, int K, void* stream) {
@@ -245,11 +278,12 @@ int asdsl_b200_gemv_q4km(const uint8_t* w, const float* x, float* y, int M, int 
     if (K % 256) return set_error(kEinval, "in_features must be divisible by 256 for Q4_K_M");
     if (K > kMaxK) return set_error(kEinval, "gemv_q4km_q8_avx2: in_features too large");
     const long long nb = K / 256;
-    StreamIn s[1] = {{w, nb * 144, static_cast<long long>(M) * nb * 144}};
+    StreamIn s[1] = {{w, 4 * nb * 144, static_cast<long long>(M) * nb * 144}};
     GemvArgs ga = base_args(M, K, 32);
     ga.x = x;
     ga.y = y;
-    return launch_stream_gemv<kFmtQ4K, kProQ4K, kEpiStore>(s, 1, M, 0, ga, as_stream(stream));
+    return launch_stream_gemv<kFmtQ4K, kProQ4K, kEpiStore>(s, 1, (M + 3) / 4, 0, ga, as_stream(stream),
+                                                           rows_opt(nb * 144));
 }
 
 int asdsl_b200_gemv_q4_packed(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
@@ -295,6 +329,32 @@ int asdsl_b200_matmul_batch_q4(const uint8_t* w, const float* scales, const floa
 
 size_t asdsl_b200_argmax_scratch_bytes(void) { return 256 + 2 * 4 * 1024; }
 
+int asdsl_b200_relayout_q4_128(const uint8_t* blocks, uint8_t* quant, uint8_t* scales, int M, int K, void* stream) {
+    if (!blocks || !quant || !scales) return set_error(kEinval, "relayout_q4_128: null pointer");
+    if (int rc = check_k128(K, "relayout_q4_128")) return rc;
+    if (M <= 0) return set_error(kEinval, "relayout_q4_128: invalid dimensions");
+    const long long work = (static_cast<long long>(M) + 3) / 4 * (K / 128) * 4;
+    const int threads = 256;
+    long long blocks_n = (work + threads - 1) / threads;
+    if (blocks_n > 65535) blocks_n = 65535;
+    k_relayout_q4_128<<<static_cast<unsigned>(blocks_n), threads, 0, as_stream(stream)>>>(blocks, quant, scales, M, K);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_gemv_q4_128_banded(const uint8_t* quant, const uint8_t* scales, const float* x, float* y, int M, int K,
+                                  void* stream) {
+    if (!quant || !scales || !x || !y) return set_error(kEinval, "gemv_q4_128_banded: null pointer");
+    if (int rc = check_k128(K, "gemv_q4_128_banded")) return rc;
+    if (M < 0) return set_error(kEinval, "gemv_q4_128_banded: invalid dimensions");
+    StreamIn s[2];
+    q128b_streams(s, quant, scales, M, K);
+    GemvArgs ga = base_args(M, K, 128);
+    ga.x = x;
+    ga.y = y;
+    return launch_stream_gemv<kFmtQ128B, kProA8, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+}
+
 int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y, float* out_val,
                            int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes, int M, int K,
                            void* stream) {
@@ -305,56 +365,79 @@ int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const 
     uint8_t* sc = static_cast<uint8_t*>(scratch);
     GemvArgs ga;
     StreamIn s[2];
+    auto finish = [&](GemvArgs& a) {
+        a.x = x;
+        a.y = y;
+        a.counter = reinterpret_cast<unsigned int*>(sc);
+        a.part_val = reinterpret_cast<float*>(sc + 256);
+        a.part_idx = reinterpret_cast<int*>(sc + 256 + 4 * 1024);
+        a.out_val = out_val;
+        a.out_idx = out_idx;
+        a.row_base = row_base;
+    };
+    const long long nbands = (static_cast<long long>(M) + 3) / 4;
     if (fmt == ASDSL_B200_FMT_PREQ2) {
         if (!w1) return set_error(kEinval, "gemv_argmax: null pointer");
         if (int rc = check_k(K, 32, "gemv_argmax")) return rc;
         preq2_streams(s, w0, w1, M, K);
         ga = base_args(M, K, 32);
-    } else if (fmt == ASDSL_B200_FMT_Q4_128) {
-        if (K <= 0 || K % 128 || K > 17920) return set_error(kEinval, "gemv_argmax: in_features must be k*128 <= 17920");
-        const long long ng = K / 128;
-        s[0] = StreamIn{w0, ng * 66, static_cast<long long>(M) * ng * 66};
-        ga = base_args(M, K, 128);
-    } else {
-        return set_error(kEinval, "gemv_argmax: unsupported weight format");
+        finish(ga);
+        return launch_stream_gemv<kFmtPreq2, kProA8, kEpiArgmax>(s, 2, nbands, 0, ga, as_stream(stream));
     }
-    ga.x = x;
-    ga.y = y;
-    ga.counter = reinterpret_cast<unsigned int*>(sc);
-    ga.part_val = reinterpret_cast<float*>(sc + 256);
-    ga.part_idx = reinterpret_cast<int*>(sc + 256 + 4 * 1024);
-    ga.out_val = out_val;
-    ga.out_idx = out_idx;
-    ga.row_base = row_base;
-    if (fmt == ASDSL_B200_FMT_PREQ2)
-        return launch_stream_gemv<kFmtPreq2, kProA8, kEpiArgmax>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
-    return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiArgmax>(s, 1, M, 0, ga, as_stream(stream));
+    if (fmt == ASDSL_B200_FMT_Q4_128) {
+        if (int rc = check_k128(K, "gemv_argmax")) return rc;
+        const long long ng = K / 128;
+        s[0] = StreamIn{w0, 4 * ng * 66, static_cast<long long>(M) * ng * 66};
+        ga = base_args(M, K, 128);
+        finish(ga);
+        return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiArgmax>(s, 1, nbands, 0, ga, as_stream(stream),
+                                                                  rows_opt(ng * 66));
+    }
+    if (fmt == ASDSL_B200_FMT_Q4_128_BANDED) {
+        if (!w1) return set_error(kEinval, "gemv_argmax: null pointer");
+        if (int rc = check_k128(K, "gemv_argmax")) return rc;
+        q128b_streams(s, w0, w1, M, K);
+        ga = base_args(M, K, 128);
+        finish(ga);
+        return launch_stream_gemv<kFmtQ128B, kProA8, kEpiArgmax>(s, 2, nbands, 0, ga, as_stream(stream));
+    }
+    return set_error(kEinval, "gemv_argmax: unsupported weight format");
 }
 
 int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* h, int I, int K,
                            void* stream) {
     if (!w0 || !x || !h) return set_error(kEinval, "gateup_silu: null pointer");
     if (I <= 0) return set_error(kEinval, "gateup_silu: invalid dimensions");
+    if (I % 4) return set_error(kEinval, "gateup_silu: intermediate size must be a multiple of 4");
     GemvArgs ga;
     StreamIn s[2];
+    const long long nb = I / 4;
     if (fmt == ASDSL_B200_FMT_PREQ2) {
         if (!w1) return set_error(kEinval, "gateup_silu: null pointer");
-        if (I % 4) return set_error(kEinval, "gateup_silu: intermediate size must be a multiple of 4 for preq2");
         if (int rc = check_k(K, 32, "gateup_silu")) return rc;
         preq2_streams(s, w0, w1, 2LL * I, K);
         ga = base_args(I, K, 32);
         ga.x = x;
         ga.h = h;
-        return launch_stream_gemv<kFmtPreq2, kProA8, kEpiSilu>(s, 2, I / 4, I / 4, ga, as_stream(stream));
+        return launch_stream_gemv<kFmtPreq2, kProA8, kEpiSilu>(s, 2, nb, nb, ga, as_stream(stream));
     }
     if (fmt == ASDSL_B200_FMT_Q4_128) {
-        if (K <= 0 || K % 128 || K > 17920) return set_error(kEinval, "gateup_silu: in_features must be k*128 <= 17920");
+        if (int rc = check_k128(K, "gateup_silu")) return rc;
         const long long ng = K / 128;
-        s[0] = StreamIn{w0, ng * 66, 2LL * I * ng * 66};
+        s[0] = StreamIn{w0, 4 * ng * 66, 2LL * I * ng * 66};
         ga = base_args(I, K, 128);
         ga.x = x;
         ga.h = h;
-        return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiSilu>(s, 1, I, I, ga, as_stream(stream));
+        return launch_stream_gemv<kFmtQ4_128, kProA8, kEpiSilu>(s, 1, nb, nb, ga, as_stream(stream), rows_opt(ng * 66));
+    }
+    if (fmt == ASDSL_B200_FMT_Q4_128_BANDED) {
+        if (!w1) return set_error(kEinval, "gateup_silu: null pointer");
+        if (int rc = check_k128(K, "gateup_silu")) return rc;
+        q128b_streams(s, w0, w1, 2LL * I, K);
+        ga = base_args(I, K, 128);
+        ga.x = x;
+        ga.h = h;
+        return launch_stream_gemv<kFmtQ128B, kProA8, kEpiSilu>(s, 2, nb, nb, ga, as_stream(stream));
     }
     return set_error(kEinval, "gateup_silu: unsupported weight format");
 }

@@ -58,14 +58,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// The suspend-time hint lets a waiting thread sleep (up to the hint) until the
+// phase completes instead of spinning, so idle warps do not steal issue slots.
+constexpr uint32_t kTryWaitSuspendNs = 100000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -171,6 +175,60 @@ __device__ __forceinline__ uint4 lds128_a2(const uint8_t* p) {
     const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
     return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
                       __funnelshift_r(w3, w4, sh));
+}
+
+// explicit shared-memory loads on 32-bit shared-window addresses
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t a) { return __uint_as_float(lds32(a)); }
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds8(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+// 16 bytes at a 2-byte aligned shared address (Q4_128's 66-byte blocks)
+__device__ __forceinline__ uint4 lds128_a2s(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12), w4 = lds32(b + 16);
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+
+// unsigned-bytes x signed-bytes dot, accumulated (dp4a.u32.s32)
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Integer dot of a 16-byte nibble run (32 weights, low nibble = even element)
+// with a permuted 32-element x8 record: low nibbles in place against the even
+// words, high nibbles masked in place (16x their value) against the odd words,
+// combined exactly at the end.
+__device__ __forceinline__ int dot_nib32_split(uint4 w, uint4 xa, uint4 xb) {
+    const uint32_t lo = 0x0F0F0F0Fu, hi = 0xF0F0F0F0u;
+    int dl = dp4a_us(w.x & lo, xa.x, 0);
+    int dh = dp4a_us(w.x & hi, xa.y, 0);
+    dl = dp4a_us(w.y & lo, xa.z, dl);
+    dh = dp4a_us(w.y & hi, xa.w, dh);
+    dl = dp4a_us(w.z & lo, xb.x, dl);
+    dh = dp4a_us(w.z & hi, xb.y, dh);
+    dl = dp4a_us(w.w & lo, xb.z, dl);
+    dh = dp4a_us(w.w & hi, xb.w, dh);
+    return dl + (dh >> 4);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -2,19 +2,29 @@
 //
 // One kernel template serves every weight format of the reference's decode
 // path.  A weight matrix is a set of byte "streams" (preq2: quant + meta;
-// packed: nibbles + scales + biases; the block formats: one stream), each made
-// of fixed-size "units" (a 4-row band for preq2, one row otherwise).  Each CTA
-// owns a contiguous run of units, so each of its streams is ONE contiguous
-// span of HBM; a single producer thread walks that span with 1-D bulk copies
-// (cp.async.bulk, no multicast) into a ring of shared-memory stages guarded by
-// mbarriers, and consumer warps decode nibbles in registers, dot them against
-// the int8 activation with dp4a, and apply the per-group fp32 combine.
+// banded Q4_128: quant + scales; packed: nibbles + scales + biases; the
+// row-major block formats: one stream), each made of fixed-size "units"
+// (a band of 4 rows, or one row for the fp32-activation packed format).
+// Each CTA owns a contiguous run of units, so each of its streams is ONE
+// contiguous span of HBM.  A single producer thread walks that span in large
+// 1-D bulk copies (cp.async.bulk, no multicast; tens of KB per copy, which is
+// what streams HBM at full rate) into a ring of shared-memory stages guarded
+// by mbarriers, and every consumer warp takes work items from every stage.
 //
-// The activation prologue (A8 quantization, optionally preceded by RMSNorm) is
-// fused: every CTA quantizes the whole input vector into shared memory while
-// its first weight copies are in flight.  Epilogues: plain store, in-place
-// residual add, paired gate/up SiLU*up, and per-CTA argmax with a last-CTA
-// reduction.
+// Work item = (band of 4 rows, K slice, segment).  Lane l walks 32-weight
+// slices q = l, l+32, ... of all four rows at once, two slices in flight, so
+// a slice's int8 activation record is loaded once for four rows; rows are
+// visited in a lane-rotated order that keeps 128-bit shared loads bank-
+// conflict free; nibbles are masked in place (LOP3) and dotted with dp4a; a
+// 6-shuffle reduce-scatter leaves row j of the band in lane 8*j.  When a unit
+// is split in several items (K slices, or the gate and up halves of the fused
+// SiLU), the last item to finish sums the partials in a fixed order.
+//
+// The activation prologue is fused: each CTA quantizes the input vector to
+// int8 with the reference's A8 rounding (optionally after RMSNorm) while its
+// first weight stages stream in.  Programmatic dependent launch: the producer
+// starts streaming weights before griddepcontrol.wait, consumers wait before
+// touching any activation or output, so a kernel can overlap its predecessor.
 //
 // Reference formats and math (asdsl/kernels/native/):
 //   preq2  gemv_preq2_avx2.cpp:196-297    preq   gemv_q4_preq_restored.cpp:305-473
@@ -27,12 +37,13 @@
 namespace asdsl {
 
 enum WeightFormat : int {
-    kFmtPreq2 = 0,   // meta [M][ng][4] + quant [ceil(M/4)][ng][64], gs 32
-    kFmtPreq = 1,    // [M][ng][20] blocks, gs 32
-    kFmtQ4_128 = 2,  // [M][K/128][66] blocks, symmetric, implicit zero 8
-    kFmtS256 = 3,    // [M][K/256][144] blocks, 8 fp16 sub-scales, zero 8, A8 gs 32
-    kFmtQ4K = 4,     // [M][K/256][144] reference-interpretation Q4_K, own A8
-    kFmtPacked = 5,  // nibbles [M][K/2] + fp32 scales [M][ng] + fp32 biases [M][ng], fp32 x
+    kFmtPreq2 = 0,    // meta [M][ng][4] + quant [ceil(M/4)][ng][64], gs 32
+    kFmtPreq = 1,     // [M][ng][20] blocks, gs 32
+    kFmtQ4_128 = 2,   // [M][K/128][66] blocks, symmetric, implicit zero 8 (reference bytes)
+    kFmtS256 = 3,     // [M][K/256][144] blocks, 8 fp16 sub-scales, zero 8, A8 gs 32
+    kFmtQ4K = 4,      // [M][K/256][144] reference-interpretation Q4_K, own A8
+    kFmtPacked = 5,   // nibbles [M][K/2] + fp32 scales [M][ng] + fp32 biases [M][ng], fp32 x
+    kFmtQ128B = 6,    // banded Q4_128: quant [nb][K/128][4][64] + scales [nb][K/128][4] fp16
 };
 
 enum Prologue : int {
@@ -50,11 +61,27 @@ enum Epilogue : int {
     kEpiArgmax = 3,  // y[row] = v (optional) + global first-max argmax
 };
 
-constexpr int kConsumerWarps = 8;
+// measured on B200 (decode chains and lm_head): one 17-warp CTA per SM with
+// 64 KB stages beats two 9-warp CTAs
+#ifndef ASDSL_CONSUMER_WARPS
+#define ASDSL_CONSUMER_WARPS 16
+#endif
+#ifndef ASDSL_CTAS_PER_SM
+#define ASDSL_CTAS_PER_SM 1
+#endif
+constexpr int kConsumerWarps = ASDSL_CONSUMER_WARPS;
+constexpr int kCtasPerSm = ASDSL_CTAS_PER_SM;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);  // + one producer warp
 constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kMaxStages = 16;
+constexpr int kConsumerThreads = 32 * kConsumerWarps;
+constexpr int kMaxStages = 24;
 constexpr int kMaxStreams = 3;
+
+template <int FMT>
+struct FmtTraits {
+    static constexpr int kStreams = (FMT == kFmtPreq2 || FMT == kFmtQ128B) ? 2 : (FMT == kFmtPacked ? 3 : 1);
+    static constexpr int kRowsPerUnit = (FMT == kFmtPacked) ? 1 : 4;
+};
 
 struct StreamDesc {
     const uint8_t* base;   // 16-byte aligned
@@ -66,15 +93,19 @@ struct StreamDesc {
 
 struct PipeArgs {
     StreamDesc s[kMaxStreams];
-    int n_streams;
     int n_units;          // units per segment
-    int pair_unit_off;    // > 0: paired (gate/up) mode, segment 1 starts this many units later
+    int pair_unit_off;    // paired (gate/up) mode: segment 1 starts this many units later
     int units_per_chunk;
     int n_stages;
+    int k_parts;          // work items per unit and segment: the K range in k_parts slices
+    int q_bounds[9];      // slice boundaries (in 32-weight slices) of the k_parts parts
+    float inv_ipu;        // 1 / (k_parts * segments), for division-free item indexing
     uint32_t seg_bytes;   // bytes of one segment inside a stage
     uint32_t stage_bytes; // bytes of one stage (1 or 2 segments)
     uint32_t xarea_off;   // dynamic smem offsets
     uint32_t stage_off;
+    uint32_t split_off;   // K-split / segment-split partials
+    int row_bytes;        // row-major block formats: bytes of one row
 };
 
 struct GemvArgs {
@@ -85,7 +116,7 @@ struct GemvArgs {
     float eps;
     int K;                 // in_features
     int M;                 // out rows (per segment)
-    int gs;                // activation group size (32, or 128 for Q4_128)
+    int gs;                // activation group size (32, or 128 for the Q4_128 formats)
     float* y;
     float* resid;
     float* h;
@@ -125,64 +156,88 @@ __device__ __forceinline__ Span chunk_span(const StreamDesc& sd, long long u_beg
 }
 
 // ---------------------------------------------------------------------------
-// activation prologue: x -> shared memory
-// x8 (permuted per 32-group), xs[ng], xsi[ng] (int sums), xss[ng] (sum*scale)
-// or, for kProF32, xf[K] floats + sx[ng] group sums.
-// Runs on the consumer warps only; `nthreads` = consumer threads.
+// shared-memory activation area
+//   x8[K]      int8 codes, permuted per 32-slice (see x8_perm_offset)
+//   xs[K/32]   A8 scale of each 32-slice's group (replicated for gs 128)
+//   xss[K/32]  (float)sum(codes of the slice) * xs
+//   xsi[K/32]  sum(codes of the slice)
+//   red[32]    reduction scratch
+//   kProF32:   xf[K] fp32 x and sx[K/gs] per-group sums instead of the codes
 // ---------------------------------------------------------------------------
 struct XArea {
+    float* xf;
     int8_t* x8;
     float* xs;
-    int* xsi;
     float* xss;
-    float* xf;
+    int* xsi;
     float* sx;
-    float* red;  // reduction scratch (kConsumerWarps floats)
+    float* red;
 };
 
-__device__ __forceinline__ XArea xarea_layout(uint8_t* base, int K, int pro, int gs) {
+// the same area as 32-bit shared-window addresses (for explicit ld.shared)
+struct XAddr {
+    uint32_t x8, xs, xss, xsi;
+};
+
+__host__ __device__ __forceinline__ uint32_t xarea_layout_bytes(int K, int gs, bool f32) {
+    const uint32_t nq = static_cast<uint32_t>(K / 32);
+    const uint32_t ng = static_cast<uint32_t>(K / gs);
+    uint32_t b = f32 ? 4u * K + 4u * ng : ((static_cast<uint32_t>(K) + 15u) & ~15u) + 12u * nq;
+    b = (b + 15u) & ~15u;
+    b += 4u * 32u;  // red
+    return (b + 127u) & ~127u;
+}
+
+__device__ __forceinline__ XArea xarea_layout(uint8_t* base, int K, int gs, bool f32) {
     XArea a;
+    const int nq = K / 32;
     const int ng = K / gs;
-    if (pro == kProF32) {
-        a.xf = reinterpret_cast<float*>(base);
+    uint8_t* p = base;
+    if (f32) {
+        a.xf = reinterpret_cast<float*>(p);
         a.sx = a.xf + K;
-        a.red = a.sx + ng;
+        p = reinterpret_cast<uint8_t*>(a.sx + ng);
         a.x8 = nullptr;
-        a.xs = nullptr;
+        a.xs = a.xss = nullptr;
         a.xsi = nullptr;
-        a.xss = nullptr;
     } else {
-        a.x8 = reinterpret_cast<int8_t*>(base);
-        a.xs = reinterpret_cast<float*>(base + ((K + 15) & ~15));
-        a.xsi = reinterpret_cast<int*>(a.xs + ng);
-        a.xss = reinterpret_cast<float*>(a.xsi + ng);
-        a.red = a.xss + ng;
         a.xf = nullptr;
         a.sx = nullptr;
+        a.x8 = reinterpret_cast<int8_t*>(p);
+        p += (K + 15) & ~15;
+        a.xs = reinterpret_cast<float*>(p);
+        a.xss = a.xs + nq;
+        a.xsi = reinterpret_cast<int*>(a.xss + nq);
+        p = reinterpret_cast<uint8_t*>(a.xsi + nq);
     }
+    uintptr_t r = reinterpret_cast<uintptr_t>(p);
+    r = (r + 15) & ~uintptr_t(15);
+    a.red = reinterpret_cast<float*>(r);
     return a;
 }
 
 __device__ __forceinline__ void consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory");
 }
 
-// Fused activation prologue.  The A8 rounding is the reference's compiled
-// rounding (see common.cuh); with gs = 128 each 128-group is quantized as one
-// group but stored as four permuted 32-records.
+// ---------------------------------------------------------------------------
+// fused activation prologue (consumer warps), straight from global memory.
+// Quad-parallel: each thread owns 4 consecutive elements; an A8 group of gs
+// elements is gs/4 consecutive threads of one warp.
+// ---------------------------------------------------------------------------
 template <int PRO>
-__device__ void run_prologue(const GemvArgs& ga, XArea xa, int cw, int lane) {
+__device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
     const int K = ga.K;
-    const int gs = ga.gs;
-    const int ng = K / gs;
-    const int ctid = cw * 32 + lane;
-    const int nthr = kConsumerWarps * 32;
+    const int lane = ctid & 31;
 
     if constexpr (PRO == kProF32) {
-        for (int i = ctid; i < K; i += nthr) xa.xf[i] = __ldg(ga.x + i);
+        for (int i = ctid * 4; i < K; i += kConsumerThreads * 4)
+            *reinterpret_cast<float4*>(xa.xf + i) = __ldg(reinterpret_cast<const float4*>(ga.x + i));
         consumer_sync();
-        // group sums in the reference's 8-lane order (gemv_q4_avx2.cpp:677-685)
-        for (int g = ctid; g < ng; g += nthr) {
+        // per-group sums in the reference's 8-lane order (gemv_q4_avx2.cpp:677-685)
+        const int gs = ga.gs;
+        const int ng = K / gs;
+        for (int g = ctid; g < ng; g += kConsumerThreads) {
             float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             for (int j = 0; j < gs; j += 8)
 #pragma unroll
@@ -195,96 +250,107 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int cw, int lane) {
         consumer_sync();
         return;
     } else {
+        const int nquads = K >> 2;
         float inv_rms = 1.0f;
         if constexpr (PRO == kProRmsA8) {
-            // sum of squares -> inv = 1/sqrt(sum/n + eps)  (unified_engine.cpp:499-513)
+            // inv = 1/sqrt(sum(x^2)/n + eps)  (unified_engine.cpp:499-513)
             float ss = 0.0f;
-            for (int i = ctid; i < K; i += nthr) {
-                const float v = __ldg(ga.x + i);
-                ss = __fmaf_rn(v, v, ss);
+            for (int t = ctid; t < nquads; t += kConsumerThreads) {
+                const float4 f = __ldg(reinterpret_cast<const float4*>(ga.x) + t);
+                ss = __fmaf_rn(f.x, f.x, ss);
+                ss = __fmaf_rn(f.y, f.y, ss);
+                ss = __fmaf_rn(f.z, f.z, ss);
+                ss = __fmaf_rn(f.w, f.w, ss);
             }
             ss = warp_sum(ss);
-            if (lane == 0) xa.red[cw] = ss;
+            if (lane == 0) xa.red[ctid >> 5] = ss;
             consumer_sync();
             float tot = 0.0f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) tot = __fadd_rn(tot, xa.red[w]);
             inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), ga.eps)));
         }
-        // one warp per 32-element sub-group; groups of 128 reduce over 4 warps' worth
-        // of sub-groups, so iterate by activation group and let each lane own
-        // gs/32 elements.
-        const int sub = gs / 32;  // 1 or 4
-        for (int g = cw; g < ng; g += kConsumerWarps) {
-            float v[4];
-            float amax = 0.0f;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                if (s < sub) {
-                    const int idx = g * gs + s * 32 + lane;
-                    float t;
-                    if constexpr (PRO == kProQ8) {
-                        t = 0.0f;
-                    } else {
-                        t = __ldg(ga.x + idx);
-                        if constexpr (PRO == kProRmsA8) t = __fmul_rn(__fmul_rn(t, inv_rms), __ldg(ga.norm_w + idx));
-                    }
-                    v[s] = t;
-                    amax = fmaxf(amax, fabsf(t));
-                } else {
-                    v[s] = 0.0f;
-                }
-            }
-            int qs[4];
-            float scale;
+        const int gs = ga.gs;   // 32 or 128
+        const int tpg = gs >> 2;  // threads per A8 group: 8 or 32
+#pragma unroll 2
+        for (int base = 0; base < nquads; base += kConsumerThreads) {
+            const int t = base + ctid;  // quad index (uniform trip count across the warp)
+            const bool live = t < nquads;
+            const int e0 = t * 4;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            int c[4] = {0, 0, 0, 0};
+            float scale = 1.0f;
             if constexpr (PRO == kProQ8) {
-                scale = __ldg(ga.xs_in + g);
-#pragma unroll
-                for (int s = 0; s < 4; ++s) qs[s] = (s < sub) ? static_cast<int>(__ldg(ga.xq + g * gs + s * 32 + lane)) : 0;
-            } else if constexpr (PRO == kProQ4K) {
-                // gemv_q4_avx2.cpp:377-400: amax < 1e-12 -> scale 0, codes 0;
-                // q = clamp(round_half_away(x * 127/amax), -127, 127)
-                amax = warp_max(amax);
-                if (amax < 1e-12f) {
-                    scale = 0.0f;
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) qs[s] = 0;
-                } else {
-                    const float inv = __fdiv_rn(127.0f, amax);
-                    scale = __fmul_rn(amax, inv127f());
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        int q = static_cast<int>(roundf(__fmul_rn(v[s], inv)));
-                        q = q > 127 ? 127 : (q < -127 ? -127 : q);
-                        qs[s] = q;
-                    }
+                if (live) {
+                    const char4 q4 = *reinterpret_cast<const char4*>(ga.xq + e0);
+                    c[0] = q4.x;
+                    c[1] = q4.y;
+                    c[2] = q4.z;
+                    c[3] = q4.w;
+                    scale = __ldg(ga.xs_in + e0 / gs);
                 }
             } else {
-                amax = warp_max(amax);
-                if (amax < 1e-9f) {
-                    scale = 1.0f;
+                if (live) {
+                    const float4 f = __ldg(reinterpret_cast<const float4*>(ga.x) + t);
+                    v[0] = f.x;
+                    v[1] = f.y;
+                    v[2] = f.z;
+                    v[3] = f.w;
+                    if constexpr (PRO == kProRmsA8) {
+                        const float4 w = __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
+                        v[0] = __fmul_rn(__fmul_rn(v[0], inv_rms), w.x);
+                        v[1] = __fmul_rn(__fmul_rn(v[1], inv_rms), w.y);
+                        v[2] = __fmul_rn(__fmul_rn(v[2], inv_rms), w.z);
+                        v[3] = __fmul_rn(__fmul_rn(v[3], inv_rms), w.w);
+                    }
+                }
+                float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+                for (int o = 1; o < tpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                if constexpr (PRO == kProQ4K) {
+                    // gemv_q4_avx2.cpp:377-400: amax < 1e-12 -> scale 0, codes 0;
+                    // q = clamp(round_half_away(x * 127/amax), -127, 127)
+                    if (amax < 1e-12f) {
+                        scale = 0.0f;
+                    } else {
+                        const float inv = __fdiv_rn(127.0f, amax);
+                        scale = __fmul_rn(amax, inv127f());
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) qs[s] = 0;
+                        for (int j = 0; j < 4; ++j) {
+                            int q = static_cast<int>(roundf(__fmul_rn(v[j], inv)));
+                            c[j] = q > 127 ? 127 : (q < -127 ? -127 : q);
+                        }
+                    }
                 } else {
-                    const float inv = __fdiv_rn(127.0f, amax);
-                    scale = __fmul_rn(amax, inv127f());
+                    // gemv_q4_preq_restored.cpp:529-547
+                    if (amax < 1e-9f) {
+                        scale = 1.0f;
+                    } else {
+                        const float inv = __fdiv_rn(127.0f, amax);
+                        scale = __fmul_rn(amax, inv127f());
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) qs[s] = a8_code(v[s], inv);
+                        for (int j = 0; j < 4; ++j) c[j] = a8_code(v[j], inv);
+                    }
                 }
             }
-            int qsum = 0;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                if (s < sub) {
-                    xa.x8[(g * sub + s) * 32 + x8_perm_offset(lane)] = static_cast<int8_t>(qs[s]);
-                    qsum += qs[s];
-                }
+            if (live) {
+                // quad (4 consecutive elements, first one even) -> even word gets c0, c2 and the odd
+                // word c1, c3 at byte (e0 & 7) / 2 (see x8_perm_offset)
+                const int w8 = (e0 & ~31) + ((e0 & 31) >> 3) * 8 + ((e0 & 7) >> 1);
+                *reinterpret_cast<uint16_t*>(xa.x8 + w8) =
+                    static_cast<uint16_t>((c[0] & 0xFF) | ((c[2] & 0xFF) << 8));
+                *reinterpret_cast<uint16_t*>(xa.x8 + w8 + 4) =
+                    static_cast<uint16_t>((c[1] & 0xFF) | ((c[3] & 0xFF) << 8));
             }
-            qsum = warp_sum_i(qsum);
-            if (lane == 0) {
-                xa.xs[g] = scale;
-                xa.xsi[g] = qsum;
-                xa.xss[g] = __fmul_rn(static_cast<float>(qsum), scale);
+            // per 32-slice sums (8 quads)
+            int s = c[0] + c[1] + c[2] + c[3];
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s += __shfl_xor_sync(0xffffffffu, s, 4);
+            if (live && (t & 7) == 0) {
+                const int q = e0 >> 5;
+                xa.xs[q] = scale;
+                xa.xsi[q] = s;
+                xa.xss[q] = __fmul_rn(static_cast<float>(s), scale);
             }
         }
         consumer_sync();
@@ -292,167 +358,192 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int cw, int lane) {
 }
 
 // ---------------------------------------------------------------------------
-// per-unit compute.  Each returns the row values for the unit in lanes:
-//   preq2: lanes 0..3 hold rows band*4 + lane (after reduction)
-//   row formats: all lanes hold the row value (after reduction)
+// band compute: 4 rows x K slices [q0, q1).  Accumulates into a[r] the lane's
+// partial (acc - corr) of row (r + rot) & 3.
 // ---------------------------------------------------------------------------
+struct SliceData {
+    uint4 xa, xb;
+    float xs, xss;
+    int xsi;
+    uint4 w[4];
+    uint32_t m[4];  // per-row scale (and zero) bits, or the Q4_K block address
+};
 
-// preq2 band: lane -> (group g0 + lane/4, row slot lane%4)
-__device__ __forceinline__ float unit_preq2(const uint8_t* q, const uint8_t* m, int ng, const XArea& xa,
-                                            int lane) {
-    const int slot = lane & 3;
-    const int gl = lane >> 2;
-    float acc = 0.0f, corr = 0.0f;
-    const uint8_t* mrow = m + slot * ng * 4;
-    for (int g0 = 0; g0 < ng; g0 += 8) {
-        const int g = g0 + gl;
-        if (g < ng) {
-            const uint4 w = *reinterpret_cast<const uint4*>(q + g * 64 + slot * 16);
-            const uint32_t mw = *reinterpret_cast<const uint32_t*>(mrow + g * 4);
-            const uint4 xa4 = *reinterpret_cast<const uint4*>(xa.x8 + g * 32);
-            const uint4 xb4 = *reinterpret_cast<const uint4*>(xa.x8 + g * 32 + 16);
-            const int d = dot_nib32(w, xa4, xb4, 0);
-            const float ws = half_bits_to_float(mw);
-            const float wz = half_bits_to_float(mw >> 16);
-            const float comb = __fmul_rn(ws, xa.xs[g]);
-            acc = __fmaf_rn(static_cast<float>(d), comb, acc);
-            corr = __fmaf_rn(__fmul_rn(wz, ws), xa.xss[g], corr);
-        }
-    }
+template <int FMT>
+__device__ __forceinline__ void slice_load(SliceData& d, uint32_t s0, uint32_t s1, int nq, int rs, const XAddr& xs,
+                                           const uint32_t rr[4], int q) {
+    const uint32_t uq = static_cast<uint32_t>(q);
+    const uint32_t xr = xs.x8 + uq * 32u;
+    d.xa = lds128(xr);
+    d.xb = lds128(xr + 16);
+    d.xs = ldsf(xs.xs + 4u * uq);
+    d.xss = ldsf(xs.xss + 4u * uq);
+    if constexpr (FMT == kFmtQ4K) d.xsi = static_cast<int>(lds32(xs.xsi + 4u * uq));
 #pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-        acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        corr += __shfl_xor_sync(0xffffffffu, corr, o);
-    }
-    return acc - corr;
-}
-
-// preq row: 20-byte blocks at 4-byte aligned addresses; lane -> group
-__device__ __forceinline__ float unit_preq(const uint8_t* row, int ng, const XArea& xa, int lane) {
-    float acc = 0.0f, corr = 0.0f;
-    for (int g = lane; g < ng; g += 32) {
-        const uint32_t* b = reinterpret_cast<const uint32_t*>(row + g * 20);
-        const uint32_t m = b[0];
-        const uint4 w = make_uint4(b[1], b[2], b[3], b[4]);
-        const uint4 xa4 = *reinterpret_cast<const uint4*>(xa.x8 + g * 32);
-        const uint4 xb4 = *reinterpret_cast<const uint4*>(xa.x8 + g * 32 + 16);
-        const int d = dot_nib32(w, xa4, xb4, 0);
-        const float ws = half_bits_to_float(m), wz = half_bits_to_float(m >> 16);
-        const float xs = xa.xs[g];
-        acc = __fmaf_rn(static_cast<float>(d), __fmul_rn(ws, xs), acc);
-        corr = __fadd_rn(corr, __fmul_rn(__fmul_rn(__fmul_rn(wz, static_cast<float>(xa.xsi[g])), ws), xs));
-    }
-    acc = warp_sum(acc);
-    corr = warp_sum(corr);
-    return acc - corr;
-}
-
-// Q4_128 row: 66-byte blocks; 4 lanes per block (16 nibble bytes each)
-__device__ __forceinline__ float unit_q4_128(const uint8_t* row, int ng, const XArea& xa, int lane) {
-    const int c = lane & 3;
-    float acc = 0.0f, corr = 0.0f;
-    for (int g0 = 0; g0 < ng; g0 += 8) {
-        const int g = g0 + (lane >> 2);
-        int d = 0;
-        float comb = 0.0f;
-        if (g < ng) {
-            const uint8_t* blk = row + g * 66;
-            const uint4 w = lds128_a2(blk + 2 + c * 16);
-            const int8_t* xr = xa.x8 + (g * 4 + c) * 32;
-            d = dot_nib32(w, *reinterpret_cast<const uint4*>(xr), *reinterpret_cast<const uint4*>(xr + 16), 0);
-            const uint16_t sb = *reinterpret_cast<const uint16_t*>(blk);
-            comb = __fmul_rn(half_bits_to_float(sb), xa.xs[g]);
-        }
-        d += __shfl_xor_sync(0xffffffffu, d, 1);
-        d += __shfl_xor_sync(0xffffffffu, d, 2);
-        if (g < ng && c == 0) {
-            acc = __fmaf_rn(static_cast<float>(d), comb, acc);
-            corr = __fmaf_rn(__fmul_rn(8.0f, static_cast<float>(xa.xsi[g])), comb, corr);
+    for (int r = 0; r < 4; ++r) {
+        const uint32_t row = rr[r];
+        if constexpr (FMT == kFmtPreq2) {
+            // quant band: [ng][4 rows][16 B]; meta band: [4 rows][ng][4 B]
+            d.w[r] = lds128(s0 + uq * 64u + row * 16u);
+            d.m[r] = lds32(s1 + row * static_cast<uint32_t>(nq) * 4u + uq * 4u);
+        } else if constexpr (FMT == kFmtQ128B) {
+            // quant band: [K/128][4 rows][64 B]; scales band: [K/128][4 rows] fp16
+            const uint32_t g = uq >> 2, cq = uq & 3u;
+            d.w[r] = lds128(s0 + g * 256u + row * 64u + cq * 16u);
+            d.m[r] = lds16(s1 + g * 8u + row * 2u);
+        } else if constexpr (FMT == kFmtQ4_128) {
+            const uint32_t g = uq >> 2, cq = uq & 3u;
+            const uint32_t blk = s0 + row * static_cast<uint32_t>(rs) + g * 66u;
+            d.w[r] = lds128_a2s(blk + 2u + cq * 16u);
+            d.m[r] = lds16(blk);
+        } else if constexpr (FMT == kFmtPreq) {
+            const uint32_t b = s0 + row * static_cast<uint32_t>(rs) + uq * 20u;
+            d.m[r] = lds32(b);
+            d.w[r] = make_uint4(lds32(b + 4), lds32(b + 8), lds32(b + 12), lds32(b + 16));
+        } else if constexpr (FMT == kFmtS256) {
+            const uint32_t k8 = uq & 7u;
+            const uint32_t blk = s0 + row * static_cast<uint32_t>(rs) + (uq >> 3) * 144u;
+            d.w[r] = lds128(blk + 16u + k8 * 16u);
+            d.m[r] = lds16(blk + 2u * k8);
+        } else if constexpr (FMT == kFmtQ4K) {
+            const uint32_t sb = uq & 7u;
+            const uint32_t blk = s0 + row * static_cast<uint32_t>(rs) + (uq >> 3) * 144u;
+            d.w[r] = lds128(blk + 16u + sb * 16u);
+            d.m[r] = blk;  // block address: scales are unpacked in slice_math
         }
     }
-    acc = warp_sum(acc);
-    corr = warp_sum(corr);
-    return acc - corr;
 }
 
-// S256 row: 144-byte super-blocks, lane -> 32-weight sub-block
-__device__ __forceinline__ float unit_s256(const uint8_t* row, int nsb, const XArea& xa, int lane) {
-    float acc = 0.0f, corr = 0.0f;
-    const int nsub = nsb * 8;
-    for (int t = lane; t < nsub; t += 32) {
-        const int sb = t >> 3, k = t & 7;
-        const uint8_t* blk = row + sb * 144;
-        const uint4 w = *reinterpret_cast<const uint4*>(blk + 16 + k * 16);
-        const uint16_t sh = *reinterpret_cast<const uint16_t*>(blk + 2 * k);
-        const int8_t* xr = xa.x8 + t * 32;
-        const int d = dot_nib32(w, *reinterpret_cast<const uint4*>(xr), *reinterpret_cast<const uint4*>(xr + 16), 0);
-        const float sc = __fmul_rn(half_bits_to_float(sh), xa.xs[t]);
-        acc = __fmaf_rn(static_cast<float>(d), sc, acc);
-        corr = __fmaf_rn(__fmul_rn(8.0f, static_cast<float>(xa.xsi[t])), sc, corr);
+template <int FMT>
+__device__ __forceinline__ void slice_math(float a[4], const SliceData& d, uint32_t q) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int dot = dot_nib32_split(d.w[r], d.xa, d.xb);
+        if constexpr (FMT == kFmtPreq2 || FMT == kFmtPreq) {
+            const float ws = half_bits_to_float(d.m[r]), wz = half_bits_to_float(d.m[r] >> 16);
+            a[r] = __fmaf_rn(static_cast<float>(dot), __fmul_rn(ws, d.xs), a[r]);
+            a[r] = __fmaf_rn(-__fmul_rn(wz, ws), d.xss, a[r]);
+        } else if constexpr (FMT == kFmtQ4K) {
+            // reference Q4_K sub-block (gemv_q4_avx2.cpp:294-329): 6-bit LE bitstream values
+            // sb (scale) and sb + 8 (min) of the super-block at d.m[r]
+            const uint32_t blk = d.m[r];
+            const uint32_t sb = q & 7u;
+            const uint32_t dd = lds32(blk);
+            const float dsc = half_bits_to_float(dd), dmin = half_bits_to_float(dd >> 16);
+            auto get6 = [&](uint32_t idx) -> int {
+                const uint32_t bit = idx * 6u, byte = bit >> 3, off = bit & 7u;
+                const uint32_t lo = lds8(blk + 4u + byte);
+                if (off <= 2) return static_cast<int>((lo >> off) & 0x3Fu);
+                return static_cast<int>(((lo >> off) | (lds8(blk + 5u + byte) << (8u - off))) & 0x3Fu);
+            };
+            const float sub_scale = __fmul_rn(dsc, static_cast<float>(get6(sb)));
+            const float sub_min = __fmul_rn(dmin, static_cast<float>(get6(sb + 8u)));
+            const float part = __fsub_rn(__fmul_rn(sub_scale, static_cast<float>(dot)),
+                                         __fmul_rn(sub_min, static_cast<float>(d.xsi)));
+            a[r] = __fmaf_rn(part, d.xs, a[r]);
+        } else {
+            // symmetric formats: implicit zero 8 (Q4_128, S256)
+            const float ws = half_bits_to_float(d.m[r]);
+            a[r] = __fmaf_rn(static_cast<float>(dot), __fmul_rn(ws, d.xs), a[r]);
+            a[r] = __fmaf_rn(-__fmul_rn(8.0f, ws), d.xss, a[r]);
+        }
     }
-    acc = warp_sum(acc);
-    corr = warp_sum(corr);
-    return acc - corr;
 }
 
-// Q4_K row (reference interpretation, gemv_q4_avx2.cpp:283-329)
-__device__ __forceinline__ int get6_bits(const uint8_t* p, int idx) {
-    const int bit = idx * 6, byte = bit >> 3, off = bit & 7;
-    const int lo = p[byte];
-    if (off <= 2) return (lo >> off) & 0x3F;
-    return ((lo >> off) | (p[byte + 1] << (8 - off))) & 0x3F;
-}
-
-__device__ __forceinline__ float unit_q4k(const uint8_t* row, int nb, const XArea& xa, int lane) {
-    float acc = 0.0f;
-    const int nsub = nb * 8;
-    for (int t = lane; t < nsub; t += 32) {
-        const int b = t >> 3, sb = t & 7;
-        const uint8_t* blk = row + b * 144;
-        const uint32_t dd = *reinterpret_cast<const uint32_t*>(blk);
-        const float d = half_bits_to_float(dd), dmin = half_bits_to_float(dd >> 16);
-        const float sub_scale = __fmul_rn(d, static_cast<float>(get6_bits(blk + 4, sb)));
-        const float sub_min = __fmul_rn(dmin, static_cast<float>(get6_bits(blk + 4, sb + 8)));
-        const uint4 w = *reinterpret_cast<const uint4*>(blk + 16 + sb * 16);
-        const int8_t* xr = xa.x8 + t * 32;
-        const int dot = dot_nib32(w, *reinterpret_cast<const uint4*>(xr), *reinterpret_cast<const uint4*>(xr + 16), 0);
-        const float part = __fsub_rn(__fmul_rn(sub_scale, static_cast<float>(dot)),
-                                     __fmul_rn(sub_min, static_cast<float>(xa.xsi[t])));
-        acc = __fmaf_rn(part, xa.xs[t], acc);
+template <int FMT>
+__device__ __forceinline__ void band_compute(float a[4], uint32_t s0, uint32_t s1, int K, int rs, const XAddr& xs,
+                                             int lane, int rot, int q0, int q1) {
+    const int nq = K >> 5;
+    const uint32_t rr[4] = {static_cast<uint32_t>(rot & 3), static_cast<uint32_t>((rot + 1) & 3),
+                            static_cast<uint32_t>((rot + 2) & 3), static_cast<uint32_t>((rot + 3) & 3)};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) a[r] = 0.0f;
+    // two slices in flight: load both, then do the math
+    int q = q0 + lane;
+    for (; q + 32 < q1; q += 64) {
+        SliceData d0, d1;
+        slice_load<FMT>(d0, s0, s1, nq, rs, xs, rr, q);
+        slice_load<FMT>(d1, s0, s1, nq, rs, xs, rr, q + 32);
+        slice_math<FMT>(a, d0, static_cast<uint32_t>(q));
+        slice_math<FMT>(a, d1, static_cast<uint32_t>(q + 32));
     }
-    return warp_sum(acc);
+    if (q < q1) {
+        SliceData d0;
+        slice_load<FMT>(d0, s0, s1, nq, rs, xs, rr, q);
+        slice_math<FMT>(a, d0, static_cast<uint32_t>(q));
+    }
+}
+
+// rotate a lane's four partials back to row order: v[j] = a[(j - rot) & 3]
+__device__ __forceinline__ void unrotate(float a[4], int rot) {
+    if (rot & 1) {
+        const float t = a[3];
+        a[3] = a[2];
+        a[2] = a[1];
+        a[1] = a[0];
+        a[0] = t;
+    }
+    if (rot & 2) {
+        float t = a[0];
+        a[0] = a[2];
+        a[2] = t;
+        t = a[1];
+        a[1] = a[3];
+        a[3] = t;
+    }
+}
+
+// reduce-scatter of four per-lane values over the warp: returns, in lane l,
+// the warp sum of value j = l >> 3 (rows 0..3 land in lanes 0, 8, 16, 24).
+__device__ __forceinline__ float reduce4(const float v[4], int lane) {
+    const bool hi16 = lane & 16;
+    const float s0 = hi16 ? v[0] : v[2];
+    const float s1 = hi16 ? v[1] : v[3];
+    const float r0 = __shfl_xor_sync(0xffffffffu, s0, 16);
+    const float r1 = __shfl_xor_sync(0xffffffffu, s1, 16);
+    const float k0 = (hi16 ? v[2] : v[0]) + r0;
+    const float k1 = (hi16 ? v[3] : v[1]) + r1;
+    const bool hi8 = lane & 8;
+    const float r = __shfl_xor_sync(0xffffffffu, hi8 ? k0 : k1, 8);
+    float k = (hi8 ? k1 : k0) + r;
+    k += __shfl_xor_sync(0xffffffffu, k, 4);
+    k += __shfl_xor_sync(0xffffffffu, k, 2);
+    k += __shfl_xor_sync(0xffffffffu, k, 1);
+    return k;
 }
 
 // packed W4A32 row (no activation quantization): y = sum_g dot_f32 * s + b * sum(x_g)
 __device__ __forceinline__ float unit_packed(const uint8_t* wrow, const float* srow, const float* brow, int K,
                                              int gs, const XArea& xa, int lane) {
-    // lane -> 8 consecutive weights (4 bytes) per step; groups are gs/8 lanes wide
-    const int ng = K / gs;
     float acc = 0.0f;
     const int lanes_per_group = gs / 8;  // gs multiple of 8 (checked on host)
+    const bool shuffle_ok = (256 % gs) == 0;
     for (int base = 0; base < K; base += 256) {
         const int k = base + lane * 8;
         float d = 0.0f;
         int g = -1;
         if (k < K) {
             const uint32_t w = *reinterpret_cast<const uint32_t*>(wrow + (k >> 1));
-            const float* xp = xa.xf + k;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) d = __fmaf_rn(static_cast<float>((w >> (4 * e)) & 0xF), xp[e], d);
+            const float4 x0 = *reinterpret_cast<const float4*>(xa.xf + k);
+            const float4 x1 = *reinterpret_cast<const float4*>(xa.xf + k + 4);
+            d = __fmaf_rn(static_cast<float>(w & 0xF), x0.x, d);
+            d = __fmaf_rn(static_cast<float>((w >> 4) & 0xF), x0.y, d);
+            d = __fmaf_rn(static_cast<float>((w >> 8) & 0xF), x0.z, d);
+            d = __fmaf_rn(static_cast<float>((w >> 12) & 0xF), x0.w, d);
+            d = __fmaf_rn(static_cast<float>((w >> 16) & 0xF), x1.x, d);
+            d = __fmaf_rn(static_cast<float>((w >> 20) & 0xF), x1.y, d);
+            d = __fmaf_rn(static_cast<float>((w >> 24) & 0xF), x1.z, d);
+            d = __fmaf_rn(static_cast<float>(w >> 28), x1.w, d);
             g = k / gs;
         }
-        // combine lanes of the same group (groups never straddle a 256-weight step
-        // when 256 % gs == 0; otherwise fall back to per-lane scaling)
-        if ((256 % gs) == 0 && lanes_per_group <= 32) {
+        if (shuffle_ok) {
             for (int o = 1; o < lanes_per_group; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-            if (g >= 0 && (lane % lanes_per_group) == 0)
-                acc += __fmaf_rn(d, srow[g], __fmul_rn(brow[g], xa.sx[g]));
+            if (g >= 0 && (lane % lanes_per_group) == 0) acc += __fmaf_rn(d, srow[g], __fmul_rn(brow[g], xa.sx[g]));
         } else if (g >= 0) {
             acc = __fmaf_rn(d, srow[g], acc);
             if ((k % gs) == 0) acc = __fmaf_rn(brow[g], xa.sx[g], acc);
         }
     }
-    (void)ng;
     return warp_sum(acc);
 }
 
@@ -490,55 +581,80 @@ __device__ __forceinline__ void argmax_take(float& bv, int& bi, float v, int i) 
 // the kernel
 // ---------------------------------------------------------------------------
 template <int FMT, int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
+    using T = FmtTraits<FMT>;
+    constexpr int NS = T::kStreams;
+    constexpr int NSEG = (EPI == kEpiSilu) ? 2 : 1;
+    constexpr bool kF32 = (PRO == kProF32);
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     uint8_t* stages = smem + pa.stage_off;
     const int S = pa.n_stages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    XArea xa = xarea_layout(smem + pa.xarea_off, ga.K, ga.gs, kF32);
 
     const long long U = pa.n_units;
     const long long u0 = U * blockIdx.x / gridDim.x;
     const long long u1 = U * (blockIdx.x + 1) / gridDim.x;
     const int CU = pa.units_per_chunk;
+    const int P = pa.k_parts;
+    const int IPU = P * NSEG;  // work items per unit
     const int n_chunks = static_cast<int>((u1 - u0 + CU - 1) / CU);
-    const int nseg = pa.pair_unit_off > 0 ? 2 : 1;
+    // split partials [stage][unit in chunk][item][row] and per-unit arrival counts
+    float* s_part = reinterpret_cast<float*>(smem + pa.split_off);
+    int* s_cnt = reinterpret_cast<int*>(s_part + S * CU * IPU * 4);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
         }
         fence_mbar_init();
     }
+    if (IPU > 1)
+        for (int i = threadIdx.x; i < S * CU; i += blockDim.x) s_cnt[i] = 0;
     __syncthreads();
+    // let a dependent kernel launch now; it touches our outputs only after its own wait
+    grid_launch_dependents();
 
     if (warp == kProducerWarp) {
         if (lane != 0) return;
+        // weights never depend on the previous kernel: stream them before its completion
         const uint64_t pol = l2_policy_evict_first();
         int issued = 0;
-        bool ok = true;
         for (int j = 0; j < n_chunks; ++j) {
             const int s = j % S;
             const int use = j / S;
             if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
                 atomicOr(ga.status, kStatusWaitEmpty);
-                ok = false;
                 break;
             }
             const long long cb = u0 + static_cast<long long>(j) * CU;
             const long long ce = (cb + CU < u1) ? cb + CU : u1;
+            uint8_t* st = stages + static_cast<size_t>(s) * pa.stage_bytes;
             uint32_t tx = 0;
-            for (int seg = 0; seg < nseg; ++seg)
-                for (int i = 0; i < pa.n_streams; ++i) {
+            bool tail = false;
+#pragma unroll
+            for (int seg = 0; seg < NSEG; ++seg)
+#pragma unroll
+                for (int i = 0; i < NS; ++i) {
                     const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
                     tx += static_cast<uint32_t>(sp.a1 - sp.a0);
+                    // bytes past the stream's last 16-byte boundary: plain loads by this thread
+                    const long long t0 = sp.a1 > sp.start ? sp.a1 : sp.start;
+                    uint8_t* region = st + seg * pa.seg_bytes + pa.s[i].region_off;
+                    for (long long t = t0; t < sp.end; ++t) {
+                        region[t - sp.a0] = pa.s[i].base[t];
+                        tail = true;
+                    }
                 }
+            if (tail) fence_proxy_async_smem();
             mbar_arrive_expect_tx(&full[s], tx);
-            uint8_t* st = stages + static_cast<size_t>(s) * pa.stage_bytes;
-            for (int seg = 0; seg < nseg; ++seg)
-                for (int i = 0; i < pa.n_streams; ++i) {
+#pragma unroll
+            for (int seg = 0; seg < NSEG; ++seg)
+#pragma unroll
+                for (int i = 0; i < NS; ++i) {
                     const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
                     if (sp.a1 > sp.a0)
                         bulk_g2s_stream(st + seg * pa.seg_bytes + pa.s[i].region_off, pa.s[i].base + sp.a0,
@@ -554,21 +670,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream_gemv(const PipeArgs pa, 
                 break;
             }
         }
-        (void)ok;
         return;
     }
 
-    // ---------------- consumer warps ----------------
+    // ---------------- consumer warps: every warp takes part of every stage ----------------
     const int cw = warp;
-    XArea xa = xarea_layout(smem + pa.xarea_off, ga.K, PRO, ga.gs);
-    run_prologue<PRO>(ga, xa, cw, lane);
+    grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
+    run_prologue<PRO>(ga, xa, threadIdx.x);
 
     const int K = ga.K;
     const int M = ga.M;
+    const int nq = K >> 5;
+    const int rot = (FMT == kFmtPreq2) ? ((lane >> 1) & 3) : ((lane >> 2) & 3);
+    XAddr xad;
+    xad.x8 = kF32 ? 0u : smem_u32(xa.x8);
+    xad.xs = kF32 ? 0u : smem_u32(xa.xs);
+    xad.xss = kF32 ? 0u : smem_u32(xa.xss);
+    xad.xsi = kF32 ? 0u : smem_u32(xa.xsi);
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
 
-    for (int j = cw; j < n_chunks; j += kConsumerWarps) {
+    for (int j = 0; j < n_chunks; ++j) {
         const int s = j % S;
         const int use = j / S;
         if (!mbar_wait(&full[s], use & 1)) {
@@ -577,71 +699,89 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream_gemv(const PipeArgs pa, 
         }
         const long long cb = u0 + static_cast<long long>(j) * CU;
         const long long ce = (cb + CU < u1) ? cb + CU : u1;
+        const int n_units_here = static_cast<int>(ce - cb);
         uint8_t* st = stages + static_cast<size_t>(s) * pa.stage_bytes;
-
-        // bytes past the last 16-byte boundary of a stream arrive by plain loads
-        bool wrote_tail = false;
-        for (int seg = 0; seg < nseg; ++seg)
-            for (int i = 0; i < pa.n_streams; ++i) {
-                const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
-                const long long t0 = sp.a1 > sp.start ? sp.a1 : sp.start;
-                if (sp.end > t0) {
-                    uint8_t* dst = st + seg * pa.seg_bytes + pa.s[i].region_off + (t0 - sp.a0);
-                    const int nt = static_cast<int>(sp.end - t0);
-                    if (lane < nt) dst[lane] = pa.s[i].base[t0 + lane];
-                    wrote_tail = true;
-                }
+        uint32_t ub[NSEG][NS];
+#pragma unroll
+        for (int sg = 0; sg < NSEG; ++sg)
+#pragma unroll
+            for (int i = 0; i < NS; ++i) {
+                const Span sp = chunk_span(pa.s[i], cb + sg * pa.pair_unit_off, ce + sg * pa.pair_unit_off);
+                ub[sg][i] = smem_u32(st + sg * pa.seg_bytes + pa.s[i].region_off) + static_cast<uint32_t>(sp.start - sp.a0);
             }
-        if (wrote_tail) {
-            fence_proxy_async_smem();
-            __syncwarp();
-        }
 
-        // data pointers for unit k of segment seg, stream i
-        auto uptr = [&](int seg, int i, long long k) -> const uint8_t* {
-            const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
-            return st + seg * pa.seg_bytes + pa.s[i].region_off + (sp.start - sp.a0) + k * pa.s[i].unit_bytes;
-        };
-
-        for (long long k = 0; k < ce - cb; ++k) {
+        const int n_items = n_units_here * IPU;
+        for (int it = cw; it < n_items; it += kConsumerWarps) {
+            // k = it / IPU exactly (small integers), without an integer division
+            const int k = (IPU == 1) ? it : __float2int_rz(__fmul_rn(static_cast<float>(it) + 0.5f, pa.inv_ipu));
+            const int rem = it - k * IPU;
+            const int seg = (NSEG == 1 || rem < P) ? 0 : 1;
+            const int part = rem - seg * P;
             const long long unit = cb + k;
-            float v[2];
-            for (int seg = 0; seg < nseg; ++seg) {
-                if constexpr (FMT == kFmtPreq2) {
-                    v[seg] = unit_preq2(uptr(seg, 0, k), uptr(seg, 1, k), K / 32, xa, lane);
-                } else if constexpr (FMT == kFmtPreq) {
-                    v[seg] = unit_preq(uptr(seg, 0, k), K / 32, xa, lane);
-                } else if constexpr (FMT == kFmtQ4_128) {
-                    v[seg] = unit_q4_128(uptr(seg, 0, k), K / 128, xa, lane);
-                } else if constexpr (FMT == kFmtS256) {
-                    v[seg] = unit_s256(uptr(seg, 0, k), K / 256, xa, lane);
-                } else if constexpr (FMT == kFmtQ4K) {
-                    v[seg] = unit_q4k(uptr(seg, 0, k), K / 256, xa, lane);
-                } else {
-                    v[seg] = unit_packed(uptr(seg, 0, k), reinterpret_cast<const float*>(uptr(seg, 1, k)),
-                                         reinterpret_cast<const float*>(uptr(seg, 2, k)), K, ga.gs, xa, lane);
-                }
-            }
-            // rows of this unit and the lanes that own them
-            long long row;
-            bool own;
-            if constexpr (FMT == kFmtPreq2) {
-                row = unit * 4 + lane;
-                own = lane < 4 && row < M;
+            if constexpr (FMT == kFmtPacked) {
+                const Span sp0 = chunk_span(pa.s[0], cb, ce);
+                const Span sp1 = chunk_span(pa.s[1], cb, ce);
+                const Span sp2 = chunk_span(pa.s[2], cb, ce);
+                const float v = unit_packed(
+                    st + pa.s[0].region_off + (sp0.start - sp0.a0) + k * pa.s[0].unit_bytes,
+                    reinterpret_cast<const float*>(st + pa.s[1].region_off + (sp1.start - sp1.a0) +
+                                                   k * pa.s[1].unit_bytes),
+                    reinterpret_cast<const float*>(st + pa.s[2].region_off + (sp2.start - sp2.a0) +
+                                                   k * pa.s[2].unit_bytes),
+                    K, ga.gs, xa, lane);
+                if (lane == 0 && unit < M) ga.y[unit] = v;
             } else {
-                row = unit;
-                own = lane == 0 && row < M;
-            }
-            if (own) {
-                if constexpr (EPI == kEpiStore) {
-                    ga.y[row] = v[0];
-                } else if constexpr (EPI == kEpiResid) {
-                    ga.resid[row] = __fadd_rn(v[0], ga.resid[row]);
-                } else if constexpr (EPI == kEpiSilu) {
-                    ga.h[row] = ref_silu_mul(v[0], v[1]);
+                const int q0 = (P == 1) ? 0 : pa.q_bounds[part];
+                const int q1 = (P == 1) ? nq : pa.q_bounds[part + 1];
+                float a[4];
+                const uint32_t p0 = (seg == 0 ? ub[0][0] : ub[NSEG - 1][0]) + static_cast<uint32_t>(k * pa.s[0].unit_bytes);
+                uint32_t p1 = 0u;
+                if constexpr (NS > 1)
+                    p1 = (seg == 0 ? ub[0][NS - 1] : ub[NSEG - 1][NS - 1]) +
+                         static_cast<uint32_t>(k * pa.s[NS - 1].unit_bytes);
+                band_compute<FMT>(a, p0, p1, K, pa.row_bytes, xad, lane, rot, q0, q1);
+                unrotate(a, rot);
+                const float v = reduce4(a, lane);
+                float vrow[NSEG];
+                bool finish = true;
+                if (IPU > 1) {
+                    // deposit this item's row partials; the last item of the unit sums all
+                    // of them in a fixed order (deterministic) and runs the epilogue
+                    const int slot = s * CU + k;
+                    if ((lane & 7) == 0) s_part[(slot * IPU + rem) * 4 + (lane >> 3)] = v;
+                    __syncwarp();
+                    int prev = 0;
+                    if (lane == 0) {
+                        __threadfence_block();
+                        prev = atomicAdd(&s_cnt[slot], 1);
+                    }
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    finish = (prev == IPU - 1);
+                    if (finish) {
+                        __threadfence_block();
+#pragma unroll
+                        for (int sg = 0; sg < NSEG; ++sg) {
+                            float acc = 0.0f;
+                            for (int p2 = 0; p2 < P; ++p2) acc += s_part[(slot * IPU + sg * P + p2) * 4 + (lane >> 3)];
+                            vrow[sg] = acc;
+                        }
+                        if (lane == 0) s_cnt[slot] = 0;  // re-arm for the stage's next use
+                    }
                 } else {
-                    if (ga.y) ga.y[row] = v[0];
-                    argmax_take(best_v, best_i, v[0], ga.row_base + static_cast<int>(row));
+                    vrow[0] = v;
+                }
+                const long long row = unit * 4 + (lane >> 3);
+                if (finish && (lane & 7) == 0 && row < M) {
+                    if constexpr (EPI == kEpiStore) {
+                        ga.y[row] = vrow[0];
+                    } else if constexpr (EPI == kEpiResid) {
+                        ga.resid[row] = __fadd_rn(vrow[0], ga.resid[row]);
+                    } else if constexpr (EPI == kEpiSilu) {
+                        ga.h[row] = ref_silu_mul(vrow[0], vrow[NSEG - 1]);
+                    } else {
+                        if (ga.y) ga.y[row] = vrow[0];
+                        argmax_take(best_v, best_i, vrow[0], ga.row_base + static_cast<int>(row));
+                    }
                 }
             }
         }
@@ -659,7 +799,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream_gemv(const PipeArgs pa, 
         }
         __shared__ float s_v[kConsumerWarps];
         __shared__ int s_i[kConsumerWarps];
-        __shared__ bool s_last;
+        __shared__ int s_last;
         if (lane == 0) {
             s_v[cw] = best_v;
             s_i[cw] = best_i;
@@ -673,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream_gemv(const PipeArgs pa, 
             ga.part_idx[blockIdx.x] = bi;
             __threadfence();
             const unsigned int prev = atomicAdd(ga.counter, 1u);
-            s_last = (prev == gridDim.x - 1);
+            s_last = (prev == gridDim.x - 1) ? 1 : 0;
         }
         consumer_sync();
         if (s_last && cw == 0) {
@@ -693,6 +833,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream_gemv(const PipeArgs pa, 
                 *ga.out_idx = (bi == 0x7fffffff) ? ga.row_base : bi;
                 *ga.counter = 0u;  // re-arm for the next call
             }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q4_128 -> banded device layout (pure byte moves; bit-exact by construction):
+//   quant  [nb][K/128][4 rows][64 B nibbles]   scales [nb][K/128][4 rows] fp16
+// rows past M in the last band are zero.  One thread per (band, group, row).
+// ---------------------------------------------------------------------------
+__global__ void k_relayout_q4_128(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ quant,
+                                  uint8_t* __restrict__ scales, int M, int K) {
+    const int ng = K / 128;
+    const long long nb = (M + 3) / 4;
+    const long long total = nb * ng * 4;
+    for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int r = static_cast<int>(t & 3);
+        const long long bg = t >> 2;
+        const int g = static_cast<int>(bg % ng);
+        const long long b = bg / ng;
+        const long long row = b * 4 + r;
+        uint8_t* qd = quant + (bg * 4 + r) * 64;
+        uint8_t* sd = scales + (bg * 4 + r) * 2;
+        if (row < M) {
+            const uint8_t* src = blocks + (row * ng + g) * 66;
+            sd[0] = src[0];
+            sd[1] = src[1];
+            for (int i = 0; i < 64; ++i) qd[i] = src[2 + i];
+        } else {
+            sd[0] = 0;
+            sd[1] = 0;
+            for (int i = 0; i < 64; ++i) qd[i] = 0;
         }
     }
 }

@@ -63,15 +63,27 @@ inline int sm_count() {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // dynamic shared memory budget of one streaming-GEMV CTA
-constexpr uint32_t kSmemBudget = 200 * 1024;
-constexpr uint32_t kBarBytes = 2 * kMaxStages * 8;
+// shared-memory budget per CTA: kCtasPerSm CTAs must fit one SM (228 KB)
+#ifndef ASDSL_SMEM_BUDGET_KB
+#define ASDSL_SMEM_BUDGET_KB (208 / ASDSL_CTAS_PER_SM)
+#endif
+#ifndef ASDSL_CHUNK_KB
+#define ASDSL_CHUNK_KB 64
+#endif
+constexpr uint32_t kSmemBudget = ASDSL_SMEM_BUDGET_KB * 1024;
+constexpr uint32_t kBarBytes = 512;  // full[kMaxStages] + empty[kMaxStages]
+static_assert(kBarBytes >= 2 * kMaxStages * 8, "barrier area too small");
 
 inline uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-inline uint32_t xarea_bytes(int pro, int K, int gs) {
-    const int ng = K / gs;
-    if (pro == kProF32) return round_up(static_cast<uint32_t>((K + ng + kConsumerWarps) * 4), 128);
-    return round_up(static_cast<uint32_t>(((K + 15) & ~15) + ng * 12 + kConsumerWarps * 4), 128);
+// process-wide launch policy (asdsl_b200_set_launch_policy)
+struct LaunchPolicy {
+    int ctas_per_sm = kCtasPerSm;  // 1 leaves an SM slot free for the next kernel of a chain
+    int pdl = 1;                   // programmatic dependent launch on every streaming GEMV
+};
+inline LaunchPolicy& launch_policy() {
+    static LaunchPolicy p;
+    return p;
 }
 
 struct StreamIn {
@@ -83,6 +95,8 @@ struct StreamIn {
 struct LaunchOpts {
     int max_ctas = 0;      // 0 = one CTA per SM
     bool pdl = false;      // programmatic dependent launch attribute
+    int row_bytes = 0;     // row-major block formats: bytes of one row
+    int chunk_target = ASDSL_CHUNK_KB * 1024;  // bytes per pipeline stage (all segments and streams)
 };
 
 template <int FMT, int PRO, int EPI>
@@ -92,7 +106,7 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     if (n_units > 0x7fffffffLL) return set_error(kEinval, "too many rows");
     PipeArgs pa;
     std::memset(&pa, 0, sizeof(pa));
-    pa.n_streams = n_streams;
+    if (n_streams != FmtTraits<FMT>::kStreams) return set_error(kEinval, "internal: stream count mismatch");
     pa.n_units = static_cast<int>(n_units);
     pa.pair_unit_off = static_cast<int>(pair_unit_off);
     long long ub_sum = 0;
@@ -103,15 +117,33 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     }
     const int nseg = pair_unit_off > 0 ? 2 : 1;
     const int sms = sm_count();
-    int grid = opt.max_ctas > 0 ? opt.max_ctas : sms;
+    const LaunchPolicy pol = launch_policy();
+    int grid = opt.max_ctas > 0 ? opt.max_ctas : sms * pol.ctas_per_sm;
     if (grid > n_units) grid = static_cast<int>(n_units);
     const long long per_cta = (n_units + grid - 1) / grid;
 
-    const uint32_t xa = xarea_bytes(PRO, ga.K, ga.gs);
-    long long cu = 12288 / (ub_sum > 0 ? ub_sum : 1);
+    // stage = chunk of `cu` units (all segments and streams): big bulk copies stream
+    // HBM best (>= 16 KB each), and every consumer warp shares every stage.
+    const uint32_t xa = xarea_layout_bytes(ga.K, ga.gs, PRO == kProF32);
+    const long long unit_stage = ub_sum * nseg;
+    long long cu = opt.chunk_target / (unit_stage > 0 ? unit_stage : 1);
     if (cu < 1) cu = 1;
     if (cu > per_cta) cu = per_cta;
-    uint32_t seg_bytes = 0, stage_bytes = 0;
+    // K-split so a chunk carries at least one work item per consumer warp
+    int parts = 1;
+    const int nq = ga.K / 32;
+    if (FmtTraits<FMT>::kRowsPerUnit == 4 && nq % 32 == 0 && cu * nseg < kConsumerWarps) {
+        // split K only when each part keeps >= 2 whole lane iterations (two slices in
+        // flight); short rows are cheaper unsplit than merged through shared memory
+        const int li = nq / 32;
+        for (int d = 2; d <= 8 && d <= li; ++d) {
+            if (li % d || li / d < 2) continue;
+            parts = d;
+            if (cu * nseg * d >= kConsumerWarps) break;
+        }
+    }
+    const int ipu = parts * nseg;
+    uint32_t seg_bytes = 0, stage_bytes = 0, split_bytes = 0;
     int stages = 0;
     for (;;) {
         seg_bytes = 0;
@@ -120,13 +152,24 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
             seg_bytes += round_up(static_cast<uint32_t>(cu * in[i].unit_bytes + 48), 16);
         }
         stage_bytes = seg_bytes * nseg;
+        split_bytes = 0;
         const long long avail = static_cast<long long>(kSmemBudget) - kBarBytes - xa;
         stages = avail > 0 ? static_cast<int>(avail / stage_bytes) : 0;
         if (stages > kMaxStages) stages = kMaxStages;
+        if (ipu > 1 && stages > 0) {
+            // partial sums + counters live beside the stages
+            for (;;) {
+                split_bytes = round_up(static_cast<uint32_t>(stages * cu * ipu * 4 * 4 + stages * cu * 4), 128);
+                if (stages <= 2 || static_cast<long long>(stages) * stage_bytes + split_bytes <= avail) break;
+                --stages;
+            }
+        }
         if (stages >= 2 || cu == 1) break;
         cu = cu / 2 > 0 ? cu / 2 : 1;
     }
-    if (stages < 2) return set_error(kEinval, "in_features too large for the shared-memory pipeline");
+    if (stages < 2 || static_cast<long long>(stages) * stage_bytes + split_bytes >
+                          static_cast<long long>(kSmemBudget) - kBarBytes - xa)
+        return set_error(kEinval, "in_features too large for the shared-memory pipeline");
     for (int i = 0; i < n_streams; ++i) {
         pa.s[i].base = static_cast<const uint8_t*>(in[i].base);
         pa.s[i].unit_bytes = in[i].unit_bytes;
@@ -134,11 +177,22 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     }
     pa.units_per_chunk = static_cast<int>(cu);
     pa.n_stages = stages;
+    pa.k_parts = parts;
+    {
+        for (int p = 0; p <= parts; ++p) pa.q_bounds[p] = (nq / parts) * p;
+        pa.inv_ipu = 1.0f / static_cast<float>(ipu);
+    }
     pa.seg_bytes = seg_bytes;
     pa.stage_bytes = stage_bytes;
     pa.xarea_off = kBarBytes;
     pa.stage_off = round_up(kBarBytes + xa, 128);
-    const uint32_t smem = pa.stage_off + static_cast<uint32_t>(stages) * stage_bytes;
+    pa.split_off = pa.stage_off + static_cast<uint32_t>(stages) * stage_bytes;
+    pa.row_bytes = opt.row_bytes;
+    if (PRO != kProQ8 && !aligned16(ga.x)) return set_error(kEinval, "activations must be 16-byte aligned");
+    if (PRO == kProRmsA8 && !aligned16(ga.norm_w)) return set_error(kEinval, "norm weights must be 16-byte aligned");
+    if (PRO == kProQ8 && (reinterpret_cast<uintptr_t>(ga.xq) & 3u))
+        return set_error(kEinval, "int8 activations must be 4-byte aligned");
+    const uint32_t smem = pa.split_off + split_bytes;
 
     ga.status = device_status_ptr();
     if (!ga.status) return set_error(kEcuda, "cannot resolve the device status word");
@@ -162,7 +216,7 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    if (opt.pdl) {
+    if (opt.pdl || pol.pdl) {
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;

@@ -121,16 +121,16 @@ def cpu_layer_step_runner(host: dict):
         x = host["x"]
         if rk is not None:
             qkv = rk.gemv_preq2_fused(host["qkv_meta"], host["qkv_quant"], x, QKV, H)
-            o = rk.gemv_preq2_fused(host["o_meta"], host["o_quant"], x, H, QD)
-            xq, xs = rk.quantize_activation(x, 128)
+            o = rk.gemv_preq2_fused(host["o_meta"], host["o_quant"], qkv[:QD], H, QD)
+            xq, xs = rk.quantize_activation(o, 128)
             gu = rk.gemv_q4_128_q8(host["gate_up_q4_128"], xq, xs, 2 * I, H)
             h = orc.swiglu(gu[:I], gu[I:])
             hq, hs = rk.quantize_activation(h, 128)
             y = rk.gemv_q4_128_q8(host["down_q4_128"], hq, hs, H, I)
         else:
             qkv = orc.gemv_preq2_fused(host["qkv_meta"], host["qkv_quant"], x, QKV, H)
-            o = orc.gemv_preq2_fused(host["o_meta"], host["o_quant"], x, H, QD)
-            gu = orc.gemv_q4_128_fused(host["gate_up_q4_128"], x, 2 * I, H)
+            o = orc.gemv_preq2_fused(host["o_meta"], host["o_quant"], qkv[:QD], H, QD)
+            gu = orc.gemv_q4_128_fused(host["gate_up_q4_128"], o, 2 * I, H)
             h = orc.swiglu(gu[:I], gu[I:])
             y = orc.gemv_q4_128_fused(host["down_q4_128"], h, H, I)
         return qkv, o, y
@@ -248,11 +248,10 @@ def main():
         base.step(x)
     stream.synchronize()
     orc = Oracle()
-    c = host["cfg"]
-    ref_y_gu = orc.gemv_q4_128_fused(host["gate_up_q4_128"], host["x"], 2 * c["inter"], c["hidden"])
-    ref_h = orc.swiglu(ref_y_gu[: c["inter"]], ref_y_gu[c["inter"]:])
-    ref_y = orc.gemv_q4_128_fused(host["down_q4_128"], ref_h, c["hidden"], c["inter"])
-    err = rel_err(base.y.cpu().numpy(), ref_y)
+    from asdsl_b200.layer import layer_reference
+
+    ref = layer_reference(orc, host)
+    err = max(rel_err(t.cpu().numpy(), ref[k]) for k, t in (("qkv", base.qkv_out), ("o", base.o_out), ("y", base.y)))
     if err > 1e-3:
         raise SystemExit(f"bench: GPU result mismatch vs oracle ({err})")
 
@@ -295,24 +294,63 @@ def main():
     ms_step = ms / args.steps
     value = world * bytes_per_step / (ms_step * 1e-3) / 1e9
 
-    # dominant kernel alone (gate_up + SiLU, Q4_128): per-launch duration over rotated copies
-    dom_iters = 200
+    # each kernel alone, captured in a CUDA graph of `per_graph` launches over the rotated copies
     lib = _lib.load()
     s_ptr = stream.cuda_stream
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for i in range(10):
-        L = layers[i % len(layers)]
-        lib.asdsl_b200_gateup_silu(2, L.gu.data_ptr(), None, x.data_ptr(), L.h.data_ptr(), L.I, L.H, s_ptr)
-    e0.record(stream)
-    for i in range(dom_iters):
-        L = layers[i % len(layers)]
-        lib.asdsl_b200_gateup_silu(2, L.gu.data_ptr(), None, x.data_ptr(), L.h.data_ptr(), L.I, L.H, s_ptr)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    dom_ms = e0.elapsed_time(e1) / dom_iters
-    dom_bytes = base.gu.numel() + 4 * (base.H + base.I)
+
+    def k_qkv(L):
+        lib.asdsl_b200_gemv_preq2_fused(L.qkv_meta.data_ptr(), L.qkv_quant.data_ptr(), x.data_ptr(),
+                                        L.qkv_out.data_ptr(), L.QKV, L.H, 32, s_ptr)
+
+    def k_o(L):
+        lib.asdsl_b200_gemv_preq2_fused(L.o_meta.data_ptr(), L.o_quant.data_ptr(), L.qkv_out.data_ptr(),
+                                        L.o_out.data_ptr(), L.H, L.QD, 32, s_ptr)
+
+    def k_gu(L):
+        lib.asdsl_b200_gateup_silu(4, L.gu_q.data_ptr(), L.gu_s.data_ptr(), L.o_out.data_ptr(), L.h.data_ptr(), L.I,
+                                   L.H, s_ptr)
+
+    def k_dn(L):
+        lib.asdsl_b200_gemv_q4_128_banded(L.dn_q.data_ptr(), L.dn_s.data_ptr(), L.h.data_ptr(), L.y.data_ptr(), L.H,
+                                          L.I, s_ptr)
+
+    kern_bytes = {
+        "qkv_preq2": (k_qkv, base.qkv_meta.numel() + base.qkv_quant.numel() + 4 * (base.H + base.QKV)),
+        "o_preq2": (k_o, base.o_meta.numel() + base.o_quant.numel() + 4 * (base.QD + base.H)),
+        "gateup_silu_q4_128": (k_gu, base.gu_q.numel() + base.gu_s.numel() + 4 * (base.H + base.I)),
+        "down_q4_128": (k_dn, base.dn_q.numel() + base.dn_s.numel() + 4 * (base.I + base.H)),
+    }
+    per_kernel = {}
+    per_graph = 4 * len(layers)
+    for name, (fn, nbytes) in kern_bytes.items():
+        with torch.cuda.stream(stream):
+            for L in layers:
+                fn(L)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(per_graph):
+                fn(layers[i % len(layers)])
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 25
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
+        per_kernel[name] = {"us": round(us, 3), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+        del g
+    dom = "gateup_silu_q4_128"
+    dom_ms = per_kernel[dom]["us"] * 1e-3
+    dom_bytes = per_kernel[dom]["bytes"]
     peak, peak_kind = _peaks()
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    if rank == 0:
+        print("per-kernel:", json.dumps(per_kernel), file=sys.stderr, flush=True)
 
     # e2e through the public host-buffer API (pinned H2D of x, D2H of all outputs)
     e2e_steps = min(args.steps, 200)
@@ -361,9 +399,9 @@ def main():
                        "bytes_per_step": bytes_per_step, "weight_copies_rotated": len(layers),
                        "l2": f"rotating {len(layers)} weight copies ({len(layers) * base.weight_bytes / 1e6:.0f} MB > 126 MB L2)",
                        "parallelism": f"replica x{world}", "frac_of_8TBs": round(value / world / NOMINAL_HBM_GBS, 4)},
-            "roofline": {"bound": "hbm", "kernel": "k_stream_gemv<Q4_128, A8, SiLU> (gate_up 16384x3072 + SiLU)",
+            "roofline": {"bound": "hbm", "kernel": "k_stream_gemv<Q4_128 banded, A8, SiLU> (gate_up 16384x3072 + SiLU)",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": _traffic("gateup_silu_q4_128_c1"),
+                         "frac": round(achieved / peak, 4), "traffic": _traffic("gateup_silu_q4_128_c1"), "per_kernel": per_kernel,
                          "launch_us": round(dom_ms * 1e3, 3), "bytes_per_launch": dom_bytes},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * base.H,

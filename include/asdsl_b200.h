@@ -37,9 +37,18 @@ extern "C" {
 #define ASDSL_B200_FMT_PREQ 1   /* [M][K/32][20] blocks (repack_q4_32.py:63-102) */
 #define ASDSL_B200_FMT_Q4_128 2 /* [M][K/128][66] blocks (repack_q4_128.py:34-92) */
 #define ASDSL_B200_FMT_S256 3   /* [M][K/256][144] blocks (gemv_q4_s256.cpp:1-17) */
+#define ASDSL_B200_FMT_Q4_128_BANDED 4 /* device re-layout of Q4_128: quant [ceil(M/4)][K/128][4][64] +
+                                          scales [ceil(M/4)][K/128][4] fp16 (asdsl_b200_relayout_q4_128) */
 
 const char* asdsl_b200_version(void);
 const char* asdsl_b200_last_error(void);
+
+/* Process-wide launch policy of the streaming GEMVs: CTAs per SM (1 or 2; 1 leaves room
+ * for the next kernel of a dependent chain to start early) and programmatic dependent
+ * launch (nonzero = on, the default).  No reference counterpart: the reference's CPU
+ * threading knobs (ASDSL_PERSISTENT_POOL, ASDSL_CHUNKED_GEMV, engine_flags.hpp:8-15,
+ * gemv_chunked.hpp:16-45) play this role there. */
+int asdsl_b200_set_launch_policy(int ctas_per_sm, int use_pdl);
 
 /* Reads (and with clear != 0 resets) the current device's status word: bits
  * set by kernels whose bounded waits gave up.  Synchronizes the device. */
@@ -114,11 +123,25 @@ int asdsl_b200_matmul_batch_q4(const uint8_t* w_packed, const float* scales, con
                                const float* X_batch, float* Y_batch, int M, int K, int B, int group_size,
                                void* stream);
 
+/* Re-lay Q4_128 blocks (repack_q4_128.py:34-92) into the banded device layout: pure byte moves,
+ * bit-exact; rows past M in the last band are zero.  quant: ceil(M/4)*(K/128)*256 bytes,
+ * scales: ceil(M/4)*(K/128)*8 bytes.  Device-side counterpart of the reference's per-format
+ * repackers (asdsl/quantization/repack_q4_128.py, repack_preq2.py:22-46 for the band idea). */
+int asdsl_b200_relayout_q4_128(const uint8_t* blocks, uint8_t* quant, uint8_t* scales, int out_features,
+                               int in_features, void* stream);
+
+/* Q4_128 GEMV on the banded layout with fused A8 at gs 128: same result as
+ * quantize_activation_avx2(..., 128) + gemv_q4_128_preq_avx2 on the original blocks
+ * (asdsl/kernels/native/gemv_q4_128.cpp:94-257). */
+int asdsl_b200_gemv_q4_128_banded(const uint8_t* quant, const uint8_t* scales, const float* x, float* y,
+                                  int out_features, int in_features, void* stream);
+
 /* Bytes of device scratch the fused-argmax GEMVs need (zero-filled once by the caller;
  * the kernels leave it re-armed). */
 size_t asdsl_b200_argmax_scratch_bytes(void);
 
-/* lm_head GEMV with fused first-max argmax (fused A8; fmt PREQ2 at gs 32 or Q4_128 at gs 128).
+/* lm_head GEMV with fused first-max argmax (fused A8; fmt PREQ2 at gs 32, Q4_128 or Q4_128_BANDED
+ * at gs 128; for the banded layout w0 = quant, w1 = scales).
  * Writes logits to y (may be NULL) and the maximum / its global row index (row_base + local row)
  * to out_val[0] / out_idx[0].  Replaces the engine's lm_head GEMV + argmax_f32_avx2
  * (asdsl/kernels/native/unified_engine.cpp:1628-1644 and :207-233). */
@@ -127,7 +150,8 @@ int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const 
                            int out_features, int in_features, void* stream);
 
 /* Fused gate_up GEMV + SiLU(gate)*up: rows [0, I) are gate, [I, 2I) are up, h[i] = silu(gate_i)*up_i
- * with the reference's fast_exp.  fmt PREQ2 (w0 = meta, w1 = quant) or Q4_128 (w0 = blocks).
+ * with the reference's fast_exp.  fmt PREQ2 (w0 = meta, w1 = quant), Q4_128 (w0 = blocks) or
+ * Q4_128_BANDED (w0 = quant, w1 = scales).
  * Replaces the gate_up GEMV + swiglu_inplace pair (asdsl/kernels/native/unified_engine.cpp:1539-1570,
  * :836-857). */
 int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* h,

@@ -147,8 +147,8 @@ def test_q4_128(ng, oracle, native, M, K):
     ng.gemv_q4_128_preq_avx2(blocks, xq, xs, y, M, K, 128)
     assert rel_err(y, ref) < TOL
     yt = torch.empty(M, dtype=torch.float32, device="cuda")
-    native.call("asdsl_b200_gemv_q4_128_fused", _dev(blocks).data_ptr(), _dev(x).data_ptr(), yt.data_ptr(), M, K,
-                None)
+    bd, xd = _dev(blocks), _dev(x)  # keep the device copies alive until the kernel has run
+    native.call("asdsl_b200_gemv_q4_128_fused", bd.data_ptr(), xd.data_ptr(), yt.data_ptr(), M, K, None)
     assert rel_err(yt.cpu().numpy(), ref) < TOL
     _status_clean(native)
 
@@ -237,9 +237,10 @@ def test_gemv_argmax(oracle, native, fmt, M, K):
     y = torch.empty(M, dtype=torch.float32, device="cuda")
     ov = torch.empty(1, dtype=torch.float32, device="cuda")
     oi = torch.empty(1, dtype=torch.int32, device="cuda")
+    xd = _dev(x)
     for rep in range(2):  # twice: the scratch counter must re-arm itself
         native.call("asdsl_b200_gemv_argmax", fmt, w0.data_ptr(), None if w1 is None else w1.data_ptr(),
-                    _dev(x).data_ptr(), y.data_ptr(), ov.data_ptr(), oi.data_ptr(), 1000 * rep,
+                    xd.data_ptr(), y.data_ptr(), ov.data_ptr(), oi.data_ptr(), 1000 * rep,
                     scratch.data_ptr(), scratch.numel(), M, K, None)
         yh = y.cpu().numpy()
         assert rel_err(yh, ref) < TOL
@@ -269,8 +270,9 @@ def test_gateup_silu(oracle, native, fmt, I, K):
         w0, w1 = _dev(blocks), None
     ref = oracle.swiglu(gu[:I], gu[I:])
     h = torch.empty(I, dtype=torch.float32, device="cuda")
+    xd = _dev(x)
     native.call("asdsl_b200_gateup_silu", fmt, w0.data_ptr(), None if w1 is None else w1.data_ptr(),
-                _dev(x).data_ptr(), h.data_ptr(), I, K, None)
+                xd.data_ptr(), h.data_ptr(), I, K, None)
     assert rel_err(h.cpu().numpy(), ref) < TOL
     _status_clean(native)
 
@@ -319,3 +321,51 @@ def test_errors_on_device_path(ng):
     with pytest.raises(ValueError):
         ng.gemv_preq2_fused_avx2(np.zeros(64, np.uint8), np.zeros(64, np.uint8), np.zeros(64, np.float32),
                                  np.zeros(4, np.float32), 4, 64, 64)
+
+
+@pytest.mark.parametrize("M,K", [(1, 128), (61, 384), (16384, 3072), (3072, 8192)])
+def test_q4_128_banded_relayout_and_gemv(oracle, native, M, K):
+    """Device re-layout is byte-exact; banded GEMV / argmax / SiLU match the oracle on the raw blocks."""
+    from asdsl_b200.layer import relayout_q4_128
+    from asdsl_b200.quantization.repack import q4_128_to_banded, repack_fp32_to_q4_128_blocks
+
+    rng = np.random.default_rng(M + 5 * K)
+    w = (rng.standard_normal((M, K)) * 0.02).astype(np.float32)
+    blocks = repack_fp32_to_q4_128_blocks(w, M, K)
+    bd = _dev(blocks)
+    q, s = relayout_q4_128(bd, M, K)
+    hq, hs = q4_128_to_banded(blocks, M, K)
+    assert np.array_equal(q.cpu().numpy(), hq) and np.array_equal(s.cpu().numpy(), hs)
+    x = _x(rng, K)
+    xd = _dev(x)
+    y = torch.empty(M, dtype=torch.float32, device="cuda")
+    native.call("asdsl_b200_gemv_q4_128_banded", q.data_ptr(), s.data_ptr(), xd.data_ptr(), y.data_ptr(), M, K, None)
+    ref = oracle.gemv_q4_128_fused(blocks, x, M, K)
+    assert rel_err(y.cpu().numpy(), ref) < TOL
+    scratch = torch.zeros(native.load().asdsl_b200_argmax_scratch_bytes(), dtype=torch.uint8, device="cuda")
+    ov = torch.empty(1, dtype=torch.float32, device="cuda")
+    oi = torch.empty(1, dtype=torch.int32, device="cuda")
+    native.call("asdsl_b200_gemv_argmax", 4, q.data_ptr(), s.data_ptr(), xd.data_ptr(), y.data_ptr(), ov.data_ptr(),
+                oi.data_ptr(), 0, scratch.data_ptr(), scratch.numel(), M, K, None)
+    yh = y.cpu().numpy()
+    assert int(oi.item()) == int(np.argmax(yh)) and rel_err(yh, ref) < TOL
+    if M % 8 == 0:
+        I = M // 2
+        h = torch.empty(I, dtype=torch.float32, device="cuda")
+        native.call("asdsl_b200_gateup_silu", 4, q.data_ptr(), s.data_ptr(), xd.data_ptr(), h.data_ptr(), I, K, None)
+        assert rel_err(h.cpu().numpy(), oracle.swiglu(ref[:I], ref[I:])) < TOL
+    _status_clean(native)
+
+
+def test_layer_projection_set_matches_oracle(native, oracle):
+    """Config-1-shaped layer chain (small seeded weights through the same pipeline) vs the oracle."""
+    from asdsl_b200.layer import build_c1_host, from_host, layer_reference
+
+    cfg = dict(hidden=512, qkv_rows=768, q_dim=512, inter=1024)
+    host = build_c1_host(7, cfg)
+    L = from_host(host)
+    out = L.forward(host["x"])
+    ref = layer_reference(oracle, host)
+    for k in ("qkv", "o", "y"):
+        assert rel_err(out[k], ref[k]) < TOL, k
+    _status_clean(native)
