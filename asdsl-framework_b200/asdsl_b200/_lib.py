@@ -51,6 +51,7 @@ _SIGS = {
     "asdsl_b200_relayout_q4_128": [_P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_q4_128_banded": [_P, _P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_argmax": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P],
+    "asdsl_b200_gemv_argmax_static": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_gateup_silu": [_I, _P, _P, _P, _P, _I, _I, _P],
 }
 _RESTYPES = {

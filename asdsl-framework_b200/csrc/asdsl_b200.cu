@@ -404,6 +404,56 @@ int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const 
     return set_error(kEinval, "gemv_argmax: unsupported weight format");
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// allocation-free variant of gemv_argmax: the argmax scratch lives in a
+// file-scope device array (one copy per device), sized for grids of up to
+// kStaticArgmaxCtas CTAs: a 256-byte counter slot + 4-byte value and index per CTA.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kStaticArgmaxCtas = 1024;
+constexpr size_t kStaticArgmaxBytes = 256 + 2 * 4 * static_cast<size_t>(kStaticArgmaxCtas);  // 8448 bytes
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_ptr[kStaticMaxDevices] = {};
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_argmax_static_scratch[kStaticArgmaxBytes];
+
+extern "C" {
+
+int asdsl_b200_gemv_argmax_static(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
+                                  float* out_val, int32_t* out_idx, int row_base, int M, int K, void* stream) {
+    const long long max_ctas = static_cast<long long>(sm_count()) * launch_policy().ctas_per_sm;
+    const size_t need = 256 + 2 * 4 * static_cast<size_t>(max_ctas);
+    if (need > kStaticArgmaxBytes || asdsl_b200_argmax_scratch_bytes() > kStaticArgmaxBytes)
+        return set_error(kErange, "gemv_argmax_static: this device needs " + std::to_string(need) +
+                                      " bytes of argmax scratch (" + std::to_string(max_ctas) +
+                                      " CTAs); the static maximum is " + std::to_string(kStaticArgmaxBytes) +
+                                      " bytes (" + std::to_string(kStaticArgmaxCtas) + " CTAs)");
+    int dev = 0;
+    ASDSL_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kStaticMaxDevices)
+        return set_error(kErange, "gemv_argmax_static: device ordinal " + std::to_string(dev) + " beyond " +
+                                      std::to_string(kStaticMaxDevices - 1));
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_static_scratch_mu);
+        if (!g_static_scratch_ptr[dev]) {
+            // first call on this device: resolve the array's address (device `dev` is current)
+            // and zero it on the caller's stream; the kernel re-arms the counter after each use
+            void* p = nullptr;
+            ASDSL_CUDA(cudaGetSymbolAddress(&p, g_argmax_static_scratch));
+            ASDSL_CUDA(cudaMemsetAsync(p, 0, kStaticArgmaxBytes, as_stream(stream)));
+            g_static_scratch_ptr[dev] = p;
+        }
+        scratch = g_static_scratch_ptr[dev];
+    }
+    return asdsl_b200_gemv_argmax(fmt, w0, w1, x, y, out_val, out_idx, row_base, scratch, kStaticArgmaxBytes, M, K,
+                                  stream);
+}
+
 int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* h, int I, int K,
                            void* stream) {
     if (!w0 || !x || !h) return set_error(kEinval, "gateup_silu: null pointer");

@@ -149,6 +149,18 @@ int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const 
                            float* out_val, int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes,
                            int out_features, int in_features, void* stream);
 
+/* asdsl_b200_gemv_argmax without caller scratch, for callers that cannot allocate device memory.
+ * No counterpart in the reference (its CPU argmax needs no device scratch).
+ * The scratch is a file-scope device array of 8448 bytes (one per device), enough for grids of up
+ * to 1024 CTAs; a device that would launch more is rejected with ASDSL_B200_ERANGE.  The function
+ * allocates nothing.  The FIRST call on each device (with that device current) resolves the array's
+ * address with cudaGetSymbolAddress and zeroes it on `stream`; make that first call before any
+ * stream capture.  All calls on one device share the array: calls that overlap in time (on two
+ * streams, or from two host threads) race and must be serialised by the caller. */
+int asdsl_b200_gemv_argmax_static(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
+                                  float* out_val, int32_t* out_idx, int row_base, int out_features,
+                                  int in_features, void* stream);
+
 /* Fused gate_up GEMV + SiLU(gate)*up: rows [0, I) are gate, [I, 2I) are up, h[i] = silu(gate_i)*up_i
  * with the reference's fast_exp.  fmt PREQ2 (w0 = meta, w1 = quant), Q4_128 (w0 = blocks) or
  * Q4_128_BANDED (w0 = quant, w1 = scales).
