@@ -53,7 +53,38 @@ _SIGS = {
     "asdsl_b200_gemv_argmax": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P],
     "asdsl_b200_gemv_argmax_static": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_gateup_silu": [_I, _P, _P, _P, _P, _I, _I, _P],
+    # device-resident decode engine
+    "asdsl_b200_engine_create": [_P, _P],
+    "asdsl_b200_engine_destroy": [_P],
+    "asdsl_b200_engine_set_globals": [_P, _P, _I, _P, _P, _P],
+    "asdsl_b200_engine_set_output_proj": [_P, _P, _I],
+    "asdsl_b200_engine_set_lm_head_preq2": [_P, _P, _SZ, _P, _SZ],
+    "asdsl_b200_engine_set_layer_norms": [_P, _I, _P, _P],
+    "asdsl_b200_engine_set_projection": [_P, _I, _I, _I, _P, _SZ, _P, _SZ],
+    "asdsl_b200_engine_finalize": [_P],
+    "asdsl_b200_engine_forward_token": [_P, _I, _I, _P, _P],
+    "asdsl_b200_engine_generate": [_P, _P, _I, _I, _P, _I, _P, _I, _P],
+    "asdsl_b200_engine_reset_session": [_P],
+    "asdsl_b200_engine_get_kv_seq_len": [_P, _P],
+    "asdsl_b200_engine_truncate_kv": [_P, _I],
+    "asdsl_b200_engine_snapshot_kv": [_P],
+    "asdsl_b200_engine_restore_kv": [_P],
+    "asdsl_b200_engine_export_lm_head": [_P, _P, _P, _SZ, _P, _SZ],
+    "asdsl_b200_engine_stream": [_P, _P],
+    "asdsl_b200_engine_set_position": [_P, _I, _I],
+    "asdsl_b200_engine_replay": [_P, _I, _I],
+    "asdsl_b200_engine_read_buffer": [_P, _I, _P, _SZ],
 }
+
+
+class EngineConfigC(ctypes.Structure):
+    """asdsl_b200_engine_config (include/asdsl_b200.h)."""
+
+    _fields_ = [
+        ("num_layers", _I), ("hidden_size", _I), ("num_heads", _I), ("num_kv_heads", _I), ("head_dim", _I),
+        ("intermediate_size", _I), ("vocab_size", _I), ("rms_norm_eps", _F), ("group_size", _I),
+        ("lm_head_group_size", _I), ("max_seq_len", _I), ("rotary_dim", _I), ("weight_format", _I),
+    ]
 _RESTYPES = {
     "asdsl_b200_version": ctypes.c_char_p,
     "asdsl_b200_last_error": ctypes.c_char_p,

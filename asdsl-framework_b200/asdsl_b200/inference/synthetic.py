@@ -27,6 +27,11 @@ PHI4_MINI = dict(num_layers=32, hidden=3072, n_heads=24, n_kv_heads=8, head_dim=
 TINY = dict(num_layers=2, hidden=256, n_heads=2, n_kv_heads=1, head_dim=128, inter=512,
             vocab=512, max_seq=64, rotary_dim=96, eps=1e-5, theta=10000.0)
 
+# long-trajectory parity shape: Phi-4-mini's head geometry (GQA 3:1 would need 3 heads per
+# KV head; 6/2 keeps it), small enough for the CPU oracle to run 128+ steps in seconds
+SMALL = dict(num_layers=4, hidden=768, n_heads=6, n_kv_heads=2, head_dim=128, inter=2048,
+             vocab=8192, max_seq=256, rotary_dim=96, eps=1e-5, theta=10000.0)
+
 
 def rope_tables(max_seq: int, rotary_dim: int, theta: float = 10000.0):
     """cos/sin [max_seq, rotary_dim/2] float32, angles in float64

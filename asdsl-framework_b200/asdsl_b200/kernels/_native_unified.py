@@ -1,0 +1,297 @@
+"""Drop-in for the reference's ``asdsl.kernels._native_unified`` module (EngineConfig,
+UnifiedEngine), backed by the device-resident decode engine of libasdsl_b200.so.
+
+Reference: asdsl/kernels/native/unified_engine.cpp -- pybind registration :2203-2222
+(EngineConfig) and :2655-2713 (UnifiedEngine), weight binding :2240-2442, methods
+:2449-2630.  Same constructor arguments, same ``layers_dict`` keys, same method names,
+argument meaning and exception classes (std::invalid_argument -> ValueError,
+std::out_of_range -> IndexError).
+
+Differences that follow from running on the GPU:
+  * weights are copied once into engine-owned device memory (the reference borrows
+    the numpy arrays); preq-only layers are repacked to preq2 on the host first;
+  * ``forward_token`` returns a reused host buffer like the reference (:2485-2492);
+  * ``generate`` replays one CUDA graph per token and copies the tokens back once
+    (with stop tokens, once per 16 tokens);
+  * an empty prompt raises ValueError (the reference reads stale logits).
+The format selection mirrors the reference's environment switches: preq2 blobs
+(``*_meta``/``*_quant``) are used unless ``ASDSL_C01`` (gate_up/down) or ``ASDSL_C03``
+(qkv/o) select the ``*_g128`` Q4_128 blobs (unified_engine.cpp:1404-1410, :1532-1538).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from asdsl_b200 import _lib
+from asdsl_b200.quantization.repack import repack_preq_blocks_to_preq2
+
+_PROJ = ("qkv_proj", "o_proj", "gate_up_proj", "down_proj")
+
+
+class EngineConfig:
+    """unified_engine.h:14-109 (fields bound at unified_engine.cpp:2204-2222)."""
+
+    def __init__(self):
+        self.num_layers = 32
+        self.hidden_size = 3072
+        self.num_heads = 24
+        self.num_kv_heads = 8
+        self.head_dim = 128
+        self.intermediate_size = 8192
+        self.vocab_size = 200064
+        self.rms_norm_eps = 1e-5
+        self.group_size = 32
+        self.lm_head_group_size = 0
+        self.max_seq_len = 2048
+        self.rotary_dim = 96
+        self.weight_format = 0
+
+    def _c(self) -> _lib.EngineConfigC:
+        c = _lib.EngineConfigC()
+        for name, _ in _lib.EngineConfigC._fields_:
+            setattr(c, name, getattr(self, name))
+        return c
+
+
+def _env_on(name: str) -> bool:
+    v = os.environ.get(name)
+    return bool(v) and v[0] != "0"
+
+
+def _host(a, dtype=None) -> np.ndarray:
+    if hasattr(a, "detach"):  # torch tensor
+        a = a.detach().cpu().numpy()
+    a = np.asarray(a)
+    if dtype is not None and a.dtype != dtype:
+        a = a.astype(dtype)
+    return np.ascontiguousarray(a)
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class UnifiedEngine:
+    """UnifiedEngine(config, token_embd, output_norm, output_proj, cos_table, sin_table,
+    layers_dict, lm_head_preq2_meta=None, lm_head_preq2_quant=None)  (:2662-2682)."""
+
+    def __init__(self, config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
+                 lm_head_preq2_meta=None, lm_head_preq2_quant=None):
+        lib = _lib.load()
+        self._lib = lib
+        self.config_ = config
+        self._e = ctypes.c_void_p()
+        _lib.check(lib.asdsl_b200_engine_create(ctypes.byref(config._c()), ctypes.byref(self._e)),
+                   "UnifiedEngine")
+        try:
+            self._load(config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
+                       lm_head_preq2_meta, lm_head_preq2_quant)
+        except BaseException:
+            lib.asdsl_b200_engine_destroy(self._e)
+            self._e = None
+            raise
+        self._logits = np.empty(config.vocab_size, dtype=np.float32)
+
+    # ------------------------------------------------------------------ construction
+    def _load(self, cfg, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict, lm_meta,
+              lm_quant):
+        lib, e = self._lib, self._e
+        emb = _host(token_embd)
+        if emb.dtype not in (np.float16, np.float32):
+            emb = emb.astype(np.float32)
+        if emb.size != cfg.vocab_size * cfg.hidden_size:
+            raise ValueError("token_embd must be (vocab_size, hidden_size)")
+        norm = _host(output_norm, np.float32).ravel()
+        half = cfg.rotary_dim // 2
+        cos = _host(cos_table, np.float32)
+        sin = _host(sin_table, np.float32)
+        if norm.size != cfg.hidden_size:
+            raise ValueError("output_norm must have hidden_size elements")
+        if cos.size < cfg.max_seq_len * half or sin.size < cfg.max_seq_len * half:
+            raise ValueError("cos/sin tables must be (max_seq_len, rotary_dim/2)")
+        _lib.check(lib.asdsl_b200_engine_set_globals(e, _ptr(emb), int(emb.dtype == np.float16), _ptr(norm),
+                                                     _ptr(cos), _ptr(sin)), "UnifiedEngine")
+        if output_proj is not None:
+            op = _host(output_proj)
+            if op.dtype not in (np.float16, np.float32):
+                op = op.astype(np.float32)
+            if op.size != cfg.vocab_size * cfg.hidden_size:
+                raise ValueError("output_proj must be (vocab_size, hidden_size)")
+            _lib.check(lib.asdsl_b200_engine_set_output_proj(e, _ptr(op), int(op.dtype == np.float16)),
+                       "UnifiedEngine")
+        if lm_meta is not None and lm_quant is not None:
+            m = _host(lm_meta, np.uint8).ravel()
+            q = _host(lm_quant, np.uint8).ravel()
+            _lib.check(lib.asdsl_b200_engine_set_lm_head_preq2(e, _ptr(m), m.size, _ptr(q), q.size), "UnifiedEngine")
+        use_c01, use_c03 = _env_on("ASDSL_C01"), _env_on("ASDSL_C03")
+        for i in range(cfg.num_layers):
+            L = layers_dict[i]
+            ra = _host(L["rms_att"], np.float32).ravel()
+            rf = _host(L["rms_ffn"], np.float32).ravel()
+            _lib.check(lib.asdsl_b200_engine_set_layer_norms(e, i, _ptr(ra), _ptr(rf)), "UnifiedEngine")
+            for w, name in enumerate(_PROJ):
+                rows, cols = self._shape(cfg, w)
+                g128 = (use_c01 and name in ("gate_up_proj", "down_proj")) or \
+                       (use_c03 and name in ("qkv_proj", "o_proj"))
+                if g128 and f"{name}_g128" in L:
+                    b = _host(L[f"{name}_g128"], np.uint8).ravel()
+                    _lib.check(lib.asdsl_b200_engine_set_projection(e, i, w, _lib.FMT_Q4_128, _ptr(b), b.size,
+                                                                    None, 0), "UnifiedEngine")
+                    continue
+                if f"{name}_meta" in L and f"{name}_quant" in L:
+                    m = _host(L[f"{name}_meta"], np.uint8).ravel()
+                    q = _host(L[f"{name}_quant"], np.uint8).ravel()
+                elif name in L:
+                    m, q = repack_preq_blocks_to_preq2(_host(L[name], np.uint8).ravel(), rows, cols, 32)
+                    m, q = m.ravel(), q.ravel()
+                else:
+                    raise KeyError(name)
+                _lib.check(lib.asdsl_b200_engine_set_projection(e, i, w, _lib.FMT_PREQ2, _ptr(m), m.size, _ptr(q),
+                                                                q.size), "UnifiedEngine")
+        _lib.check(lib.asdsl_b200_engine_finalize(e), "UnifiedEngine")
+
+    @staticmethod
+    def _shape(cfg, which: int):
+        qd = cfg.num_heads * cfg.head_dim
+        kvd = cfg.num_kv_heads * cfg.head_dim
+        return [(qd + 2 * kvd, cfg.hidden_size), (cfg.hidden_size, qd), (2 * cfg.intermediate_size, cfg.hidden_size),
+                (cfg.hidden_size, cfg.intermediate_size)][which]
+
+    def close(self):
+        if getattr(self, "_e", None):
+            self._lib.asdsl_b200_engine_destroy(self._e)
+            self._e = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------------ decode
+    def forward_token(self, token: int, pos: int) -> np.ndarray:
+        """Logits of one decode step; the returned buffer is reused by the next call (:2485-2492)."""
+        _lib.check(self._lib.asdsl_b200_engine_forward_token(self._e, int(token), int(pos), _ptr(self._logits), None),
+                   "forward_token")
+        return self._logits
+
+    def forward_token_prefill(self, token: int, pos: int) -> None:
+        """Forward one token updating KV; skip lm_head (:2494-2497)."""
+        _lib.check(self._lib.asdsl_b200_engine_forward_token(self._e, int(token), int(pos), None, None),
+                   "forward_token_prefill")
+
+    def forward_token_argmax(self, token: int, pos: int) -> int:
+        """Single decode step; returns the argmax token id (:2499-2506)."""
+        out = ctypes.c_int32(0)
+        _lib.check(self._lib.asdsl_b200_engine_forward_token(self._e, int(token), int(pos), _ptr(self._logits),
+                                                             ctypes.byref(out)), "forward_token_argmax")
+        return int(out.value)
+
+    def generate(self, prompt, max_tokens: int) -> list[int]:
+        return self.generate_with_stops(prompt, max_tokens, [])
+
+    def generate_with_stops(self, prompt, max_tokens: int, stop_tokens) -> list[int]:
+        p = np.ascontiguousarray(np.asarray(list(prompt), dtype=np.int32))
+        s = np.ascontiguousarray(np.asarray(list(stop_tokens), dtype=np.int32))
+        mt = max(int(max_tokens), 0)
+        out = np.zeros(p.size + mt + 1, dtype=np.int32)
+        n = ctypes.c_int(0)
+        rc = self._lib.asdsl_b200_engine_generate(self._e, _ptr(p) if p.size else None, int(p.size), mt,
+                                                  _ptr(s) if s.size else None, int(s.size), _ptr(out), int(out.size),
+                                                  ctypes.byref(n))
+        _lib.check(rc, "generate")
+        return [int(t) for t in out[: n.value]]
+
+    # ------------------------------------------------------------------ session / KV
+    def reset_session(self) -> None:
+        _lib.check(self._lib.asdsl_b200_engine_reset_session(self._e), "reset_session")
+
+    def get_kv_seq_len(self) -> int:
+        v = ctypes.c_int(0)
+        _lib.check(self._lib.asdsl_b200_engine_get_kv_seq_len(self._e, ctypes.byref(v)), "get_kv_seq_len")
+        return int(v.value)
+
+    def truncate_kv(self, new_len: int) -> None:
+        _lib.check(self._lib.asdsl_b200_engine_truncate_kv(self._e, int(new_len)), "truncate_kv")
+
+    def snapshot_kv(self) -> None:
+        _lib.check(self._lib.asdsl_b200_engine_snapshot_kv(self._e), "snapshot_kv")
+
+    def restore_kv(self) -> None:
+        _lib.check(self._lib.asdsl_b200_engine_restore_kv(self._e), "restore_kv")
+
+    def export_lm_head_preq2(self):
+        """Copy of the lm_head preq2 blobs (meta, quant) (:2470-2483)."""
+        cfg = self.config_
+        fmt = ctypes.c_int(-1)
+        _lib.check(self._lib.asdsl_b200_engine_export_lm_head(self._e, ctypes.byref(fmt), None, 0, None, 0),
+                   "export_lm_head_preq2")
+        if fmt.value != _lib.FMT_PREQ2:
+            raise RuntimeError("export_lm_head_preq2: lm_head preq2 not ready")
+        ng = cfg.hidden_size // 32
+        meta = np.empty(cfg.vocab_size * ng * 4, dtype=np.uint8)
+        quant = np.empty(((cfg.vocab_size + 3) // 4) * ng * 64, dtype=np.uint8)
+        _lib.check(self._lib.asdsl_b200_engine_export_lm_head(self._e, ctypes.byref(fmt), _ptr(meta), meta.size,
+                                                              _ptr(quant), quant.size), "export_lm_head_preq2")
+        return meta, quant
+
+    # ------------------------------------------------------------------ device-level access
+    def stream_ptr(self) -> int:
+        s = ctypes.c_void_p()
+        _lib.check(self._lib.asdsl_b200_engine_stream(self._e, ctypes.byref(s)), "stream")
+        return int(s.value or 0)
+
+    def set_position(self, pos: int, token: int = -1) -> None:
+        _lib.check(self._lib.asdsl_b200_engine_set_position(self._e, int(pos), int(token)), "set_position")
+
+    def replay(self, n: int, decode: bool = True) -> None:
+        """Enqueue n decode (or prefill) graph replays on the engine stream without synchronising."""
+        _lib.check(self._lib.asdsl_b200_engine_replay(self._e, 1 if decode else 0, int(n)), "replay")
+
+    _BUFFERS = ("resid", "qkv", "att", "h", "logits", "kq", "vq", "ks", "vs")
+
+    def read_buffer(self, name: str) -> np.ndarray:
+        """Host copy of an engine buffer (tests): the last layer's values for the activations."""
+        cfg = self.config_
+        qd, kvd = cfg.num_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim
+        per_codes = cfg.num_layers * cfg.max_seq_len * kvd
+        per_scales = cfg.num_layers * cfg.max_seq_len * cfg.num_kv_heads * (cfg.head_dim // 64)
+        shapes = {"resid": (cfg.hidden_size, np.float32), "qkv": (qd + 2 * kvd, np.float32),
+                  "att": (qd, np.float32), "h": (cfg.intermediate_size, np.float32),
+                  "logits": (cfg.vocab_size, np.float32), "kq": (per_codes, np.int8), "vq": (per_codes, np.int8),
+                  "ks": (per_scales, np.float32), "vs": (per_scales, np.float32)}
+        n, dt = shapes[name]
+        out = np.empty(n, dtype=dt)
+        _lib.check(self._lib.asdsl_b200_engine_read_buffer(self._e, self._BUFFERS.index(name), _ptr(out), out.nbytes),
+                   "read_buffer")
+        return out
+
+
+def engine_from_model(model: dict, lm_head_group_size: int = 32, max_seq_len: int | None = None,
+                      use_preq2_cache: bool = False) -> UnifiedEngine:
+    """UnifiedEngine over a synthetic model of asdsl_b200.inference.synthetic.build_model, wired as
+    the reference's unified_bridge.build_unified_engine does (tied fp16 embedding as lm_head source)."""
+    c = model["config"]
+    cfg = EngineConfig()
+    cfg.num_layers = c["num_layers"]
+    cfg.hidden_size = c["hidden"]
+    cfg.num_heads = c["n_heads"]
+    cfg.num_kv_heads = c["n_kv_heads"]
+    cfg.head_dim = c["head_dim"]
+    cfg.intermediate_size = c["inter"]
+    cfg.vocab_size = c["vocab"]
+    cfg.rms_norm_eps = c["eps"]
+    cfg.group_size = 32
+    cfg.lm_head_group_size = lm_head_group_size
+    cfg.max_seq_len = max_seq_len or c["max_seq"]
+    cfg.rotary_dim = c["rotary_dim"]
+    cfg.weight_format = 0
+    layers = {i: L for i, L in enumerate(model["layers"])}
+    meta = model.get("lm_meta") if use_preq2_cache else None
+    quant = model.get("lm_quant") if use_preq2_cache else None
+    return UnifiedEngine(cfg, model["embed_f16"], model["output_norm"], None if meta is not None else model["embed_f16"],
+                         model["cos"], model["sin"], layers, meta, quant)

@@ -493,3 +493,6 @@ int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const 
 }
 
 }  // extern "C"
+
+// device-resident decode engine (asdsl_b200_engine_*)
+#include "engine.cuh"

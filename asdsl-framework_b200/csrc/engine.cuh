@@ -1,0 +1,809 @@
+// engine.cuh -- device-resident decode engine behind the C ABI (asdsl_b200_engine_*).
+//
+// Mirrors UnifiedEngine (asdsl/kernels/native/unified_engine.cpp, .h) for the decode
+// path: forward_token :1339-1688, generate :1717-1764, reset_session :1325-1337,
+// snapshot_kv / restore_kv / truncate_kv :1285-1307.
+//
+// One decode step is a fixed kernel sequence on the engine's stream:
+//   embed -> per layer [ qkv GEMV (RMSNorm + A8 prologue) -> attention (RoPE, int8 KV
+//   write, GQA) -> o GEMV (+= residual) -> gate_up GEMV (RMSNorm + A8 prologue, SiLU*up
+//   epilogue) -> down GEMV (+= residual) ] -> lm_head GEMV (RMSNorm + A8, fused argmax)
+//   -> advance (seq[pos+1] = argmax, pos += 1).
+// The position and the token sequence are device-resident, so the sequence is
+// captured once as a CUDA graph ("decode"; "prefill" omits the lm_head) and replayed
+// per token without a host round trip; kernels chain with programmatic dependent
+// launch so each GEMV's weight stream starts while its predecessor drains.
+// Included by asdsl_b200.cu (single translation unit).
+#pragma once
+
+#include <algorithm>
+#include <vector>
+
+#include "engine_ops.cuh"
+
+namespace {
+
+struct EngProj {
+    int fmt = -1;           // ASDSL_B200_FMT_PREQ2 or ASDSL_B200_FMT_Q4_128_BANDED (device layout)
+    uint8_t* w0 = nullptr;  // preq2 meta | banded quant
+    uint8_t* w1 = nullptr;  // preq2 quant | banded scales
+    int rows = 0, cols = 0;
+};
+
+struct EngLayer {
+    float* rms_att = nullptr;
+    float* rms_ffn = nullptr;
+    EngProj p[4];  // qkv, o, gate_up, down
+};
+
+constexpr int kProjQkv = 0, kProjO = 1, kProjGateUp = 2, kProjDown = 3;
+
+}  // namespace
+
+struct asdsl_b200_engine {
+    asdsl_b200_engine_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> allocs;
+    // globals
+    void* embed = nullptr;
+    int embed_f16 = 1;
+    float* out_norm = nullptr;
+    float* cos_t = nullptr;
+    float* sin_t = nullptr;
+    void* out_proj = nullptr;  // lm_head source (fp16 or fp32), dropped after quantization
+    int out_proj_f16 = 1;
+    std::vector<EngLayer> layers;
+    EngProj lm;
+    bool lm_ready = false;
+    // activations
+    float *resid = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    // int8 KV cache [layer][pos][kv_head][128] + fp32 scales [layer][pos][kv_head][2]
+    int8_t *kq = nullptr, *vq = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    long long kv_codes_per_layer = 0, kv_scales_per_layer = 0;
+    // decode state
+    asdsl::DecodeState* st = nullptr;
+    int* seq = nullptr;  // [max_seq + 1]
+    float* am_val = nullptr;
+    int* am_idx = nullptr;
+    uint8_t* am_scratch = nullptr;
+    // pinned host staging
+    int* h_stage = nullptr;  // [4]: pos, token, argmax, status
+    cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
+    bool finalized = false;
+    int kv_seq_len = 0;
+    std::vector<int> snapshots;
+};
+
+namespace {
+
+using asdsl::kEcuda;
+using asdsl::kEinval;
+using asdsl::kErange;
+using asdsl::kEtimeout;
+using asdsl::kOk;
+using asdsl::set_error;
+
+template <typename T>
+int eng_alloc(asdsl_b200_engine* e, T** p, size_t bytes) {
+    void* q = nullptr;
+    if (bytes == 0) bytes = 16;
+    const cudaError_t rc = cudaMalloc(&q, bytes);
+    if (rc != cudaSuccess)
+        return set_error(asdsl::kEnomem, std::string("engine: cudaMalloc of ") + std::to_string(bytes) +
+                                             " bytes failed: " + cudaGetErrorString(rc));
+    e->allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return kOk;
+}
+
+void eng_free(asdsl_b200_engine* e, void* p) {
+    if (!p) return;
+    for (auto& q : e->allocs)
+        if (q == p) {
+            cudaFree(q);
+            q = nullptr;
+        }
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+void proj_shape(const asdsl_b200_engine_config& c, int which, int* rows, int* cols) {
+    const int qd = c.num_heads * c.head_dim, kvd = c.num_kv_heads * c.head_dim;
+    switch (which) {
+        case kProjQkv: *rows = qd + 2 * kvd; *cols = c.hidden_size; break;
+        case kProjO: *rows = c.hidden_size; *cols = qd; break;
+        case kProjGateUp: *rows = 2 * c.intermediate_size; *cols = c.hidden_size; break;
+        default: *rows = c.hidden_size; *cols = c.intermediate_size; break;
+    }
+}
+
+// one GEMV of the decode step, with the prologue / epilogue its position needs
+template <int PRO, int EPI>
+int eng_gemv(const EngProj& p, GemvArgs ga, long long pair_off_rows, cudaStream_t s) {
+    StreamIn in[2];
+    const long long M = pair_off_rows > 0 ? pair_off_rows : p.rows;
+    const long long nb = (M + 3) / 4;
+    if (p.fmt == ASDSL_B200_FMT_PREQ2) {
+        preq2_streams(in, p.w0, p.w1, p.rows, p.cols);
+        ga.gs = 32;
+        return launch_stream_gemv<kFmtPreq2, PRO, EPI>(in, 2, nb, pair_off_rows > 0 ? nb : 0, ga, s);
+    }
+    q128b_streams(in, p.w0, p.w1, p.rows, p.cols);
+    ga.gs = 128;
+    return launch_stream_gemv<kFmtQ128B, PRO, EPI>(in, 2, nb, pair_off_rows > 0 ? nb : 0, ga, s);
+}
+
+int launch_small(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (pdl && launch_policy().pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    ASDSL_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
+    return kOk;
+}
+
+// enqueue one forward step (token seq[pos] at st->pos) on e->stream
+int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
+    const asdsl_b200_engine_config& c = e->cfg;
+    cudaStream_t s = e->stream;
+    const int H = c.hidden_size;
+    {
+        const int blocks = (H + 255) / 256;
+        if (e->embed_f16) {
+            const uint16_t* emb = static_cast<const uint16_t*>(e->embed);
+            void* args[] = {&emb, &e->resid, &e->st, &e->seq, const_cast<int*>(&c.hidden_size),
+                            const_cast<int*>(&c.vocab_size), const_cast<int*>(&c.max_seq_len)};
+            if (int rc = launch_small(reinterpret_cast<const void*>(&k_embed<uint16_t>), dim3(blocks), dim3(256),
+                                      args, s, false))
+                return rc;
+        } else {
+            const float* emb = static_cast<const float*>(e->embed);
+            void* args[] = {&emb, &e->resid, &e->st, &e->seq, const_cast<int*>(&c.hidden_size),
+                            const_cast<int*>(&c.vocab_size), const_cast<int*>(&c.max_seq_len)};
+            if (int rc = launch_small(reinterpret_cast<const void*>(&k_embed<float>), dim3(blocks), dim3(256), args,
+                                      s, false))
+                return rc;
+        }
+    }
+    for (int l = 0; l < c.num_layers; ++l) {
+        const EngLayer& L = e->layers[l];
+        // qkv = W_qkv . A8(RMSNorm(resid) * rms_att)
+        {
+            GemvArgs ga = base_args(L.p[kProjQkv].rows, H, 32);
+            ga.x = e->resid;
+            ga.norm_w = L.rms_att;
+            ga.eps = c.rms_norm_eps;
+            ga.y = e->qkv;
+            if (int rc = eng_gemv<kProRmsA8, kEpiStore>(L.p[kProjQkv], ga, 0, s)) return rc;
+        }
+        // attention (RoPE, KV write, GQA) -> att
+        {
+            asdsl::AttnArgs aa;
+            aa.qkv = e->qkv;
+            aa.out = e->att;
+            aa.kq = e->kq + l * e->kv_codes_per_layer;
+            aa.vq = e->vq + l * e->kv_codes_per_layer;
+            aa.ks = e->ks + l * e->kv_scales_per_layer;
+            aa.vs = e->vs + l * e->kv_scales_per_layer;
+            aa.cos_t = e->cos_t;
+            aa.sin_t = e->sin_t;
+            aa.st = e->st;
+            aa.n_heads = c.num_heads;
+            aa.n_kv = c.num_kv_heads;
+            aa.rot = c.rotary_dim;
+            aa.max_seq = c.max_seq_len;
+            void* args[] = {&aa};
+            if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention), dim3(c.num_heads),
+                                      dim3(asdsl::kAttnWarps * 32), args, s, true))
+                return rc;
+        }
+        // resid += W_o . A8(att)
+        {
+            GemvArgs ga = base_args(H, L.p[kProjO].cols, 32);
+            ga.x = e->att;
+            ga.resid = e->resid;
+            if (int rc = eng_gemv<kProA8, kEpiResid>(L.p[kProjO], ga, 0, s)) return rc;
+        }
+        // h = silu(gate) * up, gate_up = W_gu . A8(RMSNorm(resid) * rms_ffn)
+        {
+            GemvArgs ga = base_args(c.intermediate_size, H, 32);
+            ga.x = e->resid;
+            ga.norm_w = L.rms_ffn;
+            ga.eps = c.rms_norm_eps;
+            ga.h = e->h;
+            if (int rc = eng_gemv<kProRmsA8, kEpiSilu>(L.p[kProjGateUp], ga, c.intermediate_size, s)) return rc;
+        }
+        // resid += W_down . A8(h)
+        {
+            GemvArgs ga = base_args(H, c.intermediate_size, 32);
+            ga.x = e->h;
+            ga.resid = e->resid;
+            if (int rc = eng_gemv<kProA8, kEpiResid>(L.p[kProjDown], ga, 0, s)) return rc;
+        }
+    }
+    if (with_lm) {
+        GemvArgs ga = base_args(c.vocab_size, H, 32);
+        ga.x = e->resid;
+        ga.norm_w = e->out_norm;
+        ga.eps = c.rms_norm_eps;
+        ga.y = e->logits;
+        ga.counter = reinterpret_cast<unsigned int*>(e->am_scratch);
+        ga.part_val = reinterpret_cast<float*>(e->am_scratch + 256);
+        ga.part_idx = reinterpret_cast<int*>(e->am_scratch + 256 + 4 * 1024);
+        ga.out_val = e->am_val;
+        ga.out_idx = e->am_idx;
+        ga.row_base = 0;
+        if (int rc = eng_gemv<kProRmsA8, kEpiArgmax>(e->lm, ga, 0, s)) return rc;
+        void* args[] = {&e->st, &e->seq, &e->am_idx, const_cast<int*>(&c.max_seq_len)};
+        if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_advance_decode), dim3(1), dim3(32), args, s,
+                                  true))
+            return rc;
+    } else {
+        void* args[] = {&e->st, const_cast<int*>(&c.max_seq_len)};
+        if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_advance_prefill), dim3(1), dim3(32), args,
+                                  s, true))
+            return rc;
+    }
+    return kOk;
+}
+
+int eng_capture(asdsl_b200_engine* e, bool with_lm, cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    ASDSL_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = eng_enqueue_step(e, with_lm);
+    const cudaError_t ec = cudaStreamEndCapture(e->stream, &g);
+    if (rc != kOk) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    ASDSL_CUDA(ec);
+    const cudaError_t ei = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    ASDSL_CUDA(ei);
+    return kOk;
+}
+
+// set pos (and seq[pos] = token when token >= 0) from the pinned stage, stream-ordered
+int eng_set_pos(asdsl_b200_engine* e, int pos, int token) {
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));  // the pinned stage may still be read by a prior copy
+    e->h_stage[0] = pos;
+    e->h_stage[1] = token;
+    ASDSL_CUDA(cudaMemcpyAsync(&e->st->pos, &e->h_stage[0], sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    if (token >= 0)
+        ASDSL_CUDA(cudaMemcpyAsync(e->seq + pos, &e->h_stage[1], sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    return kOk;
+}
+
+int eng_zero_kv_from(asdsl_b200_engine* e, int from) {
+    if (from < 0) from = 0;
+    if (from >= e->cfg.max_seq_len) return kOk;
+    const long long per_pos_codes = static_cast<long long>(e->cfg.num_kv_heads) * e->cfg.head_dim;
+    const long long per_pos_scales = static_cast<long long>(e->cfg.num_kv_heads) * (e->cfg.head_dim / 64);
+    asdsl::k_kv_fill<<<sm_count() * 4, 256, 0, e->stream>>>(e->kq, e->vq, e->ks, e->vs, e->cfg.num_layers,
+                                                            e->kv_codes_per_layer, e->kv_scales_per_layer,
+                                                            per_pos_codes * from, per_pos_scales * from);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int eng_status(asdsl_b200_engine* e) {
+    unsigned int* sp = device_status_ptr();
+    if (!sp) return set_error(kEcuda, "cannot resolve the device status word");
+    ASDSL_CUDA(cudaMemcpyAsync(&e->h_stage[3], sp, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    if (e->h_stage[3] != 0)
+        return set_error(kEtimeout, "engine: a kernel gave up a bounded wait (device status " +
+                                        std::to_string(e->h_stage[3]) + ")");
+    return kOk;
+}
+
+#define ENG_CHECK(e)                                                                        \
+    do {                                                                                    \
+        if (!(e)) return set_error(kEinval, "engine: null engine");                         \
+    } while (0)
+#define ENG_READY(e)                                                                        \
+    do {                                                                                    \
+        ENG_CHECK(e);                                                                       \
+        if (!(e)->finalized) return set_error(kEinval, "engine: finalize() has not run");   \
+    } while (0)
+
+}  // namespace
+
+extern "C" {
+
+int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_engine** out) {
+    if (!cfg || !out) return set_error(kEinval, "engine_create: null pointer");
+    *out = nullptr;
+    const asdsl_b200_engine_config& c = *cfg;
+    if (c.num_layers <= 0 || c.hidden_size <= 0 || c.num_heads <= 0 || c.num_kv_heads <= 0 || c.vocab_size <= 0 ||
+        c.intermediate_size <= 0 || c.max_seq_len <= 0)
+        return set_error(kEinval, "engine_create: dimensions must be positive");
+    if (c.head_dim != 128) return set_error(kEinval, "engine_create: head_dim must be 128");
+    if (c.num_heads % c.num_kv_heads) return set_error(kEinval, "engine_create: num_heads % num_kv_heads != 0");
+    if (c.rotary_dim < 0 || c.rotary_dim > c.head_dim || (c.rotary_dim & 1))
+        return set_error(kEinval, "engine_create: rotary_dim must be even and <= head_dim");
+    if (c.weight_format != 0 || c.group_size != 32)
+        return set_error(kEinval, "engine_create: only weight_format 0 with group_size 32 is supported");
+    const int lm_gs = c.lm_head_group_size > 0 ? c.lm_head_group_size : c.group_size;
+    if (lm_gs != 32 && lm_gs != 128) return set_error(kEinval, "engine_create: lm_head_group_size must be 32 or 128");
+    if (c.hidden_size % 128 || c.intermediate_size % 128 || (c.num_heads * c.head_dim) % 128)
+        return set_error(kEinval, "engine_create: hidden, intermediate and q dims must be multiples of 128");
+    if (c.hidden_size > 17920 || c.intermediate_size > 17920)
+        return set_error(kEinval, "engine_create: in_features exceeds 17920");
+    if (sm_count() > 1024) return set_error(kEinval, "engine_create: too many SMs for the argmax scratch layout");
+
+    auto* e = new asdsl_b200_engine();
+    e->cfg = c;
+    if (e->cfg.lm_head_group_size <= 0) e->cfg.lm_head_group_size = c.group_size;
+    cudaGetDevice(&e->device);
+    int rc = kOk;
+    auto fail = [&](int code) {
+        asdsl_b200_engine_destroy(e);
+        return code;
+    };
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(set_error(kEcuda, "engine_create: cannot create stream"));
+    const int qd = c.num_heads * c.head_dim, kvd = c.num_kv_heads * c.head_dim;
+    e->layers.resize(c.num_layers);
+    e->kv_codes_per_layer = static_cast<long long>(c.max_seq_len) * kvd;
+    e->kv_scales_per_layer = static_cast<long long>(c.max_seq_len) * c.num_kv_heads * (c.head_dim / 64);
+    if ((rc = eng_alloc(e, &e->resid, 4ull * c.hidden_size)) || (rc = eng_alloc(e, &e->qkv, 4ull * (qd + 2 * kvd))) ||
+        (rc = eng_alloc(e, &e->att, 4ull * qd)) || (rc = eng_alloc(e, &e->h, 4ull * c.intermediate_size)) ||
+        (rc = eng_alloc(e, &e->logits, 4ull * c.vocab_size)) ||
+        (rc = eng_alloc(e, &e->kq, static_cast<size_t>(c.num_layers) * e->kv_codes_per_layer)) ||
+        (rc = eng_alloc(e, &e->vq, static_cast<size_t>(c.num_layers) * e->kv_codes_per_layer)) ||
+        (rc = eng_alloc(e, &e->ks, 4ull * c.num_layers * e->kv_scales_per_layer)) ||
+        (rc = eng_alloc(e, &e->vs, 4ull * c.num_layers * e->kv_scales_per_layer)) ||
+        (rc = eng_alloc(e, &e->st, sizeof(asdsl::DecodeState))) ||
+        (rc = eng_alloc(e, &e->seq, 4ull * (c.max_seq_len + 1))) || (rc = eng_alloc(e, &e->am_val, 16)) ||
+        (rc = eng_alloc(e, &e->am_idx, 16)) ||
+        (rc = eng_alloc(e, &e->am_scratch, asdsl_b200_argmax_scratch_bytes())) ||
+        (rc = eng_alloc(e, &e->out_norm, 4ull * c.hidden_size)) ||
+        (rc = eng_alloc(e, &e->cos_t, 4ull * c.max_seq_len * (c.rotary_dim / 2 > 0 ? c.rotary_dim / 2 : 1))) ||
+        (rc = eng_alloc(e, &e->sin_t, 4ull * c.max_seq_len * (c.rotary_dim / 2 > 0 ? c.rotary_dim / 2 : 1))))
+        return fail(rc);
+    for (auto& L : e->layers)
+        if ((rc = eng_alloc(e, &L.rms_att, 4ull * c.hidden_size)) || (rc = eng_alloc(e, &L.rms_ffn, 4ull * c.hidden_size)))
+            return fail(rc);
+    if (cudaHostAlloc(reinterpret_cast<void**>(&e->h_stage), 16 * sizeof(int), cudaHostAllocDefault) != cudaSuccess)
+        return fail(set_error(kEcuda, "engine_create: cannot allocate pinned staging"));
+    if (cudaMemsetAsync(e->am_scratch, 0, asdsl_b200_argmax_scratch_bytes(), e->stream) != cudaSuccess ||
+        cudaMemsetAsync(e->st, 0, sizeof(asdsl::DecodeState), e->stream) != cudaSuccess ||
+        cudaMemsetAsync(e->seq, 0, 4ull * (c.max_seq_len + 1), e->stream) != cudaSuccess)
+        return fail(set_error(kEcuda, "engine_create: memset failed"));
+    if ((rc = eng_zero_kv_from(e, 0))) return fail(rc);
+    if (cudaStreamSynchronize(e->stream) != cudaSuccess) return fail(set_error(kEcuda, "engine_create: sync failed"));
+    *out = e;
+    return kOk;
+}
+
+int asdsl_b200_engine_destroy(asdsl_b200_engine* e) {
+    if (!e) return kOk;
+    DeviceGuard dg(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    if (e->g_decode) cudaGraphExecDestroy(e->g_decode);
+    if (e->g_prefill) cudaGraphExecDestroy(e->g_prefill);
+    for (void* p : e->allocs)
+        if (p) cudaFree(p);
+    if (e->h_stage) cudaFreeHost(e->h_stage);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return kOk;
+}
+
+int asdsl_b200_engine_set_globals(asdsl_b200_engine* e, const void* token_embd, int embd_is_f16,
+                                  const float* output_norm, const float* cos_table, const float* sin_table) {
+    ENG_CHECK(e);
+    if (!token_embd || !output_norm || !cos_table || !sin_table)
+        return set_error(kEinval, "engine_set_globals: null pointer");
+    if (e->finalized) return set_error(kEinval, "engine_set_globals: engine already finalized");
+    DeviceGuard dg(e->device);
+    const asdsl_b200_engine_config& c = e->cfg;
+    const size_t esz = (embd_is_f16 ? 2ull : 4ull) * c.vocab_size * c.hidden_size;
+    if (e->embed) eng_free(e, e->embed);
+    e->embed = nullptr;
+    if (int rc = eng_alloc(e, reinterpret_cast<uint8_t**>(&e->embed), esz)) return rc;
+    e->embed_f16 = embd_is_f16 ? 1 : 0;
+    const size_t half = c.rotary_dim / 2;
+    ASDSL_CUDA(cudaMemcpy(e->embed, token_embd, esz, cudaMemcpyDefault));
+    ASDSL_CUDA(cudaMemcpy(e->out_norm, output_norm, 4ull * c.hidden_size, cudaMemcpyDefault));
+    if (half) {
+        ASDSL_CUDA(cudaMemcpy(e->cos_t, cos_table, 4ull * c.max_seq_len * half, cudaMemcpyDefault));
+        ASDSL_CUDA(cudaMemcpy(e->sin_t, sin_table, 4ull * c.max_seq_len * half, cudaMemcpyDefault));
+    }
+    return kOk;
+}
+
+int asdsl_b200_engine_set_output_proj(asdsl_b200_engine* e, const void* output_proj, int is_f16) {
+    ENG_CHECK(e);
+    if (!output_proj) return set_error(kEinval, "engine_set_output_proj: null pointer");
+    if (e->finalized) return set_error(kEinval, "engine_set_output_proj: engine already finalized");
+    DeviceGuard dg(e->device);
+    const size_t sz = (is_f16 ? 2ull : 4ull) * e->cfg.vocab_size * e->cfg.hidden_size;
+    if (e->out_proj) eng_free(e, e->out_proj);
+    e->out_proj = nullptr;
+    if (int rc = eng_alloc(e, reinterpret_cast<uint8_t**>(&e->out_proj), sz)) return rc;
+    e->out_proj_f16 = is_f16 ? 1 : 0;
+    ASDSL_CUDA(cudaMemcpy(e->out_proj, output_proj, sz, cudaMemcpyDefault));
+    return kOk;
+}
+
+int asdsl_b200_engine_set_lm_head_preq2(asdsl_b200_engine* e, const uint8_t* meta, size_t meta_bytes,
+                                        const uint8_t* quant, size_t quant_bytes) {
+    ENG_CHECK(e);
+    if (!meta || !quant) return set_error(kEinval, "engine_set_lm_head_preq2: null pointer");
+    if (e->finalized) return set_error(kEinval, "engine_set_lm_head_preq2: engine already finalized");
+    const asdsl_b200_engine_config& c = e->cfg;
+    const long long ng = c.hidden_size / 32;
+    const size_t em = static_cast<size_t>(c.vocab_size) * ng * 4;
+    const size_t eq = static_cast<size_t>((c.vocab_size + 3) / 4) * ng * 64;
+    // as the reference constructor: blobs of the wrong size (or a g128 lm_head) are ignored
+    if (c.lm_head_group_size != 32 || meta_bytes != em || quant_bytes != eq) return kOk;
+    DeviceGuard dg(e->device);
+    if (!e->lm.w0 || e->lm.fmt != ASDSL_B200_FMT_PREQ2) {
+        if (int rc = eng_alloc(e, &e->lm.w0, em)) return rc;
+        if (int rc = eng_alloc(e, &e->lm.w1, eq)) return rc;
+    }
+    ASDSL_CUDA(cudaMemcpy(e->lm.w0, meta, em, cudaMemcpyDefault));
+    ASDSL_CUDA(cudaMemcpy(e->lm.w1, quant, eq, cudaMemcpyDefault));
+    e->lm.fmt = ASDSL_B200_FMT_PREQ2;
+    e->lm.rows = c.vocab_size;
+    e->lm.cols = c.hidden_size;
+    e->lm_ready = true;
+    return kOk;
+}
+
+int asdsl_b200_engine_set_layer_norms(asdsl_b200_engine* e, int layer, const float* rms_att, const float* rms_ffn) {
+    ENG_CHECK(e);
+    if (!rms_att || !rms_ffn) return set_error(kEinval, "engine_set_layer_norms: null pointer");
+    if (layer < 0 || layer >= e->cfg.num_layers) return set_error(kErange, "engine_set_layer_norms: layer out of range");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaMemcpy(e->layers[layer].rms_att, rms_att, 4ull * e->cfg.hidden_size, cudaMemcpyDefault));
+    ASDSL_CUDA(cudaMemcpy(e->layers[layer].rms_ffn, rms_ffn, 4ull * e->cfg.hidden_size, cudaMemcpyDefault));
+    return kOk;
+}
+
+int asdsl_b200_engine_set_projection(asdsl_b200_engine* e, int layer, int which, int fmt, const uint8_t* w0,
+                                     size_t w0_bytes, const uint8_t* w1, size_t w1_bytes) {
+    ENG_CHECK(e);
+    if (e->finalized) return set_error(kEinval, "engine_set_projection: engine already finalized");
+    if (layer < 0 || layer >= e->cfg.num_layers) return set_error(kErange, "engine_set_projection: layer out of range");
+    if (which < 0 || which > 3) return set_error(kEinval, "engine_set_projection: projection index must be 0..3");
+    if (!w0) return set_error(kEinval, "engine_set_projection: null pointer");
+    DeviceGuard dg(e->device);
+    int rows = 0, cols = 0;
+    proj_shape(e->cfg, which, &rows, &cols);
+    EngProj& p = e->layers[layer].p[which];
+    if (p.w0) eng_free(e, p.w0);
+    if (p.w1) eng_free(e, p.w1);
+    p = EngProj();
+    p.rows = rows;
+    p.cols = cols;
+    const long long nb = (rows + 3) / 4;
+    if (fmt == ASDSL_B200_FMT_PREQ2) {
+        const long long ng = cols / 32;
+        const size_t em = static_cast<size_t>(rows) * ng * 4, eq = static_cast<size_t>(nb) * ng * 64;
+        if (!w1) return set_error(kEinval, "engine_set_projection: null pointer");
+        if (w0_bytes != em || w1_bytes != eq)
+            return set_error(kEinval, "engine_set_projection: preq2 blob sizes do not match the projection shape");
+        if (int rc = eng_alloc(e, &p.w0, em)) return rc;
+        if (int rc = eng_alloc(e, &p.w1, eq)) return rc;
+        ASDSL_CUDA(cudaMemcpy(p.w0, w0, em, cudaMemcpyDefault));
+        ASDSL_CUDA(cudaMemcpy(p.w1, w1, eq, cudaMemcpyDefault));
+        p.fmt = ASDSL_B200_FMT_PREQ2;
+        return kOk;
+    }
+    if (fmt == ASDSL_B200_FMT_Q4_128) {
+        const long long ng = cols / 128;
+        const size_t eb = static_cast<size_t>(rows) * ng * 66;
+        if (w0_bytes != eb)
+            return set_error(kEinval, "engine_set_projection: Q4_128 blob size does not match the projection shape");
+        uint8_t* raw = nullptr;
+        if (int rc = eng_alloc(e, &raw, eb)) return rc;
+        if (int rc = eng_alloc(e, &p.w0, static_cast<size_t>(nb) * ng * 256)) return rc;
+        if (int rc = eng_alloc(e, &p.w1, static_cast<size_t>(nb) * ng * 8)) return rc;
+        ASDSL_CUDA(cudaMemcpy(raw, w0, eb, cudaMemcpyDefault));
+        int rc = asdsl_b200_relayout_q4_128(raw, p.w0, p.w1, rows, cols, e->stream);
+        if (rc == kOk && cudaStreamSynchronize(e->stream) != cudaSuccess)
+            rc = set_error(kEcuda, "engine_set_projection: relayout failed");
+        eng_free(e, raw);
+        if (rc) return rc;
+        p.fmt = ASDSL_B200_FMT_Q4_128_BANDED;
+        return kOk;
+    }
+    return set_error(kEinval, "engine_set_projection: fmt must be PREQ2 or Q4_128");
+}
+
+int asdsl_b200_engine_finalize(asdsl_b200_engine* e) {
+    ENG_CHECK(e);
+    if (e->finalized) return kOk;
+    DeviceGuard dg(e->device);
+    const asdsl_b200_engine_config& c = e->cfg;
+    if (!e->embed) return set_error(kEinval, "engine_finalize: set_globals() has not run");
+    for (int l = 0; l < c.num_layers; ++l)
+        for (int w = 0; w < 4; ++w)
+            if (e->layers[l].p[w].fmt < 0)
+                return set_error(kEinval, "engine_finalize: layer " + std::to_string(l) + " projection " +
+                                              std::to_string(w) + " has no weights");
+    if (!e->lm_ready) {
+        if (!e->out_proj) return set_error(kEinval, "engine_finalize: no lm_head source (output_proj or preq2 blobs)");
+        const long long nb = (c.vocab_size + 3) / 4;
+        const unsigned blocks = static_cast<unsigned>(sm_count() * 8);
+        if (c.lm_head_group_size == 32) {
+            const long long ng = c.hidden_size / 32;
+            if (int rc = eng_alloc(e, &e->lm.w0, static_cast<size_t>(c.vocab_size) * ng * 4)) return rc;
+            if (int rc = eng_alloc(e, &e->lm.w1, static_cast<size_t>(nb) * ng * 64)) return rc;
+            ASDSL_CUDA(cudaMemsetAsync(e->lm.w1, 0, static_cast<size_t>(nb) * ng * 64, e->stream));
+            if (e->out_proj_f16)
+                asdsl::k_lmhead_quant_preq2<uint16_t><<<blocks, 256, 0, e->stream>>>(
+                    static_cast<const uint16_t*>(e->out_proj), reinterpret_cast<uint32_t*>(e->lm.w0),
+                    reinterpret_cast<uint4*>(e->lm.w1), c.vocab_size, c.hidden_size);
+            else
+                asdsl::k_lmhead_quant_preq2<float><<<blocks, 256, 0, e->stream>>>(
+                    static_cast<const float*>(e->out_proj), reinterpret_cast<uint32_t*>(e->lm.w0),
+                    reinterpret_cast<uint4*>(e->lm.w1), c.vocab_size, c.hidden_size);
+            e->lm.fmt = ASDSL_B200_FMT_PREQ2;
+        } else {
+            const long long ng = c.hidden_size / 128;
+            if (int rc = eng_alloc(e, &e->lm.w0, static_cast<size_t>(nb) * ng * 256)) return rc;
+            if (int rc = eng_alloc(e, &e->lm.w1, static_cast<size_t>(nb) * ng * 8)) return rc;
+            ASDSL_CUDA(cudaMemsetAsync(e->lm.w0, 0, static_cast<size_t>(nb) * ng * 256, e->stream));
+            ASDSL_CUDA(cudaMemsetAsync(e->lm.w1, 0, static_cast<size_t>(nb) * ng * 8, e->stream));
+            if (e->out_proj_f16)
+                asdsl::k_lmhead_quant_q128b<uint16_t><<<blocks, 256, 0, e->stream>>>(
+                    static_cast<const uint16_t*>(e->out_proj), reinterpret_cast<uint4*>(e->lm.w0),
+                    reinterpret_cast<uint16_t*>(e->lm.w1), c.vocab_size, c.hidden_size);
+            else
+                asdsl::k_lmhead_quant_q128b<float><<<blocks, 256, 0, e->stream>>>(
+                    static_cast<const float*>(e->out_proj), reinterpret_cast<uint4*>(e->lm.w0),
+                    reinterpret_cast<uint16_t*>(e->lm.w1), c.vocab_size, c.hidden_size);
+            e->lm.fmt = ASDSL_B200_FMT_Q4_128_BANDED;
+        }
+        ASDSL_CUDA(cudaGetLastError());
+        e->lm.rows = c.vocab_size;
+        e->lm.cols = c.hidden_size;
+        ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+        e->lm_ready = true;
+    }
+    // the lm_head source is no longer needed (the reference drops it too)
+    if (e->out_proj) {
+        eng_free(e, e->out_proj);
+        e->out_proj = nullptr;
+    }
+    // one eager step of each kind (kernel attributes, module loading), then capture
+    if (int rc = eng_set_pos(e, 0, 0)) return rc;
+    if (int rc = eng_enqueue_step(e, true)) return rc;
+    if (int rc = eng_set_pos(e, 0, 0)) return rc;
+    if (int rc = eng_enqueue_step(e, false)) return rc;
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    if (int rc = eng_status(e)) return rc;
+    if (int rc = eng_capture(e, true, &e->g_decode)) return rc;
+    if (int rc = eng_capture(e, false, &e->g_prefill)) return rc;
+    if (int rc = eng_zero_kv_from(e, 0)) return rc;
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    e->kv_seq_len = 0;
+    e->finalized = true;
+    return kOk;
+}
+
+int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, float* logits, int32_t* argmax) {
+    ENG_READY(e);
+    if (token < 0 || token >= e->cfg.vocab_size)
+        return set_error(kErange, "forward_token: token_id out of vocab range");
+    if (pos < 0 || pos >= e->cfg.max_seq_len) return set_error(kErange, "forward_token: pos out of kv-cache range");
+    DeviceGuard dg(e->device);
+    if (int rc = eng_set_pos(e, pos, token)) return rc;
+    const bool lm = logits || argmax;
+    ASDSL_CUDA(cudaGraphLaunch(lm ? e->g_decode : e->g_prefill, e->stream));
+    if (logits)
+        ASDSL_CUDA(cudaMemcpyAsync(logits, e->logits, 4ull * e->cfg.vocab_size, cudaMemcpyDefault, e->stream));
+    if (argmax) ASDSL_CUDA(cudaMemcpyAsync(&e->h_stage[2], e->am_idx, 4, cudaMemcpyDeviceToHost, e->stream));
+    if (int rc = eng_status(e)) return rc;  // synchronizes the stream
+    if (argmax) *argmax = e->h_stage[2];
+    if (pos + 1 > e->kv_seq_len) e->kv_seq_len = pos + 1;
+    return kOk;
+}
+
+int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int n_prompt, int max_tokens,
+                               const int32_t* stops, int n_stops, int32_t* out, int out_cap, int* n_out) {
+    ENG_READY(e);
+    if (!prompt || !out || !n_out || (n_stops > 0 && !stops)) return set_error(kEinval, "generate: null pointer");
+    if (n_prompt <= 0) return set_error(kEinval, "generate: the prompt must hold at least one token");
+    if (max_tokens < 0) max_tokens = 0;
+    const asdsl_b200_engine_config& c = e->cfg;
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= c.vocab_size)
+            return set_error(kErange, "forward_token: token_id out of vocab range");
+    if (n_prompt > c.max_seq_len) return set_error(kErange, "forward_token: pos out of kv-cache range");
+    // tokens t_0..t_{T-1}; t_j needs the forward of position n + j - 1 (< max_seq)
+    const int room = c.max_seq_len - n_prompt;  // forwards of generated tokens that fit
+    const int producible = max_tokens <= room ? max_tokens : room + 1;
+    if (out_cap < n_prompt + producible) return set_error(kEinval, "generate: output buffer too small");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    ASDSL_CUDA(cudaMemcpyAsync(e->seq, prompt, 4ull * n_prompt, cudaMemcpyHostToDevice, e->stream));
+    if (int rc = eng_set_pos(e, 0, -1)) return rc;
+    for (int i = 0; i + 1 < n_prompt; ++i) ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+    // the last prompt token's forward is the first decode step; without one it is a prefill step
+    if (producible == 0) ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+    int produced = 0, stop_at = -1;
+    const int chunk = n_stops > 0 ? 16 : (producible > 0 ? producible : 1);
+    while (produced < producible && stop_at < 0) {
+        const int n = std::min(chunk, producible - produced);
+        for (int i = 0; i < n; ++i) ASDSL_CUDA(cudaGraphLaunch(e->g_decode, e->stream));
+        ASDSL_CUDA(cudaMemcpyAsync(out + n_prompt + produced, e->seq + n_prompt + produced, 4ull * n,
+                                   cudaMemcpyDeviceToHost, e->stream));
+        if (int rc = eng_status(e)) return rc;
+        for (int i = 0; i < n && n_stops > 0; ++i) {
+            const int t = out[n_prompt + produced + i];
+            for (int s = 0; s < n_stops; ++s)
+                if (stops[s] == t) {
+                    stop_at = produced + i;
+                    break;
+                }
+            if (stop_at >= 0) break;
+        }
+        produced += n;
+    }
+    for (int i = 0; i < n_prompt; ++i) out[i] = prompt[i];
+    if (stop_at >= 0) {
+        // the reference forwards t_0..t_{s-1}: keep KV below n + s
+        const int kv = n_prompt + stop_at;
+        if (int rc = eng_zero_kv_from(e, kv)) return rc;
+        ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+        e->kv_seq_len = std::max(e->kv_seq_len, kv);
+        *n_out = n_prompt + stop_at + 1;
+        return kOk;
+    }
+    if (max_tokens > room) {
+        // the reference's forward of t_room at position max_seq throws
+        e->kv_seq_len = c.max_seq_len;
+        *n_out = n_prompt + produced;
+        return set_error(kErange, "forward_token: pos out of kv-cache range");
+    }
+    if (max_tokens > 0) {
+        // forward of the last token (KV only), as the reference's loop does
+        ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+    }
+    if (int rc = eng_status(e)) return rc;
+    e->kv_seq_len = std::max(e->kv_seq_len, n_prompt + max_tokens);
+    *n_out = n_prompt + produced;
+    return kOk;
+}
+
+int asdsl_b200_engine_replay(asdsl_b200_engine* e, int decode, int n) {
+    ENG_READY(e);
+    if (n < 0) return set_error(kEinval, "engine_replay: n must be >= 0");
+    DeviceGuard dg(e->device);
+    for (int i = 0; i < n; ++i) ASDSL_CUDA(cudaGraphLaunch(decode ? e->g_decode : e->g_prefill, e->stream));
+    return kOk;
+}
+
+int asdsl_b200_engine_set_position(asdsl_b200_engine* e, int pos, int token) {
+    ENG_READY(e);
+    if (pos < 0 || pos >= e->cfg.max_seq_len) return set_error(kErange, "engine_set_position: pos out of range");
+    if (token >= e->cfg.vocab_size) return set_error(kErange, "engine_set_position: token out of range");
+    DeviceGuard dg(e->device);
+    return eng_set_pos(e, pos, token);
+}
+
+int asdsl_b200_engine_stream(asdsl_b200_engine* e, void** stream) {
+    ENG_CHECK(e);
+    if (!stream) return set_error(kEinval, "engine_stream: null pointer");
+    *stream = e->stream;
+    return kOk;
+}
+
+int asdsl_b200_engine_reset_session(asdsl_b200_engine* e) {
+    ENG_CHECK(e);
+    DeviceGuard dg(e->device);
+    if (int rc = eng_zero_kv_from(e, 0)) return rc;
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    e->kv_seq_len = 0;
+    e->snapshots.clear();
+    return kOk;
+}
+
+int asdsl_b200_engine_get_kv_seq_len(asdsl_b200_engine* e, int* out) {
+    ENG_CHECK(e);
+    if (!out) return set_error(kEinval, "get_kv_seq_len: null pointer");
+    *out = e->kv_seq_len;
+    return kOk;
+}
+
+int asdsl_b200_engine_truncate_kv(asdsl_b200_engine* e, int new_len) {
+    ENG_CHECK(e);
+    if (new_len < 0) new_len = 0;
+    if (new_len > e->cfg.max_seq_len) new_len = e->cfg.max_seq_len;
+    DeviceGuard dg(e->device);
+    if (int rc = eng_zero_kv_from(e, new_len)) return rc;
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    e->kv_seq_len = new_len;
+    return kOk;
+}
+
+int asdsl_b200_engine_snapshot_kv(asdsl_b200_engine* e) {
+    ENG_CHECK(e);
+    e->snapshots.push_back(e->kv_seq_len);
+    return kOk;
+}
+
+int asdsl_b200_engine_restore_kv(asdsl_b200_engine* e) {
+    ENG_CHECK(e);
+    if (e->snapshots.empty()) return kOk;
+    const int len = e->snapshots.back();
+    e->snapshots.pop_back();
+    return asdsl_b200_engine_truncate_kv(e, len);
+}
+
+int asdsl_b200_engine_export_lm_head(asdsl_b200_engine* e, int* fmt, uint8_t* w0, size_t w0_bytes, uint8_t* w1,
+                                     size_t w1_bytes) {
+    ENG_READY(e);
+    if (!fmt) return set_error(kEinval, "export_lm_head: null pointer");
+    const asdsl_b200_engine_config& c = e->cfg;
+    const long long nb = (c.vocab_size + 3) / 4;
+    size_t b0, b1;
+    if (e->lm.fmt == ASDSL_B200_FMT_PREQ2) {
+        b0 = static_cast<size_t>(c.vocab_size) * (c.hidden_size / 32) * 4;
+        b1 = static_cast<size_t>(nb) * (c.hidden_size / 32) * 64;
+    } else {
+        b0 = static_cast<size_t>(nb) * (c.hidden_size / 128) * 256;
+        b1 = static_cast<size_t>(nb) * (c.hidden_size / 128) * 8;
+    }
+    *fmt = e->lm.fmt;
+    if (!w0 && !w1) return kOk;  // size query
+    if (!w0 || !w1 || w0_bytes < b0 || w1_bytes < b1) return set_error(kEinval, "export_lm_head: buffers too small");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaMemcpy(w0, e->lm.w0, b0, cudaMemcpyDefault));
+    ASDSL_CUDA(cudaMemcpy(w1, e->lm.w1, b1, cudaMemcpyDefault));
+    return kOk;
+}
+
+int asdsl_b200_engine_read_buffer(asdsl_b200_engine* e, int which, void* host, size_t bytes) {
+    ENG_READY(e);
+    const asdsl_b200_engine_config& c = e->cfg;
+    const size_t qd = static_cast<size_t>(c.num_heads) * c.head_dim, kvd = static_cast<size_t>(c.num_kv_heads) * c.head_dim;
+    const void* src = nullptr;
+    size_t n = 0;
+    switch (which) {
+        case 0: src = e->resid; n = 4ull * c.hidden_size; break;
+        case 1: src = e->qkv; n = 4 * (qd + 2 * kvd); break;
+        case 2: src = e->att; n = 4 * qd; break;
+        case 3: src = e->h; n = 4ull * c.intermediate_size; break;
+        case 4: src = e->logits; n = 4ull * c.vocab_size; break;
+        case 5: src = e->kq; n = static_cast<size_t>(c.num_layers) * e->kv_codes_per_layer; break;
+        case 6: src = e->vq; n = static_cast<size_t>(c.num_layers) * e->kv_codes_per_layer; break;
+        case 7: src = e->ks; n = 4ull * c.num_layers * e->kv_scales_per_layer; break;
+        case 8: src = e->vs; n = 4ull * c.num_layers * e->kv_scales_per_layer; break;
+        default: return set_error(kEinval, "engine_read_buffer: unknown buffer");
+    }
+    if (!host) return set_error(kEinval, "engine_read_buffer: null pointer");
+    if (bytes < n) return set_error(kEinval, "engine_read_buffer: buffer too small (" + std::to_string(n) + " bytes)");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    ASDSL_CUDA(cudaMemcpy(host, src, n, cudaMemcpyDeviceToHost));
+    return kOk;
+}
+
+}  // extern "C"

@@ -1,0 +1,364 @@
+// engine_ops.cuh -- the non-GEMV kernels of the device-resident decode step.
+//
+// Reference: asdsl/kernels/native/unified_engine.cpp (UnifiedEngine).
+//   embedding row (fp16/fp32 -> fp32)        load_embed_row_f32         :181-197
+//   partial RoPE on q and k                  rope_apply_inplace         :768-801
+//   int8 KV write, 64-element blocks         set_kv_cache               :859-920
+//   single-query GQA attention, int8 KV      compute_attention_flash_q8 :922-1027
+//   KV zero-fill from a position             zero_kv_from               :1263-1283
+//   engine lm_head quantizers (g32 / g128)   UnifiedEngine ctor         :320-400, :411-461
+// The position and the token sequence live in device memory (DecodeState, seq[]),
+// so one captured CUDA graph serves every decode step.
+#pragma once
+
+#include "common.cuh"
+
+namespace asdsl {
+
+struct DecodeState {
+    int pos;  // position of the token being forwarded; that token is seq[pos]
+    int pad[3];
+};
+
+template <typename T>
+__device__ __forceinline__ float load_as_float(const T* p);
+template <>
+__device__ __forceinline__ float load_as_float<uint16_t>(const uint16_t* p) {
+    return half_bits_to_float(*p);
+}
+template <>
+__device__ __forceinline__ float load_as_float<float>(const float* p) {
+    return *p;
+}
+
+// resid = fp32(embedding[seq[pos]])  (load_embed_row_f32); the token was range-checked on the host
+template <typename T>
+__global__ void k_embed(const T* __restrict__ emb, float* __restrict__ resid, const DecodeState* st,
+                        const int* seq, int H, int V, int max_seq) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int p = st->pos;
+    if (p < 0 || p >= max_seq) return;
+    const int tok = seq[p];
+    if (tok < 0 || tok >= V) return;
+    const T* row = emb + static_cast<long long>(tok) * H;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x)
+        resid[i] = load_as_float<T>(row + i);
+}
+
+// ---------------------------------------------------------------------------
+// Attention for one decode position.  One CTA per query head, 8 warps; each
+// 8-lane group of a warp takes one position at a time (16 head dims per lane).
+//   * RoPE on the head's q and on its KV head's k (pairs (i, i + rot/2));
+//   * the current position's k (roped) and v are quantized per 64-dim block
+//     exactly as set_kv_cache does; the first query head of each KV group stores
+//     them, every head uses the dequantized values for position `pos` directly;
+//   * online softmax over positions (libm-accurate expf), groups merged in a
+//     fixed order at the end.
+// head_dim is 128 (two 64-dim KV scale blocks); the host checks it.
+// ---------------------------------------------------------------------------
+constexpr int kAttnWarps = 8;
+constexpr int kAttnGroups = kAttnWarps * 4;  // 8-lane position groups per CTA
+constexpr int kAttnHeadDim = 128;
+
+struct AttnArgs {
+    const float* qkv;     // [q_dim + 2 kv_dim] (q | k | v), this layer's projection output
+    float* out;           // [q_dim]
+    int8_t* kq;           // this layer's K codes  [max_seq][n_kv][128]
+    int8_t* vq;           // this layer's V codes
+    float* ks;            // this layer's K scales [max_seq][n_kv][2]
+    float* vs;
+    const float* cos_t;   // [max_seq][rot/2]
+    const float* sin_t;
+    const DecodeState* st;
+    int n_heads, n_kv, rot, max_seq;
+};
+
+__global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
+    constexpr int hd = kAttnHeadDim;
+    __shared__ float s_q[hd];
+    __shared__ float s_k[hd], s_v[hd];  // dequantized current-position k, v
+    __shared__ float s_ks[2], s_vs[2];
+    __shared__ float s_red[2][2][2];   // [k|v][64-block][warp of block]
+    __shared__ float s_m[kAttnGroups], s_l[kAttnGroups];
+    __shared__ float s_num[kAttnGroups][hd];
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int h = blockIdx.x;
+    const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
+    const int g = h / groups;
+    const int half = a.rot / 2;
+    const int pos = a.st->pos;
+    if (pos < 0 || pos >= a.max_seq) return;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
+    const float* cp = a.cos_t + static_cast<long long>(pos) * half;
+    const float* sp = a.sin_t + static_cast<long long>(pos) * half;
+
+    // --- RoPE on q and k: thread t < 128 owns dim t (rope_apply_inplace :768-801) ---
+    float kval = 0.f, vval = 0.f;
+    if (tid < hd) {
+        const float* qh = a.qkv + h * hd;
+        const float* kh = a.qkv + q_dim + g * hd;
+        float qv = qh[tid], kv = kh[tid];
+        if (tid < half) {
+            // o0 = fma(x_first, c, -(x_second * s))
+            qv = __fmaf_rn(qh[tid], cp[tid], -__fmul_rn(qh[tid + half], sp[tid]));
+            kv = __fmaf_rn(kh[tid], cp[tid], -__fmul_rn(kh[tid + half], sp[tid]));
+        } else if (tid < 2 * half) {
+            // o1 = fma(x_first, s, x_second * c)
+            const int i = tid - half;
+            qv = __fmaf_rn(qh[i], sp[i], __fmul_rn(qh[tid], cp[i]));
+            kv = __fmaf_rn(kh[i], sp[i], __fmul_rn(kh[tid], cp[i]));
+        }
+        s_q[tid] = qv;
+        kval = kv;
+        vval = a.qkv[q_dim + kv_dim + g * hd + tid];
+    }
+    // --- quantize this position's k and v per 64-dim block (set_kv_cache :872-917) ---
+    // dims 0..63 are warps 0-1, dims 64..127 warps 2-3
+    const float km = warp_max(fabsf(kval));
+    const float vm = warp_max(fabsf(vval));
+    if (tid < hd && lane == 0) {
+        s_red[0][tid >> 6][(tid >> 5) & 1] = km;
+        s_red[1][tid >> 6][(tid >> 5) & 1] = vm;
+    }
+    __syncthreads();
+    if (tid < 2) {
+        const float ka = fmaxf(s_red[0][tid][0], s_red[0][tid][1]);
+        const float va = fmaxf(s_red[1][tid][0], s_red[1][tid][1]);
+        s_ks[tid] = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
+        s_vs[tid] = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
+    }
+    __syncthreads();
+    if (tid < hd) {
+        const int b = tid >> 6;
+        const float ksc = s_ks[b], vsc = s_vs[b];
+        int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
+        int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
+        qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
+        qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+        s_k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
+        s_v[tid] = __fmul_rn(static_cast<float>(qv), vsc);
+        if (h % groups == 0) {
+            const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
+            a.kq[kb + tid] = static_cast<int8_t>(qk);
+            a.vq[kb + tid] = static_cast<int8_t>(qv);
+            if ((tid & 63) == 0) {
+                const long long sb = (static_cast<long long>(pos) * a.n_kv + g) * 2 + b;
+                a.ks[sb] = ksc;
+                a.vs[sb] = vsc;
+            }
+        }
+    }
+    __syncthreads();
+
+    // --- scores + online softmax: an 8-lane group per position, 16 dims per lane ---
+    const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));
+    const int grp = warp * 4 + (lane >> 3);  // 0 .. kAttnGroups-1
+    const int l8 = lane & 7;                 // dims 16*l8 .. 16*l8+15 (scale block l8 >> 2)
+    float qreg[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qreg[i] = s_q[l8 * 16 + i];
+    float m = -INFINITY, l = 0.0f;
+    float num[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) num[i] = 0.0f;
+    const int npos = pos + 1;
+    for (int p0 = 0; p0 < npos; p0 += kAttnGroups) {
+        const int p = p0 + grp;
+        const bool live = p < npos;  // uniform within the 8-lane group
+        float dot = 0.0f;
+        float vdq[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) vdq[i] = 0.0f;
+        if (live) {
+            if (p == pos) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    dot = __fmaf_rn(qreg[i], s_k[l8 * 16 + i], dot);
+                    vdq[i] = s_v[l8 * 16 + i];
+                }
+            } else {
+                const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
+                const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + (l8 >> 2);
+                const uint4 kw = *reinterpret_cast<const uint4*>(a.kq + rb);
+                const uint4 vw = *reinterpret_cast<const uint4*>(a.vq + rb);
+                const float ksc = a.ks[sb], vsc = a.vs[sb];
+                const uint32_t kk[4] = {kw.x, kw.y, kw.z, kw.w};
+                const uint32_t vv[4] = {vw.x, vw.y, vw.z, vw.w};
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int kc = static_cast<int8_t>((kk[i >> 2] >> (8 * (i & 3))) & 0xFF);
+                    const int vc = static_cast<int8_t>((vv[i >> 2] >> (8 * (i & 3))) & 0xFF);
+                    dot = __fmaf_rn(qreg[i], __fmul_rn(static_cast<float>(kc), ksc), dot);
+                    vdq[i] = __fmul_rn(static_cast<float>(vc), vsc);
+                }
+            }
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+        if (live) {
+            const float s = __fmul_rn(dot, inv_sqrt_d);
+            const float nm = fmaxf(m, s);
+            const float old_scale = (l > 0.0f) ? expf(m - nm) : 0.0f;
+            const float w = expf(s - nm);
+            l = __fmaf_rn(l, old_scale, w);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) num[i] = __fmaf_rn(w, vdq[i], __fmul_rn(num[i], old_scale));
+            m = nm;
+        }
+    }
+    if (l8 == 0) {
+        s_m[grp] = m;
+        s_l[grp] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s_num[grp][l8 * 16 + i] = num[i];
+    __syncthreads();
+    // --- merge the groups in a fixed order --------------------------------------------
+    if (tid < hd) {
+        float M = -INFINITY;
+        for (int k = 0; k < kAttnGroups; ++k)
+            if (s_l[k] > 0.0f) M = fmaxf(M, s_m[k]);
+        float L = 0.0f, acc = 0.0f;
+        for (int k = 0; k < kAttnGroups; ++k) {
+            if (s_l[k] > 0.0f) {
+                const float sc = expf(s_m[k] - M);
+                L = __fmaf_rn(s_l[k], sc, L);
+                acc = __fmaf_rn(s_num[k][tid], sc, acc);
+            }
+        }
+        a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, L));
+    }
+}
+
+// decode step done: seq[pos + 1] = argmax token, pos += 1 (seq holds max_seq + 1 entries;
+// a step at an out-of-range position forwarded nothing and does not advance)
+__global__ void k_advance_decode(DecodeState* st, int* seq, const int* argmax_idx, int max_seq) {
+    grid_dependency_wait();
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int p = st->pos;
+    if (p < 0 || p >= max_seq) return;
+    seq[p + 1] = *argmax_idx;
+    st->pos = p + 1;
+}
+
+// prefill step done (no lm_head): pos += 1, the next token is already in seq
+__global__ void k_advance_prefill(DecodeState* st, int max_seq) {
+    grid_dependency_wait();
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int p = st->pos;
+    if (p < 0 || p >= max_seq) return;
+    st->pos = p + 1;
+}
+
+// zero_kv_from: codes 0 and scales 1.0 for positions >= from in every layer
+__global__ void k_kv_fill(int8_t* kq, int8_t* vq, float* ks, float* vs, int layers, long long per_layer_codes,
+                          long long per_layer_scales, long long from_codes, long long from_scales) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    const long long t0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+    const long long nc = per_layer_codes - from_codes;
+    const long long ns = per_layer_scales - from_scales;
+    for (int l = 0; l < layers; ++l) {
+        for (long long i = t0; i < nc; i += stride) {
+            kq[l * per_layer_codes + from_codes + i] = 0;
+            vq[l * per_layer_codes + from_codes + i] = 0;
+        }
+        for (long long i = t0; i < ns; i += stride) {
+            ks[l * per_layer_scales + from_scales + i] = 1.0f;
+            vs[l * per_layer_scales + from_scales + i] = 1.0f;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// engine lm_head quantizers, bit-exact with the reference constructor:
+// one thread per (row, group); amax < 1e-12 -> scale 0, nibbles 0x88;
+// else scale = fp16_rne(amax * fl(1/7)), q = clamp(round_half_away(x * (7/amax)) + 8, 0, 15)
+// ---------------------------------------------------------------------------
+// 8 codes of 4 bits, low nibble = even element, clamp(round_half_away(x * inv) + 8, 0, 15)
+__device__ __forceinline__ uint32_t lm_pack8(const float* x, float inv) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        int q = static_cast<int>(roundf(__fmul_rn(x[j], inv))) + 8;
+        q = q < 0 ? 0 : (q > 15 ? 15 : q);
+        w |= static_cast<uint32_t>(q) << (4 * j);
+    }
+    return w;
+}
+
+// fp16 bits of amax * fl(1/7), or 0 for an all-zero group
+__device__ __forceinline__ uint32_t lm_scale_bits(float amax) {
+    if (amax < 1e-12f) return 0u;
+    return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(__fmul_rn(amax, inv7f()))));
+}
+
+template <typename T>
+__global__ void k_lmhead_quant_preq2(const T* __restrict__ w, uint32_t* __restrict__ meta,
+                                     uint4* __restrict__ quant, int rows, int cols) {
+    const int ng = cols / 32;
+    const long long total = static_cast<long long>(rows) * ng;
+    for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = t / ng;
+        const int g = static_cast<int>(t - r * ng);
+        const T* src = w + r * cols + g * 32;
+        float x[32];
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            x[j] = load_as_float<T>(src + j);
+            amax = fmaxf(amax, fabsf(x[j]));
+        }
+        // meta word: fp16 scale (low half), fp16 zero 8.0 = 0x4800 (high half)
+        meta[r * ng + g] = lm_scale_bits(amax) | (0x4800u << 16);
+        uint4 qv = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+        if (amax >= 1e-12f) {
+            const float inv = __fdiv_rn(7.0f, amax);
+            qv.x = lm_pack8(x, inv);
+            qv.y = lm_pack8(x + 8, inv);
+            qv.z = lm_pack8(x + 16, inv);
+            qv.w = lm_pack8(x + 24, inv);
+        }
+        // preq2 band slot: [r/4][g][r%4][16 bytes]
+        quant[((r >> 2) * ng + g) * 4 + (r & 3)] = qv;
+    }
+}
+
+// g128 variant, written directly in the banded device layout
+// (quant [nb][K/128][4][64], scales [nb][K/128][4] fp16)
+template <typename T>
+__global__ void k_lmhead_quant_q128b(const T* __restrict__ w, uint4* __restrict__ quant,
+                                     uint16_t* __restrict__ scales, int rows, int cols) {
+    const int ng = cols / 128;
+    const long long total = static_cast<long long>(rows) * ng;
+    for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = t / ng;
+        const int g = static_cast<int>(t - r * ng);
+        const T* src = w + r * cols + g * 128;
+        float amax = 0.0f;
+        for (int j = 0; j < 128; ++j) amax = fmaxf(amax, fabsf(load_as_float<T>(src + j)));
+        const long long slot = ((r >> 2) * ng + g) * 4 + (r & 3);
+        scales[slot] = static_cast<uint16_t>(lm_scale_bits(amax));
+        const float inv = amax >= 1e-12f ? __fdiv_rn(7.0f, amax) : 0.0f;
+        for (int c = 0; c < 4; ++c) {
+            uint4 qv = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+            if (amax >= 1e-12f) {
+                float x[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) x[j] = load_as_float<T>(src + c * 32 + j);
+                qv.x = lm_pack8(x, inv);
+                qv.y = lm_pack8(x + 8, inv);
+                qv.z = lm_pack8(x + 16, inv);
+                qv.w = lm_pack8(x + 24, inv);
+            }
+            quant[slot * 4 + c] = qv;
+        }
+    }
+}
+
+}  // namespace asdsl

@@ -169,6 +169,87 @@ int asdsl_b200_gemv_argmax_static(int fmt, const uint8_t* w0, const uint8_t* w1,
 int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* h,
                            int intermediate, int in_features, void* stream);
 
+/* ======================================================================================
+ * Device-resident decode engine: UnifiedEngine (asdsl/kernels/native/unified_engine.h:14-109,
+ * :134-282; unified_engine.cpp) for the C0 decode path.  The engine owns its device memory
+ * (weights re-laid out on upload, int8 KV cache, activations) and one CUDA stream; a decode
+ * step is one CUDA-graph replay.  Every setter accepts host or device pointers (copied).
+ * ==================================================================================== */
+
+/* EngineConfig (unified_engine.h:14-109, pybind fields unified_engine.cpp:2204-2222).
+ * Supported here: head_dim 128, weight_format 0 with group_size 32, lm_head_group_size 32 or 128
+ * (0 = group_size), hidden / intermediate / q dims multiples of 128. */
+typedef struct asdsl_b200_engine_config {
+    int num_layers;
+    int hidden_size;
+    int num_heads;
+    int num_kv_heads;
+    int head_dim;
+    int intermediate_size;
+    int vocab_size;
+    float rms_norm_eps;
+    int group_size;
+    int lm_head_group_size;
+    int max_seq_len;
+    int rotary_dim;
+    int weight_format;
+} asdsl_b200_engine_config;
+
+typedef struct asdsl_b200_engine asdsl_b200_engine;
+
+/* UnifiedEngine constructor, split into create + setters + finalize
+ * (pybind constructor unified_engine.cpp:2662-2682, weight binding :2240-2442). */
+int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_engine** out);
+int asdsl_b200_engine_destroy(asdsl_b200_engine* e);
+/* token_embd [vocab][hidden] fp16 (embd_is_f16 = 1) or fp32; output_norm [hidden];
+ * cos/sin tables [max_seq_len][rotary_dim/2] fp32. */
+int asdsl_b200_engine_set_globals(asdsl_b200_engine* e, const void* token_embd, int embd_is_f16,
+                                  const float* output_norm, const float* cos_table, const float* sin_table);
+/* lm_head source [vocab][hidden] fp16 or fp32, quantized on the device at finalize with the
+ * reference constructor's rules (unified_engine.cpp:320-400 g32 -> preq2, :411-461 g128). */
+int asdsl_b200_engine_set_output_proj(asdsl_b200_engine* e, const void* output_proj, int is_f16);
+/* Cached lm_head preq2 blobs (unified_engine.cpp:295-318): used when lm_head_group_size is 32
+ * and both sizes match, otherwise ignored as the reference does. */
+int asdsl_b200_engine_set_lm_head_preq2(asdsl_b200_engine* e, const uint8_t* meta, size_t meta_bytes,
+                                        const uint8_t* quant, size_t quant_bytes);
+/* layers_dict[i]["rms_att"], ["rms_ffn"]  (unified_engine.cpp:2306-2320). */
+int asdsl_b200_engine_set_layer_norms(asdsl_b200_engine* e, int layer, const float* rms_att, const float* rms_ffn);
+/* layers_dict[i] projection weights: which 0 qkv, 1 o, 2 gate_up (gate rows then up rows), 3 down.
+ * fmt PREQ2 (w0 = *_meta, w1 = *_quant; unified_engine.cpp:2368-2386) or Q4_128 (w0 = *_g128 blocks,
+ * re-laid out to the banded device layout; :2330-2349). */
+int asdsl_b200_engine_set_projection(asdsl_b200_engine* e, int layer, int which, int fmt, const uint8_t* w0,
+                                     size_t w0_bytes, const uint8_t* w1, size_t w1_bytes);
+/* Builds the lm_head, runs one eager step and captures the decode / prefill graphs. */
+int asdsl_b200_engine_finalize(asdsl_b200_engine* e);
+/* forward_token (unified_engine.cpp:1339-1688; pybind :2485-2510): logits (host or device, vocab floats)
+ * and / or argmax may be NULL; both NULL = forward_token_prefill (no lm_head).
+ * token / pos out of range -> ASDSL_B200_ERANGE. */
+int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, float* logits, int32_t* argmax);
+/* generate / generate_with_stops (unified_engine.cpp:1717-1764): out = prompt + generated tokens
+ * (the stop token included), *n_out its length; out_cap >= n_prompt + max_tokens + 1. */
+int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int n_prompt, int max_tokens,
+                               const int32_t* stops, int n_stops, int32_t* out, int out_cap, int* n_out);
+/* reset_session / get_kv_seq_len / truncate_kv / snapshot_kv / restore_kv (unified_engine.cpp:1285-1337). */
+int asdsl_b200_engine_reset_session(asdsl_b200_engine* e);
+int asdsl_b200_engine_get_kv_seq_len(asdsl_b200_engine* e, int* out);
+int asdsl_b200_engine_truncate_kv(asdsl_b200_engine* e, int new_len);
+int asdsl_b200_engine_snapshot_kv(asdsl_b200_engine* e);
+int asdsl_b200_engine_restore_kv(asdsl_b200_engine* e);
+/* export_lm_head_preq2 (unified_engine.cpp:2470-2483): *fmt = PREQ2 (w0 meta, w1 quant) or
+ * Q4_128_BANDED (w0 quant, w1 scales); NULL buffers = format query only. */
+int asdsl_b200_engine_export_lm_head(asdsl_b200_engine* e, int* fmt, uint8_t* w0, size_t w0_bytes, uint8_t* w1,
+                                     size_t w1_bytes);
+/* Benchmark / graph-level control (no reference counterpart): the engine's stream, stream-ordered
+ * setting of (pos, seq[pos] = token; token < 0 leaves seq alone), and n replays of the decode
+ * (decode = 1) or prefill graph without synchronising. */
+int asdsl_b200_engine_stream(asdsl_b200_engine* e, void** stream);
+int asdsl_b200_engine_set_position(asdsl_b200_engine* e, int pos, int token);
+int asdsl_b200_engine_replay(asdsl_b200_engine* e, int decode, int n);
+/* Copy of an engine buffer to host memory after the engine stream drains (tests only; no reference
+ * counterpart): which 0 residual stream, 1 qkv, 2 attention output, 3 SiLU(gate)*up, 4 logits,
+ * 5 K codes, 6 V codes, 7 K scales, 8 V scales (the last layer's values for 1-4). */
+int asdsl_b200_engine_read_buffer(asdsl_b200_engine* e, int which, void* host, size_t bytes);
+
 #ifdef __cplusplus
 }
 #endif

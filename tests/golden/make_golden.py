@@ -10,6 +10,9 @@ Sources of truth per fixture:
   repack_*.npz  asdsl.quantization.repack_q4_32 / _preq2 / _q4_128 (the repackers)
   kern_*.npz    the reference's compiled AVX2 kernels (oracle/_ref via ref_shim.cpp)
   engine_tiny.npz  the reference's compiled UnifiedEngine (_native_unified in oracle/_ref)
+  engine_long.npz  the same engine: 160 greedy steps on TINY-shaped models with a 256-position
+                   cache (seeds 5 and 7), shapes on which the reference and a faithful
+                   restatement with another fp32 summation order agree token for token
 Inputs are small and stored verbatim, except the tiny engine's weights, which
 are regenerated from a seed; their sha256 is stored to catch generator drift.
 """
@@ -29,11 +32,80 @@ sys.path.insert(0, os.path.join(ROOT, "asdsl-framework_b200"))
 sys.path.insert(0, ROOT)
 
 
+def ref_engine(nu, model):
+    """The reference's UnifiedEngine over a synthetic model (preq blocks + preq2 blobs per layer,
+    tied fp16 embedding as lm_head source), as unified_bridge.build_unified_engine wires it."""
+    from asdsl_b200.quantization.repack import preq2_to_preq
+
+    c = model["config"]
+    cfg = nu.EngineConfig()
+    cfg.num_layers, cfg.hidden_size = c["num_layers"], c["hidden"]
+    cfg.num_heads, cfg.num_kv_heads, cfg.head_dim = c["n_heads"], c["n_kv_heads"], c["head_dim"]
+    cfg.intermediate_size, cfg.vocab_size = c["inter"], c["vocab"]
+    cfg.rms_norm_eps, cfg.group_size, cfg.lm_head_group_size = c["eps"], 32, 0
+    cfg.max_seq_len, cfg.rotary_dim, cfg.weight_format = c["max_seq"], c["rotary_dim"], 0
+    H, I = c["hidden"], c["inter"]
+    qkv_rows = (c["n_heads"] + 2 * c["n_kv_heads"]) * c["head_dim"]
+    shapes = {"qkv_proj": (qkv_rows, H), "o_proj": (H, c["n_heads"] * c["head_dim"]),
+              "gate_up_proj": (2 * I, H), "down_proj": (H, I)}
+    layers = {}
+    for li, L in enumerate(model["layers"]):
+        d = {"rms_att": L["rms_att"], "rms_ffn": L["rms_ffn"]}
+        for name, (r, k) in shapes.items():
+            d[name] = preq2_to_preq(L[name + "_meta"], L[name + "_quant"], r, k).reshape(-1)
+            d[name + "_meta"] = L[name + "_meta"]
+            d[name + "_quant"] = L[name + "_quant"]
+        layers[li] = d
+    os.environ["ASDSL_PREQ2"] = "1"
+    return nu.UnifiedEngine(cfg, model["embed_f16"], model["output_norm"], model["embed_f16"], model["cos"],
+                            model["sin"], layers)
+
+
+def load_ref_unified():
+    from oracle.oracle import ref_lib_path
+
+    spec = importlib.util.spec_from_file_location("_native_unified", ref_lib_path())
+    nu = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(nu)
+    return nu
+
+
+def engine_long() -> None:
+    """engine_long.npz: the reference engine's greedy trajectories over 160 steps."""
+    from asdsl_b200.inference.synthetic import TINY, build_model, model_digest
+
+    nu = load_ref_unified()
+    out = {}
+    for seed in (5, 7):
+        model = build_model(dict(TINY, max_seq=256), seed=seed, norms_one=False)
+        eng = ref_engine(nu, model)
+        prompt = [3]
+        toks = list(prompt)
+        logits = np.array(eng.forward_token(prompt[0], 0), copy=True)
+        margins = []
+        for _ in range(160):
+            srt = np.sort(logits)
+            margins.append(float(srt[-1] - srt[-2]))
+            toks.append(int(np.argmax(logits)))
+            logits = np.array(eng.forward_token(toks[-1], len(toks) - 1), copy=True)
+        eng.reset_session()
+        assert list(eng.generate(prompt, 160)) == toks
+        out[f"s{seed}_digest"] = np.array(model_digest(model))
+        out[f"s{seed}_tokens"] = np.array(toks, np.int32)
+        out[f"s{seed}_margins"] = np.array(margins)
+    np.savez_compressed(os.path.join(OUT, "engine_long.npz"), **out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", choices=["engine_long"], default=None)
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
+    if args.only == "engine_long":
+        engine_long()
+        print("golden fixture engine_long.npz written to", OUT)
+        return
     from asdsl.quantization import core as rcore
     from asdsl.quantization.repack_preq2 import repack_preq_blocks_to_preq2
     from asdsl.quantization.repack_q4_32 import blocks_to_flat, repack_asymmetric_to_q4_32_blocks
@@ -120,34 +192,10 @@ def main() -> None:
 
     # ---------------- tiny engine (compiled reference UnifiedEngine) ----------------
     from asdsl_b200.inference.synthetic import TINY, build_model, model_digest
-    from asdsl_b200.quantization.repack import preq2_to_preq
 
-    spec = importlib.util.spec_from_file_location("_native_unified", ref_lib_path())
-    nu = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(nu)
+    nu = load_ref_unified()
     model = build_model(TINY, seed=5, norms_one=False)
-    c = model["config"]
-    cfg = nu.EngineConfig()
-    cfg.num_layers, cfg.hidden_size = c["num_layers"], c["hidden"]
-    cfg.num_heads, cfg.num_kv_heads, cfg.head_dim = c["n_heads"], c["n_kv_heads"], c["head_dim"]
-    cfg.intermediate_size, cfg.vocab_size = c["inter"], c["vocab"]
-    cfg.rms_norm_eps, cfg.group_size, cfg.lm_head_group_size = c["eps"], 32, 0
-    cfg.max_seq_len, cfg.rotary_dim, cfg.weight_format = c["max_seq"], c["rotary_dim"], 0
-    H, I = c["hidden"], c["inter"]
-    qkv_rows = (c["n_heads"] + 2 * c["n_kv_heads"]) * c["head_dim"]
-    shapes = {"qkv_proj": (qkv_rows, H), "o_proj": (H, c["n_heads"] * c["head_dim"]),
-              "gate_up_proj": (2 * I, H), "down_proj": (H, I)}
-    layers = {}
-    for li, L in enumerate(model["layers"]):
-        d = {"rms_att": L["rms_att"], "rms_ffn": L["rms_ffn"]}
-        for name, (r, k) in shapes.items():
-            d[name] = preq2_to_preq(L[name + "_meta"], L[name + "_quant"], r, k).reshape(-1)
-            d[name + "_meta"] = L[name + "_meta"]
-            d[name + "_quant"] = L[name + "_quant"]
-        layers[li] = d
-    os.environ["ASDSL_PREQ2"] = "1"
-    eng = nu.UnifiedEngine(cfg, model["embed_f16"], model["output_norm"], model["embed_f16"], model["cos"],
-                           model["sin"], layers)
+    eng = ref_engine(nu, model)
     lm_meta, lm_quant = eng.export_lm_head_preq2()
     prompt = [7]
     steps = 40
@@ -167,6 +215,7 @@ def main() -> None:
                         seed=np.array(5), prompt=np.array(prompt, np.int32), tokens=np.array(toks, np.int32),
                         generate=np.array(gen, np.int32), logits0=logits0, margins=np.array(margins),
                         lm_meta=lm_meta, lm_quant=lm_quant)
+    engine_long()
     print("golden fixtures written to", OUT)
 
 

@@ -84,3 +84,21 @@ def test_oracle_vs_live_reference_random(oracle):
         if K % 256 == 0:
             w = random_q4k_bytes(rng, M, K)
             assert rel_err(oracle.gemv_q4km(w, x, M, K), rk.gemv_q4km(w, x, M, K)) < TOL
+
+
+def test_oracle_engine_long_trajectories_vs_reference(oracle, golden):
+    """160 greedy steps of the oracle engine equal the reference engine's (engine_long.npz)."""
+    from asdsl_b200.inference.synthetic import TINY, build_model, model_digest
+
+    g = golden("engine_long.npz")
+    for seed in (5, 7):
+        model = build_model(dict(TINY, max_seq=256), seed=seed, norms_one=False)
+        assert model_digest(model) == str(g[f"s{seed}_digest"])
+        c = model["config"]
+        model["lm_meta"], model["lm_quant"] = oracle.lmhead_quant_preq2(model["embed_f16"], c["vocab"], c["hidden"])
+        eng = OracleEngine(model, oracle)
+        try:
+            toks, _ = eng.generate([3], 160)
+        finally:
+            eng.close()
+        assert toks == [int(t) for t in g[f"s{seed}_tokens"]]
