@@ -22,7 +22,7 @@ LIB_PATH = os.path.join(_HERE, "libasdsl_b200.so")
 
 OK, EINVAL, ERANGE, ECUDA, ENCCL, ETIMEOUT, ENOMEM = range(7)
 
-FMT_PREQ2, FMT_PREQ, FMT_Q4_128, FMT_S256, FMT_Q4_128_BANDED = 0, 1, 2, 3, 4
+FMT_PREQ2, FMT_PREQ, FMT_Q4_128, FMT_S256, FMT_Q4_128_BANDED, FMT_Q4K = 0, 1, 2, 3, 4, 5
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -53,6 +53,7 @@ _SIGS = {
     "asdsl_b200_gemv_argmax": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P],
     "asdsl_b200_gemv_argmax_static": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_gateup_silu": [_I, _P, _P, _P, _P, _I, _I, _P],
+    "asdsl_b200_gemv_multi": [_I, _P, _P, _P, _P, _I, _I, _I, _P],
     # device-resident decode engine
     "asdsl_b200_engine_create": [_P, _P],
     "asdsl_b200_engine_destroy": [_P],

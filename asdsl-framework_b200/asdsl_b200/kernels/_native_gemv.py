@@ -152,6 +152,37 @@ def gemv_q4km_q8_avx2(weights_q4km, x, y, out_features: int, in_features: int) -
         _writeback(y, yd)
 
 
+def gemv_multi(fmt: int, w0, w1, X, Y, out_features: int, in_features: int) -> None:
+    """Multi-token W4A8 GEMV (speculative verification): Y[t] = W . A8(X[t]) for every row t of
+    X (n_tokens, in_features); one weight stream serves up to 16 rows.  Row t equals the
+    single-token kernel's result (gemv_q4_32_preq_fused_avx2 / gemv_preq2_fused_avx2 /
+    gemv_q4km_q8_avx2 on X[t]); fmt is one of _lib.FMT_PREQ, FMT_PREQ2, FMT_Q4_128_BANDED, FMT_Q4K."""
+    xt = X if isinstance(X, torch.Tensor) else np.asarray(X)
+    if xt.ndim != 2 or int(xt.shape[1]) != in_features:
+        raise ValueError("X must be (n_tokens, in_features)")
+    n = int(xt.shape[0])
+    ysize = Y.numel() if isinstance(Y, torch.Tensor) else np.asarray(Y).size
+    if ysize != n * out_features:
+        raise ValueError("Y must hold n_tokens * out_features values")
+    w0d = dv.to_device(w0, np.uint8)
+    w1d = dv.to_device(w1, np.uint8) if w1 is not None else None
+    xd = dv.to_device(xt, np.float32)
+    yd = _out(Y, n * out_features, np.float32)
+    _lib.call("asdsl_b200_gemv_multi", int(fmt), w0d.data_ptr(), None if w1d is None else w1d.data_ptr(),
+              xd.data_ptr(), yd.data_ptr(), int(out_features), int(in_features), n, dv.stream_ptr())
+    _writeback(Y, yd)
+
+
+def gemv_q4_32_preq_multi(blocks, X, Y, out_features: int, in_features: int) -> None:
+    """k serial gemv_q4_32_preq_fused_avx2 calls in one weight stream (preq 20-byte blocks)."""
+    gemv_multi(_lib.FMT_PREQ, blocks, None, X, Y, out_features, in_features)
+
+
+def gemv_q4km_q8_multi(weights_q4km, X, Y, out_features: int, in_features: int) -> None:
+    """k serial gemv_q4km_q8_avx2 calls in one weight stream (reference Q4_K blocks)."""
+    gemv_multi(_lib.FMT_Q4K, weights_q4km, None, X, Y, out_features, in_features)
+
+
 def _packed_args(w_packed, x, scales, biases, M, K, group_size, expected_w):
     xt = x if isinstance(x, torch.Tensor) else np.asarray(x)
     batch = 1 if xt.ndim == 1 else int(xt.shape[0])

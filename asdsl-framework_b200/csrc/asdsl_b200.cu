@@ -407,6 +407,86 @@ int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const 
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// multi-token W4A8 GEMV: one pass streams the weights once for up to 16 activation rows
+// ---------------------------------------------------------------------------
+namespace {
+template <int FMT, int PRO>
+int multi_pass(int T, const StreamIn* s, int ns, long long nb, GemvArgs ga, cudaStream_t st, const LaunchOpts& o) {
+    ga.n_tokens = T;
+    if (T <= 2) return launch_stream_gemv<FMT, PRO, kEpiStore, 2>(s, ns, nb, 0, ga, st, o);
+    if (T <= 4) return launch_stream_gemv<FMT, PRO, kEpiStore, 4>(s, ns, nb, 0, ga, st, o);
+    if (T <= 8) return launch_stream_gemv<FMT, PRO, kEpiStore, 8>(s, ns, nb, 0, ga, st, o);
+    return launch_stream_gemv<FMT, PRO, kEpiStore, 16>(s, ns, nb, 0, ga, st, o);
+}
+}  // namespace
+
+extern "C" {
+
+int asdsl_b200_gemv_multi(int fmt, const uint8_t* w0, const uint8_t* w1, const float* X, float* Y, int M, int K,
+                          int n_tokens, void* stream) {
+    if (!w0 || !X || !Y) return set_error(kEinval, "gemv_multi: null pointer");
+    if (M <= 0 || K <= 0 || n_tokens <= 0) return set_error(kEinval, "gemv_multi: invalid dimensions");
+    StreamIn s[2];
+    int ns = 1;
+    LaunchOpts o;
+    int gs = 32;
+    const bool q4k = (fmt == ASDSL_B200_FMT_Q4K);
+    if (fmt == ASDSL_B200_FMT_PREQ) {
+        if (int rc = check_k(K, 32, "gemv_multi")) return rc;
+        const long long ng = K / 32;
+        s[0] = StreamIn{w0, 4 * ng * 20, static_cast<long long>(M) * ng * 20};
+        o = rows_opt(ng * 20);
+    } else if (fmt == ASDSL_B200_FMT_PREQ2) {
+        if (!w1) return set_error(kEinval, "gemv_multi: null pointer");
+        if (int rc = check_k(K, 32, "gemv_multi")) return rc;
+        preq2_streams(s, w0, w1, M, K);
+        ns = 2;
+    } else if (fmt == ASDSL_B200_FMT_Q4_128_BANDED) {
+        if (!w1) return set_error(kEinval, "gemv_multi: null pointer");
+        if (int rc = check_k128(K, "gemv_multi")) return rc;
+        q128b_streams(s, w0, w1, M, K);
+        ns = 2;
+        gs = 128;
+    } else if (q4k) {
+        if (K % 256) return set_error(kEinval, "in_features must be divisible by 256 for Q4_K_M");
+        if (K > kMaxK) return set_error(kEinval, "gemv_multi: in_features too large");
+        const long long nb = K / 256;
+        s[0] = StreamIn{w0, 4 * nb * 144, static_cast<long long>(M) * nb * 144};
+        o = rows_opt(nb * 144);
+    } else {
+        return set_error(kEinval, "gemv_multi: unsupported weight format");
+    }
+    // tokens per pass: 16 at most, and their A8 areas within half of the shared-memory budget
+    const uint32_t xa = xarea_layout_bytes(K, gs, false);
+    int per_pass = static_cast<int>((kSmemBudget / 2) / xa);
+    if (per_pass > 16) per_pass = 16;
+    if (per_pass < 1) per_pass = 1;
+    const long long nb = (static_cast<long long>(M) + 3) / 4;
+    for (int t0 = 0; t0 < n_tokens; t0 += per_pass) {
+        const int T = (n_tokens - t0 < per_pass) ? n_tokens - t0 : per_pass;
+        GemvArgs ga = base_args(M, K, gs);
+        ga.x = X + static_cast<long long>(t0) * K;
+        ga.y = Y + static_cast<long long>(t0) * M;
+        int rc = kOk;
+        if (T == 1) {
+            if (fmt == ASDSL_B200_FMT_PREQ) rc = launch_stream_gemv<kFmtPreq, kProA8, kEpiStore>(s, ns, nb, 0, ga, as_stream(stream), o);
+            else if (fmt == ASDSL_B200_FMT_PREQ2) rc = launch_stream_gemv<kFmtPreq2, kProA8, kEpiStore>(s, ns, nb, 0, ga, as_stream(stream), o);
+            else if (q4k) rc = launch_stream_gemv<kFmtQ4K, kProQ4K, kEpiStore>(s, ns, nb, 0, ga, as_stream(stream), o);
+            else rc = launch_stream_gemv<kFmtQ128B, kProA8, kEpiStore>(s, ns, nb, 0, ga, as_stream(stream), o);
+        } else {
+            if (fmt == ASDSL_B200_FMT_PREQ) rc = multi_pass<kFmtPreq, kProA8>(T, s, ns, nb, ga, as_stream(stream), o);
+            else if (fmt == ASDSL_B200_FMT_PREQ2) rc = multi_pass<kFmtPreq2, kProA8>(T, s, ns, nb, ga, as_stream(stream), o);
+            else if (q4k) rc = multi_pass<kFmtQ4K, kProQ4K>(T, s, ns, nb, ga, as_stream(stream), o);
+            else rc = multi_pass<kFmtQ128B, kProA8>(T, s, ns, nb, ga, as_stream(stream), o);
+        }
+        if (rc) return rc;
+    }
+    return kOk;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
 // allocation-free variant of gemv_argmax: the argmax scratch lives in a
 // file-scope device array (one copy per device), sized for grids of up to
 // kStaticArgmaxCtas CTAs: a 256-byte counter slot + 4-byte value and index per CTA.

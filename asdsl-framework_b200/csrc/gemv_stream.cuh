@@ -128,6 +128,7 @@ struct GemvArgs {
     int* out_idx;
     int row_base;          // global index of row 0 (row-sharded lm_head)
     unsigned int* status;  // device status word
+    int n_tokens;          // multi-token kernels (NT > 1): activation rows x[t][K] -> y[t][M]
 };
 
 // ---------------------------------------------------------------------------
@@ -369,9 +370,9 @@ struct SliceData {
     uint32_t m[4];  // per-row scale (and zero) bits, or the Q4_K block address
 };
 
+// the activation half of a slice: A8 codes (permuted), group scale, scale*sum, sum
 template <int FMT>
-__device__ __forceinline__ void slice_load(SliceData& d, uint32_t s0, uint32_t s1, int nq, int rs, const XAddr& xs,
-                                           const uint32_t rr[4], int q) {
+__device__ __forceinline__ void slice_load_x(SliceData& d, const XAddr& xs, int q) {
     const uint32_t uq = static_cast<uint32_t>(q);
     const uint32_t xr = xs.x8 + uq * 32u;
     d.xa = lds128(xr);
@@ -379,6 +380,13 @@ __device__ __forceinline__ void slice_load(SliceData& d, uint32_t s0, uint32_t s
     d.xs = ldsf(xs.xs + 4u * uq);
     d.xss = ldsf(xs.xss + 4u * uq);
     if constexpr (FMT == kFmtQ4K) d.xsi = static_cast<int>(lds32(xs.xsi + 4u * uq));
+}
+
+// the weight half of a slice: 4 rows of 32 nibbles and their scale / zero bits
+template <int FMT>
+__device__ __forceinline__ void slice_load_w(SliceData& d, uint32_t s0, uint32_t s1, int nq, int rs,
+                                             const uint32_t rr[4], int q) {
+    const uint32_t uq = static_cast<uint32_t>(q);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const uint32_t row = rr[r];
@@ -412,6 +420,13 @@ __device__ __forceinline__ void slice_load(SliceData& d, uint32_t s0, uint32_t s
             d.m[r] = blk;  // block address: scales are unpacked in slice_math
         }
     }
+}
+
+template <int FMT>
+__device__ __forceinline__ void slice_load(SliceData& d, uint32_t s0, uint32_t s1, int nq, int rs, const XAddr& xs,
+                                           const uint32_t rr[4], int q) {
+    slice_load_x<FMT>(d, xs, q);
+    slice_load_w<FMT>(d, s0, s1, nq, rs, rr, q);
 }
 
 template <int FMT>
@@ -580,8 +595,9 @@ __device__ __forceinline__ void argmax_take(float& bv, int& bi, float v, int i) 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int FMT, int PRO, int EPI>
+template <int FMT, int PRO, int EPI, int NT = 1>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
+    static_assert(NT == 1 || (EPI == kEpiStore && FMT != kFmtPacked), "multi-token: store epilogue, W4A8 formats");
     using T = FmtTraits<FMT>;
     constexpr int NS = T::kStreams;
     constexpr int NSEG = (EPI == kEpiSilu) ? 2 : 1;
@@ -603,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     const int n_chunks = static_cast<int>((u1 - u0 + CU - 1) / CU);
     // split partials [stage][unit in chunk][item][row] and per-unit arrival counts
     float* s_part = reinterpret_cast<float*>(smem + pa.split_off);
-    int* s_cnt = reinterpret_cast<int*>(s_part + S * CU * IPU * 4);
+    int* s_cnt = reinterpret_cast<int*>(s_part + S * CU * IPU * 4 * NT);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -676,7 +692,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     // ---------------- consumer warps: every warp takes part of every stage ----------------
     const int cw = warp;
     grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
-    run_prologue<PRO>(ga, xa, threadIdx.x);
+    // multi-token: one A8 area per activation row, xa_stride bytes apart
+    const uint32_t xa_stride = (NT > 1) ? xarea_layout_bytes(ga.K, ga.gs, false) : 0u;
+    if constexpr (NT == 1) {
+        run_prologue<PRO>(ga, xa, threadIdx.x);
+    } else {
+        for (int t = 0; t < ga.n_tokens; ++t) {
+            GemvArgs gt = ga;
+            gt.x = ga.x + static_cast<size_t>(t) * ga.K;
+            run_prologue<PRO>(gt, xarea_layout(smem + pa.xarea_off + t * xa_stride, ga.K, ga.gs, false),
+                              threadIdx.x);
+        }
+    }
 
     const int K = ga.K;
     const int M = ga.M;
@@ -730,6 +757,86 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
                                                    k * pa.s[2].unit_bytes),
                     K, ga.gs, xa, lane);
                 if (lane == 0 && unit < M) ga.y[unit] = v;
+            } else if constexpr (NT > 1) {
+                const int q0 = (P == 1) ? 0 : pa.q_bounds[part];
+                const int q1 = (P == 1) ? nq : pa.q_bounds[part + 1];
+                const uint32_t p0 = ub[0][0] + static_cast<uint32_t>(k * pa.s[0].unit_bytes);
+                uint32_t p1 = 0u;
+                if constexpr (NS > 1) p1 = ub[0][NS - 1] + static_cast<uint32_t>(k * pa.s[NS - 1].unit_bytes);
+                const uint32_t rr[4] = {static_cast<uint32_t>(rot & 3), static_cast<uint32_t>((rot + 1) & 3),
+                                        static_cast<uint32_t>((rot + 2) & 3), static_cast<uint32_t>((rot + 3) & 3)};
+                const int ntok = ga.n_tokens;
+                float vt[NT];
+                // tokens in groups of four: each slice's weights are loaded once per group
+#pragma unroll
+                for (int t0 = 0; t0 < NT; t0 += 4) {
+                    if (t0 >= ntok) continue;
+                    float a4[4][4];
+#pragma unroll
+                    for (int tt = 0; tt < 4; ++tt)
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) a4[tt][r] = 0.0f;
+                    for (int q = q0 + lane; q < q1; q += 32) {
+                        SliceData d;
+                        slice_load_w<FMT>(d, p0, p1, nq, pa.row_bytes, rr, q);
+#pragma unroll
+                        for (int tt = 0; tt < 4; ++tt) {
+                            if (t0 + tt < ntok) {
+                                const uint32_t off = static_cast<uint32_t>(t0 + tt) * xa_stride;
+                                XAddr xt;
+                                xt.x8 = xad.x8 + off;
+                                xt.xs = xad.xs + off;
+                                xt.xss = xad.xss + off;
+                                xt.xsi = xad.xsi + off;
+                                slice_load_x<FMT>(d, xt, q);
+                                slice_math<FMT>(a4[tt], d, static_cast<uint32_t>(q));
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int tt = 0; tt < 4; ++tt) {
+                        if (t0 + tt < NT) {
+                            unrotate(a4[tt], rot);
+                            vt[t0 + tt] = reduce4(a4[tt], lane);
+                        }
+                    }
+                }
+                bool finish = true;
+                if (IPU > 1) {
+                    const int slot = s * CU + k;
+                    if ((lane & 7) == 0) {
+#pragma unroll
+                        for (int t = 0; t < NT; ++t)
+                            if (t < ntok) s_part[((slot * IPU + rem) * NT + t) * 4 + (lane >> 3)] = vt[t];
+                    }
+                    __syncwarp();
+                    int prev = 0;
+                    if (lane == 0) {
+                        __threadfence_block();
+                        prev = atomicAdd(&s_cnt[slot], 1);
+                    }
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    finish = (prev == IPU - 1);
+                    if (finish) {
+                        __threadfence_block();
+#pragma unroll
+                        for (int t = 0; t < NT; ++t) {
+                            if (t < ntok) {
+                                float acc = 0.0f;
+                                for (int p2 = 0; p2 < P; ++p2)
+                                    acc += s_part[((slot * IPU + p2) * NT + t) * 4 + (lane >> 3)];
+                                vt[t] = acc;
+                            }
+                        }
+                        if (lane == 0) s_cnt[slot] = 0;
+                    }
+                }
+                const long long row = unit * 4 + (lane >> 3);
+                if (finish && (lane & 7) == 0 && row < M) {
+#pragma unroll
+                    for (int t = 0; t < NT; ++t)
+                        if (t < ntok) ga.y[static_cast<long long>(t) * M + row] = vt[t];
+                }
             } else {
                 const int q0 = (P == 1) ? 0 : pa.q_bounds[part];
                 const int q1 = (P == 1) ? nq : pa.q_bounds[part + 1];

@@ -99,9 +99,11 @@ struct LaunchOpts {
     int chunk_target = ASDSL_CHUNK_KB * 1024;  // bytes per pipeline stage (all segments and streams)
 };
 
-template <int FMT, int PRO, int EPI>
+template <int FMT, int PRO, int EPI, int NT = 1>
 int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, long long pair_unit_off,
                        GemvArgs ga, cudaStream_t stream, const LaunchOpts& opt = LaunchOpts()) {
+    if (NT == 1) ga.n_tokens = 1;
+    if (ga.n_tokens < 1 || ga.n_tokens > NT) return set_error(kEinval, "internal: token count out of range");
     if (n_units <= 0) return kOk;
     if (n_units > 0x7fffffffLL) return set_error(kEinval, "too many rows");
     PipeArgs pa;
@@ -124,7 +126,7 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
 
     // stage = chunk of `cu` units (all segments and streams): big bulk copies stream
     // HBM best (>= 16 KB each), and every consumer warp shares every stage.
-    const uint32_t xa = xarea_layout_bytes(ga.K, ga.gs, PRO == kProF32);
+    const uint32_t xa = xarea_layout_bytes(ga.K, ga.gs, PRO == kProF32) * static_cast<uint32_t>(ga.n_tokens);
     const long long unit_stage = ub_sum * nseg;
     long long cu = opt.chunk_target / (unit_stage > 0 ? unit_stage : 1);
     if (cu < 1) cu = 1;
@@ -159,7 +161,7 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
         if (ipu > 1 && stages > 0) {
             // partial sums + counters live beside the stages
             for (;;) {
-                split_bytes = round_up(static_cast<uint32_t>(stages * cu * ipu * 4 * 4 + stages * cu * 4), 128);
+                split_bytes = round_up(static_cast<uint32_t>(stages * cu * ipu * 4 * 4 * NT + stages * cu * 4), 128);
                 if (stages <= 2 || static_cast<long long>(stages) * stage_bytes + split_bytes <= avail) break;
                 --stages;
             }
@@ -197,7 +199,7 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     ga.status = device_status_ptr();
     if (!ga.status) return set_error(kEcuda, "cannot resolve the device status word");
 
-    auto kern = k_stream_gemv<FMT, PRO, EPI>;
+    auto kern = k_stream_gemv<FMT, PRO, EPI, NT>;
     {
         static std::mutex mu;
         static bool configured[64] = {false};

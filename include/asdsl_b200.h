@@ -39,6 +39,7 @@ extern "C" {
 #define ASDSL_B200_FMT_S256 3   /* [M][K/256][144] blocks (gemv_q4_s256.cpp:1-17) */
 #define ASDSL_B200_FMT_Q4_128_BANDED 4 /* device re-layout of Q4_128: quant [ceil(M/4)][K/128][4][64] +
                                           scales [ceil(M/4)][K/128][4] fp16 (asdsl_b200_relayout_q4_128) */
+#define ASDSL_B200_FMT_Q4K 5    /* [M][K/256][144] reference-interpretation Q4_K (gemv_q4_avx2.cpp:110-120) */
 
 const char* asdsl_b200_version(void);
 const char* asdsl_b200_last_error(void);
@@ -168,6 +169,17 @@ int asdsl_b200_gemv_argmax_static(int fmt, const uint8_t* w0, const uint8_t* w1,
  * :836-857). */
 int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* h,
                            int intermediate, int in_features, void* stream);
+
+/* Multi-token W4A8 GEMV (speculative verification): Y[t][M] = W . A8(X[t][K]) for t < n_tokens,
+ * each row exactly the single-token result.  Replaces the per-token loop of the verify path
+ * (forward_verify_serial, asdsl/kernels/native/unified_engine.cpp:1766-1772, over
+ * gemv_q4_32_preq_fused_avx2 / gemv_q4km_q8_avx2) and the batched gemm_q4_32_q8_avx2
+ * (asdsl/kernels/native/gemm_batch.cpp:146-260).  fmt PREQ (w0 = blocks), PREQ2 (w0 = meta,
+ * w1 = quant), Q4_128_BANDED (w0 = quant, w1 = scales; A8 at gs 128) or Q4K (w0 = blocks, the
+ * Q4_K kernel's own A8).  Up to 16 tokens share one weight stream (fewer when 16 A8 rows of
+ * in_features do not fit beside the pipeline); more tokens take further passes. */
+int asdsl_b200_gemv_multi(int fmt, const uint8_t* w0, const uint8_t* w1, const float* X, float* Y,
+                          int out_features, int in_features, int n_tokens, void* stream);
 
 /* ======================================================================================
  * Device-resident decode engine: UnifiedEngine (asdsl/kernels/native/unified_engine.h:14-109,
