@@ -1,0 +1,176 @@
+"""Row-sharded lm_head / gate_up and K-split down projection across the GPUs of one box.
+
+One process per GPU (torch.distributed, NCCL over NVLink); every rank holds a contiguous slice
+of the projection's rows (lm_head, gate_up) or of its input columns (down):
+
+* lm_head (BASELINE config 2 / the engine's lm_head, unified_engine.cpp:1628-1662 with
+  argmax_f32_avx2 :207-233): rank r owns rows [a_r, b_r), runs the fused GEMV + first-max
+  argmax on them with row_base = a_r, and the ranks all-gather one (max, index) pair each
+  (8 bytes).  The final pick is the first maximum in rank order; ranks hold ascending row
+  ranges, so that is the lowest global index among equal maxima, as the reference's scan.
+* gate_up: rank r owns gate rows [a_r, b_r) and the matching up rows [I + a_r, I + b_r), so
+  SiLU(gate)*up is local and yields h[a_r:b_r).
+* down: rank r owns input columns [a_r, b_r) of down_proj (whole activation groups: the A8
+  quantization is per group, so the local A8 of h[a_r:b_r) equals the slice of the global
+  one); partial outputs are summed with one all-reduce of hidden_size floats.  The sum order
+  across ranks differs from the reference's, which the GEMV tolerance covers.
+
+The per-shard compute goes through the C ABI kernels by default; tests running the ranks as
+gloo processes on the CPU pass the CPU oracle as `local` backend instead, so the collective
+logic is the same code on both.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from asdsl_b200 import _lib
+
+
+def shard_range(n: int, world: int, rank: int, align: int = 4) -> tuple[int, int]:
+    """[a, b) of `n` items for `rank`: contiguous, ascending in rank, boundaries multiples of
+    `align` (4-row bands; 32 or 128 columns for whole activation groups), sizes differing by at
+    most `align`."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("invalid rank / world size")
+    if n % align:
+        raise ValueError(f"{n} items cannot be split on a {align}-item boundary")
+    units = n // align
+    a = units * rank // world
+    b = units * (rank + 1) // world
+    return a * align, b * align
+
+
+def combine_argmax(pairs: torch.Tensor) -> tuple[float, int]:
+    """pairs [world, 2] int32: (max value bits as float32, global index) per rank, in rank
+    order.  First maximum wins (ties -> lowest rank = lowest index range)."""
+    vals = pairs[:, 0].contiguous().view(torch.float32)
+    best = int(torch.nonzero(vals == vals.max())[0].item())
+    return float(vals[best].item()), int(pairs[best, 1].item())
+
+
+def _all_gather_pairs(pair: torch.Tensor, world: int) -> torch.Tensor:
+    import torch.distributed as dist
+
+    parts = [torch.empty_like(pair) for _ in range(world)]
+    dist.all_gather(parts, pair)
+    return torch.stack(parts)
+
+
+def _group(world=None, rank=None):
+    """(world size, rank) of the default process group, or the explicit pair (rank emulation:
+    one process computing one shard, with the caller combining the shards)."""
+    if world is not None:
+        return int(world), int(rank)
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size(), dist.get_rank()
+    return 1, 0
+
+
+class ShardedLMHead:
+    """This rank's Q4_128 lm_head rows in the banded device layout (or the CPU oracle's raw
+    blocks when `local` is given) and the fused argmax + all-gather of (max, index)."""
+
+    def __init__(self, blocks: np.ndarray, vocab: int, hidden: int, local=None, device=None, world=None, rank=None):
+        self.world, self.rank = _group(world, rank)
+        self.V, self.H = vocab, hidden
+        self.a, self.b = shard_range(vocab, self.world, self.rank, 4)
+        ng = hidden // 128
+        rows = np.asarray(blocks, dtype=np.uint8).reshape(vocab, ng * 66)[self.a : self.b]
+        self.rows = self.b - self.a
+        self.local = local
+        if local is None:
+            from asdsl_b200.layer import relayout_q4_128
+
+            dev = device or torch.device("cuda", torch.cuda.current_device())
+            self.device = dev
+            raw = torch.from_numpy(np.ascontiguousarray(rows).reshape(-1)).to(dev)
+            self.quant, self.scales = relayout_q4_128(raw, self.rows, hidden)
+            del raw
+            self.scratch = torch.zeros(_lib.load().asdsl_b200_argmax_scratch_bytes(), dtype=torch.uint8, device=dev)
+            self.val = torch.empty(1, dtype=torch.float32, device=dev)
+            self.idx = torch.empty(1, dtype=torch.int32, device=dev)
+            self.logits = torch.empty(max(self.rows, 1), dtype=torch.float32, device=dev)
+        else:
+            self.device = torch.device("cpu")
+            self.blocks = np.ascontiguousarray(rows)
+
+    def local_pair(self, x) -> torch.Tensor:
+        """(max bits, global index) of this rank's rows, int32 [2] on this rank's device."""
+        if self.local is not None:
+            y = self.local.gemv_q4_128_fused(self.blocks, np.asarray(x, np.float32), self.rows, self.H)
+            i = int(self.local.argmax(y))
+            return torch.tensor([np.float32(y[i]).view(np.int32), self.a + i], dtype=torch.int32)
+        _lib.call("asdsl_b200_gemv_argmax", _lib.FMT_Q4_128_BANDED, self.quant.data_ptr(), self.scales.data_ptr(),
+                  x.data_ptr(), self.logits.data_ptr(), self.val.data_ptr(), self.idx.data_ptr(), self.a,
+                  self.scratch.data_ptr(), self.scratch.numel(), self.rows, self.H,
+                  torch.cuda.current_stream(self.device).cuda_stream)
+        return torch.cat([self.val.view(torch.int32), self.idx])
+
+    def argmax(self, x) -> tuple[float, int]:
+        pair = self.local_pair(x)
+        if self.world == 1:
+            return combine_argmax(pair.view(1, 2))
+        return combine_argmax(_all_gather_pairs(pair, self.world).cpu())
+
+
+class ShardedMLP:
+    """gate_up rows and down columns of one layer for this rank (preq2 gs32 blobs), with the
+    fused gate_up+SiLU on the local rows and an all-reduce of the down partial sums."""
+
+    def __init__(self, gu_meta, gu_quant, dn_meta, dn_quant, hidden: int, inter: int, local=None, device=None,
+                 world=None, rank=None):
+        self.world, self.rank = _group(world, rank)
+        self.H, self.I = hidden, inter
+        self.a, self.b = shard_range(inter, self.world, self.rank, 32)
+        if self.a % 4 or self.b % 4:
+            raise ValueError("gate_up shards must start on 4-row bands")
+        self.n = self.b - self.a
+        H, I = hidden, inter
+        ngH, ngI = H // 32, I // 32
+        gm = np.asarray(gu_meta, np.uint8).reshape(2 * I, ngH * 4)
+        gq = np.asarray(gu_quant, np.uint8).reshape(2 * I // 4, ngH * 64)
+        # local gate rows then local up rows, as the paired SiLU layout expects
+        self.gu_meta = np.ascontiguousarray(np.concatenate([gm[self.a : self.b], gm[I + self.a : I + self.b]]))
+        self.gu_quant = np.ascontiguousarray(
+            np.concatenate([gq[self.a // 4 : self.b // 4], gq[(I + self.a) // 4 : (I + self.b) // 4]]))
+        g0, g1 = self.a // 32, self.b // 32
+        dm = np.asarray(dn_meta, np.uint8).reshape(H, ngI, 4)
+        dq = np.asarray(dn_quant, np.uint8).reshape((H + 3) // 4, ngI, 64)
+        self.dn_meta = np.ascontiguousarray(dm[:, g0:g1, :]).reshape(-1)
+        self.dn_quant = np.ascontiguousarray(dq[:, g0:g1, :]).reshape(-1)
+        self.local = local
+        if local is None:
+            dev = device or torch.device("cuda", torch.cuda.current_device())
+            self.device = dev
+            t = lambda a: torch.from_numpy(np.ascontiguousarray(a).reshape(-1)).to(dev)  # noqa: E731
+            self.d_gm, self.d_gq, self.d_dm, self.d_dq = t(self.gu_meta), t(self.gu_quant), t(self.dn_meta), t(self.dn_quant)
+            self.h = torch.empty(self.n, dtype=torch.float32, device=dev)
+            self.y = torch.empty(H, dtype=torch.float32, device=dev)
+        else:
+            self.device = torch.device("cpu")
+
+    def local_partial(self, x):
+        """down[:, a:b] . A8(silu(gate[a:b] x) * up[a:b] x): this rank's partial output."""
+        if self.local is not None:
+            o = self.local
+            gu = o.gemv_preq2_fused(self.gu_meta, self.gu_quant, np.asarray(x, np.float32), 2 * self.n, self.H)
+            h = o.swiglu(gu[: self.n], gu[self.n :])
+            return torch.from_numpy(o.gemv_preq2_fused(self.dn_meta, self.dn_quant, h, self.H, self.n))
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.call("asdsl_b200_gateup_silu", _lib.FMT_PREQ2, self.d_gm.data_ptr(), self.d_gq.data_ptr(), x.data_ptr(),
+                  self.h.data_ptr(), self.n, self.H, s)
+        _lib.call("asdsl_b200_gemv_preq2_fused", self.d_dm.data_ptr(), self.d_dq.data_ptr(), self.h.data_ptr(),
+                  self.y.data_ptr(), self.H, self.n, 32, s)
+        return self.y
+
+    def forward(self, x) -> torch.Tensor:
+        y = self.local_partial(x)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(y, op=dist.ReduceOp.SUM)
+        return y
