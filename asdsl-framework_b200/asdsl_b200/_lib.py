@@ -54,6 +54,11 @@ _SIGS = {
     "asdsl_b200_gemv_argmax_static": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_gateup_silu": [_I, _P, _P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_multi": [_I, _P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_xchg_create": [_I, _I, _P, _P],
+    "asdsl_b200_xchg_handle_bytes": [],
+    "asdsl_b200_xchg_open": [_P, _P],
+    "asdsl_b200_xchg_destroy": [_P],
+    "asdsl_b200_gemv_argmax_xchg": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P, _P],
     # device-resident decode engine
     "asdsl_b200_engine_create": [_P, _P],
     "asdsl_b200_engine_destroy": [_P],
@@ -90,6 +95,7 @@ _RESTYPES = {
     "asdsl_b200_version": ctypes.c_char_p,
     "asdsl_b200_last_error": ctypes.c_char_p,
     "asdsl_b200_argmax_scratch_bytes": _SZ,
+    "asdsl_b200_xchg_handle_bytes": _SZ,
 }
 
 _lib = None

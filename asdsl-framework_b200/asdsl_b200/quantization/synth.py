@@ -100,3 +100,14 @@ def random_q4k_bytes(rng: np.random.Generator, rows: int, cols: int, d: float = 
     blocks[:, :, 0:2] = np.array([d], dtype=np.float16).view(np.uint8)
     blocks[:, :, 2:4] = np.array([dmin], dtype=np.float16).view(np.uint8)
     return blocks
+
+
+def random_q4_128(rng: np.random.Generator, rows: int, cols: int, scale_range=(0.006, 0.012)) -> np.ndarray:
+    """Random Q4_128 blocks [rows][cols/128][66]: uniform nibbles and fp16 scales in the range the
+    symmetric quantizer gives N(0, 0.02) rows (amax / 7); for timing-sized weights whose float
+    source would take minutes to quantize on the host."""
+    ng = cols // 128
+    blocks = rng.integers(0, 256, size=(rows, ng, 66), dtype=np.uint8)
+    s = rng.uniform(*scale_range, size=(rows, ng)).astype(np.float16)
+    blocks[:, :, 0:2] = s.view(np.uint8).reshape(rows, ng, 2)
+    return blocks

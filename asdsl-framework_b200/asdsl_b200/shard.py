@@ -70,11 +70,45 @@ def _group(world=None, rank=None):
     return 1, 0
 
 
+class _Exchange:
+    """Slot buffer of the in-kernel argmax exchange (asdsl_b200_xchg_*): created on every rank,
+    its CUDA IPC handle all-gathered in rank order, then the peers' buffers mapped."""
+
+    def __init__(self, world: int, rank: int, device):
+        import ctypes
+
+        lib = _lib.load()
+        self._lib = lib
+        hb = int(lib.asdsl_b200_xchg_handle_bytes())
+        h = (ctypes.c_uint8 * hb)()
+        self.ptr = ctypes.c_void_p()
+        _lib.check(lib.asdsl_b200_xchg_create(world, rank, ctypes.byref(self.ptr), h), "xchg_create")
+        mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device=device)
+        if world > 1:
+            import torch.distributed as dist
+
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(parts, mine)
+            allh = np.ascontiguousarray(torch.cat(parts).cpu().numpy())
+        else:
+            allh = np.ascontiguousarray(mine.cpu().numpy())
+        _lib.check(lib.asdsl_b200_xchg_open(self.ptr, allh.ctypes.data), "xchg_open")
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            self._lib.asdsl_b200_xchg_destroy(self.ptr)
+            self.ptr = None
+
+
 class ShardedLMHead:
     """This rank's Q4_128 lm_head rows in the banded device layout (or the CPU oracle's raw
-    blocks when `local` is given) and the fused argmax + all-gather of (max, index)."""
+    blocks when `local` is given) and the argmax across ranks: with fused=True (GPUs, the
+    default) one kernel per step exchanges the (max, index) pairs over NVLink peer stores
+    (asdsl_b200_gemv_argmax_xchg); otherwise an all-gather of the pairs through the process
+    group follows the local fused GEMV + argmax."""
 
-    def __init__(self, blocks: np.ndarray, vocab: int, hidden: int, local=None, device=None, world=None, rank=None):
+    def __init__(self, blocks: np.ndarray, vocab: int, hidden: int, local=None, device=None, world=None, rank=None,
+                 fused: bool = True):
         self.world, self.rank = _group(world, rank)
         self.V, self.H = vocab, hidden
         self.a, self.b = shard_range(vocab, self.world, self.rank, 4)
@@ -94,9 +128,25 @@ class ShardedLMHead:
             self.val = torch.empty(1, dtype=torch.float32, device=dev)
             self.idx = torch.empty(1, dtype=torch.int32, device=dev)
             self.logits = torch.empty(max(self.rows, 1), dtype=torch.float32, device=dev)
+            self.xchg = _Exchange(self.world, self.rank, dev) if (fused and world is None) else None
         else:
             self.device = torch.device("cpu")
             self.blocks = np.ascontiguousarray(rows)
+            self.xchg = None
+
+    def close(self):
+        if getattr(self, "xchg", None) is not None:
+            self.xchg.close()
+            self.xchg = None
+
+    def fused_step(self, x) -> torch.Tensor:
+        """One kernel: local GEMV + argmax + exchange with the peers; returns the global index
+        (int32 [1] on this rank's device; self.val holds the maximum)."""
+        _lib.call("asdsl_b200_gemv_argmax_xchg", _lib.FMT_Q4_128_BANDED, self.quant.data_ptr(), self.scales.data_ptr(),
+                  x.data_ptr(), self.logits.data_ptr(), self.val.data_ptr(), self.idx.data_ptr(), self.a,
+                  self.scratch.data_ptr(), self.scratch.numel(), self.rows, self.H, self.xchg.ptr,
+                  torch.cuda.current_stream(self.device).cuda_stream)
+        return self.idx
 
     def local_pair(self, x) -> torch.Tensor:
         """(max bits, global index) of this rank's rows, int32 [2] on this rank's device."""
@@ -111,6 +161,9 @@ class ShardedLMHead:
         return torch.cat([self.val.view(torch.int32), self.idx])
 
     def argmax(self, x) -> tuple[float, int]:
+        if self.xchg is not None:
+            idx = int(self.fused_step(x).item())
+            return float(self.val.item()), idx
         pair = self.local_pair(x)
         if self.world == 1:
             return combine_argmax(pair.view(1, 2))

@@ -355,9 +355,22 @@ int asdsl_b200_gemv_q4_128_banded(const uint8_t* quant, const uint8_t* scales, c
     return launch_stream_gemv<kFmtQ128B, kProA8, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
 }
 
-int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y, float* out_val,
-                           int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes, int M, int K,
-                           void* stream) {
+}  // extern "C"
+
+// cross-GPU argmax exchange of a row-sharded lm_head (asdsl_b200_xchg_*)
+struct asdsl_b200_xchg {
+    int world = 1, rank = 0, device = 0;
+    unsigned long long* slots = nullptr;       // this rank's [2][world] words
+    int* epoch = nullptr;                      // device-resident step counter
+    unsigned long long** peer_table = nullptr; // device array [world]
+    void* mapped[64] = {};                     // opened peer mappings (null for self)
+    bool open = false;
+};
+
+namespace {
+int gemv_argmax_impl(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y, float* out_val,
+                     int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes, int M, int K, void* stream,
+                     const asdsl_b200_xchg* xg) {
     if (!w0 || !x || !out_val || !out_idx || !scratch) return set_error(kEinval, "gemv_argmax: null pointer");
     if (scratch_bytes < asdsl_b200_argmax_scratch_bytes()) return set_error(kEinval, "gemv_argmax: scratch too small");
     if (M <= 0) return set_error(kEinval, "gemv_argmax: invalid dimensions");
@@ -374,6 +387,13 @@ int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const 
         a.out_val = out_val;
         a.out_idx = out_idx;
         a.row_base = row_base;
+        if (xg) {
+            a.xchg_peers = xg->peer_table;
+            a.xchg_self = xg->slots;
+            a.xchg_epoch = xg->epoch;
+            a.xchg_world = xg->world;
+            a.xchg_rank = xg->rank;
+        }
     };
     const long long nbands = (static_cast<long long>(M) + 3) / 4;
     if (fmt == ASDSL_B200_FMT_PREQ2) {
@@ -402,6 +422,91 @@ int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const 
         return launch_stream_gemv<kFmtQ128B, kProA8, kEpiArgmax>(s, 2, nbands, 0, ga, as_stream(stream));
     }
     return set_error(kEinval, "gemv_argmax: unsupported weight format");
+}
+}  // namespace
+
+extern "C" {
+
+int asdsl_b200_gemv_argmax(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y, float* out_val,
+                           int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes, int M, int K,
+                           void* stream) {
+    return gemv_argmax_impl(fmt, w0, w1, x, y, out_val, out_idx, row_base, scratch, scratch_bytes, M, K, stream,
+                            nullptr);
+}
+
+int asdsl_b200_xchg_create(int world, int rank, asdsl_b200_xchg** out, void* ipc_handle) {
+    if (!out || !ipc_handle) return set_error(kEinval, "xchg_create: null pointer");
+    if (world < 1 || world > 64 || rank < 0 || rank >= world) return set_error(kEinval, "xchg_create: bad rank / world");
+    *out = nullptr;
+    auto* x = new asdsl_b200_xchg();
+    x->world = world;
+    x->rank = rank;
+    cudaGetDevice(&x->device);
+    auto fail = [&](int rc) {
+        asdsl_b200_xchg_destroy(x);
+        return rc;
+    };
+    const size_t bytes = 2ull * world * sizeof(unsigned long long);
+    if (cudaMalloc(reinterpret_cast<void**>(&x->slots), bytes) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&x->epoch), sizeof(int)) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&x->peer_table), world * sizeof(void*)) != cudaSuccess)
+        return fail(set_error(asdsl::kEnomem, "xchg_create: device allocation failed"));
+    if (cudaMemset(x->slots, 0, bytes) != cudaSuccess || cudaMemset(x->epoch, 0, sizeof(int)) != cudaSuccess)
+        return fail(set_error(kEcuda, "xchg_create: memset failed"));
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, x->slots);
+    if (e != cudaSuccess) return fail(set_error(kEcuda, std::string("xchg_create: cudaIpcGetMemHandle: ") + cudaGetErrorString(e)));
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *out = x;
+    return kOk;
+}
+
+size_t asdsl_b200_xchg_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int asdsl_b200_xchg_open(asdsl_b200_xchg* x, const void* handles) {
+    if (!x || !handles) return set_error(kEinval, "xchg_open: null pointer");
+    if (x->open) return kOk;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != x->device) return set_error(kEinval, "xchg_open: call with the exchange's device current");
+    unsigned long long* table[64];
+    for (int r = 0; r < x->world; ++r) {
+        if (r == x->rank) {
+            table[r] = x->slots;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + r * sizeof(h), sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error(kEcuda, std::string("xchg_open: cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+        x->mapped[r] = p;
+        table[r] = static_cast<unsigned long long*>(p);
+    }
+    ASDSL_CUDA(cudaMemcpy(x->peer_table, table, x->world * sizeof(void*), cudaMemcpyHostToDevice));
+    x->open = true;
+    return kOk;
+}
+
+int asdsl_b200_xchg_destroy(asdsl_b200_xchg* x) {
+    if (!x) return kOk;
+    for (int r = 0; r < 64; ++r)
+        if (x->mapped[r]) cudaIpcCloseMemHandle(x->mapped[r]);
+    if (x->slots) cudaFree(x->slots);
+    if (x->epoch) cudaFree(x->epoch);
+    if (x->peer_table) cudaFree(x->peer_table);
+    delete x;
+    return kOk;
+}
+
+int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
+                                float* out_val, int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes,
+                                int M, int K, asdsl_b200_xchg* xg, void* stream) {
+    if (!xg || !xg->open) return set_error(kEinval, "gemv_argmax_xchg: exchange not opened");
+    if (static_cast<long long>(row_base) + M > (1ll << 24))
+        return set_error(kEinval, "gemv_argmax_xchg: global row indices must stay below 2^24");
+    return gemv_argmax_impl(fmt, w0, w1, x, y, out_val, out_idx, row_base, scratch, scratch_bytes, M, K, stream, xg);
 }
 
 }  // extern "C"

@@ -22,10 +22,21 @@ enum : unsigned int {
     kStatusWaitEmpty = 2u,    // producer gave up waiting for a stage to drain
     kStatusWaitDrain = 4u,    // producer gave up draining its copies at exit
     kStatusBadLaunch = 8u,    // kernel saw an inconsistent launch configuration
+    kStatusXchgWait = 16u,    // a cross-GPU exchange gave up waiting for a peer's word
 };
 
 // Wall-clock limit of any single device-side wait.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+// system-scope 64-bit store / load for words exchanged with peer GPUs over NVLink
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;

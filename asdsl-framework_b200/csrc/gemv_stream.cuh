@@ -129,6 +129,12 @@ struct GemvArgs {
     int row_base;          // global index of row 0 (row-sharded lm_head)
     unsigned int* status;  // device status word
     int n_tokens;          // multi-token kernels (NT > 1): activation rows x[t][K] -> y[t][M]
+    // argmax exchange with the peer GPUs of a row-sharded lm_head (null = single GPU):
+    // slot buffers [2 parities][world] of packed (max bits | index << 32 | epoch << 56)
+    unsigned long long* const* xchg_peers;  // [world] every rank's slot buffer (peer mappings)
+    unsigned long long* xchg_self;          // this rank's slot buffer
+    int* xchg_epoch;                        // device-resident step counter of the exchange
+    int xchg_world, xchg_rank;
 };
 
 // ---------------------------------------------------------------------------
@@ -936,8 +942,50 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
                 argmax_take(bv, bi, ov, oi);
             }
             if (lane == 0) {
-                *ga.out_val = bv;
-                *ga.out_idx = (bi == 0x7fffffff) ? ga.row_base : bi;
+                float fv = bv;
+                int fi = (bi == 0x7fffffff) ? ga.row_base : bi;
+                if (ga.xchg_self != nullptr) {
+                    // fused all-gather of (max, index): store this rank's word into every rank's
+                    // slot (NVLink peer stores), then wait -- bounded -- for all words of this
+                    // step and keep the first maximum in rank order (= lowest global index)
+                    const int W = ga.xchg_world;
+                    const int e = *ga.xchg_epoch + 1;
+                    const int par = e & 1;
+                    const unsigned long long e8 = static_cast<unsigned long long>(e & 0xFF);
+                    const unsigned long long word = static_cast<unsigned long long>(__float_as_uint(fv)) |
+                                                    (static_cast<unsigned long long>(fi & 0xFFFFFF) << 32) |
+                                                    (e8 << 56);
+                    for (int r = 0; r < W; ++r) st_release_sys_u64(ga.xchg_peers[r] + par * W + ga.xchg_rank, word);
+                    float gv = -INFINITY;
+                    int gi = fi;
+                    bool ok = true;
+                    const unsigned long long t0 = globaltimer_ns();
+                    for (int r = 0; r < W && ok; ++r) {
+                        unsigned long long w = ld_acquire_sys_u64(ga.xchg_self + par * W + r);
+                        while ((w >> 56) != e8) {
+                            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                                ok = false;
+                                break;
+                            }
+                            w = ld_acquire_sys_u64(ga.xchg_self + par * W + r);
+                        }
+                        if (!ok) break;
+                        const float v = __uint_as_float(static_cast<unsigned int>(w));
+                        if (r == 0 || v > gv) {
+                            gv = v;
+                            gi = static_cast<int>((w >> 32) & 0xFFFFFFull);
+                        }
+                    }
+                    if (ok) {
+                        fv = gv;
+                        fi = gi;
+                    } else {
+                        atomicOr(ga.status, kStatusXchgWait);
+                    }
+                    *ga.xchg_epoch = e;
+                }
+                *ga.out_val = fv;
+                *ga.out_idx = fi;
                 *ga.counter = 0u;  // re-arm for the next call
             }
         }

@@ -286,6 +286,115 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
 
 
 # ---------------------------------------------------------------------------
+# config 2: lm_head 200064x3072 Q4_128, row-sharded over the ranks, fused argmax + all-gather
+# ---------------------------------------------------------------------------
+LM_METRIC = "lm_head W4 GEMV + argmax HBM GB/s (200064x3072 Q4_128, row-sharded, all ranks)"
+
+
+def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dict:
+    """Strong scaling: the whole 200064-row lm_head is split over the ranks; a step is the local
+    fused GEMV + argmax, the all-gather of one (max, index) pair per rank (NCCL) and the device
+    pick of the first maximum.  value = all ranks' weight bytes / max-over-ranks step time.
+    Each rank rotates enough weight copies to stream > 126 MB (L2) per cycle."""
+    import numpy as np
+    import torch
+
+    from asdsl_b200 import _lib
+    from asdsl_b200.quantization.synth import random_q4_128
+    from asdsl_b200.shard import ShardedLMHead
+
+    V, H = 200064, 3072
+    rng = np.random.default_rng(seed)
+    blocks = random_q4_128(rng, V, H)
+    x = rng.standard_normal(H).astype(np.float32)
+    heads = [ShardedLMHead(blocks, V, H)]
+    shard_bytes = heads[0].quant.numel() + heads[0].scales.numel()
+    n_copies = max(1, -(-160_000_000 // shard_bytes))
+    for _ in range(n_copies - 1):
+        heads.append(ShardedLMHead(blocks, V, H))
+    xd = torch.from_numpy(x).cuda()
+    # correctness: the combined index is the first maximum of the full logits (rank 0 checks)
+    val, idx = heads[0].argmax(xd)
+    check = None
+    if rank == 0:
+        from oracle.oracle import Oracle, build as build_oracle
+
+        if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+            build_oracle()
+        y = Oracle().gemv_q4_128_fused(blocks, x, V, H)
+        srt = np.sort(y)
+        tie = srt[-1] - srt[-2] <= 4e-3 * np.abs(y).max()
+        check = {"argmax": idx, "oracle_argmax": int(np.argmax(y)), "near_tie": bool(tie)}
+        if not tie and idx != int(np.argmax(y)):
+            raise SystemExit(f"bench: sharded lm_head argmax {idx} != oracle {int(np.argmax(y))}")
+    del blocks
+
+    def step(h):
+        if h.xchg is not None:
+            return h.fused_step(xd)
+        pair = h.local_pair(xd)
+        if world > 1:
+            import torch.distributed as dist
+
+            parts = torch.empty(world * 2, dtype=torch.int32, device=xd.device)
+            dist.all_gather_into_tensor(parts, pair)
+        else:
+            parts = pair
+        g = parts.view(-1, 2)
+        best = torch.argmax(g[:, 0].contiguous().view(torch.float32))  # first maximum, rank order
+        return g[best, 1]
+
+    for i in range(5):
+        step(heads[i % len(heads)])
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        step(heads[i % len(heads)])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # e2e: host activation in, host token out, every step
+    hx = torch.from_numpy(x).pin_memory()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = min(steps, 100)
+    f0.record()
+    for i in range(n_e2e):
+        xd.copy_(hx, non_blocking=True)
+        int(step(heads[i % len(heads)]).item())
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / n_e2e
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0].item()), float(t[1].item())
+    assert _lib.device_status(clear=True) == 0
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()  # no rank still stores into a peer's slots
+    for h in heads:
+        h.close()
+    total = V * (H // 128) * 66
+    return {"metric": LM_METRIC, "value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 5), "n_gpus": world, "scaling": "strong", "steps": steps,
+            "bytes_per_step": total, "weight_copies_rotated_per_rank": len(heads),
+            "collective": ("in-kernel exchange of one (max, index) word per rank over NVLink peer stores"
+                           if world > 1 else None),
+            "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
+                    "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 5)},
+            "check": check, "config": {"workload": "c2_lm_head_row_sharded", "seed": seed,
+                                       "weights": "random Q4_128 bytes (synthetic)"}}
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 def main():
@@ -298,6 +407,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
+    ap.add_argument("--no-lm-head", action="store_true", help="skip the config-2 sharded lm_head measurement")
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--clock-preroll", type=float, default=1.5,
                     help="seconds of untimed replays inside the clock-sampling window before timing")
@@ -514,6 +624,7 @@ def main():
     decode = None
     if world == 1 and not args.no_decode:
         decode = decode_bench(args.decode_steps)
+    lm_sharded = None if args.no_lm_head else lm_head_bench(world, rank)
 
     if rank == 0:
         clocks = clk.summary()
@@ -545,6 +656,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "decode": decode,
+            "lm_head_sharded": lm_sharded,
         }
         print(json.dumps(out), flush=True)
     for g in graphs:

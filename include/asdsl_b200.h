@@ -162,6 +162,28 @@ int asdsl_b200_gemv_argmax_static(int fmt, const uint8_t* w0, const uint8_t* w1,
                                   float* out_val, int32_t* out_idx, int row_base, int out_features,
                                   int in_features, void* stream);
 
+/* Row-sharded lm_head across the GPUs of one box (one process per GPU): the argmax of the
+ * last CTA is exchanged with the peers inside the kernel (NVLink peer stores of one packed
+ * (max, index, step) word per rank into every rank's slot buffer, bounded wait for all words),
+ * so every rank ends the kernel holding the global first maximum.  Replaces the engine's
+ * lm_head GEMV + argmax_f32_avx2 (asdsl/kernels/native/unified_engine.cpp:1628-1662, :207-233)
+ * split over GPUs with an all-gather of (max, index).
+ * Setup: each rank calls asdsl_b200_xchg_create (ipc_handle receives
+ * asdsl_b200_xchg_handle_bytes() bytes), the handles are all-gathered in rank order by the host
+ * (e.g. torch.distributed), and each rank calls asdsl_b200_xchg_open with the world's handles.
+ * Every rank must then call asdsl_b200_gemv_argmax_xchg the same number of times; a call whose
+ * peers do not arrive within 2 s returns ASDSL_B200_ETIMEOUT through the device status word.
+ * Global indices (row_base + local row) must stay below 2^24. */
+typedef struct asdsl_b200_xchg asdsl_b200_xchg;
+int asdsl_b200_xchg_create(int world, int rank, asdsl_b200_xchg** out, void* ipc_handle);
+size_t asdsl_b200_xchg_handle_bytes(void);
+int asdsl_b200_xchg_open(asdsl_b200_xchg* xchg, const void* handles);
+int asdsl_b200_xchg_destroy(asdsl_b200_xchg* xchg);
+int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
+                                float* out_val, int32_t* out_idx, int row_base, void* scratch,
+                                size_t scratch_bytes, int out_features, int in_features, asdsl_b200_xchg* xchg,
+                                void* stream);
+
 /* Fused gate_up GEMV + SiLU(gate)*up: rows [0, I) are gate, [I, 2I) are up, h[i] = silu(gate_i)*up_i
  * with the reference's fast_exp.  fmt PREQ2 (w0 = meta, w1 = quant), Q4_128 (w0 = blocks) or
  * Q4_128_BANDED (w0 = quant, w1 = scales).

@@ -65,3 +65,23 @@ def test_sharded_mlp_device(native, oracle, world):
         acc += mlp.local_partial(xd).cpu().numpy()
     assert rel_err(acc, ref) < TOL
     assert native.device_status(clear=True) == 0
+
+
+def test_sharded_lm_head_fused_exchange_single_rank(native, oracle, lm_case):
+    """The in-kernel exchange path with a world of one (the kernel stores into and waits on
+    its own slot buffer); repeated calls advance the device-resident step counter."""
+    from asdsl_b200.shard import ShardedLMHead
+
+    blocks, x, V, H = lm_case
+    y = oracle.gemv_q4_128_fused(blocks, x, V, H)
+    head = ShardedLMHead(blocks, V, H)
+    try:
+        assert head.xchg is not None
+        xd = torch.from_numpy(x).cuda()
+        for _ in range(300):  # crosses the 8-bit step wrap
+            val, idx = head.argmax(xd)
+            assert idx == int(np.argmax(head.logits.cpu().numpy()))
+        assert rel_err(head.logits.cpu().numpy(), y) < TOL
+    finally:
+        head.close()
+    assert native.device_status(clear=True) == 0
