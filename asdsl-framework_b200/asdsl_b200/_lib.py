@@ -77,6 +77,8 @@ _SIGS = {
     "asdsl_b200_engine_restore_kv": [_P],
     "asdsl_b200_engine_export_lm_head": [_P, _P, _P, _SZ, _P, _SZ],
     "asdsl_b200_engine_stream": [_P, _P],
+    "asdsl_b200_engine_set_persistent": [_P, _I],
+    "asdsl_b200_engine_profile_step": [_P, _I, _P, _I, _P],
     "asdsl_b200_engine_set_position": [_P, _I, _I],
     "asdsl_b200_engine_replay": [_P, _I, _I],
     "asdsl_b200_engine_read_buffer": [_P, _I, _P, _SZ],

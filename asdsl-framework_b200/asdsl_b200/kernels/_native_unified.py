@@ -80,7 +80,7 @@ class UnifiedEngine:
     layers_dict, lm_head_preq2_meta=None, lm_head_preq2_quant=None)  (:2662-2682)."""
 
     def __init__(self, config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
-                 lm_head_preq2_meta=None, lm_head_preq2_quant=None):
+                 lm_head_preq2_meta=None, lm_head_preq2_quant=None, persistent: bool | None = None):
         lib = _lib.load()
         self._lib = lib
         self.config_ = config
@@ -88,6 +88,8 @@ class UnifiedEngine:
         _lib.check(lib.asdsl_b200_engine_create(ctypes.byref(config._c()), ctypes.byref(self._e)),
                    "UnifiedEngine")
         try:
+            if persistent is not None:
+                _lib.check(lib.asdsl_b200_engine_set_persistent(self._e, 1 if persistent else 0), "UnifiedEngine")
             self._load(config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
                        lm_head_preq2_meta, lm_head_preq2_quant)
         except BaseException:
@@ -252,6 +254,25 @@ class UnifiedEngine:
         """Enqueue n decode (or prefill) graph replays on the engine stream without synchronising."""
         _lib.check(self._lib.asdsl_b200_engine_replay(self._e, 1 if decode else 0, int(n)), "replay")
 
+    def profile_step(self, decode: bool = True) -> list[dict]:
+        """Per-op timing of one persistent decode step at the current position: for each op its
+        kind, work time (earliest start to latest end over CTAs) and barrier time, in us."""
+        cap = 4 * self.config_.num_layers * 5 + 16
+        buf = (ctypes.c_ulonglong * (3 * cap))()
+        n = ctypes.c_int(0)
+        _lib.check(self._lib.asdsl_b200_engine_profile_step(self._e, 1 if decode else 0, buf, cap, ctypes.byref(n)),
+                   "profile_step")
+        names = ["embed"]
+        for _ in range(self.config_.num_layers):
+            names += ["qkv", "attention", "o", "gate_up", "down"]
+        names += ["lm_head", "argmax"] if decode else []
+        out = []
+        for i in range(n.value):
+            t0, t1, t2 = buf[3 * i], buf[3 * i + 1], buf[3 * i + 2]
+            out.append({"op": names[i] if i < len(names) else str(i), "work_us": (t1 - t0) / 1e3,
+                        "barrier_us": (t2 - t1) / 1e3 if t2 >= t1 else 0.0})
+        return out
+
     _BUFFERS = ("resid", "qkv", "att", "h", "logits", "kq", "vq", "ks", "vs")
 
     def read_buffer(self, name: str) -> np.ndarray:
@@ -272,7 +293,7 @@ class UnifiedEngine:
 
 
 def engine_from_model(model: dict, lm_head_group_size: int = 32, max_seq_len: int | None = None,
-                      use_preq2_cache: bool = False) -> UnifiedEngine:
+                      use_preq2_cache: bool = False, persistent: bool | None = None) -> UnifiedEngine:
     """UnifiedEngine over a synthetic model of asdsl_b200.inference.synthetic.build_model, wired as
     the reference's unified_bridge.build_unified_engine does (tied fp16 embedding as lm_head source)."""
     c = model["config"]
@@ -294,4 +315,4 @@ def engine_from_model(model: dict, lm_head_group_size: int = 32, max_seq_len: in
     meta = model.get("lm_meta") if use_preq2_cache else None
     quant = model.get("lm_quant") if use_preq2_cache else None
     return UnifiedEngine(cfg, model["embed_f16"], model["output_norm"], None if meta is not None else model["embed_f16"],
-                         model["cos"], model["sin"], layers, meta, quant)
+                         model["cos"], model["sin"], layers, meta, quant, persistent=persistent)

@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "decode_step.cuh"
 #include "engine_ops.cuh"
 
 namespace {
@@ -72,6 +73,14 @@ struct asdsl_b200_engine {
     int* h_stage = nullptr;  // [4]: pos, token, argmax, status
     cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
     bool finalized = false;
+    // per-op kernel chain (default; measured faster on B200) or the persistent decode-step kernel
+    int persistent = 0;
+    asdsl::StepOp* d_prog[2] = {nullptr, nullptr};  // [0] prefill, [1] decode
+    asdsl::StepArgs prog_args[2] = {};
+    uint32_t prog_smem = 0;
+    unsigned int* grid_bar = nullptr;
+    float* part_val = nullptr;
+    int* part_idx = nullptr;
     int kv_seq_len = 0;
     std::vector<int> snapshots;
 };
@@ -163,8 +172,195 @@ int launch_small(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_
     return kOk;
 }
 
+// ---------------------------------------------------------------------------
+// persistent decode-step program (csrc/decode_step.cuh)
+// ---------------------------------------------------------------------------
+constexpr uint32_t kStepSlotBytes = 40 * 1024;
+constexpr uint32_t kStepSmemMax = 227 * 1024;
+
+int eng_gemv_op(const EngProj& p, int kind, const GemvArgs& ga, long long pair_rows, int grid, uint32_t slot,
+                int n_slots, asdsl::StepOp& op, uint32_t* part_b, uint32_t* cnt_b) {
+    std::memset(&op, 0, sizeof(op));
+    op.type = asdsl::kOpGemv;
+    op.kind = kind;
+    StreamIn in[2];
+    const long long M = pair_rows > 0 ? pair_rows : p.rows;
+    const long long nb = (M + 3) / 4;
+    op.ga = ga;
+    op.ga.status = device_status_ptr();
+    if (p.fmt == ASDSL_B200_FMT_PREQ2) {
+        preq2_streams(in, p.w0, p.w1, p.rows, p.cols);
+        op.fmt = kFmtPreq2;
+        op.ga.gs = 32;
+    } else {
+        q128b_streams(in, p.w0, p.w1, p.rows, p.cols);
+        op.fmt = kFmtQ128B;
+        op.ga.gs = 128;
+    }
+    op.ga.n_tokens = 1;
+    return plan_ring_gemv(in, 2, nb, pair_rows > 0 ? nb : 0, p.cols, grid, slot, n_slots, 0, op.pa, part_b, cnt_b);
+}
+
+int eng_build_program(asdsl_b200_engine* e, bool with_lm) {
+    const asdsl_b200_engine_config& c = e->cfg;
+    const int grid = sm_count();
+    if (grid < c.num_heads) return set_error(kEinval, "engine: fewer SMs than attention heads");
+    const int H = c.hidden_size;
+    // shared memory: barriers | A8 area / attention scratch | K-split counters | partials | ring
+    const uint32_t xbytes = round_up(std::max<uint32_t>(xarea_layout_bytes(std::max(H, std::max(c.intermediate_size,
+                                                                     c.num_heads * c.head_dim)), 32, false),
+                                                        static_cast<uint32_t>(sizeof(asdsl::AttnSmem))), 128);
+    std::vector<asdsl::StepOp> ops;
+    uint32_t part_max = 0, cnt_max = 0;
+    // the ring gets what the fixed regions leave; the split regions are sized after planning,
+    // so plan with a conservative slot count first, then check the total
+    const uint32_t fixed = kBarBytes + xbytes + 8 * 1024;  // 8 KB reserve for the split regions
+    int n_slots = static_cast<int>((kStepSmemMax - 2048 - fixed) / kStepSlotBytes);
+    if (n_slots > kMaxStages) n_slots = kMaxStages;
+    if (n_slots < 2) return set_error(kEinval, "engine: no room for the decode-step ring");
+    auto add_gemv = [&](const EngProj& p, int kind, const GemvArgs& ga, long long pair_rows) -> int {
+        asdsl::StepOp op;
+        uint32_t pb = 0, cb = 0;
+        if (int rc = eng_gemv_op(p, kind, ga, pair_rows, grid, kStepSlotBytes, n_slots, op, &pb, &cb)) return rc;
+        part_max = std::max(part_max, pb);
+        cnt_max = std::max(cnt_max, cb);
+        ops.push_back(op);
+        return kOk;
+    };
+    {
+        asdsl::StepOp op;
+        std::memset(&op, 0, sizeof(op));
+        op.type = asdsl::kOpEmbed;
+        ops.push_back(op);
+    }
+    for (int l = 0; l < c.num_layers; ++l) {
+        const EngLayer& L = e->layers[l];
+        GemvArgs ga = base_args(L.p[kProjQkv].rows, H, 32);
+        ga.x = e->resid;
+        ga.norm_w = L.rms_att;
+        ga.eps = c.rms_norm_eps;
+        ga.y = e->qkv;
+        if (int rc = add_gemv(L.p[kProjQkv], asdsl::kGvStore, ga, 0)) return rc;
+        {
+            asdsl::StepOp op;
+            std::memset(&op, 0, sizeof(op));
+            op.type = asdsl::kOpAttn;
+            op.aa.qkv = e->qkv;
+            op.aa.out = e->att;
+            op.aa.kq = e->kq + l * e->kv_codes_per_layer;
+            op.aa.vq = e->vq + l * e->kv_codes_per_layer;
+            op.aa.ks = e->ks + l * e->kv_scales_per_layer;
+            op.aa.vs = e->vs + l * e->kv_scales_per_layer;
+            op.aa.cos_t = e->cos_t;
+            op.aa.sin_t = e->sin_t;
+            op.aa.st = e->st;
+            op.aa.n_heads = c.num_heads;
+            op.aa.n_kv = c.num_kv_heads;
+            op.aa.rot = c.rotary_dim;
+            op.aa.max_seq = c.max_seq_len;
+            ops.push_back(op);
+        }
+        ga = base_args(H, L.p[kProjO].cols, 32);
+        ga.x = e->att;
+        ga.resid = e->resid;
+        if (int rc = add_gemv(L.p[kProjO], asdsl::kGvResid, ga, 0)) return rc;
+        ga = base_args(c.intermediate_size, H, 32);
+        ga.x = e->resid;
+        ga.norm_w = L.rms_ffn;
+        ga.eps = c.rms_norm_eps;
+        ga.h = e->h;
+        if (int rc = add_gemv(L.p[kProjGateUp], asdsl::kGvSilu, ga, c.intermediate_size)) return rc;
+        ga = base_args(H, c.intermediate_size, 32);
+        ga.x = e->h;
+        ga.resid = e->resid;
+        if (int rc = add_gemv(L.p[kProjDown], asdsl::kGvResid, ga, 0)) return rc;
+    }
+    if (with_lm) {
+        GemvArgs ga = base_args(c.vocab_size, H, 32);
+        ga.x = e->resid;
+        ga.norm_w = e->out_norm;
+        ga.eps = c.rms_norm_eps;
+        ga.y = e->logits;
+        if (int rc = add_gemv(e->lm, asdsl::kGvArgmax, ga, 0)) return rc;
+        asdsl::StepOp op;
+        std::memset(&op, 0, sizeof(op));
+        op.type = asdsl::kOpArgmaxFinal;
+        ops.push_back(op);
+    }
+    const uint32_t cnt_off = kBarBytes + xbytes;
+    const uint32_t part_off = cnt_off + round_up(cnt_max, 128);
+    const uint32_t ring_off = round_up(part_off + part_max, 128);
+    const uint32_t smem = ring_off + static_cast<uint32_t>(n_slots) * kStepSlotBytes;
+    if (smem > kStepSmemMax - 2048) return set_error(kEinval, "engine: decode-step shared memory over budget");
+    const int idx = with_lm ? 1 : 0;
+    if (e->d_prog[idx]) {
+        cudaFree(e->d_prog[idx]);
+        e->d_prog[idx] = nullptr;
+    }
+    ASDSL_CUDA(cudaMalloc(reinterpret_cast<void**>(&e->d_prog[idx]), ops.size() * sizeof(asdsl::StepOp)));
+    ASDSL_CUDA(cudaMemcpy(e->d_prog[idx], ops.data(), ops.size() * sizeof(asdsl::StepOp), cudaMemcpyHostToDevice));
+    asdsl::StepArgs& A = e->prog_args[idx];
+    std::memset(&A, 0, sizeof(A));
+    A.ops = e->d_prog[idx];
+    A.n_ops = static_cast<int>(ops.size());
+    A.n_slots = n_slots;
+    A.slot_bytes = kStepSlotBytes;
+    A.xarea_off = kBarBytes;
+    A.cnt_off = cnt_off;
+    A.cnt_bytes = round_up(cnt_max, 128);
+    A.part_off = part_off;
+    A.ring_off = ring_off;
+    A.emb = e->embed;
+    A.emb_f16 = e->embed_f16;
+    A.resid = e->resid;
+    A.H = H;
+    A.V = c.vocab_size;
+    A.st = e->st;
+    A.seq = e->seq;
+    A.max_seq = c.max_seq_len;
+    A.decode = with_lm ? 1 : 0;
+    A.part_val = e->part_val;
+    A.part_idx = e->part_idx;
+    A.out_val = e->am_val;
+    A.out_idx = e->am_idx;
+    A.bar = e->grid_bar;
+    A.status = device_status_ptr();
+    e->prog_smem = std::max(e->prog_smem, smem);
+    return kOk;
+}
+
+int eng_launch_program(asdsl_b200_engine* e, bool with_lm) {
+    const asdsl::StepArgs& A = e->prog_args[with_lm ? 1 : 0];
+    {
+        static std::mutex mu;
+        static uint32_t configured[64] = {0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev >= 0 && dev < 64 && configured[dev] < e->prog_smem) {
+            ASDSL_CUDA(cudaFuncSetAttribute(asdsl::k_decode_step, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(e->prog_smem)));
+            configured[dev] = e->prog_smem;
+        }
+    }
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count()));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = e->prog_smem;
+    cfg.stream = e->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ASDSL_CUDA(cudaLaunchKernelEx(&cfg, asdsl::k_decode_step, A));
+    return kOk;
+}
+
 // enqueue one forward step (token seq[pos] at st->pos) on e->stream
 int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
+    if (e->persistent) return eng_launch_program(e, with_lm);
     const asdsl_b200_engine_config& c = e->cfg;
     cudaStream_t s = e->stream;
     const int H = c.hidden_size;
@@ -312,9 +508,12 @@ int eng_status(asdsl_b200_engine* e) {
     if (!sp) return set_error(kEcuda, "cannot resolve the device status word");
     ASDSL_CUDA(cudaMemcpyAsync(&e->h_stage[3], sp, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     ASDSL_CUDA(cudaStreamSynchronize(e->stream));
-    if (e->h_stage[3] != 0)
+    if (e->h_stage[3] != 0) {
+        // an aborted persistent step can leave its grid-barrier counter mid-count: re-arm it
+        if (e->grid_bar) cudaMemsetAsync(e->grid_bar, 0, 64, e->stream);
         return set_error(kEtimeout, "engine: a kernel gave up a bounded wait (device status " +
                                         std::to_string(e->h_stage[3]) + ")");
+    }
     return kOk;
 }
 
@@ -355,6 +554,7 @@ int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_eng
 
     auto* e = new asdsl_b200_engine();
     e->cfg = c;
+    if (const char* m = std::getenv("ASDSL_B200_DECODE_KERNEL")) e->persistent = (std::string(m) == "persistent") ? 1 : 0;
     if (e->cfg.lm_head_group_size <= 0) e->cfg.lm_head_group_size = c.group_size;
     cudaGetDevice(&e->device);
     int rc = kOk;
@@ -379,6 +579,8 @@ int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_eng
         (rc = eng_alloc(e, &e->seq, 4ull * (c.max_seq_len + 1))) || (rc = eng_alloc(e, &e->am_val, 16)) ||
         (rc = eng_alloc(e, &e->am_idx, 16)) ||
         (rc = eng_alloc(e, &e->am_scratch, asdsl_b200_argmax_scratch_bytes())) ||
+        (rc = eng_alloc(e, &e->grid_bar, 64)) || (rc = eng_alloc(e, &e->part_val, 4ull * 1024)) ||
+        (rc = eng_alloc(e, &e->part_idx, 4ull * 1024)) ||
         (rc = eng_alloc(e, &e->out_norm, 4ull * c.hidden_size)) ||
         (rc = eng_alloc(e, &e->cos_t, 4ull * c.max_seq_len * (c.rotary_dim / 2 > 0 ? c.rotary_dim / 2 : 1))) ||
         (rc = eng_alloc(e, &e->sin_t, 4ull * c.max_seq_len * (c.rotary_dim / 2 > 0 ? c.rotary_dim / 2 : 1))))
@@ -389,6 +591,7 @@ int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_eng
     if (cudaHostAlloc(reinterpret_cast<void**>(&e->h_stage), 16 * sizeof(int), cudaHostAllocDefault) != cudaSuccess)
         return fail(set_error(kEcuda, "engine_create: cannot allocate pinned staging"));
     if (cudaMemsetAsync(e->am_scratch, 0, asdsl_b200_argmax_scratch_bytes(), e->stream) != cudaSuccess ||
+        cudaMemsetAsync(e->grid_bar, 0, 64, e->stream) != cudaSuccess ||
         cudaMemsetAsync(e->st, 0, sizeof(asdsl::DecodeState), e->stream) != cudaSuccess ||
         cudaMemsetAsync(e->seq, 0, 4ull * (c.max_seq_len + 1), e->stream) != cudaSuccess)
         return fail(set_error(kEcuda, "engine_create: memset failed"));
@@ -405,6 +608,8 @@ int asdsl_b200_engine_destroy(asdsl_b200_engine* e) {
     if (e->g_decode) cudaGraphExecDestroy(e->g_decode);
     if (e->g_prefill) cudaGraphExecDestroy(e->g_prefill);
     for (void* p : e->allocs)
+        if (p) cudaFree(p);
+    for (auto*& p : e->d_prog)
         if (p) cudaFree(p);
     if (e->h_stage) cudaFreeHost(e->h_stage);
     if (e->stream) cudaStreamDestroy(e->stream);
@@ -591,6 +796,10 @@ int asdsl_b200_engine_finalize(asdsl_b200_engine* e) {
         eng_free(e, e->out_proj);
         e->out_proj = nullptr;
     }
+    if (e->persistent) {
+        if (int rc = eng_build_program(e, true)) return rc;
+        if (int rc = eng_build_program(e, false)) return rc;
+    }
     // one eager step of each kind (kernel attributes, module loading), then capture
     if (int rc = eng_set_pos(e, 0, 0)) return rc;
     if (int rc = eng_enqueue_step(e, true)) return rc;
@@ -689,6 +898,45 @@ int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int 
     if (int rc = eng_status(e)) return rc;
     e->kv_seq_len = std::max(e->kv_seq_len, n_prompt + max_tokens);
     *n_out = n_prompt + produced;
+    return kOk;
+}
+
+int asdsl_b200_engine_profile_step(asdsl_b200_engine* e, int decode, unsigned long long* host_trace, int max_ops,
+                                   int* n_ops) {
+    ENG_READY(e);
+    if (!host_trace || !n_ops) return set_error(kEinval, "engine_profile_step: null pointer");
+    if (!e->persistent) return set_error(kEinval, "engine_profile_step: needs the persistent decode kernel");
+    DeviceGuard dg(e->device);
+    asdsl::StepArgs A = e->prog_args[decode ? 1 : 0];
+    if (max_ops < A.n_ops) return set_error(kEinval, "engine_profile_step: trace buffer too small");
+    unsigned long long* d = nullptr;
+    ASDSL_CUDA(cudaMalloc(reinterpret_cast<void**>(&d), 3ull * A.n_ops * sizeof(unsigned long long)));
+    std::vector<unsigned long long> init(3ull * A.n_ops, 0ull);
+    for (int i = 0; i < A.n_ops; ++i) init[3 * i] = ~0ull;
+    cudaError_t ce = cudaMemcpy(d, init.data(), init.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice);
+    A.trace = d;
+    int rc = kOk;
+    if (ce != cudaSuccess) {
+        rc = set_error(kEcuda, "engine_profile_step: copy failed");
+    } else {
+        // one eager step with the trace on, at the current position
+        e->prog_args[decode ? 1 : 0].trace = d;
+        rc = eng_launch_program(e, decode != 0);
+        e->prog_args[decode ? 1 : 0].trace = nullptr;
+        if (rc == kOk && cudaStreamSynchronize(e->stream) != cudaSuccess) rc = set_error(kEcuda, "engine_profile_step: step failed");
+        if (rc == kOk && cudaMemcpy(host_trace, d, init.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = set_error(kEcuda, "engine_profile_step: copy back failed");
+    }
+    cudaFree(d);
+    *n_ops = A.n_ops;
+    if (rc == kOk) rc = eng_status(e);
+    return rc;
+}
+
+int asdsl_b200_engine_set_persistent(asdsl_b200_engine* e, int persistent) {
+    ENG_CHECK(e);
+    if (e->finalized) return set_error(kEinval, "engine_set_persistent: engine already finalized");
+    e->persistent = persistent ? 1 : 0;
     return kOk;
 }
 

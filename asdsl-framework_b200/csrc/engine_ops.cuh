@@ -74,72 +74,82 @@ struct AttnArgs {
     int n_heads, n_kv, rot, max_seq;
 };
 
-__global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
+// shared memory of one attention head
+struct AttnSmem {
+    float q[kAttnHeadDim];
+    float k[kAttnHeadDim];  // dequantized current-position k, v
+    float v[kAttnHeadDim];
+    float ks[2], vs[2];
+    float red[2][2][2];     // [k|v][64-block][warp of block]
+    float m[kAttnGroups], l[kAttnGroups];
+    float num[kAttnGroups][kAttnHeadDim];
+};
+
+// One head of the decode attention, run by kAttnWarps warps (thread ids 0..255).  `sync` is
+// the barrier of those warps; kCoherent reads qkv through L2 (it was written by other CTAs of
+// the same persistent kernel).
+template <bool kCoherent, typename Sync>
+__device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSmem& S, int tid, Sync sync) {
     constexpr int hd = kAttnHeadDim;
-    __shared__ float s_q[hd];
-    __shared__ float s_k[hd], s_v[hd];  // dequantized current-position k, v
-    __shared__ float s_ks[2], s_vs[2];
-    __shared__ float s_red[2][2][2];   // [k|v][64-block][warp of block]
-    __shared__ float s_m[kAttnGroups], s_l[kAttnGroups];
-    __shared__ float s_num[kAttnGroups][hd];
-    grid_dependency_wait();
-    grid_launch_dependents();
-    const int h = blockIdx.x;
     const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
     const int g = h / groups;
     const int half = a.rot / 2;
     const int pos = a.st->pos;
     if (pos < 0 || pos >= a.max_seq) return;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lane = tid & 31, warp = tid >> 5;
     const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
     const float* cp = a.cos_t + static_cast<long long>(pos) * half;
     const float* sp = a.sin_t + static_cast<long long>(pos) * half;
+    auto ldq = [&](const float* p) -> float {
+        if constexpr (kCoherent) return __ldcg(p);
+        else return *p;
+    };
 
     // --- RoPE on q and k: thread t < 128 owns dim t (rope_apply_inplace :768-801) ---
     float kval = 0.f, vval = 0.f;
     if (tid < hd) {
         const float* qh = a.qkv + h * hd;
         const float* kh = a.qkv + q_dim + g * hd;
-        float qv = qh[tid], kv = kh[tid];
+        float qv = ldq(qh + tid), kv = ldq(kh + tid);
         if (tid < half) {
             // o0 = fma(x_first, c, -(x_second * s))
-            qv = __fmaf_rn(qh[tid], cp[tid], -__fmul_rn(qh[tid + half], sp[tid]));
-            kv = __fmaf_rn(kh[tid], cp[tid], -__fmul_rn(kh[tid + half], sp[tid]));
+            qv = __fmaf_rn(qv, cp[tid], -__fmul_rn(ldq(qh + tid + half), sp[tid]));
+            kv = __fmaf_rn(kv, cp[tid], -__fmul_rn(ldq(kh + tid + half), sp[tid]));
         } else if (tid < 2 * half) {
             // o1 = fma(x_first, s, x_second * c)
             const int i = tid - half;
-            qv = __fmaf_rn(qh[i], sp[i], __fmul_rn(qh[tid], cp[i]));
-            kv = __fmaf_rn(kh[i], sp[i], __fmul_rn(kh[tid], cp[i]));
+            qv = __fmaf_rn(ldq(qh + i), sp[i], __fmul_rn(qv, cp[i]));
+            kv = __fmaf_rn(ldq(kh + i), sp[i], __fmul_rn(kv, cp[i]));
         }
-        s_q[tid] = qv;
+        S.q[tid] = qv;
         kval = kv;
-        vval = a.qkv[q_dim + kv_dim + g * hd + tid];
+        vval = ldq(a.qkv + q_dim + kv_dim + g * hd + tid);
     }
     // --- quantize this position's k and v per 64-dim block (set_kv_cache :872-917) ---
     // dims 0..63 are warps 0-1, dims 64..127 warps 2-3
     const float km = warp_max(fabsf(kval));
     const float vm = warp_max(fabsf(vval));
     if (tid < hd && lane == 0) {
-        s_red[0][tid >> 6][(tid >> 5) & 1] = km;
-        s_red[1][tid >> 6][(tid >> 5) & 1] = vm;
+        S.red[0][tid >> 6][(tid >> 5) & 1] = km;
+        S.red[1][tid >> 6][(tid >> 5) & 1] = vm;
     }
-    __syncthreads();
+    sync();
     if (tid < 2) {
-        const float ka = fmaxf(s_red[0][tid][0], s_red[0][tid][1]);
-        const float va = fmaxf(s_red[1][tid][0], s_red[1][tid][1]);
-        s_ks[tid] = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
-        s_vs[tid] = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
+        const float ka = fmaxf(S.red[0][tid][0], S.red[0][tid][1]);
+        const float va = fmaxf(S.red[1][tid][0], S.red[1][tid][1]);
+        S.ks[tid] = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
+        S.vs[tid] = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
     }
-    __syncthreads();
+    sync();
     if (tid < hd) {
         const int b = tid >> 6;
-        const float ksc = s_ks[b], vsc = s_vs[b];
+        const float ksc = S.ks[b], vsc = S.vs[b];
         int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
         int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
         qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
         qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
-        s_k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
-        s_v[tid] = __fmul_rn(static_cast<float>(qv), vsc);
+        S.k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
+        S.v[tid] = __fmul_rn(static_cast<float>(qv), vsc);
         if (h % groups == 0) {
             const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
             a.kq[kb + tid] = static_cast<int8_t>(qk);
@@ -151,7 +161,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
             }
         }
     }
-    __syncthreads();
+    sync();
 
     // --- scores + online softmax: an 8-lane group per position, 16 dims per lane ---
     const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));
@@ -159,7 +169,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
     const int l8 = lane & 7;                 // dims 16*l8 .. 16*l8+15 (scale block l8 >> 2)
     float qreg[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) qreg[i] = s_q[l8 * 16 + i];
+    for (int i = 0; i < 16; ++i) qreg[i] = S.q[l8 * 16 + i];
     float m = -INFINITY, l = 0.0f;
     float num[16];
 #pragma unroll
@@ -176,8 +186,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
             if (p == pos) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    dot = __fmaf_rn(qreg[i], s_k[l8 * 16 + i], dot);
-                    vdq[i] = s_v[l8 * 16 + i];
+                    dot = __fmaf_rn(qreg[i], S.k[l8 * 16 + i], dot);
+                    vdq[i] = S.v[l8 * 16 + i];
                 }
             } else {
                 const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
@@ -211,27 +221,38 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
         }
     }
     if (l8 == 0) {
-        s_m[grp] = m;
-        s_l[grp] = l;
+        S.m[grp] = m;
+        S.l[grp] = l;
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) s_num[grp][l8 * 16 + i] = num[i];
-    __syncthreads();
+    for (int i = 0; i < 16; ++i) S.num[grp][l8 * 16 + i] = num[i];
+    sync();
     // --- merge the groups in a fixed order --------------------------------------------
     if (tid < hd) {
         float M = -INFINITY;
         for (int k = 0; k < kAttnGroups; ++k)
-            if (s_l[k] > 0.0f) M = fmaxf(M, s_m[k]);
+            if (S.l[k] > 0.0f) M = fmaxf(M, S.m[k]);
         float L = 0.0f, acc = 0.0f;
         for (int k = 0; k < kAttnGroups; ++k) {
-            if (s_l[k] > 0.0f) {
-                const float sc = expf(s_m[k] - M);
-                L = __fmaf_rn(s_l[k], sc, L);
-                acc = __fmaf_rn(s_num[k][tid], sc, acc);
+            if (S.l[k] > 0.0f) {
+                const float sc = expf(S.m[k] - M);
+                L = __fmaf_rn(S.l[k], sc, L);
+                acc = __fmaf_rn(S.num[k][tid], sc, acc);
             }
         }
         a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, L));
     }
+}
+
+struct BlockSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+__global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
+    __shared__ AttnSmem S;
+    grid_dependency_wait();
+    grid_launch_dependents();
+    attention_head<false>(a, blockIdx.x, S, threadIdx.x, BlockSync());
 }
 
 // decode step done: seq[pos + 1] = argmax token, pos += 1 (seq holds max_seq + 1 entries;

@@ -232,7 +232,15 @@ __device__ __forceinline__ void consumer_sync() {
 // Quad-parallel: each thread owns 4 consecutive elements; an A8 group of gs
 // elements is gs/4 consecutive threads of one warp.
 // ---------------------------------------------------------------------------
-template <int PRO>
+// activation load: read-only path in a standalone GEMV; L2 (coherent across SMs) when the
+// activation is produced by other CTAs of the same persistent kernel
+template <bool kCoherent>
+__device__ __forceinline__ float4 load_x4(const float4* p) {
+    if constexpr (kCoherent) return __ldcg(p);
+    else return __ldg(p);
+}
+
+template <int PRO, bool kCoherent = false>
 __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
     const int K = ga.K;
     const int lane = ctid & 31;
@@ -258,16 +266,37 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
         return;
     } else {
         const int nquads = K >> 2;
+        const int gs = ga.gs;     // 32 or 128
+        const int tpg = gs >> 2;  // threads per A8 group: 8 or 32
+        // up to K = 8192 every thread's quads are loaded once, into registers: the RMSNorm sum of
+        // squares and the quantization then share one round trip to memory
+        constexpr int kRegIters = 4;
+        const bool in_regs = (PRO != kProQ8) && nquads <= kRegIters * kConsumerThreads;
+        float4 xr[kRegIters];
+        if (in_regs) {
+#pragma unroll
+            for (int k = 0; k < kRegIters; ++k) {
+                const int t = k * kConsumerThreads + ctid;
+                xr[k] = (t < nquads) ? load_x4<kCoherent>(reinterpret_cast<const float4*>(ga.x) + t)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
         float inv_rms = 1.0f;
         if constexpr (PRO == kProRmsA8) {
             // inv = 1/sqrt(sum(x^2)/n + eps)  (unified_engine.cpp:499-513)
             float ss = 0.0f;
-            for (int t = ctid; t < nquads; t += kConsumerThreads) {
-                const float4 f = __ldg(reinterpret_cast<const float4*>(ga.x) + t);
+            auto acc = [&](const float4& f) {
                 ss = __fmaf_rn(f.x, f.x, ss);
                 ss = __fmaf_rn(f.y, f.y, ss);
                 ss = __fmaf_rn(f.z, f.z, ss);
                 ss = __fmaf_rn(f.w, f.w, ss);
+            };
+            if (in_regs) {
+#pragma unroll
+                for (int k = 0; k < kRegIters; ++k) acc(xr[k]);
+            } else {
+                for (int t = ctid; t < nquads; t += kConsumerThreads)
+                    acc(load_x4<kCoherent>(reinterpret_cast<const float4*>(ga.x) + t));
             }
             ss = warp_sum(ss);
             if (lane == 0) xa.red[ctid >> 5] = ss;
@@ -277,11 +306,9 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
             for (int w = 0; w < kConsumerWarps; ++w) tot = __fadd_rn(tot, xa.red[w]);
             inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), ga.eps)));
         }
-        const int gs = ga.gs;   // 32 or 128
-        const int tpg = gs >> 2;  // threads per A8 group: 8 or 32
-#pragma unroll 2
-        for (int base = 0; base < nquads; base += kConsumerThreads) {
-            const int t = base + ctid;  // quad index (uniform trip count across the warp)
+        // one quad (4 consecutive elements) of thread t: A8 codes into the permuted x8 area and,
+        // from the lane holding a 32-slice's first quad, its scale and code sums
+        auto quad = [&](int t, const float4* preloaded) {
             const bool live = t < nquads;
             const int e0 = t * 4;
             float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -298,7 +325,8 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
                 }
             } else {
                 if (live) {
-                    const float4 f = __ldg(reinterpret_cast<const float4*>(ga.x) + t);
+                    const float4 f = preloaded ? *preloaded
+                                               : load_x4<kCoherent>(reinterpret_cast<const float4*>(ga.x) + t);
                     v[0] = f.x;
                     v[1] = f.y;
                     v[2] = f.z;
@@ -349,16 +377,26 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
                     static_cast<uint16_t>((c[1] & 0xFF) | ((c[3] & 0xFF) << 8));
             }
             // per 32-slice sums (8 quads)
-            int s = c[0] + c[1] + c[2] + c[3];
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            s += __shfl_xor_sync(0xffffffffu, s, 4);
+            int sm = c[0] + c[1] + c[2] + c[3];
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 4);
             if (live && (t & 7) == 0) {
                 const int q = e0 >> 5;
                 xa.xs[q] = scale;
-                xa.xsi[q] = s;
-                xa.xss[q] = __fmul_rn(static_cast<float>(s), scale);
+                xa.xsi[q] = sm;
+                xa.xss[q] = __fmul_rn(static_cast<float>(sm), scale);
             }
+        };
+        if (in_regs) {
+#pragma unroll
+            for (int k = 0; k < kRegIters; ++k) {
+                if (k * kConsumerThreads >= nquads) break;  // uniform across the CTA
+                quad(k * kConsumerThreads + ctid, &xr[k]);
+            }
+        } else {
+#pragma unroll 2
+            for (int base = 0; base < nquads; base += kConsumerThreads) quad(base + ctid, nullptr);
         }
         consumer_sync();
     }
@@ -599,141 +637,107 @@ __device__ __forceinline__ void argmax_take(float& bv, int& bi, float v, int i) 
 }
 
 // ---------------------------------------------------------------------------
-// the kernel
+// producer: one thread streams this CTA's units [u0, u1) of one GEMV, chunk by chunk, into
+// the ring slots that follow ring position jg (slot = position % S); jg advances past them.
+// Returns false when a wait for a free slot gave up (status bit set).
 // ---------------------------------------------------------------------------
-template <int FMT, int PRO, int EPI, int NT = 1>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
-    static_assert(NT == 1 || (EPI == kEpiStore && FMT != kFmtPacked), "multi-token: store epilogue, W4A8 formats");
+template <int NS, int NSEG>
+__device__ bool produce_chunks(const PipeArgs& pa, long long u0, long long u1, uint8_t* ring, uint32_t slot_bytes,
+                               int S, uint64_t* full, uint64_t* empty, int& jg, unsigned int* status, uint64_t pol) {
+    const int CU = pa.units_per_chunk;
+    const int n_chunks = static_cast<int>((u1 - u0 + CU - 1) / CU);
+    for (int j = 0; j < n_chunks; ++j) {
+        const int jr = jg + j;
+        const int s = jr % S;
+        const int use = jr / S;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+            atomicOr(status, kStatusWaitEmpty);
+            jg += j;
+            return false;
+        }
+        const long long cb = u0 + static_cast<long long>(j) * CU;
+        const long long ce = (cb + CU < u1) ? cb + CU : u1;
+        uint8_t* st = ring + static_cast<size_t>(s) * slot_bytes;
+        uint32_t tx = 0;
+        bool tail = false;
+#pragma unroll
+        for (int seg = 0; seg < NSEG; ++seg)
+#pragma unroll
+            for (int i = 0; i < NS; ++i) {
+                const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
+                tx += static_cast<uint32_t>(sp.a1 - sp.a0);
+                // bytes past the stream's last 16-byte boundary: plain loads by this thread
+                const long long t0 = sp.a1 > sp.start ? sp.a1 : sp.start;
+                uint8_t* region = st + seg * pa.seg_bytes + pa.s[i].region_off;
+                for (long long t = t0; t < sp.end; ++t) {
+                    region[t - sp.a0] = pa.s[i].base[t];
+                    tail = true;
+                }
+            }
+        if (tail) fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+        for (int seg = 0; seg < NSEG; ++seg)
+#pragma unroll
+            for (int i = 0; i < NS; ++i) {
+                const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
+                if (sp.a1 > sp.a0)
+                    bulk_g2s_stream(st + seg * pa.seg_bytes + pa.s[i].region_off, pa.s[i].base + sp.a0,
+                                    static_cast<uint32_t>(sp.a1 - sp.a0), &full[s], pol);
+            }
+    }
+    jg += n_chunks;
+    return true;
+}
+
+// wait for the copies of the last min(S, jg) ring positions: a CTA never exits with copies in flight
+__device__ __forceinline__ void drain_ring(uint64_t* full, int S, int jg, unsigned int* status) {
+    const int first = jg > S ? jg - S : 0;
+    for (int j = first; j < jg; ++j) {
+        if (!mbar_wait(&full[j % S], (j / S) & 1)) {
+            atomicOr(status, kStatusWaitDrain);
+            break;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// consumers: the 16 consumer warps of a CTA take every chunk of this CTA's units [u0, u1)
+// from the ring slots that follow position jg, run the band math and the epilogue, release
+// the slots, and advance jg past them.  The A8 area (xa / xad) is filled by the caller.
+// ---------------------------------------------------------------------------
+template <int FMT, int PRO, int EPI, int NT>
+__device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XArea& xa, const XAddr& xad,
+                               uint32_t xa_stride, long long u0, long long u1, uint8_t* ring, uint32_t slot_bytes,
+                               int S, uint64_t* full, uint64_t* empty, float* s_part, int* s_cnt, int& jg,
+                               float& best_v, int& best_i) {
     using T = FmtTraits<FMT>;
     constexpr int NS = T::kStreams;
     constexpr int NSEG = (EPI == kEpiSilu) ? 2 : 1;
-    constexpr bool kF32 = (PRO == kProF32);
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kMaxStages;
-    uint8_t* stages = smem + pa.stage_off;
-    const int S = pa.n_stages;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    XArea xa = xarea_layout(smem + pa.xarea_off, ga.K, ga.gs, kF32);
-
-    const long long U = pa.n_units;
-    const long long u0 = U * blockIdx.x / gridDim.x;
-    const long long u1 = U * (blockIdx.x + 1) / gridDim.x;
+    const int lane = threadIdx.x & 31;
+    const int cw = threadIdx.x >> 5;
     const int CU = pa.units_per_chunk;
     const int P = pa.k_parts;
-    const int IPU = P * NSEG;  // work items per unit
+    const int IPU = P * NSEG;
     const int n_chunks = static_cast<int>((u1 - u0 + CU - 1) / CU);
-    // split partials [stage][unit in chunk][item][row] and per-unit arrival counts
-    float* s_part = reinterpret_cast<float*>(smem + pa.split_off);
-    int* s_cnt = reinterpret_cast<int*>(s_part + S * CU * IPU * 4 * NT);
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        fence_mbar_init();
-    }
-    if (IPU > 1)
-        for (int i = threadIdx.x; i < S * CU; i += blockDim.x) s_cnt[i] = 0;
-    __syncthreads();
-    // let a dependent kernel launch now; it touches our outputs only after its own wait
-    grid_launch_dependents();
-
-    if (warp == kProducerWarp) {
-        if (lane != 0) return;
-        // weights never depend on the previous kernel: stream them before its completion
-        const uint64_t pol = l2_policy_evict_first();
-        int issued = 0;
-        for (int j = 0; j < n_chunks; ++j) {
-            const int s = j % S;
-            const int use = j / S;
-            if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
-                atomicOr(ga.status, kStatusWaitEmpty);
-                break;
-            }
-            const long long cb = u0 + static_cast<long long>(j) * CU;
-            const long long ce = (cb + CU < u1) ? cb + CU : u1;
-            uint8_t* st = stages + static_cast<size_t>(s) * pa.stage_bytes;
-            uint32_t tx = 0;
-            bool tail = false;
-#pragma unroll
-            for (int seg = 0; seg < NSEG; ++seg)
-#pragma unroll
-                for (int i = 0; i < NS; ++i) {
-                    const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
-                    tx += static_cast<uint32_t>(sp.a1 - sp.a0);
-                    // bytes past the stream's last 16-byte boundary: plain loads by this thread
-                    const long long t0 = sp.a1 > sp.start ? sp.a1 : sp.start;
-                    uint8_t* region = st + seg * pa.seg_bytes + pa.s[i].region_off;
-                    for (long long t = t0; t < sp.end; ++t) {
-                        region[t - sp.a0] = pa.s[i].base[t];
-                        tail = true;
-                    }
-                }
-            if (tail) fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&full[s], tx);
-#pragma unroll
-            for (int seg = 0; seg < NSEG; ++seg)
-#pragma unroll
-                for (int i = 0; i < NS; ++i) {
-                    const Span sp = chunk_span(pa.s[i], cb + seg * pa.pair_unit_off, ce + seg * pa.pair_unit_off);
-                    if (sp.a1 > sp.a0)
-                        bulk_g2s_stream(st + seg * pa.seg_bytes + pa.s[i].region_off, pa.s[i].base + sp.a0,
-                                        static_cast<uint32_t>(sp.a1 - sp.a0), &full[s], pol);
-                }
-            issued = j + 1;
-        }
-        // drain: never leave the CTA with copies in flight
-        const int first = issued > S ? issued - S : 0;
-        for (int j = first; j < issued; ++j) {
-            if (!mbar_wait(&full[j % S], (j / S) & 1)) {
-                atomicOr(ga.status, kStatusWaitDrain);
-                break;
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumer warps: every warp takes part of every stage ----------------
-    const int cw = warp;
-    grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
-    // multi-token: one A8 area per activation row, xa_stride bytes apart
-    const uint32_t xa_stride = (NT > 1) ? xarea_layout_bytes(ga.K, ga.gs, false) : 0u;
-    if constexpr (NT == 1) {
-        run_prologue<PRO>(ga, xa, threadIdx.x);
-    } else {
-        for (int t = 0; t < ga.n_tokens; ++t) {
-            GemvArgs gt = ga;
-            gt.x = ga.x + static_cast<size_t>(t) * ga.K;
-            run_prologue<PRO>(gt, xarea_layout(smem + pa.xarea_off + t * xa_stride, ga.K, ga.gs, false),
-                              threadIdx.x);
-        }
-    }
-
     const int K = ga.K;
     const int M = ga.M;
     const int nq = K >> 5;
     const int rot = (FMT == kFmtPreq2) ? ((lane >> 1) & 3) : ((lane >> 2) & 3);
-    XAddr xad;
-    xad.x8 = kF32 ? 0u : smem_u32(xa.x8);
-    xad.xs = kF32 ? 0u : smem_u32(xa.xs);
-    xad.xss = kF32 ? 0u : smem_u32(xa.xss);
-    xad.xsi = kF32 ? 0u : smem_u32(xa.xsi);
-    float best_v = -INFINITY;
-    int best_i = 0x7fffffff;
-
+    int item_base = jg;  // any per-CTA running offset works; the ring position varies per op
     for (int j = 0; j < n_chunks; ++j) {
-        const int s = j % S;
-        const int use = j / S;
+        const int jr = jg + j;
+        const int s = jr % S;
+        const int use = jr / S;
         if (!mbar_wait(&full[s], use & 1)) {
             if (lane == 0) atomicOr(ga.status, kStatusWaitFull);
-            break;
+            jg += n_chunks;
+            return;
         }
         const long long cb = u0 + static_cast<long long>(j) * CU;
         const long long ce = (cb + CU < u1) ? cb + CU : u1;
         const int n_units_here = static_cast<int>(ce - cb);
-        uint8_t* st = stages + static_cast<size_t>(s) * pa.stage_bytes;
+        uint8_t* st = ring + static_cast<size_t>(s) * slot_bytes;
         uint32_t ub[NSEG][NS];
 #pragma unroll
         for (int sg = 0; sg < NSEG; ++sg)
@@ -744,7 +748,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
             }
 
         const int n_items = n_units_here * IPU;
-        for (int it = cw; it < n_items; it += kConsumerWarps) {
+        // items are dealt round-robin over the whole run of chunks (not from warp 0 in every
+        // chunk), so chunks with fewer items than warps still keep every warp busy
+        const int it0 = (cw - item_base % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
+        item_base += n_items;
+        for (int it = it0; it < n_items; it += kConsumerWarps) {
             // k = it / IPU exactly (small integers), without an integer division
             const int k = (IPU == 1) ? it : __float2int_rz(__fmul_rn(static_cast<float>(it) + 0.5f, pa.inv_ipu));
             const int rem = it - k * IPU;
@@ -888,7 +896,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
                     if constexpr (EPI == kEpiStore) {
                         ga.y[row] = vrow[0];
                     } else if constexpr (EPI == kEpiResid) {
-                        ga.resid[row] = __fadd_rn(vrow[0], ga.resid[row]);
+                        // L2 read: in a persistent kernel other CTAs wrote neighbouring rows of this line
+                        ga.resid[row] = __fadd_rn(vrow[0], __ldcg(ga.resid + row));
                     } else if constexpr (EPI == kEpiSilu) {
                         ga.h[row] = ref_silu_mul(vrow[0], vrow[NSEG - 1]);
                     } else {
@@ -900,6 +909,89 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    jg += n_chunks;
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int FMT, int PRO, int EPI, int NT = 1>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
+    static_assert(NT == 1 || (EPI == kEpiStore && FMT != kFmtPacked), "multi-token: store epilogue, W4A8 formats");
+    using T = FmtTraits<FMT>;
+    constexpr int NS = T::kStreams;
+    constexpr int NSEG = (EPI == kEpiSilu) ? 2 : 1;
+    constexpr bool kF32 = (PRO == kProF32);
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxStages;
+    uint8_t* stages = smem + pa.stage_off;
+    const int S = pa.n_stages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    XArea xa = xarea_layout(smem + pa.xarea_off, ga.K, ga.gs, kF32);
+
+    const long long U = pa.n_units;
+    const long long u0 = U * blockIdx.x / gridDim.x;
+    const long long u1 = U * (blockIdx.x + 1) / gridDim.x;
+    const int CU = pa.units_per_chunk;
+    const int P = pa.k_parts;
+    const int IPU = P * NSEG;  // work items per unit
+    // split partials [stage][unit in chunk][item][row] and per-unit arrival counts
+    float* s_part = reinterpret_cast<float*>(smem + pa.split_off);
+    int* s_cnt = reinterpret_cast<int*>(s_part + S * CU * IPU * 4 * NT);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    if (IPU > 1)
+        for (int i = threadIdx.x; i < S * CU; i += blockDim.x) s_cnt[i] = 0;
+    __syncthreads();
+    // let a dependent kernel launch now; it touches our outputs only after its own wait
+    grid_launch_dependents();
+
+    if (warp == kProducerWarp) {
+        if (lane != 0) return;
+        // weights never depend on the previous kernel: stream them before its completion
+        const uint64_t pol = l2_policy_evict_first();
+        int jg = 0;
+        produce_chunks<NS, NSEG>(pa, u0, u1, stages, pa.stage_bytes, S, full, empty, jg, ga.status, pol);
+        drain_ring(full, S, jg, ga.status);
+        return;
+    }
+
+    // ---------------- consumer warps: every warp takes part of every stage ----------------
+    const int cw = warp;
+    grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
+    // multi-token: one A8 area per activation row, xa_stride bytes apart
+    const uint32_t xa_stride = (NT > 1) ? xarea_layout_bytes(ga.K, ga.gs, false) : 0u;
+    if constexpr (NT == 1) {
+        run_prologue<PRO>(ga, xa, threadIdx.x);
+    } else {
+        for (int t = 0; t < ga.n_tokens; ++t) {
+            GemvArgs gt = ga;
+            gt.x = ga.x + static_cast<size_t>(t) * ga.K;
+            run_prologue<PRO>(gt, xarea_layout(smem + pa.xarea_off + t * xa_stride, ga.K, ga.gs, false),
+                              threadIdx.x);
+        }
+    }
+
+    XAddr xad;
+    xad.x8 = kF32 ? 0u : smem_u32(xa.x8);
+    xad.xs = kF32 ? 0u : smem_u32(xa.xs);
+    xad.xss = kF32 ? 0u : smem_u32(xa.xss);
+    xad.xsi = kF32 ? 0u : smem_u32(xa.xsi);
+    float best_v = -INFINITY;
+    int best_i = 0x7fffffff;
+
+    {
+        int jg = 0;
+        consume_chunks<FMT, PRO, EPI, NT>(pa, ga, xa, xad, xa_stride, u0, u1, stages, pa.stage_bytes, S, full, empty,
+                                          s_part, s_cnt, jg, best_v, best_i);
     }
 
     if constexpr (EPI == kEpiArgmax) {

@@ -99,6 +99,63 @@ struct LaunchOpts {
     int chunk_target = ASDSL_CHUNK_KB * 1024;  // bytes per pipeline stage (all segments and streams)
 };
 
+// Plan one GEMV of a persistent multi-op kernel whose ring has n_slots fixed slots of
+// slot_bytes: the same chunking and K-split rules as launch_stream_gemv, with the chunk
+// bounded by the slot.  Returns the bytes of K-split partials and counters the op needs.
+inline int plan_ring_gemv(const StreamIn* in, int n_streams, long long n_units, long long pair_unit_off, int K,
+                          int grid, uint32_t slot_bytes, int n_slots, int row_bytes, PipeArgs& pa,
+                          uint32_t* part_bytes, uint32_t* cnt_bytes) {
+    std::memset(&pa, 0, sizeof(pa));
+    if (n_units <= 0 || n_units > 0x7fffffffLL) return set_error(kEinval, "plan_ring_gemv: bad unit count");
+    pa.n_units = static_cast<int>(n_units);
+    pa.pair_unit_off = static_cast<int>(pair_unit_off);
+    long long ub_sum = 0;
+    for (int i = 0; i < n_streams; ++i) {
+        if (!aligned16(in[i].base)) return set_error(kEinval, "weight buffers must be 16-byte aligned device pointers");
+        ub_sum += in[i].unit_bytes;
+    }
+    const int nseg = pair_unit_off > 0 ? 2 : 1;
+    const long long per_cta = (n_units + grid - 1) / grid;
+    long long cu = per_cta;
+    for (;; --cu) {
+        uint32_t seg = 0;
+        for (int i = 0; i < n_streams; ++i) seg += round_up(static_cast<uint32_t>(cu * in[i].unit_bytes + 48), 16);
+        if (static_cast<long long>(seg) * nseg <= slot_bytes || cu == 1) break;
+    }
+    int parts = 1;
+    const int nq = K / 32;
+    if (nq % 32 == 0 && cu * nseg < kConsumerWarps) {
+        const int li = nq / 32;
+        for (int d = 2; d <= 8 && d <= li; ++d) {
+            if (li % d || li / d < 2) continue;
+            parts = d;
+            if (cu * nseg * d >= kConsumerWarps) break;
+        }
+    }
+    uint32_t seg_bytes = 0;
+    for (int i = 0; i < n_streams; ++i) {
+        pa.s[i].base = static_cast<const uint8_t*>(in[i].base);
+        pa.s[i].unit_bytes = in[i].unit_bytes;
+        pa.s[i].total_bytes = in[i].total_bytes;
+        pa.s[i].region_off = seg_bytes;
+        seg_bytes += round_up(static_cast<uint32_t>(cu * in[i].unit_bytes + 48), 16);
+    }
+    if (static_cast<long long>(seg_bytes) * nseg > slot_bytes)
+        return set_error(kEinval, "plan_ring_gemv: one unit does not fit a ring slot");
+    const int ipu = parts * nseg;
+    pa.units_per_chunk = static_cast<int>(cu);
+    pa.n_stages = n_slots;
+    pa.k_parts = parts;
+    for (int p = 0; p <= parts; ++p) pa.q_bounds[p] = (nq / parts) * p;
+    pa.inv_ipu = 1.0f / static_cast<float>(ipu);
+    pa.seg_bytes = seg_bytes;
+    pa.stage_bytes = seg_bytes * nseg;
+    pa.row_bytes = row_bytes;
+    *part_bytes = ipu > 1 ? round_up(static_cast<uint32_t>(n_slots * cu * ipu * 4 * 4), 16) : 0u;
+    *cnt_bytes = ipu > 1 ? round_up(static_cast<uint32_t>(n_slots * cu * 4), 16) : 0u;
+    return kOk;
+}
+
 template <int FMT, int PRO, int EPI, int NT = 1>
 int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, long long pair_unit_off,
                        GemvArgs ga, cudaStream_t stream, const LaunchOpts& opt = LaunchOpts()) {

@@ -277,6 +277,19 @@ int asdsl_b200_engine_export_lm_head(asdsl_b200_engine* e, int* fmt, uint8_t* w0
  * setting of (pos, seq[pos] = token; token < 0 leaves seq alone), and n replays of the decode
  * (decode = 1) or prefill graph without synchronising. */
 int asdsl_b200_engine_stream(asdsl_b200_engine* e, void** stream);
+/* Decode-step implementation, chosen before finalize: persistent = 0 (default) runs the per-op
+ * kernel chain (163 kernels per token in one CUDA graph, chained by programmatic dependent
+ * launch); 1 runs each step as one cooperative kernel over a program of ops with grid barriers
+ * between them.  The environment variable ASDSL_B200_DECODE_KERNEL=persistent selects 1 at
+ * create. */
+int asdsl_b200_engine_set_persistent(asdsl_b200_engine* e, int persistent);
+/* Per-op profile of one step of the persistent decode kernel at the current position (the
+ * device-side counterpart of the reference's ASDSL_ENGINE_PROFILE per-op breakdown,
+ * unified_engine.cpp:58-95): host_trace[3*i + {0,1,2}] = earliest start of op i over all CTAs,
+ * latest end of its work, latest exit from the grid barrier after it (globaltimer ns).  The
+ * step runs eagerly and advances the position like a replay. */
+int asdsl_b200_engine_profile_step(asdsl_b200_engine* e, int decode, unsigned long long* host_trace, int max_ops,
+                                   int* n_ops);
 int asdsl_b200_engine_set_position(asdsl_b200_engine* e, int pos, int token);
 int asdsl_b200_engine_replay(asdsl_b200_engine* e, int decode, int n);
 /* Copy of an engine buffer to host memory after the engine stream drains (tests only; no reference

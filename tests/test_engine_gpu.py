@@ -249,3 +249,27 @@ def test_engine_lm_head_g128_quantizer(native, oracle, tiny):
     finally:
         eng.close()
     assert native.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("persistent", [False, True])
+def test_engine_decode_kernel_modes_agree(native, golden, persistent):
+    """The persistent decode-step kernel and the per-op kernel chain give the reference's
+    160-step trajectory, and logits within LOGIT_TOL of each other along it."""
+    from asdsl_b200.inference.synthetic import TINY, build_model
+
+    g = golden("engine_long.npz")
+    model = build_model(dict(TINY, max_seq=256), seed=7, norms_one=False)
+    eng = _engine(model, persistent=persistent)
+    other = _engine(model, persistent=not persistent)
+    try:
+        assert eng.generate([3], 160) == [int(t) for t in g["s7_tokens"]]
+        toks = [int(t) for t in g["s7_tokens"]]
+        eng.reset_session()
+        for pos in range(12):
+            a = eng.forward_token(toks[pos], pos).copy()
+            b = other.forward_token(toks[pos], pos).copy()
+            assert rel_err(a, b) < LOGIT_TOL
+    finally:
+        eng.close()
+        other.close()
+    assert native.device_status(clear=True) == 0
