@@ -144,6 +144,22 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(h16 & 0xFFFFu)));
 }
 
+// both fp16 halves of a 32-bit word (low half -> .x) in one packed conversion
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// exact float of a 4-bit code (low nibble of v) without the conversion unit
+__device__ __forceinline__ float nibble_to_float(uint32_t v) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | (v & 0xFu)), 8388608.0f);
+}
+
+// exact int -> float for |v| < 2^22 without the conversion unit: the integer is placed in the
+// mantissa of 1.5 * 2^23 and the offset subtracted (the W4A8 group dots are below 2^16)
+__device__ __forceinline__ float small_int_to_float(int v) {
+    return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
+}
+
 // A8 code of one value given inv = 127/amax: RNE, saturated like _mm_packs.
 __device__ __forceinline__ int a8_code(float x, float inv) {
     int q = __float2int_rn(__fmul_rn(x, inv));

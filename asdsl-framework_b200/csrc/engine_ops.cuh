@@ -201,8 +201,8 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
                 for (int i = 0; i < 16; ++i) {
                     const int kc = static_cast<int8_t>((kk[i >> 2] >> (8 * (i & 3))) & 0xFF);
                     const int vc = static_cast<int8_t>((vv[i >> 2] >> (8 * (i & 3))) & 0xFF);
-                    dot = __fmaf_rn(qreg[i], __fmul_rn(static_cast<float>(kc), ksc), dot);
-                    vdq[i] = __fmul_rn(static_cast<float>(vc), vsc);
+                    dot = __fmaf_rn(qreg[i], __fmul_rn(small_int_to_float(kc), ksc), dot);
+                    vdq[i] = __fmul_rn(small_int_to_float(vc), vsc);
                 }
             }
         }

@@ -479,8 +479,9 @@ __device__ __forceinline__ void slice_math(float a[4], const SliceData& d, uint3
     for (int r = 0; r < 4; ++r) {
         const int dot = dot_nib32_split(d.w[r], d.xa, d.xb);
         if constexpr (FMT == kFmtPreq2 || FMT == kFmtPreq) {
-            const float ws = half_bits_to_float(d.m[r]), wz = half_bits_to_float(d.m[r] >> 16);
-            a[r] = __fmaf_rn(static_cast<float>(dot), __fmul_rn(ws, d.xs), a[r]);
+            const float2 sz = half2_bits_to_float2(d.m[r]);  // (scale, zero)
+            const float ws = sz.x, wz = sz.y;
+            a[r] = __fmaf_rn(small_int_to_float(dot), __fmul_rn(ws, d.xs), a[r]);
             a[r] = __fmaf_rn(-__fmul_rn(wz, ws), d.xss, a[r]);
         } else if constexpr (FMT == kFmtQ4K) {
             // reference Q4_K sub-block (gemv_q4_avx2.cpp:294-329): 6-bit LE bitstream values
@@ -497,13 +498,13 @@ __device__ __forceinline__ void slice_math(float a[4], const SliceData& d, uint3
             };
             const float sub_scale = __fmul_rn(dsc, static_cast<float>(get6(sb)));
             const float sub_min = __fmul_rn(dmin, static_cast<float>(get6(sb + 8u)));
-            const float part = __fsub_rn(__fmul_rn(sub_scale, static_cast<float>(dot)),
-                                         __fmul_rn(sub_min, static_cast<float>(d.xsi)));
+            const float part = __fsub_rn(__fmul_rn(sub_scale, small_int_to_float(dot)),
+                                         __fmul_rn(sub_min, small_int_to_float(d.xsi)));
             a[r] = __fmaf_rn(part, d.xs, a[r]);
         } else {
             // symmetric formats: implicit zero 8 (Q4_128, S256)
             const float ws = half_bits_to_float(d.m[r]);
-            a[r] = __fmaf_rn(static_cast<float>(dot), __fmul_rn(ws, d.xs), a[r]);
+            a[r] = __fmaf_rn(small_int_to_float(dot), __fmul_rn(ws, d.xs), a[r]);
             a[r] = __fmaf_rn(-__fmul_rn(8.0f, ws), d.xss, a[r]);
         }
     }
@@ -585,14 +586,14 @@ __device__ __forceinline__ float unit_packed(const uint8_t* wrow, const float* s
             const uint32_t w = *reinterpret_cast<const uint32_t*>(wrow + (k >> 1));
             const float4 x0 = *reinterpret_cast<const float4*>(xa.xf + k);
             const float4 x1 = *reinterpret_cast<const float4*>(xa.xf + k + 4);
-            d = __fmaf_rn(static_cast<float>(w & 0xF), x0.x, d);
-            d = __fmaf_rn(static_cast<float>((w >> 4) & 0xF), x0.y, d);
-            d = __fmaf_rn(static_cast<float>((w >> 8) & 0xF), x0.z, d);
-            d = __fmaf_rn(static_cast<float>((w >> 12) & 0xF), x0.w, d);
-            d = __fmaf_rn(static_cast<float>((w >> 16) & 0xF), x1.x, d);
-            d = __fmaf_rn(static_cast<float>((w >> 20) & 0xF), x1.y, d);
-            d = __fmaf_rn(static_cast<float>((w >> 24) & 0xF), x1.z, d);
-            d = __fmaf_rn(static_cast<float>(w >> 28), x1.w, d);
+            d = __fmaf_rn(nibble_to_float(w), x0.x, d);
+            d = __fmaf_rn(nibble_to_float(w >> 4), x0.y, d);
+            d = __fmaf_rn(nibble_to_float(w >> 8), x0.z, d);
+            d = __fmaf_rn(nibble_to_float(w >> 12), x0.w, d);
+            d = __fmaf_rn(nibble_to_float(w >> 16), x1.x, d);
+            d = __fmaf_rn(nibble_to_float(w >> 20), x1.y, d);
+            d = __fmaf_rn(nibble_to_float(w >> 24), x1.z, d);
+            d = __fmaf_rn(nibble_to_float(w >> 28), x1.w, d);
             g = k / gs;
         }
         if (shuffle_ok) {
