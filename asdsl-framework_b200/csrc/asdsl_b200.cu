@@ -512,6 +512,57 @@ int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, c
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// self-test of the bounded waits: a wait that nothing ever completes must give up, set its
+// status bit and return, leaving the context usable
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void k_selftest_wait(int which, const unsigned long long* never_set, unsigned int* status) {
+    if (threadIdx.x != 0) return;
+    if (which == 0) {
+        // an mbarrier expecting one arrival that never comes (the streaming pipeline's wait)
+        __shared__ __align__(8) uint64_t bar;
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        if (!mbar_wait(&bar, 0)) atomicOr(status, kStatusWaitFull);
+    } else {
+        // a peer word that never arrives (the cross-GPU exchange's wait)
+        const unsigned long long t0 = globaltimer_ns();
+        while ((ld_acquire_sys_u64(never_set) >> 56) != 1ull) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(status, kStatusXchgWait);
+                break;
+            }
+        }
+    }
+}
+}  // namespace
+
+extern "C" {
+
+int asdsl_b200_selftest_bounded_wait(int which, void* stream) {
+    if (which != 0 && which != 1) return set_error(kEinval, "selftest_bounded_wait: which must be 0 or 1");
+    unsigned int* st = device_status_ptr();
+    if (!st) return set_error(kEcuda, "cannot resolve the device status word");
+    unsigned long long* flag = nullptr;
+    ASDSL_CUDA(cudaMalloc(reinterpret_cast<void**>(&flag), sizeof(unsigned long long)));
+    cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(unsigned long long), as_stream(stream));
+    if (e == cudaSuccess) {
+        k_selftest_wait<<<1, 32, 0, as_stream(stream)>>>(which, flag, st);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+    cudaFree(flag);
+    ASDSL_CUDA(e);
+    unsigned int v = 0;
+    ASDSL_CUDA(cudaMemcpy(&v, st, sizeof(v), cudaMemcpyDeviceToHost));
+    const unsigned int expect = which == 0 ? kStatusWaitFull : kStatusXchgWait;
+    if (v & expect) return set_error(kEtimeout, "selftest_bounded_wait: the wait gave up as designed");
+    return set_error(kEcuda, "selftest_bounded_wait: the wait did not report its timeout");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
 // multi-token W4A8 GEMV: one pass streams the weights once for up to 16 activation rows
 // ---------------------------------------------------------------------------
 namespace {

@@ -55,6 +55,12 @@ int asdsl_b200_set_launch_policy(int ctas_per_sm, int use_pdl);
  * set by kernels whose bounded waits gave up.  Synchronizes the device. */
 int asdsl_b200_device_status(unsigned int* status, int clear);
 
+/* Self-test of the failure detection (no reference counterpart): runs one wait that nothing
+ * ever completes -- which 0: an mbarrier of the streaming pipeline, 1: a cross-GPU exchange
+ * word -- and returns ASDSL_B200_ETIMEOUT once the 2 s limit made it give up and set its
+ * status bit (the bit stays set until asdsl_b200_device_status clears it).  Blocks ~2 s. */
+int asdsl_b200_selftest_bounded_wait(int which, void* stream);
+
 /* A8 activation quantization.
  * Replaces quantize_activation_avx2 (asdsl/kernels/native/gemv_q4_preq_restored.cpp:505-549;
  * binding asdsl/kernels/native/gemv_q4_avx2.cpp:1352-1365).
