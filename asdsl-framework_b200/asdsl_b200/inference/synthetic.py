@@ -100,3 +100,43 @@ def model_digest(model: dict) -> str:
         for k in sorted(L):
             h.update(np.ascontiguousarray(L[k]).tobytes())
     return h.hexdigest()
+
+
+def build_model_device(cfg: dict, seed: int, device="cuda", norms_one: bool = True) -> dict:
+    """The same kind of random-init model as build_model (preq2 bytes: uniform nibbles, fp16
+    scales in [0.004, 0.012) and zeros in [7, 8); fp16 N(0, 0.02) embedding), generated on the
+    GPU with torch's CUDA generator: seconds instead of minutes for the full Phi-4-mini shape, for
+    timing runs that need no host copy of the weights.  Not byte-identical to build_model."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    H, I = cfg["hidden"], cfg["inter"]
+    qd = cfg["n_heads"] * cfg["head_dim"]
+    kvd = cfg["n_kv_heads"] * cfg["head_dim"]
+
+    def preq2(rows, cols):
+        ng = cols // 32
+        s = (torch.rand((rows, ng), generator=g, device=device) * 0.008 + 0.004).half()
+        z = (torch.rand((rows, ng), generator=g, device=device) + 7.0).half()
+        meta = torch.stack([s, z], dim=2).contiguous().view(torch.uint8).reshape(-1)
+        nb = (rows + 3) // 4
+        quant = torch.randint(0, 256, (nb * ng * 64,), generator=g, device=device, dtype=torch.uint8)
+        if rows % 4:
+            quant.view(nb, ng, 64)[nb - 1, :, (rows % 4) * 16:] = 0
+        return meta, quant
+
+    layers = []
+    for _ in range(cfg["num_layers"]):
+        L = {}
+        for name, (rows, cols) in (("qkv_proj", (qd + 2 * kvd, H)), ("o_proj", (H, qd)),
+                                   ("gate_up_proj", (2 * I, H)), ("down_proj", (H, I))):
+            L[name + "_meta"], L[name + "_quant"] = preq2(rows, cols)
+        ones = torch.ones(H, dtype=torch.float32, device=device)
+        L["rms_att"] = ones if norms_one else (torch.rand(H, generator=g, device=device) * 0.4 + 0.8)
+        L["rms_ffn"] = ones if norms_one else (torch.rand(H, generator=g, device=device) * 0.4 + 0.8)
+        layers.append(L)
+    embed = (torch.randn((cfg["vocab"], H), generator=g, device=device) * 0.02).half()
+    cos, sin = rope_tables(cfg["max_seq"], cfg["rotary_dim"], cfg.get("theta", 10000.0))
+    return dict(config=dict(cfg), embed_f16=embed, output_norm=torch.ones(H, dtype=torch.float32, device=device),
+                cos=cos, sin=sin, layers=layers)

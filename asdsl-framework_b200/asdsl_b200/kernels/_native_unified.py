@@ -71,8 +71,25 @@ def _host(a, dtype=None) -> np.ndarray:
     return np.ascontiguousarray(a)
 
 
-def _ptr(a: np.ndarray) -> int:
+def _ptr(a) -> int:
+    if hasattr(a, "data_ptr"):  # torch tensor (CUDA or CPU), contiguous
+        return a.data_ptr()
     return a.ctypes.data
+
+
+def _nbytes(a) -> int:
+    return a.numel() * a.element_size() if hasattr(a, "element_size") else a.nbytes
+
+
+def _blob(a, dtype):
+    """A weight / table argument as something with a pointer: CUDA tensors are used where they
+    are (the engine copies device to device), everything else becomes a contiguous host array."""
+    if hasattr(a, "is_cuda") and a.is_cuda:
+        import torch
+
+        tdt = {np.uint8: torch.uint8, np.float32: torch.float32, np.float16: torch.float16}[np.dtype(dtype).type]
+        return a.contiguous() if a.dtype == tdt else a.to(tdt).contiguous()
+    return _host(a, dtype)
 
 
 class UnifiedEngine:
@@ -102,10 +119,20 @@ class UnifiedEngine:
     def _load(self, cfg, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict, lm_meta,
               lm_quant):
         lib, e = self._lib, self._e
-        emb = _host(token_embd)
-        if emb.dtype not in (np.float16, np.float32):
-            emb = emb.astype(np.float32)
-        if emb.size != cfg.vocab_size * cfg.hidden_size:
+        if hasattr(token_embd, "is_cuda") and token_embd.is_cuda:
+            import torch
+
+            emb = token_embd.contiguous() if token_embd.dtype in (torch.float16, torch.float32) else \
+                token_embd.float().contiguous()
+            emb_f16 = emb.dtype == torch.float16
+            emb_n = emb.numel()
+        else:
+            emb = _host(token_embd)
+            if emb.dtype not in (np.float16, np.float32):
+                emb = emb.astype(np.float32)
+            emb_f16 = emb.dtype == np.float16
+            emb_n = emb.size
+        if emb_n != cfg.vocab_size * cfg.hidden_size:
             raise ValueError("token_embd must be (vocab_size, hidden_size)")
         norm = _host(output_norm, np.float32).ravel()
         half = cfg.rotary_dim // 2
@@ -115,16 +142,25 @@ class UnifiedEngine:
             raise ValueError("output_norm must have hidden_size elements")
         if cos.size < cfg.max_seq_len * half or sin.size < cfg.max_seq_len * half:
             raise ValueError("cos/sin tables must be (max_seq_len, rotary_dim/2)")
-        _lib.check(lib.asdsl_b200_engine_set_globals(e, _ptr(emb), int(emb.dtype == np.float16), _ptr(norm),
-                                                     _ptr(cos), _ptr(sin)), "UnifiedEngine")
+        _lib.check(lib.asdsl_b200_engine_set_globals(e, _ptr(emb), int(emb_f16), _ptr(norm), _ptr(cos), _ptr(sin)),
+                   "UnifiedEngine")
         if output_proj is not None:
-            op = _host(output_proj)
-            if op.dtype not in (np.float16, np.float32):
-                op = op.astype(np.float32)
-            if op.size != cfg.vocab_size * cfg.hidden_size:
+            if output_proj is token_embd:
+                op, op_f16, op_n = emb, emb_f16, emb_n
+            elif hasattr(output_proj, "is_cuda") and output_proj.is_cuda:
+                import torch
+
+                op = output_proj.contiguous() if output_proj.dtype in (torch.float16, torch.float32) else \
+                    output_proj.float().contiguous()
+                op_f16, op_n = op.dtype == torch.float16, op.numel()
+            else:
+                op = _host(output_proj)
+                if op.dtype not in (np.float16, np.float32):
+                    op = op.astype(np.float32)
+                op_f16, op_n = op.dtype == np.float16, op.size
+            if op_n != cfg.vocab_size * cfg.hidden_size:
                 raise ValueError("output_proj must be (vocab_size, hidden_size)")
-            _lib.check(lib.asdsl_b200_engine_set_output_proj(e, _ptr(op), int(op.dtype == np.float16)),
-                       "UnifiedEngine")
+            _lib.check(lib.asdsl_b200_engine_set_output_proj(e, _ptr(op), int(op_f16)), "UnifiedEngine")
         if lm_meta is not None and lm_quant is not None:
             m = _host(lm_meta, np.uint8).ravel()
             q = _host(lm_quant, np.uint8).ravel()
@@ -132,8 +168,8 @@ class UnifiedEngine:
         use_c01, use_c03 = _env_on("ASDSL_C01"), _env_on("ASDSL_C03")
         for i in range(cfg.num_layers):
             L = layers_dict[i]
-            ra = _host(L["rms_att"], np.float32).ravel()
-            rf = _host(L["rms_ffn"], np.float32).ravel()
+            ra = _blob(L["rms_att"], np.float32).reshape(-1)
+            rf = _blob(L["rms_ffn"], np.float32).reshape(-1)
             _lib.check(lib.asdsl_b200_engine_set_layer_norms(e, i, _ptr(ra), _ptr(rf)), "UnifiedEngine")
             for w, name in enumerate(_PROJ):
                 rows, cols = self._shape(cfg, w)
@@ -145,15 +181,15 @@ class UnifiedEngine:
                                                                     None, 0), "UnifiedEngine")
                     continue
                 if f"{name}_meta" in L and f"{name}_quant" in L:
-                    m = _host(L[f"{name}_meta"], np.uint8).ravel()
-                    q = _host(L[f"{name}_quant"], np.uint8).ravel()
+                    m = _blob(L[f"{name}_meta"], np.uint8).reshape(-1)
+                    q = _blob(L[f"{name}_quant"], np.uint8).reshape(-1)
                 elif name in L:
                     m, q = repack_preq_blocks_to_preq2(_host(L[name], np.uint8).ravel(), rows, cols, 32)
                     m, q = m.ravel(), q.ravel()
                 else:
                     raise KeyError(name)
-                _lib.check(lib.asdsl_b200_engine_set_projection(e, i, w, _lib.FMT_PREQ2, _ptr(m), m.size, _ptr(q),
-                                                                q.size), "UnifiedEngine")
+                _lib.check(lib.asdsl_b200_engine_set_projection(e, i, w, _lib.FMT_PREQ2, _ptr(m), _nbytes(m), _ptr(q),
+                                                                _nbytes(q)), "UnifiedEngine")
         _lib.check(lib.asdsl_b200_engine_finalize(e), "UnifiedEngine")
 
     @staticmethod

@@ -197,7 +197,7 @@ def run_reference(args, host, bytes_per_step):
 DECODE_METRIC = "Q4 decode tokens/sec at batch 1 (Phi-4-mini shape, C0 preq2 gs32)"
 
 
-def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: bool = True) -> dict:
+def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: bool = True, world: int = 1) -> dict:
     """Tokens/s of the engine's greedy decode on the full Phi-4-mini shape (
     32 layers, all projections preq2 gs32, tied fp16 embedding quantized on the device into the
     lm_head, norms 1.0, int8 KV), random-init weights from `seed`.
@@ -213,10 +213,18 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
     from asdsl_b200.inference.synthetic import PHI4_MINI, build_model
     from asdsl_b200.kernels._native_unified import engine_from_model
 
-    model = build_model(PHI4_MINI, seed=seed, norms_one=True)
+    if world > 1:
+        # N > 1: independent replicas, one per GPU (weak scaling); weights generated on the device
+        from asdsl_b200.inference.synthetic import build_model_device
+
+        model = build_model_device(PHI4_MINI, seed=seed)
+        gate = False
+    else:
+        model = build_model(PHI4_MINI, seed=seed, norms_one=True)
     eng = engine_from_model(model)
     c = model["config"]
-    weight_bytes = sum(int(v.nbytes) for L in model["layers"] for k, v in L.items() if k.endswith(("_meta", "_quant")))
+    nbytes = lambda v: v.numel() * v.element_size() if hasattr(v, "element_size") else v.nbytes  # noqa: E731
+    weight_bytes = sum(int(nbytes(v)) for L in model["layers"] for k, v in L.items() if k.endswith(("_meta", "_quant")))
     ng = c["hidden"] // 32
     lm_bytes = c["vocab"] * ng * 4 + ((c["vocab"] + 3) // 4) * ng * 64
     try:
@@ -247,38 +255,62 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
             eng.set_position(0, prompt_token)
             eng.replay(8)
         torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            torch.cuda.synchronize()
         eng.set_position(0, prompt_token)
         e0.record(stream)
         eng.replay(steps)
         e1.record(stream)
         e1.synchronize()
         ms = e0.elapsed_time(e1)
-        tok_s = steps / (ms * 1e-3)
+        if world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        tok_s = world * steps / (ms * 1e-3)
         # e2e: the public generate() call (host prompt in, host tokens out)
         eng.reset_session()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         toks = eng.generate([prompt_token], steps)
         f1.record(stream)
         f1.synchronize()
         e2e_ms = f0.elapsed_time(f1)
+        if world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([e2e_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
         assert len(toks) == steps + 1
         assert _lib.device_status(clear=True) == 0
     finally:
         eng.close()
     bytes_per_token = weight_bytes + lm_bytes
     peak, peak_kind = _peaks()
-    achieved = bytes_per_token * tok_s / 1e9
+    achieved = bytes_per_token * tok_s / world / 1e9  # per GPU
     return {
         "metric": DECODE_METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "steps": steps,
-        "ms_per_token": round(ms / steps, 4), "higher_is_better": True,
+        "ms_per_token": round(ms / steps, 4), "higher_is_better": True, "n_gpus": world,
+        "scaling": "weak" if world > 1 else None,
+        "parallelism": f"replica x{world} (one independent batch-1 sequence per GPU)" if world > 1 else "1 GPU",
         "config": {"workload": "c3_phi4_mini_decode", "seed": seed, "layers": c["num_layers"], "vocab": c["vocab"],
-                   "prompt": [prompt_token], "weights": "random-init preq2 bytes (synthetic)",
+                   "prompt": [prompt_token],
+                   "weights": ("random-init preq2 bytes generated on the device (synthetic)" if world > 1
+                               else "random-init preq2 bytes (synthetic)"),
                    "l2": "2.4 GB of weights per token >> 126 MB L2"},
-        "roofline": {"bound": "hbm", "bytes_per_token": bytes_per_token, "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "bytes_per_token": bytes_per_token, "achieved_per_gpu": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "frac_of_8TBs": round(achieved / NOMINAL_HBM_GBS, 4)},
-        "e2e": {"value": round(steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+        "e2e": {"value": round(world * steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4, "ms_total": round(e2e_ms, 3)},
         "gpu_launches": steps * (3 + 5 * c["num_layers"]),
         "gate_logits_rel_err": gate_err,
@@ -622,8 +654,8 @@ def main():
                          f"rotating {args.copies} weight copies past the last-level cache"}
 
     decode = None
-    if world == 1 and not args.no_decode:
-        decode = decode_bench(args.decode_steps)
+    if not args.no_decode:
+        decode = decode_bench(args.decode_steps, world=world)
     lm_sharded = None if args.no_lm_head else lm_head_bench(world, rank)
 
     if rank == 0:

@@ -273,3 +273,29 @@ def test_engine_decode_kernel_modes_agree(native, golden, persistent):
         eng.close()
         other.close()
     assert native.device_status(clear=True) == 0
+
+
+def test_engine_from_device_tensors(native):
+    """Weights handed over as CUDA tensors (build_model_device, the multi-GPU bench's replicas)
+    give the same engine as the same bytes handed over from host memory."""
+    import torch
+
+    from asdsl_b200.inference.synthetic import SMALL, build_model_device
+
+    model = build_model_device(SMALL, seed=5, norms_one=False)
+    host = dict(model, embed_f16=model["embed_f16"].cpu().numpy(), output_norm=model["output_norm"].cpu().numpy(),
+                layers=[{k: v.cpu().numpy() for k, v in L.items()} for L in model["layers"]])
+    dev, ref = _engine(model), _engine(host)
+    try:
+        assert dev.generate([3], 24) == ref.generate([3], 24)
+        dev.reset_session()
+        ref.reset_session()
+        a = dev.forward_token(5, 0).copy()
+        b = ref.forward_token(5, 0).copy()
+        assert np.array_equal(a, b)
+    finally:
+        dev.close()
+        ref.close()
+    del model
+    torch.cuda.synchronize()
+    assert native.device_status(clear=True) == 0
