@@ -162,6 +162,12 @@ __device__ __forceinline__ Span chunk_span(const StreamDesc& sd, long long u_beg
     return sp;
 }
 
+// start - a0 of chunk_span for a chunk starting at unit u inside the stream (its start never
+// clamps there): the low four bits of u * unit_bytes, which 32-bit arithmetic gives exactly
+__device__ __forceinline__ uint32_t chunk_off16(const StreamDesc& sd, long long u) {
+    return (static_cast<uint32_t>(u) * static_cast<uint32_t>(sd.unit_bytes)) & 15u;
+}
+
 // ---------------------------------------------------------------------------
 // shared-memory activation area
 //   x8[K]      int8 codes, permuted per 32-slice (see x8_perm_offset)
@@ -647,10 +653,9 @@ __device__ bool produce_chunks(const PipeArgs& pa, long long u0, long long u1, u
                                int S, uint64_t* full, uint64_t* empty, int& jg, unsigned int* status, uint64_t pol) {
     const int CU = pa.units_per_chunk;
     const int n_chunks = static_cast<int>((u1 - u0 + CU - 1) / CU);
+    int s = jg % S;
+    int use = jg / S;
     for (int j = 0; j < n_chunks; ++j) {
-        const int jr = jg + j;
-        const int s = jr % S;
-        const int use = jr / S;
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
             atomicOr(status, kStatusWaitEmpty);
             jg += j;
@@ -686,6 +691,10 @@ __device__ bool produce_chunks(const PipeArgs& pa, long long u0, long long u1, u
                     bulk_g2s_stream(st + seg * pa.seg_bytes + pa.s[i].region_off, pa.s[i].base + sp.a0,
                                     static_cast<uint32_t>(sp.a1 - sp.a0), &full[s], pol);
             }
+        if (++s == S) {
+            s = 0;
+            ++use;
+        }
     }
     jg += n_chunks;
     return true;
@@ -726,27 +735,27 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
     const int nq = K >> 5;
     const int rot = (FMT == kFmtPreq2) ? ((lane >> 1) & 3) : ((lane >> 2) & 3);
     int item_base = jg;  // any per-CTA running offset works; the ring position varies per op
+    // ring slot and phase of chunk j, advanced incrementally (no division per chunk)
+    int s = jg % S;
+    int use = jg / S;
+    const uint32_t ring_s = smem_u32(ring);
     for (int j = 0; j < n_chunks; ++j) {
-        const int jr = jg + j;
-        const int s = jr % S;
-        const int use = jr / S;
         if (!mbar_wait(&full[s], use & 1)) {
             if (lane == 0) atomicOr(ga.status, kStatusWaitFull);
             jg += n_chunks;
             return;
         }
         const long long cb = u0 + static_cast<long long>(j) * CU;
-        const long long ce = (cb + CU < u1) ? cb + CU : u1;
-        const int n_units_here = static_cast<int>(ce - cb);
+        const int n_units_here = static_cast<int>(((cb + CU < u1) ? cb + CU : u1) - cb);
         uint8_t* st = ring + static_cast<size_t>(s) * slot_bytes;
+        const uint32_t st_s = ring_s + static_cast<uint32_t>(s) * slot_bytes;
         uint32_t ub[NSEG][NS];
 #pragma unroll
         for (int sg = 0; sg < NSEG; ++sg)
 #pragma unroll
-            for (int i = 0; i < NS; ++i) {
-                const Span sp = chunk_span(pa.s[i], cb + sg * pa.pair_unit_off, ce + sg * pa.pair_unit_off);
-                ub[sg][i] = smem_u32(st + sg * pa.seg_bytes + pa.s[i].region_off) + static_cast<uint32_t>(sp.start - sp.a0);
-            }
+            for (int i = 0; i < NS; ++i)
+                ub[sg][i] = st_s + sg * pa.seg_bytes + pa.s[i].region_off +
+                            chunk_off16(pa.s[i], cb + sg * pa.pair_unit_off);
 
         const int n_items = n_units_here * IPU;
         // items are dealt round-robin over the whole run of chunks (not from warp 0 in every
@@ -761,6 +770,7 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
             const int part = rem - seg * P;
             const long long unit = cb + k;
             if constexpr (FMT == kFmtPacked) {
+                const long long ce = cb + n_units_here;
                 const Span sp0 = chunk_span(pa.s[0], cb, ce);
                 const Span sp1 = chunk_span(pa.s[1], cb, ce);
                 const Span sp2 = chunk_span(pa.s[2], cb, ce);
@@ -910,6 +920,10 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == S) {
+            s = 0;
+            ++use;
+        }
     }
     jg += n_chunks;
 }
