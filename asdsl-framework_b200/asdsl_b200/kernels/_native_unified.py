@@ -114,6 +114,7 @@ class UnifiedEngine:
             self._e = None
             raise
         self._logits = np.empty(config.vocab_size, dtype=np.float32)
+        self._vocab = int(config.vocab_size)
 
     # ------------------------------------------------------------------ construction
     def _load(self, cfg, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict, lm_meta,
@@ -228,6 +229,23 @@ class UnifiedEngine:
         _lib.check(self._lib.asdsl_b200_engine_forward_token(self._e, int(token), int(pos), _ptr(self._logits),
                                                              ctypes.byref(out)), "forward_token_argmax")
         return int(out.value)
+
+    def forward_verify_serial_all_logits(self, prompt, start_pos: int) -> np.ndarray:
+        """forward_token(prompt[i], start_pos + i) for every i; float32 [len(prompt) * vocab], row i
+        the logits of step i (:2602-2611 over forward_verify_serial, unified_engine.cpp:1767-1772).
+        All steps run on the device back to back with one copy out."""
+        p = np.ascontiguousarray(np.asarray(list(prompt), dtype=np.int32))
+        out = np.empty(p.size * self._vocab, dtype=np.float32)
+        if p.size:
+            _lib.check(self._lib.asdsl_b200_engine_forward_verify(self._e, _ptr(p), int(p.size), int(start_pos),
+                                                                  _ptr(out)), "forward_verify_serial_all_logits")
+        return out
+
+    def forward_batch_all_logits(self, prompt, start_pos: int) -> np.ndarray:
+        """Speculative-verify logits (:2591-2600).  The reference's forward_verify_batch takes the
+        serial per-token path whenever preq2 weights are in use (unified_engine.cpp:1783-1787), so
+        the result equals forward_verify_serial_all_logits (forward_token numerics, lossless PLD)."""
+        return self.forward_verify_serial_all_logits(prompt, start_pos)
 
     def generate(self, prompt, max_tokens: int) -> list[int]:
         return self.generate_with_stops(prompt, max_tokens, [])

@@ -83,6 +83,10 @@ struct asdsl_b200_engine {
     int* part_idx = nullptr;
     int kv_seq_len = 0;
     std::vector<int> snapshots;
+    // verify (n tokens, all logits): device copy of the tokens and a grow-only logits block
+    int* verify_tok = nullptr;          // [max_seq]
+    float* verify_logits = nullptr;     // [verify_rows][vocab]
+    int verify_rows = 0;
 };
 
 namespace {
@@ -577,6 +581,7 @@ int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_eng
         (rc = eng_alloc(e, &e->vs, 4ull * c.num_layers * e->kv_scales_per_layer)) ||
         (rc = eng_alloc(e, &e->st, sizeof(asdsl::DecodeState))) ||
         (rc = eng_alloc(e, &e->seq, 4ull * (c.max_seq_len + 1))) || (rc = eng_alloc(e, &e->am_val, 16)) ||
+        (rc = eng_alloc(e, &e->verify_tok, 4ull * c.max_seq_len)) ||
         (rc = eng_alloc(e, &e->am_idx, 16)) ||
         (rc = eng_alloc(e, &e->am_scratch, asdsl_b200_argmax_scratch_bytes())) ||
         (rc = eng_alloc(e, &e->grid_bar, 64)) || (rc = eng_alloc(e, &e->part_val, 4ull * 1024)) ||
@@ -612,6 +617,7 @@ int asdsl_b200_engine_destroy(asdsl_b200_engine* e) {
     for (auto*& p : e->d_prog)
         if (p) cudaFree(p);
     if (e->h_stage) cudaFreeHost(e->h_stage);
+    if (e->verify_logits) cudaFree(e->verify_logits);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
     return kOk;
@@ -831,6 +837,47 @@ int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, fl
     if (int rc = eng_status(e)) return rc;  // synchronizes the stream
     if (argmax) *argmax = e->h_stage[2];
     if (pos + 1 > e->kv_seq_len) e->kv_seq_len = pos + 1;
+    return kOk;
+}
+
+// forward_verify_serial (unified_engine.cpp:1767-1772): forward_token(tokens[i], start_pos + i) for
+// i < n, logits of every step.  All n steps run back to back on the engine stream: before step
+// i + 1 the token the decode step wrote into seq[start_pos + i + 1] (its argmax) is replaced by
+// tokens[i + 1], and each step's logits go to row i of a device block copied out once.
+int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
+                                     float* out_logits) {
+    ENG_READY(e);
+    if (n <= 0) return kOk;
+    if (!tokens || !out_logits) return set_error(kEinval, "forward_verify: null pointer");
+    const asdsl_b200_engine_config& c = e->cfg;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= c.vocab_size)
+            return set_error(kErange, "forward_token: token_id out of vocab range");
+    if (start_pos < 0 || start_pos >= c.max_seq_len || n > c.max_seq_len - start_pos)
+        return set_error(kErange, "forward_token: pos out of kv-cache range");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    const size_t row = 4ull * c.vocab_size;
+    if (e->verify_rows < n) {
+        if (e->verify_logits) cudaFree(e->verify_logits);
+        e->verify_logits = nullptr;
+        e->verify_rows = 0;
+        ASDSL_CUDA(cudaMalloc(&e->verify_logits, row * n));
+        e->verify_rows = n;
+    }
+    ASDSL_CUDA(cudaMemcpyAsync(e->verify_tok, tokens, 4ull * n, cudaMemcpyHostToDevice, e->stream));
+    if (int rc = eng_set_pos(e, start_pos, tokens[0])) return rc;
+    for (int i = 0; i < n; ++i) {
+        if (i > 0)
+            ASDSL_CUDA(cudaMemcpyAsync(e->seq + start_pos + i, e->verify_tok + i, 4, cudaMemcpyDeviceToDevice,
+                                       e->stream));
+        ASDSL_CUDA(cudaGraphLaunch(e->g_decode, e->stream));
+        ASDSL_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(e->verify_logits) + row * i, e->logits, row,
+                                   cudaMemcpyDeviceToDevice, e->stream));
+    }
+    ASDSL_CUDA(cudaMemcpyAsync(out_logits, e->verify_logits, row * n, cudaMemcpyDefault, e->stream));
+    if (int rc = eng_status(e)) return rc;  // synchronizes the stream
+    if (start_pos + n > e->kv_seq_len) e->kv_seq_len = start_pos + n;
     return kOk;
 }
 

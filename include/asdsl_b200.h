@@ -265,6 +265,13 @@ int asdsl_b200_engine_finalize(asdsl_b200_engine* e);
  * and / or argmax may be NULL; both NULL = forward_token_prefill (no lm_head).
  * token / pos out of range -> ASDSL_B200_ERANGE. */
 int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, float* logits, int32_t* argmax);
+/* forward_verify_serial (unified_engine.cpp:1767-1772; pybind forward_verify_serial_all_logits
+ * :2602-2611, and forward_batch_all_logits :2591-2600, which takes the serial path under preq2,
+ * :1774-1789): forward_token(tokens[i], start_pos + i) for i < n; out_logits (host or device) receives
+ * n x vocab floats, row i = the logits of step i.  n <= 0 is a no-op; a token or position out of range
+ * -> ASDSL_B200_ERANGE before any step runs. */
+int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
+                                     float* out_logits);
 /* generate / generate_with_stops (unified_engine.cpp:1717-1764): out = prompt + generated tokens
  * (the stop token included), *n_out its length; out_cap >= n_prompt + max_tokens + 1. */
 int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int n_prompt, int max_tokens,

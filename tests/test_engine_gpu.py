@@ -299,3 +299,44 @@ def test_engine_from_device_tensors(native):
     del model
     torch.cuda.synchronize()
     assert native.device_status(clear=True) == 0
+
+
+def test_engine_verify_all_logits(native, tiny):
+    """forward_verify_serial_all_logits / forward_batch_all_logits (the PLD verify call,
+    unified_bridge.py:455-470): row i equals forward_token(tokens[i], start + i) bit for bit, the KV
+    cache ends as after those calls, and a snapshot / restore around it leaves the session as it was."""
+    g, model = tiny
+    c = model["config"]
+    V = c["vocab"]
+    eng = _engine(model)
+    try:
+        eng.generate([5, 8], 6)
+        start = eng.get_kv_seq_len()  # the next position to forward
+        draft = [11, 17, 3, 250, 9]
+        eng.snapshot_kv()
+        rows = eng.forward_verify_serial_all_logits(draft, start).reshape(len(draft), V)
+        assert eng.get_kv_seq_len() == start + len(draft)
+        eng.restore_kv()
+        assert eng.get_kv_seq_len() == start
+        batch = eng.forward_batch_all_logits(draft, start).reshape(len(draft), V)
+        assert np.array_equal(rows, batch)
+        # the same steps one by one
+        eng.truncate_kv(start)
+        for i, t in enumerate(draft):
+            assert np.array_equal(eng.forward_token(t, start + i), rows[i])
+        # PLD accept/commit flow: verify, restore, truncate, re-forward the accepted tokens
+        eng.truncate_kv(start)
+        eng.snapshot_kv()
+        v2 = eng.forward_batch_all_logits(draft[:3], start).reshape(3, V)
+        eng.restore_kv()
+        assert np.array_equal(v2, rows[:3])
+        assert eng.forward_verify_serial_all_logits([], start).size == 0
+        with pytest.raises(IndexError):
+            eng.forward_batch_all_logits([1, V], start)
+        with pytest.raises(IndexError):
+            eng.forward_batch_all_logits([1, 2, 3], c["max_seq"] - 2)
+        # a rejected call forwarded nothing
+        assert eng.get_kv_seq_len() == start
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0
