@@ -50,6 +50,10 @@ _SIGS = {
     "asdsl_b200_matmul_batch_q4": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "asdsl_b200_argmax_scratch_bytes": [],
     "asdsl_b200_relayout_q4_128": [_P, _P, _P, _I, _I, _P],
+    "asdsl_b200_quantize_weights": [_P, ctypes.c_longlong, _I, _I, _I, _I, _P, _P, _P, _P],
+    "asdsl_b200_repack_preq2": [_P, _P, _P, _I, _I, _P, _P, _P],
+    "asdsl_b200_repack_q4_128_f32": [_P, _I, _I, _P, _P],
+    "asdsl_b200_requant_q4_128": [_P, _P, _P, _I, _I, _P, _P],
     "asdsl_b200_gemv_q4_128_banded": [_P, _P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_argmax": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P],
     "asdsl_b200_gemv_argmax_static": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],

@@ -102,11 +102,15 @@ def model_digest(model: dict) -> str:
     return h.hexdigest()
 
 
-def build_model_device(cfg: dict, seed: int, device="cuda", norms_one: bool = True) -> dict:
+def build_model_device(cfg: dict, seed: int, device="cuda", norms_one: bool = True, quantized: bool = False) -> dict:
     """The same kind of random-init model as build_model (preq2 bytes: uniform nibbles, fp16
     scales in [0.004, 0.012) and zeros in [7, 8); fp16 N(0, 0.02) embedding), generated on the
     GPU with torch's CUDA generator: seconds instead of minutes for the full Phi-4-mini shape, for
-    timing runs that need no host copy of the weights.  Not byte-identical to build_model."""
+    timing runs that need no host copy of the weights.  Not byte-identical to build_model.
+
+    quantized=True draws every projection as float32 N(0, 0.02) and runs the reference's C0 weight
+    pipeline on it (quantize_weights gs 32 asymmetric with the clip search -> preq -> preq2,
+    asdsl_b200.quantization.device): the bytes config 3 prescribes, from the device RNG."""
     import torch
 
     g = torch.Generator(device=device)
@@ -116,6 +120,13 @@ def build_model_device(cfg: dict, seed: int, device="cuda", norms_one: bool = Tr
     kvd = cfg["n_kv_heads"] * cfg["head_dim"]
 
     def preq2(rows, cols):
+        if quantized:
+            from asdsl_b200.quantization.device import prepare_preq2_device
+
+            w = torch.randn((rows, cols), generator=g, device=device) * 0.02
+            meta, quant = prepare_preq2_device(w)
+            del w
+            return meta, quant
         ng = cols // 32
         s = (torch.rand((rows, ng), generator=g, device=device) * 0.008 + 0.004).half()
         z = (torch.rand((rows, ng), generator=g, device=device) + 7.0).half()
@@ -140,3 +151,13 @@ def build_model_device(cfg: dict, seed: int, device="cuda", norms_one: bool = Tr
     cos, sin = rope_tables(cfg["max_seq"], cfg["rotary_dim"], cfg.get("theta", 10000.0))
     return dict(config=dict(cfg), embed_f16=embed, output_norm=torch.ones(H, dtype=torch.float32, device=device),
                 cos=cos, sin=sin, layers=layers)
+
+
+def model_to_host(model: dict) -> dict:
+    """A copy of a build_model_device model with every tensor as a host numpy array (for the CPU
+    oracle engine)."""
+    def h(v):
+        return v.cpu().numpy() if hasattr(v, "cpu") else v
+
+    return dict(config=dict(model["config"]), embed_f16=h(model["embed_f16"]), output_norm=h(model["output_norm"]),
+                cos=model["cos"], sin=model["sin"], layers=[{k: h(v) for k, v in L.items()} for L in model["layers"]])

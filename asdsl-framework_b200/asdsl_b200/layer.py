@@ -139,6 +139,29 @@ def build_c1_host(seed: int = 1, cfg: dict = C1) -> dict:
     return out
 
 
+def build_c1_device(seed: int = 1, cfg: dict = C1) -> dict:
+    """build_c1_host's bytes with the quantizer and repackers run on the GPU
+    (asdsl_b200.quantization.device): the same seeded float32 draws on the host, then
+    quantize / preq2 / C0.1 requant as device kernels; the dict holds host numpy arrays."""
+    from asdsl_b200.quantization import device
+
+    rng = np.random.default_rng(seed)
+    H, QKV, QD, I = cfg["hidden"], cfg["qkv_rows"], cfg["q_dim"], cfg["inter"]
+    out = {}
+    for name, (rows, cols) in (("qkv", (QKV, H)), ("o", (H, QD))):
+        w = torch.from_numpy((rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)).cuda()
+        meta, quant = device.prepare_preq2_device(w)
+        out[name + "_meta"] = meta.cpu().numpy().reshape(rows, (cols // 32) * 4)
+        out[name + "_quant"] = quant.cpu().numpy().reshape((rows + 3) // 4, cols // 32, 64)
+    for name, (rows, cols) in (("gate_up", (2 * I, H)), ("down", (H, I))):
+        w = torch.from_numpy((rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)).cuda()
+        qt = device.quantize_weights_device(w, 4, 32, symmetric=False, optimize_clips=True)
+        out[name + "_q4_128"] = device.requant_q4_128_device(qt, rows, cols).cpu().numpy()
+    out["x"] = rng.standard_normal(H).astype(np.float32)
+    out["cfg"] = dict(cfg)
+    return out
+
+
 def from_host(host: dict) -> LayerProjections:
     c = host["cfg"]
     return LayerProjections(host["qkv_meta"], host["qkv_quant"], host["o_meta"], host["o_quant"],

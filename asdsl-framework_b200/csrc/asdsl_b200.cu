@@ -6,6 +6,7 @@
 #include "../../include/asdsl_b200.h"
 
 #include "launch.cuh"
+#include "weight_prep.cuh"
 
 using namespace asdsl;
 
@@ -726,6 +727,89 @@ int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const 
         return launch_stream_gemv<kFmtQ128B, kProA8, kEpiSilu>(s, 2, nb, nb, ga, as_stream(stream));
     }
     return set_error(kEinval, "gateup_silu: unsupported weight format");
+}
+
+// ---------------------------------------------------------------------------
+// device-side weight preparation (weight_prep.cuh)
+// ---------------------------------------------------------------------------
+namespace {
+inline bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+inline unsigned grid_for(long long items, int threads) { return static_cast<unsigned>((items + threads - 1) / threads); }
+}  // namespace
+
+int asdsl_b200_quantize_weights(const float* w, long long numel, int bits, int group_size, int symmetric,
+                                int optimize_clips, uint8_t* packed, uint16_t* scales, uint16_t* zeros, void* stream) {
+    if (bits != 4) return set_error(kEinval, "quantize_weights: unsupported bit-width " + std::to_string(bits));
+    if (group_size != 32 && group_size != 64 && group_size != 128)
+        return set_error(kEinval, "quantize_weights: group_size must be 32, 64 or 128");
+    if (numel <= 0) return set_error(kEinval, "quantize_weights: empty tensor");
+    if (!w || !packed || !scales || (!symmetric && !zeros)) return set_error(kEinval, "quantize_weights: null pointer");
+    if (!aligned_to(w, 4) || !aligned_to(packed, 4) || !aligned_to(scales, 2) || (zeros && !aligned_to(zeros, 2)))
+        return set_error(kEinval, "quantize_weights: misaligned buffer");
+    const long long n_groups = (numel + group_size - 1) / group_size;
+    if (n_groups > (1ll << 36)) return set_error(kEinval, "quantize_weights: tensor too large");
+    constexpr int kThr = 128;
+    const unsigned grid = grid_for(n_groups, kThr);
+    cudaStream_t st = as_stream(stream);
+    auto go = [&](auto kern) {
+        kern<<<grid, kThr, 0, st>>>(w, numel, n_groups, packed, scales, symmetric ? nullptr : zeros);
+    };
+    const bool sym = symmetric != 0, opt = optimize_clips != 0;
+    switch (group_size) {
+        case 32:
+            sym ? (opt ? go(k_quantize_groups<32, true, true>) : go(k_quantize_groups<32, true, false>))
+                : (opt ? go(k_quantize_groups<32, false, true>) : go(k_quantize_groups<32, false, false>));
+            break;
+        case 64:
+            sym ? (opt ? go(k_quantize_groups<64, true, true>) : go(k_quantize_groups<64, true, false>))
+                : (opt ? go(k_quantize_groups<64, false, true>) : go(k_quantize_groups<64, false, false>));
+            break;
+        default:
+            sym ? (opt ? go(k_quantize_groups<128, true, true>) : go(k_quantize_groups<128, true, false>))
+                : (opt ? go(k_quantize_groups<128, false, true>) : go(k_quantize_groups<128, false, false>));
+            break;
+    }
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_repack_preq2(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros, int rows, int cols,
+                            uint8_t* meta, uint8_t* quant, void* stream) {
+    if (!packed || !scales || !meta || !quant) return set_error(kEinval, "repack_preq2: null pointer");
+    if (int rc = check_k(cols, 32, "repack_preq2")) return rc;
+    if (rows <= 0) return set_error(kEinval, "repack_preq2: invalid dimensions");
+    if (!aligned_to(packed, 16) || !aligned_to(quant, 16) || !aligned_to(meta, 4) || !aligned_to(scales, 2) ||
+        (zeros && !aligned_to(zeros, 2)))
+        return set_error(kEinval, "repack_preq2: misaligned buffer");
+    const long long work = (static_cast<long long>(rows) + 3) / 4 * 4 * (cols / 32);
+    k_pack_preq2<<<grid_for(work, 256), 256, 0, as_stream(stream)>>>(packed, scales, zeros, rows, cols, meta, quant);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_repack_q4_128_f32(const float* w, int rows, int cols, uint8_t* blocks, void* stream) {
+    if (!w || !blocks) return set_error(kEinval, "repack_q4_128: null pointer");
+    if (int rc = check_k128(cols, "repack_q4_128")) return rc;
+    if (rows <= 0) return set_error(kEinval, "repack_q4_128: invalid dimensions");
+    if (!aligned_to(w, 4) || !aligned_to(blocks, 2)) return set_error(kEinval, "repack_q4_128: misaligned buffer");
+    const long long work = static_cast<long long>(rows) * (cols / 128);
+    k_q4_128_from_f32<<<grid_for(work, 128), 128, 0, as_stream(stream)>>>(w, rows, cols, blocks);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_requant_q4_128(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros, int rows, int cols,
+                              uint8_t* blocks, void* stream) {
+    if (!packed || !scales || !blocks) return set_error(kEinval, "requant_q4_128: null pointer");
+    if (int rc = check_k128(cols, "requant_q4_128")) return rc;
+    if (rows <= 0) return set_error(kEinval, "requant_q4_128: invalid dimensions");
+    if (!aligned_to(scales, 2) || (zeros && !aligned_to(zeros, 2)) || !aligned_to(blocks, 2))
+        return set_error(kEinval, "requant_q4_128: misaligned buffer");
+    const long long work = static_cast<long long>(rows) * (cols / 128);
+    k_q4_128_from_quant<<<grid_for(work, 128), 128, 0, as_stream(stream)>>>(packed, scales, zeros, rows, cols,
+                                                                            blocks);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
 }
 
 }  // extern "C"

@@ -130,6 +130,27 @@ int asdsl_b200_matmul_batch_q4(const uint8_t* w_packed, const float* scales, con
                                const float* X_batch, float* Y_batch, int M, int K, int B, int group_size,
                                void* stream);
 
+/* ---- device-side weight preparation (byte-exact with the reference's NumPy pipeline) ---- */
+/* quantize_weights(w, bits=4, group_size, symmetric, optimize_clips) (asdsl/quantization/core.py:358-424,
+ * clip search :291-355): w fp32 [numel] on the device, padded with zeros to a multiple of group_size
+ * (32, 64 or 128); packed = ceil(numel/gs)*gs/2 bytes (low nibble = even element, :555-561), scales
+ * (and zeros unless symmetric, then NULL) = ceil(numel/gs) fp16 values.  bits != 4 -> EINVAL. */
+int asdsl_b200_quantize_weights(const float* w, long long numel, int bits, int group_size, int symmetric,
+                                int optimize_clips, uint8_t* packed, uint16_t* scales, uint16_t* zeros, void* stream);
+/* gs-32 quantize_weights output -> preq2 meta + quant, i.e. repack_asymmetric_to_q4_32_blocks
+ * (repack_q4_32.py:63-102; bias = -zero*scale, or -7.5*scale when zeros is NULL) followed by
+ * repack_preq_blocks_to_preq2 (repack_preq2.py:22-46).  meta rows*cols/32*4 bytes, quant
+ * ceil(rows/4)*(cols/32)*64 bytes (16-byte aligned), rows past `rows` in the last band zero. */
+int asdsl_b200_repack_preq2(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros, int rows, int cols,
+                            uint8_t* meta, uint8_t* quant, void* stream);
+/* repack_fp32_to_q4_128_blocks (repack_q4_128.py:22-31, :72-92): fp32 [rows][cols] -> Q4_128 blocks
+ * [rows][cols/128][66]. */
+int asdsl_b200_repack_q4_128_f32(const float* w, int rows, int cols, uint8_t* blocks, void* stream);
+/* The C0.1 requant (build_c01_gs128_blocks, experiments/phi4_cpu_run.py:3482-3517): a gs-32
+ * quantize_weights output dequantized as q*scale + bias in float32 (:3432-3448), then Q4_128 blocks. */
+int asdsl_b200_requant_q4_128(const uint8_t* packed, const uint16_t* scales, const uint16_t* zeros, int rows, int cols,
+                              uint8_t* blocks, void* stream);
+
 /* Re-lay Q4_128 blocks (repack_q4_128.py:34-92) into the banded device layout: pure byte moves,
  * bit-exact; rows past M in the last band are zero.  quant: ceil(M/4)*(K/128)*256 bytes,
  * scales: ceil(M/4)*(K/128)*8 bytes.  Device-side counterpart of the reference's per-format
