@@ -320,6 +320,116 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
 # ---------------------------------------------------------------------------
 # config 2: lm_head 200064x3072 Q4_128, row-sharded over the ranks, fused argmax + all-gather
 # ---------------------------------------------------------------------------
+C0_METRIC = "W4 GEMV HBM GB/s (config 0: preq2 gs32 16384x3072, batch 1)"
+
+
+def c0_bench(world: int, rank: int, steps: int = 320) -> dict:
+    """Config 0: one preq2 gs-32 GEMV, 16384 x 3072.  W ~ N(0, 0.02) from default_rng(0), then
+    x ~ N(0, 1) from the same generator; W goes through the reference's quantizer pipeline
+    (quantize_weights gs 32 asymmetric + clip search -> preq -> preq2), run on the device.
+    value: back-to-back launches in CUDA graphs over weight copies rotated past the L2 (inputs
+    resident); e2e: the same call with the activation copied in from pinned host memory and y
+    copied out, every step.  At N > 1 every rank runs its own copy (replicas, weak scaling)."""
+    import numpy as np
+    import torch
+
+    from asdsl_b200 import _lib
+    from asdsl_b200.quantization.device import prepare_preq2_device
+
+    M, K = 16384, 3072
+    rng = np.random.default_rng(0)
+    w = torch.from_numpy((rng.standard_normal((M, K)) * 0.02).astype(np.float32)).cuda()
+    meta, quant = prepare_preq2_device(w)
+    del w
+    x = rng.standard_normal(K).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(M, dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    lib = _lib.load()
+
+    def run(c):
+        _lib.check(lib.asdsl_b200_gemv_preq2_fused(c[0].data_ptr(), c[1].data_ptr(), xd.data_ptr(), yd.data_ptr(),
+                                                   M, K, 32, s.cuda_stream), "gemv_preq2_fused")
+
+    # reuse distance of a copy > 300 MB (well past the 126 MB L2, so no launch finds its weights there)
+    n_copies = max(2, -(-320_000_000 // (meta.numel() + quant.numel())))
+    copies = [(meta, quant)] + [(meta.clone(), quant.clone()) for _ in range(n_copies - 1)]
+    with torch.cuda.stream(s):
+        run(copies[0])
+    s.synchronize()
+    err = None
+    if rank == 0:
+        from oracle.oracle import Oracle, build as build_oracle, rel_err
+
+        if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+            build_oracle()
+        ref = Oracle().gemv_preq2_fused(meta.cpu().numpy(), quant.cpu().numpy(), x, M, K)
+        err = float(rel_err(yd.cpu().numpy(), ref))
+        if err > 1e-3:
+            raise SystemExit(f"bench: config-0 GEMV mismatch vs oracle ({err})")
+    n = 16
+    with torch.cuda.stream(s):
+        for c in copies:
+            run(c)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(n):
+            run(copies[i % len(copies)])
+    reps = max(steps // n, 3)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(reps):
+            g.replay()
+    e1.record(s)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n)
+    # e2e: pinned x in, y out, every call
+    hx = torch.from_numpy(x).pin_memory()
+    hy = torch.empty(M, dtype=torch.float32).pin_memory()
+    n_e2e = 100
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(s)
+    with torch.cuda.stream(s):
+        for i in range(n_e2e):
+            xd.copy_(hx, non_blocking=True)
+            run(copies[i % len(copies)])
+            hy.copy_(yd, non_blocking=True)
+    f1.record(s)
+    f1.synchronize()
+    e2e_us = f0.elapsed_time(f1) * 1e3 / n_e2e
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([us, e2e_us], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us, e2e_us = float(t[0].item()), float(t[1].item())
+    assert _lib.device_status(clear=True) == 0
+    algo = M * (K // 32) * 20 + 4 * K + 4 * M  # packed weights + x + y
+    peak, peak_kind = _peaks()
+    per_gpu = algo / (us * 1e-6) / 1e9
+    return {"metric": C0_METRIC, "value": round(world * per_gpu, 1), "unit": "GB/s", "us_per_launch": round(us, 3),
+            "n_gpus": world, "scaling": "weak" if world > 1 else None, "launches": reps * n,
+            "config": {"workload": "c0_preq2_gemv", "seed": 0, "M": M, "K": K,
+                       "weights": "N(0, 0.02) from default_rng(0), reference quantizer pipeline run on the device",
+                       "l2": f"{len(copies)} rotated weight copies ({len(copies) * algo / 1e6:.0f} MB > 126 MB L2)"},
+            "roofline": {"bound": "hbm", "bytes_per_launch": algo, "achieved_per_gpu": round(per_gpu, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(per_gpu / peak, 4),
+                         "frac_of_8TBs": round(per_gpu / NOMINAL_HBM_GBS, 4), "traffic": _traffic("stream_gemv_c0")},
+            "e2e": {"value": round(world * algo / (e2e_us * 1e-6) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": 4 * K, "d2h_bytes_per_step": 4 * M, "us_per_step": round(e2e_us, 3)},
+            "check": {"rel_err_vs_oracle": err}}
+
+
 LM_METRIC = "lm_head W4 GEMV + argmax HBM GB/s (200064x3072 Q4_128, row-sharded, all ranks)"
 
 
@@ -327,7 +437,8 @@ def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dic
     """Strong scaling: the whole 200064-row lm_head is split over the ranks; a step is the local
     fused GEMV + argmax, the all-gather of one (max, index) pair per rank (NCCL) and the device
     pick of the first maximum.  value = all ranks' weight bytes / max-over-ranks step time.
-    Each rank rotates enough weight copies to stream > 126 MB (L2) per cycle."""
+    Each rank rotates enough weight copies that a copy is reused only after > 300 MB (the L2 is
+    126 MB)."""
     import numpy as np
     import torch
 
@@ -341,7 +452,7 @@ def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dic
     x = rng.standard_normal(H).astype(np.float32)
     heads = [ShardedLMHead(blocks, V, H)]
     shard_bytes = heads[0].quant.numel() + heads[0].scales.numel()
-    n_copies = max(1, -(-160_000_000 // shard_bytes))
+    n_copies = max(1, -(-320_000_000 // shard_bytes))  # reuse distance > 300 MB, well past the L2
     for _ in range(n_copies - 1):
         heads.append(ShardedLMHead(blocks, V, H))
     xd = torch.from_numpy(x).cuda()
@@ -435,11 +546,14 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--copies", type=int, default=4, help="weight copies rotated to defeat L2 (> 126 MB total)")
+    ap.add_argument("--copies", type=int, default=6,
+                    help="weight copies rotated so no launch finds its weights in the 126 MB L2 (reuse distance 273 MB)")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--no-lm-head", action="store_true", help="skip the config-2 sharded lm_head measurement")
+    ap.add_argument("--no-c0", action="store_true", help="skip the config-0 single-GEMV measurement")
+    ap.add_argument("--only-c0", action="store_true", help="run only the config-0 section (profiling)")
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--clock-preroll", type=float, default=1.5,
                     help="seconds of untimed replays inside the clock-sampling window before timing")
@@ -491,6 +605,16 @@ def main():
         dist.barrier()
     _lib.load()
 
+    if args.only_c0:
+        # profiling aid: the config-0 section alone
+        out = c0_bench(world, rank)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
     # the config-1 weights through the reference's quantizer pipeline, run on the device
     # (byte-identical to the host restatement build_c1_host, ~20x faster)
     host = build_c1_device(1)
@@ -518,20 +642,29 @@ def main():
     if err > 1e-3:
         raise SystemExit(f"bench: GPU result mismatch vs oracle ({err})")
 
-    # one CUDA graph per weight copy; replay round-robin
-    graphs = []
+    # one CUDA graph holds one step per weight copy (consecutive layer steps, as a decode graph
+    # chains its layers); exactly `steps` steps are timed: full graphs, then a graph of the rest
     for L in layers:
         with torch.cuda.stream(stream):
             L.step(x)  # warm + set kernel attributes before capture
         stream.synchronize()
+
+    def capture(n_steps):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            L.step(x)
-        graphs.append(g)
+            for j in range(n_steps):
+                layers[j % len(layers)].step(x)
+        return g
+
+    per_graph_steps = len(layers)
+    g_full = capture(per_graph_steps)
+    n_full, n_rest = divmod(args.steps, per_graph_steps)
+    g_rest = capture(n_rest) if n_rest else None
+    graphs = [g_full] + ([g_rest] if g_rest is not None else [])
     launches_per_step = 4
 
-    for i in range(args.warmup):
-        graphs[i % len(graphs)].replay()
+    for _ in range(max(1, -(-args.warmup // per_graph_steps))):
+        g_full.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -540,12 +673,10 @@ def main():
     with ClockSampler(dev_index) as clk:
         # untimed pre-roll so the clock samples (every 200 ms) see the GPU under this load
         t_end = time.perf_counter() + args.clock_preroll
-        i = 0
         while time.perf_counter() < t_end:
             with torch.cuda.stream(stream):
-                for _ in range(256):
-                    graphs[i % len(graphs)].replay()
-                    i += 1
+                for _ in range(48):
+                    g_full.replay()
             stream.synchronize()
         if world > 1:
             dist.barrier()
@@ -554,8 +685,10 @@ def main():
             dist.barrier()
         ev0.record(stream)
         with torch.cuda.stream(stream):
-            for i in range(args.steps):
-                graphs[i % len(graphs)].replay()
+            for _ in range(n_full):
+                g_full.replay()
+            if g_rest is not None:
+                g_rest.replay()
         ev1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -607,6 +740,7 @@ def main():
                 fn(layers[i % len(layers)])
         for _ in range(3):
             g.replay()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 25
         e0.record(stream)
@@ -655,6 +789,7 @@ def main():
                "sample": f"{n} full config-1 layer steps ({dt:.1f} s) on the host cores, OpenMP threads = cores, "
                          f"rotating {args.copies} weight copies past the last-level cache"}
 
+    c0 = None if args.no_c0 else c0_bench(world, rank)
     decode = None
     if not args.no_decode:
         decode = decode_bench(args.decode_steps, world=world)
@@ -677,6 +812,7 @@ def main():
             "data": "synthetic",
             "config": {"workload": "c1_layer_projection_set", "seed": 1, "global_batch": 1,
                        "bytes_per_step": bytes_per_step, "weight_copies_rotated": len(layers),
+                       "graph": f"{per_graph_steps} layer steps per CUDA graph (one per weight copy)",
                        "l2": f"rotating {len(layers)} weight copies ({len(layers) * base.weight_bytes / 1e6:.0f} MB > 126 MB L2)",
                        "clock_preroll_s": args.clock_preroll,
                        "parallelism": f"replica x{world}", "frac_of_8TBs": round(value / world / NOMINAL_HBM_GBS, 4)},
@@ -689,6 +825,7 @@ def main():
                     "d2h_bytes_per_step": 4 * (base.QKV + 2 * base.H), "ms_per_step": round(e2e_ms, 5)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
+            "c0_gemv": c0,
             "decode": decode,
             "lm_head_sharded": lm_sharded,
         }
