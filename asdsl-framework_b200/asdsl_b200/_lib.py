@@ -36,6 +36,7 @@ _SIGS = {
     "asdsl_b200_device_status": [_P, _I],
     "asdsl_b200_selftest_bounded_wait": [_I, _P],
     "asdsl_b200_set_launch_policy": [_I, _I],
+    "asdsl_b200_set_mma_min_tokens": [_I],
     "asdsl_b200_quantize_activation": [_P, _P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_preq2_fused": [_P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_gemv_preq2": [_P, _P, _P, _P, _P, _I, _I, _I, _P],

@@ -7,6 +7,7 @@
 
 #include "launch.cuh"
 #include "weight_prep.cuh"
+#include "gemv_mma.cuh"
 
 using namespace asdsl;
 
@@ -130,6 +131,12 @@ extern "C" {
 const char* asdsl_b200_version(void) { return "asdsl-b200 0.1 (sm_100a)"; }
 
 const char* asdsl_b200_last_error(void) { return last_error_msg().c_str(); }
+
+int asdsl_b200_set_mma_min_tokens(int n_tokens) {
+    if (n_tokens < 0) return set_error(kEinval, "set_mma_min_tokens: negative token count");
+    launch_policy().mma_min_tokens = n_tokens;
+    return kOk;
+}
 
 int asdsl_b200_set_launch_policy(int ctas_per_sm, int use_pdl) {
     if (ctas_per_sm < 1 || ctas_per_sm > kCtasPerSm)
@@ -566,12 +573,73 @@ int asdsl_b200_selftest_bounded_wait(int which, void* stream) {
 // ---------------------------------------------------------------------------
 // multi-token W4A8 GEMV: one pass streams the weights once for up to 16 activation rows
 // ---------------------------------------------------------------------------
+// Activation scratch of the multi-token GEMVs: the tokens of one pass are quantized once into a
+// slot (at most half the shared-memory budget, the per-pass limit) by k_quant_tokens.  A static
+// device array (no allocation, so captured graphs need no warm-up call), handed out round-robin
+// from a ring of kTokSlots per device: calls overlapping on more streams than that would share one.
+constexpr int kTokSlots = 8;
+constexpr size_t kTokSlotBytes = kSmemBudget / 2;
+static __device__ __align__(128) unsigned char g_tok_scratch[kTokSlots * kTokSlotBytes];
+
 namespace {
+int token_scratch_slot(uint8_t** out) {
+    static std::mutex mu;
+    static void* base[64] = {nullptr};
+    static unsigned next[64] = {0};
+    int dev = 0;
+    ASDSL_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(kEinval, "gemv_multi: device index out of range");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!base[dev]) ASDSL_CUDA(cudaGetSymbolAddress(&base[dev], g_tok_scratch));
+    *out = static_cast<uint8_t*>(base[dev]) + (next[dev]++ % kTokSlots) * kTokSlotBytes;
+    return kOk;
+}
+
+// quantize the T tokens of a pass into a scratch slot (PDL: overlaps the previous kernel's tail)
+template <int PRO>
+int quant_tokens(GemvArgs& ga, int T, cudaStream_t st) {
+    const uint32_t xa_stride = xarea_layout_bytes(ga.K, ga.gs, false);
+    if (static_cast<size_t>(xa_stride) * T > kTokSlotBytes) return set_error(kEinval, "internal: token scratch too small");
+    uint8_t* slot = nullptr;
+    if (int rc = token_scratch_slot(&slot)) return rc;
+    GemvArgs g = ga;
+    g.n_tokens = T;
+    void* args[] = {&g, &slot, const_cast<uint32_t*>(&xa_stride)};
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(T));
+    cfg.blockDim = dim3(kConsumerThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (launch_policy().pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    ASDSL_CUDA(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(&k_quant_tokens<PRO>), args));
+    ga.xa_pre = slot;
+    return kOk;
+}
+
 template <int FMT, int PRO>
 int multi_pass(int T, const StreamIn* s, int ns, long long nb, GemvArgs ga, cudaStream_t st, const LaunchOpts& o) {
     ga.n_tokens = T;
+    // from 4 rows the tokens are quantized once up front (in every CTA's prologue they cost more
+    // than the extra launch); 2 rows stay in the prologue
+    if (T >= 4)
+        if (int rc = quant_tokens<PRO>(ga, T, st)) return rc;
     if (T <= 2) return launch_stream_gemv<FMT, PRO, kEpiStore, 2>(s, ns, nb, 0, ga, st, o);
     if (T <= 4) return launch_stream_gemv<FMT, PRO, kEpiStore, 4>(s, ns, nb, 0, ga, st, o);
+    if constexpr (MmaFmt<FMT>::kSupported) {
+        // 16 x 8 x 32 group dots on the tensor cores, when selected (asdsl_b200_set_mma_min_tokens);
+        // off by default: on B200 the lane-dot path measures faster for 8 and 16 rows
+        const int mt = launch_policy().mma_min_tokens;
+        if (mt > 0 && T >= mt && T >= 5 && mma_plan_fits(s, ns, ga.K, ga.gs, T)) {
+            if (T <= 8) return launch_stream_gemv_mma<FMT, PRO, 8>(s, ns, nb, ga, st, o);
+            return launch_stream_gemv_mma<FMT, PRO, 16>(s, ns, nb, ga, st, o);
+        }
+    }
     if (T <= 8) return launch_stream_gemv<FMT, PRO, kEpiStore, 8>(s, ns, nb, 0, ga, st, o);
     return launch_stream_gemv<FMT, PRO, kEpiStore, 16>(s, ns, nb, 0, ga, st, o);
 }

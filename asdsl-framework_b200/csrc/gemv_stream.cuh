@@ -135,6 +135,9 @@ struct GemvArgs {
     unsigned long long* xchg_self;          // this rank's slot buffer
     int* xchg_epoch;                        // device-resident step counter of the exchange
     int xchg_world, xchg_rank;
+    // multi-token kernels: the tokens' A8 areas, quantized once by k_quant_tokens in the layout
+    // of the shared-memory areas (n_tokens x xarea_layout_bytes); null = each CTA quantizes
+    const uint8_t* xa_pre;
 };
 
 // ---------------------------------------------------------------------------
@@ -406,6 +409,38 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
         }
         consumer_sync();
     }
+}
+
+// Multi-token prologue: copy the A8 areas that k_quant_tokens wrote (one per token, the layout of
+// the shared-memory areas) into shared memory, or quantize every token here when there are none.
+template <int PRO>
+__device__ void token_prologue(const GemvArgs& ga, uint8_t* area0, uint32_t xa_stride) {
+    if (ga.xa_pre != nullptr) {
+        const int n16 = static_cast<int>((xa_stride * static_cast<uint32_t>(ga.n_tokens)) >> 4);
+        const uint4* src = reinterpret_cast<const uint4*>(ga.xa_pre);
+        uint4* dst = reinterpret_cast<uint4*>(area0);
+        for (int i = threadIdx.x; i < n16; i += kConsumerThreads) dst[i] = __ldcg(src + i);
+        consumer_sync();
+        return;
+    }
+    for (int t = 0; t < ga.n_tokens; ++t) {
+        GemvArgs gt = ga;
+        gt.x = ga.x + static_cast<size_t>(t) * ga.K;
+        run_prologue<PRO>(gt, xarea_layout(area0 + t * xa_stride, ga.K, ga.gs, false), threadIdx.x);
+    }
+}
+
+// The tokens' A8 areas for a multi-token GEMV, once instead of in every CTA: block t (of
+// kConsumerThreads threads, the prologue's barrier width) quantizes token t into
+// out + t * xa_stride exactly as the GEMV's own prologue would in shared memory.
+template <int PRO>
+__global__ void __launch_bounds__(kConsumerThreads) k_quant_tokens(const GemvArgs ga, uint8_t* out,
+                                                                 uint32_t xa_stride) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    GemvArgs gt = ga;
+    gt.x = ga.x + static_cast<size_t>(blockIdx.x) * ga.K;
+    run_prologue<PRO>(gt, xarea_layout(out + blockIdx.x * xa_stride, ga.K, ga.gs, false), threadIdx.x);
 }
 
 // ---------------------------------------------------------------------------
@@ -987,12 +1022,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     if constexpr (NT == 1) {
         run_prologue<PRO>(ga, xa, threadIdx.x);
     } else {
-        for (int t = 0; t < ga.n_tokens; ++t) {
-            GemvArgs gt = ga;
-            gt.x = ga.x + static_cast<size_t>(t) * ga.K;
-            run_prologue<PRO>(gt, xarea_layout(smem + pa.xarea_off + t * xa_stride, ga.K, ga.gs, false),
-                              threadIdx.x);
-        }
+        token_prologue<PRO>(ga, smem + pa.xarea_off, xa_stride);
     }
 
     XAddr xad;

@@ -83,6 +83,7 @@ inline uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 struct LaunchPolicy {
     int ctas_per_sm = kCtasPerSm;  // 1 leaves an SM slot free for the next kernel of a chain
     int pdl = 1;                   // programmatic dependent launch on every streaming GEMV
+    int mma_min_tokens = 0;        // multi-token GEMVs from this many rows on the tensor cores (0 = never)
 };
 inline LaunchPolicy& launch_policy() {
     static LaunchPolicy p;

@@ -430,6 +430,98 @@ def c0_bench(world: int, rank: int, steps: int = 320) -> dict:
             "check": {"rel_err_vs_oracle": err}}
 
 
+C4_METRIC = "multi-token W4A8 GEMV (config 4, speculative verify): us per call and weight-stream GB/s"
+
+
+def c4_bench(rank: int) -> dict:
+    """Config 4: Y[t] = W . A8(X[t]) for k in {1, 2, 4, 8, 16} token rows in one weight stream, on
+    8192 x 3072 and 3072 x 8192, preq gs32 (reference quantizer pipeline on the device, then the
+    preq byte order) and Q4_K (reference interpretation, own quantizer), W ~ N(0, 0.02) and
+    X ~ N(0, 1) from default_rng(4).  Every k = 16 row is checked against the single-token oracle
+    (1e-3).  Timing: graphs of 16 calls over weight copies rotated past 300 MB."""
+    import numpy as np
+    import torch
+
+    from asdsl_b200 import _lib
+    from asdsl_b200.quantization.device import prepare_preq2_device
+    from asdsl_b200.quantization.repack import preq2_to_preq
+    from asdsl_b200.quantization.synth import quantize_q4k
+    from oracle.oracle import Oracle, build as build_oracle, rel_err
+
+    if rank == 0 and not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+        build_oracle()
+    orc = Oracle() if rank == 0 else None
+    lib = _lib.load()
+    rng = np.random.default_rng(4)
+    s = torch.cuda.Stream()
+    out = {"metric": C4_METRIC, "unit": "us", "config": {"workload": "c4_multi_token", "seed": 4, "tol": 1e-3},
+           "cases": []}
+    peak, peak_kind = _peaks()
+    for (M, K) in ((8192, 3072), (3072, 8192)):
+        w = (rng.standard_normal((M, K)) * 0.02).astype(np.float32)
+        meta, quant = prepare_preq2_device(torch.from_numpy(w).cuda())
+        preq = preq2_to_preq(meta.cpu().numpy(), quant.cpu().numpy(), M, K).reshape(-1)
+        del meta, quant
+        q4k = quantize_q4k(w).reshape(-1)
+        X = rng.standard_normal((16, K)).astype(np.float32)
+        Xd = torch.from_numpy(X).cuda()
+        for name, fmt, wbytes in (("preq_gs32", _lib.FMT_PREQ, preq), ("q4_k", _lib.FMT_Q4K, q4k)):
+            wd = torch.from_numpy(wbytes).cuda()
+            Y = torch.empty(16 * M, dtype=torch.float32, device="cuda")
+
+            def run(wt, k):
+                _lib.check(lib.asdsl_b200_gemv_multi(fmt, wt.data_ptr(), None, Xd.data_ptr(), Y.data_ptr(), M, K, k,
+                                                     s.cuda_stream), "gemv_multi")
+
+            err = None
+            if orc is not None:
+                with torch.cuda.stream(s):
+                    run(wd, 16)
+                s.synchronize()
+                y = Y.cpu().numpy().reshape(16, M)
+                ref = [orc.gemv_preq_fused(wbytes, X[t], M, K) if fmt == _lib.FMT_PREQ else
+                       orc.gemv_q4km(wbytes, X[t], M, K) for t in range(16)]
+                err = max(float(rel_err(y[t], ref[t])) for t in range(16))
+                if err > 1e-3:
+                    raise SystemExit(f"bench: config-4 {name} {M}x{K} mismatch vs oracle ({err})")
+            copies = [wd] + [wd.clone() for _ in range(max(1, -(-320_000_000 // wd.numel())) - 1)]
+            per_k, per_k_tc = [], []
+            for k, mma in ((1, 0), (2, 0), (4, 0), (8, 0), (16, 0), (8, 1), (16, 1)):
+                # the tensor-core variant (asdsl_b200_set_mma_min_tokens) timed beside the default
+                _lib.check(lib.asdsl_b200_set_mma_min_tokens(5 if mma else 0), "set_mma_min_tokens")
+                with torch.cuda.stream(s):
+                    for c in copies[:2]:
+                        run(c, k)
+                s.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for i in range(16):
+                        run(copies[i % len(copies)], k)
+                with torch.cuda.stream(s):
+                    for _ in range(3):
+                        g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                with torch.cuda.stream(s):
+                    for _ in range(10):
+                        g.replay()
+                e1.record(s)
+                e1.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / 160
+                gbs = (wd.numel() + 4 * k * (K + M)) / (us * 1e-6) / 1e9
+                (per_k_tc if mma else per_k).append({"k": k, "us": round(us, 3), "gbs": round(gbs, 1),
+                                                     "frac": round(gbs / peak, 4), "us_per_token": round(us / k, 3)})
+                del g
+            _lib.check(lib.asdsl_b200_set_mma_min_tokens(0), "set_mma_min_tokens")
+            out["cases"].append({"format": name, "M": M, "K": K, "weight_bytes": int(wd.numel()),
+                                 "rel_err_k16": err, "per_k": per_k, "tensor_core": per_k_tc})
+            del copies, wd
+    assert _lib.device_status(clear=True) == 0
+    out["peak"], out["peak_kind"] = peak, peak_kind
+    return out
+
+
 LM_METRIC = "lm_head W4 GEMV + argmax HBM GB/s (200064x3072 Q4_128, row-sharded, all ranks)"
 
 
@@ -554,6 +646,8 @@ def main():
     ap.add_argument("--no-lm-head", action="store_true", help="skip the config-2 sharded lm_head measurement")
     ap.add_argument("--no-c0", action="store_true", help="skip the config-0 single-GEMV measurement")
     ap.add_argument("--only-c0", action="store_true", help="run only the config-0 section (profiling)")
+    ap.add_argument("--c4", action=argparse.BooleanOptionalAction, default=True,
+                    help="the config-4 multi-token section (N=1 only)")
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--clock-preroll", type=float, default=1.5,
                     help="seconds of untimed replays inside the clock-sampling window before timing")
@@ -790,6 +884,7 @@ def main():
                          f"rotating {args.copies} weight copies past the last-level cache"}
 
     c0 = None if args.no_c0 else c0_bench(world, rank)
+    c4 = c4_bench(rank) if (args.c4 and world == 1) else None
     decode = None
     if not args.no_decode:
         decode = decode_bench(args.decode_steps, world=world)
@@ -826,6 +921,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "c0_gemv": c0,
+            "c4_multi": c4,
             "decode": decode,
             "lm_head_sharded": lm_sharded,
         }

@@ -50,6 +50,11 @@ const char* asdsl_b200_last_error(void);
  * threading knobs (ASDSL_PERSISTENT_POOL, ASDSL_CHUNKED_GEMV, engine_flags.hpp:8-15,
  * gemv_chunked.hpp:16-45) play this role there. */
 int asdsl_b200_set_launch_policy(int ctas_per_sm, int use_pdl);
+/* No reference counterpart.  Multi-token GEMVs (asdsl_b200_gemv_multi) with at least n_tokens rows
+ * (and at least 5) compute their group dots with int8 tensor-core MMAs (mma.sync m16n8k32) instead
+ * of lane dp4a chains; 0 (the default) never does.  Same results within the multi-token tolerance
+ * (only the float summation order across groups differs). */
+int asdsl_b200_set_mma_min_tokens(int n_tokens);
 
 /* Reads (and with clear != 0 resets) the current device's status word: bits
  * set by kernels whose bounded waits gave up.  Synchronizes the device. */

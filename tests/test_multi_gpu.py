@@ -43,9 +43,17 @@ def _oracle_row(oracle, fmt, w0, w1, x, M, K):
     return oracle.gemv_preq2_fused(w0, w1, x, M, K)
 
 
+@pytest.fixture(params=["lane_dot", "tensor_core"])
+def multi_path(request, native):
+    """both multi-token paths: lane dp4a chains (default) and int8 tensor-core MMAs for >= 5 rows"""
+    native.call("asdsl_b200_set_mma_min_tokens", 5 if request.param == "tensor_core" else 0)
+    yield request.param
+    native.call("asdsl_b200_set_mma_min_tokens", 0)
+
+
 @pytest.mark.parametrize("fmt_name", ["PREQ", "Q4K"])
 @pytest.mark.parametrize("M,K", [(8192, 3072), (3072, 8192)])
-def test_gemv_multi_config4(native, oracle, fmt_name, M, K):
+def test_gemv_multi_config4(native, oracle, fmt_name, M, K, multi_path):
     from asdsl_b200.kernels._native_gemv import gemv_multi
 
     fmt = getattr(native, f"FMT_{fmt_name}")
@@ -66,9 +74,10 @@ def test_gemv_multi_config4(native, oracle, fmt_name, M, K):
 
 @pytest.mark.parametrize("fmt_name,M,K", [("PREQ", 61, 512), ("Q4K", 23, 512), ("PREQ2", 61, 512),
                                           ("PREQ2", 5120, 3072), ("PREQ", 37, 3072)])
-@pytest.mark.parametrize("k", [3, 5, 17])
-def test_gemv_multi_ragged(native, oracle, fmt_name, M, K, k):
-    """odd token counts (partial token groups, a second pass past 16) and ragged row bands"""
+@pytest.mark.parametrize("k", [3, 5, 8, 9, 12, 17])
+def test_gemv_multi_ragged(native, oracle, fmt_name, M, K, k, multi_path):
+    """odd token counts (partial token groups, a second pass past 16; 8 and more rows run on the
+    tensor cores with partial 16-row tiles and partial 8-token groups) and ragged row bands"""
     from asdsl_b200.kernels._native_gemv import gemv_multi
 
     fmt = getattr(native, f"FMT_{fmt_name}")
