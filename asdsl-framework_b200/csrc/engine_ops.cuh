@@ -82,28 +82,62 @@ struct AttnSmem {
     float ks[2], vs[2];
     float red[2][2][2];     // [k|v][64-block][warp of block]
     float m[kAttnGroups], l[kAttnGroups];
+    float sc[kAttnGroups];  // merge: exp(m[k] - M) of each live group, 0 for an empty one
+    float L;                // merge: the softmax denominator
     float num[kAttnGroups][kAttnHeadDim];
+};
+
+// no-op wait: the caller already ordered the head after the kernel that wrote qkv
+struct NoWait {
+    __device__ __forceinline__ void operator()() const {}
 };
 
 // One head of the decode attention, run by kAttnWarps warps (thread ids 0..255).  `sync` is
 // the barrier of those warps; kCoherent reads qkv through L2 (it was written by other CTAs of
 // the same persistent kernel).
-template <bool kCoherent, typename Sync>
-__device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSmem& S, int tid, Sync sync) {
+//
+// Everything that does not depend on the kernel that wrote qkv -- the position, the RoPE
+// factors and the first block of cached K/V -- is loaded before `wait()` returns, so those loads
+// overlap the previous kernel's tail.
+template <bool kCoherent, typename Sync, typename Wait = NoWait>
+__device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSmem& S, int tid, Sync sync,
+                                               Wait wait = Wait()) {
     constexpr int hd = kAttnHeadDim;
     const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
     const int g = h / groups;
     const int half = a.rot / 2;
     const int pos = a.st->pos;
-    if (pos < 0 || pos >= a.max_seq) return;
+    if (pos < 0 || pos >= a.max_seq) {
+        wait();
+        return;
+    }
     const int lane = tid & 31, warp = tid >> 5;
     const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
-    const float* cp = a.cos_t + static_cast<long long>(pos) * half;
-    const float* sp = a.sin_t + static_cast<long long>(pos) * half;
     auto ldq = [&](const float* p) -> float {
         if constexpr (kCoherent) return __ldcg(p);
         else return *p;
     };
+    // RoPE factors of this thread's dim pair
+    float rc = 0.f, rs = 0.f;
+    if (tid < 2 * half) {
+        const int i = tid < half ? tid : tid - half;
+        rc = a.cos_t[static_cast<long long>(pos) * half + i];
+        rs = a.sin_t[static_cast<long long>(pos) * half + i];
+    }
+    // the first cached position of this thread's 8-lane group (an earlier token wrote it)
+    const int grp = warp * 4 + (lane >> 3);  // 0 .. kAttnGroups-1
+    const int l8 = lane & 7;                 // dims 16*l8 .. 16*l8+15 (scale block l8 >> 2)
+    uint4 pk = make_uint4(0u, 0u, 0u, 0u), pv = pk;
+    float pks = 0.f, pvs = 0.f;
+    if (grp < pos) {
+        const long long rb = (static_cast<long long>(grp) * a.n_kv + g) * hd + l8 * 16;
+        const long long sb = (static_cast<long long>(grp) * a.n_kv + g) * 2 + (l8 >> 2);
+        pk = *reinterpret_cast<const uint4*>(a.kq + rb);
+        pv = *reinterpret_cast<const uint4*>(a.vq + rb);
+        pks = a.ks[sb];
+        pvs = a.vs[sb];
+    }
+    wait();
 
     // --- RoPE on q and k: thread t < 128 owns dim t (rope_apply_inplace :768-801) ---
     float kval = 0.f, vval = 0.f;
@@ -113,13 +147,13 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
         float qv = ldq(qh + tid), kv = ldq(kh + tid);
         if (tid < half) {
             // o0 = fma(x_first, c, -(x_second * s))
-            qv = __fmaf_rn(qv, cp[tid], -__fmul_rn(ldq(qh + tid + half), sp[tid]));
-            kv = __fmaf_rn(kv, cp[tid], -__fmul_rn(ldq(kh + tid + half), sp[tid]));
+            qv = __fmaf_rn(qv, rc, -__fmul_rn(ldq(qh + tid + half), rs));
+            kv = __fmaf_rn(kv, rc, -__fmul_rn(ldq(kh + tid + half), rs));
         } else if (tid < 2 * half) {
             // o1 = fma(x_first, s, x_second * c)
             const int i = tid - half;
-            qv = __fmaf_rn(ldq(qh + i), sp[i], __fmul_rn(qv, cp[i]));
-            kv = __fmaf_rn(ldq(kh + i), sp[i], __fmul_rn(kv, cp[i]));
+            qv = __fmaf_rn(ldq(qh + i), rs, __fmul_rn(qv, rc));
+            kv = __fmaf_rn(ldq(kh + i), rs, __fmul_rn(kv, rc));
         }
         S.q[tid] = qv;
         kval = kv;
@@ -165,8 +199,6 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
 
     // --- scores + online softmax: an 8-lane group per position, 16 dims per lane ---
     const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));
-    const int grp = warp * 4 + (lane >> 3);  // 0 .. kAttnGroups-1
-    const int l8 = lane & 7;                 // dims 16*l8 .. 16*l8+15 (scale block l8 >> 2)
     float qreg[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) qreg[i] = S.q[l8 * 16 + i];
@@ -190,11 +222,16 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
                     vdq[i] = S.v[l8 * 16 + i];
                 }
             } else {
-                const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
-                const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + (l8 >> 2);
-                const uint4 kw = *reinterpret_cast<const uint4*>(a.kq + rb);
-                const uint4 vw = *reinterpret_cast<const uint4*>(a.vq + rb);
-                const float ksc = a.ks[sb], vsc = a.vs[sb];
+                uint4 kw = pk, vw = pv;
+                float ksc = pks, vsc = pvs;
+                if (p0 > 0) {
+                    const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
+                    const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + (l8 >> 2);
+                    kw = *reinterpret_cast<const uint4*>(a.kq + rb);
+                    vw = *reinterpret_cast<const uint4*>(a.vq + rb);
+                    ksc = a.ks[sb];
+                    vsc = a.vs[sb];
+                }
                 const uint32_t kk[4] = {kw.x, kw.y, kw.z, kw.w};
                 const uint32_t vv[4] = {vw.x, vw.y, vw.z, vw.w};
 #pragma unroll
@@ -228,19 +265,28 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
     for (int i = 0; i < 16; ++i) S.num[grp][l8 * 16 + i] = num[i];
     sync();
     // --- merge the groups in a fixed order --------------------------------------------
-    if (tid < hd) {
-        float M = -INFINITY;
-        for (int k = 0; k < kAttnGroups; ++k)
-            if (S.l[k] > 0.0f) M = fmaxf(M, S.m[k]);
-        float L = 0.0f, acc = 0.0f;
-        for (int k = 0; k < kAttnGroups; ++k) {
-            if (S.l[k] > 0.0f) {
-                const float sc = expf(S.m[k] - M);
-                L = __fmaf_rn(S.l[k], sc, L);
-                acc = __fmaf_rn(S.num[k][tid], sc, acc);
-            }
+    // warp 0: the maximum over live groups, each group's exp(m - M) once, and the denominator
+    if (warp == 0) {
+        static_assert(kAttnGroups == 32, "one lane per position group");
+        const bool live_k = S.l[lane] > 0.0f;
+        float M = live_k ? S.m[lane] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        S.sc[lane] = live_k ? expf(S.m[lane] - M) : 0.0f;
+        __syncwarp();
+        if (lane == 0) {
+            float L = 0.0f;
+            for (int k = 0; k < kAttnGroups; ++k)
+                if (S.l[k] > 0.0f) L = __fmaf_rn(S.l[k], S.sc[k], L);
+            S.L = L;
         }
-        a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, L));
+    }
+    sync();
+    if (tid < hd) {
+        float acc = 0.0f;
+        for (int k = 0; k < kAttnGroups; ++k)
+            if (S.l[k] > 0.0f) acc = __fmaf_rn(S.num[k][tid], S.sc[k], acc);
+        a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, S.L));
     }
 }
 
@@ -248,11 +294,17 @@ struct BlockSync {
     __device__ __forceinline__ void operator()() const { __syncthreads(); }
 };
 
+// the programmatic-launch wait on the qkv kernel, taken inside the head after its independent loads
+struct GridWait {
+    __device__ __forceinline__ void operator()() const {
+        grid_dependency_wait();
+        grid_launch_dependents();
+    }
+};
+
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
     __shared__ AttnSmem S;
-    grid_dependency_wait();
-    grid_launch_dependents();
-    attention_head<false>(a, blockIdx.x, S, threadIdx.x, BlockSync());
+    attention_head<false>(a, blockIdx.x, S, threadIdx.x, BlockSync(), GridWait());
 }
 
 // decode step done: seq[pos + 1] = argmax token, pos += 1 (seq holds max_seq + 1 entries;
