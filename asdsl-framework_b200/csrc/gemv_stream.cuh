@@ -553,10 +553,8 @@ __device__ __forceinline__ void slice_math(float a[4], const SliceData& d, uint3
 
 template <int FMT>
 __device__ __forceinline__ void band_compute(float a[4], uint32_t s0, uint32_t s1, int K, int rs, const XAddr& xs,
-                                             int lane, int rot, int q0, int q1) {
+                                             int lane, const uint32_t (&rr)[4], int q0, int q1) {
     const int nq = K >> 5;
-    const uint32_t rr[4] = {static_cast<uint32_t>(rot & 3), static_cast<uint32_t>((rot + 1) & 3),
-                            static_cast<uint32_t>((rot + 2) & 3), static_cast<uint32_t>((rot + 3) & 3)};
 #pragma unroll
     for (int r = 0; r < 4; ++r) a[r] = 0.0f;
     // two slices in flight: load both, then do the math
@@ -769,6 +767,9 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
     const int M = ga.M;
     const int nq = K >> 5;
     const int rot = (FMT == kFmtPreq2) ? ((lane >> 1) & 3) : ((lane >> 2) & 3);
+    // this lane's row visiting order within a band (bank-conflict-free 16-byte loads)
+    const uint32_t rr_lane[4] = {static_cast<uint32_t>(rot & 3), static_cast<uint32_t>((rot + 1) & 3),
+                                 static_cast<uint32_t>((rot + 2) & 3), static_cast<uint32_t>((rot + 3) & 3)};
     int item_base = jg;  // any per-CTA running offset works; the ring position varies per op
     // ring slot and phase of chunk j, advanced incrementally (no division per chunk)
     int s = jg % S;
@@ -901,12 +902,14 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                 const int q0 = (P == 1) ? 0 : pa.q_bounds[part];
                 const int q1 = (P == 1) ? nq : pa.q_bounds[part + 1];
                 float a[4];
-                const uint32_t p0 = (seg == 0 ? ub[0][0] : ub[NSEG - 1][0]) + static_cast<uint32_t>(k * pa.s[0].unit_bytes);
+                // 32-bit offsets: a stage is far below 4 GB
+                const uint32_t p0 = (seg == 0 ? ub[0][0] : ub[NSEG - 1][0]) +
+                                    static_cast<uint32_t>(k) * static_cast<uint32_t>(pa.s[0].unit_bytes);
                 uint32_t p1 = 0u;
                 if constexpr (NS > 1)
                     p1 = (seg == 0 ? ub[0][NS - 1] : ub[NSEG - 1][NS - 1]) +
-                         static_cast<uint32_t>(k * pa.s[NS - 1].unit_bytes);
-                band_compute<FMT>(a, p0, p1, K, pa.row_bytes, xad, lane, rot, q0, q1);
+                         static_cast<uint32_t>(k) * static_cast<uint32_t>(pa.s[NS - 1].unit_bytes);
+                band_compute<FMT>(a, p0, p1, K, pa.row_bytes, xad, lane, rr_lane, q0, q1);
                 unrotate(a, rot);
                 const float v = reduce4(a, lane);
                 float vrow[NSEG];
@@ -937,7 +940,7 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                 } else {
                     vrow[0] = v;
                 }
-                const long long row = unit * 4 + (lane >> 3);
+                const int row = static_cast<int>(unit) * 4 + (lane >> 3);  // rows are an int (M)
                 if (finish && (lane & 7) == 0 && row < M) {
                     if constexpr (EPI == kEpiStore) {
                         ga.y[row] = vrow[0];
