@@ -60,6 +60,7 @@ __global__ void k_embed(const T* __restrict__ emb, float* __restrict__ resid, co
 constexpr int kAttnWarps = 8;
 constexpr int kAttnGroups = kAttnWarps * 4;  // 8-lane position groups per CTA
 constexpr int kAttnHeadDim = 128;
+constexpr int kAttnPrefetch = 4;  // position blocks of cached K/V loaded before the dependency wait
 
 struct AttnArgs {
     const float* qkv;     // [q_dim + 2 kv_dim] (q | k | v), this layer's projection output
@@ -79,11 +80,9 @@ struct AttnSmem {
     float q[kAttnHeadDim];
     float k[kAttnHeadDim];  // dequantized current-position k, v
     float v[kAttnHeadDim];
-    float ks[2], vs[2];
     float red[2][2][2];     // [k|v][64-block][warp of block]
     float m[kAttnGroups], l[kAttnGroups];
     float sc[kAttnGroups];  // merge: exp(m[k] - M) of each live group, 0 for an empty one
-    float L;                // merge: the softmax denominator
     float num[kAttnGroups][kAttnHeadDim];
 };
 
@@ -124,18 +123,25 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
         rc = a.cos_t[static_cast<long long>(pos) * half + i];
         rs = a.sin_t[static_cast<long long>(pos) * half + i];
     }
-    // the first cached position of this thread's 8-lane group (an earlier token wrote it)
+    // the cached positions of this thread's 8-lane group in the first kAttnPrefetch position
+    // blocks (earlier tokens wrote them)
     const int grp = warp * 4 + (lane >> 3);  // 0 .. kAttnGroups-1
     const int l8 = lane & 7;                 // dims 16*l8 .. 16*l8+15 (scale block l8 >> 2)
-    uint4 pk = make_uint4(0u, 0u, 0u, 0u), pv = pk;
-    float pks = 0.f, pvs = 0.f;
-    if (grp < pos) {
-        const long long rb = (static_cast<long long>(grp) * a.n_kv + g) * hd + l8 * 16;
-        const long long sb = (static_cast<long long>(grp) * a.n_kv + g) * 2 + (l8 >> 2);
-        pk = *reinterpret_cast<const uint4*>(a.kq + rb);
-        pv = *reinterpret_cast<const uint4*>(a.vq + rb);
-        pks = a.ks[sb];
-        pvs = a.vs[sb];
+    uint4 pk[kAttnPrefetch], pv[kAttnPrefetch];
+    float pks[kAttnPrefetch], pvs[kAttnPrefetch];
+#pragma unroll
+    for (int i = 0; i < kAttnPrefetch; ++i) {
+        const int p = i * kAttnGroups + grp;
+        pk[i] = pv[i] = make_uint4(0u, 0u, 0u, 0u);
+        pks[i] = pvs[i] = 0.f;
+        if (p < pos) {
+            const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
+            const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + (l8 >> 2);
+            pk[i] = *reinterpret_cast<const uint4*>(a.kq + rb);
+            pv[i] = *reinterpret_cast<const uint4*>(a.vq + rb);
+            pks[i] = a.ks[sb];
+            pvs[i] = a.vs[sb];
+        }
     }
     wait();
 
@@ -168,16 +174,13 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
         S.red[1][tid >> 6][(tid >> 5) & 1] = vm;
     }
     sync();
-    if (tid < 2) {
-        const float ka = fmaxf(S.red[0][tid][0], S.red[0][tid][1]);
-        const float va = fmaxf(S.red[1][tid][0], S.red[1][tid][1]);
-        S.ks[tid] = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
-        S.vs[tid] = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
-    }
-    sync();
     if (tid < hd) {
+        // every thread derives its block's scales from the two warp maxima (no second barrier)
         const int b = tid >> 6;
-        const float ksc = S.ks[b], vsc = S.vs[b];
+        const float ka = fmaxf(S.red[0][b][0], S.red[0][b][1]);
+        const float va = fmaxf(S.red[1][b][0], S.red[1][b][1]);
+        const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
+        const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
         int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
         int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
         qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
@@ -222,9 +225,18 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
                     vdq[i] = S.v[l8 * 16 + i];
                 }
             } else {
-                uint4 kw = pk, vw = pv;
-                float ksc = pks, vsc = pvs;
-                if (p0 > 0) {
+                uint4 kw = make_uint4(0u, 0u, 0u, 0u), vw = kw;
+                float ksc = 0.f, vsc = 0.f;
+                const int blk = p0 / kAttnGroups;
+#pragma unroll
+                for (int i = 0; i < kAttnPrefetch; ++i)
+                    if (blk == i) {
+                        kw = pk[i];
+                        vw = pv[i];
+                        ksc = pks[i];
+                        vsc = pvs[i];
+                    }
+                if (blk >= kAttnPrefetch) {
                     const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
                     const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + (l8 >> 2);
                     kw = *reinterpret_cast<const uint4*>(a.kq + rb);
@@ -273,20 +285,17 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         S.sc[lane] = live_k ? expf(S.m[lane] - M) : 0.0f;
-        __syncwarp();
-        if (lane == 0) {
-            float L = 0.0f;
-            for (int k = 0; k < kAttnGroups; ++k)
-                if (S.l[k] > 0.0f) L = __fmaf_rn(S.l[k], S.sc[k], L);
-            S.L = L;
-        }
     }
     sync();
     if (tid < hd) {
-        float acc = 0.0f;
-        for (int k = 0; k < kAttnGroups; ++k)
-            if (S.l[k] > 0.0f) acc = __fmaf_rn(S.num[k][tid], S.sc[k], acc);
-        a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, S.L));
+        float L = 0.0f, acc = 0.0f;
+        for (int k = 0; k < kAttnGroups; ++k) {
+            if (S.l[k] > 0.0f) {
+                L = __fmaf_rn(S.l[k], S.sc[k], L);
+                acc = __fmaf_rn(S.num[k][tid], S.sc[k], acc);
+            }
+        }
+        a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, L));
     }
 }
 
