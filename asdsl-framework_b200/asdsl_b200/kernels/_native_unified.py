@@ -247,6 +247,27 @@ class UnifiedEngine:
         the result equals forward_verify_serial_all_logits (forward_token numerics, lossless PLD)."""
         return self.forward_verify_serial_all_logits(prompt, start_pos)
 
+    def forward_batch(self, prompt, start_pos: int) -> np.ndarray:
+        """prompt[i] at position start_pos + i, up to 16 tokens per weight read (:2526-2534 over
+        UnifiedEngine::forward_batch, unified_engine.cpp:1117); float32 [vocab], the last token's
+        logits.  Bit-identical to forward_token over the same tokens (logits and KV cache)."""
+        p = np.ascontiguousarray(np.asarray(list(prompt), dtype=np.int32))
+        out = np.zeros(self._vocab, dtype=np.float32)
+        if p.size:
+            _lib.check(self._lib.asdsl_b200_engine_forward_batch(self._e, _ptr(p), int(p.size), int(start_pos),
+                                                                 _ptr(out), 0), "forward_batch")
+        return out
+
+    def forward_verify_batch_raw_all_logits(self, prompt, start_pos: int) -> np.ndarray:
+        """The batched verify (:2613-2625: forward_batch(..., all_logits=true)); float32
+        [len(prompt) * vocab].  Here it equals forward_verify_serial_all_logits bit for bit."""
+        p = np.ascontiguousarray(np.asarray(list(prompt), dtype=np.int32))
+        out = np.empty(p.size * self._vocab, dtype=np.float32)
+        if p.size:
+            _lib.check(self._lib.asdsl_b200_engine_forward_batch(self._e, _ptr(p), int(p.size), int(start_pos),
+                                                                 _ptr(out), 1), "forward_verify_batch_raw_all_logits")
+        return out
+
     def generate(self, prompt, max_tokens: int) -> list[int]:
         return self.generate_with_stops(prompt, max_tokens, [])
 

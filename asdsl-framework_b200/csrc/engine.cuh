@@ -87,6 +87,9 @@ struct asdsl_b200_engine {
     int* verify_tok = nullptr;          // [max_seq]
     float* verify_logits = nullptr;     // [verify_rows][vocab]
     int verify_rows = 0;
+    // batched forward: activation blocks of batch_rows tokens (row t = token t), allocated on first use
+    int batch_rows = 0;
+    float *b_resid = nullptr, *b_qkv = nullptr, *b_att = nullptr, *b_gu = nullptr, *b_h = nullptr;
 };
 
 namespace {
@@ -521,6 +524,206 @@ int eng_status(asdsl_b200_engine* e) {
     return kOk;
 }
 
+// ---------------------------------------------------------------------------
+// batched forward (UnifiedEngine::forward_batch, unified_engine.cpp:1117): the tokens of one pass
+// share every weight read -- one multi-token GEMV per projection -- and give rows bit-identical
+// to forward_token's:
+//   * each multi-token GEMV sums a row's slices in the single-token kernel's order, with the
+//     K-split of the single-token launch of the same projection (eng_single_parts);
+//   * the A8 areas come from the single-token prologue code (k_quant_tokens);
+//   * attention reads its own position back from the cache, which dequantizes to the values the
+//     single-token head keeps in shared memory;
+//   * gate/up rows are stored, then SiLU(gate) * up runs the paired epilogue's arithmetic.
+// ---------------------------------------------------------------------------
+__global__ void k_silu_rows(const float* __restrict__ gu, float* __restrict__ h, int I, int n) {
+    const long long total = static_cast<long long>(I) * n;
+    for (long long k = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; k < total;
+         k += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long t = k / I;
+        const long long i = k - t * I;
+        h[k] = ref_silu_mul(gu[2 * t * I + i], gu[2 * t * I + I + i]);
+    }
+}
+
+int eng_streams(const EngProj& p, StreamIn* in) {
+    if (p.fmt == ASDSL_B200_FMT_PREQ2) preq2_streams(in, p.w0, p.w1, p.rows, p.cols);
+    else q128b_streams(in, p.w0, p.w1, p.rows, p.cols);
+    return p.fmt == ASDSL_B200_FMT_PREQ2 ? 32 : 128;
+}
+
+// the K-split eng_gemv's single-token launch of p uses (pair_rows > 0: the paired gate/up form)
+int eng_single_parts(const EngProj& p, long long pair_rows) {
+    StreamIn in[2];
+    eng_streams(p, in);
+    const long long M = pair_rows > 0 ? pair_rows : p.rows;
+    const int nseg = pair_rows > 0 ? 2 : 1;
+    const long long ub = in[0].unit_bytes + in[1].unit_bytes;
+    return plan_split((M + 3) / 4, ub * nseg, nseg, FmtTraits<kFmtPreq2>::kRowsPerUnit, p.cols, LaunchOpts()).parts;
+}
+
+// T token rows through projection p (all p.rows rows, no pairing) with the K-split `parts`
+template <int FMT, int PRO, int EPI>
+int eng_gemv_rows_fmt(const StreamIn* in, long long nb, GemvArgs ga, int T, const LaunchOpts& o, cudaStream_t s) {
+    ga.n_tokens = T;
+    if (T == 1) return launch_stream_gemv<FMT, PRO, EPI, 1>(in, 2, nb, 0, ga, s, o);
+    if (T >= 4)
+        if (int rc = quant_tokens<PRO>(ga, T, s)) return rc;
+    if (T <= 2) return launch_stream_gemv<FMT, PRO, EPI, 2>(in, 2, nb, 0, ga, s, o);
+    if (T <= 4) return launch_stream_gemv<FMT, PRO, EPI, 4>(in, 2, nb, 0, ga, s, o);
+    if (T <= 8) return launch_stream_gemv<FMT, PRO, EPI, 8>(in, 2, nb, 0, ga, s, o);
+    return launch_stream_gemv<FMT, PRO, EPI, 16>(in, 2, nb, 0, ga, s, o);
+}
+
+template <int PRO, int EPI>
+int eng_gemv_rows(const EngProj& p, GemvArgs ga, int T, int parts, cudaStream_t s) {
+    StreamIn in[2];
+    ga.gs = eng_streams(p, in);
+    LaunchOpts o;
+    o.k_parts = parts;
+    const long long nb = (static_cast<long long>(p.rows) + 3) / 4;
+    if (p.fmt == ASDSL_B200_FMT_PREQ2) return eng_gemv_rows_fmt<kFmtPreq2, PRO, EPI>(in, nb, ga, T, o, s);
+    return eng_gemv_rows_fmt<kFmtQ128B, PRO, EPI>(in, nb, ga, T, o, s);
+}
+
+// tokens per pass: at most 16, and the A8 areas of every projection's input within a token
+// scratch slot
+int eng_batch_cap(const asdsl_b200_engine_config& c) {
+    const int qd = c.num_heads * c.head_dim;
+    const int ks[3] = {c.hidden_size, qd, c.intermediate_size};
+    int cap = 16;
+    for (int k : ks) {
+        const int per = static_cast<int>(kTokSlotBytes / xarea_layout_bytes(k, 32, false));
+        const int per128 = static_cast<int>(kTokSlotBytes / xarea_layout_bytes(k, 128, false));
+        cap = std::min(cap, std::min(per, per128));
+    }
+    return cap < 1 ? 1 : cap;
+}
+
+int eng_batch_alloc(asdsl_b200_engine* e) {
+    if (e->batch_rows > 0) return kOk;
+    const asdsl_b200_engine_config& c = e->cfg;
+    const size_t B = static_cast<size_t>(eng_batch_cap(c));
+    const size_t qd = static_cast<size_t>(c.num_heads) * c.head_dim, kvd = static_cast<size_t>(c.num_kv_heads) * c.head_dim;
+    const size_t H = c.hidden_size, I = c.intermediate_size;
+    if (int rc = eng_alloc(e, &e->b_resid, 4 * B * H)) return rc;
+    if (int rc = eng_alloc(e, &e->b_qkv, 4 * B * (qd + 2 * kvd))) return rc;
+    if (int rc = eng_alloc(e, &e->b_att, 4 * B * qd)) return rc;
+    if (int rc = eng_alloc(e, &e->b_gu, 4 * B * 2 * I)) return rc;
+    if (int rc = eng_alloc(e, &e->b_h, 4 * B * I)) return rc;
+    e->batch_rows = static_cast<int>(B);
+    return kOk;
+}
+
+// one pass of T <= batch_rows tokens (device ids tok[0..T)) at positions start .. start + T - 1;
+// logits: null, or T rows of vocab logits (all_rows) / the last token's row plus its argmax
+int eng_batch_pass(asdsl_b200_engine* e, const int* tok, int T, int start, float* logits, bool all_rows) {
+    const asdsl_b200_engine_config& c = e->cfg;
+    cudaStream_t s = e->stream;
+    const int H = c.hidden_size, I = c.intermediate_size;
+    const int qkv_rows = c.num_heads * c.head_dim + 2 * c.num_kv_heads * c.head_dim;
+    {
+        const dim3 grid((H + 255) / 256, T);
+        if (e->embed_f16) {
+            const uint16_t* emb = static_cast<const uint16_t*>(e->embed);
+            void* args[] = {&emb, &e->b_resid, const_cast<int**>(&tok), const_cast<int*>(&c.hidden_size)};
+            if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_embed_rows<uint16_t>), grid, dim3(256),
+                                      args, s, false))
+                return rc;
+        } else {
+            const float* emb = static_cast<const float*>(e->embed);
+            void* args[] = {&emb, &e->b_resid, const_cast<int**>(&tok), const_cast<int*>(&c.hidden_size)};
+            if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_embed_rows<float>), grid, dim3(256),
+                                      args, s, false))
+                return rc;
+        }
+    }
+    for (int l = 0; l < c.num_layers; ++l) {
+        const EngLayer& L = e->layers[l];
+        {
+            GemvArgs ga = base_args(L.p[kProjQkv].rows, H, 32);
+            ga.x = e->b_resid;
+            ga.norm_w = L.rms_att;
+            ga.eps = c.rms_norm_eps;
+            ga.y = e->b_qkv;
+            if (int rc = eng_gemv_rows<kProRmsA8, kEpiStore>(L.p[kProjQkv], ga, T, eng_single_parts(L.p[kProjQkv], 0), s))
+                return rc;
+        }
+        {
+            asdsl::AttnArgs aa;
+            aa.qkv = e->b_qkv;
+            aa.out = e->b_att;
+            aa.kq = e->kq + l * e->kv_codes_per_layer;
+            aa.vq = e->vq + l * e->kv_codes_per_layer;
+            aa.ks = e->ks + l * e->kv_scales_per_layer;
+            aa.vs = e->vs + l * e->kv_scales_per_layer;
+            aa.cos_t = e->cos_t;
+            aa.sin_t = e->sin_t;
+            aa.st = nullptr;
+            aa.n_heads = c.num_heads;
+            aa.n_kv = c.num_kv_heads;
+            aa.rot = c.rotary_dim;
+            aa.max_seq = c.max_seq_len;
+            int start_ = start, stride_ = qkv_rows;
+            void* args[] = {&aa, &start_, &stride_};
+            if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_kv_write_rows), dim3(c.num_kv_heads, T),
+                                      dim3(asdsl::kAttnHeadDim), args, s, false))
+                return rc;
+            if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_rows), dim3(c.num_heads, T),
+                                      dim3(asdsl::kAttnWarps * 32), args, s, false))
+                return rc;
+        }
+        {
+            GemvArgs ga = base_args(H, L.p[kProjO].cols, 32);
+            ga.x = e->b_att;
+            ga.resid = e->b_resid;
+            if (int rc = eng_gemv_rows<kProA8, kEpiResid>(L.p[kProjO], ga, T, eng_single_parts(L.p[kProjO], 0), s))
+                return rc;
+        }
+        {
+            GemvArgs ga = base_args(2 * I, H, 32);
+            ga.x = e->b_resid;
+            ga.norm_w = L.rms_ffn;
+            ga.eps = c.rms_norm_eps;
+            ga.y = e->b_gu;
+            if (int rc = eng_gemv_rows<kProRmsA8, kEpiStore>(L.p[kProjGateUp], ga, T, eng_single_parts(L.p[kProjGateUp], I), s))
+                return rc;
+            const long long total = static_cast<long long>(I) * T;
+            const unsigned blocks = static_cast<unsigned>(std::min<long long>((total + 255) / 256, sm_count() * 8));
+            k_silu_rows<<<blocks, 256, 0, s>>>(e->b_gu, e->b_h, I, T);
+            ASDSL_CUDA(cudaGetLastError());
+        }
+        {
+            GemvArgs ga = base_args(H, I, 32);
+            ga.x = e->b_h;
+            ga.resid = e->b_resid;
+            if (int rc = eng_gemv_rows<kProA8, kEpiResid>(L.p[kProjDown], ga, T, eng_single_parts(L.p[kProjDown], 0), s))
+                return rc;
+        }
+    }
+    if (!logits) return kOk;
+    if (all_rows) {
+        GemvArgs ga = base_args(c.vocab_size, H, 32);
+        ga.x = e->b_resid;
+        ga.norm_w = e->out_norm;
+        ga.eps = c.rms_norm_eps;
+        ga.y = logits;
+        return eng_gemv_rows<kProRmsA8, kEpiStore>(e->lm, ga, T, eng_single_parts(e->lm, 0), s);
+    }
+    // the last token: the decode step's lm_head launch (logits and argmax)
+    GemvArgs ga = base_args(c.vocab_size, H, 32);
+    ga.x = e->b_resid + static_cast<long long>(T - 1) * H;
+    ga.norm_w = e->out_norm;
+    ga.eps = c.rms_norm_eps;
+    ga.y = logits;
+    ga.counter = reinterpret_cast<unsigned int*>(e->am_scratch);
+    ga.part_val = reinterpret_cast<float*>(e->am_scratch + 256);
+    ga.part_idx = reinterpret_cast<int*>(e->am_scratch + 256 + 4 * 1024);
+    ga.out_val = e->am_val;
+    ga.out_idx = e->am_idx;
+    ga.row_base = 0;
+    return eng_gemv<kProRmsA8, kEpiArgmax>(e->lm, ga, 0, s);
+}
+
 #define ENG_CHECK(e)                                                                        \
     do {                                                                                    \
         if (!(e)) return set_error(kEinval, "engine: null engine");                         \
@@ -876,6 +1079,50 @@ int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens
                                    cudaMemcpyDeviceToDevice, e->stream));
     }
     ASDSL_CUDA(cudaMemcpyAsync(out_logits, e->verify_logits, row * n, cudaMemcpyDefault, e->stream));
+    if (int rc = eng_status(e)) return rc;  // synchronizes the stream
+    if (start_pos + n > e->kv_seq_len) e->kv_seq_len = start_pos + n;
+    return kOk;
+}
+
+// UnifiedEngine::forward_batch (unified_engine.cpp:1117): tokens[i] at position start_pos + i
+// for i < n, passes of up to batch_rows tokens through the multi-token GEMVs.  out_logits: null,
+// the last token's logits (all_logits = 0), or n rows (all_logits != 0, as forward_verify_batch's
+// forward_batch(..., true) call).  Rows and KV cache are bit-identical to n forward_token calls
+// of the per-op decode chain.
+int asdsl_b200_engine_forward_batch(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
+                                    float* out_logits, int all_logits) {
+    ENG_READY(e);
+    if (n <= 0) return kOk;
+    if (!tokens) return set_error(kEinval, "forward_batch: null pointer");
+    const asdsl_b200_engine_config& c = e->cfg;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= c.vocab_size)
+            return set_error(kErange, "forward_token: token_id out of vocab range");
+    if (start_pos < 0 || start_pos >= c.max_seq_len || n > c.max_seq_len - start_pos)
+        return set_error(kErange, "forward_token: pos out of kv-cache range");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    if (int rc = eng_batch_alloc(e)) return rc;
+    const size_t row = 4ull * c.vocab_size;
+    const bool all = out_logits && all_logits;
+    if (all && e->verify_rows < n) {
+        if (e->verify_logits) cudaFree(e->verify_logits);
+        e->verify_logits = nullptr;
+        e->verify_rows = 0;
+        ASDSL_CUDA(cudaMalloc(&e->verify_logits, row * n));
+        e->verify_rows = n;
+    }
+    ASDSL_CUDA(cudaMemcpyAsync(e->verify_tok, tokens, 4ull * n, cudaMemcpyHostToDevice, e->stream));
+    const int B = e->batch_rows;
+    for (int t0 = 0; t0 < n; t0 += B) {
+        const int T = std::min(B, n - t0);
+        float* lg = nullptr;
+        if (all) lg = e->verify_logits + static_cast<size_t>(t0) * c.vocab_size;
+        else if (out_logits && t0 + T == n) lg = e->logits;
+        if (int rc = eng_batch_pass(e, e->verify_tok + t0, T, start_pos + t0, lg, all)) return rc;
+    }
+    if (all) ASDSL_CUDA(cudaMemcpyAsync(out_logits, e->verify_logits, row * n, cudaMemcpyDefault, e->stream));
+    else if (out_logits) ASDSL_CUDA(cudaMemcpyAsync(out_logits, e->logits, row, cudaMemcpyDefault, e->stream));
     if (int rc = eng_status(e)) return rc;  // synchronizes the stream
     if (start_pos + n > e->kv_seq_len) e->kv_seq_len = start_pos + n;
     return kOk;

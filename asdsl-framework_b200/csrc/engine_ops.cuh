@@ -98,14 +98,19 @@ struct NoWait {
 // Everything that does not depend on the kernel that wrote qkv -- the position, the RoPE
 // factors and the first block of cached K/V -- is loaded before `wait()` returns, so those loads
 // overlap the previous kernel's tail.
-template <bool kCoherent, typename Sync, typename Wait = NoWait>
+//
+// kBatch: one token of a batch at position `batch_pos`, whose K/V (and those of the batch's
+// other tokens) k_kv_write_rows already stored; every position, its own included, is read from
+// the cache.  A cached position dequantizes to exactly the values the single-token head keeps in
+// shared memory for its own position, so both give bit-identical outputs.
+template <bool kCoherent, typename Sync, typename Wait = NoWait, bool kBatch = false>
 __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSmem& S, int tid, Sync sync,
-                                               Wait wait = Wait()) {
+                                               Wait wait = Wait(), int batch_pos = -1) {
     constexpr int hd = kAttnHeadDim;
     const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
     const int g = h / groups;
     const int half = a.rot / 2;
-    const int pos = a.st->pos;
+    const int pos = kBatch ? batch_pos : a.st->pos;
     if (pos < 0 || pos >= a.max_seq) {
         wait();
         return;
@@ -134,7 +139,7 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
         const int p = i * kAttnGroups + grp;
         pk[i] = pv[i] = make_uint4(0u, 0u, 0u, 0u);
         pks[i] = pvs[i] = 0.f;
-        if (p < pos) {
+        if (kBatch ? p <= pos : p < pos) {
             const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
             const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + (l8 >> 2);
             pk[i] = *reinterpret_cast<const uint4*>(a.kq + rb);
@@ -167,34 +172,36 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
     }
     // --- quantize this position's k and v per 64-dim block (set_kv_cache :872-917) ---
     // dims 0..63 are warps 0-1, dims 64..127 warps 2-3
-    const float km = warp_max(fabsf(kval));
-    const float vm = warp_max(fabsf(vval));
-    if (tid < hd && lane == 0) {
-        S.red[0][tid >> 6][(tid >> 5) & 1] = km;
-        S.red[1][tid >> 6][(tid >> 5) & 1] = vm;
-    }
-    sync();
-    if (tid < hd) {
-        // every thread derives its block's scales from the two warp maxima (no second barrier)
-        const int b = tid >> 6;
-        const float ka = fmaxf(S.red[0][b][0], S.red[0][b][1]);
-        const float va = fmaxf(S.red[1][b][0], S.red[1][b][1]);
-        const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
-        const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
-        int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
-        int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
-        qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
-        qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
-        S.k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
-        S.v[tid] = __fmul_rn(static_cast<float>(qv), vsc);
-        if (h % groups == 0) {
-            const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
-            a.kq[kb + tid] = static_cast<int8_t>(qk);
-            a.vq[kb + tid] = static_cast<int8_t>(qv);
-            if ((tid & 63) == 0) {
-                const long long sb = (static_cast<long long>(pos) * a.n_kv + g) * 2 + b;
-                a.ks[sb] = ksc;
-                a.vs[sb] = vsc;
+    if constexpr (!kBatch) {
+        const float km = warp_max(fabsf(kval));
+        const float vm = warp_max(fabsf(vval));
+        if (tid < hd && lane == 0) {
+            S.red[0][tid >> 6][(tid >> 5) & 1] = km;
+            S.red[1][tid >> 6][(tid >> 5) & 1] = vm;
+        }
+        sync();
+        if (tid < hd) {
+            // every thread derives its block's scales from the two warp maxima (no second barrier)
+            const int b = tid >> 6;
+            const float ka = fmaxf(S.red[0][b][0], S.red[0][b][1]);
+            const float va = fmaxf(S.red[1][b][0], S.red[1][b][1]);
+            const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
+            const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
+            int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
+            int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
+            qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
+            qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+            S.k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
+            S.v[tid] = __fmul_rn(static_cast<float>(qv), vsc);
+            if (h % groups == 0) {
+                const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
+                a.kq[kb + tid] = static_cast<int8_t>(qk);
+                a.vq[kb + tid] = static_cast<int8_t>(qv);
+                if ((tid & 63) == 0) {
+                    const long long sb = (static_cast<long long>(pos) * a.n_kv + g) * 2 + b;
+                    a.ks[sb] = ksc;
+                    a.vs[sb] = vsc;
+                }
             }
         }
     }
@@ -218,7 +225,7 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
 #pragma unroll
         for (int i = 0; i < 16; ++i) vdq[i] = 0.0f;
         if (live) {
-            if (p == pos) {
+            if (!kBatch && p == pos) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     dot = __fmaf_rn(qreg[i], S.k[l8 * 16 + i], dot);
@@ -314,6 +321,80 @@ struct GridWait {
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
     __shared__ AttnSmem S;
     attention_head<false>(a, blockIdx.x, S, threadIdx.x, BlockSync(), GridWait());
+}
+
+// ---------------------------------------------------------------------------
+// Batched forward (n tokens at positions start .. start + n - 1, row t of every activation
+// block belongs to token t).  The KV writes of all n tokens run first (k_kv_write_rows), then
+// every (head, token) pair attends over the positions <= its own, all read from the cache.
+// ---------------------------------------------------------------------------
+
+// resid[t] = fp32(embedding[tok[t]]); the tokens were range-checked on the host
+template <typename T>
+__global__ void k_embed_rows(const T* __restrict__ emb, float* __restrict__ resid, const int* tok, int H) {
+    const int t = blockIdx.y;
+    const T* row = emb + static_cast<long long>(tok[t]) * H;
+    float* dst = resid + static_cast<long long>(t) * H;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x)
+        dst[i] = load_as_float<T>(row + i);
+}
+
+// RoPE on k, then the int8 KV write of one (KV head, token): the arithmetic of attention_head's
+// single-token write (set_kv_cache :859-920), one thread per head dim (128 threads)
+__global__ void __launch_bounds__(kAttnHeadDim) k_kv_write_rows(AttnArgs a, int start, int qkv_stride) {
+    constexpr int hd = kAttnHeadDim;
+    const int g = blockIdx.x, t = blockIdx.y;
+    const int pos = start + t;
+    if (pos < 0 || pos >= a.max_seq) return;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int half = a.rot / 2;
+    const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
+    const float* row = a.qkv + static_cast<long long>(t) * qkv_stride;
+    const float* kh = row + q_dim + g * hd;
+    float kval = kh[tid];
+    if (tid < 2 * half) {
+        const int i = tid < half ? tid : tid - half;
+        const float rc = a.cos_t[static_cast<long long>(pos) * half + i];
+        const float rs = a.sin_t[static_cast<long long>(pos) * half + i];
+        if (tid < half) kval = __fmaf_rn(kval, rc, -__fmul_rn(kh[tid + half], rs));
+        else kval = __fmaf_rn(kh[i], rs, __fmul_rn(kval, rc));
+    }
+    const float vval = row[q_dim + kv_dim + g * hd + tid];
+    __shared__ float red[2][2][2];  // [k|v][64-block][warp of block]
+    const float km = warp_max(fabsf(kval));
+    const float vm = warp_max(fabsf(vval));
+    if (lane == 0) {
+        red[0][tid >> 6][(tid >> 5) & 1] = km;
+        red[1][tid >> 6][(tid >> 5) & 1] = vm;
+    }
+    __syncthreads();
+    const int b = tid >> 6;
+    const float ka = fmaxf(red[0][b][0], red[0][b][1]);
+    const float va = fmaxf(red[1][b][0], red[1][b][1]);
+    const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
+    const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
+    int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
+    int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
+    qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
+    qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+    const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
+    a.kq[kb + tid] = static_cast<int8_t>(qk);
+    a.vq[kb + tid] = static_cast<int8_t>(qv);
+    if ((tid & 63) == 0) {
+        const long long sb = (static_cast<long long>(pos) * a.n_kv + g) * 2 + b;
+        a.ks[sb] = ksc;
+        a.vs[sb] = vsc;
+    }
+}
+
+// attention of every (query head, token) pair of the batch: grid (n_heads, n)
+__global__ void __launch_bounds__(kAttnWarps * 32) k_attention_rows(AttnArgs a, int start, int qkv_stride) {
+    __shared__ AttnSmem S;
+    const int t = blockIdx.y;
+    AttnArgs at = a;
+    at.qkv = a.qkv + static_cast<long long>(t) * qkv_stride;
+    at.out = a.out + static_cast<long long>(t) * a.n_heads * kAttnHeadDim;
+    attention_head<false, BlockSync, NoWait, true>(at, blockIdx.x, S, threadIdx.x, BlockSync(), NoWait(), start + t);
 }
 
 // decode step done: seq[pos + 1] = argmax token, pos += 1 (seq holds max_seq + 1 entries;

@@ -895,8 +895,15 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                 const long long row = unit * 4 + (lane >> 3);
                 if (finish && (lane & 7) == 0 && row < M) {
 #pragma unroll
-                    for (int t = 0; t < NT; ++t)
-                        if (t < ntok) ga.y[static_cast<long long>(t) * M + row] = vt[t];
+                    for (int t = 0; t < NT; ++t) {
+                        if (t < ntok) {
+                            const long long o = static_cast<long long>(t) * M + row;
+                            if constexpr (EPI == kEpiResid)
+                                ga.resid[o] = __fadd_rn(vt[t], __ldcg(ga.resid + o));  // token t's residual row
+                            else
+                                ga.y[o] = vt[t];
+                        }
+                    }
                 }
             } else {
                 const int q0 = (P == 1) ? 0 : pa.q_bounds[part];
@@ -971,7 +978,8 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
 // ---------------------------------------------------------------------------
 template <int FMT, int PRO, int EPI, int NT = 1>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
-    static_assert(NT == 1 || (EPI == kEpiStore && FMT != kFmtPacked), "multi-token: store epilogue, W4A8 formats");
+    static_assert(NT == 1 || ((EPI == kEpiStore || EPI == kEpiResid) && FMT != kFmtPacked),
+                  "multi-token: store or residual epilogue, W4A8 formats");
     using T = FmtTraits<FMT>;
     constexpr int NS = T::kStreams;
     constexpr int NSEG = (EPI == kEpiSilu) ? 2 : 1;

@@ -101,7 +101,46 @@ struct LaunchOpts {
     bool pdl = false;      // programmatic dependent launch attribute
     int row_bytes = 0;     // row-major block formats: bytes of one row
     int chunk_target = ASDSL_CHUNK_KB * 1024;  // bytes per pipeline stage (all segments and streams)
+    int k_parts = 0;       // K-split of every unit; 0 = the plan's own choice (plan_split)
 };
+
+// The chunk (units per pipeline stage) and K-split of launch_stream_gemv's plan for a GEMV of
+// n_units units of unit_stage bytes (all streams and segments), before shared memory bounds the
+// chunk.  The K-split fixes the order in which a row's slices are summed, so two launches that
+// must give bit-identical rows (a single-token GEMV and a multi-token one over the same weights)
+// pass the same k_parts.
+struct PlanSplit {
+    int grid;
+    long long cu;
+    int parts;
+};
+inline PlanSplit plan_split(long long n_units, long long unit_stage, int nseg, int rows_per_unit, int K,
+                            const LaunchOpts& opt) {
+    PlanSplit ps;
+    ps.grid = opt.max_ctas > 0 ? opt.max_ctas : sm_count() * launch_policy().ctas_per_sm;
+    if (ps.grid > n_units) ps.grid = static_cast<int>(n_units);
+    if (ps.grid < 1) ps.grid = 1;
+    const long long per_cta = (n_units + ps.grid - 1) / ps.grid;
+    // stage = chunk of `cu` units (all segments and streams): big bulk copies stream
+    // HBM best (>= 16 KB each), and every consumer warp shares every stage.
+    ps.cu = opt.chunk_target / (unit_stage > 0 ? unit_stage : 1);
+    if (ps.cu < 1) ps.cu = 1;
+    if (ps.cu > per_cta) ps.cu = per_cta;
+    // K-split so a chunk carries at least one work item per consumer warp
+    ps.parts = 1;
+    const int nq = K / 32;
+    if (rows_per_unit == 4 && nq % 32 == 0 && ps.cu * nseg < kConsumerWarps) {
+        // split K only when each part keeps >= 2 whole lane iterations (two slices in
+        // flight); short rows are cheaper unsplit than merged through shared memory
+        const int li = nq / 32;
+        for (int d = 2; d <= 8 && d <= li; ++d) {
+            if (li % d || li / d < 2) continue;
+            ps.parts = d;
+            if (ps.cu * nseg * d >= kConsumerWarps) break;
+        }
+    }
+    return ps;
+}
 
 // Plan one GEMV of a persistent multi-op kernel whose ring has n_slots fixed slots of
 // slot_bytes: the same chunking and K-split rules as launch_stream_gemv, with the chunk
@@ -179,31 +218,19 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
         ub_sum += in[i].unit_bytes;
     }
     const int nseg = pair_unit_off > 0 ? 2 : 1;
-    const int sms = sm_count();
     const LaunchPolicy pol = launch_policy();
-    int grid = opt.max_ctas > 0 ? opt.max_ctas : sms * pol.ctas_per_sm;
-    if (grid > n_units) grid = static_cast<int>(n_units);
-    const long long per_cta = (n_units + grid - 1) / grid;
-
-    // stage = chunk of `cu` units (all segments and streams): big bulk copies stream
-    // HBM best (>= 16 KB each), and every consumer warp shares every stage.
     const uint32_t xa = xarea_layout_bytes(ga.K, ga.gs, PRO == kProF32) * static_cast<uint32_t>(ga.n_tokens);
-    const long long unit_stage = ub_sum * nseg;
-    long long cu = opt.chunk_target / (unit_stage > 0 ? unit_stage : 1);
-    if (cu < 1) cu = 1;
-    if (cu > per_cta) cu = per_cta;
-    // K-split so a chunk carries at least one work item per consumer warp
-    int parts = 1;
+    const PlanSplit ps = plan_split(n_units, ub_sum * nseg, nseg, FmtTraits<FMT>::kRowsPerUnit, ga.K, opt);
+    const int grid = ps.grid;
+    long long cu = ps.cu;
+    int parts = ps.parts;
     const int nq = ga.K / 32;
-    if (FmtTraits<FMT>::kRowsPerUnit == 4 && nq % 32 == 0 && cu * nseg < kConsumerWarps) {
-        // split K only when each part keeps >= 2 whole lane iterations (two slices in
-        // flight); short rows are cheaper unsplit than merged through shared memory
-        const int li = nq / 32;
-        for (int d = 2; d <= 8 && d <= li; ++d) {
-            if (li % d || li / d < 2) continue;
-            parts = d;
-            if (cu * nseg * d >= kConsumerWarps) break;
-        }
+    if (opt.k_parts > 0) {
+        // a forced split must cut K into parts of whole lane iterations (32 slices)
+        if (opt.k_parts > 1 &&
+            (opt.k_parts > 8 || nq % (32 * opt.k_parts) != 0 || FmtTraits<FMT>::kRowsPerUnit != 4))
+            return set_error(kEinval, "internal: K-split does not divide in_features");
+        parts = opt.k_parts;
     }
     const int ipu = parts * nseg;
     uint32_t seg_bytes = 0, stage_bytes = 0, split_bytes = 0;

@@ -197,7 +197,8 @@ def run_reference(args, host, bytes_per_step):
 DECODE_METRIC = "Q4 decode tokens/sec at batch 1 (Phi-4-mini shape, C0 preq2 gs32)"
 
 
-def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: bool = True, world: int = 1) -> dict:
+def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: bool = True, world: int = 1,
+                 prefill_tokens: int = 128) -> dict:
     """Tokens/s of the engine's greedy decode on the full Phi-4-mini shape (
     32 layers, all projections preq2 gs32, tied fp16 embedding quantized on the device into the
     lm_head, norms 1.0, int8 KV), random-init weights from `seed`.
@@ -291,6 +292,23 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         assert len(toks) == steps + 1
+        # prompt prefill through the public API, prefill_tokens seeded prompt tokens from position 0:
+        # serial = generate(prompt, 0) (one prefill-graph replay per token, no lm_head); batched =
+        # forward_batch(prompt, 0) (passes of up to 16 tokens per weight read, plus the last
+        # token's lm_head and its logits copied to the host)
+        # (1 GPU only: a side figure, not timed across ranks)
+        prompt = np.random.default_rng(seed).integers(0, c["vocab"], size=prefill_tokens).tolist()
+        pre = {}
+        calls = (("serial", lambda: eng.generate(prompt, 0)), ("batched", lambda: eng.forward_batch(prompt, 0)))
+        for name, call in calls if world == 1 and prefill_tokens > 0 else ():
+            eng.reset_session()
+            call()  # warm (first use allocates the batch activation blocks)
+            eng.reset_session()
+            f0.record(stream)
+            call()
+            f1.record(stream)
+            f1.synchronize()
+            pre[name] = f0.elapsed_time(f1)
         assert _lib.device_status(clear=True) == 0
     finally:
         eng.close()
@@ -314,6 +332,12 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
                 "d2h_bytes_per_step": 4, "ms_total": round(e2e_ms, 3)},
         "gpu_launches": steps * (3 + 5 * c["num_layers"]),
         "gate_logits_rel_err": gate_err,
+        "prefill": ({"tokens": prefill_tokens, "serial_ms": round(pre["serial"], 3),
+                     "batched_ms": round(pre["batched"], 3),
+                     "batched_tokens_per_s": round(prefill_tokens / (pre["batched"] * 1e-3), 1),
+                     "serial_tokens_per_s": round(prefill_tokens / (pre["serial"] * 1e-3), 1),
+                     "note": "public API calls timed by events on the engine stream; batched rows are "
+                             "bit-identical to serial forward_token"} if pre else None),
     }
 
 

@@ -298,6 +298,15 @@ int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, fl
  * -> ASDSL_B200_ERANGE before any step runs. */
 int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
                                      float* out_logits);
+/* forward_batch (unified_engine.cpp:1117; pybind forward_batch :2526-2534 with all_logits = 0, and
+ * forward_verify_batch_raw_all_logits :2613-2625 with all_logits = 1): tokens[i] at position
+ * start_pos + i for i < n, passes of up to 16 tokens, each sharing one weight read per projection
+ * (multi-token GEMVs).  out_logits (host or device; may be NULL) receives the last token's vocab
+ * logits, or n x vocab rows when all_logits != 0.  Logits and KV cache are bit-identical to n
+ * forward_token calls of the per-op decode chain (the reference's batched GEMM path is not: its
+ * binding documents that it may diverge).  Ranges as forward_verify. */
+int asdsl_b200_engine_forward_batch(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
+                                    float* out_logits, int all_logits);
 /* generate / generate_with_stops (unified_engine.cpp:1717-1764): out = prompt + generated tokens
  * (the stop token included), *n_out its length; out_cap >= n_prompt + max_tokens + 1. */
 int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int n_prompt, int max_tokens,

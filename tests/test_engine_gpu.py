@@ -340,3 +340,70 @@ def test_engine_verify_all_logits(native, tiny):
     finally:
         eng.close()
     assert native.device_status(clear=True) == 0
+
+
+_KV = ("kq", "vq", "ks", "vs")
+
+
+@pytest.mark.parametrize("n", [1, 2, 5, 16, 23])
+def test_engine_forward_batch_bit_identical(native, small, n):
+    """forward_batch / forward_verify_batch_raw_all_logits (UnifiedEngine::forward_batch,
+    unified_engine.cpp:1117; pybind :2526-2534, :2613-2625): every logits row and the whole int8
+    KV cache equal n forward_token calls bit for bit -- from a mid-session start, across passes of
+    up to 16 tokens (n = 23), and with the prefix itself forwarded as a batch."""
+    c = small["config"]
+    V = c["vocab"]
+    toks = np.random.default_rng(100 + n).integers(0, V, size=n).tolist()
+    prefix = [7, 1, 300]
+    eng = _engine(small)
+    try:
+        for i, t in enumerate(prefix):
+            eng.forward_token_prefill(t, i)
+        rows = eng.forward_verify_serial_all_logits(toks, len(prefix)).reshape(n, V)
+        kv = {b: eng.read_buffer(b).copy() for b in _KV}
+        eng.reset_session()
+        assert eng.forward_batch(prefix, 0).shape == (V,)
+        batch = eng.forward_verify_batch_raw_all_logits(toks, len(prefix)).reshape(n, V)
+        assert eng.get_kv_seq_len() == len(prefix) + n
+        assert np.array_equal(batch, rows)
+        for b in _KV:
+            assert np.array_equal(eng.read_buffer(b), kv[b]), b
+        # the last-token form, after truncating back to the prefix
+        eng.truncate_kv(len(prefix))
+        assert np.array_equal(eng.forward_batch(toks, len(prefix)), rows[-1])
+        for b in _KV:
+            assert np.array_equal(eng.read_buffer(b), kv[b]), b
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("lm_gs", [32, 128])
+def test_engine_forward_batch_phi4_dims(native, lm_gs):
+    """forward_batch at full Phi-4-mini dimensions (one layer, vocab 200064): 20 prompt tokens in
+    passes bounded by the MLP input's A8 areas, all logits rows and the KV cache bit-identical to
+    forward_token; the next decode step after a batched prefill equals the serial one."""
+    from asdsl_b200.inference.synthetic import PHI4_MINI, build_model
+
+    model = build_model(dict(PHI4_MINI, num_layers=1, max_seq=64), seed=5, norms_one=False)
+    c = model["config"]
+    V = c["vocab"]
+    toks = np.random.default_rng(7).integers(0, V, size=20).tolist()
+    eng = _engine(model, lm_head_group_size=lm_gs)
+    try:
+        rows = eng.forward_verify_serial_all_logits(toks, 0).reshape(20, V)
+        nxt = eng.forward_token(int(np.argmax(rows[-1])), 20).copy()
+        kv = {b: eng.read_buffer(b).copy() for b in _KV}
+        eng.reset_session()
+        batch = eng.forward_verify_batch_raw_all_logits(toks, 0).reshape(20, V)
+        assert np.array_equal(batch, rows)
+        assert np.array_equal(eng.forward_token(int(np.argmax(batch[-1])), 20), nxt)
+        for b in _KV:
+            assert np.array_equal(eng.read_buffer(b), kv[b]), b
+        with pytest.raises(IndexError):
+            eng.forward_batch([1, V], 0)
+        with pytest.raises(IndexError):
+            eng.forward_batch([1, 2, 3], c["max_seq"] - 2)
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0
