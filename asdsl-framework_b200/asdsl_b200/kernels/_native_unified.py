@@ -115,6 +115,9 @@ class UnifiedEngine:
             raise
         self._logits = np.empty(config.vocab_size, dtype=np.float32)
         self._vocab = int(config.vocab_size)
+        # decode mode as the engine resolved it (asdsl_b200_engine_create reads the same variable)
+        self._persistent = bool(persistent) if persistent is not None else \
+            os.environ.get("ASDSL_B200_DECODE_KERNEL") == "persistent"
 
     # ------------------------------------------------------------------ construction
     def _load(self, cfg, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict, lm_meta,
@@ -243,9 +246,13 @@ class UnifiedEngine:
 
     def forward_batch_all_logits(self, prompt, start_pos: int) -> np.ndarray:
         """Speculative-verify logits (:2591-2600).  The reference's forward_verify_batch takes the
-        serial per-token path whenever preq2 weights are in use (unified_engine.cpp:1783-1787), so
-        the result equals forward_verify_serial_all_logits (forward_token numerics, lossless PLD)."""
-        return self.forward_verify_serial_all_logits(prompt, start_pos)
+        serial per-token path whenever preq2 weights are in use (unified_engine.cpp:1783-1787) so
+        that PLD stays lossless: the result must equal forward_verify_serial_all_logits.  Here the
+        batched forward gives those rows bit for bit with one weight read per pass, so it runs that
+        (the persistent-kernel mode, whose K-splits differ, keeps the serial replays)."""
+        if self._persistent:
+            return self.forward_verify_serial_all_logits(prompt, start_pos)
+        return self.forward_verify_batch_raw_all_logits(prompt, start_pos)
 
     def forward_batch(self, prompt, start_pos: int) -> np.ndarray:
         """prompt[i] at position start_pos + i, up to 16 tokens per weight read (:2526-2534 over

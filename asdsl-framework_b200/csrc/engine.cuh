@@ -574,6 +574,16 @@ int eng_gemv_rows_fmt(const StreamIn* in, long long nb, GemvArgs ga, int T, cons
     return launch_stream_gemv<FMT, PRO, EPI, 16>(in, 2, nb, 0, ga, s, o);
 }
 
+// rows of one multi-token GEMV over K inputs: at most 16, and their A8 areas within a token
+// scratch slot (10 for K = 8192)
+int eng_rows_cap(int K) {
+    const uint32_t xa = std::max(xarea_layout_bytes(K, 32, false), xarea_layout_bytes(K, 128, false));
+    const int cap = static_cast<int>(kTokSlotBytes / xa);
+    return cap > 16 ? 16 : (cap < 1 ? 1 : cap);
+}
+
+// T token rows through projection p with the K-split `parts`, in the fewest equal sub-passes
+// that fit eng_rows_cap (row t: x + t K, y / resid + t M)
 template <int PRO, int EPI>
 int eng_gemv_rows(const EngProj& p, GemvArgs ga, int T, int parts, cudaStream_t s) {
     StreamIn in[2];
@@ -581,28 +591,26 @@ int eng_gemv_rows(const EngProj& p, GemvArgs ga, int T, int parts, cudaStream_t 
     LaunchOpts o;
     o.k_parts = parts;
     const long long nb = (static_cast<long long>(p.rows) + 3) / 4;
-    if (p.fmt == ASDSL_B200_FMT_PREQ2) return eng_gemv_rows_fmt<kFmtPreq2, PRO, EPI>(in, nb, ga, T, o, s);
-    return eng_gemv_rows_fmt<kFmtQ128B, PRO, EPI>(in, nb, ga, T, o, s);
-}
-
-// tokens per pass: at most 16, and the A8 areas of every projection's input within a token
-// scratch slot
-int eng_batch_cap(const asdsl_b200_engine_config& c) {
-    const int qd = c.num_heads * c.head_dim;
-    const int ks[3] = {c.hidden_size, qd, c.intermediate_size};
-    int cap = 16;
-    for (int k : ks) {
-        const int per = static_cast<int>(kTokSlotBytes / xarea_layout_bytes(k, 32, false));
-        const int per128 = static_cast<int>(kTokSlotBytes / xarea_layout_bytes(k, 128, false));
-        cap = std::min(cap, std::min(per, per128));
+    const int cap = eng_rows_cap(ga.K);
+    const int n_sub = (T + cap - 1) / cap;
+    const int per = (T + n_sub - 1) / n_sub;
+    for (int t0 = 0; t0 < T; t0 += per) {
+        GemvArgs g = ga;
+        const int n = std::min(per, T - t0);
+        g.x = ga.x + static_cast<long long>(t0) * ga.K;
+        if (ga.y) g.y = ga.y + static_cast<long long>(t0) * ga.M;
+        if (ga.resid) g.resid = ga.resid + static_cast<long long>(t0) * ga.M;
+        const int rc = p.fmt == ASDSL_B200_FMT_PREQ2 ? eng_gemv_rows_fmt<kFmtPreq2, PRO, EPI>(in, nb, g, n, o, s)
+                                                      : eng_gemv_rows_fmt<kFmtQ128B, PRO, EPI>(in, nb, g, n, o, s);
+        if (rc) return rc;
     }
-    return cap < 1 ? 1 : cap;
+    return kOk;
 }
 
 int eng_batch_alloc(asdsl_b200_engine* e) {
     if (e->batch_rows > 0) return kOk;
     const asdsl_b200_engine_config& c = e->cfg;
-    const size_t B = static_cast<size_t>(eng_batch_cap(c));
+    const size_t B = 16;  // tokens per pass; a projection whose input is wider takes sub-passes
     const size_t qd = static_cast<size_t>(c.num_heads) * c.head_dim, kvd = static_cast<size_t>(c.num_kv_heads) * c.head_dim;
     const size_t H = c.hidden_size, I = c.intermediate_size;
     if (int rc = eng_alloc(e, &e->b_resid, 4 * B * H)) return rc;
@@ -1146,8 +1154,20 @@ int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int 
     DeviceGuard dg(e->device);
     ASDSL_CUDA(cudaStreamSynchronize(e->stream));
     ASDSL_CUDA(cudaMemcpyAsync(e->seq, prompt, 4ull * n_prompt, cudaMemcpyHostToDevice, e->stream));
-    if (int rc = eng_set_pos(e, 0, -1)) return rc;
-    for (int i = 0; i + 1 < n_prompt; ++i) ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+    // prompt tokens before the last one: batched passes (bit-identical to the per-op chain's
+    // prefill graph); the persistent-kernel mode keeps its own prefill graph
+    const int n_pre = n_prompt - 1;
+    if (n_pre > 0 && !e->persistent) {
+        if (int rc = eng_batch_alloc(e)) return rc;
+        for (int t0 = 0; t0 < n_pre; t0 += e->batch_rows) {
+            const int T = std::min(e->batch_rows, n_pre - t0);
+            if (int rc = eng_batch_pass(e, e->seq + t0, T, t0, nullptr, false)) return rc;
+        }
+        if (int rc = eng_set_pos(e, n_pre, -1)) return rc;
+    } else {
+        if (int rc = eng_set_pos(e, 0, -1)) return rc;
+        for (int i = 0; i + 1 < n_prompt; ++i) ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+    }
     // the last prompt token's forward is the first decode step; without one it is a prefill step
     if (producible == 0) ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
     int produced = 0, stop_at = -1;

@@ -292,23 +292,40 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         assert len(toks) == steps + 1
-        # prompt prefill through the public API, prefill_tokens seeded prompt tokens from position 0:
-        # serial = generate(prompt, 0) (one prefill-graph replay per token, no lm_head); batched =
-        # forward_batch(prompt, 0) (passes of up to 16 tokens per weight read, plus the last
-        # token's lm_head and its logits copied to the host)
-        # (1 GPU only: a side figure, not timed across ranks)
+        # prompt prefill and speculative verify through the public API (1 GPU only: side figures,
+        # not timed across ranks), events on the engine stream around each call:
+        #   prefill: prefill_tokens seeded tokens from position 0, serial = forward_token_prefill per
+        #     token (one prefill-graph replay each), batched = forward_batch (passes of 16 tokens,
+        #     plus the last token's lm_head and logits);
+        #   verify: 8 draft tokens after that prompt, all logits to the host, serial =
+        #     forward_verify_serial_all_logits, batched = forward_batch_all_logits.
         prompt = np.random.default_rng(seed).integers(0, c["vocab"], size=prefill_tokens).tolist()
+        draft = np.random.default_rng(seed + 1).integers(0, c["vocab"], size=8).tolist()
+
+        def serial_prefill():
+            for i, t in enumerate(prompt):
+                eng.forward_token_prefill(t, i)
+
         pre = {}
-        calls = (("serial", lambda: eng.generate(prompt, 0)), ("batched", lambda: eng.forward_batch(prompt, 0)))
-        for name, call in calls if world == 1 and prefill_tokens > 0 else ():
-            eng.reset_session()
-            call()  # warm (first use allocates the batch activation blocks)
-            eng.reset_session()
-            f0.record(stream)
-            call()
-            f1.record(stream)
-            f1.synchronize()
+        calls = (("prefill_serial", serial_prefill, False), ("prefill_batched", lambda: eng.forward_batch(prompt, 0), False),
+                 ("verify_serial", lambda: eng.forward_verify_serial_all_logits(draft, prefill_tokens), True),
+                 ("verify_batched", lambda: eng.forward_batch_all_logits(draft, prefill_tokens), True))
+        rows = {}
+        for name, call, after_prompt in calls if world == 1 and prefill_tokens > 0 else ():
+            for rep in range(2):  # the first call warms (the batch blocks are allocated on first use)
+                eng.reset_session()
+                if after_prompt:
+                    eng.forward_batch(prompt, 0)
+                torch.cuda.synchronize()
+                f0.record(stream)
+                out = call()
+                f1.record(stream)
+                f1.synchronize()
             pre[name] = f0.elapsed_time(f1)
+            if after_prompt:
+                rows[name] = out
+        if rows and not np.array_equal(rows["verify_serial"], rows["verify_batched"]):
+            raise SystemExit("bench: batched verify rows differ from serial forward_token rows")
         assert _lib.device_status(clear=True) == 0
     finally:
         eng.close()
@@ -332,12 +349,15 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
                 "d2h_bytes_per_step": 4, "ms_total": round(e2e_ms, 3)},
         "gpu_launches": steps * (3 + 5 * c["num_layers"]),
         "gate_logits_rel_err": gate_err,
-        "prefill": ({"tokens": prefill_tokens, "serial_ms": round(pre["serial"], 3),
-                     "batched_ms": round(pre["batched"], 3),
-                     "batched_tokens_per_s": round(prefill_tokens / (pre["batched"] * 1e-3), 1),
-                     "serial_tokens_per_s": round(prefill_tokens / (pre["serial"] * 1e-3), 1),
+        "prefill": ({"tokens": prefill_tokens, "serial_ms": round(pre["prefill_serial"], 3),
+                     "batched_ms": round(pre["prefill_batched"], 3),
+                     "serial_tokens_per_s": round(prefill_tokens / (pre["prefill_serial"] * 1e-3), 1),
+                     "batched_tokens_per_s": round(prefill_tokens / (pre["prefill_batched"] * 1e-3), 1),
+                     "verify_8_serial_ms": round(pre["verify_serial"], 3),
+                     "verify_8_batched_ms": round(pre["verify_batched"], 3),
                      "note": "public API calls timed by events on the engine stream; batched rows are "
-                             "bit-identical to serial forward_token"} if pre else None),
+                             "bit-identical to serial forward_token (checked here for the verify rows)"}
+                    if pre else None),
     }
 
 

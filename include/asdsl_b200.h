@@ -308,7 +308,9 @@ int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens
 int asdsl_b200_engine_forward_batch(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
                                     float* out_logits, int all_logits);
 /* generate / generate_with_stops (unified_engine.cpp:1717-1764): out = prompt + generated tokens
- * (the stop token included), *n_out its length; out_cap >= n_prompt + max_tokens + 1. */
+ * (the stop token included), *n_out its length; out_cap >= n_prompt + max_tokens + 1.  The prompt
+ * tokens but the last are forwarded in batched passes (the forward_batch arithmetic, bit-identical
+ * to per-token forwards), the rest one decode-graph replay per token. */
 int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int n_prompt, int max_tokens,
                                const int32_t* stops, int n_stops, int32_t* out, int out_cap, int* n_out);
 /* reset_session / get_kv_seq_len / truncate_kv / snapshot_kv / restore_kv (unified_engine.cpp:1285-1337). */

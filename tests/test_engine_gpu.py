@@ -407,3 +407,67 @@ def test_engine_forward_batch_phi4_dims(native, lm_gs):
     finally:
         eng.close()
     assert native.device_status(clear=True) == 0
+
+
+def test_engine_generate_batched_prefill_matches_serial(native, small):
+    """generate() forwards all prompt tokens but the last in batched passes: the tokens it
+    produces and the KV cache it leaves equal forward_token_prefill over the prompt followed by
+    greedy forward_token_argmax steps (unified_engine.cpp:1717-1764), across a 16-token pass
+    boundary; with stop tokens too."""
+    c = small["config"]
+    prompt = np.random.default_rng(9).integers(0, c["vocab"], size=21).tolist()
+    eng = _engine(small)
+    try:
+        toks = eng.generate(prompt, 10)
+        kv = {b: eng.read_buffer(b).copy() for b in _KV}
+        eng.reset_session()
+        for i, t in enumerate(prompt[:-1]):
+            eng.forward_token_prefill(t, i)
+        seq, t, pos = list(prompt), prompt[-1], len(prompt) - 1
+        for _ in range(10):
+            t = eng.forward_token_argmax(t, pos)
+            seq.append(t)
+            pos += 1
+        eng.forward_token_prefill(t, pos)  # generate also forwards its last token (KV only)
+        assert toks == seq
+        for b in _KV:
+            assert np.array_equal(eng.read_buffer(b), kv[b]), b
+        eng.reset_session()
+        stop = seq[len(prompt) + 4]
+        assert eng.generate_with_stops(prompt, 10, [stop]) == seq[: seq.index(stop, len(prompt)) + 1]
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0
+
+
+def test_engine_forward_batch_q4_128_projections(native, small, monkeypatch):
+    """The C0.1 / C0.3 formats (ASDSL_C01, ASDSL_C03: every projection Q4_128 at gs 128,
+    unified_engine.cpp:1404-1410, :1532-1538): the batched forward's rows and KV cache equal
+    forward_token's bit for bit on the banded Q4_128 device layout too."""
+    from asdsl_b200.quantization.synth import random_q4_128
+
+    c = small["config"]
+    V = c["vocab"]
+    rng = np.random.default_rng(21)
+    model = dict(small)
+    model["layers"] = [dict(L) for L in small["layers"]]
+    qd, kvd, H, I = c["n_heads"] * c["head_dim"], c["n_kv_heads"] * c["head_dim"], c["hidden"], c["inter"]
+    shapes = {"qkv_proj": (qd + 2 * kvd, H), "o_proj": (H, qd), "gate_up_proj": (2 * I, H), "down_proj": (H, I)}
+    for L in model["layers"]:
+        for name, (rows, cols) in shapes.items():
+            L[f"{name}_g128"] = random_q4_128(rng, rows, cols)
+    monkeypatch.setenv("ASDSL_C01", "1")
+    monkeypatch.setenv("ASDSL_C03", "1")
+    toks = np.random.default_rng(22).integers(0, V, size=19).tolist()
+    eng = _engine(model)
+    try:
+        rows_s = eng.forward_verify_serial_all_logits(toks, 0).reshape(len(toks), V)
+        kv = {b: eng.read_buffer(b).copy() for b in _KV}
+        eng.reset_session()
+        rows_b = eng.forward_batch_all_logits(toks, 0).reshape(len(toks), V)
+        assert np.array_equal(rows_b, rows_s)
+        for b in _KV:
+            assert np.array_equal(eng.read_buffer(b), kv[b]), b
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0
