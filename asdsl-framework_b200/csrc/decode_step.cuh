@@ -139,6 +139,7 @@ __device__ void step_gemv(const StepOp& op, const StepArgs& A, uint8_t* smem, ui
     run_prologue<PRO, true>(ga, xa, threadIdx.x);
     XAddr xad;
     xad.x8 = smem_u32(xa.x8);
+    xad.x8b = xad.x8 + static_cast<uint32_t>(ga.K >> 1);
     xad.xs = smem_u32(xa.xs);
     xad.xss = smem_u32(xa.xss);
     xad.xsi = smem_u32(xa.xsi);

@@ -217,8 +217,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream_gemv_mma(const PipeArgs 
             const int tb = oct * 8 + g;
             const int tc0 = oct * 8 + 2 * tq, tc1 = tc0 + 1;
             const bool vb = tb < ntok;
+            // bytes 8 tq .. 8 tq + 7 of each slice's permuted codes: plane A (tq 0, 1) or B (tq 2, 3)
             const uint32_t xb = xbase + static_cast<uint32_t>(vb ? tb : 0) * xa_stride +
-                                static_cast<uint32_t>(q0) * 32u + static_cast<uint32_t>(tq) * 8u;
+                                (tq >= 2 ? static_cast<uint32_t>(K >> 1) : 0u) + static_cast<uint32_t>(q0) * 16u +
+                                static_cast<uint32_t>(tq & 1) * 8u;
             const uint32_t xc0 = xbase + static_cast<uint32_t>(tc0 < ntok ? tc0 : 0) * xa_stride + xs_off;
             const uint32_t xc1 = xbase + static_cast<uint32_t>(tc1 < ntok ? tc1 : 0) * xa_stride + xs_off;
             // operands of one group, loaded one group ahead of the MMA that uses them (the
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_stream_gemv_mma(const PipeArgs 
                 const uint32_t dq = static_cast<uint32_t>(q - q0);
                 d.wa = ra.word_at(q, dq);
                 d.wb = rb.word_at(q, dq);
-                d.b = vb ? lds64(xb + dq * 32u) : make_uint2(0u, 0u);
+                d.b = vb ? lds64(xb + dq * 16u) : make_uint2(0u, 0u);
                 const uint32_t qo = 4u * static_cast<uint32_t>(q);
                 d.xs0 = ldsf(xc0 + qo);
                 d.xs1 = ldsf(xc1 + qo);

@@ -71,6 +71,10 @@ enum Epilogue : int {
 #endif
 constexpr int kConsumerWarps = ASDSL_CONSUMER_WARPS;
 constexpr int kCtasPerSm = ASDSL_CTAS_PER_SM;
+#ifndef ASDSL_MT_GROUP
+// multi-token GEMVs: activation rows per weight-slice load (each group keeps 4 x rows accumulators)
+#define ASDSL_MT_GROUP 4
+#endif
 constexpr int kThreads = 32 * (kConsumerWarps + 1);  // + one producer warp
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
@@ -173,7 +177,9 @@ __device__ __forceinline__ uint32_t chunk_off16(const StreamDesc& sd, long long 
 
 // ---------------------------------------------------------------------------
 // shared-memory activation area
-//   x8[K]      int8 codes, permuted per 32-slice (see x8_perm_offset)
+//   x8[K]      int8 codes, permuted per 32-slice, in two planes of K/2 bytes: plane A holds bytes
+//              0-15 of every slice's 32 permuted codes, plane B bytes 16-31, so the 16-byte loads of
+//              32 lanes on 32 consecutive slices hit every bank once (no 2-way conflict)
 //   xs[K/32]   A8 scale of each 32-slice's group (replicated for gs 128)
 //   xss[K/32]  (float)sum(codes of the slice) * xs
 //   xsi[K/32]  sum(codes of the slice)
@@ -192,7 +198,7 @@ struct XArea {
 
 // the same area as 32-bit shared-window addresses (for explicit ld.shared)
 struct XAddr {
-    uint32_t x8, xs, xss, xsi;
+    uint32_t x8, x8b, xs, xss, xsi;  // x8b: plane B of the codes (x8 + K/2)
 };
 
 __host__ __device__ __forceinline__ uint32_t xarea_layout_bytes(int K, int gs, bool f32) {
@@ -378,8 +384,9 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
             }
             if (live) {
                 // quad (4 consecutive elements, first one even) -> even word gets c0, c2 and the odd
-                // word c1, c3 at byte (e0 & 7) / 2 (see x8_perm_offset)
-                const int w8 = (e0 & ~31) + ((e0 & 31) >> 3) * 8 + ((e0 & 7) >> 1);
+                // word c1, c3 at byte (e0 & 7) / 2 of the 8-byte pair of its 8 elements; the pairs of
+                // elements 0-15 of a slice go to plane A, those of 16-31 to plane B
+                const int w8 = ((e0 & 16) ? (ga.K >> 1) : 0) + (e0 >> 5) * 16 + ((e0 & 15) >> 3) * 8 + ((e0 & 7) >> 1);
                 *reinterpret_cast<uint16_t*>(xa.x8 + w8) =
                     static_cast<uint16_t>((c[0] & 0xFF) | ((c[2] & 0xFF) << 8));
                 *reinterpret_cast<uint16_t*>(xa.x8 + w8 + 4) =
@@ -459,9 +466,8 @@ struct SliceData {
 template <int FMT>
 __device__ __forceinline__ void slice_load_x(SliceData& d, const XAddr& xs, int q) {
     const uint32_t uq = static_cast<uint32_t>(q);
-    const uint32_t xr = xs.x8 + uq * 32u;
-    d.xa = lds128(xr);
-    d.xb = lds128(xr + 16);
+    d.xa = lds128(xs.x8 + uq * 16u);
+    d.xb = lds128(xs.x8b + uq * 16u);
     d.xs = ldsf(xs.xs + 4u * uq);
     d.xss = ldsf(xs.xss + 4u * uq);
     if constexpr (FMT == kFmtQ4K) d.xsi = static_cast<int>(lds32(xs.xsi + 4u * uq));
@@ -828,24 +834,26 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                                         static_cast<uint32_t>((rot + 2) & 3), static_cast<uint32_t>((rot + 3) & 3)};
                 const int ntok = ga.n_tokens;
                 float vt[NT];
-                // tokens in groups of four: each slice's weights are loaded once per group
+                // tokens in groups of TG: each slice's weights are loaded once per group
+                constexpr int TG = NT < ASDSL_MT_GROUP ? NT : ASDSL_MT_GROUP;
 #pragma unroll
-                for (int t0 = 0; t0 < NT; t0 += 4) {
+                for (int t0 = 0; t0 < NT; t0 += TG) {
                     if (t0 >= ntok) continue;
-                    float a4[4][4];
+                    float a4[TG][4];
 #pragma unroll
-                    for (int tt = 0; tt < 4; ++tt)
+                    for (int tt = 0; tt < TG; ++tt)
 #pragma unroll
                         for (int r = 0; r < 4; ++r) a4[tt][r] = 0.0f;
                     for (int q = q0 + lane; q < q1; q += 32) {
                         SliceData d;
                         slice_load_w<FMT>(d, p0, p1, nq, pa.row_bytes, rr, q);
 #pragma unroll
-                        for (int tt = 0; tt < 4; ++tt) {
+                        for (int tt = 0; tt < TG; ++tt) {
                             if (t0 + tt < ntok) {
                                 const uint32_t off = static_cast<uint32_t>(t0 + tt) * xa_stride;
                                 XAddr xt;
                                 xt.x8 = xad.x8 + off;
+                                xt.x8b = xad.x8b + off;
                                 xt.xs = xad.xs + off;
                                 xt.xss = xad.xss + off;
                                 xt.xsi = xad.xsi + off;
@@ -855,7 +863,7 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                         }
                     }
 #pragma unroll
-                    for (int tt = 0; tt < 4; ++tt) {
+                    for (int tt = 0; tt < TG; ++tt) {
                         if (t0 + tt < NT) {
                             unrotate(a4[tt], rot);
                             vt[t0 + tt] = reduce4(a4[tt], lane);
@@ -1038,6 +1046,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
 
     XAddr xad;
     xad.x8 = kF32 ? 0u : smem_u32(xa.x8);
+    xad.x8b = kF32 ? 0u : xad.x8 + static_cast<uint32_t>(ga.K >> 1);
     xad.xs = kF32 ? 0u : smem_u32(xa.xs);
     xad.xss = kF32 ? 0u : smem_u32(xa.xss);
     xad.xsi = kF32 ? 0u : smem_u32(xa.xsi);
