@@ -77,6 +77,7 @@ _SIGS = {
     "asdsl_b200_engine_forward_token": [_P, _I, _I, _P, _P],
     "asdsl_b200_engine_forward_verify": [_P, _P, _I, _I, _P],
     "asdsl_b200_engine_forward_batch": [_P, _P, _I, _I, _P, _I],
+    "asdsl_b200_gemm_q4_128_f32": [_P, _P, _P, _I, _I, _I, _I, _P],
     "asdsl_b200_engine_generate": [_P, _P, _I, _I, _P, _I, _P, _I, _P],
     "asdsl_b200_engine_reset_session": [_P],
     "asdsl_b200_engine_get_kv_seq_len": [_P, _P],

@@ -122,6 +122,25 @@ def gemv_q4_128_preq_avx2(blocks, x_q8, x_scales, y, out_features: int, in_featu
     _writeback(y, yd)
 
 
+def gemm_q4_128_q8_avx2(blocks, x_batch, y_batch, out_features: int, in_features: int, group_size: int,
+                        batch_size: int) -> None:
+    """Batched prompt GEMM on fp32 activations (gemm_q4_128_q8_avx2, gemv_q4_128.cpp:262-306):
+    y_batch[b][out] = W . x_batch[b] for b < min(batch_size, 64), bit-identical to the reference;
+    rows b >= 64 of y_batch keep their values.  group_size != 128 raises ValueError."""
+    if group_size != 128:
+        raise ValueError("gemm_q4_128_q8_avx2: group_size must be 128")
+    b = dv.to_device(blocks, np.uint8)
+    xd = dv.to_device(x_batch, np.float32)
+    n = int(batch_size) * int(out_features)
+    if dv.is_cuda_tensor(y_batch) and y_batch.is_contiguous() and y_batch.numel() >= n:
+        yd = y_batch
+    else:
+        yd = dv.to_device(y_batch, np.float32)  # rows the GEMM leaves alone keep the caller's values
+    _lib.call("asdsl_b200_gemm_q4_128_f32", b.data_ptr(), xd.data_ptr(), yd.data_ptr(), int(out_features),
+              int(in_features), int(group_size), int(batch_size), dv.stream_ptr())
+    _writeback(y_batch, yd)
+
+
 def gemv_q4_s256_preq_avx2(blocks, x_q8, x_scales, y, out_features: int, in_features: int,
                            group_size: int = 32) -> None:
     b = dv.to_device(blocks, np.uint8)

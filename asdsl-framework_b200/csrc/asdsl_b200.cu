@@ -8,6 +8,7 @@
 #include "launch.cuh"
 #include "weight_prep.cuh"
 #include "gemv_mma.cuh"
+#include "gemm_q4_128.cuh"
 
 using namespace asdsl;
 
@@ -247,6 +248,34 @@ int asdsl_b200_gemv_q4_128(const uint8_t* blocks, const int8_t* xq, const float*
     ga.y = y;
     return launch_stream_gemv<kFmtQ4_128, kProQ8, kEpiStore>(s, 1, (M + 3) / 4, 0, ga, as_stream(stream),
                                                              rows_opt(ng * 66));
+}
+
+int asdsl_b200_gemm_q4_128_f32(const uint8_t* blocks, const float* X, float* Y, int M, int K, int gs, int batch,
+                               void* stream) {
+    if (gs != 128) return set_error(kEinval, "gemm_q4_128_q8_avx2: group_size must be 128");
+    if (!blocks || !X || !Y) return set_error(kEinval, "gemm_q4_128_q8_avx2: null pointer");
+    if (K <= 0 || K % 128) return set_error(kEinval, "gemm_q4_128_q8_avx2: in_features must be divisible by 128");
+    if (M < 0 || batch < 0) return set_error(kEinval, "gemm_q4_128_q8_avx2: invalid dimensions");
+    if (reinterpret_cast<uintptr_t>(blocks) & 1u) return set_error(kEinval, "gemm_q4_128_q8_avx2: blocks must be 2-byte aligned");
+    if (!aligned16(X)) return set_error(kEinval, "gemm_q4_128_q8_avx2: activations must be 16-byte aligned");
+    const int B = batch < asdsl::kGemmMaxBatch ? batch : asdsl::kGemmMaxBatch;  // the reference stops at 64
+    if (M == 0 || B == 0) return kOk;
+    static std::mutex mu;
+    static bool configured[64] = {false};
+    int dev = 0;
+    ASDSL_CUDA(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev >= 0 && dev < 64 && !configured[dev]) {
+            ASDSL_CUDA(cudaFuncSetAttribute(asdsl::k_gemm_q4_128_f32, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(asdsl::kGemmSmem)));
+            configured[dev] = true;
+        }
+    }
+    const unsigned grid = static_cast<unsigned>((M + asdsl::kGemmRows - 1) / asdsl::kGemmRows);
+    asdsl::k_gemm_q4_128_f32<<<grid, 256, asdsl::kGemmSmem, as_stream(stream)>>>(blocks, X, Y, M, K, B);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
 }
 
 int asdsl_b200_gemv_q4_128_fused(const uint8_t* blocks, const float* x, float* y, int M, int K, void* stream) {

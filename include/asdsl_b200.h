@@ -101,6 +101,16 @@ int asdsl_b200_gemv_q4_32_preq_fused(const uint8_t* blocks, const float* x, floa
 int asdsl_b200_gemv_q4_128(const uint8_t* blocks, const int8_t* x_q8, const float* x_scales, float* y,
                            int out_features, int in_features, int group_size, void* stream);
 
+/* Batched prompt GEMM on fp32 activations over Q4_128 blocks [M][K/128][66] (no A8): Y[b][M] for
+ * b < min(batch, 64) of X[b][K], each row's per-group 8-lane fma dots in the reference's order, so
+ * the outputs are bit-identical; Y rows b >= 64 are not written, as in the reference.
+ * Replaces gemm_q4_128_q8_avx2 (asdsl/kernels/native/gemv_q4_128.cpp:262-306), the GEMM of the
+ * reference engine's forward_batch for g128 projections (unified_engine.cpp:1154-1215).
+ * group_size != 128 -> EINVAL (the reference's invalid_argument); blocks 2-byte and X 16-byte
+ * aligned; in_features a multiple of 128. */
+int asdsl_b200_gemm_q4_128_f32(const uint8_t* blocks, const float* X, float* Y, int out_features, int in_features,
+                               int group_size, int batch, void* stream);
+
 /* Q4_128 GEMV with fused A8 at gs 128: quantize_activation_avx2(..., 128) followed
  * by gemv_q4_128_preq_avx2, as the engine's C0.1 branches do
  * (asdsl/kernels/native/unified_engine.cpp:1532-1538, :1592-1598). */

@@ -200,6 +200,43 @@ void or_gemv_q4_128_q8(const uint8_t* blocks, const int8_t* xq, const float* xs,
     free(xsum);
 }
 
+/* Batched prompt GEMM on fp32 activations (gemm_q4_128_q8_avx2, gemv_q4_128.cpp:262-306): per
+ * (row, 128-group) the weights dequantized exactly, w = ((q & 15) - 8) * ws; per batch row an
+ * 8-lane fma dot over the group (lane j takes elements j, j+8, ...), folded as
+ * (l0+l4 + l1+l5) + (l2+l6 + l3+l7) (hsum256_q4128, :49-58), added to that row's accumulator.
+ * Only batch rows b < 64 are computed; y rows b >= 64 are left as they are.  gs != 128 -> -1. */
+int or_gemm_q4_128_f32(const uint8_t* blocks, const float* x, float* y, int M, int K, int gs, int batch) {
+    if (gs != 128) return -1;
+    const int ng = K / 128;
+    const int nb = batch < 64 ? batch : 64;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < M; ++r) {
+        const uint8_t* row = blocks + (size_t)r * ng * 66;
+        float acc[64];
+        for (int b = 0; b < nb; ++b) acc[b] = 0.0f;
+        for (int g = 0; g < ng; ++g) {
+            const uint8_t* blk = row + g * 66;
+            const float ws = h2f(rd16(blk));
+            float wf[128];
+            for (int i = 0; i < 64; ++i) {
+                const uint8_t v = blk[2 + i];
+                wf[2 * i] = (float)((v & 0x0F) - 8) * ws;
+                wf[2 * i + 1] = (float)((v >> 4) - 8) * ws;
+            }
+            for (int b = 0; b < nb; ++b) {
+                const float* xb = x + (size_t)b * K + g * 128;
+                float l[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int i = 0; i < 128; i += 8)
+                    for (int j = 0; j < 8; ++j) l[j] = fmaf(wf[i + j], xb[i + j], l[j]);
+                const float h0 = l[0] + l[4], h1 = l[1] + l[5], h2 = l[2] + l[6], h3 = l[3] + l[7];
+                acc[b] += (h0 + h1) + (h2 + h3);
+            }
+        }
+        for (int b = 0; b < nb; ++b) y[(size_t)b * M + r] = acc[b];
+    }
+    return 0;
+}
+
 /* Q4_S256: gemv_q4_s256.cpp:110-138: 8 fp16 sub-scales + 128 nibble bytes,
  * activations at gs 32; acc += dot*(ws*xs), corr += 8*xsum*(ws*xs). */
 void or_gemv_q4_s256_q8(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K) {

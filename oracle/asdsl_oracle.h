@@ -31,6 +31,8 @@ void or_gemv_preq_q8(const uint8_t* blocks, const int8_t* xq, const float* xs, f
                                                                     /* gemv_q4_preq_restored.cpp:305-336,338-473 */
 void or_gemv_q4_128_q8(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K);
                                                                     /* gemv_q4_128.cpp:94-257 */
+int or_gemm_q4_128_f32(const uint8_t* blocks, const float* x, float* y, int M, int K, int gs, int batch);
+                                                                    /* gemv_q4_128.cpp:262-306 */
 void or_gemv_q4_s256_q8(const uint8_t* blocks, const int8_t* xq, const float* xs, float* y, int M, int K);
                                                                     /* gemv_q4_s256.cpp:83-209 */
 /* fp32-activation entries (A8 inside, as the reference's fused entries) */

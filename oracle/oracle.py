@@ -109,6 +109,17 @@ class Oracle:
         xq, xs, _ = self.quantize_activation(x, 128)
         return self.gemv_q4_128_q8(blocks, xq, xs, M, K)
 
+    def gemm_q4_128_f32(self, blocks, X, M, K, gs=128, y=None):
+        """Batched fp32-activation Q4_128 GEMM (gemm_q4_128_q8_avx2); X [B][K] -> Y [B][M], rows
+        b >= 64 left as given in `y` (zeros by default)."""
+        X = np.ascontiguousarray(X, np.float32)
+        B = X.shape[0]
+        y = np.zeros((B, M), np.float32) if y is None else np.array(y, np.float32, copy=True)
+        if self.lib.or_gemm_q4_128_f32(_p(np.ascontiguousarray(blocks)), _p(X), _p(y), _I(M), _I(K), _I(gs),
+                                       _I(B)):
+            raise ValueError("gemm_q4_128_q8_avx2: group_size must be 128")
+        return y
+
     def gemv_s256_q8(self, blocks, xq, xs, M, K):
         y = np.zeros(M, np.float32)
         self.lib.or_gemv_q4_s256_q8(_p(np.ascontiguousarray(blocks)), _p(np.ascontiguousarray(xq)),
@@ -281,6 +292,14 @@ class RefKernels:
         y = np.zeros(M, np.float32)
         self._chk(self.lib.ref_gemv_q4_128(_p(np.ascontiguousarray(blocks)), _p(xq), _p(xs), _p(y), _I(M), _I(K),
                                            _I(128)))
+        return y
+
+    def gemm_q4_128_f32(self, blocks, X, M, K, gs=128, y=None):
+        X = np.ascontiguousarray(X, np.float32)
+        B = X.shape[0]
+        y = np.zeros((B, M), np.float32) if y is None else np.array(y, np.float32, copy=True)
+        self._chk(self.lib.ref_gemm_q4_128(_p(np.ascontiguousarray(blocks)), _p(X), _p(y), _I(M), _I(K), _I(gs),
+                                           _I(B)))
         return y
 
     def gemv_s256_q8(self, blocks, xq, xs, M, K):

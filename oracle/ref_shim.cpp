@@ -28,6 +28,8 @@ void gemv_q4_128_preq_avx2(const uint8_t* blocks, const int8_t* x_q8, const floa
 void gemv_q4_s256_preq_avx2(const uint8_t* blocks, const int8_t* x_q8, const float* x_scales, float* y,
                             int out_features, int in_features, int group_size);
 void gemv_q4km_q8_avx2(const uint8_t* weights_q4km, const float* x, float* y, int out_features, int in_features);
+void gemm_q4_128_q8_avx2(const uint8_t* blocks, const float* x_batch, float* y_batch, int out_features,
+                         int in_features, int group_size, int batch_size);
 void gemv_q4_packed_impl_v2(const uint8_t* w_packed, const float* x, const float* scales, const float* biases,
                             float* y, int M, int K, int group_size);
 void gemv_q4_unpacked_impl(const uint8_t* w, const float* x, const float* scales, const float* biases,
@@ -70,6 +72,9 @@ int ref_gemv_q4_s256(const uint8_t* blocks, const int8_t* xq, const float* xs, f
 }
 int ref_gemv_q4km(const uint8_t* w, const float* x, float* y, int M, int K) {
     SHIM_TRY(gemv_q4km_q8_avx2(w, x, y, M, K));
+}
+int ref_gemm_q4_128(const uint8_t* blocks, const float* x, float* y, int M, int K, int gs, int batch) {
+    SHIM_TRY(gemm_q4_128_q8_avx2(blocks, x, y, M, K, gs, batch));
 }
 int ref_gemv_q4_packed(const uint8_t* w, const float* x, const float* s, const float* b, float* y,
                        int M, int K, int gs) {

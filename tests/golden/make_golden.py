@@ -10,6 +10,8 @@ Sources of truth per fixture:
   repack_*.npz  asdsl.quantization.repack_q4_32 / _preq2 / _q4_128 (the repackers)
   kern_*.npz    the reference's compiled AVX2 kernels (oracle/_ref via ref_shim.cpp)
   engine_tiny.npz  the reference's compiled UnifiedEngine (_native_unified in oracle/_ref)
+  gemm_q4_128.npz  the reference's compiled gemm_q4_128_q8_avx2 (gemv_q4_128.cpp:262-306, fp32
+                   activations, batch rows >= 64 left untouched) via ref_shim.cpp
   engine_long.npz  the same engine: 160 greedy steps on TINY-shaped models with a 256-position
                    cache (seeds 5 and 7), shapes on which the reference and a faithful
                    restatement with another fp32 summation order agree token for token
@@ -96,15 +98,38 @@ def engine_long() -> None:
     np.savez_compressed(os.path.join(OUT, "engine_long.npz"), **out)
 
 
+def gemm_q4_128() -> None:
+    """Prompt GEMM fixture: random Q4_128 blocks (scales in the symmetric quantizer's range, one
+    all-zero-scale group) and N(0, 1) activations; batches of 5 and 66 rows (the reference leaves
+    y rows 64 and 65 as it found them: the fixture pre-fills them with -1)."""
+    from asdsl_b200.quantization.synth import random_q4_128
+    from oracle.oracle import RefKernels
+
+    rk = RefKernels()
+    rng = np.random.default_rng(20261202)
+    M, K = 70, 512
+    blocks = random_q4_128(rng, M, K)
+    blocks[3, 1, 0:2] = 0  # scale 0.0
+    x5 = rng.standard_normal((5, K)).astype(np.float32)
+    x66 = rng.standard_normal((66, K)).astype(np.float32)
+    y5 = rk.gemm_q4_128_f32(blocks, x5, M, K)
+    y66 = rk.gemm_q4_128_f32(blocks, x66, M, K, y=np.full((66, M), -1.0, np.float32))
+    np.savez_compressed(os.path.join(OUT, "gemm_q4_128.npz"), blocks=blocks, x5=x5, y5=y5, x66=x66, y66=y66)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["engine_long"], default=None)
+    ap.add_argument("--only", choices=["engine_long", "gemm_q4_128"], default=None)
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     if args.only == "engine_long":
         engine_long()
         print("golden fixture engine_long.npz written to", OUT)
+        return
+    if args.only == "gemm_q4_128":
+        gemm_q4_128()
+        print("golden fixture gemm_q4_128.npz written to", OUT)
         return
     from asdsl.quantization import core as rcore
     from asdsl.quantization.repack_preq2 import repack_preq_blocks_to_preq2
@@ -216,6 +241,7 @@ def main() -> None:
                         generate=np.array(gen, np.int32), logits0=logits0, margins=np.array(margins),
                         lm_meta=lm_meta, lm_quant=lm_quant)
     engine_long()
+    gemm_q4_128()
     print("golden fixtures written to", OUT)
 
 

@@ -161,6 +161,43 @@ def test_q4_128_golden(ng, golden):
     assert rel_err(y, g["y_q4_128"]) < TOL
 
 
+def test_gemm_q4_128_f32_golden(ng, golden, native):
+    """gemm_q4_128_q8_avx2 (gemv_q4_128.cpp:262-306): bit-identical to the reference's own outputs
+    (tests/golden/gemm_q4_128.npz, an all-zero-scale group included), for 5 batch rows and for 66,
+    where the reference computes rows 0..63 and leaves rows 64 and 65 as they were (-1 here)."""
+    g = golden("gemm_q4_128.npz")
+    M, K = 70, 512
+    y5 = np.zeros((5, M), np.float32)
+    ng.gemm_q4_128_q8_avx2(g["blocks"], g["x5"], y5, M, K, 128, 5)
+    assert np.array_equal(y5, g["y5"])
+    y66 = np.full((66, M), -1.0, np.float32)
+    ng.gemm_q4_128_q8_avx2(g["blocks"], g["x66"], y66, M, K, 128, 66)
+    assert np.array_equal(y66, g["y66"])
+    with pytest.raises(ValueError, match="group_size must be 128"):
+        ng.gemm_q4_128_q8_avx2(g["blocks"], g["x5"], y5, M, K, 32, 5)
+    _status_clean(native)
+
+
+@pytest.mark.parametrize("M,K,B", [(1000, 3072, 37), (3072, 8192, 64), (16384, 3072, 16), (33, 128, 1)])
+def test_gemm_q4_128_f32_vs_oracle(oracle, native, M, K, B):
+    """The prompt GEMM at the engine's g128 shapes (gate_up 16384x3072, down 3072x8192) and ragged
+    ones (rows not a multiple of the 32-row tile, 1 and 37 batch rows), device tensors in place:
+    bit-identical to the oracle restatement of the reference's order."""
+    from asdsl_b200 import _lib
+    from asdsl_b200.quantization.synth import random_q4_128
+
+    rng = np.random.default_rng(M + K + B)
+    blocks = random_q4_128(rng, M, K)
+    X = rng.standard_normal((B, K)).astype(np.float32)
+    Yd = torch.full((B, M), 7.0, dtype=torch.float32, device="cuda")
+    bd, xd = _dev(blocks), _dev(X)  # alive until the kernel has run
+    _lib.call("asdsl_b200_gemm_q4_128_f32", bd.data_ptr(), xd.data_ptr(), Yd.data_ptr(), M, K, 128, B,
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(Yd.cpu().numpy(), oracle.gemm_q4_128_f32(blocks, X, M, K))
+    _status_clean(native)
+
+
 @pytest.mark.parametrize("M,K", [(19, 512), (8192, 3072), (3072, 8192)])
 def test_s256(ng, oracle, native, M, K):
     from asdsl_b200.quantization.synth import quantize_s256

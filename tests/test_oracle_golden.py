@@ -40,6 +40,18 @@ def test_gemv_formats_vs_reference(oracle, golden):
     assert rel_err(oracle.gemv_q4km(g["q4k"], g["x"], m, K), g["y_q4k"]) < 1e-5
 
 
+def test_gemm_q4_128_f32_vs_reference(oracle, golden):
+    """The prompt GEMM restatement (gemm_q4_128_q8_avx2, gemv_q4_128.cpp:262-306) reproduces the
+    reference's outputs bit for bit, rows >= 64 of a 66-row batch untouched, gs != 128 rejected."""
+    g = golden("gemm_q4_128.npz")
+    M, K = 70, 512
+    assert np.array_equal(oracle.gemm_q4_128_f32(g["blocks"], g["x5"], M, K), g["y5"])
+    y66 = oracle.gemm_q4_128_f32(g["blocks"], g["x66"], M, K, y=np.full((66, M), -1.0, np.float32))
+    assert np.array_equal(y66, g["y66"]) and (y66[64:] == -1.0).all()
+    with pytest.raises(ValueError):
+        oracle.gemm_q4_128_f32(g["blocks"], g["x5"], M, K, gs=32)
+
+
 def test_engine_tiny_vs_reference_engine(oracle, golden):
     from asdsl_b200.inference.synthetic import TINY, build_model, model_digest
 
@@ -84,6 +96,12 @@ def test_oracle_vs_live_reference_random(oracle):
         if K % 256 == 0:
             w = random_q4k_bytes(rng, M, K)
             assert rel_err(oracle.gemv_q4km(w, x, M, K), rk.gemv_q4km(w, x, M, K)) < TOL
+        if K % 128 == 0:
+            from asdsl_b200.quantization.synth import random_q4_128
+
+            blk = random_q4_128(rng, M, K)
+            X = rng.standard_normal((3, K)).astype(np.float32)
+            assert np.array_equal(oracle.gemm_q4_128_f32(blk, X, M, K), rk.gemm_q4_128_f32(blk, X, M, K))
 
 
 def test_oracle_engine_long_trajectories_vs_reference(oracle, golden):
