@@ -10,7 +10,6 @@
  *
  * Each declaration cites the reference interface it replaces
  * (aarushk09/asdsl-framework, paths relative to the repository root).
- * Reference-side bindings are shown in INTEGRATION.md.
  */
 #ifndef ASDSL_B200_H
 #define ASDSL_B200_H
