@@ -63,6 +63,19 @@ def test_argument_errors_map_to_reference_exceptions(lib):
         _lib.call("asdsl_b200_gemv_q4_packed", 16, 16, 16, 16, 16, 4, 36, 12, 1, None)
     # Q4_K with empty shapes returns without work, like the reference
     assert _lib.call("asdsl_b200_gemv_q4km", None, None, None, 0, 256, None) == 0
+    # prompt GEMM (gemm_q4_128_q8_avx2): the reference's group-size message first, then this
+    # library's own checks; an empty batch is no work
+    with pytest.raises(ValueError, match="gemm_q4_128_q8_avx2: group_size must be 128"):
+        _lib.call("asdsl_b200_gemm_q4_128_f32", 16, 16, 16, 16, 128, 32, 4, None)
+    with pytest.raises(ValueError, match="null pointer"):
+        _lib.call("asdsl_b200_gemm_q4_128_f32", None, 16, 16, 16, 128, 128, 4, None)
+    with pytest.raises(ValueError, match="divisible by 128"):
+        _lib.call("asdsl_b200_gemm_q4_128_f32", 16, 16, 16, 16, 100, 128, 4, None)
+    with pytest.raises(ValueError, match="2-byte aligned"):
+        _lib.call("asdsl_b200_gemm_q4_128_f32", 17, 16, 16, 16, 128, 128, 4, None)
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        _lib.call("asdsl_b200_gemm_q4_128_f32", 16, 20, 16, 16, 128, 128, 4, None)
+    assert _lib.call("asdsl_b200_gemm_q4_128_f32", 16, 16, 16, 16, 128, 128, 0, None) == 0
 
 
 def test_python_api_fails_loudly_without_gpu():
