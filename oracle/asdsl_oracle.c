@@ -12,11 +12,28 @@
  *     the rounded reciprocal constant (reciprocal math), so the A8 scale is
  *     amax * fl(1/127) and the engine lm_head scale is amax * fl(1/7);
  *   - `127.0f / amax` and `7.0f / amax` stay true IEEE divisions.
- * Summation order inside a row is the reference's structure (even/odd group
- * accumulators, 8-lane partial sums) where that is cheap to restate; the
+ * The decode engine's path (the preq2 GEMV, RMSNorm, SwiGLU, attention) is
+ * restated in the exact operation order of the reference's compiled code, so
+ * this oracle's engine is bit-identical to the reference's UnifiedEngine
+ * (tests/test_oracle_exact.py checks that against oracle/_ref):
+ *   - the preq2 GEMV keeps the 8 int32 lanes of each group's dot product
+ *     (pmaddubsw + pmaddwd lanes: elements 4j..4j+3) as 8 float accumulators
+ *     per even/odd group, and ends with (hsum(even) + hsum(odd)) - (corr_even
+ *     + corr_odd), the order GCC emits for gemv_preq2_avx2.cpp:250;
+ *   - `1.0f / std::sqrt(a)` (RMSNorm, attention's 1/sqrt(head_dim)) is emitted
+ *     as RSQRTSS plus one Newton step, (x0*(a*x0) - 3) * (x0 * -0.5), and the
+ *     vector divide of SwiGLU's sigmoid as RCPPS plus one Newton step,
+ *     (x0 + x0) - x0*(x0*d); both estimates come from this host's CPU, like the
+ *     reference's;
+ *   - RMSNorm's per-element product is (x*w)*inv, SwiGLU's (g*u)*sigmoid, and
+ *     1 + p*2^i is one FMA; attention's num*old_scale + tile_num is one FMA.
+ * The other GEMV formats keep the reference's structure (even/odd group
+ * accumulators, 8-lane partial sums) where that is cheap to restate; their
  * remaining fp32 reassociation differences are covered by the 1e-3 tolerance.
  */
 #include "asdsl_oracle.h"
+
+#include <xmmintrin.h>
 
 #include <math.h>
 #include <stdlib.h>
@@ -37,6 +54,25 @@ static inline uint16_t f2h(float f) {
     return h;
 }
 static inline uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* The host CPU's approximate reciprocal instructions, as the reference's compiled code runs them,
+ * and GCC's one-step Newton refinements of them under -ffast-math (operand order as emitted). */
+static inline float x86_rsqrt(float a) { return _mm_cvtss_f32(_mm_rsqrt_ss(_mm_set_ss(a))); }
+static inline float x86_rcp(float a) { return _mm_cvtss_f32(_mm_rcp_ss(_mm_set_ss(a))); }
+float or_nr_rsqrt(float a) {
+    const float x0 = x86_rsqrt(a);
+    const float t = fmaf(x0, x0 * a, -3.0f);
+    return t * (x0 * -0.5f);
+}
+float or_nr_recip(float d) {
+    const float x0 = x86_rcp(d);
+    const float e = x0 * (x0 * d);
+    return (x0 + x0) - e;
+}
+/* hsum256_ps (unified_engine.cpp:152-161): ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7)) */
+static inline float hsum8(const float v[8]) {
+    return ((v[0] + v[4]) + (v[1] + v[5])) + ((v[2] + v[6]) + (v[3] + v[7]));
+}
 
 /* ---------------------------------------------------------------------------
  * A8: asdsl/kernels/native/gemv_q4_preq_restored.cpp:505-549
@@ -116,9 +152,11 @@ static inline int32_t sum32(const int8_t* q) {
     return s;
 }
 
-/* preq2: gemv_preq2_avx2.cpp:196-253 (process_one_row).  Per group:
- * term = (float)dot * (ws*xs); corr = wz*ws*(xsum*xs); even/odd accumulators;
- * y = sum(term) - sum(corr). */
+/* preq2: gemv_preq2_avx2.cpp:196-253 (process_one_row, the OpenMP row loop at :289-292), in the
+ * compiled operation order.  Per group g: combined = ws*xs; corr_term = (wz*ws)*xsum_scaled;
+ * lane j of the int32 dot (pmaddubsw + pmaddwd: elements 4j..4j+3) -> term_j = (float)dot_j *
+ * combined, added to lane j of the even or odd accumulator; corr_term to the even or odd scalar.
+ * y = (hsum(acc_even) + hsum(acc_odd)) - (corr_even + corr_odd). */
 void or_gemv_preq2_q8(const uint8_t* meta, const uint8_t* quant, const int8_t* xq, const float* xs,
                       float* y, int M, int K) {
     const int ng = K / 32;
@@ -128,17 +166,23 @@ void or_gemv_preq2_q8(const uint8_t* meta, const uint8_t* quant, const int8_t* x
     for (int r = 0; r < M; ++r) {
         const uint8_t* mrow = meta + (size_t)r * ng * 4;
         const uint8_t* qband = quant + (size_t)(r / 4) * ng * 64 + (r % 4) * 16;
-        float acc[2] = {0.0f, 0.0f}, corr[2] = {0.0f, 0.0f};
+        float acc[2][8] = {{0}}, corr[2] = {0.0f, 0.0f};
         for (int g = 0; g < ng; ++g) {
             const float ws = h2f(rd16(mrow + g * 4));
             const float wz = h2f(rd16(mrow + g * 4 + 2));
             const float comb = ws * xs[g];
-            const float ct = wz * ws * xsum_scaled[g];
-            const int32_t d = dot32(qband + (size_t)g * 64, xq + g * 32);
-            acc[g & 1] += (float)d * comb;
+            const float ct = (wz * ws) * xsum_scaled[g];
+            const uint8_t* nib = qband + (size_t)g * 64;
+            const int8_t* xg = xq + g * 32;
+            for (int j = 0; j < 8; ++j) {
+                const int32_t d = (int32_t)(nib[2 * j] & 0x0F) * xg[4 * j] + (int32_t)(nib[2 * j] >> 4) * xg[4 * j + 1] +
+                                  (int32_t)(nib[2 * j + 1] & 0x0F) * xg[4 * j + 2] +
+                                  (int32_t)(nib[2 * j + 1] >> 4) * xg[4 * j + 3];
+                acc[g & 1][j] += (float)d * comb;
+            }
             corr[g & 1] += ct;
         }
-        y[r] = acc[0] + acc[1] - corr[0] - corr[1];
+        y[r] = (hsum8(acc[0]) + hsum8(acc[1])) - (corr[0] + corr[1]);
     }
     free(xsum_scaled);
 }
@@ -416,10 +460,11 @@ static float sumsq8(const float* x, int n) {
     return s;
 }
 
+/* compiled order: inv = nr_rsqrt(sum/n + eps) (RSQRTSS + Newton), out = (x*w)*inv */
 void or_rmsnorm(float* out, const float* in, const float* w, int n, float eps) {
     const float s = sumsq8(in, n);
-    const float inv = 1.0f / sqrtf(s / (float)n + eps);
-    for (int i = 0; i < n; ++i) out[i] = (in[i] * inv) * w[i];
+    const float inv = or_nr_rsqrt(s / (float)n + eps);
+    for (int i = 0; i < n; ++i) out[i] = (in[i] * w[i]) * inv;
 }
 
 /* :663-693 */
@@ -448,33 +493,29 @@ void or_rope(float* q, float* k, const float* cos_t, const float* sin_t, int pos
     }
 }
 
-/* fast_exp_avx2, :803-825: the reference's own degree-5 polynomial in 2^x
- * after range reduction with round-to-nearest-even. */
-static inline float ref_fast_exp(float x) {
-    x = fmaxf(x, -87.3f);
-    x = fminf(x, 87.3f);
-    x = x * 1.4426950408889634f;
-    const float fi = rintf(x);
-    const int i = (int)fi;
-    const float f = x - fi;
-    float p = fmaf(0.001333838100523091f, f, 0.009618129107628477f);
-    p = fmaf(p, f, 0.05550410866482158f);
-    p = fmaf(p, f, 0.2402265069591007f);
-    p = fmaf(p, f, 0.6931471805599453f);
-    p = fmaf(p, f, 1.0f);
-    uint32_t eb = (uint32_t)(i + 127) << 23;
-    float e;
-    memcpy(&e, &eb, 4);
-    return p * e;
-}
-
-/* swiglu_inplace :836-857 (vector path: size is a multiple of 8) */
+/* swiglu_inplace :836-857 (vector path: size is a multiple of 8) with fast_exp_avx2 (:803-825)
+ * inlined, in the compiled order: d = fma(p, 2^i, 1) (the multiply by 2^i and the add contracted),
+ * sigmoid = RCPPS(d) + one Newton step, val = (g*u)*sigmoid. */
 void or_swiglu(float* gate, const float* up, int n) {
     for (int i = 0; i < n; ++i) {
         const float g = gate[i];
-        const float e = ref_fast_exp(0.0f - g);
-        const float sig = 1.0f / (1.0f + e);
-        gate[i] = (g * sig) * up[i];
+        float x = -g;
+        x = fmaxf(x, -87.3f);
+        x = fminf(x, 87.3f);
+        x = x * 1.4426950408889634f;
+        const float fi = rintf(x);
+        const int k = (int)fi;
+        const float f = x - fi;
+        float p = fmaf(0.001333838100523091f, f, 0.009618129107628477f);
+        p = fmaf(p, f, 0.05550410866482158f);
+        p = fmaf(p, f, 0.2402265069591007f);
+        p = fmaf(p, f, 0.6931471805599453f);
+        p = fmaf(p, f, 1.0f);
+        const uint32_t eb = (uint32_t)(k + 127) << 23;
+        float e;
+        memcpy(&e, &eb, 4);
+        const float d = fmaf(p, e, 1.0f);
+        gate[i] = (g * up[i]) * or_nr_recip(d);
     }
 }
 
@@ -492,7 +533,7 @@ int or_argmax(const float* v, int n) {
 }
 
 /* :859-920 one position: per head per 64-block; scale = absmax*fl(1/127)
- * (or 1e-12), inv = 1/scale, q = clamp(RNE(x*inv), -127, 127). */
+ * (or 1e-12), inv = 127/absmax (or 1e12), q = clamp(RNE(x*inv), -127, 127). */
 void or_kv_write(int8_t* kq, float* ks, int8_t* vq, float* vs, const float* k, const float* v,
                  int n_kv_heads, int head_dim) {
     const int nbk = head_dim / 64;
@@ -508,7 +549,9 @@ void or_kv_write(int8_t* kq, float* ks, int8_t* vq, float* vs, const float* k, c
             const float sv = va > 1e-12f ? va * kInv127 : 1e-12f;
             ks[h * nbk + b] = sk;
             vs[h * nbk + b] = sv;
-            const float ik = 1.0f / sk, iv = 1.0f / sv;
+            /* the compiled code folds 1/(absmax * fl(1/127)) into 127/absmax (reciprocal math);
+             * the tiny-block branch multiplies by fl(1e12) */
+            const float ik = ka > 1e-12f ? 127.0f / ka : 1e12f, iv = va > 1e-12f ? 127.0f / va : 1e12f;
             for (int i = 0; i < 64; ++i) {
                 int a = (int)rintf(k[off + i] * ik), c = (int)rintf(v[off + i] * iv);
                 a = a < -127 ? -127 : (a > 127 ? 127 : a);
@@ -527,7 +570,7 @@ void or_attention(float* out, const float* q, const int8_t* kq, const float* ks,
                   const float* vs, int seq_pos, int n_heads, int n_kv_heads, int head_dim,
                   long pos_stride_q8, long pos_stride_sc) {
     const int groups = n_heads / n_kv_heads > 0 ? n_heads / n_kv_heads : 1;
-    const float inv_sqrt_d = 1.0f / sqrtf((float)head_dim);
+    const float inv_sqrt_d = or_nr_rsqrt((float)head_dim); /* RSQRTSS + Newton, as compiled */
     const int nbk = head_dim / 64;
     float* scores = (float*)malloc(sizeof(float) * 64);
     float* num = (float*)malloc(sizeof(float) * (size_t)head_dim);
@@ -574,7 +617,7 @@ void or_attention(float* out, const float* q, const int8_t* kq, const float* ks,
             }
             m = nm;
             l = l * old_scale + tl;
-            for (int i = 0; i < head_dim; ++i) num[i] = num[i] * old_scale + tnum[i];
+            for (int i = 0; i < head_dim; ++i) num[i] = fmaf(num[i], old_scale, tnum[i]); /* contracted */
         }
         const float il = 1.0f / l;
         for (int i = 0; i < head_dim; ++i) out[(size_t)h * head_dim + i] = num[i] * il;

@@ -45,6 +45,10 @@ void or_gemv_q4_packed(const uint8_t* w, const float* x, const float* scales, co
 void or_lmhead_quant_q4_32_preq2(const uint16_t* w_f16, uint8_t* meta, uint8_t* quant, int rows, int cols);
 void or_lmhead_quant_q4_128(const uint16_t* w_f16, uint8_t* blocks, int rows, int cols);
 
+/* GCC -ffast-math's 1/sqrt(a) and 1/d on this host: RSQRTSS / RCPSS estimate + one Newton step */
+float or_nr_rsqrt(float a);
+float or_nr_recip(float d);
+
 /* Engine ops (unified_engine.cpp) */
 void or_rmsnorm(float* out, const float* in, const float* w, int n, float eps);          /* :499-524 */
 void or_residual_add_rmsnorm(float* hidden, float* residual, const float* w, int n, float eps); /* :663-693 */
