@@ -60,6 +60,11 @@ _SIGS = {
     "asdsl_b200_gemv_argmax_static": [_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_gateup_silu": [_I, _P, _P, _P, _P, _I, _I, _P],
     "asdsl_b200_gemv_multi": [_I, _P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_gemv_preq2_fused_exact": [_P, _P, _P, _P, _F, _P, _I, _I, _P],
+    "asdsl_b200_gateup_silu_exact": [_P, _P, _P, _P, _F, _P, _I, _I, _P],
+    "asdsl_b200_exact_numerics_init": [_P],
+    "asdsl_b200_exact_host_tables": [_P, _P, _P, _I, _P],
+    "asdsl_b200_exact_expf": [_P, _P, ctypes.c_longlong, _P],
     "asdsl_b200_xchg_create": [_I, _I, _P, _P],
     "asdsl_b200_xchg_handle_bytes": [],
     "asdsl_b200_xchg_open": [_P, _P],
@@ -87,6 +92,7 @@ _SIGS = {
     "asdsl_b200_engine_export_lm_head": [_P, _P, _P, _SZ, _P, _SZ],
     "asdsl_b200_engine_stream": [_P, _P],
     "asdsl_b200_engine_set_persistent": [_P, _I],
+    "asdsl_b200_engine_set_numerics": [_P, _I],
     "asdsl_b200_engine_profile_step": [_P, _I, _P, _I, _P],
     "asdsl_b200_engine_set_position": [_P, _I, _I],
     "asdsl_b200_engine_replay": [_P, _I, _I],

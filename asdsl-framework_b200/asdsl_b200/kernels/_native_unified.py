@@ -94,10 +94,16 @@ def _blob(a, dtype):
 
 class UnifiedEngine:
     """UnifiedEngine(config, token_embd, output_norm, output_proj, cos_table, sin_table,
-    layers_dict, lm_head_preq2_meta=None, lm_head_preq2_quant=None)  (:2662-2682)."""
+    layers_dict, lm_head_preq2_meta=None, lm_head_preq2_quant=None)  (:2662-2682).
+
+    numerics: "fast" (default) or "reference_exact" (every op in the reference's compiled
+    operation order: logits and greedy tokens bit-identical to the reference's UnifiedEngine on
+    this host; asdsl_b200_engine_set_numerics).  The environment variable ASDSL_B200_NUMERICS
+    sets the default."""
 
     def __init__(self, config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
-                 lm_head_preq2_meta=None, lm_head_preq2_quant=None, persistent: bool | None = None):
+                 lm_head_preq2_meta=None, lm_head_preq2_quant=None, persistent: bool | None = None,
+                 numerics: str | None = None):
         lib = _lib.load()
         self._lib = lib
         self.config_ = config
@@ -107,6 +113,12 @@ class UnifiedEngine:
         try:
             if persistent is not None:
                 _lib.check(lib.asdsl_b200_engine_set_persistent(self._e, 1 if persistent else 0), "UnifiedEngine")
+            numerics = numerics or os.environ.get("ASDSL_B200_NUMERICS", "fast")
+            if numerics not in ("fast", "reference_exact"):
+                raise ValueError(f"UnifiedEngine: numerics must be 'fast' or 'reference_exact', got {numerics!r}")
+            _lib.check(lib.asdsl_b200_engine_set_numerics(self._e, 1 if numerics == "reference_exact" else 0),
+                       "UnifiedEngine")
+            self.numerics = numerics
             self._load(config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
                        lm_head_preq2_meta, lm_head_preq2_quant)
         except BaseException:
@@ -250,7 +262,7 @@ class UnifiedEngine:
         that PLD stays lossless: the result must equal forward_verify_serial_all_logits.  Here the
         batched forward gives those rows bit for bit with one weight read per pass, so it runs that
         (the persistent-kernel mode, whose K-splits differ, keeps the serial replays)."""
-        if self._persistent:
+        if self._persistent or self.numerics == "reference_exact":
             return self.forward_verify_serial_all_logits(prompt, start_pos)
         return self.forward_verify_batch_raw_all_logits(prompt, start_pos)
 
@@ -375,7 +387,8 @@ class UnifiedEngine:
 
 
 def engine_from_model(model: dict, lm_head_group_size: int = 32, max_seq_len: int | None = None,
-                      use_preq2_cache: bool = False, persistent: bool | None = None) -> UnifiedEngine:
+                      use_preq2_cache: bool = False, persistent: bool | None = None,
+                      numerics: str | None = None) -> UnifiedEngine:
     """UnifiedEngine over a synthetic model of asdsl_b200.inference.synthetic.build_model, wired as
     the reference's unified_bridge.build_unified_engine does (tied fp16 embedding as lm_head source)."""
     c = model["config"]
@@ -397,4 +410,4 @@ def engine_from_model(model: dict, lm_head_group_size: int = 32, max_seq_len: in
     meta = model.get("lm_meta") if use_preq2_cache else None
     quant = model.get("lm_quant") if use_preq2_cache else None
     return UnifiedEngine(cfg, model["embed_f16"], model["output_norm"], None if meta is not None else model["embed_f16"],
-                         model["cos"], model["sin"], layers, meta, quant, persistent=persistent)
+                         model["cos"], model["sin"], layers, meta, quant, persistent=persistent, numerics=numerics)

@@ -911,5 +911,128 @@ int asdsl_b200_requant_q4_128(const uint8_t* packed, const uint16_t* scales, con
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// reference-exact numerics mode: the host CPU's RSQRTSS / RCPSS / expf tables (x86_numerics.h),
+// uploaded once per device
+// ---------------------------------------------------------------------------
+#include "x86_numerics.h"
+#include "attention_exact.cuh"
+
+namespace {
+std::mutex g_exact_mu;
+ExactTabs g_exact_dev[64];
+bool g_exact_ready[64] = {};
+
+int exact_tabs_device(ExactTabs* out) {
+    const HostExactTables& T = host_exact_tables();
+    if (!T.ok) return set_error(kEinval, "reference-exact numerics: " + T.err);
+    int dev = 0;
+    ASDSL_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(kErange, "reference-exact numerics: device ordinal beyond 63");
+    std::lock_guard<std::mutex> lk(g_exact_mu);
+    if (!g_exact_ready[dev]) {
+        const size_t n = kRcpTabSize + kRsqrtTabSize + T.exp_exc.size();
+        uint32_t* d = nullptr;
+        ASDSL_CUDA(cudaMalloc(&d, 4 * n));
+        std::vector<uint32_t> h(n);
+        std::memcpy(h.data(), T.rcp, 4 * kRcpTabSize);
+        std::memcpy(h.data() + kRcpTabSize, T.rsqrt, 4 * kRsqrtTabSize);
+        std::memcpy(h.data() + kRcpTabSize + kRsqrtTabSize, T.exp_exc.data(), 4 * T.exp_exc.size());
+        const cudaError_t ec = cudaMemcpy(d, h.data(), 4 * n, cudaMemcpyHostToDevice);
+        if (ec != cudaSuccess) {
+            cudaFree(d);
+            return cuda_check(ec, "reference-exact numerics: table upload");
+        }
+        g_exact_dev[dev].rcp = d;
+        g_exact_dev[dev].rsqrt = d + kRcpTabSize;
+        g_exact_dev[dev].exp_exc = d + kRcpTabSize + kRsqrtTabSize;
+        g_exact_dev[dev].n_exp_exc = static_cast<int>(T.exp_exc.size() / 2);
+        g_exact_ready[dev] = true;
+    }
+    *out = g_exact_dev[dev];
+    return kOk;
+}
+}  // namespace
+
+namespace {
+__global__ void k_exact_expf(const float* __restrict__ x, float* __restrict__ y, long long n, ExactTabs t) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        y[i] = exact_expf(x[i], t);
+}
+}  // namespace
+
+extern "C" {
+
+int asdsl_b200_exact_expf(const float* x, float* y, long long n, void* stream) {
+    if (!x || !y || n < 0) return set_error(kEinval, "exact_expf: invalid arguments");
+    if (n == 0) return kOk;
+    ExactTabs t;
+    if (int rc = exact_tabs_device(&t)) return rc;
+    k_exact_expf<<<sm_count() * 8, 256, 0, as_stream(stream)>>>(x, y, n, t);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_exact_numerics_init(int* n_exp_exceptions) {
+    ExactTabs t;
+    if (int rc = exact_tabs_device(&t)) return rc;
+    if (n_exp_exceptions) *n_exp_exceptions = t.n_exp_exc;
+    return kOk;
+}
+
+int asdsl_b200_exact_host_tables(uint32_t* rcp, uint32_t* rsqrt, uint32_t* exp_exc, int exp_cap, int* n_exp) {
+    const HostExactTables& T = host_exact_tables();
+    if (!T.ok) return set_error(kEinval, "reference-exact numerics: " + T.err);
+    const int n = static_cast<int>(T.exp_exc.size() / 2);
+    if (n_exp) *n_exp = n;
+    if (rcp) std::memcpy(rcp, T.rcp, 4 * kRcpTabSize);
+    if (rsqrt) std::memcpy(rsqrt, T.rsqrt, 4 * kRsqrtTabSize);
+    if (exp_exc) {
+        if (exp_cap < n) return set_error(kEinval, "exact_host_tables: exception buffer too small");
+        std::memcpy(exp_exc, T.exp_exc.data(), 8ull * n);
+    }
+    return kOk;
+}
+
+int asdsl_b200_gemv_preq2_fused_exact(const uint8_t* meta, const uint8_t* quant, const float* x, const float* norm_w,
+                                      float eps, float* y, int M, int K, void* stream) {
+    if (!meta || !quant || !x || !y) return set_error(kEinval, "gemv_preq2_fused_exact: null pointer");
+    if (int rc = check_k(K, 32, "gemv_preq2_fused_exact")) return rc;
+    if (M < 0) return set_error(kEinval, "gemv_preq2_fused_exact: invalid dimensions");
+    StreamIn s[2];
+    preq2_streams(s, meta, quant, M, K);
+    GemvArgs ga = base_args(M, K, 32);
+    ga.x = x;
+    ga.y = y;
+    if (!norm_w) return launch_stream_gemv<kFmtPreq2X, kProA8X, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+    if (K % 8) return set_error(kEinval, "gemv_preq2_fused_exact: RMSNorm needs in_features % 8 == 0");
+    if (int rc = exact_tabs_device(&ga.ex)) return rc;
+    ga.norm_w = norm_w;
+    ga.eps = eps;
+    return launch_stream_gemv<kFmtPreq2X, kProRmsA8X, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+}
+
+int asdsl_b200_gateup_silu_exact(const uint8_t* meta, const uint8_t* quant, const float* x, const float* norm_w,
+                                 float eps, float* h, int I, int K, void* stream) {
+    if (!meta || !quant || !x || !h) return set_error(kEinval, "gateup_silu_exact: null pointer");
+    if (I <= 0 || I % 4) return set_error(kEinval, "gateup_silu_exact: intermediate size must be a positive multiple of 4");
+    if (int rc = check_k(K, 32, "gateup_silu_exact")) return rc;
+    StreamIn s[2];
+    preq2_streams(s, meta, quant, 2LL * I, K);
+    GemvArgs ga = base_args(I, K, 32);
+    if (int rc = exact_tabs_device(&ga.ex)) return rc;
+    ga.x = x;
+    ga.h = h;
+    const long long nb = I / 4;
+    if (!norm_w) return launch_stream_gemv<kFmtPreq2X, kProA8X, kEpiSiluX>(s, 2, nb, nb, ga, as_stream(stream));
+    if (K % 8) return set_error(kEinval, "gateup_silu_exact: RMSNorm needs in_features % 8 == 0");
+    ga.norm_w = norm_w;
+    ga.eps = eps;
+    return launch_stream_gemv<kFmtPreq2X, kProRmsA8X, kEpiSiluX>(s, 2, nb, nb, ga, as_stream(stream));
+}
+
+}  // extern "C"
+
 // device-resident decode engine (asdsl_b200_engine_*)
 #include "engine.cuh"

@@ -75,6 +75,11 @@ struct asdsl_b200_engine {
     bool finalized = false;
     // per-op kernel chain (default; measured faster on B200) or the persistent decode-step kernel
     int persistent = 0;
+    // reference-exact numerics (asdsl_b200_engine_set_numerics): every op in the reference's
+    // compiled operation order, with the host CPU's RSQRTSS / RCPPS / expf tables
+    int exact = 0;
+    asdsl::ExactTabs ex{};
+    float inv_sqrt_d = 0.0f;  // 1/sqrt(head_dim) as the reference computes it (RSQRTSS + Newton)
     asdsl::StepOp* d_prog[2] = {nullptr, nullptr};  // [0] prefill, [1] decode
     asdsl::StepArgs prog_args[2] = {};
     uint32_t prog_smem = 0;
@@ -160,6 +165,18 @@ int eng_gemv(const EngProj& p, GemvArgs ga, long long pair_off_rows, cudaStream_
     q128b_streams(in, p.w0, p.w1, p.rows, p.cols);
     ga.gs = 128;
     return launch_stream_gemv<kFmtQ128B, PRO, EPI>(in, 2, nb, pair_off_rows > 0 ? nb : 0, ga, s);
+}
+
+// the same GEMV in the reference-exact mode (preq2 weights only; checked at finalize)
+template <int PRO, int EPI>
+int eng_gemv_x(const asdsl_b200_engine* e, const EngProj& p, GemvArgs ga, long long pair_off_rows, cudaStream_t s) {
+    StreamIn in[2];
+    const long long M = pair_off_rows > 0 ? pair_off_rows : p.rows;
+    const long long nb = (M + 3) / 4;
+    preq2_streams(in, p.w0, p.w1, p.rows, p.cols);
+    ga.gs = 32;
+    ga.ex = e->ex;
+    return launch_stream_gemv<kFmtPreq2X, PRO, EPI>(in, 2, nb, pair_off_rows > 0 ? nb : 0, ga, s);
 }
 
 int launch_small(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t s, bool pdl) {
@@ -398,7 +415,9 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
             ga.norm_w = L.rms_att;
             ga.eps = c.rms_norm_eps;
             ga.y = e->qkv;
-            if (int rc = eng_gemv<kProRmsA8, kEpiStore>(L.p[kProjQkv], ga, 0, s)) return rc;
+            if (int rc = e->exact ? eng_gemv_x<kProRmsA8X, kEpiStore>(e, L.p[kProjQkv], ga, 0, s)
+                                  : eng_gemv<kProRmsA8, kEpiStore>(L.p[kProjQkv], ga, 0, s))
+                return rc;
         }
         // attention (RoPE, KV write, GQA) -> att
         {
@@ -416,17 +435,26 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
             aa.n_kv = c.num_kv_heads;
             aa.rot = c.rotary_dim;
             aa.max_seq = c.max_seq_len;
-            void* args[] = {&aa};
-            if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention), dim3(c.num_heads),
-                                      dim3(asdsl::kAttnWarps * 32), args, s, true))
-                return rc;
+            if (e->exact) {
+                void* args[] = {&aa, &e->ex, &e->inv_sqrt_d};
+                if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_exact), dim3(c.num_heads),
+                                          dim3(asdsl::kAttnXThreads), args, s, true))
+                    return rc;
+            } else {
+                void* args[] = {&aa};
+                if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention), dim3(c.num_heads),
+                                          dim3(asdsl::kAttnWarps * 32), args, s, true))
+                    return rc;
+            }
         }
         // resid += W_o . A8(att)
         {
             GemvArgs ga = base_args(H, L.p[kProjO].cols, 32);
             ga.x = e->att;
             ga.resid = e->resid;
-            if (int rc = eng_gemv<kProA8, kEpiResid>(L.p[kProjO], ga, 0, s)) return rc;
+            if (int rc = e->exact ? eng_gemv_x<kProA8X, kEpiResid>(e, L.p[kProjO], ga, 0, s)
+                                  : eng_gemv<kProA8, kEpiResid>(L.p[kProjO], ga, 0, s))
+                return rc;
         }
         // h = silu(gate) * up, gate_up = W_gu . A8(RMSNorm(resid) * rms_ffn)
         {
@@ -435,14 +463,18 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
             ga.norm_w = L.rms_ffn;
             ga.eps = c.rms_norm_eps;
             ga.h = e->h;
-            if (int rc = eng_gemv<kProRmsA8, kEpiSilu>(L.p[kProjGateUp], ga, c.intermediate_size, s)) return rc;
+            if (int rc = e->exact ? eng_gemv_x<kProRmsA8X, kEpiSiluX>(e, L.p[kProjGateUp], ga, c.intermediate_size, s)
+                                  : eng_gemv<kProRmsA8, kEpiSilu>(L.p[kProjGateUp], ga, c.intermediate_size, s))
+                return rc;
         }
         // resid += W_down . A8(h)
         {
             GemvArgs ga = base_args(H, c.intermediate_size, 32);
             ga.x = e->h;
             ga.resid = e->resid;
-            if (int rc = eng_gemv<kProA8, kEpiResid>(L.p[kProjDown], ga, 0, s)) return rc;
+            if (int rc = e->exact ? eng_gemv_x<kProA8X, kEpiResid>(e, L.p[kProjDown], ga, 0, s)
+                                  : eng_gemv<kProA8, kEpiResid>(L.p[kProjDown], ga, 0, s))
+                return rc;
         }
     }
     if (with_lm) {
@@ -457,7 +489,9 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
         ga.out_val = e->am_val;
         ga.out_idx = e->am_idx;
         ga.row_base = 0;
-        if (int rc = eng_gemv<kProRmsA8, kEpiArgmax>(e->lm, ga, 0, s)) return rc;
+        if (int rc = e->exact ? eng_gemv_x<kProRmsA8X, kEpiArgmax>(e, e->lm, ga, 0, s)
+                              : eng_gemv<kProRmsA8, kEpiArgmax>(e->lm, ga, 0, s))
+            return rc;
         void* args[] = {&e->st, &e->seq, &e->am_idx, const_cast<int*>(&c.max_seq_len)};
         if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_advance_decode), dim3(1), dim3(32), args, s,
                                   true))
@@ -742,6 +776,39 @@ int eng_batch_pass(asdsl_b200_engine* e, const int* tok, int T, int start, float
         if (!(e)->finalized) return set_error(kEinval, "engine: finalize() has not run");   \
     } while (0)
 
+// forward_batch without the batched passes (the reference-exact mode, whose rows follow the
+// reference's per-token order): n serial replays -- the decode graph where a step's logits are
+// wanted, else the prefill graph -- with tokens[i] put into seq before step i; the logits of every
+// step (all_logits) or of the last one.  The stream is idle on entry.
+int eng_forward_serial(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos, float* out_logits,
+                       int all_logits) {
+    const size_t row = 4ull * e->cfg.vocab_size;
+    const bool all = out_logits && all_logits;
+    if (all && e->verify_rows < n) {
+        if (e->verify_logits) cudaFree(e->verify_logits);
+        e->verify_logits = nullptr;
+        e->verify_rows = 0;
+        ASDSL_CUDA(cudaMalloc(&e->verify_logits, row * n));
+        e->verify_rows = n;
+    }
+    ASDSL_CUDA(cudaMemcpyAsync(e->verify_tok, tokens, 4ull * n, cudaMemcpyHostToDevice, e->stream));
+    if (int rc = eng_set_pos(e, start_pos, -1)) return rc;
+    for (int i = 0; i < n; ++i) {
+        ASDSL_CUDA(cudaMemcpyAsync(e->seq + start_pos + i, e->verify_tok + i, 4, cudaMemcpyDeviceToDevice,
+                                   e->stream));
+        const bool want = all || (out_logits && i == n - 1);
+        ASDSL_CUDA(cudaGraphLaunch(want ? e->g_decode : e->g_prefill, e->stream));
+        if (all)
+            ASDSL_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(e->verify_logits) + row * i, e->logits, row,
+                                       cudaMemcpyDeviceToDevice, e->stream));
+    }
+    if (all) ASDSL_CUDA(cudaMemcpyAsync(out_logits, e->verify_logits, row * n, cudaMemcpyDefault, e->stream));
+    else if (out_logits) ASDSL_CUDA(cudaMemcpyAsync(out_logits, e->logits, row, cudaMemcpyDefault, e->stream));
+    if (int rc = eng_status(e)) return rc;  // synchronizes the stream
+    if (start_pos + n > e->kv_seq_len) e->kv_seq_len = start_pos + n;
+    return kOk;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1008,6 +1075,24 @@ int asdsl_b200_engine_finalize(asdsl_b200_engine* e) {
         ASDSL_CUDA(cudaStreamSynchronize(e->stream));
         e->lm_ready = true;
     }
+    if (e->exact) {
+        // the reference-exact mode covers the C0 path: preq2 gs 32 everywhere (lm_head included)
+        for (int l = 0; l < c.num_layers; ++l)
+            for (int w = 0; w < 4; ++w)
+                if (e->layers[l].p[w].fmt != ASDSL_B200_FMT_PREQ2)
+                    return set_error(kEinval, "engine_finalize: the reference-exact mode needs preq2 (gs 32) projections");
+        if (e->lm.fmt != ASDSL_B200_FMT_PREQ2)
+            return set_error(kEinval, "engine_finalize: the reference-exact mode needs a gs 32 (preq2) lm_head");
+        if (c.head_dim != asdsl::kAttnHeadDim || c.max_seq_len > asdsl::kAttnXMaxSeq || c.hidden_size % 8 ||
+            c.intermediate_size % 4)
+            return set_error(kEinval, "engine_finalize: the reference-exact mode needs head_dim 128, max_seq_len <= " +
+                                          std::to_string(asdsl::kAttnXMaxSeq) + " and hidden_size % 8 == 0");
+        if (e->persistent) return set_error(kEinval, "engine_finalize: the reference-exact mode runs the per-op chain");
+        if (int rc = exact_tabs_device(&e->ex)) return rc;
+#ifdef ASDSL_HOST_X86
+        e->inv_sqrt_d = asdsl::host_nr_rsqrt(static_cast<float>(c.head_dim));
+#endif
+    }
     // the lm_head source is no longer needed (the reference drops it too)
     if (e->out_proj) {
         eng_free(e, e->out_proj);
@@ -1110,6 +1195,7 @@ int asdsl_b200_engine_forward_batch(asdsl_b200_engine* e, const int32_t* tokens,
         return set_error(kErange, "forward_token: pos out of kv-cache range");
     DeviceGuard dg(e->device);
     ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    if (e->exact) return eng_forward_serial(e, tokens, n, start_pos, out_logits, all_logits);
     if (int rc = eng_batch_alloc(e)) return rc;
     const size_t row = 4ull * c.vocab_size;
     const bool all = out_logits && all_logits;
@@ -1155,9 +1241,9 @@ int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int 
     ASDSL_CUDA(cudaStreamSynchronize(e->stream));
     ASDSL_CUDA(cudaMemcpyAsync(e->seq, prompt, 4ull * n_prompt, cudaMemcpyHostToDevice, e->stream));
     // prompt tokens before the last one: batched passes (bit-identical to the per-op chain's
-    // prefill graph); the persistent-kernel mode keeps its own prefill graph
+    // prefill graph); the persistent-kernel and reference-exact modes replay their prefill graph
     const int n_pre = n_prompt - 1;
-    if (n_pre > 0 && !e->persistent) {
+    if (n_pre > 0 && !e->persistent && !e->exact) {
         if (int rc = eng_batch_alloc(e)) return rc;
         for (int t0 = 0; t0 < n_pre; t0 += e->batch_rows) {
             const int T = std::min(e->batch_rows, n_pre - t0);
@@ -1245,6 +1331,15 @@ int asdsl_b200_engine_profile_step(asdsl_b200_engine* e, int decode, unsigned lo
     *n_ops = A.n_ops;
     if (rc == kOk) rc = eng_status(e);
     return rc;
+}
+
+int asdsl_b200_engine_set_numerics(asdsl_b200_engine* e, int mode) {
+    ENG_CHECK(e);
+    if (e->finalized) return set_error(kEinval, "engine_set_numerics: engine already finalized");
+    if (mode != ASDSL_B200_NUMERICS_FAST && mode != ASDSL_B200_NUMERICS_REFERENCE_EXACT)
+        return set_error(kEinval, "engine_set_numerics: unknown mode");
+    e->exact = mode == ASDSL_B200_NUMERICS_REFERENCE_EXACT ? 1 : 0;
+    return kOk;
 }
 
 int asdsl_b200_engine_set_persistent(asdsl_b200_engine* e, int persistent) {

@@ -62,6 +62,13 @@ constexpr int kAttnGroups = kAttnWarps * 4;  // 8-lane position groups per CTA
 constexpr int kAttnHeadDim = 128;
 constexpr int kAttnPrefetch = 4;  // position blocks of cached K/V loaded before the dependency wait
 
+// set_kv_cache's code multiplier as the reference's compiled code computes it
+// (unified_engine.cpp:885-887): GCC folds 1/(absmax * fl(1/127)) into 127/absmax; a block with
+// absmax <= 1e-12 has scale 1e-12 and multiplier fl(1e12)
+__device__ __forceinline__ float kv_code_inv(float absmax) {
+    return absmax > 1e-12f ? __fdiv_rn(127.0f, absmax) : __int_as_float(0x5368D4A5);
+}
+
 struct AttnArgs {
     const float* qkv;     // [q_dim + 2 kv_dim] (q | k | v), this layer's projection output
     float* out;           // [q_dim]
@@ -187,8 +194,8 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
             const float va = fmaxf(S.red[1][b][0], S.red[1][b][1]);
             const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
             const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
-            int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
-            int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
+            int qk = __float2int_rn(__fmul_rn(kval, kv_code_inv(ka)));
+            int qv = __float2int_rn(__fmul_rn(vval, kv_code_inv(va)));
             qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
             qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
             S.k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
@@ -373,8 +380,8 @@ __global__ void __launch_bounds__(kAttnHeadDim) k_kv_write_rows(AttnArgs a, int 
     const float va = fmaxf(red[1][b][0], red[1][b][1]);
     const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
     const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
-    int qk = __float2int_rn(__fmul_rn(kval, __fdiv_rn(1.0f, ksc)));
-    int qv = __float2int_rn(__fmul_rn(vval, __fdiv_rn(1.0f, vsc)));
+    int qk = __float2int_rn(__fmul_rn(kval, kv_code_inv(ka)));
+    int qv = __float2int_rn(__fmul_rn(vval, kv_code_inv(va)));
     qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
     qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
     const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;

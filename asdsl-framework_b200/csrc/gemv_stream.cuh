@@ -33,6 +33,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "exact_math.cuh"
 
 namespace asdsl {
 
@@ -44,6 +45,7 @@ enum WeightFormat : int {
     kFmtQ4K = 4,      // [M][K/256][144] reference-interpretation Q4_K, own A8
     kFmtPacked = 5,   // nibbles [M][K/2] + fp32 scales [M][ng] + fp32 biases [M][ng], fp32 x
     kFmtQ128B = 6,    // banded Q4_128: quant [nb][K/128][4][64] + scales [nb][K/128][4] fp16
+    kFmtPreq2X = 7,   // preq2 bytes, every row summed in the reference's compiled order (exact mode)
 };
 
 enum Prologue : int {
@@ -52,6 +54,8 @@ enum Prologue : int {
     kProRmsA8 = 2,  // RMSNorm(x) * w then A8
     kProQ4K = 3,    // the Q4_K kernel's own A8 (half-away, clamp +-127)
     kProF32 = 4,    // fp32 x kept as is, plus per-group sums (packed W4A32)
+    kProA8X = 5,    // kProA8 for kFmtPreq2X: codes in lane order (4 per 32-bit word, see band_exact)
+    kProRmsA8X = 6, // kProRmsA8 for kFmtPreq2X: the reference's compiled RMSNorm, then A8 in lane order
 };
 
 enum Epilogue : int {
@@ -59,7 +63,12 @@ enum Epilogue : int {
     kEpiResid = 1,   // resid[row] += v (in place; the decode residual stream)
     kEpiSilu = 2,    // paired gate/up: h[i] = silu(gate_i) * up_i
     kEpiArgmax = 3,  // y[row] = v (optional) + global first-max argmax
+    kEpiSiluX = 4,   // kEpiSilu with swiglu_inplace's compiled arithmetic (exact mode)
 };
+
+__host__ __device__ constexpr bool pro_is_rms(int pro) { return pro == kProRmsA8 || pro == kProRmsA8X; }
+__host__ __device__ constexpr bool pro_is_lane_order(int pro) { return pro == kProA8X || pro == kProRmsA8X; }
+__host__ __device__ constexpr bool epi_is_silu(int epi) { return epi == kEpiSilu || epi == kEpiSiluX; }
 
 // measured on B200 (decode chains and lm_head): one 17-warp CTA per SM with
 // 64 KB stages beats two 9-warp CTAs
@@ -83,7 +92,8 @@ constexpr int kMaxStreams = 3;
 
 template <int FMT>
 struct FmtTraits {
-    static constexpr int kStreams = (FMT == kFmtPreq2 || FMT == kFmtQ128B) ? 2 : (FMT == kFmtPacked ? 3 : 1);
+    static constexpr int kStreams =
+        (FMT == kFmtPreq2 || FMT == kFmtPreq2X || FMT == kFmtQ128B) ? 2 : (FMT == kFmtPacked ? 3 : 1);
     static constexpr int kRowsPerUnit = (FMT == kFmtPacked) ? 1 : 4;
 };
 
@@ -142,6 +152,8 @@ struct GemvArgs {
     // multi-token kernels: the tokens' A8 areas, quantized once by k_quant_tokens in the layout
     // of the shared-memory areas (n_tokens x xarea_layout_bytes); null = each CTA quantizes
     const uint8_t* xa_pre;
+    // reference-exact mode (kProRmsA8X, kEpiSiluX): the host CPU's RSQRTSS / RCPPS tables
+    ExactTabs ex;
 };
 
 // ---------------------------------------------------------------------------
@@ -254,6 +266,11 @@ __device__ __forceinline__ float4 load_x4(const float4* p) {
     if constexpr (kCoherent) return __ldcg(p);
     else return __ldg(p);
 }
+template <bool kCoherent>
+__device__ __forceinline__ float load_x1(const float* p) {
+    if constexpr (kCoherent) return __ldcg(p);
+    else return __ldg(p);
+}
 
 template <int PRO, bool kCoherent = false>
 __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
@@ -297,7 +314,27 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
             }
         }
         float inv_rms = 1.0f;
-        if constexpr (PRO == kProRmsA8) {
+        if constexpr (PRO == kProRmsA8X) {
+            // rmsnorm_f32 as compiled (unified_engine.cpp:499-524): lane l of one 8-wide vector
+            // accumulates x[8i+l]^2 by FMA in order of i; hsum256_ps fold; sum/n + eps; RSQRTSS +
+            // Newton.  Eight threads run the eight lane chains; the others wait at the barrier.
+            if (ctid < 8) {
+                float acc = 0.0f;
+                const float* xp = ga.x + ctid;
+#pragma unroll 8
+                for (int i = 0; i < (K >> 3); ++i) {
+                    const float v = load_x1<kCoherent>(xp + 8 * i);
+                    acc = __fmaf_rn(v, v, acc);
+                }
+                const float a = __fadd_rn(acc, __shfl_xor_sync(0xffu, acc, 4));  // v_l + v_{l+4}
+                const float b = __fadd_rn(a, __shfl_xor_sync(0xffu, a, 1));      // (a0+a1), (a2+a3)
+                const float h = __fadd_rn(b, __shfl_xor_sync(0xffu, b, 2));      // (a0+a1) + (a2+a3)
+                if (ctid == 0)
+                    xa.red[0] = exact_nr_rsqrt(__fadd_rn(__fdiv_rn(h, static_cast<float>(K)), ga.eps), ga.ex.rsqrt);
+            }
+            consumer_sync();
+            inv_rms = xa.red[0];
+        } else if constexpr (PRO == kProRmsA8) {
             // inv = 1/sqrt(sum(x^2)/n + eps)  (unified_engine.cpp:499-513)
             float ss = 0.0f;
             auto acc = [&](const float4& f) {
@@ -346,7 +383,14 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
                     v[1] = f.y;
                     v[2] = f.z;
                     v[3] = f.w;
-                    if constexpr (PRO == kProRmsA8) {
+                    if constexpr (PRO == kProRmsA8X) {
+                        // compiled order: (x * w) * inv
+                        const float4 w = __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
+                        v[0] = __fmul_rn(__fmul_rn(v[0], w.x), inv_rms);
+                        v[1] = __fmul_rn(__fmul_rn(v[1], w.y), inv_rms);
+                        v[2] = __fmul_rn(__fmul_rn(v[2], w.z), inv_rms);
+                        v[3] = __fmul_rn(__fmul_rn(v[3], w.w), inv_rms);
+                    } else if constexpr (PRO == kProRmsA8) {
                         const float4 w = __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
                         v[0] = __fmul_rn(__fmul_rn(v[0], inv_rms), w.x);
                         v[1] = __fmul_rn(__fmul_rn(v[1], inv_rms), w.y);
@@ -382,7 +426,12 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
                     }
                 }
             }
-            if (live) {
+            if (live && pro_is_lane_order(PRO)) {
+                // lane order: the quad is lane (e0 & 31) / 4 of its 32-group; one word of the codes
+                // in the byte order band_exact's nibble word uses, [c0, c2, c1, c3]
+                *reinterpret_cast<uint32_t*>(xa.x8 + e0) = (c[0] & 0xFFu) | ((c[2] & 0xFFu) << 8) |
+                                                           ((c[1] & 0xFFu) << 16) | ((c[3] & 0xFFu) << 24);
+            } else if (live) {
                 // quad (4 consecutive elements, first one even) -> even word gets c0, c2 and the odd
                 // word c1, c3 at byte (e0 & 7) / 2 of the 8-byte pair of its 8 elements; the pairs of
                 // elements 0-15 of a slice go to plane A, those of 16-31 to plane B
@@ -579,6 +628,51 @@ __device__ __forceinline__ void band_compute(float a[4], uint32_t s0, uint32_t s
     }
 }
 
+// ---------------------------------------------------------------------------
+// kFmtPreq2X band: the reference's process_one_row (gemv_preq2_avx2.cpp:216-253) in its compiled
+// order.  Thread (row r = lane / 8, lane j = lane % 8) owns int32 lane j of every group's dot --
+// elements 4j..4j+3, as pmaddubsw + pmaddwd produce it -- and keeps that lane of the even-group
+// and odd-group float accumulators; every thread of a row also runs the row's two scalar
+// correction chains.  Per group g (in order): combined = ws*xs; corr = (wz*ws)*xsum_scaled;
+// acc[g&1] += (float)dot_j * combined; corr_sum[g&1] += corr.  Row value =
+// (hsum(acc_even) + hsum(acc_odd)) - (corr_even + corr_odd), hsum = ((v0+v4)+(v1+v5)) +
+// ((v2+v6)+(v3+v7)), returned in every lane of the row (lane 8r among them, as reduce4 does).
+// The activation codes are in lane order (kProA8X / kProRmsA8X): the word of lane j of group g
+// at x8 + 32g + 4j holds codes [4j, 4j+2, 4j+1, 4j+3], the byte order of the nibble word below.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float band_exact(uint32_t sq, uint32_t sm, int K, const XAddr& xs, int lane) {
+    const int nq = K >> 5;
+    const uint32_t r = static_cast<uint32_t>(lane >> 3), j = static_cast<uint32_t>(lane & 7);
+    const uint32_t qa = sq + r * 16u + j * 2u;                    // + 64 g (quant band: [ng][4 rows][16 B])
+    const uint32_t ma = sm + r * static_cast<uint32_t>(nq) * 4u;  // + 4 g  (meta band: [4 rows][ng][4 B])
+    const uint32_t xa = xs.x8 + j * 4u;                           // + 32 g
+    float acc0 = 0.0f, acc1 = 0.0f, cor0 = 0.0f, cor1 = 0.0f;
+    auto group = [&](int g, float& acc, float& cor) {
+        const uint32_t ug = static_cast<uint32_t>(g);
+        const uint32_t w16 = lds16(qa + ug * 64u);
+        const uint32_t word = (w16 & 0x0F0Fu) | ((w16 << 12) & 0x0F0F0000u);  // [e0, e2, e1, e3]
+        const int d = dp4a_us(word, lds32(xa + ug * 32u), 0);
+        const float2 sz = half2_bits_to_float2(lds32(ma + ug * 4u));  // (ws, wz)
+        const float xsc = ldsf(xs.xs + 4u * ug), xss = ldsf(xs.xss + 4u * ug);
+        const float comb = __fmul_rn(sz.x, xsc);
+        acc = __fadd_rn(acc, __fmul_rn(small_int_to_float(d), comb));
+        cor = __fadd_rn(cor, __fmul_rn(__fmul_rn(sz.y, sz.x), xss));
+    };
+    int g = 0;
+#pragma unroll 4
+    for (; g + 1 < nq; g += 2) {
+        group(g, acc0, cor0);
+        group(g + 1, acc1, cor1);
+    }
+    if (g < nq) group(g, acc0, cor0);
+    auto hsum8 = [](float v) {
+        const float a = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+        const float b = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        return __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, 2));
+    };
+    return __fsub_rn(__fadd_rn(hsum8(acc0), hsum8(acc1)), __fadd_rn(cor0, cor1));
+}
+
 // rotate a lane's four partials back to row order: v[j] = a[(j - rot) & 3]
 __device__ __forceinline__ void unrotate(float a[4], int rot) {
     if (rot & 1) {
@@ -762,7 +856,7 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                                float& best_v, int& best_i) {
     using T = FmtTraits<FMT>;
     constexpr int NS = T::kStreams;
-    constexpr int NSEG = (EPI == kEpiSilu) ? 2 : 1;
+    constexpr int NSEG = epi_is_silu(EPI) ? 2 : 1;
     const int lane = threadIdx.x & 31;
     const int cw = threadIdx.x >> 5;
     const int CU = pa.units_per_chunk;
@@ -924,9 +1018,14 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                 if constexpr (NS > 1)
                     p1 = (seg == 0 ? ub[0][NS - 1] : ub[NSEG - 1][NS - 1]) +
                          static_cast<uint32_t>(k) * static_cast<uint32_t>(pa.s[NS - 1].unit_bytes);
-                band_compute<FMT>(a, p0, p1, K, pa.row_bytes, xad, lane, rr_lane, q0, q1);
-                unrotate(a, rot);
-                const float v = reduce4(a, lane);
+                float v;
+                if constexpr (FMT == kFmtPreq2X) {
+                    v = band_exact(p0, p1, K, xad, lane);
+                } else {
+                    band_compute<FMT>(a, p0, p1, K, pa.row_bytes, xad, lane, rr_lane, q0, q1);
+                    unrotate(a, rot);
+                    v = reduce4(a, lane);
+                }
                 float vrow[NSEG];
                 bool finish = true;
                 if (IPU > 1) {
@@ -964,6 +1063,8 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                         ga.resid[row] = __fadd_rn(vrow[0], __ldcg(ga.resid + row));
                     } else if constexpr (EPI == kEpiSilu) {
                         ga.h[row] = ref_silu_mul(vrow[0], vrow[NSEG - 1]);
+                    } else if constexpr (EPI == kEpiSiluX) {
+                        ga.h[row] = exact_silu_mul(vrow[0], vrow[NSEG - 1], ga.ex.rcp);
                     } else {
                         if (ga.y) ga.y[row] = vrow[0];
                         argmax_take(best_v, best_i, vrow[0], ga.row_base + static_cast<int>(row));
@@ -986,11 +1087,12 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
 // ---------------------------------------------------------------------------
 template <int FMT, int PRO, int EPI, int NT = 1>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
-    static_assert(NT == 1 || ((EPI == kEpiStore || EPI == kEpiResid) && FMT != kFmtPacked),
-                  "multi-token: store or residual epilogue, W4A8 formats");
+    static_assert(NT == 1 || ((EPI == kEpiStore || EPI == kEpiResid) && FMT != kFmtPacked && FMT != kFmtPreq2X),
+                  "multi-token: store or residual epilogue, W4A8 formats, not the exact mode");
+    static_assert((FMT == kFmtPreq2X) == pro_is_lane_order(PRO), "kFmtPreq2X pairs with the lane-order prologues");
     using T = FmtTraits<FMT>;
     constexpr int NS = T::kStreams;
-    constexpr int NSEG = (EPI == kEpiSilu) ? 2 : 1;
+    constexpr int NSEG = epi_is_silu(EPI) ? 2 : 1;
     constexpr bool kF32 = (PRO == kProF32);
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);

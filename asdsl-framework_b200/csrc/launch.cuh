@@ -225,7 +225,9 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     long long cu = ps.cu;
     int parts = ps.parts;
     const int nq = ga.K / 32;
-    if (opt.k_parts > 0) {
+    if (FMT == kFmtPreq2X) {
+        parts = 1;  // exact mode: each row's groups are summed in order by the threads of one warp
+    } else if (opt.k_parts > 0) {
         // a forced split must cut K into parts of whole lane iterations (32 slices)
         if (opt.k_parts > 1 &&
             (opt.k_parts > 8 || nq % (32 * opt.k_parts) != 0 || FmtTraits<FMT>::kRowsPerUnit != 4))
@@ -279,7 +281,7 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     pa.split_off = pa.stage_off + static_cast<uint32_t>(stages) * stage_bytes;
     pa.row_bytes = opt.row_bytes;
     if (PRO != kProQ8 && !aligned16(ga.x)) return set_error(kEinval, "activations must be 16-byte aligned");
-    if (PRO == kProRmsA8 && !aligned16(ga.norm_w)) return set_error(kEinval, "norm weights must be 16-byte aligned");
+    if (pro_is_rms(PRO) && !aligned16(ga.norm_w)) return set_error(kEinval, "norm weights must be 16-byte aligned");
     if (PRO == kProQ8 && (reinterpret_cast<uintptr_t>(ga.xq) & 3u))
         return set_error(kEinval, "int8 activations must be 4-byte aligned");
     const uint32_t smem = pa.split_off + split_bytes;

@@ -244,6 +244,26 @@ int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const 
 int asdsl_b200_gemv_multi(int fmt, const uint8_t* w0, const uint8_t* w1, const float* X, float* Y,
                           int out_features, int in_features, int n_tokens, void* stream);
 
+/* Reference-exact GEMVs (see ASDSL_B200_NUMERICS_REFERENCE_EXACT): gemv_preq2_fused_avx2
+ * (gemv_preq2_avx2.cpp:301-319) with every row summed as the compiled process_one_row does
+ * (:216-253), bit-identical to the reference kernel.  norm_w non-null folds the engine's
+ * preceding rmsnorm_f32(x) * norm_w in first (unified_engine.cpp:499-524, RSQRTSS + Newton as
+ * compiled; in_features % 8 == 0).  gateup_silu_exact: the gate_up GEMV (rows [0, 2I)) followed
+ * by swiglu_inplace (:836-857, RCPPS + Newton as compiled) -> h[I]. */
+int asdsl_b200_gemv_preq2_fused_exact(const uint8_t* meta, const uint8_t* quant, const float* x, const float* norm_w,
+                                      float eps, float* y, int M, int K, void* stream);
+int asdsl_b200_gateup_silu_exact(const uint8_t* meta, const uint8_t* quant, const float* x, const float* norm_w,
+                                 float eps, float* h, int I, int K, void* stream);
+/* Builds (once per process) the host tables of the reference-exact mode and uploads them to
+ * the current device; *n_exp_exceptions = number of inputs where the C library's expf is not
+ * the correctly rounded exp.  asdsl_b200_exact_host_tables copies the host tables out (tests):
+ * rcp[2048], rsqrt[2048], exp_exc[2 * n] (input bits, expf bits) when exp_cap >= n. */
+int asdsl_b200_exact_numerics_init(int* n_exp_exceptions);
+int asdsl_b200_exact_host_tables(uint32_t* rcp, uint32_t* rsqrt, uint32_t* exp_exc, int exp_cap, int* n_exp);
+/* The attention's expf of the reference-exact mode over a device array (x <= 0; tests): the
+ * C library's expf (unified_engine.cpp:989, :1000) bit for bit. */
+int asdsl_b200_exact_expf(const float* x, float* y, long long n, void* stream);
+
 /* ======================================================================================
  * Device-resident decode engine: UnifiedEngine (asdsl/kernels/native/unified_engine.h:14-109,
  * :134-282; unified_engine.cpp) for the C0 decode path.  The engine owns its device memory
@@ -341,6 +361,20 @@ int asdsl_b200_engine_stream(asdsl_b200_engine* e, void** stream);
  * launch); 1 runs each step as one cooperative kernel over a program of ops with grid barriers
  * between them.  The environment variable ASDSL_B200_DECODE_KERNEL=persistent selects 1 at
  * create. */
+/* Numerics of the decode step, set before finalize (no reference switch: the reference has one
+ * numerics, its compiled code's).  ASDSL_B200_NUMERICS_FAST: the streaming kernels' own fp32
+ * summation order (every GEMV within 1e-3 of the reference; the default).
+ * ASDSL_B200_NUMERICS_REFERENCE_EXACT: every op in the operation order of the reference's
+ * -ffast-math build -- forward_token (unified_engine.cpp:1339-1688) with process_one_row's
+ * 8-lane accumulators (gemv_preq2_avx2.cpp:216-253), rmsnorm_f32's RSQRTSS + Newton step
+ * (:499-524), swiglu_inplace's RCPPS + Newton step (:836-857), set_kv_cache's 127/absmax
+ * (:859-920) and attention's C-library expf (:922-1027) -- so logits and greedy tokens are
+ * bit-identical to the reference's on this host.  Needs an x86 host (the approximate-reciprocal
+ * and expf tables are captured from its CPU and C library on first use: about a second), preq2
+ * gs 32 weights, head_dim 128 and max_seq_len <= 4096; forward_batch runs serial steps. */
+#define ASDSL_B200_NUMERICS_FAST 0
+#define ASDSL_B200_NUMERICS_REFERENCE_EXACT 1
+int asdsl_b200_engine_set_numerics(asdsl_b200_engine* e, int mode);
 int asdsl_b200_engine_set_persistent(asdsl_b200_engine* e, int persistent);
 /* Per-op profile of one step of the persistent decode kernel at the current position (the
  * device-side counterpart of the reference's ASDSL_ENGINE_PROFILE per-op breakdown,

@@ -59,6 +59,13 @@ static inline uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] <
  * and GCC's one-step Newton refinements of them under -ffast-math (operand order as emitted). */
 static inline float x86_rsqrt(float a) { return _mm_cvtss_f32(_mm_rsqrt_ss(_mm_set_ss(a))); }
 static inline float x86_rcp(float a) { return _mm_cvtss_f32(_mm_rcp_ss(_mm_set_ss(a))); }
+float or_host_rcp(float a) { return x86_rcp(a); }
+float or_host_rsqrt(float a) { return x86_rsqrt(a); }
+/* the C library's expf over an array (the reference's attention calls it, unified_engine.cpp:989) */
+void or_expf_array(const float* x, float* y, long n) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < n; ++i) y[i] = expf(x[i]);
+}
 float or_nr_rsqrt(float a) {
     const float x0 = x86_rsqrt(a);
     const float t = fmaf(x0, x0 * a, -3.0f);

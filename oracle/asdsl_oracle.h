@@ -47,6 +47,9 @@ void or_lmhead_quant_q4_128(const uint16_t* w_f16, uint8_t* blocks, int rows, in
 
 /* GCC -ffast-math's 1/sqrt(a) and 1/d on this host: RSQRTSS / RCPSS estimate + one Newton step */
 float or_nr_rsqrt(float a);
+float or_host_rcp(float a);   /* the host's raw RCPSS / RSQRTSS estimates */
+float or_host_rsqrt(float a);
+void or_expf_array(const float* x, float* y, long n);
 float or_nr_recip(float d);
 
 /* Engine ops (unified_engine.cpp) */

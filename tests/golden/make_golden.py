@@ -34,9 +34,12 @@ sys.path.insert(0, os.path.join(ROOT, "asdsl-framework_b200"))
 sys.path.insert(0, ROOT)
 
 
-def ref_engine(nu, model):
+def ref_engine(nu, model, preq_blocks: bool = True):
     """The reference's UnifiedEngine over a synthetic model (preq blocks + preq2 blobs per layer,
-    tied fp16 embedding as lm_head source), as unified_bridge.build_unified_engine wires it."""
+    tied fp16 embedding as lm_head source), as unified_bridge.build_unified_engine wires it.
+    preq_blocks=False passes one-byte placeholders for the 20-byte preq blocks, which the engine
+    binds but never reads when preq2 blobs are present (ASDSL_PREQ2=1, unified_engine.cpp:129-143):
+    the full-size model then needs no second copy of its weights."""
     from asdsl_b200.quantization.repack import preq2_to_preq
 
     c = model["config"]
@@ -54,7 +57,8 @@ def ref_engine(nu, model):
     for li, L in enumerate(model["layers"]):
         d = {"rms_att": L["rms_att"], "rms_ffn": L["rms_ffn"]}
         for name, (r, k) in shapes.items():
-            d[name] = preq2_to_preq(L[name + "_meta"], L[name + "_quant"], r, k).reshape(-1)
+            d[name] = (preq2_to_preq(L[name + "_meta"], L[name + "_quant"], r, k).reshape(-1) if preq_blocks
+                       else np.zeros(1, np.uint8))
             d[name + "_meta"] = L[name + "_meta"]
             d[name + "_quant"] = L[name + "_quant"]
         layers[li] = d
