@@ -5,6 +5,9 @@
 // declared in include/asdsl_b200.h with the reference interface it replaces.
 #include "../../include/asdsl_b200.h"
 
+#include <utility>
+#include <vector>
+
 #include "launch.cuh"
 #include "weight_prep.cuh"
 #include "gemv_mma.cuh"
@@ -411,7 +414,9 @@ int gemv_argmax_impl(int fmt, const uint8_t* w0, const uint8_t* w1, const float*
     if (!w0 || !x || !out_val || !out_idx || !scratch) return set_error(kEinval, "gemv_argmax: null pointer");
     if (scratch_bytes < asdsl_b200_argmax_scratch_bytes()) return set_error(kEinval, "gemv_argmax: scratch too small");
     if (M <= 0) return set_error(kEinval, "gemv_argmax: invalid dimensions");
-    if (sm_count() > 1024) return set_error(kEinval, "gemv_argmax: too many SMs for the scratch layout");
+    // the scratch holds one (value, index) pair per CTA of the grid, at fixed 1024-entry offsets
+    if (static_cast<long long>(sm_count()) * launch_policy().ctas_per_sm > 1024)
+        return set_error(kErange, "gemv_argmax: the grid exceeds the scratch layout's 1024 CTAs");
     uint8_t* sc = static_cast<uint8_t*>(scratch);
     GemvArgs ga;
     StreamIn s[2];
@@ -540,6 +545,8 @@ int asdsl_b200_xchg_destroy(asdsl_b200_xchg* x) {
 int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
                                 float* out_val, int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes,
                                 int M, int K, asdsl_b200_xchg* xg, void* stream) {
+    if (row_base < 0)
+        return set_error(kEinval, "gemv_argmax_xchg: row_base must be >= 0 (the exchange packs a 24-bit index)");
     if (!xg || !xg->open) return set_error(kEinval, "gemv_argmax_xchg: exchange not opened");
     if (static_cast<long long>(row_base) + M > (1ll << 24))
         return set_error(kEinval, "gemv_argmax_xchg: global row indices must stay below 2^24");
@@ -604,23 +611,40 @@ int asdsl_b200_selftest_bounded_wait(int which, void* stream) {
 // ---------------------------------------------------------------------------
 // Activation scratch of the multi-token GEMVs: the tokens of one pass are quantized once into a
 // slot (at most half the shared-memory budget, the per-pass limit) by k_quant_tokens.  A static
-// device array (no allocation, so captured graphs need no warm-up call), handed out round-robin
-// from a ring of kTokSlots per device: calls overlapping on more streams than that would share one.
+// device array (no allocation, so captured graphs need no warm-up call) of kTokSlots slots per
+// device.  Each stream keeps one slot: the calls of one stream are ordered (k_quant_tokens waits
+// for the previous kernel of its stream before it writes), and the first kTokSlots streams that
+// call on a device get distinct slots.  Later streams share slots (assigned in turn), so
+// multi-token calls on more than kTokSlots streams of one device must not overlap.
 constexpr int kTokSlots = 8;
 constexpr size_t kTokSlotBytes = kSmemBudget / 2;
 static __device__ __align__(128) unsigned char g_tok_scratch[kTokSlots * kTokSlotBytes];
 
 namespace {
-int token_scratch_slot(uint8_t** out) {
+int token_scratch_slot(cudaStream_t st, uint8_t** out) {
     static std::mutex mu;
     static void* base[64] = {nullptr};
     static unsigned next[64] = {0};
+    static std::vector<std::pair<cudaStream_t, unsigned>> owner[64];  // stream -> slot
     int dev = 0;
     ASDSL_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(kEinval, "gemv_multi: device index out of range");
     std::lock_guard<std::mutex> lk(mu);
     if (!base[dev]) ASDSL_CUDA(cudaGetSymbolAddress(&base[dev], g_tok_scratch));
-    *out = static_cast<uint8_t*>(base[dev]) + (next[dev]++ % kTokSlots) * kTokSlotBytes;
+    unsigned slot = 0;
+    bool found = false;
+    for (const auto& o : owner[dev])
+        if (o.first == st) {
+            slot = o.second;
+            found = true;
+            break;
+        }
+    if (!found) {
+        slot = next[dev]++ % kTokSlots;
+        owner[dev].emplace_back(st, slot);
+        if (owner[dev].size() > 4096) owner[dev].erase(owner[dev].begin());  // bounded table
+    }
+    *out = static_cast<uint8_t*>(base[dev]) + slot * kTokSlotBytes;
     return kOk;
 }
 
@@ -630,7 +654,7 @@ int quant_tokens(GemvArgs& ga, int T, cudaStream_t st) {
     const uint32_t xa_stride = xarea_layout_bytes(ga.K, ga.gs, false);
     if (static_cast<size_t>(xa_stride) * T > kTokSlotBytes) return set_error(kEinval, "internal: token scratch too small");
     uint8_t* slot = nullptr;
-    if (int rc = token_scratch_slot(&slot)) return rc;
+    if (int rc = token_scratch_slot(st, &slot)) return rc;
     GemvArgs g = ga;
     g.n_tokens = T;
     void* args[] = {&g, &slot, const_cast<uint32_t*>(&xa_stride)};

@@ -145,7 +145,7 @@ def cpu_layer_step_runner(hosts: list[dict]):
             o = rk.gemv_preq2_fused(host["o_meta"], host["o_quant"], qkv[:QD], H, QD)
             xq, xs = rk.quantize_activation(o, 128)
             gu = rk.gemv_q4_128_q8(host["gate_up_q4_128"], xq, xs, 2 * I, H)
-            h = orc.swiglu(gu[:I], gu[I:])
+            h = rk.swiglu(gu[:I], gu[I:])  # the reference's own swiglu_inplace
             hq, hs = rk.quantize_activation(h, 128)
             y = rk.gemv_q4_128_q8(host["down_q4_128"], hq, hs, H, I)
         else:
@@ -159,6 +159,34 @@ def cpu_layer_step_runner(hosts: list[dict]):
     return step, kind
 
 
+def host_cpu_setup() -> dict:
+    """All host cores for the reference's OpenMP loops, whatever OMP_NUM_THREADS the launcher set
+    (torchrun exports 1): the reference library's OpenMP runtime (libgomp) gets omp_set_num_threads
+    before its first parallel region.  Returns what the CPU arm ran with."""
+    import ctypes
+
+    cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    threads = cores
+    try:
+        gomp = ctypes.CDLL("libgomp.so.1")
+        gomp.omp_set_num_threads(cores)
+        threads = int(gomp.omp_get_max_threads())
+    except OSError:
+        pass
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            model = next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), "")
+    except OSError:
+        pass
+    from oracle.oracle import host_has_avx_vnni, ref_lib_path
+
+    lib = ref_lib_path() or ""
+    return {"cores": cores, "omp_threads": threads, "cpu_model": model, "avx_vnni": host_has_avx_vnni(),
+            "reference_build": "-mavxvnni (HAVE_AVXVNNI dpbusd path)" if "/vnni/" in lib else "AVX2 (maddubs path)"}
+
+
 def time_cpu(step, budget_s: float, min_steps: int = 3, max_steps: int = 10**6):
     step()  # warm (page-in, OpenMP pool)
     n, t0 = 0, time.perf_counter()
@@ -169,6 +197,7 @@ def time_cpu(step, budget_s: float, min_steps: int = 3, max_steps: int = 10**6):
 
 
 def run_reference(args, host, bytes_per_step):
+    hw = host_cpu_setup()
     step, kind = cpu_layer_step_runner(host_copies(host, args.copies))
     for _ in range(max(args.warmup, 0)):
         step()
@@ -177,12 +206,13 @@ def run_reference(args, host, bytes_per_step):
         step()
     dt = time.perf_counter() - t0
     gbs = bytes_per_step * args.steps / dt / 1e9
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    cores = hw["omp_threads"]
     return {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u4 x s8 -> f32 (W4A8)", "data": "synthetic",
-        "config": {"workload": "c1_layer_projection_set", "seed": 1, "global_batch": 1, "cpu_threads": cores},
+        "config": {"workload": "c1_layer_projection_set", "seed": 1, "global_batch": 1, "cpu_threads": cores,
+                   "host": hw},
         "impl": "reference",
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
                          "sample": f"{args.steps} full config-1 layer steps on the host cores, "
@@ -197,11 +227,56 @@ def run_reference(args, host, bytes_per_step):
 DECODE_METRIC = "Q4 decode tokens/sec at batch 1 (Phi-4-mini shape, C0 preq2 gs32)"
 
 
-def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: bool = True, world: int = 1,
-                 prefill_tokens: int = 128) -> dict:
+def reference_trajectory(model, steps: int, prompt_token: int) -> dict:
+    """The reference's UnifiedEngine (oracle/_ref, compiled from its sources; on the host cores)
+    on the bytes of `model` (a build_model_device model): first-step logits and the greedy tokens
+    of generate([prompt_token], steps).  Falls back to the oracle engine (bit-identical to the
+    reference engine: tests/test_oracle_exact.py) when the reference was not built."""
+    import numpy as np
+
+    from asdsl_b200.inference.synthetic import model_to_host
+    from oracle.oracle import Oracle, OracleEngine, build as build_oracle, ref_lib_path
+
+    host_cpu_setup()
+    host = model_to_host(model)
+    t0 = time.perf_counter()
+    if ref_lib_path():
+        sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+        from make_golden import load_ref_unified, ref_engine
+
+        eng = ref_engine(load_ref_unified(), host, preq_blocks=False)
+        logits0 = np.array(eng.forward_token(prompt_token, 0), copy=True)
+        eng.reset_session()
+        toks = [int(t) for t in eng.generate([prompt_token], steps)]
+        kind = "reference"
+        del eng
+    else:
+        if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+            build_oracle()
+        orc = Oracle()
+        c = host["config"]
+        host["lm_meta"], host["lm_quant"] = orc.lmhead_quant_preq2(host["embed_f16"], c["vocab"], c["hidden"])
+        eng = OracleEngine(host, orc)
+        logits0 = eng.forward_token(prompt_token, 0)
+        eng.close()
+        eng = OracleEngine(host, orc)
+        toks, _ = eng.generate([prompt_token], steps)
+        eng.close()
+        kind = "port"
+    dt = time.perf_counter() - t0
+    return {"logits0": logits0, "tokens": toks, "kind": kind, "cpu_s": dt, "steps": steps}
+
+
+def decode_bench(model, numerics: str = "fast", ref: dict | None = None, steps: int = 128, seed: int = 3,
+                 prompt_token: int = 1, world: int = 1, prefill_tokens: int = 128) -> dict:
     """Tokens/s of the engine's greedy decode on the full Phi-4-mini shape (
     32 layers, all projections preq2 gs32, tied fp16 embedding quantized on the device into the
-    lm_head, norms 1.0, int8 KV), random-init weights from `seed`.
+    lm_head, norms 1.0, int8 KV), random-init weights `model` (build_model_device, seed 3).
+
+    numerics "reference_exact": every op in the reference's compiled order; its first-step logits
+    must equal the reference engine's bit for bit and its greedy tokens the reference's for all
+    `steps` (checked against `ref`).  "fast": the streaming kernels' own summation order; its
+    distance to the reference is reported.
 
     value: `steps` decode-graph replays from position 0 on the engine stream, inputs resident
     (CUDA events on that stream).  e2e: generate([prompt], steps) through the public API (prompt
@@ -211,44 +286,29 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
     import torch
 
     from asdsl_b200 import _lib
-    from asdsl_b200.inference.synthetic import PHI4_MINI, build_model_device, model_to_host
     from asdsl_b200.kernels._native_unified import engine_from_model
 
-    # every projection float32 N(0, 0.02) from the device RNG, then the reference's C0 weight
-    # pipeline (quantize_weights gs 32 asymmetric + clip search -> preq -> preq2) on the device;
-    # at N > 1 each rank is an independent replica (weak scaling)
-    model = build_model_device(PHI4_MINI, seed=seed, quantized=True)
-    if world > 1:
-        gate = False
-    eng = engine_from_model(model)
+    exact = numerics == "reference_exact"
+    eng = engine_from_model(model, numerics=numerics)
     c = model["config"]
     nbytes = lambda v: v.numel() * v.element_size() if hasattr(v, "element_size") else v.nbytes  # noqa: E731
     weight_bytes = sum(int(nbytes(v)) for L in model["layers"] for k, v in L.items() if k.endswith(("_meta", "_quant")))
     ng = c["hidden"] // 32
     lm_bytes = c["vocab"] * ng * 4 + ((c["vocab"] + 3) // 4) * ng * 64
+    if exact:
+        prefill_tokens = 0  # forward_batch is serial in this mode
     try:
-        gate_err = None
-        if gate:
-            # first decode step against the CPU oracle engine on the same bytes
-            from oracle.oracle import Oracle, OracleEngine, build as build_oracle, rel_err
+        gate_err, logits_bitwise = None, None
+        if ref is not None and prompt_token == ref["tokens"][0]:
+            from oracle.oracle import rel_err
 
-            if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
-                build_oracle()
-            orc = Oracle()
-            host = model_to_host(model)
-            host["lm_meta"], host["lm_quant"] = orc.lmhead_quant_preq2(host["embed_f16"], c["vocab"], c["hidden"])
-            ref = OracleEngine(host, orc)
-            try:
-                lo = ref.forward_token(prompt_token, 0)
-            finally:
-                ref.close()
-            del host
             la = eng.forward_token(prompt_token, 0).copy()
-            gate_err = rel_err(la, lo)
-            # 32 layers of per-group int8 re-quantization amplify last-ulp summation-order
-            # differences: the reference engine and the oracle differ by 0.055 on this step
+            gate_err = rel_err(la, ref["logits0"])
+            logits_bitwise = bool(np.array_equal(la.view(np.uint32), np.asarray(ref["logits0"], np.float32).view(np.uint32)))
+            if exact and not logits_bitwise:
+                raise SystemExit(f"bench: reference-exact decode logits differ from the reference engine ({gate_err})")
             if gate_err > 0.2:
-                raise SystemExit(f"bench: decode logits mismatch vs oracle ({gate_err})")
+                raise SystemExit(f"bench: decode logits mismatch vs the reference engine ({gate_err})")
             eng.reset_session()
         stream = torch.cuda.ExternalStream(eng.stream_ptr())
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -292,6 +352,12 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         assert len(toks) == steps + 1
+        same = None
+        if ref is not None and ref["tokens"][0] == prompt_token:
+            n = min(len(toks), len(ref["tokens"]))
+            same = next((i for i in range(n) if toks[i] != ref["tokens"][i]), n) - 1  # generated tokens equal
+            if exact and same < min(steps, ref["steps"]):
+                raise SystemExit(f"bench: reference-exact greedy tokens part from the reference's after {same} steps")
         # prompt prefill and speculative verify through the public API (1 GPU only: side figures,
         # not timed across ranks), events on the engine stream around each call:
         #   prefill: prefill_tokens seeded tokens from position 0, serial = forward_token_prefill per
@@ -334,6 +400,11 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
     achieved = bytes_per_token * tok_s / world / 1e9  # per GPU
     return {
         "metric": DECODE_METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "steps": steps,
+        "numerics": numerics,
+        "reference_check": ({"kind": ref["kind"], "first_logits_bitwise": logits_bitwise,
+                             "first_logits_rel_err": gate_err, "greedy_tokens_identical": same,
+                             "of_steps": min(steps, ref["steps"]), "reference_cpu_s": round(ref["cpu_s"], 1)}
+                            if ref is not None else None),
         "ms_per_token": round(ms / steps, 4), "higher_is_better": True, "n_gpus": world,
         "scaling": "weak" if world > 1 else None,
         "parallelism": f"replica x{world} (one independent batch-1 sequence per GPU)" if world > 1 else "1 GPU",
@@ -348,7 +419,6 @@ def decode_bench(steps: int = 128, seed: int = 3, prompt_token: int = 1, gate: b
         "e2e": {"value": round(world * steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4, "ms_total": round(e2e_ms, 3)},
         "gpu_launches": steps * (3 + 5 * c["num_layers"]),
-        "gate_logits_rel_err": gate_err,
         "prefill": ({"tokens": prefill_tokens, "serial_ms": round(pre["prefill_serial"], 3),
                      "batched_ms": round(pre["prefill_batched"], 3),
                      "serial_tokens_per_s": round(prefill_tokens / (pre["prefill_serial"] * 1e-3), 1),
@@ -570,22 +640,29 @@ LM_METRIC = "lm_head W4 GEMV + argmax HBM GB/s (200064x3072 Q4_128, row-sharded,
 
 
 def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dict:
-    """Strong scaling: the whole 200064-row lm_head is split over the ranks; a step is the local
-    fused GEMV + argmax, the all-gather of one (max, index) pair per rank (NCCL) and the device
-    pick of the first maximum.  value = all ranks' weight bytes / max-over-ranks step time.
+    """Strong scaling: the whole 200064-row lm_head is split over the ranks; a step is one kernel
+    per rank: the local fused GEMV + argmax and, at N > 1, the exchange of one (max, index) word
+    per rank over NVLink peer stores inside the same kernel, ending with the first maximum.
+    value = all ranks' weight bytes / max-over-ranks step time.  Weights as config 2 states:
+    fp32 N(0, 0.02) (device RNG, seed 2) through the reference's repack_fp32_to_q4_128_blocks
+    (asdsl_b200.quantization.device, byte-identical to the host pipeline), x ~ N(0, 1).
     Each rank rotates enough weight copies that a copy is reused only after > 300 MB (the L2 is
     126 MB)."""
     import numpy as np
     import torch
 
     from asdsl_b200 import _lib
-    from asdsl_b200.quantization.synth import random_q4_128
+    from asdsl_b200.quantization.device import repack_fp32_to_q4_128_device
     from asdsl_b200.shard import ShardedLMHead
 
     V, H = 200064, 3072
-    rng = np.random.default_rng(seed)
-    blocks = random_q4_128(rng, V, H)
-    x = rng.standard_normal(H).astype(np.float32)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    w = torch.randn((V, H), generator=g, device="cuda") * 0.02
+    blocks = repack_fp32_to_q4_128_device(w, V, H).cpu().numpy()
+    x = torch.randn(H, generator=g, device="cuda").cpu().numpy().astype(np.float32)
+    del w
+    torch.cuda.empty_cache()
     heads = [ShardedLMHead(blocks, V, H)]
     shard_bytes = heads[0].quant.numel() + heads[0].scales.numel()
     n_copies = max(1, -(-320_000_000 // shard_bytes))  # reuse distance > 300 MB, well past the L2
@@ -670,7 +747,8 @@ def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dic
             "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 5)},
             "check": check, "config": {"workload": "c2_lm_head_row_sharded", "seed": seed,
-                                       "weights": "random Q4_128 bytes (synthetic)"}}
+                                       "weights": "fp32 N(0, 0.02) (device RNG) -> repack_fp32_to_q4_128_blocks "
+                                                  "on the device (the reference's g128 quantizer)"}}
 
 
 # ---------------------------------------------------------------------------
@@ -706,8 +784,6 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        cores = os.cpu_count() or 1
-        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
         from asdsl_b200.layer import build_c1_host
 
         host = build_c1_host(1)
@@ -919,19 +995,31 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cores = os.cpu_count() or 1
-        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        hw = host_cpu_setup()
+        cores = hw["omp_threads"]
         step, kind = cpu_layer_step_runner(host_copies(host, args.copies))
         n, dt = time_cpu(step, args.cpu_budget)
         cpu = {"value": round(bytes_per_step * n / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+               "host": hw,
                "sample": f"{n} full config-1 layer steps ({dt:.1f} s) on the host cores, OpenMP threads = cores, "
                          f"rotating {args.copies} weight copies past the last-level cache"}
 
     c0 = None if args.no_c0 else c0_bench(world, rank)
     c4 = c4_bench(rank) if (args.c4 and world == 1) else None
-    decode = None
+    decode = decode_fast = None
     if not args.no_decode:
-        decode = decode_bench(args.decode_steps, world=world)
+        from asdsl_b200.inference.synthetic import PHI4_MINI, build_model_device
+
+        # every projection float32 N(0, 0.02) from the device RNG, then the reference's C0 weight
+        # pipeline (quantize_weights gs 32 asymmetric + clip search -> preq -> preq2) on the device;
+        # at N > 1 each rank is an independent replica (weak scaling)
+        dmodel = build_model_device(PHI4_MINI, seed=3, quantized=True)
+        ref = reference_trajectory(dmodel, args.decode_steps, 1) if (world == 1 and not args.no_cpu_baseline) else None
+        # the headline decode figure is the reference-exact mode: tokens bit-consistent with the
+        # reference's own engine; the fast mode's figure and its distance to the reference beside it
+        decode = decode_bench(dmodel, "reference_exact", ref, args.decode_steps, world=world)
+        decode_fast = decode_bench(dmodel, "fast", ref, args.decode_steps, world=world)
+        del dmodel
     lm_sharded = None if args.no_lm_head else lm_head_bench(world, rank)
 
     if rank == 0:
@@ -967,6 +1055,7 @@ def main():
             "c0_gemv": c0,
             "c4_multi": c4,
             "decode": decode,
+            "decode_fast": decode_fast,
             "lm_head_sharded": lm_sharded,
         }
         print(json.dumps(out), flush=True)

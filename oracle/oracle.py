@@ -31,14 +31,38 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(_P)
 
 
+def reference_root() -> str | None:
+    """The reference source tree: $ASDSL_REFERENCE, else a "reference" directory beside the repo."""
+    root = os.environ.get("ASDSL_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return root if os.path.isdir(os.path.join(root, "asdsl", "kernels", "native")) else None
+
+
 def build(ref: bool = False) -> None:
     """Build liboracle.so (and the reference library when `ref` and the sources exist)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if ref and os.path.isdir("/root/reference/asdsl/kernels/native"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", "-j8"], check=True)
+    root = reference_root()
+    if ref and root:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "-j8", f"REF={root}"], check=True)
+
+
+def host_has_avx_vnni() -> bool:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    return "avx_vnni" in line.split()
+    except OSError:
+        pass
+    return False
 
 
 def ref_lib_path() -> str | None:
+    """The reference library: its -mavxvnni build on hosts with AVX-VNNI (the reference's
+    HAVE_AVXVNNI path), else the plain AVX2 build."""
+    if host_has_avx_vnni():
+        c = glob.glob(os.path.join(REF_DIR, "vnni", "_native_unified*.so"))
+        if c:
+            return c[0]
     c = glob.glob(os.path.join(REF_DIR, "_native_unified*.so"))
     return c[0] if c else None
 
@@ -56,6 +80,25 @@ class Oracle:
         L.or_engine_create.restype = _P
         L.or_engine_forward_token.restype = _I
         L.or_argmax.restype = _I
+
+    # -- the host's approximate reciprocals and C-library expf (reference-exact checks)
+    def host_rcp(self, x: float) -> float:
+        f = self.lib.or_host_rcp
+        f.restype, f.argtypes = ctypes.c_float, [ctypes.c_float]
+        return f(x)
+
+    def host_rsqrt(self, x: float) -> float:
+        f = self.lib.or_host_rsqrt
+        f.restype, f.argtypes = ctypes.c_float, [ctypes.c_float]
+        return f(x)
+
+    def expf_array(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros_like(x)
+        f = self.lib.or_expf_array
+        f.restype, f.argtypes = None, [_P, _P, ctypes.c_long]
+        f(_p(x), _p(y), x.size)
+        return y
 
     # -- activation quantization
     def quantize_activation(self, x, gs=32):
@@ -274,6 +317,20 @@ class RefKernels:
         self._chk(self.lib.ref_gemv_preq2_fused(_p(np.ascontiguousarray(meta)), _p(np.ascontiguousarray(quant)),
                                                 _p(np.ascontiguousarray(x, np.float32)), _p(y), _I(M), _I(K), _I(32)))
         return y
+
+    def swiglu(self, gate, up):
+        """UnifiedEngine::swiglu_inplace (unified_engine.cpp:836-857): silu(gate) * up."""
+        g = np.array(gate, np.float32, copy=True)
+        u = np.array(up, np.float32, copy=True)
+        self._chk(self.lib.ref_swiglu(_p(g), _p(u), _I(g.size)))
+        return g
+
+    def rmsnorm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        self._chk(self.lib.ref_rmsnorm(_p(out), _p(x), _p(np.ascontiguousarray(w, np.float32)), _I(x.size),
+                                       ctypes.c_float(eps)))
+        return out
 
     def gemv_preq_q8(self, blocks, xq, xs, M, K):
         y = np.zeros(M, np.float32)

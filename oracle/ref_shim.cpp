@@ -9,8 +9,15 @@
  * by oracle/Makefile, next to the reference's sources compiled where they lie.
  */
 #include <cstdint>
+#include <cstdlib>
 #include <exception>
 #include <cstdio>
+
+// The engine ops (swiglu_inplace, rmsnorm_f32, ...) are private members of UnifiedEngine that
+// touch no member state; this test-only face opens them to call them on a zeroed object.
+#define private public
+#include "unified_engine.h"
+#undef private
 
 // Declarations of the reference's C++ entry points
 // (asdsl/kernels/native/gemv_q4_kernel.h:25-121, unified_engine.h:114-137).
@@ -83,6 +90,20 @@ int ref_gemv_q4_packed(const uint8_t* w, const float* x, const float* s, const f
 int ref_gemv_q4_unpacked(const uint8_t* w, const float* x, const float* s, const float* b, float* y,
                          int M, int K, int gs) {
     SHIM_TRY(gemv_q4_unpacked_impl(w, x, s, b, y, M, K, gs));
+}
+
+namespace {
+asdsl::UnifiedEngine* op_host() {
+    static void* p = std::calloc(1, sizeof(asdsl::UnifiedEngine));
+    return static_cast<asdsl::UnifiedEngine*>(p);
+}
+}  // namespace
+
+// UnifiedEngine::swiglu_inplace (unified_engine.cpp:836-857): gate[i] = silu(gate[i]) * up[i]
+int ref_swiglu(float* gate, float* up, int n) { SHIM_TRY(op_host()->swiglu_inplace(gate, up, n, 0.0f)); }
+// UnifiedEngine::rmsnorm_f32 (unified_engine.cpp:499-524)
+int ref_rmsnorm(float* out, const float* in, const float* w, int n, float eps) {
+    SHIM_TRY(op_host()->rmsnorm_f32(out, in, w, n, eps));
 }
 
 }  // extern "C"

@@ -1,8 +1,9 @@
 """Generate tests/golden/*.npz from the reference itself.  Run in a container where
-the reference is mounted (default /root/reference) and oracle/_ref is built
+the reference sources are present ($ASDSL_REFERENCE, or a "reference" directory beside the repo)
+and oracle/_ref is built
 (``make -C oracle ref``):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref PATH]
 
 Nothing at test time reads the reference; the fixtures carry its outputs.
 Sources of truth per fixture:
@@ -123,7 +124,9 @@ def gemm_q4_128() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    from oracle.oracle import reference_root
+
+    ap.add_argument("--ref", default=reference_root())
     ap.add_argument("--only", choices=["engine_long", "gemm_q4_128"], default=None)
     args = ap.parse_args()
     sys.path.insert(0, args.ref)

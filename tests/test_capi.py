@@ -76,6 +76,14 @@ def test_argument_errors_map_to_reference_exceptions(lib):
     with pytest.raises(ValueError, match="16-byte aligned"):
         _lib.call("asdsl_b200_gemm_q4_128_f32", 16, 20, 16, 16, 128, 128, 4, None)
     assert _lib.call("asdsl_b200_gemm_q4_128_f32", 16, 16, 16, 16, 128, 128, 0, None) == 0
+    # the cross-GPU argmax packs a 24-bit global row index: a negative row base is rejected
+    with pytest.raises(ValueError, match="row_base must be >= 0"):
+        _lib.call("asdsl_b200_gemv_argmax_xchg", 0, 16, 16, 16, 16, 16, 16, -4, 16, 1 << 16, 8, 64, None, None)
+    # reference-exact entries: the same host-side checks
+    with pytest.raises(ValueError, match="null pointer"):
+        _lib.call("asdsl_b200_gemv_preq2_fused_exact", None, None, None, None, 0.0, None, 16, 64, None)
+    with pytest.raises(ValueError, match="positive multiple of 4"):
+        _lib.call("asdsl_b200_gateup_silu_exact", 16, 16, 16, None, 0.0, 16, 6, 64, None)
 
 
 def test_python_api_fails_loudly_without_gpu():

@@ -53,10 +53,6 @@ def _emu_rsqrt(x, tab):
 
 def test_rcp_rsqrt_table_model_matches_host_instructions(tables, oracle):
     rcp, rsq, _ = tables
-    oracle.lib.or_host_rcp.restype = ctypes.c_float
-    oracle.lib.or_host_rsqrt.restype = ctypes.c_float
-    oracle.lib.or_host_rcp.argtypes = [ctypes.c_float]
-    oracle.lib.or_host_rsqrt.argtypes = [ctypes.c_float]
     rng = np.random.default_rng(0)
     e = rng.integers(1, 255, 4000).astype(np.uint32)
     m = rng.integers(0, 1 << 23, 4000).astype(np.uint32)
@@ -65,8 +61,8 @@ def test_rcp_rsqrt_table_model_matches_host_instructions(tables, oracle):
     got_s = _emu_rsqrt(xs, rsq)
     for i, xb in enumerate(xs):
         x = float(np.uint32(xb).view(np.float32))
-        assert np.float32(oracle.lib.or_host_rcp(x)).view(np.uint32) == got_r[i], hex(xb)
-        assert np.float32(oracle.lib.or_host_rsqrt(x)).view(np.uint32) == got_s[i], hex(xb)
+        assert np.float32(oracle.host_rcp(x)).view(np.uint32) == got_r[i], hex(xb)
+        assert np.float32(oracle.host_rsqrt(x)).view(np.uint32) == got_s[i], hex(xb)
 
 
 def test_expf_exceptions_match_c_library(tables, oracle):
@@ -77,14 +73,12 @@ def test_expf_exceptions_match_c_library(tables, oracle):
     rng = np.random.default_rng(1)
     pick = exc[rng.choice(len(exc), 4000, replace=False)]
     x = pick[:, 0].view(np.float32).copy()
-    y = np.zeros_like(x)
-    oracle.lib.or_expf_array(x.ctypes.data, y.ctypes.data, ctypes.c_long(x.size))
+    y = oracle.expf_array(x)
     assert np.array_equal(y.view(np.uint32), pick[:, 1])
     # away from the listed inputs, expf is exp in double rounded to float
     xr = -rng.uniform(0, 104, 300000).astype(np.float32)
     xr = xr[~np.isin(xr.view(np.uint32), keys)]
-    yr = np.zeros_like(xr)
-    oracle.lib.or_expf_array(xr.ctypes.data, yr.ctypes.data, ctypes.c_long(xr.size))
+    yr = oracle.expf_array(xr)
     libm = ctypes.CDLL("libm.so.6")
     libm.exp.restype = ctypes.c_double
     libm.exp.argtypes = [ctypes.c_double]
