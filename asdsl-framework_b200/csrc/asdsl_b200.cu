@@ -1024,17 +1024,16 @@ int asdsl_b200_gemv_preq2_fused_exact(const uint8_t* meta, const uint8_t* quant,
     if (!meta || !quant || !x || !y) return set_error(kEinval, "gemv_preq2_fused_exact: null pointer");
     if (int rc = check_k(K, 32, "gemv_preq2_fused_exact")) return rc;
     if (M < 0) return set_error(kEinval, "gemv_preq2_fused_exact: invalid dimensions");
-    StreamIn s[2];
-    preq2_streams(s, meta, quant, M, K);
     GemvArgs ga = base_args(M, K, 32);
     ga.x = x;
     ga.y = y;
-    if (!norm_w) return launch_stream_gemv<kFmtPreq2X, kProA8X, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+    if (M == 0) return kOk;
+    if (!norm_w) return launch_exact_gemv<kProA8X, kEpiStore>(meta, quant, M, 0, ga, as_stream(stream));
     if (K % 8) return set_error(kEinval, "gemv_preq2_fused_exact: RMSNorm needs in_features % 8 == 0");
     if (int rc = exact_tabs_device(&ga.ex)) return rc;
     ga.norm_w = norm_w;
     ga.eps = eps;
-    return launch_stream_gemv<kFmtPreq2X, kProRmsA8X, kEpiStore>(s, 2, (M + 3) / 4, 0, ga, as_stream(stream));
+    return launch_exact_gemv<kProRmsA8X, kEpiStore>(meta, quant, M, 0, ga, as_stream(stream));
 }
 
 int asdsl_b200_gateup_silu_exact(const uint8_t* meta, const uint8_t* quant, const float* x, const float* norm_w,
@@ -1042,18 +1041,15 @@ int asdsl_b200_gateup_silu_exact(const uint8_t* meta, const uint8_t* quant, cons
     if (!meta || !quant || !x || !h) return set_error(kEinval, "gateup_silu_exact: null pointer");
     if (I <= 0 || I % 4) return set_error(kEinval, "gateup_silu_exact: intermediate size must be a positive multiple of 4");
     if (int rc = check_k(K, 32, "gateup_silu_exact")) return rc;
-    StreamIn s[2];
-    preq2_streams(s, meta, quant, 2LL * I, K);
     GemvArgs ga = base_args(I, K, 32);
     if (int rc = exact_tabs_device(&ga.ex)) return rc;
     ga.x = x;
     ga.h = h;
-    const long long nb = I / 4;
-    if (!norm_w) return launch_stream_gemv<kFmtPreq2X, kProA8X, kEpiSiluX>(s, 2, nb, nb, ga, as_stream(stream));
+    if (!norm_w) return launch_exact_gemv<kProA8X, kEpiSiluX>(meta, quant, 2LL * I, I, ga, as_stream(stream));
     if (K % 8) return set_error(kEinval, "gateup_silu_exact: RMSNorm needs in_features % 8 == 0");
     ga.norm_w = norm_w;
     ga.eps = eps;
-    return launch_stream_gemv<kFmtPreq2X, kProRmsA8X, kEpiSiluX>(s, 2, nb, nb, ga, as_stream(stream));
+    return launch_exact_gemv<kProRmsA8X, kEpiSiluX>(meta, quant, 2LL * I, I, ga, as_stream(stream));
 }
 
 }  // extern "C"

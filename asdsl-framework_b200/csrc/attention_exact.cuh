@@ -2,7 +2,7 @@
 // (reference-exact numerics mode).
 //
 // Reference: rope_apply_inplace (unified_engine.cpp:768-801), set_kv_cache (:859-920) and
-// compute_attention_flash_q8 (:922-1027).  One CTA per query head, in the reference's order:
+// compute_attention_flash_q8 (:922-1027).  Per query head, the reference computes:
 //   * RoPE pairs (i, i + rot/2): o0 = fma(x_first, c, -(x_second*s)), o1 = fma(x_first, s, x_second*c);
 //   * int8 KV per 64-dim block: scale = absmax * fl(1/127) (1e-12 for a zero block), codes
 //     RNE(x * 127/absmax) (the compiled code folds 1/scale into 127/absmax; 1e12 for a zero block)
@@ -15,8 +15,11 @@
 //     tile_num[d] = fma(w_p, v[d]*scale, tile_num[d]) in position order; l = l*old + tile_l
 //     (two roundings); num[d] = fma(num[d], old, tile_num[d]);
 //   * out[d] = num[d] * (1/l).
-// Thread d < 128 owns dim d; every thread replays the (m, l) bookkeeping, so no broadcast is
-// needed.  The scores of all positions live in shared memory (max_seq <= kAttnXMaxSeq).
+// A tile's (tile_l, tile_num) depend only on the running maximum through that tile, so this
+// kernel (one CTA per query head) computes every score, the running maxima (a short sequential
+// scan over tiles), every weight, and all tiles' sums in parallel; only the final merge over
+// tiles runs in order.  The cached K/V of earlier positions (up to kAttnXPrefetch of them) are
+// copied into shared memory before the dependency wait, overlapping the qkv GEMV.
 #pragma once
 
 #include "engine_ops.cuh"
@@ -27,29 +30,79 @@ namespace asdsl {
 constexpr int kAttnXThreads = 256;
 constexpr int kAttnXMaxSeq = 4096;
 constexpr int kAttnXTile = 64;
+constexpr int kAttnXPrefetch = 256;   // positions of cached K/V staged in shared memory
+constexpr int kAttnXRow = kAttnHeadDim + 16;  // padded K row (conflict-free 16-byte loads per thread)
 
-struct AttnXSmem {
-    float q[kAttnHeadDim];
-    float k[kAttnHeadDim];  // this position's dequantized k, v (what the cache read gives back)
-    float v[kAttnHeadDim];
-    float red[2][2][2];
-    float w[kAttnXTile];
-    float vs[kAttnXTile][2];
-    alignas(16) int8_t vt[kAttnXTile][kAttnHeadDim];
-    float s[kAttnXMaxSeq];
+struct AttnXLayout {
+    uint32_t s, w, tile, tn, kc, vc, ksc, vsc, total;
 };
 
+// shared-memory layout of one head for a cache of max_seq positions (bytes, 16-aligned pieces)
+__host__ __device__ inline AttnXLayout attn_x_layout(int max_seq) {
+    const uint32_t nt = static_cast<uint32_t>((max_seq + kAttnXTile - 1) / kAttnXTile);
+    const uint32_t np = static_cast<uint32_t>(max_seq < kAttnXPrefetch ? max_seq : kAttnXPrefetch);
+    AttnXLayout L;
+    uint32_t o = 0;
+    auto take = [&](uint32_t bytes) {
+        const uint32_t at = o;
+        o += (bytes + 15u) & ~15u;
+        return at;
+    };
+    L.s = take(4u * max_seq);
+    L.w = take(4u * max_seq);
+    L.tile = take(4u * 4u * nt);  // per tile: running max, old scale, tile_l, tile max
+    L.tn = take(4u * nt * kAttnHeadDim);
+    L.kc = take(np * kAttnXRow);
+    L.vc = take(np * kAttnHeadDim);
+    L.ksc = take(8u * np);
+    L.vsc = take(8u * np);
+    L.total = o;
+    return L;
+}
+
 __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, ExactTabs ex, float inv_sqrt_d) {
-    __shared__ AttnXSmem S;
+    extern __shared__ __align__(16) uint8_t dsm[];
+    __shared__ float q_s[kAttnHeadDim], k_s[kAttnHeadDim], v_s[kAttnHeadDim];
+    __shared__ float red[2][2][2];
     constexpr int hd = kAttnHeadDim;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
     const int g = h / groups;
     const int half = a.rot / 2;
+    const AttnXLayout L = attn_x_layout(a.max_seq);
+    float* s_s = reinterpret_cast<float*>(dsm + L.s);
+    float* w_s = reinterpret_cast<float*>(dsm + L.w);
+    float* tile_s = reinterpret_cast<float*>(dsm + L.tile);  // [nt][4]: m_t, old_t, tl_t, tmax_t
+    float* tn_s = reinterpret_cast<float*>(dsm + L.tn);
+    int8_t* kc_s = reinterpret_cast<int8_t*>(dsm + L.kc);
+    int8_t* vc_s = reinterpret_cast<int8_t*>(dsm + L.vc);
+    float* ksc_s = reinterpret_cast<float*>(dsm + L.ksc);
+    float* vsc_s = reinterpret_cast<float*>(dsm + L.vsc);
+
+    // the position is final here: the embedding kernel of this step ran to completion first
+    const int pos = a.st->pos;
+    const bool ok = pos >= 0 && pos < a.max_seq && pos < kAttnXMaxSeq;
+    // ---- cached K/V of earlier positions -> shared memory (independent of the qkv kernel) ----
+    const int np = ok ? min(pos, kAttnXPrefetch) : 0;
+    for (int i = tid; i < np * 16; i += kAttnXThreads) {
+        const int p = i >> 4, c = i & 15;  // 16 pieces of 16 bytes: 8 of K, 8 of V
+        const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd;
+        if (c < 8)
+            *reinterpret_cast<uint4*>(kc_s + p * kAttnXRow + c * 16) =
+                *reinterpret_cast<const uint4*>(a.kq + rb + c * 16);
+        else
+            *reinterpret_cast<uint4*>(vc_s + p * hd + (c - 8) * 16) =
+                *reinterpret_cast<const uint4*>(a.vq + rb + (c - 8) * 16);
+    }
+    for (int i = tid; i < np * 2; i += kAttnXThreads) {
+        const int p = i >> 1, b = i & 1;
+        const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + b;
+        ksc_s[2 * p + b] = a.ks[sb];
+        vsc_s[2 * p + b] = a.vs[sb];
+    }
     grid_dependency_wait();
     grid_launch_dependents();
-    const int pos = a.st->pos;
-    if (pos < 0 || pos >= a.max_seq || pos >= kAttnXMaxSeq) return;
+    if (!ok) return;
     const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
 
     // ---- RoPE of q and k, int8 quantization of this position's k and v ----
@@ -70,7 +123,7 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
                 kv = __fmaf_rn(kh[i], rs, __fmul_rn(kv, rc));
             }
         }
-        S.q[tid] = qv;
+        q_s[tid] = qv;
         kval = kv;
         vval = a.qkv[q_dim + kv_dim + g * hd + tid];
     }
@@ -78,23 +131,23 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
         const float km = warp_max(fabsf(kval));
         const float vm = warp_max(fabsf(vval));
         if (tid < hd && lane == 0) {
-            S.red[0][tid >> 6][(tid >> 5) & 1] = km;
-            S.red[1][tid >> 6][(tid >> 5) & 1] = vm;
+            red[0][tid >> 6][(tid >> 5) & 1] = km;
+            red[1][tid >> 6][(tid >> 5) & 1] = vm;
         }
     }
     __syncthreads();
     if (tid < hd) {
         const int b = tid >> 6;
-        const float ka = fmaxf(S.red[0][b][0], S.red[0][b][1]);
-        const float va = fmaxf(S.red[1][b][0], S.red[1][b][1]);
+        const float ka = fmaxf(red[0][b][0], red[0][b][1]);
+        const float va = fmaxf(red[1][b][0], red[1][b][1]);
         const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
         const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
         int qk = __float2int_rn(__fmul_rn(kval, kv_code_inv(ka)));
         int qv = __float2int_rn(__fmul_rn(vval, kv_code_inv(va)));
         qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
         qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
-        S.k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
-        S.v[tid] = __fmul_rn(static_cast<float>(qv), vsc);
+        k_s[tid] = __fmul_rn(static_cast<float>(qk), ksc);
+        v_s[tid] = __fmul_rn(static_cast<float>(qv), vsc);
         if (h % groups == 0) {
             const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
             a.kq[kb + tid] = static_cast<int8_t>(qk);
@@ -120,22 +173,23 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
 #pragma unroll
                     for (int l = 0; l < 8; ++l) {
                         const int d = b * 64 + i * 8 + l;
-                        ln[l] = __fmaf_rn(S.q[d], S.k[d], i == 0 ? 0.0f : ln[l]);
+                        ln[l] = __fmaf_rn(q_s[d], k_s[d], i == 0 ? 0.0f : ln[l]);
                     }
             } else {
-                const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + b * 64;
-                const float sc = a.ks[(static_cast<long long>(p) * a.n_kv + g) * 2 + b];
-                const uint4* kp = reinterpret_cast<const uint4*>(a.kq + rb);
+                const bool staged = p < kAttnXPrefetch;
+                const float sc = staged ? ksc_s[2 * p + b] : a.ks[(static_cast<long long>(p) * a.n_kv + g) * 2 + b];
+                const int8_t* kr = staged ? kc_s + p * kAttnXRow + b * 64
+                                          : a.kq + (static_cast<long long>(p) * a.n_kv + g) * hd + b * 64;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    const uint4 w4 = kp[c];
+                    const uint4 w4 = *reinterpret_cast<const uint4*>(kr + c * 16);
                     const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         const int i = c * 2 + (e >> 3), l = e & 7;
                         const int code = static_cast<int8_t>((ww[e >> 2] >> (8 * (e & 3))) & 0xFFu);
                         const float kf = __fmul_rn(static_cast<float>(code), sc);
-                        ln[l] = __fmaf_rn(S.q[b * 64 + i * 8 + l], kf, i == 0 ? 0.0f : ln[l]);
+                        ln[l] = __fmaf_rn(q_s[b * 64 + i * 8 + l], kf, i == 0 ? 0.0f : ln[l]);
                     }
                 }
             }
@@ -143,52 +197,88 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
                                        __fadd_rn(__fadd_rn(ln[2], ln[6]), __fadd_rn(ln[3], ln[7])));
             dot = __fadd_rn(dot, hs);
         }
-        S.s[p] = __fmul_rn(dot, inv_sqrt_d);
+        s_s[p] = __fmul_rn(dot, inv_sqrt_d);
     }
     __syncthreads();
 
-    // ---- 64-position tiles in order ----
-    float m = -INFINITY, l = 0.0f, num = 0.0f;
-    for (int tk = 0; tk <= pos; tk += kAttnXTile) {
-        const int span = min(kAttnXTile, pos + 1 - tk);
-        // tile maximum (every thread computes it from shared memory: no broadcast)
-        float tmax = -INFINITY;
-        for (int p = 0; p < span; ++p) {
-            const float sp = S.s[tk + p];
-            tmax = (tmax < sp) ? sp : tmax;
+    // ---- tile maxima (one warp per tile), then the running maxima and old scales in order ----
+    const int nt = (pos + kAttnXTile) / kAttnXTile;  // tiles covering positions 0..pos
+    for (int t = warp; t < nt; t += kAttnXThreads / 32) {
+        const int tk = t * kAttnXTile, span = min(kAttnXTile, pos + 1 - tk);
+        float v = -INFINITY;
+        if (lane < span) v = s_s[tk + lane];
+        if (lane + 32 < span) {
+            const float v2 = s_s[tk + lane + 32];
+            v = (v < v2) ? v2 : v;
         }
-        const float nm = (m < tmax) ? tmax : m;
-        const float old = (l > 0.0f) ? exact_expf(__fsub_rn(m, nm), ex) : 0.0f;
-        if (tid < span) S.w[tid] = exact_expf(__fsub_rn(S.s[tk + tid], nm), ex);
-        // stage the tile's V codes (16-byte pieces) and scales; this position's v comes from S.v
-        for (int i = tid; i < span * (hd / 16); i += kAttnXThreads) {
-            const int p = i / (hd / 16), c = i % (hd / 16);
-            if (tk + p != pos)
-                *reinterpret_cast<uint4*>(&S.vt[p][c * 16]) = *reinterpret_cast<const uint4*>(
-                    a.vq + (static_cast<long long>(tk + p) * a.n_kv + g) * hd + c * 16);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float u = __shfl_xor_sync(0xffffffffu, v, o);
+            v = (v < u) ? u : v;
         }
-        for (int i = tid; i < span * 2; i += kAttnXThreads) {
-            const int p = i >> 1, b = i & 1;
-            if (tk + p != pos) S.vs[p][b] = a.vs[(static_cast<long long>(tk + p) * a.n_kv + g) * 2 + b];
-        }
-        __syncthreads();
-        float tl = 0.0f, tn = 0.0f;
-        for (int p = 0; p < span; ++p) {
-            const float wp = S.w[p];
-            tl = __fadd_rn(tl, wp);
-            if (tid < hd) {
-                const float vf = (tk + p == pos) ? S.v[tid]
-                                                 : __fmul_rn(static_cast<float>(S.vt[p][tid]), S.vs[p][tid >> 6]);
-                tn = __fmaf_rn(wp, vf, tn);
+        if (v == 0.0f) {
+            // a zero maximum: +0 and -0 compare equal, so take the sequential first-maximum rule
+            // (std::max keeps the earlier of equal values) to get its sign right
+            float q = -INFINITY;
+            for (int p = 0; p < span; ++p) {
+                const float sp = s_s[tk + p];
+                q = (q < sp) ? sp : q;
             }
+            v = q;
         }
-        l = __fadd_rn(__fmul_rn(l, old), tl);
-        num = __fmaf_rn(num, old, tn);
-        m = nm;
-        __syncthreads();  // w / vt are rewritten by the next tile
+        if (lane == 0) tile_s[4 * t + 3] = v;
     }
-    if (tid < hd) a.out[h * hd + tid] = __fmul_rn(num, __fdiv_rn(1.0f, l));
-    (void)warp;
+    __syncthreads();
+    if (tid == 0) {
+        float m = -INFINITY;
+        for (int t = 0; t < nt; ++t) {
+            const float tm = tile_s[4 * t + 3];
+            const float nm = (m < tm) ? tm : m;
+            // after the first tile l > 0 (its maximum's weight is exp(0) = 1), so old is exp(m - nm)
+            tile_s[4 * t + 1] = (t == 0) ? 0.0f : exact_expf(__fsub_rn(m, nm), ex);
+            tile_s[4 * t + 0] = nm;
+            m = nm;
+        }
+    }
+    __syncthreads();
+    // ---- weights of every position ----
+    for (int p = tid; p <= pos; p += kAttnXThreads)
+        w_s[p] = exact_expf(__fsub_rn(s_s[p], tile_s[4 * (p / kAttnXTile)]), ex);
+    __syncthreads();
+    // ---- every tile's tile_l and tile_num (thread per (tile, dim)), in position order ----
+    for (int i = tid; i < nt * hd; i += kAttnXThreads) {
+        const int t = i / hd, d = i % hd;
+        const int tk = t * kAttnXTile, span = min(kAttnXTile, pos + 1 - tk);
+        float tl = 0.0f, tn = 0.0f;
+        for (int pp = 0; pp < span; ++pp) {
+            const int p = tk + pp;
+            const float wp = w_s[p];
+            tl = __fadd_rn(tl, wp);
+            float vf;
+            if (p == pos) {
+                vf = v_s[d];
+            } else if (p < kAttnXPrefetch) {
+                vf = __fmul_rn(static_cast<float>(vc_s[p * hd + d]), vsc_s[2 * p + (d >> 6)]);
+            } else {
+                const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd;
+                vf = __fmul_rn(static_cast<float>(a.vq[rb + d]), a.vs[(static_cast<long long>(p) * a.n_kv + g) * 2 + (d >> 6)]);
+            }
+            tn = __fmaf_rn(wp, vf, tn);
+        }
+        tn_s[t * hd + d] = tn;
+        if (d == 0) tile_s[4 * t + 2] = tl;
+    }
+    __syncthreads();
+    // ---- merge the tiles in order ----
+    if (tid < hd) {
+        float l = 0.0f, num = 0.0f;
+        for (int t = 0; t < nt; ++t) {
+            const float old = tile_s[4 * t + 1];
+            l = __fadd_rn(__fmul_rn(l, old), tile_s[4 * t + 2]);
+            num = __fmaf_rn(num, old, tn_s[t * hd + tid]);
+        }
+        a.out[h * hd + tid] = __fmul_rn(num, __fdiv_rn(1.0f, l));
+    }
 }
 
 }  // namespace asdsl

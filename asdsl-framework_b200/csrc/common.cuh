@@ -216,6 +216,15 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
     return v;
 }
 __device__ __forceinline__ float ldsf(uint32_t a) { return __uint_as_float(lds32(a)); }
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float2 lds64f(uint32_t a) {
+    const uint2 v = lds64(a);
+    return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+}
 __device__ __forceinline__ uint32_t lds16(uint32_t a) {
     unsigned short v;
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));

@@ -29,6 +29,7 @@ struct EngProj {
     uint8_t* w0 = nullptr;  // preq2 meta | banded quant
     uint8_t* w1 = nullptr;  // preq2 quant | banded scales
     int rows = 0, cols = 0;
+    int xlpt = 0;  // reference-exact mode: w0 / w1 hold the exact layout in units of xlpt bands
 };
 
 struct EngLayer {
@@ -170,21 +171,18 @@ int eng_gemv(const EngProj& p, GemvArgs ga, long long pair_off_rows, cudaStream_
 // the same GEMV in the reference-exact mode (preq2 weights only; checked at finalize)
 template <int PRO, int EPI>
 int eng_gemv_x(const asdsl_b200_engine* e, const EngProj& p, GemvArgs ga, long long pair_off_rows, cudaStream_t s) {
-    StreamIn in[2];
-    const long long M = pair_off_rows > 0 ? pair_off_rows : p.rows;
-    const long long nb = (M + 3) / 4;
-    preq2_streams(in, p.w0, p.w1, p.rows, p.cols);
-    ga.gs = 32;
     ga.ex = e->ex;
-    return launch_stream_gemv<kFmtPreq2X, PRO, EPI>(in, 2, nb, pair_off_rows > 0 ? nb : 0, ga, s);
+    return launch_exact_gemv<PRO, EPI>(p.w0, p.w1, p.rows, pair_off_rows, ga, s, p.xlpt);
 }
 
-int launch_small(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t s, bool pdl) {
+int launch_small(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t s, bool pdl,
+                 unsigned dyn_smem = 0) {
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.stream = s;
+    cfg.dynamicSmemBytes = dyn_smem;
     cudaLaunchAttribute attr[1];
     if (pdl && launch_policy().pdl) {
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -438,7 +436,8 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
             if (e->exact) {
                 void* args[] = {&aa, &e->ex, &e->inv_sqrt_d};
                 if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_exact), dim3(c.num_heads),
-                                          dim3(asdsl::kAttnXThreads), args, s, true))
+                                          dim3(asdsl::kAttnXThreads), args, s, true,
+                                          asdsl::attn_x_layout(c.max_seq_len).total))
                     return rc;
             } else {
                 void* args[] = {&aa};
@@ -1089,6 +1088,39 @@ int asdsl_b200_engine_finalize(asdsl_b200_engine* e) {
                                           std::to_string(asdsl::kAttnXMaxSeq) + " and hidden_size % 8 == 0");
         if (e->persistent) return set_error(kEinval, "engine_finalize: the reference-exact mode runs the per-op chain");
         if (int rc = exact_tabs_device(&e->ex)) return rc;
+        ASDSL_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(&asdsl::k_attention_exact),
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(asdsl::attn_x_layout(c.max_seq_len).total)));
+        // every matrix into the exact layout (group-interleaved units; pure byte moves, once)
+        auto relayout = [&](EngProj& p, long long pair_rows) -> int {
+            const long long ng = p.cols / 32;
+            const long long m_seg = pair_rows > 0 ? pair_rows : p.rows;
+            const int L = asdsl::exact_lpt_for(m_seg, pair_rows > 0);
+            const long long units = ((p.rows + 3) / 4 + L - 1) / L;
+            uint8_t *mx = nullptr, *qx = nullptr;
+            if (int rc = eng_alloc(e, &mx, static_cast<size_t>(units * ng * 16 * L))) return rc;
+            if (int rc = eng_alloc(e, &qx, static_cast<size_t>(units * ng * 64 * L))) return rc;
+            const long long items = units * ng * 4 * L;
+            const unsigned blocks = static_cast<unsigned>(std::min<long long>((items + 255) / 256, sm_count() * 32ll));
+            asdsl::k_relayout_exact<<<blocks, 256, 0, e->stream>>>(p.w0, p.w1, mx, qx, p.rows, static_cast<int>(ng), L,
+                                                                   units);
+            ASDSL_CUDA(cudaGetLastError());
+            ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+            eng_free(e, p.w0);
+            eng_free(e, p.w1);
+            p.w0 = mx;
+            p.w1 = qx;
+            p.xlpt = L;
+            return kOk;
+        };
+        for (int l = 0; l < c.num_layers; ++l) {
+            EngLayer& L = e->layers[l];
+            if (int rc = relayout(L.p[kProjQkv], 0)) return rc;
+            if (int rc = relayout(L.p[kProjO], 0)) return rc;
+            if (int rc = relayout(L.p[kProjGateUp], c.intermediate_size)) return rc;
+            if (int rc = relayout(L.p[kProjDown], 0)) return rc;
+        }
+        if (int rc = relayout(e->lm, 0)) return rc;
 #ifdef ASDSL_HOST_X86
         e->inv_sqrt_d = asdsl::host_nr_rsqrt(static_cast<float>(c.head_dim));
 #endif
@@ -1418,6 +1450,8 @@ int asdsl_b200_engine_export_lm_head(asdsl_b200_engine* e, int* fmt, uint8_t* w0
                                      size_t w1_bytes) {
     ENG_READY(e);
     if (!fmt) return set_error(kEinval, "export_lm_head: null pointer");
+    if (e->lm.xlpt)
+        return set_error(kEinval, "export_lm_head: the reference-exact mode keeps the lm_head in its own layout");
     const asdsl_b200_engine_config& c = e->cfg;
     const long long nb = (c.vocab_size + 3) / 4;
     size_t b0, b1;

@@ -45,8 +45,14 @@ enum WeightFormat : int {
     kFmtQ4K = 4,      // [M][K/256][144] reference-interpretation Q4_K, own A8
     kFmtPacked = 5,   // nibbles [M][K/2] + fp32 scales [M][ng] + fp32 biases [M][ng], fp32 x
     kFmtQ128B = 6,    // banded Q4_128: quant [nb][K/128][4][64] + scales [nb][K/128][4] fp16
-    kFmtPreq2X = 7,   // preq2 bytes, every row summed in the reference's compiled order (exact mode)
+    kFmtPreq2X = 7,   // preq2 bytes, every row summed in the reference's compiled order (exact mode);
+    kFmtPreq2X2 = 8,  // 7..10: a unit of 1, 2, 4, 8 bands, each thread owning 1, 2, 4, 8 of a row's
+    kFmtPreq2X4 = 9,  // eight int32 dot lanes (exact_lpt)
+    kFmtPreq2X8 = 10,
 };
+
+__host__ __device__ constexpr bool is_exact_fmt(int fmt) { return fmt >= kFmtPreq2X && fmt <= kFmtPreq2X8; }
+__host__ __device__ constexpr int exact_lpt(int fmt) { return 1 << (fmt - kFmtPreq2X); }
 
 enum Prologue : int {
     kProA8 = 0,     // fp32 x -> A8 (gs 32 or 128)
@@ -54,7 +60,7 @@ enum Prologue : int {
     kProRmsA8 = 2,  // RMSNorm(x) * w then A8
     kProQ4K = 3,    // the Q4_K kernel's own A8 (half-away, clamp +-127)
     kProF32 = 4,    // fp32 x kept as is, plus per-group sums (packed W4A32)
-    kProA8X = 5,    // kProA8 for kFmtPreq2X: codes in lane order (4 per 32-bit word, see band_exact)
+    kProA8X = 5,    // kProA8 for kFmtPreq2X*: codes in lane order (4 per 32-bit word, see rows_exact)
     kProRmsA8X = 6, // kProRmsA8 for kFmtPreq2X: the reference's compiled RMSNorm, then A8 in lane order
 };
 
@@ -93,8 +99,8 @@ constexpr int kMaxStreams = 3;
 template <int FMT>
 struct FmtTraits {
     static constexpr int kStreams =
-        (FMT == kFmtPreq2 || FMT == kFmtPreq2X || FMT == kFmtQ128B) ? 2 : (FMT == kFmtPacked ? 3 : 1);
-    static constexpr int kRowsPerUnit = (FMT == kFmtPacked) ? 1 : 4;
+        (FMT == kFmtPreq2 || is_exact_fmt(FMT) || FMT == kFmtQ128B) ? 2 : (FMT == kFmtPacked ? 3 : 1);
+    static constexpr int kRowsPerUnit = (FMT == kFmtPacked) ? 1 : (is_exact_fmt(FMT) ? 4 * exact_lpt(FMT) : 4);
 };
 
 struct StreamDesc {
@@ -154,6 +160,7 @@ struct GemvArgs {
     const uint8_t* xa_pre;
     // reference-exact mode (kProRmsA8X, kEpiSiluX): the host CPU's RSQRTSS / RCPPS tables
     ExactTabs ex;
+    int exact_inter;  // kFmtPreq2X*: the weights are in the exact (group-interleaved) layout
 };
 
 // ---------------------------------------------------------------------------
@@ -317,13 +324,26 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
         if constexpr (PRO == kProRmsA8X) {
             // rmsnorm_f32 as compiled (unified_engine.cpp:499-524): lane l of one 8-wide vector
             // accumulates x[8i+l]^2 by FMA in order of i; hsum256_ps fold; sum/n + eps; RSQRTSS +
-            // Newton.  Eight threads run the eight lane chains; the others wait at the barrier.
+            // Newton.  The CTA stages x in shared memory (behind the A8 area, one coalesced pass),
+            // then eight threads run the eight sequential lane chains from there.
+            float* xst = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xa.x8) + xarea_layout_bytes(K, ga.gs, false));
+            if (in_regs) {
+#pragma unroll
+                for (int k = 0; k < kRegIters; ++k) {
+                    const int t = k * kConsumerThreads + ctid;
+                    if (t < nquads) reinterpret_cast<float4*>(xst)[t] = xr[k];
+                }
+            } else {
+                for (int t = ctid; t < nquads; t += kConsumerThreads)
+                    reinterpret_cast<float4*>(xst)[t] = load_x4<kCoherent>(reinterpret_cast<const float4*>(ga.x) + t);
+            }
+            consumer_sync();
             if (ctid < 8) {
                 float acc = 0.0f;
-                const float* xp = ga.x + ctid;
-#pragma unroll 8
+                const float* xp = xst + ctid;
+#pragma unroll 16
                 for (int i = 0; i < (K >> 3); ++i) {
-                    const float v = load_x1<kCoherent>(xp + 8 * i);
+                    const float v = xp[8 * i];
                     acc = __fmaf_rn(v, v, acc);
                 }
                 const float a = __fadd_rn(acc, __shfl_xor_sync(0xffu, acc, 4));  // v_l + v_{l+4}
@@ -428,7 +448,7 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
             }
             if (live && pro_is_lane_order(PRO)) {
                 // lane order: the quad is lane (e0 & 31) / 4 of its 32-group; one word of the codes
-                // in the byte order band_exact's nibble word uses, [c0, c2, c1, c3]
+                // in the byte order rows_exact's nibble words use, [c0, c2, c1, c3]
                 *reinterpret_cast<uint32_t*>(xa.x8 + e0) = (c[0] & 0xFFu) | ((c[2] & 0xFFu) << 8) |
                                                            ((c[1] & 0xFFu) << 16) | ((c[3] & 0xFFu) << 24);
             } else if (live) {
@@ -448,9 +468,14 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
             sm += __shfl_xor_sync(0xffffffffu, sm, 4);
             if (live && (t & 7) == 0) {
                 const int q = e0 >> 5;
-                xa.xs[q] = scale;
-                xa.xsi[q] = sm;
-                xa.xss[q] = __fmul_rn(static_cast<float>(sm), scale);
+                if constexpr (pro_is_lane_order(PRO)) {
+                    // (scale, xsum_scaled) pairs over the xs and xss areas: one 8-byte load per group
+                    reinterpret_cast<float2*>(xa.xs)[q] = make_float2(scale, __fmul_rn(static_cast<float>(sm), scale));
+                } else {
+                    xa.xs[q] = scale;
+                    xa.xsi[q] = sm;
+                    xa.xss[q] = __fmul_rn(static_cast<float>(sm), scale);
+                }
             }
         };
         if (in_regs) {
@@ -629,48 +654,169 @@ __device__ __forceinline__ void band_compute(float a[4], uint32_t s0, uint32_t s
 }
 
 // ---------------------------------------------------------------------------
-// kFmtPreq2X band: the reference's process_one_row (gemv_preq2_avx2.cpp:216-253) in its compiled
-// order.  Thread (row r = lane / 8, lane j = lane % 8) owns int32 lane j of every group's dot --
-// elements 4j..4j+3, as pmaddubsw + pmaddwd produce it -- and keeps that lane of the even-group
-// and odd-group float accumulators; every thread of a row also runs the row's two scalar
-// correction chains.  Per group g (in order): combined = ws*xs; corr = (wz*ws)*xsum_scaled;
-// acc[g&1] += (float)dot_j * combined; corr_sum[g&1] += corr.  Row value =
-// (hsum(acc_even) + hsum(acc_odd)) - (corr_even + corr_odd), hsum = ((v0+v4)+(v1+v5)) +
-// ((v2+v6)+(v3+v7)), returned in every lane of the row (lane 8r among them, as reduce4 does).
-// The activation codes are in lane order (kProA8X / kProRmsA8X): the word of lane j of group g
-// at x8 + 32g + 4j holds codes [4j, 4j+2, 4j+1, 4j+3], the byte order of the nibble word below.
+// Exact-mode rows (kFmtPreq2X*): the reference's process_one_row (gemv_preq2_avx2.cpp:216-253) in
+// its compiled order, for a unit of LPT bands (4 * LPT rows).  Eight int32 dot lanes per group --
+// lane j = elements 4j..4j+3, as pmaddubsw + pmaddwd produce them -- are spread over 8 / LPT
+// threads per row, LPT consecutive lanes each; every thread keeps its lanes of the even-group and
+// odd-group float accumulators and runs the row's two scalar correction chains.  Per group g, in
+// order: combined = ws*xs; corr = (wz*ws)*xsum_scaled; acc[g&1][j] += (float)dot_j * combined;
+// corr_sum[g&1] += corr.  Row value = (hsum(acc_even) + hsum(acc_odd)) - (corr_even + corr_odd),
+// hsum = ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7)), returned in every thread of the row.
+// The activation codes are in lane order (kProA8X / kProRmsA8X): lane j of group g is the word at
+// x8 + 32g + 4j with codes [4j, 4j+2, 4j+1, 4j+3], the byte order of the nibble word below.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float band_exact(uint32_t sq, uint32_t sm, int K, const XAddr& xs, int lane) {
+// lane words of 4 nibble bytes w (lanes A = bytes 0-1, B = bytes 2-3): bytes [e0, e2, e1, e3]
+__device__ __forceinline__ uint32_t nib_lane_lo(uint32_t w) { return (w & 0x0F0Fu) | ((w << 12) & 0x0F0F0000u); }
+__device__ __forceinline__ uint32_t nib_lane_hi(uint32_t w) {
+    return ((w >> 16) & 0x0F0Fu) | ((w >> 4) & 0x0F0F0000u);
+}
+
+// Two byte layouts of a unit of LPT bands (4 * LPT rows):
+//   kInter = false: the reference's preq2 bytes as they are -- quant [band][g][4 rows][16 B], meta
+//     [row][g][4 B] -- whose meta rows are ng*4 bytes apart, a multiple of 128: the rows of a warp
+//     read one bank (used by the standalone exact entry points);
+//   kInter = true: the engine's exact layout (k_relayout_exact, pure byte moves at finalize) --
+//     quant [g][4*LPT rows][16 B] and meta [g][4*LPT rows][4 B] per unit -- where every group's
+//     bytes of all the unit's rows are contiguous: conflict-free loads.
+template <int LPT, bool kInter>
+__device__ __forceinline__ float rows_exact(const uint8_t* sq, const uint8_t* sm, int K, const uint8_t* x8,
+                                            const float* xz, int lane, int half) {
+    // the even-group and odd-group chains of a row are independent: threads of a row split by
+    // parity first, then by lane sets of LPT lanes
+    constexpr int TPR = 16 / LPT;  // threads per row
+    constexpr int HT = TPR / 2;    // threads per row and parity
     const int nq = K >> 5;
-    const uint32_t r = static_cast<uint32_t>(lane >> 3), j = static_cast<uint32_t>(lane & 7);
-    const uint32_t qa = sq + r * 16u + j * 2u;                    // + 64 g (quant band: [ng][4 rows][16 B])
-    const uint32_t ma = sm + r * static_cast<uint32_t>(nq) * 4u;  // + 4 g  (meta band: [4 rows][ng][4 B])
-    const uint32_t xa = xs.x8 + j * 4u;                           // + 32 g
-    float acc0 = 0.0f, acc1 = 0.0f, cor0 = 0.0f, cor1 = 0.0f;
-    auto group = [&](int g, float& acc, float& cor) {
-        const uint32_t ug = static_cast<uint32_t>(g);
-        const uint32_t w16 = lds16(qa + ug * 64u);
-        const uint32_t word = (w16 & 0x0F0Fu) | ((w16 << 12) & 0x0F0F0000u);  // [e0, e2, e1, e3]
-        const int d = dp4a_us(word, lds32(xa + ug * 32u), 0);
-        const float2 sz = half2_bits_to_float2(lds32(ma + ug * 4u));  // (ws, wz)
-        const float xsc = ldsf(xs.xs + 4u * ug), xss = ldsf(xs.xss + 4u * ug);
-        const float comb = __fmul_rn(sz.x, xsc);
-        acc = __fadd_rn(acc, __fmul_rn(small_int_to_float(d), comb));
-        cor = __fadd_rn(cor, __fmul_rn(__fmul_rn(sz.y, sz.x), xss));
-    };
-    int g = 0;
-#pragma unroll 4
-    for (; g + 1 < nq; g += 2) {
-        group(g, acc0, cor0);
-        group(g + 1, acc1, cor1);
+    const int rho = half * (2 * LPT) + lane / TPR;  // row within the unit
+    const int sub = lane % TPR;
+    const int par = sub / HT;  // 0: even groups, 1: odd groups
+    const int ls = sub % HT;   // this thread's lanes: LPT * ls ..
+    const uint8_t* qa;
+    const uint8_t* ma;
+    int qstride, mstride;
+    if constexpr (kInter) {
+        qa = sq + rho * 16 + ls * (2 * LPT);
+        ma = sm + rho * 4;
+        qstride = 64 * LPT;
+        mstride = 16 * LPT;
+    } else {
+        qa = sq + (rho >> 2) * nq * 64 + (rho & 3) * 16 + ls * (2 * LPT);
+        ma = sm + rho * nq * 4;
+        qstride = 64;
+        mstride = 4;
     }
-    if (g < nq) group(g, acc0, cor0);
-    auto hsum8 = [](float v) {
-        const float a = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    const uint8_t* xa = x8 + ls * (4 * LPT);
+    float acc[LPT];
+#pragma unroll
+    for (int i = 0; i < LPT; ++i) acc[i] = 0.0f;
+    float cor = 0.0f;
+    const float kMagic = 12582912.0f;  // 1.5 * 2^23: dp4a accumulates into its bit pattern
+#pragma unroll 4
+    for (int g = par; g < nq; g += 2) {
+        const uint8_t* qg = qa + g * qstride;
+        const uint8_t* xg = xa + g * 32;
+        uint32_t lw[LPT];  // lane words of nibbles
+        uint32_t xw[LPT];  // activation words
+        if constexpr (LPT == 1) {
+            lw[0] = nib_lane_lo(*reinterpret_cast<const uint16_t*>(qg));
+            xw[0] = *reinterpret_cast<const uint32_t*>(xg);
+        } else if constexpr (LPT == 2) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(qg);
+            lw[0] = nib_lane_lo(w);
+            lw[1] = nib_lane_hi(w);
+            const uint2 x2 = *reinterpret_cast<const uint2*>(xg);
+            xw[0] = x2.x;
+            xw[1] = x2.y;
+        } else if constexpr (LPT == 4) {
+            const uint2 w = *reinterpret_cast<const uint2*>(qg);
+            lw[0] = nib_lane_lo(w.x);
+            lw[1] = nib_lane_hi(w.x);
+            lw[2] = nib_lane_lo(w.y);
+            lw[3] = nib_lane_hi(w.y);
+            const uint4 x4 = *reinterpret_cast<const uint4*>(xg);
+            xw[0] = x4.x;
+            xw[1] = x4.y;
+            xw[2] = x4.z;
+            xw[3] = x4.w;
+        } else {
+            const uint4 w = *reinterpret_cast<const uint4*>(qg);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lw[2 * i] = nib_lane_lo(ww[i]);
+                lw[2 * i + 1] = nib_lane_hi(ww[i]);
+            }
+            const uint4 xa4 = *reinterpret_cast<const uint4*>(xg), xb4 = *reinterpret_cast<const uint4*>(xg + 16);
+            xw[0] = xa4.x;
+            xw[1] = xa4.y;
+            xw[2] = xa4.z;
+            xw[3] = xa4.w;
+            xw[4] = xb4.x;
+            xw[5] = xb4.y;
+            xw[6] = xb4.z;
+            xw[7] = xb4.w;
+        }
+        const float2 sz = half2_bits_to_float2(*reinterpret_cast<const uint32_t*>(ma + g * mstride));  // (ws, wz)
+        const float2 xs2 = *reinterpret_cast<const float2*>(xz + 2 * g);  // (xs, xsum_scaled)
+        const float comb = __fmul_rn(sz.x, xs2.x);
+#pragma unroll
+        for (int i = 0; i < LPT; ++i) {
+            // (float)dot exactly: |dot| < 2^13, so 0x4B400000 + dot is the float 1.5*2^23 + dot
+            const float d = __fsub_rn(__int_as_float(dp4a_us(lw[i], xw[i], 0x4B400000)), kMagic);
+            acc[i] = __fadd_rn(acc[i], __fmul_rn(d, comb));
+        }
+        cor = __fadd_rn(cor, __fmul_rn(__fmul_rn(sz.y, sz.x), xs2.y));
+    }
+    // hsum over this parity's 8 lanes, held LPT per thread by HT threads
+    float hs;
+    if constexpr (LPT == 8) {
+        hs = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[4]), __fadd_rn(acc[1], acc[5])),
+                       __fadd_rn(__fadd_rn(acc[2], acc[6]), __fadd_rn(acc[3], acc[7])));
+    } else if constexpr (LPT == 4) {
+        float a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 1));
+        hs = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+    } else if constexpr (LPT == 2) {
+        const float a0 = __fadd_rn(acc[0], __shfl_xor_sync(0xffffffffu, acc[0], 2));
+        const float a1 = __fadd_rn(acc[1], __shfl_xor_sync(0xffffffffu, acc[1], 2));
+        const float b = __fadd_rn(a0, a1);
+        hs = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, 1));
+    } else {
+        const float a = __fadd_rn(acc[0], __shfl_xor_sync(0xffffffffu, acc[0], 4));
         const float b = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-        return __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, 2));
-    };
-    return __fsub_rn(__fadd_rn(hsum8(acc0), hsum8(acc1)), __fadd_rn(cor0, cor1));
+        hs = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, 2));
+    }
+    // (hsum(even) + hsum(odd)) - (corr_even + corr_odd): the partner thread holds the other parity
+    const float hs2 = __shfl_xor_sync(0xffffffffu, hs, HT);
+    const float cor2 = __shfl_xor_sync(0xffffffffu, cor, HT);
+    return __fsub_rn(__fadd_rn(hs, hs2), __fadd_rn(cor, cor2));
+}
+
+// The exact layout of one preq2 matrix (rows M, ng = K/32 groups) in units of L bands: quant
+// [unit][g][4L rows][16 B], meta [unit][g][4L rows][4 B]; rows past M are zero.  Pure byte moves;
+// one thread per (unit, group, row).
+__global__ void k_relayout_exact(const uint8_t* __restrict__ meta, const uint8_t* __restrict__ quant,
+                                 uint8_t* __restrict__ meta_x, uint8_t* __restrict__ quant_x, long long M, int ng,
+                                 int L, long long units) {
+    const long long R = 4ll * L;
+    const long long total = units * ng * R;
+    for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = t % R;
+        const long long ug = t / R;
+        const long long g = ug % ng;
+        const long long u = ug / ng;
+        const long long row = u * R + r;
+        uint4 qv = make_uint4(0u, 0u, 0u, 0u);
+        uint32_t mv = 0u;
+        if (row < M) {
+            const long long band = row >> 2;
+            qv = *reinterpret_cast<const uint4*>(quant + (band * ng + g) * 64 + (row & 3) * 16);
+            mv = *reinterpret_cast<const uint32_t*>(meta + (row * ng + g) * 4);
+        }
+        *reinterpret_cast<uint4*>(quant_x + t * 16) = qv;
+        *reinterpret_cast<uint32_t*>(meta_x + t * 4) = mv;
+    }
 }
 
 // rotate a lane's four partials back to row order: v[j] = a[(j - rot) & 3]
@@ -1018,14 +1164,9 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                 if constexpr (NS > 1)
                     p1 = (seg == 0 ? ub[0][NS - 1] : ub[NSEG - 1][NS - 1]) +
                          static_cast<uint32_t>(k) * static_cast<uint32_t>(pa.s[NS - 1].unit_bytes);
-                float v;
-                if constexpr (FMT == kFmtPreq2X) {
-                    v = band_exact(p0, p1, K, xad, lane);
-                } else {
-                    band_compute<FMT>(a, p0, p1, K, pa.row_bytes, xad, lane, rr_lane, q0, q1);
-                    unrotate(a, rot);
-                    v = reduce4(a, lane);
-                }
+                band_compute<FMT>(a, p0, p1, K, pa.row_bytes, xad, lane, rr_lane, q0, q1);
+                unrotate(a, rot);
+                const float v = reduce4(a, lane);
                 float vrow[NSEG];
                 bool finish = true;
                 if (IPU > 1) {
@@ -1063,8 +1204,7 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                         ga.resid[row] = __fadd_rn(vrow[0], __ldcg(ga.resid + row));
                     } else if constexpr (EPI == kEpiSilu) {
                         ga.h[row] = ref_silu_mul(vrow[0], vrow[NSEG - 1]);
-                    } else if constexpr (EPI == kEpiSiluX) {
-                        ga.h[row] = exact_silu_mul(vrow[0], vrow[NSEG - 1], ga.ex.rcp);
+
                     } else {
                         if (ga.y) ga.y[row] = vrow[0];
                         argmax_take(best_v, best_i, vrow[0], ga.row_base + static_cast<int>(row));
@@ -1083,13 +1223,88 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
 }
 
 // ---------------------------------------------------------------------------
+// exact-mode consumers (kFmtPreq2X*): a work item is one half of a unit of LPT bands (2 * LPT
+// rows), taken by one warp; the paired SiLU form computes the item's gate rows and then its up rows
+// in the same warp, so no partial sums cross warps.  A row's value is written by its first thread.
+// ---------------------------------------------------------------------------
+template <int FMT, int PRO, int EPI, bool kInter>
+__device__ void consume_chunks_x(const PipeArgs& pa, const GemvArgs& ga, const XArea& xa, long long u0, long long u1,
+                                 uint8_t* ring, int S, uint64_t* full, uint64_t* empty, int& jg, float& best_v,
+                                 int& best_i) {
+    constexpr int LPT = exact_lpt(FMT);
+    constexpr int TPR = 16 / LPT;  // threads per row (rows_exact)
+    constexpr int NSEG = epi_is_silu(EPI) ? 2 : 1;
+    const int lane = threadIdx.x & 31;
+    const int cw = threadIdx.x >> 5;
+    const int CU = pa.units_per_chunk;
+    const int n_chunks = static_cast<int>((u1 - u0 + CU - 1) / CU);
+    const int K = ga.K;
+    const int M = ga.M;
+    const uint8_t* x8 = reinterpret_cast<const uint8_t*>(xa.x8);
+    const float* xz = xa.xs;  // (scale, xsum_scaled) pairs
+    int item_base = jg;
+    int s = jg % S;
+    int use = jg / S;
+    const bool writer = (lane % TPR) == 0;
+    for (int j = 0; j < n_chunks; ++j) {
+        if (!mbar_wait(&full[s], use & 1)) {
+            if (lane == 0) atomicOr(ga.status, kStatusWaitFull);
+            jg += n_chunks;
+            return;
+        }
+        const long long cb = u0 + static_cast<long long>(j) * CU;
+        const int n_units_here = static_cast<int>(((cb + CU < u1) ? cb + CU : u1) - cb);
+        const uint8_t* st = ring + static_cast<size_t>(s) * pa.stage_bytes;
+        const uint8_t* ub[NSEG][2];
+#pragma unroll
+        for (int sg = 0; sg < NSEG; ++sg)
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+                ub[sg][i] = st + sg * pa.seg_bytes + pa.s[i].region_off + chunk_off16(pa.s[i], cb + sg * pa.pair_unit_off);
+        // two items per unit: its first and second half of rows
+        const int n_items = 2 * n_units_here;
+        const int it0 = (cw - item_base % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
+        item_base += n_items;
+        for (int it = it0; it < n_items; it += kConsumerWarps) {
+            const int un = it >> 1, half = it & 1;
+            const long long o0 = static_cast<long long>(un) * pa.s[0].unit_bytes;
+            const long long o1 = static_cast<long long>(un) * pa.s[1].unit_bytes;
+            const float v = rows_exact<LPT, kInter>(ub[0][0] + o0, ub[0][1] + o1, K, x8, xz, lane, half);
+            const int row = static_cast<int>(cb + un) * (4 * LPT) + half * (2 * LPT) + lane / TPR;
+            if constexpr (EPI == kEpiSiluX) {
+                const float u =
+                    rows_exact<LPT, kInter>(ub[NSEG - 1][0] + o0, ub[NSEG - 1][1] + o1, K, x8, xz, lane, half);
+                if (writer && row < M) ga.h[row] = exact_silu_mul(v, u, ga.ex.rcp);
+            } else if (writer && row < M) {
+                if constexpr (EPI == kEpiStore) {
+                    ga.y[row] = v;
+                } else if constexpr (EPI == kEpiResid) {
+                    ga.resid[row] = __fadd_rn(v, __ldcg(ga.resid + row));
+                } else if constexpr (EPI == kEpiArgmax) {
+                    if (ga.y) ga.y[row] = v;
+                    argmax_take(best_v, best_i, v, ga.row_base + row);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == S) {
+            s = 0;
+            ++use;
+        }
+    }
+    jg += n_chunks;
+}
+
+// ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 template <int FMT, int PRO, int EPI, int NT = 1>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const PipeArgs pa, const GemvArgs ga) {
-    static_assert(NT == 1 || ((EPI == kEpiStore || EPI == kEpiResid) && FMT != kFmtPacked && FMT != kFmtPreq2X),
+    static_assert(NT == 1 || ((EPI == kEpiStore || EPI == kEpiResid) && FMT != kFmtPacked && !is_exact_fmt(FMT)),
                   "multi-token: store or residual epilogue, W4A8 formats, not the exact mode");
-    static_assert((FMT == kFmtPreq2X) == pro_is_lane_order(PRO), "kFmtPreq2X pairs with the lane-order prologues");
+    static_assert(is_exact_fmt(FMT) == pro_is_lane_order(PRO), "kFmtPreq2X* pairs with the lane-order prologues");
+    static_assert(is_exact_fmt(FMT) || EPI != kEpiSiluX, "kEpiSiluX is the exact mode's epilogue");
     using T = FmtTraits<FMT>;
     constexpr int NS = T::kStreams;
     constexpr int NSEG = epi_is_silu(EPI) ? 2 : 1;
@@ -1157,8 +1372,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
 
     {
         int jg = 0;
-        consume_chunks<FMT, PRO, EPI, NT>(pa, ga, xa, xad, xa_stride, u0, u1, stages, pa.stage_bytes, S, full, empty,
-                                          s_part, s_cnt, jg, best_v, best_i);
+        if constexpr (is_exact_fmt(FMT)) {
+            if (ga.exact_inter)
+                consume_chunks_x<FMT, PRO, EPI, true>(pa, ga, xa, u0, u1, stages, S, full, empty, jg, best_v, best_i);
+            else
+                consume_chunks_x<FMT, PRO, EPI, false>(pa, ga, xa, u0, u1, stages, S, full, empty, jg, best_v, best_i);
+        } else
+            consume_chunks<FMT, PRO, EPI, NT>(pa, ga, xa, xad, xa_stride, u0, u1, stages, pa.stage_bytes, S, full,
+                                              empty, s_part, s_cnt, jg, best_v, best_i);
     }
 
     if constexpr (EPI == kEpiArgmax) {

@@ -219,13 +219,15 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     }
     const int nseg = pair_unit_off > 0 ? 2 : 1;
     const LaunchPolicy pol = launch_policy();
-    const uint32_t xa = xarea_layout_bytes(ga.K, ga.gs, PRO == kProF32) * static_cast<uint32_t>(ga.n_tokens);
+    // kProRmsA8X also stages the fp32 activation behind its A8 area (the sequential norm chains)
+    const uint32_t xa = xarea_layout_bytes(ga.K, ga.gs, PRO == kProF32) * static_cast<uint32_t>(ga.n_tokens) +
+                        (PRO == kProRmsA8X ? 4u * static_cast<uint32_t>(ga.K) : 0u);
     const PlanSplit ps = plan_split(n_units, ub_sum * nseg, nseg, FmtTraits<FMT>::kRowsPerUnit, ga.K, opt);
     const int grid = ps.grid;
     long long cu = ps.cu;
     int parts = ps.parts;
     const int nq = ga.K / 32;
-    if (FMT == kFmtPreq2X) {
+    if (is_exact_fmt(FMT)) {
         parts = 1;  // exact mode: each row's groups are summed in order by the threads of one warp
     } else if (opt.k_parts > 0) {
         // a forced split must cut K into parts of whole lane iterations (32 slices)
@@ -316,6 +318,58 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
     }
     ASDSL_CUDA(cudaLaunchKernelEx(&cfg, kern, pa, ga));
     return kOk;
+}
+
+// Exact-mode GEMV over preq2 weights (reference-exact numerics): rows [0, M) of meta / quant, or
+// the paired gate/up form (pair_rows = I: gate rows [0, I), up rows [I, 2I)).  A unit is L bands;
+// large row counts use more lanes per thread (fewer instructions per row), small ones fewer (more
+// threads per row).  ASDSL_EXACT_LPT = 1, 2, 4 or 8 forces the choice.
+inline int exact_lpt_for(long long m_seg, bool pair) {
+    const long long nb_seg = (m_seg + 3) / 4;
+    // a paired (gate/up) unit is computed by one warp in two passes: rank it by one half's rows
+    const long long work_rows = m_seg;
+    int lpt = work_rows >= 28416 ? 8 : (work_rows >= 14208 ? 4 : (work_rows >= 7104 ? 2 : 1));
+    static const int forced = [] {
+        const char* v = std::getenv("ASDSL_EXACT_LPT");
+        const int f = v ? std::atoi(v) : 0;
+        return (f == 1 || f == 2 || f == 4 || f == 8) ? f : 0;
+    }();
+    if (forced) lpt = forced;
+    while (lpt > 1 && pair && nb_seg % lpt) lpt >>= 1;  // the up segment starts on a unit
+    return lpt;
+}
+
+// inter_lpt = 0: meta / quant are the reference's preq2 bytes; > 0: they are in the exact layout
+// of k_relayout_exact with units of inter_lpt bands.
+template <int PRO, int EPI>
+int launch_exact_gemv(const uint8_t* meta, const uint8_t* quant, long long M_total, long long pair_rows, GemvArgs ga,
+                      cudaStream_t stream, int inter_lpt = 0) {
+    const long long K = ga.K;
+    const long long ng = K / 32;
+    const long long m_seg = pair_rows > 0 ? pair_rows : M_total;
+    const long long nb_seg = (m_seg + 3) / 4;
+    const long long nb_all = (M_total + 3) / 4;
+    const int lpt = inter_lpt > 0 ? inter_lpt : exact_lpt_for(m_seg, pair_rows > 0);
+    if (pair_rows > 0 && nb_seg % lpt) return set_error(kEinval, "internal: exact gate/up units straddle the halves");
+    StreamIn in[2];
+    if (inter_lpt > 0) {
+        const long long units_all = (nb_all + lpt - 1) / lpt;
+        in[0] = StreamIn{quant, ng * 64 * lpt, units_all * ng * 64 * lpt};
+        in[1] = StreamIn{meta, ng * 16 * lpt, units_all * ng * 16 * lpt};
+    } else {
+        in[0] = StreamIn{quant, ng * 64 * lpt, nb_all * ng * 64};
+        in[1] = StreamIn{meta, ng * 16 * lpt, M_total * ng * 4};
+    }
+    const long long nu = (nb_seg + lpt - 1) / lpt;
+    const long long off = pair_rows > 0 ? nb_seg / lpt : 0;
+    ga.gs = 32;
+    ga.exact_inter = inter_lpt > 0 ? 1 : 0;
+    switch (lpt) {
+        case 8: return launch_stream_gemv<kFmtPreq2X8, PRO, EPI>(in, 2, nu, off, ga, stream);
+        case 4: return launch_stream_gemv<kFmtPreq2X4, PRO, EPI>(in, 2, nu, off, ga, stream);
+        case 2: return launch_stream_gemv<kFmtPreq2X2, PRO, EPI>(in, 2, nu, off, ga, stream);
+        default: return launch_stream_gemv<kFmtPreq2X, PRO, EPI>(in, 2, nu, off, ga, stream);
+    }
 }
 
 }  // namespace asdsl

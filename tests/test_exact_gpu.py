@@ -37,7 +37,9 @@ def _assert_bitwise(got, want, what):
                              f"{np.asarray(got)[bad[:3]]} vs {np.asarray(want)[bad[:3]]}")
 
 
-@pytest.mark.parametrize("M,K", [(6, 64), (33, 1024), (5120, 3072), (3072, 3072), (16384, 3072), (3072, 8192)])
+# row counts chosen to cover every unit width (1, 2, 4 and 8 bands; partial last units)
+@pytest.mark.parametrize("M,K", [(6, 64), (33, 1024), (5120, 3072), (3072, 3072), (8190, 3072), (16384, 3072),
+                                 (3072, 8192), (30001, 512), (200064, 3072)])
 def test_gemv_preq2_exact_bitwise(native, oracle, M, K):
     import torch
 
