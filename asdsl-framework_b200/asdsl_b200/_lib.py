@@ -70,6 +70,13 @@ _SIGS = {
     "asdsl_b200_xchg_open": [_P, _P],
     "asdsl_b200_xchg_destroy": [_P],
     "asdsl_b200_gemv_argmax_xchg": [_I, _P, _P, _P, _P, _P, _P, _I, _P, _SZ, _I, _I, _P, _P],
+    "asdsl_b200_vxchg_create": [_I, _I, _I, _P, _P],
+    "asdsl_b200_vxchg_handle_bytes": [],
+    "asdsl_b200_vxchg_open": [_P, _P],
+    "asdsl_b200_vxchg_destroy": [_P],
+    "asdsl_b200_vxchg_set_stamps": [_P, _P, _I],
+    "asdsl_b200_xchg_set_stamps": [_P, _P, _I],
+    "asdsl_b200_allreduce_peer": [_P, _P, _P, _P, _I, _P],
     # device-resident decode engine
     "asdsl_b200_engine_create": [_P, _P],
     "asdsl_b200_engine_destroy": [_P],
@@ -113,6 +120,7 @@ _RESTYPES = {
     "asdsl_b200_last_error": ctypes.c_char_p,
     "asdsl_b200_argmax_scratch_bytes": _SZ,
     "asdsl_b200_xchg_handle_bytes": _SZ,
+    "asdsl_b200_vxchg_handle_bytes": _SZ,
 }
 
 _lib = None

@@ -12,8 +12,13 @@ of the projection's rows (lm_head, gate_up) or of its input columns (down):
   SiLU(gate)*up is local and yields h[a_r:b_r).
 * down: rank r owns input columns [a_r, b_r) of down_proj (whole activation groups: the A8
   quantization is per group, so the local A8 of h[a_r:b_r) equals the slice of the global
-  one); partial outputs are summed with one all-reduce of hidden_size floats.  The sum order
-  across ranks differs from the reference's, which the GEMV tolerance covers.
+  one); partial outputs are summed with one all-reduce of hidden_size floats -- on GPUs by
+  default one kernel over NVLink peer stores (asdsl_b200_allreduce_peer: each rank pushes its
+  partial into every rank's buffer, then sums the world's partials in rank order, so every
+  rank holds the same bits), else torch.distributed's all_reduce.  The sum order across ranks
+  differs from the reference's single row dot, which the GEMV tolerance covers; with
+  numerics="reference_exact" each rank's partial is bitwise the reference kernels' result on
+  its shard, and the output is bitwise their rank-ordered float32 sum.
 
 The per-shard compute goes through the C ABI kernels by default; tests running the ranks as
 gloo processes on the CPU pass the CPU oracle as `local` backend instead, so the collective
@@ -94,9 +99,56 @@ class _Exchange:
             allh = np.ascontiguousarray(mine.cpu().numpy())
         _lib.check(lib.asdsl_b200_xchg_open(self.ptr, allh.ctypes.data), "xchg_open")
 
+    def set_stamps(self, buf=None):
+        """record %globaltimer stamps of every exchange step into `buf` (int64 [n, 4] on the
+        device, n a power of two); None turns them off"""
+        _lib.call("asdsl_b200_xchg_set_stamps", self.ptr, buf.data_ptr() if buf is not None else None,
+                  buf.shape[0] if buf is not None else 0)
+
     def close(self):
         if getattr(self, "ptr", None):
             self._lib.asdsl_b200_xchg_destroy(self.ptr)
+            self.ptr = None
+
+
+class _VecExchange:
+    """Buffers of the peer all-reduce (asdsl_b200_vxchg_*): created on every rank with room for
+    `n_max` floats per rank and step parity, the CUDA IPC handles all-gathered in rank order,
+    then the peers' buffers mapped."""
+
+    def __init__(self, world: int, rank: int, n_max: int, device):
+        import ctypes
+
+        lib = _lib.load()
+        self._lib = lib
+        hb = int(lib.asdsl_b200_vxchg_handle_bytes())
+        h = (ctypes.c_uint8 * hb)()
+        self.ptr = ctypes.c_void_p()
+        _lib.check(lib.asdsl_b200_vxchg_create(world, rank, n_max, ctypes.byref(self.ptr), h), "vxchg_create")
+        mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device=device)
+        if world > 1:
+            import torch.distributed as dist
+
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(parts, mine)
+            allh = np.ascontiguousarray(torch.cat(parts).cpu().numpy())
+        else:
+            allh = np.ascontiguousarray(mine.cpu().numpy())
+        _lib.check(lib.asdsl_b200_vxchg_open(self.ptr, allh.ctypes.data), "vxchg_open")
+
+    def set_stamps(self, buf=None):
+        """record %globaltimer stamps of every step into `buf` (int64 [n, 4] on the device, n a
+        power of two); None turns them off"""
+        _lib.call("asdsl_b200_vxchg_set_stamps", self.ptr, buf.data_ptr() if buf is not None else None,
+                  buf.shape[0] if buf is not None else 0)
+
+    def allreduce(self, part, out, n: int, stream, add=None):
+        _lib.call("asdsl_b200_allreduce_peer", self.ptr, part.data_ptr(), out.data_ptr(),
+                  add.data_ptr() if add is not None else None, n, stream)
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            self._lib.asdsl_b200_vxchg_destroy(self.ptr)
             self.ptr = None
 
 
@@ -154,11 +206,15 @@ class ShardedLMHead:
             y = self.local.gemv_q4_128_fused(self.blocks, np.asarray(x, np.float32), self.rows, self.H)
             i = int(self.local.argmax(y))
             return torch.tensor([np.float32(y[i]).view(np.int32), self.a + i], dtype=torch.int32)
+        self.local_argmax(x)
+        return torch.cat([self.val.view(torch.int32), self.idx])
+
+    def local_argmax(self, x):
+        """one kernel: this rank's GEMV + first-max argmax into self.val / self.idx (global index)"""
         _lib.call("asdsl_b200_gemv_argmax", _lib.FMT_Q4_128_BANDED, self.quant.data_ptr(), self.scales.data_ptr(),
                   x.data_ptr(), self.logits.data_ptr(), self.val.data_ptr(), self.idx.data_ptr(), self.a,
                   self.scratch.data_ptr(), self.scratch.numel(), self.rows, self.H,
                   torch.cuda.current_stream(self.device).cuda_stream)
-        return torch.cat([self.val.view(torch.int32), self.idx])
 
     def argmax(self, x) -> tuple[float, int]:
         if self.xchg is not None:
@@ -172,10 +228,19 @@ class ShardedLMHead:
 
 class ShardedMLP:
     """gate_up rows and down columns of one layer for this rank (preq2 gs32 blobs), with the
-    fused gate_up+SiLU on the local rows and an all-reduce of the down partial sums."""
+    fused gate_up+SiLU on the local rows and an all-reduce of the down partial sums.
+
+    numerics: "fast" (the engine's default kernels) or "reference_exact" (the kernels that are
+    bitwise equal to the reference's compiled GEMV and SwiGLU).  fused=True (GPUs, the default)
+    sums the partials with the peer all-reduce kernel; fused=False through torch.distributed.
+    `exchange`: an open _VecExchange (hidden floats) to share between several layers' MLPs;
+    the caller closes it."""
 
     def __init__(self, gu_meta, gu_quant, dn_meta, dn_quant, hidden: int, inter: int, local=None, device=None,
-                 world=None, rank=None):
+                 world=None, rank=None, fused: bool = True, numerics: str = "fast", exchange=None):
+        if numerics not in ("fast", "reference_exact"):
+            raise ValueError(f"unknown numerics mode {numerics!r}")
+        self.numerics = numerics
         self.world, self.rank = _group(world, rank)
         self.H, self.I = hidden, inter
         self.a, self.b = shard_range(inter, self.world, self.rank, 32)
@@ -196,6 +261,7 @@ class ShardedMLP:
         self.dn_meta = np.ascontiguousarray(dm[:, g0:g1, :]).reshape(-1)
         self.dn_quant = np.ascontiguousarray(dq[:, g0:g1, :]).reshape(-1)
         self.local = local
+        self.vx = None
         if local is None:
             dev = device or torch.device("cuda", torch.cuda.current_device())
             self.device = dev
@@ -203,8 +269,20 @@ class ShardedMLP:
             self.d_gm, self.d_gq, self.d_dm, self.d_dq = t(self.gu_meta), t(self.gu_quant), t(self.dn_meta), t(self.dn_quant)
             self.h = torch.empty(self.n, dtype=torch.float32, device=dev)
             self.y = torch.empty(H, dtype=torch.float32, device=dev)
+            self.out = torch.empty(H, dtype=torch.float32, device=dev)
+            self._own_vx = False
+            if exchange is not None:
+                self.vx = exchange
+            elif fused and world is None and self.world > 1:
+                self.vx = _VecExchange(self.world, self.rank, H, dev)
+                self._own_vx = True
         else:
             self.device = torch.device("cpu")
+
+    def close(self):
+        if self.vx is not None and getattr(self, "_own_vx", False):
+            self.vx.close()
+        self.vx = None
 
     def local_partial(self, x):
         """down[:, a:b] . A8(silu(gate[a:b] x) * up[a:b] x): this rank's partial output."""
@@ -214,6 +292,14 @@ class ShardedMLP:
             h = o.swiglu(gu[: self.n], gu[self.n :])
             return torch.from_numpy(o.gemv_preq2_fused(self.dn_meta, self.dn_quant, h, self.H, self.n))
         s = torch.cuda.current_stream(self.device).cuda_stream
+        if self.numerics == "reference_exact":
+            import ctypes
+
+            _lib.call("asdsl_b200_gateup_silu_exact", self.d_gm.data_ptr(), self.d_gq.data_ptr(), x.data_ptr(), None,
+                      ctypes.c_float(0.0), self.h.data_ptr(), self.n, self.H, s)
+            _lib.call("asdsl_b200_gemv_preq2_fused_exact", self.d_dm.data_ptr(), self.d_dq.data_ptr(),
+                      self.h.data_ptr(), None, ctypes.c_float(0.0), self.y.data_ptr(), self.H, self.n, s)
+            return self.y
         _lib.call("asdsl_b200_gateup_silu", _lib.FMT_PREQ2, self.d_gm.data_ptr(), self.d_gq.data_ptr(), x.data_ptr(),
                   self.h.data_ptr(), self.n, self.H, s)
         _lib.call("asdsl_b200_gemv_preq2_fused", self.d_dm.data_ptr(), self.d_dq.data_ptr(), self.h.data_ptr(),
@@ -222,6 +308,9 @@ class ShardedMLP:
 
     def forward(self, x) -> torch.Tensor:
         y = self.local_partial(x)
+        if self.vx is not None:
+            self.vx.allreduce(y, self.out, self.H, torch.cuda.current_stream(self.device).cuda_stream)
+            return self.out
         if self.world > 1:
             import torch.distributed as dist
 

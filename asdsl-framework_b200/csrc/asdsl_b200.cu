@@ -405,6 +405,8 @@ struct asdsl_b200_xchg {
     unsigned long long** peer_table = nullptr; // device array [world]
     void* mapped[64] = {};                     // opened peer mappings (null for self)
     bool open = false;
+    unsigned long long* stamps = nullptr;      // optional %globaltimer stamps [n][4] (caller's memory)
+    int stamp_mask = 0;
 };
 
 namespace {
@@ -435,6 +437,8 @@ int gemv_argmax_impl(int fmt, const uint8_t* w0, const uint8_t* w1, const float*
             a.xchg_epoch = xg->epoch;
             a.xchg_world = xg->world;
             a.xchg_rank = xg->rank;
+            a.xchg_stamps = xg->stamps;
+            a.xchg_stamp_mask = xg->stamp_mask;
         }
     };
     const long long nbands = (static_cast<long long>(M) + 3) / 4;
@@ -542,6 +546,15 @@ int asdsl_b200_xchg_destroy(asdsl_b200_xchg* x) {
     return kOk;
 }
 
+int asdsl_b200_xchg_set_stamps(asdsl_b200_xchg* x, unsigned long long* stamps, int n_slots) {
+    if (!x) return set_error(kEinval, "xchg_set_stamps: null exchange");
+    if (stamps && (n_slots <= 0 || (n_slots & (n_slots - 1))))
+        return set_error(kEinval, "xchg_set_stamps: n_slots must be a power of two");
+    x->stamps = stamps;
+    x->stamp_mask = stamps ? n_slots - 1 : 0;
+    return kOk;
+}
+
 int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
                                 float* out_val, int32_t* out_idx, int row_base, void* scratch, size_t scratch_bytes,
                                 int M, int K, asdsl_b200_xchg* xg, void* stream) {
@@ -551,6 +564,230 @@ int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, c
     if (static_cast<long long>(row_base) + M > (1ll << 24))
         return set_error(kEinval, "gemv_argmax_xchg: global row indices must stay below 2^24");
     return gemv_argmax_impl(fmt, w0, w1, x, y, out_val, out_idx, row_base, scratch, scratch_bytes, M, K, stream, xg);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// vector exchange: the all-reduce of the K-split down projection (row-sharded MLP).  Every rank
+// holds a buffer of [2 parities][world][stride] 64-bit words, mapped into every peer over CUDA
+// IPC.  A word is one float of a rank's partial in its low half and the step number in its high
+// half, stored with one 64-bit relaxed system-scope store: a reader that sees the step number
+// sees the float, so no fence and no separate flag are needed.  One kernel per step: CTA d
+// stores this rank's partial into rank d's buffer (NVLink peer stores), then sums its slice of
+// the world's partials in rank order from its own buffer, polling -- bounded -- each word until
+// it carries this step's number; every rank ends with the same bits.  Buffers alternate by step
+// parity: a rank stores step e + 2 only after it has seen every rank's step e + 1 words, which
+// each rank stores only after its step-e kernel (and so its reads of step e) completed.
+// No multicast, no library kernel on peer memory.
+// ---------------------------------------------------------------------------
+struct asdsl_b200_vxchg {
+    int world = 1, rank = 0, device = 0, n_max = 0, stride = 0;
+    unsigned long long* buf = nullptr;  // this rank's [2][world][stride] words
+    int* epoch = nullptr;               // [0] last completed step, [1] CTA arrival counter
+    unsigned long long** peer_buf = nullptr;  // device array [world]: every rank's buffer, mapped here
+    void* mapped_buf[64] = {};
+    bool open = false;
+    unsigned long long* stamps = nullptr;  // optional %globaltimer stamps [n][4] (caller's memory)
+    int stamp_mask = 0;
+};
+
+namespace {
+constexpr int kVxThreads = 256;
+constexpr int kVxMaxWorld = 16;
+constexpr int kVxPerThread = 2;  // elements per thread: all their words are loaded before any wait
+
+// grid: enough CTAs that every thread owns at most kVxPerThread elements of the vector
+inline int vx_grid(int n) { return std::max(1, (n + kVxThreads * kVxPerThread - 1) / (kVxThreads * kVxPerThread)); }
+
+__global__ void __launch_bounds__(kVxThreads)
+    k_allreduce_peer(const float* __restrict__ part, float* __restrict__ out, const float* __restrict__ add, int n,
+                     int stride, int world, int rank, unsigned long long* const* __restrict__ peer_buf,
+                     const unsigned long long* self_buf, int* epoch, unsigned int* status,
+                     unsigned long long* stamps, int stamp_mask) {
+    // launched as a programmatic dependent of the GEMV that produced `part`: wait for it, then
+    // let the next kernel launch (its weight streaming overlaps this exchange)
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const int e = epoch[0] + 1;
+    const int par = e & 1;
+    const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned int>(e)) << 32;
+    // stamps (CTA 0): kernel start, own slice stored to every rank, slice gathered and summed, end
+    unsigned long long* stamp =
+        (stamps && blockIdx.x == 0 && threadIdx.x == 0) ? stamps + (e & stamp_mask) * 4 : nullptr;
+    if (stamp) stamp[0] = globaltimer_ns();
+    // this thread's elements: i = blockIdx.x * kVxThreads * kVxPerThread + j * kVxThreads + threadIdx.x
+    const int ib = blockIdx.x * kVxThreads * kVxPerThread + threadIdx.x;
+    // 1. store this rank's values of those elements, tagged, into every rank's buffer
+    const size_t my_off = (static_cast<size_t>(par) * world + rank) * stride;
+#pragma unroll
+    for (int j = 0; j < kVxPerThread; ++j) {
+        const int i = ib + j * kVxThreads;
+        if (i < n) {
+            const unsigned long long wv = tag | __float_as_uint(part[i]);
+            for (int d = 0; d < world; ++d) st_relaxed_sys_u64(peer_buf[d] + my_off + i, wv);
+        }
+    }
+    if (stamp) stamp[1] = globaltimer_ns();
+    // 2. every rank's words of those elements: all loads issued first, then a bounded wait on
+    //    each word still carrying an older step, then the rank-ordered sum
+    const unsigned long long* base = self_buf + static_cast<size_t>(par) * world * stride;
+    unsigned long long w[kVxPerThread][kVxMaxWorld];
+#pragma unroll
+    for (int j = 0; j < kVxPerThread; ++j) {
+        const int i = ib + j * kVxThreads;
+#pragma unroll
+        for (int r = 0; r < kVxMaxWorld; ++r)
+            if (r < world && i < n) w[j][r] = ld_relaxed_sys_u64(base + static_cast<size_t>(r) * stride + i);
+    }
+    const unsigned long long t0 = globaltimer_ns();
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < kVxPerThread; ++j) {
+        const int i = ib + j * kVxThreads;
+        if (i >= n) continue;
+        float acc = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kVxMaxWorld; ++r) {
+            if (r < world) {
+                while (ok && (w[j][r] & 0xFFFFFFFF00000000ull) != tag) {
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                        atomicOr(status, kStatusXchgWait);
+                        ok = false;
+                    } else {
+                        w[j][r] = ld_relaxed_sys_u64(base + static_cast<size_t>(r) * stride + i);
+                    }
+                }
+                const float v = __uint_as_float(static_cast<unsigned int>(w[j][r]));
+                acc = (r == 0) ? v : __fadd_rn(acc, v);
+            }
+        }
+        if (ok) out[i] = add ? __fadd_rn(acc, add[i]) : acc;
+    }
+    // 3. the last CTA to arrive advances the step counter (the next launch reads it)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (stamp) stamp[2] = globaltimer_ns();
+        const bool last = atomicAdd(epoch + 1, 1) == static_cast<int>(gridDim.x) - 1;
+        if (last) {
+            epoch[1] = 0;
+            epoch[0] = e;
+        }
+        if (stamp) stamp[3] = globaltimer_ns();
+    }
+}
+}  // namespace
+
+extern "C" {
+
+size_t asdsl_b200_vxchg_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int asdsl_b200_vxchg_create(int world, int rank, int n_max, asdsl_b200_vxchg** out, void* ipc_handle) {
+    if (!out || !ipc_handle) return set_error(kEinval, "vxchg_create: null pointer");
+    if (world < 1 || world > kVxMaxWorld || rank < 0 || rank >= world)
+        return set_error(kEinval, "vxchg_create: world must be in [1, 16], rank in [0, world)");
+    if (n_max <= 0 || n_max > (1 << 24)) return set_error(kEinval, "vxchg_create: vector length must be in [1, 2^24]");
+    *out = nullptr;
+    auto* x = new asdsl_b200_vxchg();
+    x->world = world;
+    x->rank = rank;
+    x->n_max = n_max;
+    x->stride = (n_max + 1) & ~1;  // 16-byte aligned slots
+    cudaGetDevice(&x->device);
+    auto fail = [&](int rc) {
+        asdsl_b200_vxchg_destroy(x);
+        return rc;
+    };
+    const size_t bbytes = 2ull * world * x->stride * sizeof(unsigned long long);
+    if (cudaMalloc(reinterpret_cast<void**>(&x->buf), bbytes) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&x->epoch), 2 * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&x->peer_buf), world * sizeof(void*)) != cudaSuccess)
+        return fail(set_error(asdsl::kEnomem, "vxchg_create: device allocation failed"));
+    // step tags start at 1: a zeroed word never matches
+    if (cudaMemset(x->buf, 0, bbytes) != cudaSuccess || cudaMemset(x->epoch, 0, 2 * sizeof(int)) != cudaSuccess)
+        return fail(set_error(kEcuda, "vxchg_create: memset failed"));
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, x->buf);
+    if (e != cudaSuccess)
+        return fail(set_error(kEcuda, std::string("vxchg_create: cudaIpcGetMemHandle: ") + cudaGetErrorString(e)));
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *out = x;
+    return kOk;
+}
+
+int asdsl_b200_vxchg_open(asdsl_b200_vxchg* x, const void* handles) {
+    if (!x || !handles) return set_error(kEinval, "vxchg_open: null pointer");
+    if (x->open) return kOk;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != x->device) return set_error(kEinval, "vxchg_open: call with the exchange's device current");
+    unsigned long long* bt[kVxMaxWorld];
+    for (int r = 0; r < x->world; ++r) {
+        if (r == x->rank) {
+            bt[r] = x->buf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + r * sizeof(h), sizeof(h));
+        const cudaError_t e = cudaIpcOpenMemHandle(&x->mapped_buf[r], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error(kEcuda, std::string("vxchg_open: cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+        bt[r] = static_cast<unsigned long long*>(x->mapped_buf[r]);
+    }
+    ASDSL_CUDA(cudaMemcpy(x->peer_buf, bt, x->world * sizeof(void*), cudaMemcpyHostToDevice));
+    x->open = true;
+    return kOk;
+}
+
+int asdsl_b200_vxchg_destroy(asdsl_b200_vxchg* x) {
+    if (!x) return kOk;
+    for (int r = 0; r < 64; ++r)
+        if (x->mapped_buf[r]) cudaIpcCloseMemHandle(x->mapped_buf[r]);
+    if (x->buf) cudaFree(x->buf);
+    if (x->epoch) cudaFree(x->epoch);
+    if (x->peer_buf) cudaFree(x->peer_buf);
+    delete x;
+    return kOk;
+}
+
+int asdsl_b200_vxchg_set_stamps(asdsl_b200_vxchg* x, unsigned long long* stamps, int n_slots) {
+    if (!x) return set_error(kEinval, "vxchg_set_stamps: null exchange");
+    if (stamps && (n_slots <= 0 || (n_slots & (n_slots - 1))))
+        return set_error(kEinval, "vxchg_set_stamps: n_slots must be a power of two");
+    x->stamps = stamps;
+    x->stamp_mask = stamps ? n_slots - 1 : 0;
+    return kOk;
+}
+
+int asdsl_b200_allreduce_peer(asdsl_b200_vxchg* x, const float* part, float* out, const float* add, int n,
+                              void* stream) {
+    if (!x || !x->open) return set_error(kEinval, "allreduce_peer: exchange not opened");
+    if (!part || !out) return set_error(kEinval, "allreduce_peer: null pointer");
+    if (n < 0 || n > x->n_max) return set_error(kEinval, "allreduce_peer: n exceeds the exchange's vector length");
+    const uintptr_t p0 = reinterpret_cast<uintptr_t>(part), o0 = reinterpret_cast<uintptr_t>(out);
+    const uintptr_t nb = static_cast<uintptr_t>(n) * sizeof(float);
+    if (n > 0 && p0 < o0 + nb && o0 < p0 + nb)
+        return set_error(kEinval, "allreduce_peer: the partial and the output must not overlap");
+    unsigned int* st = device_status_ptr();
+    if (!st) return set_error(kEcuda, "cannot resolve the device status word");
+    // n == 0 still runs the step, so that every rank takes the same number of steps
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(vx_grid(n));
+    cfg.blockDim = dim3(kVxThreads);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    if (launch_policy().pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    ASDSL_CUDA(cudaLaunchKernelEx(&cfg, k_allreduce_peer, part, out, add, n, x->stride, x->world, x->rank,
+                                  static_cast<unsigned long long* const*>(x->peer_buf),
+                                  static_cast<const unsigned long long*>(x->buf), x->epoch, st, x->stamps,
+                                  x->stamp_mask));
+    return kOk;
 }
 
 }  // extern "C"

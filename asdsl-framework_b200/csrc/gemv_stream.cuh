@@ -155,6 +155,10 @@ struct GemvArgs {
     unsigned long long* xchg_self;          // this rank's slot buffer
     int* xchg_epoch;                        // device-resident step counter of the exchange
     int xchg_world, xchg_rank;
+    // optional %globaltimer stamps of the exchange, [slot = step & mask][4]: consumers released,
+    // local argmax done, own word stored to every peer, every peer's word seen (null = off)
+    unsigned long long* xchg_stamps;
+    int xchg_stamp_mask;
     // multi-token kernels: the tokens' A8 areas, quantized once by k_quant_tokens in the layout
     // of the shared-memory areas (n_tokens x xarea_layout_bytes); null = each CTA quantizes
     const uint8_t* xa_pre;
@@ -1353,6 +1357,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     // ---------------- consumer warps: every warp takes part of every stage ----------------
     const int cw = warp;
     grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
+    if constexpr (EPI == kEpiArgmax) {
+        if (ga.xchg_stamps != nullptr && blockIdx.x == 0 && threadIdx.x == 0)
+            ga.xchg_stamps[((*ga.xchg_epoch + 1) & ga.xchg_stamp_mask) * 4] = globaltimer_ns();
+    }
     // multi-token: one A8 area per activation row, xa_stride bytes apart
     const uint32_t xa_stride = (NT > 1) ? xarea_layout_bytes(ga.K, ga.gs, false) : 0u;
     if constexpr (NT == 1) {
@@ -1435,19 +1443,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
                     const unsigned long long word = static_cast<unsigned long long>(__float_as_uint(fv)) |
                                                     (static_cast<unsigned long long>(fi & 0xFFFFFF) << 32) |
                                                     (e8 << 56);
-                    for (int r = 0; r < W; ++r) st_release_sys_u64(ga.xchg_peers[r] + par * W + ga.xchg_rank, word);
+                    unsigned long long* stamp =
+                        ga.xchg_stamps ? ga.xchg_stamps + (e & ga.xchg_stamp_mask) * 4 : nullptr;
+                    if (stamp) stamp[1] = globaltimer_ns();
+                    // the word carries its own step tag: relaxed stores, no system-scope fence
+                    for (int r = 0; r < W; ++r) st_relaxed_sys_u64(ga.xchg_peers[r] + par * W + ga.xchg_rank, word);
+                    if (stamp) stamp[2] = globaltimer_ns();
                     float gv = -INFINITY;
                     int gi = fi;
                     bool ok = true;
                     const unsigned long long t0 = globaltimer_ns();
                     for (int r = 0; r < W && ok; ++r) {
-                        unsigned long long w = ld_acquire_sys_u64(ga.xchg_self + par * W + r);
+                        unsigned long long w = ld_relaxed_sys_u64(ga.xchg_self + par * W + r);
                         while ((w >> 56) != e8) {
                             if (globaltimer_ns() - t0 > kWaitLimitNs) {
                                 ok = false;
                                 break;
                             }
-                            w = ld_acquire_sys_u64(ga.xchg_self + par * W + r);
+                            w = ld_relaxed_sys_u64(ga.xchg_self + par * W + r);
                         }
                         if (!ok) break;
                         const float v = __uint_as_float(static_cast<unsigned int>(w));
@@ -1456,6 +1469,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
                             gi = static_cast<int>((w >> 32) & 0xFFFFFFull);
                         }
                     }
+                    if (stamp) stamp[3] = globaltimer_ns();
                     if (ok) {
                         fv = gv;
                         fi = gi;

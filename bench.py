@@ -636,6 +636,31 @@ def c4_bench(rank: int) -> dict:
     return out
 
 
+def stamp_summary(buf, names, world: int) -> list | None:
+    """Median phase durations (us) of the instrumented exchange steps, per rank: `buf` holds
+    four %globaltimer stamps per step ([n, 4] int64, zero = not written); `names` label the three
+    differences; `period` is the median gap between consecutive steps' first stamps."""
+    import numpy as np
+
+    a = buf.cpu().numpy().astype(np.int64)
+    ok = (a > 0).all(1) & (np.diff(a, axis=1) >= 0).all(1)
+    a = a[ok]
+    mine = None
+    if len(a) >= 3:
+        d = np.diff(a, axis=1) / 1e3
+        mine = {names[i]: round(float(np.median(d[:, i])), 3) for i in range(3)}
+        mine["p90_" + names[2]] = round(float(np.percentile(d[:, 2], 90)), 3)
+        mine["period"] = round(float(np.median(np.diff(np.sort(a[:, 0])))) / 1e3, 3)
+        mine["steps"] = int(len(a))
+    if world == 1:
+        return [mine]
+    import torch.distributed as dist
+
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    return every
+
+
 LM_METRIC = "lm_head W4 GEMV + argmax HBM GB/s (200064x3072 Q4_128, row-sharded, all ranks)"
 
 
@@ -703,17 +728,48 @@ def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dic
     for i in range(5):
         step(heads[i % len(heads)])
     torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
+    # one CUDA graph of one step per weight copy; `steps` rounded up to whole graphs.  A second
+    # graph runs the same shard's GEMV + argmax without the exchange: the difference of the two
+    # is the exchange's cost (its peer stores, the wait for the slowest rank and its fences).
+    cs = torch.cuda.Stream()
+    # %globaltimer stamps of the first copy's exchange (one step per graph replay)
+    stamps = torch.zeros((1024, 4), dtype=torch.int64, device=xd.device)
+    if heads[0].xchg is not None:
+        heads[0].xchg.set_stamps(stamps)
+    graphs = {}
+    for kind in ("step", "local"):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cs):
+            for h in heads:
+                step(h) if kind == "step" else h.local_argmax(xd)
+        graphs[kind] = gr
+    reps = max(1, -(-steps // len(heads)))
+    steps = reps * len(heads)
+    times = {}
+    for kind in ("step", "local"):
+        for _ in range(3):
+            graphs[kind].replay()
+        torch.cuda.synchronize()
+        stamps.zero_()
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
 
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(steps):
-        step(heads[i % len(heads)])
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cs)
+        with torch.cuda.stream(cs):
+            for _ in range(reps):
+                graphs[kind].replay()
+        e1.record(cs)
+        torch.cuda.synchronize()
+        times[kind] = e0.elapsed_time(e1) / steps
+        if kind == "step":
+            phases = stamp_summary(stamps, ("local_argmax", "store_words", "wait_peers"), world)
+    ms, local_ms = times["step"], times["local"]
+    del graphs
+    if heads[0].xchg is not None:
+        heads[0].xchg.set_stamps(None)
     # e2e: host activation in, host token out, every step
     hx = torch.from_numpy(x).pin_memory()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -728,9 +784,9 @@ def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dic
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([ms, e2e_ms], device="cuda")
+        t = torch.tensor([ms, e2e_ms, local_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0].item()), float(t[1].item())
+        ms, e2e_ms, local_ms = float(t[0].item()), float(t[1].item()), float(t[2].item())
     assert _lib.device_status(clear=True) == 0
     if world > 1:
         import torch.distributed as dist
@@ -742,6 +798,14 @@ def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dic
     return {"metric": LM_METRIC, "value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "ms_per_step": round(ms, 5), "n_gpus": world, "scaling": "strong", "steps": steps,
             "bytes_per_step": total, "weight_copies_rotated_per_rank": len(heads),
+            "split_us": {"local_gemv_argmax": round(local_ms * 1e3, 3),
+                         "exchange": round(max(ms - local_ms, 0.0) * 1e3, 3)},
+            "stamps_us_per_rank": phases,
+            "stamps": ("%globaltimer in the kernel, medians over the timed steps of one weight copy: "
+                       "local_argmax = consumers released -> last CTA's argmax reduced, store_words = "
+                       "its word stored to every peer, wait_peers = until every rank's word is seen "
+                       "(includes the other ranks' lateness), period = step to step"),
+            "timing": "CUDA graph of one step per rotated weight copy, replayed; max over ranks",
             "collective": ("in-kernel exchange of one (max, index) word per rank over NVLink peer stores"
                            if world > 1 else None),
             "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
@@ -749,6 +813,173 @@ def lm_head_bench(world: int, rank: int, steps: int = 200, seed: int = 2) -> dic
             "check": check, "config": {"workload": "c2_lm_head_row_sharded", "seed": seed,
                                        "weights": "fp32 N(0, 0.02) (device RNG) -> repack_fp32_to_q4_128_blocks "
                                                   "on the device (the reference's g128 quantizer)"}}
+
+
+MLP_METRIC = ("sharded MLP W4A8 HBM GB/s (Phi-4-mini gate_up 16384x3072 + SiLU + down 3072x8192, preq2 gs32, "
+              "row/K-sharded, all ranks)")
+
+
+def mlp_sharded_bench(world: int, rank: int, steps: int = 480, seed: int = 1) -> dict:
+    """Strong scaling of one decode layer's MLP: rank r holds gate/up rows [a_r, b_r) and the
+    matching down_proj input columns; a step is the local fused gate_up + SiLU, the local down
+    GEMV (a partial of the hidden vector) and, at N > 1, the peer all-reduce kernel
+    (asdsl_b200_allreduce_peer) that leaves every rank the same summed 3072 floats.
+    value = all ranks' weight bytes / max-over-ranks step time.  Beside it: the same step with
+    torch.distributed's NCCL all_reduce in place of the peer kernel, and the local GEMVs alone, so
+    the collective's share is measured.  Weights fp32 N(0, 0.02) (device RNG, seed 1) through the
+    reference's C0 pipeline (gs 32 asymmetric + clip search -> preq2) on the device, x ~ N(0, 1);
+    each rank rotates weight copies so a copy is reused only after > 300 MB."""
+    import numpy as np
+    import torch
+
+    from asdsl_b200 import _lib
+    from asdsl_b200.quantization.device import prepare_preq2_device
+    from asdsl_b200.shard import ShardedMLP, _VecExchange
+
+    H, I = 3072, 8192
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    host = []
+    for rows, cols in ((2 * I, H), (H, I)):
+        w = torch.randn((rows, cols), generator=g, device="cuda") * 0.02
+        m, q = prepare_preq2_device(w)
+        host += [m.cpu().numpy(), q.cpu().numpy()]
+        del w, m, q
+    x = torch.randn(H, generator=g, device="cuda").cpu().numpy().astype(np.float32)
+    torch.cuda.empty_cache()
+    vx = _VecExchange(world, rank, H, dev) if world > 1 else None
+    mlps = [ShardedMLP(*host, H, I, device=dev, exchange=vx)]
+    shard_bytes = sum(t.numel() for t in (mlps[0].d_gm, mlps[0].d_gq, mlps[0].d_dm, mlps[0].d_dq))
+    n_copies = max(1, -(-320_000_000 // shard_bytes))
+    for _ in range(n_copies - 1):
+        mlps.append(ShardedMLP(*host, H, I, device=dev, exchange=vx))
+    xd = torch.from_numpy(x).to(dev)
+    out = mlps[0].forward(xd).clone()
+    torch.cuda.synchronize()
+    check = None
+    if rank == 0:
+        from oracle.oracle import Oracle, build as build_oracle, rel_err
+
+        if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+            build_oracle()
+        orc = Oracle()
+        gu = orc.gemv_preq2_fused(host[0], host[1], x, 2 * I, H)
+        ref = orc.gemv_preq2_fused(host[2], host[3], orc.swiglu(gu[:I], gu[I:]), H, I)
+        err = rel_err(out.cpu().numpy(), ref)
+        check = {"rel_err_vs_oracle": err, "tolerance": 1e-3}
+        if err > 1e-3:
+            raise SystemExit(f"bench: sharded MLP mismatch vs oracle ({err})")
+    total = sum(a.nbytes for a in host)
+    del host
+
+    def nccl_step(m):
+        y = m.local_partial(xd)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(y, op=dist.ReduceOp.SUM)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(torch.zeros(H, device=dev))  # the communicator exists before capture
+    kinds = {"step": lambda m: m.forward(xd), "local": lambda m: m.local_partial(xd)}
+    if world > 1:
+        kinds["nccl"] = nccl_step
+    cs = torch.cuda.Stream()
+    stamps = torch.zeros((1024, 4), dtype=torch.int64, device=dev)
+    if vx is not None:
+        vx.set_stamps(stamps)
+    for m in mlps:
+        kinds["step"](m)
+    torch.cuda.synchronize()
+    graphs = {}
+    for kind, fn in kinds.items():
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cs):
+            for m in mlps:
+                fn(m)
+        graphs[kind] = gr
+    reps = max(1, -(-steps // len(mlps)))
+    steps = reps * len(mlps)
+    times = {}
+    phases = None
+    for kind in kinds:
+        for _ in range(3):
+            graphs[kind].replay()
+        torch.cuda.synchronize()
+        stamps.zero_()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cs)
+        with torch.cuda.stream(cs):
+            for _ in range(reps):
+                graphs[kind].replay()
+        e1.record(cs)
+        torch.cuda.synchronize()
+        times[kind] = e0.elapsed_time(e1) / steps
+        if kind == "step" and vx is not None:
+            phases = stamp_summary(stamps, ("push", "gather_sum", "finish"), world)
+    torch.cuda.synchronize()
+    del graphs  # the NCCL graph is released before the process group goes
+    if vx is not None:
+        vx.set_stamps(None)
+    # e2e through the public call: host activation in, host output vector out, every step
+    hx = torch.from_numpy(x).pin_memory()
+    hy = torch.empty(H, dtype=torch.float32).pin_memory()
+    n_e2e = min(steps, 100)
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(n_e2e):
+        xd.copy_(hx, non_blocking=True)
+        hy.copy_(mlps[i % len(mlps)].forward(xd), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / n_e2e
+    ms, local_ms = times["step"], times["local"]
+    nccl_ms = times.get("nccl")
+    if world > 1:
+        t = torch.tensor([ms, local_ms, nccl_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, local_ms, nccl_ms, e2e_ms = (float(v) for v in t.tolist())
+    assert _lib.device_status(clear=True) == 0
+    if world > 1:
+        dist.barrier()  # no rank still stores into a peer's buffers
+    for m in mlps:
+        m.close()
+    if vx is not None:
+        vx.close()
+    xchg_us = max(ms - local_ms, 0.0) * 1e3
+    return {"metric": MLP_METRIC, "value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "us_per_step": round(ms * 1e3, 3), "n_gpus": world, "scaling": "strong", "steps": steps,
+            "bytes_per_step": total, "weight_copies_rotated_per_rank": len(mlps),
+            "split_us": {"local_gateup_silu_down": round(local_ms * 1e3, 3), "allreduce_peer": round(xchg_us, 3)},
+            "nccl_allreduce_step_us": round(nccl_ms * 1e3, 3) if nccl_ms is not None else None,
+            "stamps_us_per_rank": phases,
+            "stamps": ("%globaltimer in the all-reduce kernel (CTA 0), medians over the timed steps: push = "
+                       "kernel start -> own partial stored to the peer, gather_sum = until CTA 0's slice of every "
+                       "rank's tagged words is seen and summed (includes the other ranks' lateness), finish = "
+                       "step counter advanced, period = step to step")
+            if phases else None,
+            "collective": ("one kernel: peer stores of the 12 KB partial into every rank, bounded wait, "
+                           "rank-ordered sum (asdsl_b200_allreduce_peer)" if world > 1 else None),
+            "limiter": (None if world == 1 else
+                        "the all-reduce of the 12 KB partial (latency bound)" if xchg_us > local_ms * 1e3
+                        else "HBM streaming of the local weight shard"),
+            "timing": "CUDA graph of one step per rotated weight copy, replayed; max over ranks",
+            "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": 4 * H,
+                    "d2h_bytes_per_step": 4 * H, "us_per_step": round(e2e_ms * 1e3, 3)},
+            "gpu_launches_per_step": 3 if world > 1 else 2,
+            "check": check,
+            "config": {"workload": "c3_mlp_layer_sharded", "seed": seed, "hidden": H, "intermediate": I,
+                       "weights": "fp32 N(0, 0.02) (device RNG) -> the reference's C0 pipeline (gs 32 asymmetric, "
+                                  "clip search, preq2) on the device"}}
 
 
 # ---------------------------------------------------------------------------
@@ -766,6 +997,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--no-lm-head", action="store_true", help="skip the config-2 sharded lm_head measurement")
+    ap.add_argument("--no-mlp", action="store_true", help="skip the sharded MLP measurement")
     ap.add_argument("--no-c0", action="store_true", help="skip the config-0 single-GEMV measurement")
     ap.add_argument("--only-c0", action="store_true", help="run only the config-0 section (profiling)")
     ap.add_argument("--c4", action=argparse.BooleanOptionalAction, default=True,
@@ -1021,6 +1253,7 @@ def main():
         decode_fast = decode_bench(dmodel, "fast", ref, args.decode_steps, world=world)
         del dmodel
     lm_sharded = None if args.no_lm_head else lm_head_bench(world, rank)
+    mlp_sharded = None if args.no_mlp else mlp_sharded_bench(world, rank)
 
     if rank == 0:
         clocks = clk.summary()
@@ -1057,6 +1290,7 @@ def main():
             "decode": decode,
             "decode_fast": decode_fast,
             "lm_head_sharded": lm_sharded,
+            "mlp_sharded": mlp_sharded,
         }
         print(json.dumps(out), flush=True)
     for g in graphs:

@@ -220,10 +220,41 @@ int asdsl_b200_xchg_create(int world, int rank, asdsl_b200_xchg** out, void* ipc
 size_t asdsl_b200_xchg_handle_bytes(void);
 int asdsl_b200_xchg_open(asdsl_b200_xchg* xchg, const void* handles);
 int asdsl_b200_xchg_destroy(asdsl_b200_xchg* xchg);
+/* Optional instrumentation: each later asdsl_b200_gemv_argmax_xchg writes four %globaltimer
+ * stamps (ns) of step e to stamps[(e & (n_slots - 1)) * 4 + i]: i = 0 the consumers released
+ * (previous kernel complete, CTA 0), 1 the local argmax reduced (last CTA), 2 this rank's word
+ * stored to every peer, 3 every peer's word seen.  `stamps` is device memory of n_slots * 4
+ * words, n_slots a power of two; null turns the stamps off.  No reference counterpart. */
+int asdsl_b200_xchg_set_stamps(asdsl_b200_xchg* xchg, unsigned long long* stamps, int n_slots);
 int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, const float* x, float* y,
                                 float* out_val, int32_t* out_idx, int row_base, void* scratch,
                                 size_t scratch_bytes, int out_features, int in_features, asdsl_b200_xchg* xchg,
                                 void* stream);
+
+/* Row-sharded MLP across the GPUs of one box (one process per GPU): rank r holds gate/up rows
+ * [a_r, b_r) and the matching input columns of down_proj, so each rank's down GEMV yields a
+ * partial of the hidden vector; asdsl_b200_allreduce_peer sums the partials of all ranks in one
+ * kernel: NVLink peer stores of this rank's partial into every rank's buffer as 64-bit words
+ * (the float and the step number, so no fence or flag is needed), then a bounded wait on each
+ * word and a rank-ordered sum -- every rank gets the same bits -- optionally adding a residual:
+ * out = (sum over r of part_r) + add.  Replaces the down projection of the engine's MLP
+ * (asdsl/kernels/native/unified_engine.cpp:1586-1597) split over GPUs with an all-reduce.
+ * Setup as for asdsl_b200_xchg: create on every rank (ipc_handle receives
+ * asdsl_b200_vxchg_handle_bytes() bytes; world <= 16), all-gather the handles in rank order,
+ * open.  Every rank must call asdsl_b200_allreduce_peer the same number of times with the same
+ * n (<= n_max); `part` and `out` must not overlap; a call whose peers do not arrive within 2 s
+ * sets the device status word (ASDSL_B200_ETIMEOUT from asdsl_b200_device_status). */
+typedef struct asdsl_b200_vxchg asdsl_b200_vxchg;
+int asdsl_b200_vxchg_create(int world, int rank, int n_max, asdsl_b200_vxchg** out, void* ipc_handle);
+size_t asdsl_b200_vxchg_handle_bytes(void);
+int asdsl_b200_vxchg_open(asdsl_b200_vxchg* vxchg, const void* handles);
+int asdsl_b200_vxchg_destroy(asdsl_b200_vxchg* vxchg);
+/* Optional instrumentation as asdsl_b200_xchg_set_stamps, per asdsl_b200_allreduce_peer step
+ * (CTA 0): 0 kernel start (previous kernel complete), 1 own partial stored to its peer, 2 CTA 0's
+ * slice gathered from every rank and summed, 3 the step counter advanced. */
+int asdsl_b200_vxchg_set_stamps(asdsl_b200_vxchg* vxchg, unsigned long long* stamps, int n_slots);
+int asdsl_b200_allreduce_peer(asdsl_b200_vxchg* vxchg, const float* part, float* out, const float* add, int n,
+                              void* stream);
 
 /* Fused gate_up GEMV + SiLU(gate)*up: rows [0, I) are gate, [I, 2I) are up, h[i] = silu(gate_i)*up_i
  * with the reference's fast_exp.  fmt PREQ2 (w0 = meta, w1 = quant), Q4_128 (w0 = blocks) or

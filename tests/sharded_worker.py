@@ -1,0 +1,139 @@
+"""One rank of the multi-GPU parity check (launched by tests/test_multi_rank_gpu.py under
+torch.distributed.run, one process per GPU, NCCL process group for the host-side plumbing).
+
+Checks, on every rank, against the CPU oracle (oracle/asdsl_oracle.c):
+* ShardedMLP at the Phi-4-mini MLP shape (hidden 3072, intermediate 8192, preq2 gs32): gate_up
+  rows and down columns split over the ranks, partials summed by the peer all-reduce kernel.
+  numerics="reference_exact": every step's output is bitwise the rank-ordered float32 sum of
+  the oracle's per-shard partials, and within max|d|/max|y| <= 1e-3 of the unsharded oracle;
+  numerics="fast": within 1e-3 of the unsharded oracle; all ranks hold the same bits.  Also the
+  torch.distributed all_reduce path (fused=False) and 200 back-to-back steps (the buffers
+  alternate by step parity) with the last step checked.
+* ShardedLMHead with the in-kernel argmax exchange: the global index equals the oracle's argmax.
+Exits non-zero (AssertionError) on any mismatch; prints one OK line per rank."""
+
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (os.path.join(ROOT, "asdsl-framework_b200"), ROOT):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+TOL = 1e-3
+
+
+def _rel(a, b):
+    return float(np.max(np.abs(np.asarray(a, np.float64) - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def _same_on_all_ranks(t, world):
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous())
+    b0 = parts[0].cpu().numpy().view(np.uint32)
+    return all(np.array_equal(b0, q.cpu().numpy().view(np.uint32)) for q in parts[1:])
+
+
+def check_mlp(orc, world, rank, dev):
+    from asdsl_b200 import _lib
+    from asdsl_b200.quantization.synth import random_preq2
+    from asdsl_b200.shard import ShardedMLP, shard_range
+
+    H, I = 3072, 8192
+    rng = np.random.default_rng(1)
+    gm, gq = random_preq2(rng, 2 * I, H, scale_range=(0.004, 0.012), zero_range=(7.0, 8.0))
+    dm, dq = random_preq2(rng, H, I, scale_range=(0.004, 0.012), zero_range=(7.0, 8.0))
+    xs = [rng.standard_normal(H).astype(np.float32) for _ in range(4)]
+
+    def unsharded(x):
+        gu = orc.gemv_preq2_fused(gm, gq, x, 2 * I, H)
+        return orc.gemv_preq2_fused(dm, dq, orc.swiglu(gu[:I], gu[I:]), H, I)
+
+    def rank_ordered(x):
+        acc = None
+        for r in range(world):
+            m = ShardedMLP(gm, gq, dm, dq, H, I, local=orc, world=world, rank=r)
+            p = m.local_partial(x).numpy()
+            acc = p.copy() if acc is None else (acc + p).astype(np.float32)
+        return acc
+
+    for numerics in ("reference_exact", "fast"):
+        mlp = ShardedMLP(gm, gq, dm, dq, H, I, device=dev, numerics=numerics)
+        assert mlp.vx is not None and (mlp.a, mlp.b) == shard_range(I, world, rank, 32)
+        try:
+            for x in xs[:3]:
+                out = mlp.forward(torch.from_numpy(x).to(dev)).clone()
+                torch.cuda.synchronize(dev)
+                got = out.cpu().numpy()
+                assert _rel(got, unsharded(x)) < TOL, f"{numerics}: sharded MLP vs unsharded oracle"
+                if numerics == "reference_exact":
+                    want = rank_ordered(x)
+                    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), "exact: not bitwise"
+                assert _same_on_all_ranks(out, world), f"{numerics}: ranks differ"
+            xd = torch.from_numpy(xs[3]).to(dev)
+            for _ in range(200):
+                out = mlp.forward(xd)
+            torch.cuda.synchronize(dev)
+            assert _rel(out.cpu().numpy(), unsharded(xs[3])) < TOL, f"{numerics}: after 200 steps"
+        finally:
+            mlp.close()
+    mlp = ShardedMLP(gm, gq, dm, dq, H, I, device=dev, fused=False)
+    assert mlp.vx is None
+    out = mlp.forward(torch.from_numpy(xs[0]).to(dev))
+    assert _rel(out.cpu().numpy(), unsharded(xs[0])) < TOL, "all_reduce path"
+    assert _lib.device_status(clear=True) == 0
+
+
+def check_lm_head(orc, world, rank, dev):
+    from asdsl_b200 import _lib
+    from asdsl_b200.quantization.repack import repack_fp32_to_q4_128_blocks
+    from asdsl_b200.shard import ShardedLMHead
+
+    V, H = 32064, 3072
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((V, H), dtype=np.float32) * 0.02).astype(np.float32)
+    blocks = repack_fp32_to_q4_128_blocks(w, V, H)
+    head = ShardedLMHead(blocks, V, H, device=dev)
+    try:
+        assert head.xchg is not None
+        for step in range(3):
+            x = rng.standard_normal(H).astype(np.float32)
+            y = orc.gemv_q4_128_fused(blocks, x, V, H)
+            val, idx = head.argmax(torch.from_numpy(x).to(dev))
+            srt = np.sort(y)
+            if srt[-1] - srt[-2] > 4 * TOL * np.abs(y).max():
+                assert idx == orc.argmax(y), f"lm_head step {step}: {idx} vs {orc.argmax(y)}"
+            assert abs(val - y[idx]) <= TOL * np.abs(y).max()
+    finally:
+        head.close()
+    assert _lib.device_status(clear=True) == 0
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from asdsl_b200 import _lib
+        from oracle.oracle import Oracle
+
+        _lib.load()
+        orc = Oracle()
+        check_mlp(orc, world, rank, dev)
+        check_lm_head(orc, world, rank, dev)
+        dist.barrier()
+        print(f"rank {rank}/{world} OK", flush=True)
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
