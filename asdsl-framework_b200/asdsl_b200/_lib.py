@@ -75,6 +75,7 @@ _SIGS = {
     "asdsl_b200_vxchg_open": [_P, _P],
     "asdsl_b200_vxchg_destroy": [_P],
     "asdsl_b200_vxchg_set_stamps": [_P, _P, _I],
+    "asdsl_b200_engine_set_shard": [_P, _P, _P, _I, _I],
     "asdsl_b200_xchg_set_stamps": [_P, _P, _I],
     "asdsl_b200_allreduce_peer": [_P, _P, _P, _P, _I, _P],
     # device-resident decode engine

@@ -103,10 +103,13 @@ class UnifiedEngine:
 
     def __init__(self, config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
                  lm_head_preq2_meta=None, lm_head_preq2_quant=None, persistent: bool | None = None,
-                 numerics: str | None = None):
+                 numerics: str | None = None, shard: dict | None = None):
         lib = _lib.load()
         self._lib = lib
         self.config_ = config
+        # shard: {"vx": vector exchange, "xg": argmax exchange, "lm_rows", "lm_row_base"} of
+        # asdsl_b200.shard.sharded_engine_from_model (asdsl_b200_engine_set_shard)
+        self._shard = shard
         self._e = ctypes.c_void_p()
         _lib.check(lib.asdsl_b200_engine_create(ctypes.byref(config._c()), ctypes.byref(self._e)),
                    "UnifiedEngine")
@@ -119,6 +122,10 @@ class UnifiedEngine:
             _lib.check(lib.asdsl_b200_engine_set_numerics(self._e, 1 if numerics == "reference_exact" else 0),
                        "UnifiedEngine")
             self.numerics = numerics
+            if shard is not None:
+                _lib.check(lib.asdsl_b200_engine_set_shard(self._e, shard["vx"].ptr, shard["xg"].ptr,
+                                                           int(shard["lm_rows"]), int(shard["lm_row_base"])),
+                           "UnifiedEngine")
             self._load(config, token_embd, output_norm, output_proj, cos_table, sin_table, layers_dict,
                        lm_head_preq2_meta, lm_head_preq2_quant)
         except BaseException:
@@ -161,7 +168,7 @@ class UnifiedEngine:
         _lib.check(lib.asdsl_b200_engine_set_globals(e, _ptr(emb), int(emb_f16), _ptr(norm), _ptr(cos), _ptr(sin)),
                    "UnifiedEngine")
         if output_proj is not None:
-            if output_proj is token_embd:
+            if output_proj is token_embd and self._shard is None:
                 op, op_f16, op_n = emb, emb_f16, emb_n
             elif hasattr(output_proj, "is_cuda") and output_proj.is_cuda:
                 import torch
@@ -174,8 +181,9 @@ class UnifiedEngine:
                 if op.dtype not in (np.float16, np.float32):
                     op = op.astype(np.float32)
                 op_f16, op_n = op.dtype == np.float16, op.size
-            if op_n != cfg.vocab_size * cfg.hidden_size:
-                raise ValueError("output_proj must be (vocab_size, hidden_size)")
+            lm_rows = int(self._shard["lm_rows"]) if self._shard is not None else cfg.vocab_size
+            if op_n != lm_rows * cfg.hidden_size:
+                raise ValueError("output_proj must be (vocab_size, hidden_size) (a shard: (lm_rows, hidden_size))")
             _lib.check(lib.asdsl_b200_engine_set_output_proj(e, _ptr(op), int(op_f16)), "UnifiedEngine")
         if lm_meta is not None and lm_quant is not None:
             m = _host(lm_meta, np.uint8).ravel()
@@ -241,7 +249,8 @@ class UnifiedEngine:
     def forward_token_argmax(self, token: int, pos: int) -> int:
         """Single decode step; returns the argmax token id (:2499-2506)."""
         out = ctypes.c_int32(0)
-        _lib.check(self._lib.asdsl_b200_engine_forward_token(self._e, int(token), int(pos), _ptr(self._logits),
+        logits = None if self._shard is not None else _ptr(self._logits)
+        _lib.check(self._lib.asdsl_b200_engine_forward_token(self._e, int(token), int(pos), logits,
                                                              ctypes.byref(out)), "forward_token_argmax")
         return int(out.value)
 

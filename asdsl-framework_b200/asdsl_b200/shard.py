@@ -316,3 +316,105 @@ class ShardedMLP:
 
             dist.all_reduce(y, op=dist.ReduceOp.SUM)
         return y
+
+
+def _rows(a, ncols: int):
+    """a flat weight blob (numpy or torch, host or device) viewed as [rows, ncols] bytes"""
+    if hasattr(a, "reshape") and hasattr(a, "is_cuda"):
+        return a.reshape(-1, ncols)
+    return np.asarray(a, np.uint8).reshape(-1, ncols)
+
+
+def _cat(parts):
+    if hasattr(parts[0], "is_cuda"):
+        return torch.cat([p.contiguous() for p in parts]).contiguous()
+    return np.ascontiguousarray(np.concatenate(parts))
+
+
+def shard_mlp_blobs(L: dict, hidden: int, inter: int, a: int, b: int) -> dict:
+    """This rank's preq2 (gs 32) MLP blobs of one layer: gate rows [a, b) then up rows
+    [I + a, I + b) of gate_up_proj, and input columns [a, b) of down_proj (whole 32-column
+    groups, so the A8 quantization of h[a:b] is the slice of the global one).  Works on numpy
+    arrays and on torch tensors (host or device) alike; a, b multiples of 32."""
+    H, I = hidden, inter
+    ngH, ngI = H // 32, I // 32
+    gm = _rows(L["gate_up_proj_meta"], ngH * 4)
+    gq = _rows(L["gate_up_proj_quant"], ngH * 64)  # one row per 4-row band
+    dm = _rows(L["down_proj_meta"], ngI * 4)
+    dq = _rows(L["down_proj_quant"], ngI * 64)
+    g0, g1 = a // 32, b // 32
+    out = dict(L)
+    out["gate_up_proj_meta"] = _cat([gm[a:b], gm[I + a : I + b]]).reshape(-1)
+    out["gate_up_proj_quant"] = _cat([gq[a // 4 : b // 4], gq[(I + a) // 4 : (I + b) // 4]]).reshape(-1)
+    out["down_proj_meta"] = _cat([dm[:, g0 * 4 : g1 * 4]]).reshape(-1)
+    out["down_proj_quant"] = _cat([dq[:, g0 * 64 : g1 * 64]]).reshape(-1)
+    return out
+
+
+class ShardedEngine:
+    """The decode engine split over the GPUs of one box: one instance per rank (one process per
+    GPU, torch.distributed initialised), each holding its slice of every layer's MLP and of the
+    lm_head, the peer all-reduce of the down partials and the in-kernel argmax exchange
+    (asdsl_b200_engine_set_shard).  All ranks make the same calls (generate, forward_token_argmax,
+    reset_session) and get the same tokens."""
+
+    def __init__(self, engine, vx, xg, inter_range, lm_range):
+        self.engine, self.vx, self.xg = engine, vx, xg
+        self.inter_range, self.lm_range = inter_range, lm_range
+
+    def __getattr__(self, name):
+        if name in ("engine", "vx", "xg"):
+            raise AttributeError(name)
+        return getattr(self.engine, name)
+
+    def close(self):
+        if getattr(self, "engine", None) is not None:
+            self.engine.close()
+            self.engine = None
+        for x in ("vx", "xg"):
+            if getattr(self, x, None) is not None:
+                getattr(self, x).close()
+                setattr(self, x, None)
+
+
+def sharded_engine_from_model(model: dict, max_seq_len: int | None = None, device=None) -> ShardedEngine:
+    """engine_from_model split over the ranks of the default process group: rank r takes
+    intermediate rows [a_r, b_r) (128-aligned) of every layer's gate/up and down, and lm_head
+    rows [l_r, m_r) (4-aligned) quantized from its slice of the tied fp16 embedding by the engine,
+    as the single-GPU engine quantizes the whole.  Fast numerics, per-op chain."""
+    from asdsl_b200.kernels._native_unified import EngineConfig, UnifiedEngine
+
+    world, rank = _group()
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    c = model["config"]
+    H, I, V = c["hidden"], c["inter"], c["vocab"]
+    a, b = shard_range(I, world, rank, 128)
+    la, lb = shard_range(V, world, rank, 4)
+    layers = {i: shard_mlp_blobs(L, H, I, a, b) for i, L in enumerate(model["layers"])}
+    emb = model["embed_f16"]
+    lm_src = emb[la:lb] if hasattr(emb, "is_cuda") else np.ascontiguousarray(np.asarray(emb).reshape(V, H)[la:lb])
+    vx = _VecExchange(world, rank, H, dev)
+    xg = _Exchange(world, rank, dev)
+    cfg = EngineConfig()
+    cfg.num_layers = c["num_layers"]
+    cfg.hidden_size = H
+    cfg.num_heads = c["n_heads"]
+    cfg.num_kv_heads = c["n_kv_heads"]
+    cfg.head_dim = c["head_dim"]
+    cfg.intermediate_size = b - a
+    cfg.vocab_size = V
+    cfg.rms_norm_eps = c["eps"]
+    cfg.group_size = 32
+    cfg.lm_head_group_size = 32
+    cfg.max_seq_len = max_seq_len or c["max_seq"]
+    cfg.rotary_dim = c["rotary_dim"]
+    cfg.weight_format = 0
+    try:
+        eng = UnifiedEngine(cfg, emb, model["output_norm"], lm_src, model["cos"], model["sin"], layers,
+                            numerics="fast", persistent=False,
+                            shard={"vx": vx, "xg": xg, "lm_rows": lb - la, "lm_row_base": la})
+    except BaseException:
+        vx.close()
+        xg.close()
+        raise
+    return ShardedEngine(eng, vx, xg, (a, b), (la, lb))

@@ -584,12 +584,13 @@ int asdsl_b200_gemv_argmax_xchg(int fmt, const uint8_t* w0, const uint8_t* w1, c
 struct asdsl_b200_vxchg {
     int world = 1, rank = 0, device = 0, n_max = 0, stride = 0;
     unsigned long long* buf = nullptr;  // this rank's [2][world][stride] words
-    int* epoch = nullptr;               // [0] last completed step, [1] CTA arrival counter
+    // device control block: [0] last completed step, [1] CTA arrival counter, [2] stamp slot
+    // mask, [4..5] the stamp buffer's address (0 = off) -- read by every launch, so that the
+    // stamps reach steps replayed from CUDA graphs captured before they were turned on
+    int* epoch = nullptr;
     unsigned long long** peer_buf = nullptr;  // device array [world]: every rank's buffer, mapped here
     void* mapped_buf[64] = {};
     bool open = false;
-    unsigned long long* stamps = nullptr;  // optional %globaltimer stamps [n][4] (caller's memory)
-    int stamp_mask = 0;
 };
 
 namespace {
@@ -600,11 +601,11 @@ constexpr int kVxPerThread = 2;  // elements per thread: all their words are loa
 // grid: enough CTAs that every thread owns at most kVxPerThread elements of the vector
 inline int vx_grid(int n) { return std::max(1, (n + kVxThreads * kVxPerThread - 1) / (kVxThreads * kVxPerThread)); }
 
+// `out` may equal `add` (element i is read and written by the same thread)
 __global__ void __launch_bounds__(kVxThreads)
-    k_allreduce_peer(const float* __restrict__ part, float* __restrict__ out, const float* __restrict__ add, int n,
+    k_allreduce_peer(const float* __restrict__ part, float* out, const float* add, int n,
                      int stride, int world, int rank, unsigned long long* const* __restrict__ peer_buf,
-                     const unsigned long long* self_buf, int* epoch, unsigned int* status,
-                     unsigned long long* stamps, int stamp_mask) {
+                     const unsigned long long* self_buf, int* epoch, unsigned int* status) {
     // launched as a programmatic dependent of the GEMV that produced `part`: wait for it, then
     // let the next kernel launch (its weight streaming overlaps this exchange)
     grid_dependency_wait();
@@ -613,8 +614,9 @@ __global__ void __launch_bounds__(kVxThreads)
     const int par = e & 1;
     const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned int>(e)) << 32;
     // stamps (CTA 0): kernel start, own slice stored to every rank, slice gathered and summed, end
+    unsigned long long* stamps = reinterpret_cast<unsigned long long*>(*reinterpret_cast<const unsigned long long*>(epoch + 4));
     unsigned long long* stamp =
-        (stamps && blockIdx.x == 0 && threadIdx.x == 0) ? stamps + (e & stamp_mask) * 4 : nullptr;
+        (stamps && blockIdx.x == 0 && threadIdx.x == 0) ? stamps + (e & epoch[2]) * 4 : nullptr;
     if (stamp) stamp[0] = globaltimer_ns();
     // this thread's elements: i = blockIdx.x * kVxThreads * kVxPerThread + j * kVxThreads + threadIdx.x
     const int ib = blockIdx.x * kVxThreads * kVxPerThread + threadIdx.x;
@@ -700,11 +702,11 @@ int asdsl_b200_vxchg_create(int world, int rank, int n_max, asdsl_b200_vxchg** o
     };
     const size_t bbytes = 2ull * world * x->stride * sizeof(unsigned long long);
     if (cudaMalloc(reinterpret_cast<void**>(&x->buf), bbytes) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void**>(&x->epoch), 2 * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&x->epoch), 8 * sizeof(int)) != cudaSuccess ||
         cudaMalloc(reinterpret_cast<void**>(&x->peer_buf), world * sizeof(void*)) != cudaSuccess)
         return fail(set_error(asdsl::kEnomem, "vxchg_create: device allocation failed"));
     // step tags start at 1: a zeroed word never matches
-    if (cudaMemset(x->buf, 0, bbytes) != cudaSuccess || cudaMemset(x->epoch, 0, 2 * sizeof(int)) != cudaSuccess)
+    if (cudaMemset(x->buf, 0, bbytes) != cudaSuccess || cudaMemset(x->epoch, 0, 8 * sizeof(int)) != cudaSuccess)
         return fail(set_error(kEcuda, "vxchg_create: memset failed"));
     cudaIpcMemHandle_t h;
     const cudaError_t e = cudaIpcGetMemHandle(&h, x->buf);
@@ -754,8 +756,15 @@ int asdsl_b200_vxchg_set_stamps(asdsl_b200_vxchg* x, unsigned long long* stamps,
     if (!x) return set_error(kEinval, "vxchg_set_stamps: null exchange");
     if (stamps && (n_slots <= 0 || (n_slots & (n_slots - 1))))
         return set_error(kEinval, "vxchg_set_stamps: n_slots must be a power of two");
-    x->stamps = stamps;
-    x->stamp_mask = stamps ? n_slots - 1 : 0;
+    int ctl[6] = {0, 0, stamps ? n_slots - 1 : 0, 0, 0, 0};
+    const unsigned long long addr = reinterpret_cast<unsigned long long>(stamps);
+    std::memcpy(&ctl[4], &addr, sizeof(addr));
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != x->device) cudaSetDevice(x->device);
+    const cudaError_t e = cudaMemcpy(x->epoch + 2, ctl + 2, 4 * sizeof(int), cudaMemcpyHostToDevice);
+    if (prev >= 0 && prev != x->device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(kEcuda, std::string("vxchg_set_stamps: ") + cudaGetErrorString(e));
     return kOk;
 }
 
@@ -785,8 +794,7 @@ int asdsl_b200_allreduce_peer(asdsl_b200_vxchg* x, const float* part, float* out
     }
     ASDSL_CUDA(cudaLaunchKernelEx(&cfg, k_allreduce_peer, part, out, add, n, x->stride, x->world, x->rank,
                                   static_cast<unsigned long long* const*>(x->peer_buf),
-                                  static_cast<const unsigned long long*>(x->buf), x->epoch, st, x->stamps,
-                                  x->stamp_mask));
+                                  static_cast<const unsigned long long*>(x->buf), x->epoch, st));
     return kOk;
 }
 

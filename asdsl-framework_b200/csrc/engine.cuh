@@ -96,9 +96,21 @@ struct asdsl_b200_engine {
     // batched forward: activation blocks of batch_rows tokens (row t = token t), allocated on first use
     int batch_rows = 0;
     float *b_resid = nullptr, *b_qkv = nullptr, *b_att = nullptr, *b_gu = nullptr, *b_h = nullptr;
+    // sharded decode across the GPUs of one box (asdsl_b200_engine_set_shard): this rank holds
+    // intermediate_size gate/up rows and down columns of every layer and lm_rows lm_head rows
+    // from lm_row_base; the down partials are summed by the peer all-reduce, the argmax by the
+    // in-kernel exchange.  Null exchanges = single GPU.
+    asdsl_b200_vxchg* vx = nullptr;
+    asdsl_b200_xchg* xg = nullptr;
+    int lm_rows = 0;  // 0 = vocab_size
+    int lm_row_base = 0;
+    float* part = nullptr;  // [hidden] this rank's down partial
 };
 
 namespace {
+
+// rows of the lm_head this engine holds (all of them unless sharded)
+inline int eng_lm_rows(const asdsl_b200_engine* e) { return e->lm_rows > 0 ? e->lm_rows : e->cfg.vocab_size; }
 
 using asdsl::kEcuda;
 using asdsl::kEinval;
@@ -466,8 +478,15 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
                                   : eng_gemv<kProRmsA8, kEpiSilu>(L.p[kProjGateUp], ga, c.intermediate_size, s))
                 return rc;
         }
-        // resid += W_down . A8(h)
-        {
+        // resid += W_down . A8(h); sharded: this rank's partial, then the peer all-reduce
+        // (every rank's partial summed in rank order, plus the residual)
+        if (e->vx) {
+            GemvArgs ga = base_args(H, c.intermediate_size, 32);
+            ga.x = e->h;
+            ga.y = e->part;
+            if (int rc = eng_gemv<kProA8, kEpiStore>(L.p[kProjDown], ga, 0, s)) return rc;
+            if (int rc = asdsl_b200_allreduce_peer(e->vx, e->part, e->resid, e->resid, H, s)) return rc;
+        } else {
             GemvArgs ga = base_args(H, c.intermediate_size, 32);
             ga.x = e->h;
             ga.resid = e->resid;
@@ -477,7 +496,7 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
         }
     }
     if (with_lm) {
-        GemvArgs ga = base_args(c.vocab_size, H, 32);
+        GemvArgs ga = base_args(eng_lm_rows(e), H, 32);
         ga.x = e->resid;
         ga.norm_w = e->out_norm;
         ga.eps = c.rms_norm_eps;
@@ -487,7 +506,15 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
         ga.part_idx = reinterpret_cast<int*>(e->am_scratch + 256 + 4 * 1024);
         ga.out_val = e->am_val;
         ga.out_idx = e->am_idx;
-        ga.row_base = 0;
+        ga.row_base = e->lm_row_base;
+        if (e->xg) {
+            // the global first maximum: this rank's (max, index) word exchanged inside the kernel
+            ga.xchg_peers = e->xg->peer_table;
+            ga.xchg_self = e->xg->slots;
+            ga.xchg_epoch = e->xg->epoch;
+            ga.xchg_world = e->xg->world;
+            ga.xchg_rank = e->xg->rank;
+        }
         if (int rc = e->exact ? eng_gemv_x<kProRmsA8X, kEpiArgmax>(e, e->lm, ga, 0, s)
                               : eng_gemv<kProRmsA8, kEpiArgmax>(e->lm, ga, 0, s))
             return rc;
@@ -928,7 +955,7 @@ int asdsl_b200_engine_set_output_proj(asdsl_b200_engine* e, const void* output_p
     if (!output_proj) return set_error(kEinval, "engine_set_output_proj: null pointer");
     if (e->finalized) return set_error(kEinval, "engine_set_output_proj: engine already finalized");
     DeviceGuard dg(e->device);
-    const size_t sz = (is_f16 ? 2ull : 4ull) * e->cfg.vocab_size * e->cfg.hidden_size;
+    const size_t sz = (is_f16 ? 2ull : 4ull) * eng_lm_rows(e) * e->cfg.hidden_size;
     if (e->out_proj) eng_free(e, e->out_proj);
     e->out_proj = nullptr;
     if (int rc = eng_alloc(e, reinterpret_cast<uint8_t**>(&e->out_proj), sz)) return rc;
@@ -944,8 +971,9 @@ int asdsl_b200_engine_set_lm_head_preq2(asdsl_b200_engine* e, const uint8_t* met
     if (e->finalized) return set_error(kEinval, "engine_set_lm_head_preq2: engine already finalized");
     const asdsl_b200_engine_config& c = e->cfg;
     const long long ng = c.hidden_size / 32;
-    const size_t em = static_cast<size_t>(c.vocab_size) * ng * 4;
-    const size_t eq = static_cast<size_t>((c.vocab_size + 3) / 4) * ng * 64;
+    const int V = eng_lm_rows(e);
+    const size_t em = static_cast<size_t>(V) * ng * 4;
+    const size_t eq = static_cast<size_t>((V + 3) / 4) * ng * 64;
     // as the reference constructor: blobs of the wrong size (or a g128 lm_head) are ignored
     if (c.lm_head_group_size != 32 || meta_bytes != em || quant_bytes != eq) return kOk;
     DeviceGuard dg(e->device);
@@ -956,7 +984,7 @@ int asdsl_b200_engine_set_lm_head_preq2(asdsl_b200_engine* e, const uint8_t* met
     ASDSL_CUDA(cudaMemcpy(e->lm.w0, meta, em, cudaMemcpyDefault));
     ASDSL_CUDA(cudaMemcpy(e->lm.w1, quant, eq, cudaMemcpyDefault));
     e->lm.fmt = ASDSL_B200_FMT_PREQ2;
-    e->lm.rows = c.vocab_size;
+    e->lm.rows = V;
     e->lm.cols = c.hidden_size;
     e->lm_ready = true;
     return kOk;
@@ -1036,21 +1064,22 @@ int asdsl_b200_engine_finalize(asdsl_b200_engine* e) {
                                               std::to_string(w) + " has no weights");
     if (!e->lm_ready) {
         if (!e->out_proj) return set_error(kEinval, "engine_finalize: no lm_head source (output_proj or preq2 blobs)");
-        const long long nb = (c.vocab_size + 3) / 4;
+        const int V = eng_lm_rows(e);
+        const long long nb = (V + 3) / 4;
         const unsigned blocks = static_cast<unsigned>(sm_count() * 8);
         if (c.lm_head_group_size == 32) {
             const long long ng = c.hidden_size / 32;
-            if (int rc = eng_alloc(e, &e->lm.w0, static_cast<size_t>(c.vocab_size) * ng * 4)) return rc;
+            if (int rc = eng_alloc(e, &e->lm.w0, static_cast<size_t>(V) * ng * 4)) return rc;
             if (int rc = eng_alloc(e, &e->lm.w1, static_cast<size_t>(nb) * ng * 64)) return rc;
             ASDSL_CUDA(cudaMemsetAsync(e->lm.w1, 0, static_cast<size_t>(nb) * ng * 64, e->stream));
             if (e->out_proj_f16)
                 asdsl::k_lmhead_quant_preq2<uint16_t><<<blocks, 256, 0, e->stream>>>(
                     static_cast<const uint16_t*>(e->out_proj), reinterpret_cast<uint32_t*>(e->lm.w0),
-                    reinterpret_cast<uint4*>(e->lm.w1), c.vocab_size, c.hidden_size);
+                    reinterpret_cast<uint4*>(e->lm.w1), V, c.hidden_size);
             else
                 asdsl::k_lmhead_quant_preq2<float><<<blocks, 256, 0, e->stream>>>(
                     static_cast<const float*>(e->out_proj), reinterpret_cast<uint32_t*>(e->lm.w0),
-                    reinterpret_cast<uint4*>(e->lm.w1), c.vocab_size, c.hidden_size);
+                    reinterpret_cast<uint4*>(e->lm.w1), V, c.hidden_size);
             e->lm.fmt = ASDSL_B200_FMT_PREQ2;
         } else {
             const long long ng = c.hidden_size / 128;
@@ -1061,19 +1090,21 @@ int asdsl_b200_engine_finalize(asdsl_b200_engine* e) {
             if (e->out_proj_f16)
                 asdsl::k_lmhead_quant_q128b<uint16_t><<<blocks, 256, 0, e->stream>>>(
                     static_cast<const uint16_t*>(e->out_proj), reinterpret_cast<uint4*>(e->lm.w0),
-                    reinterpret_cast<uint16_t*>(e->lm.w1), c.vocab_size, c.hidden_size);
+                    reinterpret_cast<uint16_t*>(e->lm.w1), V, c.hidden_size);
             else
                 asdsl::k_lmhead_quant_q128b<float><<<blocks, 256, 0, e->stream>>>(
                     static_cast<const float*>(e->out_proj), reinterpret_cast<uint4*>(e->lm.w0),
-                    reinterpret_cast<uint16_t*>(e->lm.w1), c.vocab_size, c.hidden_size);
+                    reinterpret_cast<uint16_t*>(e->lm.w1), V, c.hidden_size);
             e->lm.fmt = ASDSL_B200_FMT_Q4_128_BANDED;
         }
         ASDSL_CUDA(cudaGetLastError());
-        e->lm.rows = c.vocab_size;
+        e->lm.rows = V;
         e->lm.cols = c.hidden_size;
         ASDSL_CUDA(cudaStreamSynchronize(e->stream));
         e->lm_ready = true;
     }
+    if (e->vx && (e->exact || e->persistent))
+        return set_error(kEinval, "engine_finalize: a sharded engine runs the fast per-op chain");
     if (e->exact) {
         // the reference-exact mode covers the C0 path: preq2 gs 32 everywhere (lm_head included)
         for (int l = 0; l < c.num_layers; ++l)
@@ -1155,6 +1186,8 @@ int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, fl
     if (token < 0 || token >= e->cfg.vocab_size)
         return set_error(kErange, "forward_token: token_id out of vocab range");
     if (pos < 0 || pos >= e->cfg.max_seq_len) return set_error(kErange, "forward_token: pos out of kv-cache range");
+    if (logits && e->vx)
+        return set_error(kEinval, "forward_token: a sharded engine returns the argmax (its logits are split over ranks)");
     DeviceGuard dg(e->device);
     if (int rc = eng_set_pos(e, pos, token)) return rc;
     const bool lm = logits || argmax;
@@ -1175,6 +1208,7 @@ int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, fl
 int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
                                      float* out_logits) {
     ENG_READY(e);
+    if (e->vx) return set_error(kEinval, "forward_verify: not available on a sharded engine");
     if (n <= 0) return kOk;
     if (!tokens || !out_logits) return set_error(kEinval, "forward_verify: null pointer");
     const asdsl_b200_engine_config& c = e->cfg;
@@ -1217,6 +1251,7 @@ int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens
 int asdsl_b200_engine_forward_batch(asdsl_b200_engine* e, const int32_t* tokens, int n, int start_pos,
                                     float* out_logits, int all_logits) {
     ENG_READY(e);
+    if (e->vx) return set_error(kEinval, "forward_batch: not available on a sharded engine");
     if (n <= 0) return kOk;
     if (!tokens) return set_error(kEinval, "forward_batch: null pointer");
     const asdsl_b200_engine_config& c = e->cfg;
@@ -1275,7 +1310,7 @@ int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int 
     // prompt tokens before the last one: batched passes (bit-identical to the per-op chain's
     // prefill graph); the persistent-kernel and reference-exact modes replay their prefill graph
     const int n_pre = n_prompt - 1;
-    if (n_pre > 0 && !e->persistent && !e->exact) {
+    if (n_pre > 0 && !e->persistent && !e->exact && !e->vx) {
         if (int rc = eng_batch_alloc(e)) return rc;
         for (int t0 = 0; t0 < n_pre; t0 += e->batch_rows) {
             const int T = std::min(e->batch_rows, n_pre - t0);
@@ -1365,6 +1400,32 @@ int asdsl_b200_engine_profile_step(asdsl_b200_engine* e, int decode, unsigned lo
     return rc;
 }
 
+int asdsl_b200_engine_set_shard(asdsl_b200_engine* e, asdsl_b200_vxchg* vx, asdsl_b200_xchg* xg, int lm_rows,
+                                int lm_row_base) {
+    ENG_CHECK(e);
+    if (e->finalized) return set_error(kEinval, "engine_set_shard: engine already finalized");
+    if (e->lm_ready || e->out_proj) return set_error(kEinval, "engine_set_shard: call before the lm_head is set");
+    if (!vx || !xg || !vx->open || !xg->open) return set_error(kEinval, "engine_set_shard: exchanges not opened");
+    if (vx->world != xg->world || vx->rank != xg->rank)
+        return set_error(kEinval, "engine_set_shard: the two exchanges disagree on rank / world");
+    if (vx->device != e->device || xg->device != e->device)
+        return set_error(kEinval, "engine_set_shard: the exchanges live on another device");
+    const asdsl_b200_engine_config& c = e->cfg;
+    if (vx->n_max < c.hidden_size) return set_error(kEinval, "engine_set_shard: vector exchange shorter than hidden_size");
+    if (lm_rows <= 0 || lm_row_base < 0 || static_cast<long long>(lm_row_base) + lm_rows > c.vocab_size)
+        return set_error(kErange, "engine_set_shard: lm_head rows outside the vocabulary");
+    if (static_cast<long long>(lm_row_base) + lm_rows > (1ll << 24))
+        return set_error(kErange, "engine_set_shard: global row indices must stay below 2^24");
+    DeviceGuard dg(e->device);
+    if (!e->part)
+        if (int rc = eng_alloc(e, &e->part, 4ull * c.hidden_size)) return rc;
+    e->vx = vx;
+    e->xg = xg;
+    e->lm_rows = lm_rows;
+    e->lm_row_base = lm_row_base;
+    return kOk;
+}
+
 int asdsl_b200_engine_set_numerics(asdsl_b200_engine* e, int mode) {
     ENG_CHECK(e);
     if (e->finalized) return set_error(kEinval, "engine_set_numerics: engine already finalized");
@@ -1452,6 +1513,7 @@ int asdsl_b200_engine_export_lm_head(asdsl_b200_engine* e, int* fmt, uint8_t* w0
     if (!fmt) return set_error(kEinval, "export_lm_head: null pointer");
     if (e->lm.xlpt)
         return set_error(kEinval, "export_lm_head: the reference-exact mode keeps the lm_head in its own layout");
+    if (e->vx) return set_error(kEinval, "export_lm_head: a sharded engine holds only its rows of the lm_head");
     const asdsl_b200_engine_config& c = e->cfg;
     const long long nb = (c.vocab_size + 3) / 4;
     size_t b0, b1;

@@ -395,6 +395,7 @@ def decode_bench(model, numerics: str = "fast", ref: dict | None = None, steps: 
         assert _lib.device_status(clear=True) == 0
     finally:
         eng.close()
+    decode_bench.last_tokens = toks
     bytes_per_token = weight_bytes + lm_bytes
     peak, peak_kind = _peaks()
     achieved = bytes_per_token * tok_s / world / 1e9  # per GPU
@@ -429,6 +430,94 @@ def decode_bench(model, numerics: str = "fast", ref: dict | None = None, steps: 
                              "bit-identical to serial forward_token (checked here for the verify rows)"}
                     if pre else None),
     }
+
+
+DECODE_SHARDED_METRIC = "Q4 decode tokens/sec at batch 1, MLP and lm_head sharded over the GPUs (Phi-4-mini shape)"
+
+
+def decode_sharded_bench(model, world: int, rank: int, steps: int = 128, prompt_token: int = 1,
+                         single_gpu_tokens=None) -> dict:
+    """Strong scaling of one batch-1 sequence: every rank holds 1/N of every layer's MLP
+    (gate/up rows, down columns) and of the lm_head, qkv / o / attention replicated; per layer the
+    down partials are summed by the peer all-reduce kernel (with the residual add), per token the
+    lm_head argmax is exchanged inside its kernel (asdsl.shard.sharded_engine_from_model).  Timed
+    as decode_bench times the engine (graph replays of the decode step on the engine stream, max
+    over ranks); the %globaltimer stamps of the all-reduce give its share."""
+    import numpy as np
+    import torch
+
+    from asdsl_b200 import _lib
+    from asdsl_b200.shard import sharded_engine_from_model
+
+    c = model["config"]
+    H, I, V, L = c["hidden"], c["inter"], c["vocab"], c["num_layers"]
+    eng = sharded_engine_from_model(model)
+    try:
+        a, b = eng.inter_range
+        la, lb = eng.lm_range
+        stream = torch.cuda.ExternalStream(eng.stream_ptr())
+        stamps = torch.zeros((1024, 4), dtype=torch.int64, device="cuda")
+        for _ in range(2):
+            eng.set_position(0, prompt_token)
+            eng.replay(8)
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        eng.vx.set_stamps(stamps)  # a device-side setting: reaches the captured decode graph
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        eng.set_position(0, prompt_token)
+        e0.record(stream)
+        eng.replay(steps)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        eng.vx.set_stamps(None)
+        eng.reset_session()
+        if world > 1:
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        toks = eng.generate([prompt_token], steps)
+        f1.record(stream)
+        f1.synchronize()
+        e2e_ms = f0.elapsed_time(f1)
+        if world > 1:
+            t = torch.tensor([ms, e2e_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, e2e_ms = (float(v) for v in t.tolist())
+        assert _lib.device_status(clear=True) == 0
+        if world > 1:
+            dist.barrier()
+    finally:
+        eng.close()
+    same = None
+    if single_gpu_tokens is not None:
+        n = min(len(toks), len(single_gpu_tokens))
+        same = next((i for i in range(n) if toks[i] != single_gpu_tokens[i]), n) - 1
+    ngH, ngI, ng = H // 32, I // 32, H // 32
+    qkv_rows = (c["n_heads"] + 2 * c["n_kv_heads"]) * c["head_dim"]
+    pq = lambda rows, ngr: rows * ngr * 4 + ((rows + 3) // 4) * ngr * 64  # noqa: E731  preq2 bytes
+    per_rank = L * (pq(qkv_rows, ngH) + pq(H, c["n_heads"] * c["head_dim"] // 32) + pq(2 * (b - a), ngH)
+                    + pq(H, (b - a) // 32)) + pq(lb - la, ng)
+    peak, peak_kind = _peaks()
+    tok_s = steps / (ms * 1e-3)
+    achieved = per_rank * tok_s / 1e9
+    return {"metric": DECODE_SHARDED_METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "steps": steps,
+            "ms_per_token": round(ms / steps, 4), "n_gpus": world, "scaling": "strong", "numerics": "fast",
+            "parallelism": (f"MLP rows/columns and lm_head rows split over {world} GPUs, qkv/o/attention "
+                            "replicated; peer all-reduce per layer, in-kernel argmax exchange per token"),
+            "allreduce_stamps_us_per_rank": stamp_summary(stamps, ("push", "gather_sum", "finish"), world),
+            "collectives_per_token": {"allreduce_peer_12KB": L, "argmax_exchange_8B": 1},
+            "roofline": {"bound": "hbm", "bytes_per_token_per_gpu": per_rank, "achieved_per_gpu": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4)},
+            "e2e": {"value": round(steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4, "ms_total": round(e2e_ms, 3)},
+            "greedy_tokens_equal_to_single_gpu_fast": same,
+            "gpu_launches": steps * (3 + 6 * L),
+            "config": {"workload": "c3_phi4_mini_decode_sharded", "seed": 3, "layers": L, "prompt": [prompt_token],
+                       "inter_rows_per_rank": b - a, "lm_rows_per_rank": lb - la}}
 
 
 # ---------------------------------------------------------------------------
@@ -998,6 +1087,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--no-lm-head", action="store_true", help="skip the config-2 sharded lm_head measurement")
     ap.add_argument("--no-mlp", action="store_true", help="skip the sharded MLP measurement")
+    ap.add_argument("--no-sharded-decode", action="store_true", help="skip the sharded decode measurement")
     ap.add_argument("--no-c0", action="store_true", help="skip the config-0 single-GEMV measurement")
     ap.add_argument("--only-c0", action="store_true", help="run only the config-0 section (profiling)")
     ap.add_argument("--c4", action=argparse.BooleanOptionalAction, default=True,
@@ -1238,7 +1328,7 @@ def main():
 
     c0 = None if args.no_c0 else c0_bench(world, rank)
     c4 = c4_bench(rank) if (args.c4 and world == 1) else None
-    decode = decode_fast = None
+    decode = decode_fast = decode_sharded = None
     if not args.no_decode:
         from asdsl_b200.inference.synthetic import PHI4_MINI, build_model_device
 
@@ -1251,6 +1341,8 @@ def main():
         # reference's own engine; the fast mode's figure and its distance to the reference beside it
         decode = decode_bench(dmodel, "reference_exact", ref, args.decode_steps, world=world)
         decode_fast = decode_bench(dmodel, "fast", ref, args.decode_steps, world=world)
+        decode_sharded = None if args.no_sharded_decode else decode_sharded_bench(
+            dmodel, world, rank, args.decode_steps, single_gpu_tokens=getattr(decode_bench, "last_tokens", None))
         del dmodel
     lm_sharded = None if args.no_lm_head else lm_head_bench(world, rank)
     mlp_sharded = None if args.no_mlp else mlp_sharded_bench(world, rank)
@@ -1289,6 +1381,7 @@ def main():
             "c4_multi": c4,
             "decode": decode,
             "decode_fast": decode_fast,
+            "decode_sharded": decode_sharded,
             "lm_head_sharded": lm_sharded,
             "mlp_sharded": mlp_sharded,
         }

@@ -251,7 +251,9 @@ int asdsl_b200_vxchg_open(asdsl_b200_vxchg* vxchg, const void* handles);
 int asdsl_b200_vxchg_destroy(asdsl_b200_vxchg* vxchg);
 /* Optional instrumentation as asdsl_b200_xchg_set_stamps, per asdsl_b200_allreduce_peer step
  * (CTA 0): 0 kernel start (previous kernel complete), 1 own partial stored to its peer, 2 CTA 0's
- * slice gathered from every rank and summed, 3 the step counter advanced. */
+ * slice gathered from every rank and summed, 3 the step counter advanced.  The setting lives in
+ * device memory, so it also reaches steps replayed from CUDA graphs captured earlier; call it
+ * while no step of this exchange runs. */
 int asdsl_b200_vxchg_set_stamps(asdsl_b200_vxchg* vxchg, unsigned long long* stamps, int n_slots);
 int asdsl_b200_allreduce_peer(asdsl_b200_vxchg* vxchg, const float* part, float* out, const float* add, int n,
                               void* stream);
@@ -392,6 +394,22 @@ int asdsl_b200_engine_stream(asdsl_b200_engine* e, void** stream);
  * launch); 1 runs each step as one cooperative kernel over a program of ops with grid barriers
  * between them.  The environment variable ASDSL_B200_DECODE_KERNEL=persistent selects 1 at
  * create. */
+/* Sharded decode across the GPUs of one box (one process and one engine per GPU): call after
+ * asdsl_b200_engine_create and before the lm_head and projections are set.  The engine then
+ * holds this rank's slice of every layer's MLP -- config.intermediate_size gate rows and the
+ * matching up rows (gate_up = local gate rows then local up rows) and down_proj's matching input
+ * columns -- and rows [lm_row_base, lm_row_base + lm_rows) of the lm_head (set_output_proj /
+ * set_lm_head_preq2 take those rows only).  Each layer's down partial is summed over the ranks
+ * by asdsl_b200_allreduce_peer (with the residual add); the lm_head argmax is exchanged inside
+ * its kernel (asdsl_b200_gemv_argmax_xchg), so every rank produces the same tokens.  qkv, o and
+ * attention are replicated.  Fast numerics and the per-op chain only; forward_token returns the
+ * argmax (no logits), forward_batch / forward_verify / export_lm_head are not available.
+ * finalize, forward_token and generate run exchange steps: every rank makes the same calls.
+ * Replaces the reference engine's MLP and lm_head (asdsl/kernels/native/unified_engine.cpp:
+ * 1532-1598, :1628-1662) split over GPUs. */
+int asdsl_b200_engine_set_shard(asdsl_b200_engine* engine, asdsl_b200_vxchg* vxchg, asdsl_b200_xchg* xchg,
+                                int lm_rows, int lm_row_base);
+
 /* Numerics of the decode step, set before finalize (no reference switch: the reference has one
  * numerics, its compiled code's).  ASDSL_B200_NUMERICS_FAST: the streaming kernels' own fp32
  * summation order (every GEMV within 1e-3 of the reference; the default).

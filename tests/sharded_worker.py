@@ -10,6 +10,8 @@ Checks, on every rank, against the CPU oracle (oracle/asdsl_oracle.c):
   torch.distributed all_reduce path (fused=False) and 200 back-to-back steps (the buffers
   alternate by step parity) with the last step checked.
 * ShardedLMHead with the in-kernel argmax exchange: the global index equals the oracle's argmax.
+* The sharded decode engine (MLP and lm_head split, peer all-reduce per layer, argmax exchange)
+  against the single-GPU engine along a teacher-forced trajectory.
 Exits non-zero (AssertionError) on any mismatch; prints one OK line per rank."""
 
 import datetime
@@ -114,6 +116,57 @@ def check_lm_head(orc, world, rank, dev):
     assert _lib.device_status(clear=True) == 0
 
 
+def check_engine(world, rank, dev):
+    """The sharded decode engine on SMALL (4 layers, GQA 6/2, MLP 2048, vocab 8192): teacher-forced
+    along the single-GPU engine's greedy trajectory, the ranks' lm_head rows gathered into full
+    logits within 1e-3 of the single-GPU engine's (the only difference is the order of the
+    down-partial sum, whose last-bit changes can flip an A8 rounding further on: 5e-2 then, as
+    the engine tests' cascade bar), the exchanged argmax equal to the full logits' first maximum
+    on every rank; then generate() on every rank gives the same tokens."""
+    from asdsl_b200 import _lib
+    from asdsl_b200.inference.synthetic import SMALL, build_model
+    from asdsl_b200.kernels._native_unified import engine_from_model
+    from asdsl_b200.shard import sharded_engine_from_model
+
+    model = build_model(SMALL, seed=11, norms_one=False)
+    ref = engine_from_model(model)
+    steps = 32
+    toks = [3]
+    want = []
+    for pos in range(steps):
+        want.append(ref.forward_token(toks[-1], pos).copy())
+        toks.append(int(np.argmax(want[-1])))
+    ref.close()
+    eng = sharded_engine_from_model(model, device=dev)
+    try:
+        la, lb = eng.lm_range
+        for pos in range(steps):
+            t = eng.forward_token_argmax(toks[pos], pos)
+            local = torch.from_numpy(eng.read_buffer("logits")[: lb - la].copy()).to(dev)
+            pad = torch.zeros(8200 // world + 8, dtype=torch.float32, device=dev)
+            pad[: lb - la] = local
+            parts = [torch.empty_like(pad) for _ in range(world)]
+            dist.all_gather(parts, pad)
+            counts = [torch.tensor([lb - la], device=dev) for _ in range(world)]
+            dist.all_gather(counts, torch.tensor([lb - la], device=dev))
+            full = torch.cat([q[: int(k.item())] for q, k in zip(parts, counts)]).cpu().numpy()
+            e = _rel(full, want[pos])
+            assert e < 5e-2, f"engine step {pos}: logits rel err {e}"
+            if pos == 0:
+                assert e < TOL, f"engine step 0: logits rel err {e}"
+            assert t == int(np.argmax(full)), f"engine step {pos}: exchanged argmax {t} vs {int(np.argmax(full))}"
+            srt = np.sort(want[pos])
+            if srt[-1] - srt[-2] > 8e-2 * np.abs(want[pos]).max():
+                assert t == toks[pos + 1], f"engine step {pos}: token {t} vs single-GPU {toks[pos + 1]}"
+        eng.reset_session()
+        got = torch.tensor(eng.generate([3, 17, 99], 24), device=dev)
+        assert _same_on_all_ranks(got.float(), world), "generate: ranks disagree"
+        assert got.numel() == 3 + 24
+    finally:
+        eng.close()
+    assert _lib.device_status(clear=True) == 0
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -129,6 +182,7 @@ def main():
         orc = Oracle()
         check_mlp(orc, world, rank, dev)
         check_lm_head(orc, world, rank, dev)
+        check_engine(world, rank, dev)
         dist.barrier()
         print(f"rank {rank}/{world} OK", flush=True)
     finally:
