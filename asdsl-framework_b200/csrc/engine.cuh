@@ -105,6 +105,11 @@ struct asdsl_b200_engine {
     int lm_rows = 0;  // 0 = vocab_size
     int lm_row_base = 0;
     float* part = nullptr;  // [hidden] this rank's down partial
+    // split-KV decode attention (max_seq_len > one chunk): partials [heads][chunks][stride] and
+    // per-head arrival counters
+    float* attn_part = nullptr;
+    unsigned int* attn_cnt = nullptr;
+    int attn_chunks = 0;
 };
 
 namespace {
@@ -450,6 +455,15 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
                 if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_exact), dim3(c.num_heads),
                                           dim3(asdsl::kAttnXThreads), args, s, true,
                                           asdsl::attn_x_layout(c.max_seq_len).total))
+                    return rc;
+            } else if (e->attn_chunks > 1) {
+                // long cache: heads x position chunks, partials merged in chunk order
+                aa.part = e->attn_part;
+                aa.cnt = e->attn_cnt;
+                void* args[] = {&aa};
+                if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_split),
+                                          dim3(c.num_heads, e->attn_chunks), dim3(asdsl::kAttnWarps * 32), args, s,
+                                          true))
                     return rc;
             } else {
                 void* args[] = {&aa};
@@ -897,6 +911,14 @@ int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_eng
     for (auto& L : e->layers)
         if ((rc = eng_alloc(e, &L.rms_att, 4ull * c.hidden_size)) || (rc = eng_alloc(e, &L.rms_ffn, 4ull * c.hidden_size)))
             return fail(rc);
+    e->attn_chunks = (c.max_seq_len + asdsl::kAttnChunk - 1) / asdsl::kAttnChunk;
+    if (e->attn_chunks > 1) {
+        if ((rc = eng_alloc(e, &e->attn_part, 4ull * c.num_heads * e->attn_chunks * asdsl::kAttnPartStride)) ||
+            (rc = eng_alloc(e, &e->attn_cnt, 4ull * c.num_heads)))
+            return fail(rc);
+        if (cudaMemsetAsync(e->attn_cnt, 0, 4ull * c.num_heads, e->stream) != cudaSuccess)
+            return fail(set_error(kEcuda, "engine_create: memset failed"));
+    }
     if (cudaHostAlloc(reinterpret_cast<void**>(&e->h_stage), 16 * sizeof(int), cudaHostAllocDefault) != cudaSuccess)
         return fail(set_error(kEcuda, "engine_create: cannot allocate pinned staging"));
     if (cudaMemsetAsync(e->am_scratch, 0, asdsl_b200_argmax_scratch_bytes(), e->stream) != cudaSuccess ||

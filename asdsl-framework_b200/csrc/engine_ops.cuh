@@ -61,6 +61,8 @@ constexpr int kAttnWarps = 8;
 constexpr int kAttnGroups = kAttnWarps * 4;  // 8-lane position groups per CTA
 constexpr int kAttnHeadDim = 128;
 constexpr int kAttnPrefetch = 4;  // position blocks of cached K/V loaded before the dependency wait
+constexpr int kAttnChunk = 256;   // positions per CTA of the split-KV decode attention
+constexpr int kAttnPartStride = kAttnHeadDim + 4;  // floats per (head, chunk) partial: M, L, pad, acc[128]
 
 // set_kv_cache's code multiplier as the reference's compiled code computes it
 // (unified_engine.cpp:885-887): GCC folds 1/(absmax * fl(1/127)) into 127/absmax; a block with
@@ -80,6 +82,10 @@ struct AttnArgs {
     const float* sin_t;
     const DecodeState* st;
     int n_heads, n_kv, rot, max_seq;
+    // split-KV decode attention (k_attention_split): per (head, chunk) partials and per-head
+    // arrival counters (re-armed by the last CTA of each head)
+    float* part;
+    unsigned int* cnt;
 };
 
 // shared memory of one attention head
@@ -91,12 +97,48 @@ struct AttnSmem {
     float m[kAttnGroups], l[kAttnGroups];
     float sc[kAttnGroups];  // merge: exp(m[k] - M) of each live group, 0 for an empty one
     float num[kAttnGroups][kAttnHeadDim];
+    float M;                // split-KV: the CTA's maximum over its live groups
+    int last;               // split-KV: this CTA merges the head's chunks
 };
 
 // no-op wait: the caller already ordered the head after the kernel that wrote qkv
 struct NoWait {
     __device__ __forceinline__ void operator()() const {}
 };
+
+// Split-KV: the head's last CTA to arrive merges the chunks' partials in chunk order:
+// M = max over live chunks, L = sum l_c e^(M_c - M), out = (sum acc_c e^(M_c - M)) / L.
+template <typename Sync>
+__device__ __forceinline__ void attention_merge_chunks(const AttnArgs& a, int h, AttnSmem& S, int tid, Sync sync) {
+    constexpr int hd = kAttnHeadDim;
+    const int nch = gridDim.y;
+    __threadfence();
+    sync();
+    if (tid == 0) {
+        const unsigned int prev = atomicAdd(a.cnt + h, 1u);
+        S.last = prev == static_cast<unsigned int>(nch) - 1u;
+    }
+    sync();
+    if (!S.last) return;
+    __threadfence();
+    const float* base = a.part + static_cast<long long>(h) * nch * kAttnPartStride;
+    if (tid < hd) {
+        float M = -INFINITY;
+        for (int c = 0; c < nch; ++c)
+            if (__ldcg(base + c * kAttnPartStride + 1) > 0.0f) M = fmaxf(M, __ldcg(base + c * kAttnPartStride));
+        float L = 0.0f, acc = 0.0f;
+        for (int c = 0; c < nch; ++c) {
+            const float lc = __ldcg(base + c * kAttnPartStride + 1);
+            if (lc > 0.0f) {
+                const float sc = expf(__ldcg(base + c * kAttnPartStride) - M);
+                L = __fmaf_rn(lc, sc, L);
+                acc = __fmaf_rn(__ldcg(base + c * kAttnPartStride + 4 + tid), sc, acc);
+            }
+        }
+        a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, L));
+    }
+    if (tid == 0) a.cnt[h] = 0u;  // re-armed for the next launch
+}
 
 // One head of the decode attention, run by kAttnWarps warps (thread ids 0..255).  `sync` is
 // the barrier of those warps; kCoherent reads qkv through L2 (it was written by other CTAs of
@@ -110,9 +152,15 @@ struct NoWait {
 // other tokens) k_kv_write_rows already stored; every position, its own included, is read from
 // the cache.  A cached position dequantizes to exactly the values the single-token head keeps in
 // shared memory for its own position, so both give bit-identical outputs.
-template <bool kCoherent, typename Sync, typename Wait = NoWait, bool kBatch = false>
+//
+// kSplit: split-KV decode -- this CTA covers positions [chunk * kAttnChunk, (chunk + 1) *
+// kAttnChunk) of the head (the chunk that holds `pos` also quantizes and stores this position's
+// K/V); it leaves its (max, denominator, numerator) partial in a.part, and the head's last CTA to
+// arrive merges the chunks in chunk order.  A context inside the first chunk gives the unsplit
+// head's bits.
+template <bool kCoherent, typename Sync, typename Wait = NoWait, bool kBatch = false, bool kSplit = false>
 __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSmem& S, int tid, Sync sync,
-                                               Wait wait = Wait(), int batch_pos = -1) {
+                                               Wait wait = Wait(), int batch_pos = -1, int chunk = 0) {
     constexpr int hd = kAttnHeadDim;
     const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
     const int g = h / groups;
@@ -122,6 +170,10 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
         wait();
         return;
     }
+    // positions [c0, c1) of this CTA (all of them without kSplit)
+    const int c0 = kSplit ? chunk * kAttnChunk : 0;
+    const int c1 = kSplit ? min(pos + 1, c0 + kAttnChunk) : pos + 1;
+    const bool owns_pos = !kSplit || (c0 <= pos && pos < c0 + kAttnChunk);
     const int lane = tid & 31, warp = tid >> 5;
     const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
     auto ldq = [&](const float* p) -> float {
@@ -143,10 +195,10 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
     float pks[kAttnPrefetch], pvs[kAttnPrefetch];
 #pragma unroll
     for (int i = 0; i < kAttnPrefetch; ++i) {
-        const int p = i * kAttnGroups + grp;
+        const int p = c0 + i * kAttnGroups + grp;
         pk[i] = pv[i] = make_uint4(0u, 0u, 0u, 0u);
         pks[i] = pvs[i] = 0.f;
-        if (kBatch ? p <= pos : p < pos) {
+        if ((kBatch ? p <= pos : p < pos) && p < c1) {
             const long long rb = (static_cast<long long>(p) * a.n_kv + g) * hd + l8 * 16;
             const long long sb = (static_cast<long long>(p) * a.n_kv + g) * 2 + (l8 >> 2);
             pk[i] = *reinterpret_cast<const uint4*>(a.kq + rb);
@@ -200,7 +252,7 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
             qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
             S.k[tid] = __fmul_rn(static_cast<float>(qk), ksc);
             S.v[tid] = __fmul_rn(static_cast<float>(qv), vsc);
-            if (h % groups == 0) {
+            if (h % groups == 0 && owns_pos) {
                 const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
                 a.kq[kb + tid] = static_cast<int8_t>(qk);
                 a.vq[kb + tid] = static_cast<int8_t>(qv);
@@ -223,8 +275,8 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
     float num[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) num[i] = 0.0f;
-    const int npos = pos + 1;
-    for (int p0 = 0; p0 < npos; p0 += kAttnGroups) {
+    const int npos = c1;
+    for (int p0 = c0; p0 < npos; p0 += kAttnGroups) {
         const int p = p0 + grp;
         const bool live = p < npos;  // uniform within the 8-lane group
         float dot = 0.0f;
@@ -241,7 +293,7 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
             } else {
                 uint4 kw = make_uint4(0u, 0u, 0u, 0u), vw = kw;
                 float ksc = 0.f, vsc = 0.f;
-                const int blk = p0 / kAttnGroups;
+                const int blk = (p0 - c0) / kAttnGroups;
 #pragma unroll
                 for (int i = 0; i < kAttnPrefetch; ++i)
                     if (blk == i) {
@@ -299,6 +351,7 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         S.sc[lane] = live_k ? expf(S.m[lane] - M) : 0.0f;
+        if (lane == 0) S.M = M;
     }
     sync();
     if (tid < hd) {
@@ -309,8 +362,18 @@ __device__ __forceinline__ void attention_head(const AttnArgs& a, int h, AttnSme
                 acc = __fmaf_rn(S.num[k][tid], S.sc[k], acc);
             }
         }
-        a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, L));
+        if constexpr (!kSplit) {
+            a.out[h * hd + tid] = __fmul_rn(acc, __fdiv_rn(1.0f, L));
+        } else {
+            float* pp = a.part + (static_cast<long long>(h) * gridDim.y + chunk) * kAttnPartStride;
+            pp[4 + tid] = acc;
+            if (tid == 0) {
+                pp[0] = S.M;
+                pp[1] = L;  // 0: no live position in this chunk
+            }
+        }
     }
+    if constexpr (kSplit) attention_merge_chunks(a, h, S, tid, sync);
 }
 
 struct BlockSync {
@@ -328,6 +391,26 @@ struct GridWait {
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnArgs a) {
     __shared__ AttnSmem S;
     attention_head<false>(a, blockIdx.x, S, threadIdx.x, BlockSync(), GridWait());
+}
+
+// split-KV decode attention: grid (n_heads, ceil(max_seq / kAttnChunk)); CTA (h, c) covers
+// positions [c * kAttnChunk, (c + 1) * kAttnChunk) of head h, chunks past the position only
+// arrive at the head's counter.  Replaces the serial position loop of one CTA per head at long
+// contexts (unified_engine.cpp:922-1027, whose result this merge reproduces within the fp32
+// reassociation of the chunk sums).
+__global__ void __launch_bounds__(kAttnWarps * 32) k_attention_split(AttnArgs a) {
+    __shared__ AttnSmem S;
+    const int h = blockIdx.x, c = blockIdx.y;
+    const int pos = a.st->pos;
+    if (pos >= 0 && pos < a.max_seq && c * kAttnChunk > pos) {
+        // no position of this chunk is live: leave an empty partial and arrive
+        grid_dependency_wait();
+        grid_launch_dependents();
+        if (threadIdx.x == 0) a.part[(static_cast<long long>(h) * gridDim.y + c) * kAttnPartStride + 1] = 0.0f;
+        attention_merge_chunks(a, h, S, threadIdx.x, BlockSync());
+        return;
+    }
+    attention_head<false, BlockSync, GridWait, false, true>(a, h, S, threadIdx.x, BlockSync(), GridWait(), -1, c);
 }
 
 // ---------------------------------------------------------------------------

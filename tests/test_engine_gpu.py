@@ -471,3 +471,59 @@ def test_engine_forward_batch_q4_128_projections(native, small, monkeypatch):
     finally:
         eng.close()
     assert native.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("numerics", ["fast", "reference_exact"])
+def test_engine_long_context_attention_vs_oracle(native, oracle, numerics):
+    """Decode attention at long contexts (split-KV in the fast mode: 256-position chunks merged
+    in chunk order; the reference-exact head in the other) against the oracle's
+    compute_attention_flash_q8 restatement (unified_engine.cpp:922-1027) on the engine's own
+    state: SMALL model (GQA 6/2, head_dim 128) with a 2048-position cache, filled by a batched
+    prefill, then single-token steps at positions on and across chunk boundaries.  The last
+    layer's q (RoPE applied here from its qkv output) and KV cache are read back; its attention
+    output must match the oracle's within 1e-4 (fast: fp32 reassociation of the chunk and group
+    merges) or bitwise (reference-exact)."""
+    import ctypes
+
+    from asdsl_b200.inference.synthetic import SMALL, build_model
+    from oracle.oracle import _I, _p
+
+    cfg = dict(SMALL, max_seq=2048)
+    model = build_model(cfg, seed=13, norms_one=False)
+    c = model["config"]
+    nh, nkv, hd, L = c["n_heads"], c["n_kv_heads"], 128, c["num_layers"]
+    qd, kvd = nh * hd, nkv * hd
+    eng = _engine(model, numerics=numerics)
+    try:
+        toks = np.random.default_rng(13).integers(0, c["vocab"], size=2048).tolist()
+        done = 0
+        for pos in (255, 256, 700, 1023, 1500, 2047):
+            if pos > done:
+                eng.forward_batch(toks[done:pos], done)
+            eng.forward_token_argmax(toks[pos], pos)
+            done = pos + 1
+            qkv = eng.read_buffer("qkv")
+            att = eng.read_buffer("att")
+            per_c = 2048 * kvd
+            per_s = 2048 * nkv * 2
+            kq = np.ascontiguousarray(eng.read_buffer("kq")[(L - 1) * per_c : L * per_c])
+            vq = np.ascontiguousarray(eng.read_buffer("vq")[(L - 1) * per_c : L * per_c])
+            ks = np.ascontiguousarray(eng.read_buffer("ks")[(L - 1) * per_s : L * per_s])
+            vs = np.ascontiguousarray(eng.read_buffer("vs")[(L - 1) * per_s : L * per_s])
+            q = np.ascontiguousarray(qkv[:qd].copy())
+            k = np.ascontiguousarray(qkv[qd : qd + kvd].copy())
+            cos = np.ascontiguousarray(np.asarray(model["cos"], np.float32))
+            sin = np.ascontiguousarray(np.asarray(model["sin"], np.float32))
+            oracle.lib.or_rope(_p(q), _p(k), _p(cos), _p(sin), _I(pos), _I(c["rotary_dim"]), _I(nh), _I(nkv),
+                               _I(hd))
+            want = np.zeros(qd, np.float32)
+            oracle.lib.or_attention(_p(want), _p(q), kq.ctypes.data_as(ctypes.c_void_p), _p(ks),
+                                    vq.ctypes.data_as(ctypes.c_void_p), _p(vs), _I(pos), _I(nh), _I(nkv), _I(hd),
+                                    ctypes.c_long(kvd), ctypes.c_long(nkv * 2))
+            if numerics == "reference_exact":
+                assert np.array_equal(att.view(np.uint32), want.view(np.uint32)), f"pos {pos}: not bitwise"
+            else:
+                assert rel_err(att, want) < 1e-4, f"pos {pos}: attention rel err {rel_err(att, want)}"
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0

@@ -65,3 +65,21 @@ def test_gemv_argmax_static_rejects_bad_args(native):
     p = dummy.data_ptr()
     with pytest.raises(ValueError):  # unsupported weight format
         native.call("asdsl_b200_gemv_argmax_static", 99, p, p, p, p, p, p, 0, 4, 64, None)
+
+
+def test_gemv_argmax_static_first_call_in_fresh_process(native):
+    """The first-call path (symbol address resolved, array zeroed on the stream) in a process whose
+    CUDA context has never called the static entry: this file's cases run in a child interpreter
+    with a fresh context, whatever ran before them in this process."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([os.path.join(root, "asdsl-framework_b200"), root, env.get("PYTHONPATH", "")])
+    cmd = [sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", "-m", "gpu",
+           os.path.join(root, "tests", "test_zz_no_alloc.py"), "-k", "matches_scratch_entry"]
+    r = subprocess.run(["timeout", "-k", "10", "600"] + cmd, cwd=root, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, (r.stdout + r.stderr)[-3000:]
+    assert "4 passed" in r.stdout, r.stdout[-2000:]
