@@ -281,4 +281,269 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
     }
 }
 
+// ---------------------------------------------------------------------------
+// Split form for long caches: the same operations, spread over (head, 256-position chunk) CTAs
+// in two kernels, so every value -- score, tile maximum, running maximum, old scale, weight,
+// tile sum -- is computed by the same expression as in k_attention_exact, and the merge over
+// tiles runs in tile order as there: the outputs are bitwise the single-CTA kernel's.
+//   k_attention_exact_scores: RoPE + this position's KV quantization (the chunk holding `pos`
+//     stores it), the scores of the chunk's positions and its tiles' maxima -> global scratch;
+//   k_attention_exact_sums: the running maxima through the chunk's tiles (a scan over the tile
+//     maxima), old scales, weights, every tile's (tile_l, tile_num) -> global scratch; the last
+//     CTA of the head merges all tiles in order.
+// ---------------------------------------------------------------------------
+constexpr int kAttnXChunk = 256;                       // positions per CTA (4 tiles)
+constexpr int kAttnXChunkTiles = kAttnXChunk / kAttnXTile;
+constexpr int kAttnXResStride = kAttnHeadDim + 4;      // per tile: old, tile_l, pad, pad, num[128]
+
+struct AttnXSplit {
+    float* s;            // [n_heads][max_seq] scores
+    float* tmax;         // [n_heads][max_tiles] tile maxima
+    float* tres;         // [n_heads][max_tiles][kAttnXResStride]
+    unsigned int* cnt;   // [n_heads] arrival counters of the sums kernel (re-armed by its last CTA)
+};
+
+__global__ void __launch_bounds__(kAttnXThreads)
+    k_attention_exact_scores(AttnArgs a, ExactTabs ex, float inv_sqrt_d, AttnXSplit sp) {
+    __shared__ __align__(16) int8_t kc_s[kAttnXChunk * kAttnXRow];
+    __shared__ float ksc_s[2 * kAttnXChunk];
+    __shared__ float q_s[kAttnHeadDim], k_s[kAttnHeadDim];
+    __shared__ float red[2][2][2];
+    __shared__ float s_s[kAttnXChunk];
+    constexpr int hd = kAttnHeadDim;
+    const int h = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
+    const int g = h / groups;
+    const int half = a.rot / 2;
+    const int pos = a.st->pos;
+    const int p0 = c * kAttnXChunk;
+    const bool live = pos >= 0 && pos < a.max_seq && p0 <= pos;
+    const int p1 = live ? min(pos + 1, p0 + kAttnXChunk) : p0;  // positions [p0, p1)
+    const bool owner = live && pos < p0 + kAttnXChunk;
+    // cached K of this chunk's earlier positions -> shared memory (independent of the qkv kernel)
+    const int ncached = live ? (owner ? pos - p0 : p1 - p0) : 0;
+    for (int i = tid; i < ncached * 8; i += kAttnXThreads) {
+        const int pp = i >> 3, cc = i & 7;
+        const long long rb = (static_cast<long long>(p0 + pp) * a.n_kv + g) * hd;
+        *reinterpret_cast<uint4*>(kc_s + pp * kAttnXRow + cc * 16) = *reinterpret_cast<const uint4*>(a.kq + rb + cc * 16);
+    }
+    for (int i = tid; i < ncached * 2; i += kAttnXThreads) {
+        const int pp = i >> 1, b = i & 1;
+        ksc_s[i] = a.ks[(static_cast<long long>(p0 + pp) * a.n_kv + g) * 2 + b];
+    }
+    grid_dependency_wait();
+    grid_launch_dependents();
+    if (!live) return;
+    const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
+    float kval = 0.f, vval = 0.f;
+    if (tid < hd) {
+        const float* qh = a.qkv + h * hd;
+        const float* kh = a.qkv + q_dim + g * hd;
+        float qv = qh[tid], kv = kh[tid];
+        if (tid < 2 * half) {
+            const int i = tid < half ? tid : tid - half;
+            const float rc = a.cos_t[static_cast<long long>(pos) * half + i];
+            const float rs = a.sin_t[static_cast<long long>(pos) * half + i];
+            if (tid < half) {
+                qv = __fmaf_rn(qv, rc, -__fmul_rn(qh[tid + half], rs));
+                kv = __fmaf_rn(kv, rc, -__fmul_rn(kh[tid + half], rs));
+            } else {
+                qv = __fmaf_rn(qh[i], rs, __fmul_rn(qv, rc));
+                kv = __fmaf_rn(kh[i], rs, __fmul_rn(kv, rc));
+            }
+        }
+        q_s[tid] = qv;
+        kval = kv;
+        vval = a.qkv[q_dim + kv_dim + g * hd + tid];
+    }
+    if (owner) {
+        const float km = warp_max(fabsf(kval));
+        const float vm = warp_max(fabsf(vval));
+        if (tid < hd && lane == 0) {
+            red[0][tid >> 6][(tid >> 5) & 1] = km;
+            red[1][tid >> 6][(tid >> 5) & 1] = vm;
+        }
+    }
+    __syncthreads();
+    if (owner && tid < hd) {
+        const int b = tid >> 6;
+        const float ka = fmaxf(red[0][b][0], red[0][b][1]);
+        const float va = fmaxf(red[1][b][0], red[1][b][1]);
+        const float ksc = ka > 1e-12f ? __fmul_rn(ka, inv127f()) : 1e-12f;
+        const float vsc = va > 1e-12f ? __fmul_rn(va, inv127f()) : 1e-12f;
+        int qk = __float2int_rn(__fmul_rn(kval, kv_code_inv(ka)));
+        int qv = __float2int_rn(__fmul_rn(vval, kv_code_inv(va)));
+        qk = qk < -127 ? -127 : (qk > 127 ? 127 : qk);
+        qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+        k_s[tid] = __fmul_rn(static_cast<float>(qk), ksc);
+        if (h % groups == 0) {
+            const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
+            a.kq[kb + tid] = static_cast<int8_t>(qk);
+            a.vq[kb + tid] = static_cast<int8_t>(qv);
+            if ((tid & 63) == 0) {
+                const long long sb = (static_cast<long long>(pos) * a.n_kv + g) * 2 + b;
+                a.ks[sb] = ksc;
+                a.vs[sb] = vsc;
+            }
+        }
+    }
+    __syncthreads();
+    // scores: one thread per position (k_attention_exact's expression)
+    float* s_g = sp.s + static_cast<long long>(h) * a.max_seq;
+    for (int p = p0 + tid; p < p1; p += kAttnXThreads) {
+        float dot = 0.0f;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            float ln[8];
+            if (p == pos) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) {
+                        const int d = b * 64 + i * 8 + l;
+                        ln[l] = __fmaf_rn(q_s[d], k_s[d], i == 0 ? 0.0f : ln[l]);
+                    }
+            } else {
+                const float sc = ksc_s[2 * (p - p0) + b];
+                const int8_t* kr = kc_s + (p - p0) * kAttnXRow + b * 64;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const uint4 w4 = *reinterpret_cast<const uint4*>(kr + cc * 16);
+                    const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int i = cc * 2 + (e >> 3), l = e & 7;
+                        const int code = static_cast<int8_t>((ww[e >> 2] >> (8 * (e & 3))) & 0xFFu);
+                        const float kf = __fmul_rn(static_cast<float>(code), sc);
+                        ln[l] = __fmaf_rn(q_s[b * 64 + i * 8 + l], kf, i == 0 ? 0.0f : ln[l]);
+                    }
+                }
+            }
+            const float hs = __fadd_rn(__fadd_rn(__fadd_rn(ln[0], ln[4]), __fadd_rn(ln[1], ln[5])),
+                                       __fadd_rn(__fadd_rn(ln[2], ln[6]), __fadd_rn(ln[3], ln[7])));
+            dot = __fadd_rn(dot, hs);
+        }
+        const float sv = __fmul_rn(dot, inv_sqrt_d);
+        s_s[p - p0] = sv;
+        s_g[p] = sv;
+    }
+    __syncthreads();
+    // tile maxima of this chunk (one warp per tile; a zero maximum takes the sequential rule)
+    const int t0 = p0 / kAttnXTile, nt_own = (p1 - p0 + kAttnXTile - 1) / kAttnXTile;
+    for (int tt = warp; tt < nt_own; tt += kAttnXThreads / 32) {
+        const int tk = tt * kAttnXTile, span = min(kAttnXTile, p1 - p0 - tk);
+        float v = -INFINITY;
+        if (lane < span) v = s_s[tk + lane];
+        if (lane + 32 < span) {
+            const float v2 = s_s[tk + lane + 32];
+            v = (v < v2) ? v2 : v;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float u = __shfl_xor_sync(0xffffffffu, v, o);
+            v = (v < u) ? u : v;
+        }
+        if (v == 0.0f) {
+            float q = -INFINITY;
+            for (int pp = 0; pp < span; ++pp) {
+                const float spv = s_s[tk + pp];
+                q = (q < spv) ? spv : q;
+            }
+            v = q;
+        }
+        if (lane == 0) sp.tmax[static_cast<long long>(h) * ((a.max_seq + kAttnXTile - 1) / kAttnXTile) + t0 + tt] = v;
+    }
+}
+
+__global__ void __launch_bounds__(kAttnXThreads)
+    k_attention_exact_sums(AttnArgs a, ExactTabs ex, AttnXSplit sp) {
+    __shared__ __align__(16) int8_t vc_s[kAttnXChunk * kAttnHeadDim];
+    __shared__ float vsc_s[2 * kAttnXChunk];
+    __shared__ float w_s[kAttnXChunk];
+    __shared__ float m_s[kAttnXChunkTiles], old_s[kAttnXChunkTiles];
+    __shared__ int last_s;
+    constexpr int hd = kAttnHeadDim;
+    const int h = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
+    const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
+    const int g = h / groups;
+    const int max_tiles = (a.max_seq + kAttnXTile - 1) / kAttnXTile;
+    grid_dependency_wait();  // the scores kernel (and this position's KV write) completed
+    grid_launch_dependents();
+    const int pos = a.st->pos;
+    if (pos < 0 || pos >= a.max_seq) return;  // no CTA arrives: the counter stays armed
+    const int p0 = c * kAttnXChunk;
+    const bool live = p0 <= pos;
+    const int p1 = live ? min(pos + 1, p0 + kAttnXChunk) : p0;
+    const int t0 = p0 / kAttnXTile, nt_own = (p1 - p0 + kAttnXTile - 1) / kAttnXTile;
+    const float* tmax = sp.tmax + static_cast<long long>(h) * max_tiles;
+    float* tres = sp.tres + static_cast<long long>(h) * max_tiles * kAttnXResStride;
+    if (live) {
+        // V of the chunk's positions (this position's included: the scores kernel stored it)
+        for (int i = tid; i < (p1 - p0) * 8; i += kAttnXThreads) {
+            const int pp = i >> 3, cc = i & 7;
+            const long long rb = (static_cast<long long>(p0 + pp) * a.n_kv + g) * hd;
+            *reinterpret_cast<uint4*>(vc_s + pp * hd + cc * 16) = *reinterpret_cast<const uint4*>(a.vq + rb + cc * 16);
+        }
+        for (int i = tid; i < (p1 - p0) * 2; i += kAttnXThreads) {
+            const int pp = i >> 1, b = i & 1;
+            vsc_s[i] = a.vs[(static_cast<long long>(p0 + pp) * a.n_kv + g) * 2 + b];
+        }
+        if (tid == 0) {
+            // running maxima through this chunk's tiles, and their old scales, as the single-CTA scan
+            float m = -INFINITY;
+            for (int t = 0; t < t0 + nt_own; ++t) {
+                const float tm = __ldcg(tmax + t);
+                const float nm = (m < tm) ? tm : m;
+                if (t >= t0) {
+                    m_s[t - t0] = nm;
+                    old_s[t - t0] = (t == 0) ? 0.0f : exact_expf(__fsub_rn(m, nm), ex);
+                }
+                m = nm;
+            }
+        }
+        __syncthreads();
+        const float* s_g = sp.s + static_cast<long long>(h) * a.max_seq;
+        for (int p = p0 + tid; p < p1; p += kAttnXThreads)
+            w_s[p - p0] = exact_expf(__fsub_rn(__ldcg(s_g + p), m_s[(p - p0) / kAttnXTile]), ex);
+        __syncthreads();
+        for (int i = tid; i < nt_own * hd; i += kAttnXThreads) {
+            const int tt = i / hd, d = i % hd;
+            const int tk = tt * kAttnXTile, span = min(kAttnXTile, p1 - p0 - tk);
+            float tl = 0.0f, tn = 0.0f;
+            for (int pp = 0; pp < span; ++pp) {
+                const int q = tk + pp;
+                const float wp = w_s[q];
+                tl = __fadd_rn(tl, wp);
+                const float vf = __fmul_rn(static_cast<float>(vc_s[q * hd + d]), vsc_s[2 * q + (d >> 6)]);
+                tn = __fmaf_rn(wp, vf, tn);
+            }
+            float* r = tres + static_cast<long long>(t0 + tt) * kAttnXResStride;
+            r[4 + d] = tn;
+            if (d == 0) {
+                r[0] = old_s[tt];
+                r[1] = tl;
+            }
+        }
+    }
+    // arrive; the head's last CTA merges every tile in order
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_s = atomicAdd(sp.cnt + h, 1u) == gridDim.y - 1u;
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    const int nt = (pos + kAttnXTile) / kAttnXTile;
+    if (tid < hd) {
+        float l = 0.0f, num = 0.0f;
+        for (int t = 0; t < nt; ++t) {
+            const float* r = tres + static_cast<long long>(t) * kAttnXResStride;
+            const float old = __ldcg(r);
+            l = __fadd_rn(__fmul_rn(l, old), __ldcg(r + 1));
+            num = __fmaf_rn(num, old, __ldcg(r + 4 + tid));
+        }
+        a.out[h * hd + tid] = __fmul_rn(num, __fdiv_rn(1.0f, l));
+    }
+    if (tid == 0) sp.cnt[h] = 0u;
+}
+
 }  // namespace asdsl

@@ -73,6 +73,11 @@ struct asdsl_b200_engine {
     // pinned host staging
     int* h_stage = nullptr;  // [4]: pos, token, argmax, status
     cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
+    // long-cache variants (max_seq_len > 256): attention split over 256-position chunks; replayed
+    // for steps at positions >= 256, where the host-side position mirror says the cache is long
+    cudaGraphExec_t g_decode_long = nullptr, g_prefill_long = nullptr;
+    bool capture_long = false;
+    int host_pos = 0;  // the device position as the host last set and advanced it
     bool finalized = false;
     // per-op kernel chain (default; measured faster on B200) or the persistent decode-step kernel
     int persistent = 0;
@@ -110,6 +115,7 @@ struct asdsl_b200_engine {
     float* attn_part = nullptr;
     unsigned int* attn_cnt = nullptr;
     int attn_chunks = 0;
+    asdsl::AttnXSplit xsplit{};  // reference-exact split attention scratch
 };
 
 namespace {
@@ -450,13 +456,25 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
             aa.n_kv = c.num_kv_heads;
             aa.rot = c.rotary_dim;
             aa.max_seq = c.max_seq_len;
-            if (e->exact) {
+            if (e->exact && e->capture_long) {
+                // long cache: scores and tile maxima per (head, chunk), then the tile sums and the
+                // in-order merge (bitwise the single-CTA kernel's result)
+                const dim3 grid(c.num_heads, (c.max_seq_len + asdsl::kAttnXChunk - 1) / asdsl::kAttnXChunk);
+                void* a1[] = {&aa, &e->ex, &e->inv_sqrt_d, &e->xsplit};
+                if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_exact_scores), grid,
+                                          dim3(asdsl::kAttnXThreads), a1, s, true))
+                    return rc;
+                void* a2[] = {&aa, &e->ex, &e->xsplit};
+                if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_exact_sums), grid,
+                                          dim3(asdsl::kAttnXThreads), a2, s, true))
+                    return rc;
+            } else if (e->exact) {
                 void* args[] = {&aa, &e->ex, &e->inv_sqrt_d};
                 if (int rc = launch_small(reinterpret_cast<const void*>(&asdsl::k_attention_exact), dim3(c.num_heads),
                                           dim3(asdsl::kAttnXThreads), args, s, true,
                                           asdsl::attn_x_layout(c.max_seq_len).total))
                     return rc;
-            } else if (e->attn_chunks > 1) {
+            } else if (e->capture_long && e->attn_chunks > 1) {
                 // long cache: heads x position chunks, partials merged in chunk order
                 aa.part = e->attn_part;
                 aa.cnt = e->attn_cnt;
@@ -566,9 +584,20 @@ int eng_set_pos(asdsl_b200_engine* e, int pos, int token) {
     ASDSL_CUDA(cudaStreamSynchronize(e->stream));  // the pinned stage may still be read by a prior copy
     e->h_stage[0] = pos;
     e->h_stage[1] = token;
+    e->host_pos = pos;
     ASDSL_CUDA(cudaMemcpyAsync(&e->st->pos, &e->h_stage[0], sizeof(int), cudaMemcpyHostToDevice, e->stream));
     if (token >= 0)
         ASDSL_CUDA(cudaMemcpyAsync(e->seq + pos, &e->h_stage[1], sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    return kOk;
+}
+
+// replay one step graph (decode: with the lm_head and argmax), the long-cache variant for a step at
+// position >= 256; the host mirror advances as k_advance_* advances the device position
+int eng_replay(asdsl_b200_engine* e, bool decode) {
+    const bool lng = e->g_decode_long != nullptr && e->host_pos >= 256;
+    cudaGraphExec_t g = decode ? (lng ? e->g_decode_long : e->g_decode) : (lng ? e->g_prefill_long : e->g_prefill);
+    ASDSL_CUDA(cudaGraphLaunch(g, e->stream));
+    if (e->host_pos >= 0 && e->host_pos < e->cfg.max_seq_len) ++e->host_pos;
     return kOk;
 }
 
@@ -837,7 +866,7 @@ int eng_forward_serial(asdsl_b200_engine* e, const int32_t* tokens, int n, int s
         ASDSL_CUDA(cudaMemcpyAsync(e->seq + start_pos + i, e->verify_tok + i, 4, cudaMemcpyDeviceToDevice,
                                    e->stream));
         const bool want = all || (out_logits && i == n - 1);
-        ASDSL_CUDA(cudaGraphLaunch(want ? e->g_decode : e->g_prefill, e->stream));
+        if (int rc = eng_replay(e, want)) return rc;
         if (all)
             ASDSL_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(e->verify_logits) + row * i, e->logits, row,
                                        cudaMemcpyDeviceToDevice, e->stream));
@@ -912,6 +941,9 @@ int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_eng
         if ((rc = eng_alloc(e, &L.rms_att, 4ull * c.hidden_size)) || (rc = eng_alloc(e, &L.rms_ffn, 4ull * c.hidden_size)))
             return fail(rc);
     e->attn_chunks = (c.max_seq_len + asdsl::kAttnChunk - 1) / asdsl::kAttnChunk;
+    // ASDSL_B200_ATTN_SPLIT=0: one CTA per head over every position (the split's baseline)
+    if (const char* sp = std::getenv("ASDSL_B200_ATTN_SPLIT"))
+        if (sp[0] == '0') e->attn_chunks = 1;
     if (e->attn_chunks > 1) {
         if ((rc = eng_alloc(e, &e->attn_part, 4ull * c.num_heads * e->attn_chunks * asdsl::kAttnPartStride)) ||
             (rc = eng_alloc(e, &e->attn_cnt, 4ull * c.num_heads)))
@@ -938,6 +970,8 @@ int asdsl_b200_engine_destroy(asdsl_b200_engine* e) {
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->g_decode) cudaGraphExecDestroy(e->g_decode);
     if (e->g_prefill) cudaGraphExecDestroy(e->g_prefill);
+    if (e->g_decode_long) cudaGraphExecDestroy(e->g_decode_long);
+    if (e->g_prefill_long) cudaGraphExecDestroy(e->g_prefill_long);
     for (void* p : e->allocs)
         if (p) cudaFree(p);
     for (auto*& p : e->d_prog)
@@ -1196,6 +1230,29 @@ int asdsl_b200_engine_finalize(asdsl_b200_engine* e) {
     if (int rc = eng_status(e)) return rc;
     if (int rc = eng_capture(e, true, &e->g_decode)) return rc;
     if (int rc = eng_capture(e, false, &e->g_prefill)) return rc;
+    if (!e->persistent && c.max_seq_len > 256) {
+        // the long-cache step graphs (one eager step of each kind first, as above)
+        if (e->exact) {
+            const int mt = (c.max_seq_len + asdsl::kAttnXTile - 1) / asdsl::kAttnXTile;
+            asdsl::AttnXSplit& x = e->xsplit;
+            if (int rc = eng_alloc(e, &x.s, 4ull * c.num_heads * c.max_seq_len)) return rc;
+            if (int rc = eng_alloc(e, &x.tmax, 4ull * c.num_heads * mt)) return rc;
+            if (int rc = eng_alloc(e, &x.tres, 4ull * c.num_heads * mt * asdsl::kAttnXResStride)) return rc;
+            if (int rc = eng_alloc(e, &x.cnt, 4ull * c.num_heads)) return rc;
+            ASDSL_CUDA(cudaMemsetAsync(x.cnt, 0, 4ull * c.num_heads, e->stream));
+        }
+        e->capture_long = true;
+        int rc = eng_set_pos(e, 0, 0);
+        if (!rc) rc = eng_enqueue_step(e, true);
+        if (!rc) rc = eng_set_pos(e, 0, 0);
+        if (!rc) rc = eng_enqueue_step(e, false);
+        if (!rc && cudaStreamSynchronize(e->stream) != cudaSuccess) rc = set_error(kEcuda, "engine_finalize: step failed");
+        if (!rc) rc = eng_status(e);
+        if (!rc) rc = eng_capture(e, true, &e->g_decode_long);
+        if (!rc) rc = eng_capture(e, false, &e->g_prefill_long);
+        e->capture_long = false;
+        if (rc) return rc;
+    }
     if (int rc = eng_zero_kv_from(e, 0)) return rc;
     ASDSL_CUDA(cudaStreamSynchronize(e->stream));
     e->kv_seq_len = 0;
@@ -1213,7 +1270,7 @@ int asdsl_b200_engine_forward_token(asdsl_b200_engine* e, int token, int pos, fl
     DeviceGuard dg(e->device);
     if (int rc = eng_set_pos(e, pos, token)) return rc;
     const bool lm = logits || argmax;
-    ASDSL_CUDA(cudaGraphLaunch(lm ? e->g_decode : e->g_prefill, e->stream));
+    if (int rc = eng_replay(e, lm)) return rc;
     if (logits)
         ASDSL_CUDA(cudaMemcpyAsync(logits, e->logits, 4ull * e->cfg.vocab_size, cudaMemcpyDefault, e->stream));
     if (argmax) ASDSL_CUDA(cudaMemcpyAsync(&e->h_stage[2], e->am_idx, 4, cudaMemcpyDeviceToHost, e->stream));
@@ -1255,7 +1312,7 @@ int asdsl_b200_engine_forward_verify(asdsl_b200_engine* e, const int32_t* tokens
         if (i > 0)
             ASDSL_CUDA(cudaMemcpyAsync(e->seq + start_pos + i, e->verify_tok + i, 4, cudaMemcpyDeviceToDevice,
                                        e->stream));
-        ASDSL_CUDA(cudaGraphLaunch(e->g_decode, e->stream));
+        if (int rc = eng_replay(e, true)) return rc;
         ASDSL_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(e->verify_logits) + row * i, e->logits, row,
                                    cudaMemcpyDeviceToDevice, e->stream));
     }
@@ -1341,15 +1398,18 @@ int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int 
         if (int rc = eng_set_pos(e, n_pre, -1)) return rc;
     } else {
         if (int rc = eng_set_pos(e, 0, -1)) return rc;
-        for (int i = 0; i + 1 < n_prompt; ++i) ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+        for (int i = 0; i + 1 < n_prompt; ++i)
+            if (int rc = eng_replay(e, false)) return rc;
     }
     // the last prompt token's forward is the first decode step; without one it is a prefill step
-    if (producible == 0) ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+    if (producible == 0)
+        if (int rc = eng_replay(e, false)) return rc;
     int produced = 0, stop_at = -1;
     const int chunk = n_stops > 0 ? 16 : (producible > 0 ? producible : 1);
     while (produced < producible && stop_at < 0) {
         const int n = std::min(chunk, producible - produced);
-        for (int i = 0; i < n; ++i) ASDSL_CUDA(cudaGraphLaunch(e->g_decode, e->stream));
+        for (int i = 0; i < n; ++i)
+            if (int rc = eng_replay(e, true)) return rc;
         ASDSL_CUDA(cudaMemcpyAsync(out + n_prompt + produced, e->seq + n_prompt + produced, 4ull * n,
                                    cudaMemcpyDeviceToHost, e->stream));
         if (int rc = eng_status(e)) return rc;
@@ -1382,7 +1442,7 @@ int asdsl_b200_engine_generate(asdsl_b200_engine* e, const int32_t* prompt, int 
     }
     if (max_tokens > 0) {
         // forward of the last token (KV only), as the reference's loop does
-        ASDSL_CUDA(cudaGraphLaunch(e->g_prefill, e->stream));
+        if (int rc = eng_replay(e, false)) return rc;
     }
     if (int rc = eng_status(e)) return rc;
     e->kv_seq_len = std::max(e->kv_seq_len, n_prompt + max_tokens);
@@ -1468,7 +1528,8 @@ int asdsl_b200_engine_replay(asdsl_b200_engine* e, int decode, int n) {
     ENG_READY(e);
     if (n < 0) return set_error(kEinval, "engine_replay: n must be >= 0");
     DeviceGuard dg(e->device);
-    for (int i = 0; i < n; ++i) ASDSL_CUDA(cudaGraphLaunch(decode ? e->g_decode : e->g_prefill, e->stream));
+    for (int i = 0; i < n; ++i)
+        if (int rc = eng_replay(e, decode != 0)) return rc;
     return kOk;
 }
 

@@ -392,6 +392,19 @@ def decode_bench(model, numerics: str = "fast", ref: dict | None = None, steps: 
                 rows[name] = out
         if rows and not np.array_equal(rows["verify_serial"], rows["verify_batched"]):
             raise SystemExit("bench: batched verify rows differ from serial forward_token rows")
+        # long context: the cache filled to position 1920 by a batched prefill, then `steps`
+        # decode replays at positions 1920 .. 2047 (split-KV attention in the fast mode)
+        if world == 1 and not exact and c["max_seq"] >= 2048:
+            long_tok = np.random.default_rng(seed + 2).integers(0, c["vocab"], size=1920).tolist()
+            eng.reset_session()
+            eng.forward_batch(long_tok, 0)
+            torch.cuda.synchronize()
+            eng.set_position(1920, long_tok[-1])
+            f0.record(stream)
+            eng.replay(min(steps, 128))
+            f1.record(stream)
+            f1.synchronize()
+            pre["long_ms"] = f0.elapsed_time(f1) / min(steps, 128)
         assert _lib.device_status(clear=True) == 0
     finally:
         eng.close()
@@ -420,6 +433,10 @@ def decode_bench(model, numerics: str = "fast", ref: dict | None = None, steps: 
         "e2e": {"value": round(world * steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4, "ms_total": round(e2e_ms, 3)},
         "gpu_launches": steps * (3 + 5 * c["num_layers"]),
+        "long_context": ({"positions": "1920..2047", "ms_per_token": round(pre["long_ms"], 4),
+                          "tokens_per_s": round(1e3 / pre["long_ms"], 2),
+                          "attention": "split-KV, 256-position chunks" if os.environ.get("ASDSL_B200_ATTN_SPLIT", "1")[0] != "0"
+                          else "one CTA per head"} if "long_ms" in pre else None),
         "prefill": ({"tokens": prefill_tokens, "serial_ms": round(pre["prefill_serial"], 3),
                      "batched_ms": round(pre["prefill_batched"], 3),
                      "serial_tokens_per_s": round(prefill_tokens / (pre["prefill_serial"] * 1e-3), 1),
@@ -428,7 +445,7 @@ def decode_bench(model, numerics: str = "fast", ref: dict | None = None, steps: 
                      "verify_8_batched_ms": round(pre["verify_batched"], 3),
                      "note": "public API calls timed by events on the engine stream; batched rows are "
                              "bit-identical to serial forward_token (checked here for the verify rows)"}
-                    if pre else None),
+                    if "prefill_serial" in pre else None),
     }
 
 

@@ -225,3 +225,33 @@ def test_engine_exact_config3_greedy_trajectory(native, oracle):
     first_diff = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
     assert got == want, f"config-3 greedy tokens differ from step {first_diff}"
     assert native.device_status(clear=True) == 0
+
+
+def test_engine_exact_generate_across_long_cache_boundary(native, oracle):
+    """generate() across position 256, where the engine switches from the single-CTA attention
+    graph to the split (head x 256-position chunk) one: 300 greedy tokens on a TINY-shaped model
+    with a 512-position cache equal the oracle engine's, and so do the logits at positions 255,
+    256 and 299 (teacher-forced on those tokens)."""
+    from asdsl_b200.inference.synthetic import TINY, build_model
+
+    model = build_model(dict(TINY, max_seq=512), seed=21, norms_one=False)
+    c = model["config"]
+    model["lm_meta"], model["lm_quant"] = oracle.lmhead_quant_preq2(model["embed_f16"], c["vocab"], c["hidden"])
+    ref = OracleEngine(model, oracle)
+    want, _ = ref.generate([5], 300)
+    ref.close()
+    eng = _engine(model)
+    try:
+        got = eng.generate([5], 300)
+        assert got == [int(t) for t in want]
+        eng.reset_session()
+        ref = OracleEngine(model, oracle)
+        for pos in range(300):
+            lo = ref.forward_token(int(want[pos]), pos)
+            la = eng.forward_token(int(want[pos]), pos)
+            if pos in (255, 256, 299):
+                _assert_bitwise(la, lo, f"logits at position {pos}")
+        ref.close()
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0
