@@ -3,17 +3,19 @@
 on the device (seeded), runs `--reps` launches of its kernels on one stream and exits 0.
 
 Cases (kernels they launch):
-  attention        k_attention (decode, 1024 cached positions, Phi-4-mini heads), and on the way
+  attention        k_attention_split (decode at 1024 cached positions, Phi-4-mini heads; with
+                   ASDSL_B200_ATTN_SPLIT=0 the one-CTA-per-head k_attention), and on the way
                    k_attention_rows / k_kv_write_rows / k_quant_tokens / k_stream_gemv<..,NT>
                    (the batched prefill of those positions)
-  attention_exact  k_attention_exact (reference-exact mode, 1024 cached positions)
-  multi            k_stream_gemv<preq, .., NT=16> (dp4a lanes) and k_gemv_mma (int8 mma.sync)
-                   at 3072x8192, 16 tokens
+  attention_exact  k_attention_exact (reference-exact mode, positions < 256) and, from position 256,
+                   k_attention_exact_scores + k_attention_exact_sums (1024 cached positions)
+  multi            k_stream_gemv<preq, .., NT=8> (dp4a lanes) at 3072x8192, 16 tokens
+  multi_mma        k_stream_gemv_mma (int8 mma.sync, selected from 5 tokens) at 8192x3072, 16 tokens
   gemm128          k_gemm_q4_128 (prompt GEMM), 16384x3072, 8 rows
   q4k / s256 / packed  the Q4_K, Q4_S256 and fp32-activation packed GEMVs, 8192x3072
   weight_prep      k_quantize_groups, k_pack_preq2, k_q4_128_from_f32 on 8192x3072 fp32
-  exact_gemv       k_stream_gemv<preq2 exact> (RMSNorm + A8 prologue), 16384x3072, and the
-                   gate_up + SiLU form
+  exact_gemv       k_stream_gemv<preq2 exact> (RMSNorm + A8 prologue), 16384x3072, the gate_up
+                   + SiLU form (8192 pairs), then 5120x3072 (qkv) and 3072x3072 (o) without RMSNorm
   xchg1            k_allreduce_peer and the lm_head argmax exchange with a world of one GPU
                    (the peer stores go to this GPU's own buffers)
 """
@@ -89,11 +91,25 @@ def case_multi(reps):
     blocks.view(torch.float16)[1::10].copy_(_fp16_scales(blocks.numel() // 20, -0.1, -0.05, 3))
     X = _x(K, 4, k).reshape(k, K)
     Y = torch.empty(k * M, device="cuda")
-    for mma in (0, 5):
-        _lib.call("asdsl_b200_set_mma_min_tokens", mma)
+    for _ in range(reps):
+        gemv_multi(_lib.FMT_PREQ, blocks, None, X, Y, M, K)
+
+
+def case_multi_mma(reps):
+    from asdsl_b200.kernels._native_gemv import gemv_multi
+
+    M, K, k = 8192, 3072, 16
+    blocks = _bytes(M * (K // 32) * 20, 1)
+    blocks.view(torch.float16)[0::10].copy_(_fp16_scales(blocks.numel() // 20, 0.004, 0.012, 2))
+    blocks.view(torch.float16)[1::10].copy_(_fp16_scales(blocks.numel() // 20, -0.1, -0.05, 3))
+    X = _x(K, 4, k).reshape(k, K)
+    Y = torch.empty(k * M, device="cuda")
+    _lib.call("asdsl_b200_set_mma_min_tokens", 5)
+    try:
         for _ in range(reps):
             gemv_multi(_lib.FMT_PREQ, blocks, None, X, Y, M, K)
-    _lib.call("asdsl_b200_set_mma_min_tokens", 0)
+    finally:
+        _lib.call("asdsl_b200_set_mma_min_tokens", 0)
 
 
 def case_gemm128(reps):
@@ -174,6 +190,10 @@ def case_exact_gemv(reps):
     for _ in range(reps):
         _lib.call("asdsl_b200_gateup_silu_exact", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), nw.data_ptr(),
                   ctypes.c_float(1e-5), h.data_ptr(), I, K, s)
+    for m2 in (5120, 3072):
+        for _ in range(reps):
+            _lib.call("asdsl_b200_gemv_preq2_fused_exact", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), None,
+                      ctypes.c_float(0.0), y.data_ptr(), m2, K, s)
 
 
 def case_xchg1(reps):
