@@ -1159,7 +1159,9 @@ int asdsl_b200_repack_q4_128_f32(const float* w, int rows, int cols, uint8_t* bl
     if (rows <= 0) return set_error(kEinval, "repack_q4_128: invalid dimensions");
     if (!aligned_to(w, 4) || !aligned_to(blocks, 2)) return set_error(kEinval, "repack_q4_128: misaligned buffer");
     const long long work = static_cast<long long>(rows) * (cols / 128);
-    k_q4_128_from_f32<<<grid_for(work, 128), 128, 0, as_stream(stream)>>>(w, rows, cols, blocks);
+    // one warp per group, at most 32 resident CTAs of 4 warps per SM (grid-stride beyond)
+    const unsigned blocks_n = static_cast<unsigned>(std::min<long long>(grid_for(work, 4), sm_count() * 32ll));
+    k_q4_128_from_f32<<<blocks_n, 128, 0, as_stream(stream)>>>(w, rows, cols, blocks);
     ASDSL_CUDA(cudaGetLastError());
     return kOk;
 }

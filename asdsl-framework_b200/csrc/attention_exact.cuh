@@ -460,48 +460,61 @@ __global__ void __launch_bounds__(kAttnXThreads)
     __shared__ __align__(16) int8_t vc_s[kAttnXChunk * kAttnHeadDim];
     __shared__ float vsc_s[2 * kAttnXChunk];
     __shared__ float w_s[kAttnXChunk];
-    __shared__ float m_s[kAttnXChunkTiles], old_s[kAttnXChunkTiles];
+    __shared__ float m_s[kAttnXChunkTiles], mp_s[kAttnXChunkTiles], old_s[kAttnXChunkTiles];
+    __shared__ float tm_s[kAttnXMaxSeq / kAttnXTile];
     __shared__ int last_s;
     constexpr int hd = kAttnHeadDim;
     const int h = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
     const int groups = a.n_heads / a.n_kv > 0 ? a.n_heads / a.n_kv : 1;
     const int g = h / groups;
     const int max_tiles = (a.max_seq + kAttnXTile - 1) / kAttnXTile;
-    grid_dependency_wait();  // the scores kernel (and this position's KV write) completed
-    grid_launch_dependents();
+    // the position is final here (the previous token's step advanced it); the V of earlier
+    // positions was stored by earlier steps, so it is staged before the dependency wait
     const int pos = a.st->pos;
-    if (pos < 0 || pos >= a.max_seq) return;  // no CTA arrives: the counter stays armed
+    const bool ok = pos >= 0 && pos < a.max_seq;
     const int p0 = c * kAttnXChunk;
-    const bool live = p0 <= pos;
+    const bool live = ok && p0 <= pos;
     const int p1 = live ? min(pos + 1, p0 + kAttnXChunk) : p0;
-    const int t0 = p0 / kAttnXTile, nt_own = (p1 - p0 + kAttnXTile - 1) / kAttnXTile;
-    const float* tmax = sp.tmax + static_cast<long long>(h) * max_tiles;
-    float* tres = sp.tres + static_cast<long long>(h) * max_tiles * kAttnXResStride;
-    if (live) {
-        // V of the chunk's positions (this position's included: the scores kernel stored it)
-        for (int i = tid; i < (p1 - p0) * 8; i += kAttnXThreads) {
+    const int nold = live ? min(pos, p1) - p0 : 0;  // positions of this chunk before `pos`
+    auto stage_v = [&](int pp0, int pp1) {
+        for (int i = tid + pp0 * 8; i < pp1 * 8; i += kAttnXThreads) {
             const int pp = i >> 3, cc = i & 7;
             const long long rb = (static_cast<long long>(p0 + pp) * a.n_kv + g) * hd;
             *reinterpret_cast<uint4*>(vc_s + pp * hd + cc * 16) = *reinterpret_cast<const uint4*>(a.vq + rb + cc * 16);
         }
-        for (int i = tid; i < (p1 - p0) * 2; i += kAttnXThreads) {
+        for (int i = tid + pp0 * 2; i < pp1 * 2; i += kAttnXThreads) {
             const int pp = i >> 1, b = i & 1;
             vsc_s[i] = a.vs[(static_cast<long long>(p0 + pp) * a.n_kv + g) * 2 + b];
         }
+    };
+    stage_v(0, nold);
+    grid_dependency_wait();  // the scores kernel (and this position's KV write) completed
+    grid_launch_dependents();
+    if (!ok) return;  // no CTA arrives: the counter stays armed
+    const int t0 = p0 / kAttnXTile, nt_own = (p1 - p0 + kAttnXTile - 1) / kAttnXTile;
+    const float* tmax = sp.tmax + static_cast<long long>(h) * max_tiles;
+    float* tres = sp.tres + static_cast<long long>(h) * max_tiles * kAttnXResStride;
+    if (live) {
+        stage_v(nold, p1 - p0);  // this position's V, stored by the scores kernel
+        // the tile maxima up to this chunk's last tile, loaded in parallel
+        for (int t = tid; t < t0 + nt_own; t += kAttnXThreads) tm_s[t] = __ldcg(tmax + t);
+        __syncthreads();
         if (tid == 0) {
-            // running maxima through this chunk's tiles, and their old scales, as the single-CTA scan
+            // running maxima through this chunk's tiles, as the single-CTA scan
             float m = -INFINITY;
             for (int t = 0; t < t0 + nt_own; ++t) {
-                const float tm = __ldcg(tmax + t);
+                const float tm = tm_s[t];
                 const float nm = (m < tm) ? tm : m;
                 if (t >= t0) {
+                    mp_s[t - t0] = m;
                     m_s[t - t0] = nm;
-                    old_s[t - t0] = (t == 0) ? 0.0f : exact_expf(__fsub_rn(m, nm), ex);
                 }
                 m = nm;
             }
         }
         __syncthreads();
+        // old scales of this chunk's tiles, one thread each
+        if (tid < nt_own) old_s[tid] = (t0 + tid == 0) ? 0.0f : exact_expf(__fsub_rn(mp_s[tid], m_s[tid]), ex);
         const float* s_g = sp.s + static_cast<long long>(h) * a.max_seq;
         for (int p = p0 + tid; p < p1; p += kAttnXThreads)
             w_s[p - p0] = exact_expf(__fsub_rn(__ldcg(s_g + p), m_s[(p - p0) / kAttnXTile]), ex);
@@ -534,12 +547,27 @@ __global__ void __launch_bounds__(kAttnXThreads)
     __threadfence();
     const int nt = (pos + kAttnXTile) / kAttnXTile;
     if (tid < hd) {
+        // the tiles' values are loaded eight at a time, then folded in tile order
+        constexpr int B = 8;
         float l = 0.0f, num = 0.0f;
-        for (int t = 0; t < nt; ++t) {
-            const float* r = tres + static_cast<long long>(t) * kAttnXResStride;
-            const float old = __ldcg(r);
-            l = __fadd_rn(__fmul_rn(l, old), __ldcg(r + 1));
-            num = __fmaf_rn(num, old, __ldcg(r + 4 + tid));
+        for (int tb = 0; tb < nt; tb += B) {
+            float ov[B], tlv[B], tnv[B];
+#pragma unroll
+            for (int k = 0; k < B; ++k) {
+                if (tb + k < nt) {
+                    const float* r = tres + static_cast<long long>(tb + k) * kAttnXResStride;
+                    ov[k] = __ldcg(r);
+                    tlv[k] = __ldcg(r + 1);
+                    tnv[k] = __ldcg(r + 4 + tid);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < B; ++k) {
+                if (tb + k < nt) {
+                    l = __fadd_rn(__fmul_rn(l, ov[k]), tlv[k]);
+                    num = __fmaf_rn(num, ov[k], tnv[k]);
+                }
+            }
         }
         a.out[h * hd + tid] = __fmul_rn(num, __fdiv_rn(1.0f, l));
     }

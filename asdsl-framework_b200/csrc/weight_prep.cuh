@@ -205,13 +205,52 @@ __device__ __forceinline__ void q4_128_block(Src src, uint8_t* __restrict__ blk)
     }
 }
 
-// fp32 [M][K] -> Q4_128 blocks [M][K/128][66] (repack_fp32_to_q4_128_blocks)
+// fp32 [M][K] -> Q4_128 blocks [M][K/128][66] (repack_fp32_to_q4_128_blocks): one warp per
+// 128-float group, lane l owning elements 4l..4l+3 (one coalesced 512-byte read per group; the
+// maximum by shuffles is the same value as the sequential one, fmaxf being exact), then the
+// per-element arithmetic of q4_128_block, lane l writing nibble word l
 __global__ void k_q4_128_from_f32(const float* __restrict__ w, int M, int K, uint8_t* __restrict__ blocks) {
     const int ng = K / 128;
-    const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= static_cast<long long>(M) * ng) return;
-    const float* src = w + t * 128;  // row r group g starts at r*K + g*128 = t*128
-    q4_128_block([&](int i) { return __ldg(src + i); }, blocks + t * 66);
+    const long long n = static_cast<long long>(M) * ng;
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+    const bool vec = (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
+    for (long long t = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < n;
+         t += warps) {
+        const float* src = w + t * 128 + lane * 4;  // row r group g starts at r*K + g*128 = t*128
+        float v[4];
+        if (vec) {
+            const float4 f = __ldg(reinterpret_cast<const float4*>(src));
+            v[0] = f.x;
+            v[1] = f.y;
+            v[2] = f.z;
+            v[3] = f.w;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = __ldg(src + k);
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) amax = fmaxf(amax, fabsf(v[k]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const double a64 = static_cast<double>(amax);
+        uint16_t* out = reinterpret_cast<uint16_t*>(blocks + t * 66);  // 66-byte blocks start on even bytes
+        if (a64 < 1e-12) {
+            if (lane == 0) out[0] = 0;
+            out[1 + lane] = 0x8888;
+            continue;
+        }
+        if (lane == 0) out[0] = f16_bits_from_double(__ddiv_rn(a64, 7.0));
+        const float inv = __double2float_rn(__ddiv_rn(7.0, a64));
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float q = clampf(__fadd_rn(rintf(__fmul_rn(v[k], inv)), 8.0f), 0.0f, 15.0f);
+            word |= static_cast<uint32_t>(q) << (4 * k);
+        }
+        out[1 + lane] = static_cast<uint16_t>(word);
+    }
 }
 
 // gs-32 QuantizedTensor -> float32 q * scale + bias (phi4_cpu_run.py:3432-3448) -> Q4_128 blocks:
