@@ -76,6 +76,12 @@ _SIGS = {
     "asdsl_b200_vxchg_destroy": [_P],
     "asdsl_b200_vxchg_set_stamps": [_P, _P, _I],
     "asdsl_b200_engine_set_shard": [_P, _P, _P, _I, _I],
+    "asdsl_b200_gemv_q2_packed": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "asdsl_b200_engine_set_skip_mask": [_P, _P, _I],
+    "asdsl_b200_engine_clear_skip_mask": [_P],
+    "asdsl_b200_engine_set_projection_q2": [_P, _I, _I, _P, _SZ, _P, _P, _SZ],
+    "asdsl_b200_engine_forward_token_draft": [_P, _I, _I, _P, _P, _I],
+    "asdsl_b200_gemv_q2_unpacked": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
     "asdsl_b200_xchg_set_stamps": [_P, _P, _I],
     "asdsl_b200_allreduce_peer": [_P, _P, _P, _P, _I, _P],
     # device-resident decode engine

@@ -10,6 +10,7 @@ from asdsl_b200.kernels.gemv_q4 import (  # noqa: E402
     gemv_q4km_q8,
     has_native_kernel,
 )
+from asdsl_b200.kernels.gemv_q2 import gemv_q2_packed, gemv_q2_unpacked  # noqa: E402
 
 __all__ = [
     "KERNEL_TIER",
@@ -17,5 +18,7 @@ __all__ = [
     "gemv_q4_packed",
     "gemv_q4_unpacked",
     "gemv_q4km_q8",
+    "gemv_q2_packed",
+    "gemv_q2_unpacked",
     "has_native_kernel",
 ]

@@ -214,6 +214,15 @@ class UnifiedEngine:
                     raise KeyError(name)
                 _lib.check(lib.asdsl_b200_engine_set_projection(e, i, w, _lib.FMT_PREQ2, _ptr(m), _nbytes(m), _ptr(q),
                                                                 _nbytes(q)), "UnifiedEngine")
+                # the QCSD draft bank (unified_engine.cpp:2387-2440): packed 2-bit codes, fp32 scales
+                # and biases, used by forward_token_draft_q2
+                qk = f"q2_{name}"
+                if qk in L and f"q2_{name[:-5]}_scales" in L and f"q2_{name[:-5]}_biases" in L:
+                    qw = _blob(L[qk], np.uint8).reshape(-1)
+                    qs = _blob(L[f"q2_{name[:-5]}_scales"], np.float32).reshape(-1)
+                    qb = _blob(L[f"q2_{name[:-5]}_biases"], np.float32).reshape(-1)
+                    _lib.check(lib.asdsl_b200_engine_set_projection_q2(e, i, w, _ptr(qw), _nbytes(qw), _ptr(qs), _ptr(qb),
+                                                                       _nbytes(qs) // 4), "UnifiedEngine")
         _lib.check(lib.asdsl_b200_engine_finalize(e), "UnifiedEngine")
 
     @staticmethod
@@ -245,6 +254,30 @@ class UnifiedEngine:
         """Forward one token updating KV; skip lm_head (:2494-2497)."""
         _lib.check(self._lib.asdsl_b200_engine_forward_token(self._e, int(token), int(pos), None, None),
                    "forward_token_prefill")
+
+    def forward_token_draft(self, token: int, pos: int) -> np.ndarray:
+        """Draft step: forward_token with the skip-masked layers left out (:2701;
+        unified_engine.cpp:1790-1794); the returned buffer is reused."""
+        _lib.check(self._lib.asdsl_b200_engine_forward_token_draft(self._e, int(token), int(pos),
+                                                                   _ptr(self._logits), None, 0), "forward_token_draft")
+        return self._logits
+
+    def forward_token_draft_q2(self, token: int, pos: int) -> np.ndarray:
+        """Draft step with the 2-bit draft bank in place of the 4-bit projections where the layer
+        has one (UnifiedEngine::forward_token_draft_q2, unified_engine.cpp:1796-1802)."""
+        _lib.check(self._lib.asdsl_b200_engine_forward_token_draft(self._e, int(token), int(pos),
+                                                                   _ptr(self._logits), None, 1), "forward_token_draft_q2")
+        return self._logits
+
+    def set_skip_mask(self, mask) -> None:
+        """Layers whose mask entry is true are left out of draft steps (:2711;
+        unified_engine.cpp:1309-1317)."""
+        m = np.ascontiguousarray(np.asarray(list(mask), dtype=bool).astype(np.uint8))
+        _lib.check(self._lib.asdsl_b200_engine_set_skip_mask(self._e, _ptr(m) if m.size else None, int(m.size)),
+                   "set_skip_mask")
+
+    def clear_skip_mask(self) -> None:
+        _lib.check(self._lib.asdsl_b200_engine_clear_skip_mask(self._e), "clear_skip_mask")
 
     def forward_token_argmax(self, token: int, pos: int) -> int:
         """Single decode step; returns the argmax token id (:2499-2506)."""

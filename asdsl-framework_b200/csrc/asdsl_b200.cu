@@ -11,6 +11,7 @@
 #include "launch.cuh"
 #include "weight_prep.cuh"
 #include "gemv_mma.cuh"
+#include "gemv_q2.cuh"
 #include "gemm_q4_128.cuh"
 
 using namespace asdsl;
@@ -360,6 +361,43 @@ int asdsl_b200_gemv_q4_unpacked(const uint8_t* w, const float* x, const float* s
     k_gemv_unpacked<<<(M + wpb - 1) / wpb, wpb * 32, 0, as_stream(stream)>>>(w, x, scales, biases, y, M, K, gs);
     ASDSL_CUDA(cudaGetLastError());
     return kOk;
+}
+
+namespace {
+int gemv_q2_impl(bool packed, const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                 int M, int K, int gs, void* stream, const char* fn) {
+    if (!w || !x || !scales || !biases || !y) return set_error(kEinval, std::string(fn) + ": null pointer");
+    if (M <= 0 || K <= 0 || gs <= 0) return set_error(kEinval, "M, K, group_size must be positive");
+    if (packed && K % 4) return set_error(kEinval, "K must be divisible by 4 for 2-bit packing");
+    if (K % gs) return set_error(kEinval, "K must be divisible by group_size");
+    if (packed && gs % 4) return set_error(kEinval, std::string(fn) + ": group_size must be a multiple of 4");
+    if (K > 32768) return set_error(kEinval, std::string(fn) + ": in_features exceeds 32768");
+    const size_t smem = 4ull * (K + K / gs);
+    const void* fnp = packed ? reinterpret_cast<const void*>(&asdsl::k_gemv_q2<true>)
+                             : reinterpret_cast<const void*>(&asdsl::k_gemv_q2<false>);
+    if (smem > 48 * 1024)
+        ASDSL_CUDA(cudaFuncSetAttribute(fnp, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    const unsigned grid = static_cast<unsigned>(
+        std::min<long long>((M + asdsl::kQ2Warps - 1) / asdsl::kQ2Warps, sm_count() * 8ll));
+    if (packed)
+        asdsl::k_gemv_q2<true><<<grid, asdsl::kQ2Warps * 32, smem, as_stream(stream)>>>(w, x, scales, biases, y, M, K, gs,
+                                                                                      0);
+    else
+        asdsl::k_gemv_q2<false><<<grid, asdsl::kQ2Warps * 32, smem, as_stream(stream)>>>(w, x, scales, biases, y, M, K,
+                                                                                       gs, 0);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+}  // namespace
+
+int asdsl_b200_gemv_q2_packed(const uint8_t* w_packed, const float* x, const float* scales, const float* biases,
+                              float* y, int M, int K, int gs, void* stream) {
+    return gemv_q2_impl(true, w_packed, x, scales, biases, y, M, K, gs, stream, "gemv_q2_packed");
+}
+
+int asdsl_b200_gemv_q2_unpacked(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                                int M, int K, int gs, void* stream) {
+    return gemv_q2_impl(false, w, x, scales, biases, y, M, K, gs, stream, "gemv_q2_unpacked");
 }
 
 int asdsl_b200_matmul_batch_q4(const uint8_t* w, const float* scales, const float* biases, const float* X, float* Y,

@@ -32,10 +32,19 @@ struct EngProj {
     int xlpt = 0;  // reference-exact mode: w0 / w1 hold the exact layout in units of xlpt bands
 };
 
+// a 2-bit draft-bank projection (QCSD): packed codes [rows][cols/4], fp32 scales and biases
+// [rows][cols/32]; null when the layer has none for this projection
+struct Q2Proj {
+    uint8_t* w = nullptr;
+    float* s = nullptr;
+    float* b = nullptr;
+};
+
 struct EngLayer {
     float* rms_att = nullptr;
     float* rms_ffn = nullptr;
     EngProj p[4];  // qkv, o, gate_up, down
+    Q2Proj q2[4];
 };
 
 constexpr int kProjQkv = 0, kProjO = 1, kProjGateUp = 2, kProjDown = 3;
@@ -116,6 +125,14 @@ struct asdsl_b200_engine {
     unsigned int* attn_cnt = nullptr;
     int attn_chunks = 0;
     asdsl::AttnXSplit xsplit{};  // reference-exact split attention scratch
+    // draft steps (forward_token_draft, unified_engine.cpp:1790-1802): layers in `skip` are left
+    // out, and with draft_q2 the layers' 2-bit projections replace the 4-bit ones; the step graphs
+    // are captured per (q2, long cache) on first use and dropped when the mask or the bank changes
+    bool skip[64] = {};
+    bool draft_skip = false, draft_q2 = false;  // set while a draft step is enqueued
+    cudaGraphExec_t g_draft[4] = {nullptr, nullptr, nullptr, nullptr};
+    float* xn = nullptr;  // [hidden] RMSNorm output feeding a 2-bit projection
+    float* gu = nullptr;  // [2 * intermediate] 2-bit gate_up output
 };
 
 namespace {
@@ -129,6 +146,26 @@ using asdsl::kErange;
 using asdsl::kEtimeout;
 using asdsl::kOk;
 using asdsl::set_error;
+
+__global__ void k_silu_rows(const float* __restrict__ gu, float* __restrict__ h, int I, int n);
+
+// out = (x * inv) * w, inv = 1/sqrt(mean(x^2) + eps): the fp32 RMSNorm feeding a draft step's 2-bit
+// projection (rmsnorm_f32, unified_engine.cpp:499-524; one CTA, block reduction)
+__global__ void __launch_bounds__(256) k_rmsnorm_f32(const float* __restrict__ x, const float* __restrict__ w,
+                                                     float* __restrict__ out, int n, float eps) {
+    __shared__ float red[8];
+    grid_dependency_wait();
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 256) ss = __fmaf_rn(x[i], x[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot = __fadd_rn(tot, red[k]);
+    const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(n)), eps));
+    for (int i = threadIdx.x; i < n; i += 256) out[i] = __fmul_rn(__fmul_rn(x[i], inv), w[i]);
+}
 
 template <typename T>
 int eng_alloc(asdsl_b200_engine* e, T** p, size_t bytes) {
@@ -404,6 +441,16 @@ int eng_launch_program(asdsl_b200_engine* e, bool with_lm) {
 }
 
 // enqueue one forward step (token seq[pos] at st->pos) on e->stream
+// one 2-bit draft-bank GEMV (k_gemv_q2, packed); accumulate: y += W x (the residual add)
+int eng_q2_gemv(const Q2Proj& q, const float* x, float* y, int M, int K, bool accumulate, cudaStream_t s) {
+    const size_t smem = 4ull * (K + K / 32);
+    const unsigned grid = static_cast<unsigned>(std::min<long long>((M + asdsl::kQ2Warps - 1) / asdsl::kQ2Warps,
+                                                                    sm_count() * 8ll));
+    asdsl::k_gemv_q2<true><<<grid, asdsl::kQ2Warps * 32, smem, s>>>(q.w, x, q.s, q.b, y, M, K, 32, accumulate ? 1 : 0);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
 int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
     if (e->persistent) return eng_launch_program(e, with_lm);
     const asdsl_b200_engine_config& c = e->cfg;
@@ -428,9 +475,16 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
         }
     }
     for (int l = 0; l < c.num_layers; ++l) {
+        // a draft step leaves the masked layers out (their KV is not written either)
+        if (e->draft_skip && l < 64 && e->skip[l]) continue;
         const EngLayer& L = e->layers[l];
-        // qkv = W_qkv . A8(RMSNorm(resid) * rms_att)
-        {
+        const bool q2 = e->draft_q2;
+        const int qkv_rows = L.p[kProjQkv].rows;
+        // qkv = W_qkv . A8(RMSNorm(resid) * rms_att)  (draft bank: W2_qkv . RMSNorm(resid) in fp32)
+        if (q2 && L.q2[kProjQkv].w) {
+            k_rmsnorm_f32<<<1, 256, 0, s>>>(e->resid, L.rms_att, e->xn, H, c.rms_norm_eps);
+            if (int rc = eng_q2_gemv(L.q2[kProjQkv], e->xn, e->qkv, qkv_rows, H, false, s)) return rc;
+        } else {
             GemvArgs ga = base_args(L.p[kProjQkv].rows, H, 32);
             ga.x = e->resid;
             ga.norm_w = L.rms_att;
@@ -491,7 +545,9 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
             }
         }
         // resid += W_o . A8(att)
-        {
+        if (q2 && L.q2[kProjO].w) {
+            if (int rc = eng_q2_gemv(L.q2[kProjO], e->att, e->resid, H, L.p[kProjO].cols, true, s)) return rc;
+        } else {
             GemvArgs ga = base_args(H, L.p[kProjO].cols, 32);
             ga.x = e->att;
             ga.resid = e->resid;
@@ -500,7 +556,13 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
                 return rc;
         }
         // h = silu(gate) * up, gate_up = W_gu . A8(RMSNorm(resid) * rms_ffn)
-        {
+        if (q2 && L.q2[kProjGateUp].w) {
+            k_rmsnorm_f32<<<1, 256, 0, s>>>(e->resid, L.rms_ffn, e->xn, H, c.rms_norm_eps);
+            if (int rc = eng_q2_gemv(L.q2[kProjGateUp], e->xn, e->gu, 2 * c.intermediate_size, H, false, s)) return rc;
+            k_silu_rows<<<static_cast<unsigned>((c.intermediate_size + 255) / 256), 256, 0, s>>>(e->gu, e->h,
+                                                                                                 c.intermediate_size, 1);
+            ASDSL_CUDA(cudaGetLastError());
+        } else {
             GemvArgs ga = base_args(c.intermediate_size, H, 32);
             ga.x = e->resid;
             ga.norm_w = L.rms_ffn;
@@ -512,7 +574,9 @@ int eng_enqueue_step(asdsl_b200_engine* e, bool with_lm) {
         }
         // resid += W_down . A8(h); sharded: this rank's partial, then the peer all-reduce
         // (every rank's partial summed in rank order, plus the residual)
-        if (e->vx) {
+        if (q2 && L.q2[kProjDown].w) {
+            if (int rc = eng_q2_gemv(L.q2[kProjDown], e->h, e->resid, H, c.intermediate_size, true, s)) return rc;
+        } else if (e->vx) {
             GemvArgs ga = base_args(H, c.intermediate_size, 32);
             ga.x = e->h;
             ga.y = e->part;
@@ -940,6 +1004,8 @@ int asdsl_b200_engine_create(const asdsl_b200_engine_config* cfg, asdsl_b200_eng
     for (auto& L : e->layers)
         if ((rc = eng_alloc(e, &L.rms_att, 4ull * c.hidden_size)) || (rc = eng_alloc(e, &L.rms_ffn, 4ull * c.hidden_size)))
             return fail(rc);
+    if ((rc = eng_alloc(e, &e->xn, 4ull * c.hidden_size)) || (rc = eng_alloc(e, &e->gu, 8ull * c.intermediate_size)))
+        return fail(rc);
     e->attn_chunks = (c.max_seq_len + asdsl::kAttnChunk - 1) / asdsl::kAttnChunk;
     // ASDSL_B200_ATTN_SPLIT=0: one CTA per head over every position (the split's baseline)
     if (const char* sp = std::getenv("ASDSL_B200_ATTN_SPLIT"))
@@ -971,6 +1037,8 @@ int asdsl_b200_engine_destroy(asdsl_b200_engine* e) {
     if (e->g_decode) cudaGraphExecDestroy(e->g_decode);
     if (e->g_prefill) cudaGraphExecDestroy(e->g_prefill);
     if (e->g_decode_long) cudaGraphExecDestroy(e->g_decode_long);
+    for (auto& gd : e->g_draft)
+        if (gd) cudaGraphExecDestroy(gd);
     if (e->g_prefill_long) cudaGraphExecDestroy(e->g_prefill_long);
     for (void* p : e->allocs)
         if (p) cudaFree(p);
@@ -1508,6 +1576,93 @@ int asdsl_b200_engine_set_shard(asdsl_b200_engine* e, asdsl_b200_vxchg* vx, asds
     return kOk;
 }
 
+// drop the captured draft-step graphs (the mask or the draft bank changed)
+static void eng_drop_draft_graphs(asdsl_b200_engine* e) {
+    for (auto& gd : e->g_draft) {
+        if (gd) cudaGraphExecDestroy(gd);
+        gd = nullptr;
+    }
+}
+
+int asdsl_b200_engine_set_skip_mask(asdsl_b200_engine* e, const uint8_t* mask, int n) {
+    ENG_CHECK(e);
+    if (n > 0 && !mask) return set_error(kEinval, "engine_set_skip_mask: null pointer");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    const int lim = n < 64 ? (n > 0 ? n : 0) : 64;
+    for (int i = 0; i < 64; ++i) e->skip[i] = i < lim ? mask[i] != 0 : false;
+    eng_drop_draft_graphs(e);
+    return kOk;
+}
+
+int asdsl_b200_engine_clear_skip_mask(asdsl_b200_engine* e) {
+    ENG_CHECK(e);
+    return asdsl_b200_engine_set_skip_mask(e, nullptr, 0);
+}
+
+int asdsl_b200_engine_set_projection_q2(asdsl_b200_engine* e, int layer, int which, const uint8_t* w_packed,
+                                        size_t w_bytes, const float* scales, const float* biases, size_t n_groups) {
+    ENG_CHECK(e);
+    if (layer < 0 || layer >= e->cfg.num_layers) return set_error(kErange, "engine_set_projection_q2: layer out of range");
+    if (which < 0 || which > 3) return set_error(kEinval, "engine_set_projection_q2: projection index must be 0..3");
+    if (!w_packed || !scales || !biases) return set_error(kEinval, "engine_set_projection_q2: null pointer");
+    int rows = 0, cols = 0;
+    proj_shape(e->cfg, which, &rows, &cols);
+    if (w_bytes != static_cast<size_t>(rows) * cols / 4 || n_groups != static_cast<size_t>(rows) * (cols / 32))
+        return set_error(kEinval, "engine_set_projection_q2: sizes do not match the projection (packed 2-bit, gs 32)");
+    DeviceGuard dg(e->device);
+    ASDSL_CUDA(cudaStreamSynchronize(e->stream));
+    Q2Proj& q = e->layers[layer].q2[which];
+    if (!q.w) {
+        if (int rc = eng_alloc(e, &q.w, w_bytes)) return rc;
+        if (int rc = eng_alloc(e, &q.s, 4 * n_groups)) return rc;
+        if (int rc = eng_alloc(e, &q.b, 4 * n_groups)) return rc;
+    }
+    ASDSL_CUDA(cudaMemcpy(q.w, w_packed, w_bytes, cudaMemcpyDefault));
+    ASDSL_CUDA(cudaMemcpy(q.s, scales, 4 * n_groups, cudaMemcpyDefault));
+    ASDSL_CUDA(cudaMemcpy(q.b, biases, 4 * n_groups, cudaMemcpyDefault));
+    const size_t smem = 4ull * (cols + cols / 32);
+    if (smem > 48 * 1024)
+        ASDSL_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(&asdsl::k_gemv_q2<true>),
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    eng_drop_draft_graphs(e);
+    return kOk;
+}
+
+int asdsl_b200_engine_forward_token_draft(asdsl_b200_engine* e, int token, int pos, float* logits, int32_t* argmax,
+                                          int use_q2) {
+    ENG_READY(e);
+    if (e->exact || e->persistent || e->vx)
+        return set_error(kEinval, "forward_token_draft: draft steps run in the fast per-op chain of one GPU");
+    if (token < 0 || token >= e->cfg.vocab_size)
+        return set_error(kErange, "forward_token: token_id out of vocab range");
+    if (pos < 0 || pos >= e->cfg.max_seq_len) return set_error(kErange, "forward_token: pos out of kv-cache range");
+    DeviceGuard dg(e->device);
+    if (int rc = eng_set_pos(e, pos, token)) return rc;
+    const bool lng = e->g_decode_long != nullptr && pos >= 256;
+    const int key = (use_q2 ? 2 : 0) + (lng ? 1 : 0);
+    if (!e->g_draft[key]) {
+        // first use of this kind: the step runs as enqueued, then its graph is captured for later ones
+        e->draft_skip = true;
+        e->draft_q2 = use_q2 != 0;
+        e->capture_long = lng;
+        int rc = eng_enqueue_step(e, true);
+        if (!rc) rc = eng_capture(e, true, &e->g_draft[key]);
+        e->draft_skip = e->draft_q2 = e->capture_long = false;
+        if (rc) return rc;
+    } else {
+        ASDSL_CUDA(cudaGraphLaunch(e->g_draft[key], e->stream));
+    }
+    if (e->host_pos >= 0 && e->host_pos < e->cfg.max_seq_len) ++e->host_pos;
+    if (logits)
+        ASDSL_CUDA(cudaMemcpyAsync(logits, e->logits, 4ull * e->cfg.vocab_size, cudaMemcpyDefault, e->stream));
+    if (argmax) ASDSL_CUDA(cudaMemcpyAsync(&e->h_stage[2], e->am_idx, 4, cudaMemcpyDeviceToHost, e->stream));
+    if (int rc = eng_status(e)) return rc;  // synchronizes the stream
+    if (argmax) *argmax = e->h_stage[2];
+    if (pos + 1 > e->kv_seq_len) e->kv_seq_len = pos + 1;
+    return kOk;
+}
+
 int asdsl_b200_engine_set_numerics(asdsl_b200_engine* e, int mode) {
     ENG_CHECK(e);
     if (e->finalized) return set_error(kEinval, "engine_set_numerics: engine already finalized");
@@ -1555,7 +1710,8 @@ int asdsl_b200_engine_reset_session(asdsl_b200_engine* e) {
     ASDSL_CUDA(cudaStreamSynchronize(e->stream));
     e->kv_seq_len = 0;
     e->snapshots.clear();
-    return kOk;
+    // as the reference's reset_session (unified_engine.cpp:1325-1337): the skip mask is cleared
+    return asdsl_b200_engine_clear_skip_mask(e);
 }
 
 int asdsl_b200_engine_get_kv_seq_len(asdsl_b200_engine* e, int* out) {

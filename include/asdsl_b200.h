@@ -133,6 +133,16 @@ int asdsl_b200_gemv_q4km(const uint8_t* weights_q4km, const float* x, float* y, 
 int asdsl_b200_gemv_q4_packed(const uint8_t* w_packed, const float* x, const float* scales, const float* biases,
                               float* y, int M, int K, int group_size, int batch, void* stream);
 
+/* 2-bit fp32-activation GEMVs (the QCSD draft bank): y[m] = sum_g scale[m,g] * dot(codes, x_g) +
+ * bias[m,g] * sum(x_g), codes 0..3.  _packed: four codes per byte (code j in bits 2j..2j+1),
+ * rows of K/4 bytes; _unpacked: one code per byte.  scales / biases fp32 [M][K/gs].  K <= 32768.
+ * Replace gemv_q2_packed_impl / gemv_q2_unpacked_impl (asdsl/kernels/native/gemv_q2_avx2.cpp:128-174,
+ * :53-118) and their bindings gemv_q2_packed / gemv_q2_unpacked (:346-372, :300-340). */
+int asdsl_b200_gemv_q2_packed(const uint8_t* w_packed, const float* x, const float* scales, const float* biases,
+                              float* y, int out_features, int in_features, int group_size, void* stream);
+int asdsl_b200_gemv_q2_unpacked(const uint8_t* w, const float* x, const float* scales, const float* biases,
+                                float* y, int out_features, int in_features, int group_size, void* stream);
+
 /* fp32-activation GEMV on unpacked (one code per byte) weights.
  * Replaces gemv_q4_unpacked_impl (asdsl/kernels/native/gemv_q4_avx2.cpp:755-806). */
 int asdsl_b200_gemv_q4_unpacked(const uint8_t* w, const float* x, const float* scales, const float* biases,
@@ -409,6 +419,22 @@ int asdsl_b200_engine_stream(asdsl_b200_engine* e, void** stream);
  * 1532-1598, :1628-1662) split over GPUs. */
 int asdsl_b200_engine_set_shard(asdsl_b200_engine* engine, asdsl_b200_vxchg* vxchg, asdsl_b200_xchg* xchg,
                                 int lm_rows, int lm_row_base);
+
+/* Draft steps (QCSD / SWIFT self-speculation, unified_engine.cpp:1790-1802, :1309-1322):
+ * set_skip_mask(mask, n) -- layers l < n with mask[l] != 0 are left out of draft steps (the
+ * reference's set_skip_mask; reset_session clears it, as there); set_projection_q2 -- the layer's
+ * 2-bit draft-bank projection (which: 0 qkv, 1 o, 2 gate_up, 3 down; packed codes [rows][cols/4],
+ * fp32 scales / biases [rows][cols/32]; the layers_dict keys q2_{qkv,o,gate_up,down}_{proj,scales,
+ * biases}, unified_engine.cpp:2387-2440); forward_token_draft -- one decode step at (token, pos) with
+ * the masked layers left out (forward_token_draft) and, with use_q2, the 2-bit projections in place
+ * of the 4-bit ones where set (forward_token_draft_q2), logits and/or argmax as forward_token.
+ * Fast numerics on one GPU (not with the reference-exact mode, the persistent kernel or a shard). */
+int asdsl_b200_engine_set_skip_mask(asdsl_b200_engine* engine, const uint8_t* mask, int n);
+int asdsl_b200_engine_clear_skip_mask(asdsl_b200_engine* engine);
+int asdsl_b200_engine_set_projection_q2(asdsl_b200_engine* engine, int layer, int which, const uint8_t* w_packed,
+                                        size_t w_bytes, const float* scales, const float* biases, size_t n_groups);
+int asdsl_b200_engine_forward_token_draft(asdsl_b200_engine* engine, int token, int pos, float* logits,
+                                          int32_t* argmax, int use_q2);
 
 /* Numerics of the decode step, set before finalize (no reference switch: the reference has one
  * numerics, its compiled code's).  ASDSL_B200_NUMERICS_FAST: the streaming kernels' own fp32

@@ -710,3 +710,70 @@ int or_engine_forward_token(or_engine_t* e, int token, int pos, float* logits) {
     }
     return 0;
 }
+
+/* 2-bit GEMVs of the QCSD draft bank (gemv_q2_avx2.cpp).  group_sum_x: eight interleaved lane
+ * sums of x per group folded by hsum256_ps, plus the tail (:138-148, :62-73); per row and group the
+ * dot of the codes with x, then row_sum += scale * dot + bias * group_sum_x (:154-173, :79-114).
+ * packed: code j of a byte in bits 2j..2j+1, four codes per x chunk summed as written (:163-168);
+ * unpacked: one code per byte, eight fma lanes folded by hsum256_ps plus the tail (:86-104). */
+static void q2_group_sums(const float* x, int K, int gs, float* gsum) {
+    const int ng = K / gs;
+    for (int g = 0; g < ng; ++g) {
+        const float* xg = x + g * gs;
+        float l[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        int j = 0;
+        for (; j + 8 <= gs; j += 8)
+            for (int k = 0; k < 8; ++k) l[k] += xg[j + k];
+        float sum = hsum8(l);
+        for (; j < gs; ++j) sum += xg[j];
+        gsum[g] = sum;
+    }
+}
+
+void or_gemv_q2_packed(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                       int M, int K, int gs) {
+    const int ng = K / gs, stride = K / 4;
+    float* gsum = (float*)malloc(sizeof(float) * (size_t)ng);
+    q2_group_sums(x, K, gs, gsum);
+    for (int m = 0; m < M; ++m) {
+        const uint8_t* row = w + (size_t)m * stride;
+        float row_sum = 0.0f;
+        for (int g = 0; g < ng; ++g) {
+            const int k0 = g * gs;
+            const size_t gi = (size_t)m * ng + g;
+            float dot = 0.0f;
+            for (int j = 0; j < gs; j += 4) {
+                const uint8_t b = row[(k0 + j) / 4];
+                const float v0 = (float)(b & 3), v1 = (float)((b >> 2) & 3), v2 = (float)((b >> 4) & 3),
+                            v3 = (float)((b >> 6) & 3);
+                dot += v0 * x[k0 + j] + v1 * x[k0 + j + 1] + v2 * x[k0 + j + 2] + v3 * x[k0 + j + 3];
+            }
+            row_sum += scales[gi] * dot + biases[gi] * gsum[g];
+        }
+        y[m] = row_sum;
+    }
+    free(gsum);
+}
+
+void or_gemv_q2_unpacked(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                         int M, int K, int gs) {
+    const int ng = K / gs;
+    float* gsum = (float*)malloc(sizeof(float) * (size_t)ng);
+    q2_group_sums(x, K, gs, gsum);
+    for (int m = 0; m < M; ++m) {
+        const uint8_t* row = w + (size_t)m * K;
+        float row_sum = 0.0f;
+        for (int g = 0; g < ng; ++g) {
+            const int k0 = g * gs;
+            float l[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int j = 0;
+            for (; j + 8 <= gs; j += 8)
+                for (int k = 0; k < 8; ++k) l[k] = fmaf((float)row[k0 + j + k], x[k0 + j + k], l[k]);
+            float dot = hsum8(l);
+            for (; j < gs; ++j) dot += (float)row[k0 + j] * x[k0 + j];
+            row_sum += scales[(size_t)m * ng + g] * dot + biases[(size_t)m * ng + g] * gsum[g];
+        }
+        y[m] = row_sum;
+    }
+    free(gsum);
+}

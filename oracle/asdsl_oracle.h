@@ -39,7 +39,12 @@ void or_gemv_q4_s256_q8(const uint8_t* blocks, const int8_t* xq, const float* xs
 void or_gemv_preq2_fused(const uint8_t* meta, const uint8_t* quant, const float* x, float* y, int M, int K);
 void or_gemv_q4km(const uint8_t* w, const float* x, float* y, int M, int K);   /* gemv_q4_avx2.cpp:357-420 */
 void or_gemv_q4_packed(const uint8_t* w, const float* x, const float* scales, const float* biases,
-                       float* y, int M, int K, int gs);             /* gemv_q4_avx2.cpp:665-749 */
+                       float* y, int M, int K, int gs);
+/* QCSD draft bank (gemv_q2_avx2.cpp:128-174, :53-118) */
+void or_gemv_q2_packed(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                       int M, int K, int gs);
+void or_gemv_q2_unpacked(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                         int M, int K, int gs);             /* gemv_q4_avx2.cpp:665-749 */
 
 /* Engine-side weight quantizers (unified_engine.cpp:320-400 and :411-461) */
 void or_lmhead_quant_q4_32_preq2(const uint16_t* w_f16, uint8_t* meta, uint8_t* quant, int rows, int cols);

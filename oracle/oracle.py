@@ -182,6 +182,14 @@ class Oracle:
                                    _p(y), _I(M), _I(K), _I(gs))
         return y
 
+    def gemv_q2(self, packed, w, x, s, b, M, K, gs):
+        y = np.zeros(M, np.float32)
+        f = self.lib.or_gemv_q2_packed if packed else self.lib.or_gemv_q2_unpacked
+        f(_p(np.ascontiguousarray(w, np.uint8)), _p(np.ascontiguousarray(x, np.float32)),
+          _p(np.ascontiguousarray(s, np.float32)), _p(np.ascontiguousarray(b, np.float32)), _p(y), _I(M), _I(K),
+          _I(gs))
+        return y
+
     # -- engine-side pieces
     def lmhead_quant_preq2(self, w_f16, rows, cols):
         w = np.ascontiguousarray(w_f16, np.float16).view(np.uint16)
@@ -369,6 +377,14 @@ class RefKernels:
         y = np.zeros(M, np.float32)
         self._chk(self.lib.ref_gemv_q4km(_p(np.ascontiguousarray(w)), _p(np.ascontiguousarray(x, np.float32)),
                                          _p(y), _I(M), _I(K)))
+        return y
+
+    def gemv_q2(self, packed, w, x, s, b, M, K, gs):
+        y = np.zeros(M, np.float32)
+        f = self.lib.ref_gemv_q2_packed if packed else self.lib.ref_gemv_q2_unpacked
+        self._chk(f(_p(np.ascontiguousarray(w, np.uint8)), _p(np.ascontiguousarray(x, np.float32)),
+                    _p(np.ascontiguousarray(s, np.float32)), _p(np.ascontiguousarray(b, np.float32)), _p(y), _I(M),
+                    _I(K), _I(gs)))
         return y
 
     def gemv_q4_packed(self, w, x, s, b, M, K, gs):

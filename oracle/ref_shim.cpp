@@ -41,6 +41,11 @@ void gemv_q4_packed_impl_v2(const uint8_t* w_packed, const float* x, const float
                             float* y, int M, int K, int group_size);
 void gemv_q4_unpacked_impl(const uint8_t* w, const float* x, const float* scales, const float* biases,
                            float* y, int M, int K, int group_size);
+// QCSD draft bank (asdsl/kernels/native/gemv_q2_kernels.h)
+void gemv_q2_packed_impl(const uint8_t* w_packed, const float* x, const float* scales, const float* biases,
+                         float* y, int M, int K, int group_size);
+void gemv_q2_unpacked_impl(const uint8_t* w, const float* x, const float* scales, const float* biases, float* y,
+                           int M, int K, int group_size);
 
 #define SHIM_TRY(expr)                                   \
     try {                                                \
@@ -90,6 +95,15 @@ int ref_gemv_q4_packed(const uint8_t* w, const float* x, const float* s, const f
 int ref_gemv_q4_unpacked(const uint8_t* w, const float* x, const float* s, const float* b, float* y,
                          int M, int K, int gs) {
     SHIM_TRY(gemv_q4_unpacked_impl(w, x, s, b, y, M, K, gs));
+}
+
+int ref_gemv_q2_packed(const uint8_t* w, const float* x, const float* s, const float* b, float* y, int M, int K,
+                       int gs) {
+    SHIM_TRY(gemv_q2_packed_impl(w, x, s, b, y, M, K, gs));
+}
+int ref_gemv_q2_unpacked(const uint8_t* w, const float* x, const float* s, const float* b, float* y, int M, int K,
+                         int gs) {
+    SHIM_TRY(gemv_q2_unpacked_impl(w, x, s, b, y, M, K, gs));
 }
 
 namespace {

@@ -527,3 +527,83 @@ def test_engine_long_context_attention_vs_oracle(native, oracle, numerics):
     finally:
         eng.close()
     assert native.device_status(clear=True) == 0
+
+
+def _q2_mirrored_model(seed):
+    """A TINY-shaped model whose 4-bit projections hold 2-bit codes (0..3), fp16 scale s and zero 1.5
+    per group, and whose draft bank holds the same codes with scale s and bias -1.5 s: both banks
+    are then the same dense weights, s * (code - 1.5), exactly."""
+    from asdsl_b200.inference.synthetic import TINY, build_model
+    from asdsl_b200.quantization import repack
+
+    model = build_model(TINY, seed=seed, norms_one=False)
+    c = model["config"]
+    rng = np.random.default_rng(seed + 100)
+    H, I = c["hidden"], c["inter"]
+    qd, kvd = c["n_heads"] * c["head_dim"], c["n_kv_heads"] * c["head_dim"]
+    for L in model["layers"]:
+        for name, (rows, cols) in (("qkv_proj", (qd + 2 * kvd, H)), ("o_proj", (H, qd)),
+                                   ("gate_up_proj", (2 * I, H)), ("down_proj", (H, I))):
+            codes = rng.integers(0, 4, size=(rows, cols), dtype=np.uint8)
+            s = (rng.integers(16, 48, size=rows * (cols // 32)) * 2.0 ** -12).astype(np.float32)
+            b = (-1.5 * s).astype(np.float32)
+            nib = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+            blocks = repack.repack_asymmetric_to_q4_32_blocks(nib.reshape(-1), s, b, rows, cols, 32)
+            meta, quant = repack.repack_preq_blocks_to_preq2(repack.blocks_to_flat(blocks), rows, cols)
+            L[name + "_meta"], L[name + "_quant"] = meta.reshape(-1), quant.reshape(-1)
+            q2 = (codes[:, 0::4] | (codes[:, 1::4] << 2) | (codes[:, 2::4] << 4) | (codes[:, 3::4] << 6)).astype(np.uint8)
+            short = name[:-5]
+            L["q2_" + name], L[f"q2_{short}_scales"], L[f"q2_{short}_biases"] = q2.reshape(-1), s, b
+    return model
+
+
+def test_engine_draft_skip_mask_equals_fewer_layers(native):
+    """forward_token_draft with layer 1 masked out is bitwise the step of a model without that layer
+    (unified_engine.cpp:1365-1367: a masked layer is skipped whole, KV write included); the mask
+    leaves forward_token alone and reset_session clears it (:1325-1337)."""
+    from asdsl_b200.inference.synthetic import TINY, build_model
+
+    model = build_model(dict(TINY, num_layers=3), seed=17, norms_one=False)
+    short = dict(model, config=dict(model["config"], num_layers=2), layers=[model["layers"][0], model["layers"][2]])
+    full, ref = _engine(model), _engine(short)
+    try:
+        toks = [3, 77, 5, 200, 9, 11]
+        full.set_skip_mask([False, True, False])
+        for pos, t in enumerate(toks):
+            a = full.forward_token_draft(t, pos).copy()
+            b = ref.forward_token(t, pos).copy()
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"draft step at {pos}"
+        full.reset_session()
+        ref3 = _engine(model)
+        try:
+            for pos, t in enumerate(toks[:3]):
+                a = full.forward_token_draft(t, pos).copy()  # mask cleared: all three layers
+                b = ref3.forward_token(t, pos).copy()
+                assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"cleared mask at {pos}"
+        finally:
+            ref3.close()
+    finally:
+        full.close()
+        ref.close()
+    assert native.device_status(clear=True) == 0
+
+
+def test_engine_draft_q2_bank_matches_the_same_dense_weights(native):
+    """forward_token_draft_q2 runs every projection from the 2-bit draft bank (fp32 activations,
+    gemv_q2_packed_impl) instead of the 4-bit weights (A8 activations): on a model where both banks
+    are the same dense weights the logits agree within the A8 quantization error (1e-2), and the
+    draft step's own kernels match the oracle's gemv_q2_packed on the step's inputs (test_q2.py)."""
+    from oracle.oracle import rel_err
+
+    model = _q2_mirrored_model(23)
+    eng = _engine(model)
+    try:
+        toks = [3, 77, 5, 200, 9, 11, 4, 2]
+        for pos, t in enumerate(toks):
+            a = eng.forward_token(t, pos).copy()
+            eng.truncate_kv(pos)
+            b = eng.forward_token_draft_q2(t, pos).copy()
+            assert rel_err(b, a) < 1e-2, f"step {pos}: {rel_err(b, a)}"
+    finally:
+        eng.close()
+    assert native.device_status(clear=True) == 0
