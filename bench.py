@@ -769,6 +769,65 @@ def stamp_summary(buf, names, world: int) -> list | None:
     return every
 
 
+def q2_bench(steps: int = 200) -> dict:
+    """The QCSD draft bank's 2-bit packed GEMV (asdsl_b200_gemv_q2_packed) at the Phi-4-mini
+    projection shapes: random codes, fp32 scales / biases (the bank's format), x ~ N(0, 1); back to
+    back in CUDA graphs over weight copies rotated past the L2; bytes = packed codes + 8 bytes of
+    scale and bias per 32-group + x + y.  Checked against the oracle's restatement first."""
+    import numpy as np
+    import torch
+
+    from asdsl_b200 import _lib
+    from oracle.oracle import Oracle, rel_err
+
+    out = []
+    s = torch.cuda.Stream()
+    for M, K in ((8192, 3072), (3072, 8192)):
+        rng = np.random.default_rng(M + K)
+        codes = rng.integers(0, 256, size=M * K // 4, dtype=np.uint8)
+        sc = rng.uniform(0.01, 0.03, M * (K // 32)).astype(np.float32)
+        bi = rng.uniform(-0.05, -0.01, M * (K // 32)).astype(np.float32)
+        x = rng.standard_normal(K).astype(np.float32)
+        dev = [torch.from_numpy(a).cuda() for a in (codes, sc, bi)]
+        xd, yd = torch.from_numpy(x).cuda(), torch.empty(M, device="cuda")
+        nbytes = codes.nbytes + sc.nbytes + bi.nbytes + 4 * (K + M)
+        copies = [dev] + [[t.clone() for t in dev] for _ in range(max(1, -(-320_000_000 // nbytes)) - 1)]
+
+        def run(cp):
+            _lib.call("asdsl_b200_gemv_q2_packed", cp[0].data_ptr(), xd.data_ptr(), cp[1].data_ptr(), cp[2].data_ptr(),
+                      yd.data_ptr(), M, K, 32, s.cuda_stream)
+
+        run(copies[0])
+        s.synchronize()
+        err = rel_err(yd.cpu().numpy(), Oracle().gemv_q2(True, codes, x, sc, bi, M, K, 32))
+        if err > 1e-3:
+            raise SystemExit(f"bench: q2 GEMV mismatch vs oracle ({err})")
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for cp in copies:
+                run(cp)
+        reps = max(1, steps // len(copies))
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        with torch.cuda.stream(s):
+            for _ in range(reps):
+                g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * len(copies))
+        peak, _ = _peaks()
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out.append({"M": M, "K": K, "us": round(us, 3), "bytes": nbytes, "gbs": round(gbs, 1),
+                    "frac": round(gbs / peak, 4), "rel_err_vs_oracle": err})
+        del g, copies
+    assert _lib.device_status(clear=True) == 0
+    return {"metric": "QCSD draft-bank 2-bit GEMV (packed, fp32 activations) HBM GB/s", "cases": out,
+            "config": {"workload": "q2_draft_gemv", "group_size": 32}}
+
+
 LM_METRIC = "lm_head W4 GEMV + argmax HBM GB/s (200064x3072 Q4_128, row-sharded, all ranks)"
 
 
@@ -1349,6 +1408,7 @@ def main():
 
     c0 = None if args.no_c0 else c0_bench(world, rank)
     c4 = c4_bench(rank) if (args.c4 and world == 1) else None
+    q2 = q2_bench() if (args.c4 and world == 1) else None
     decode = decode_fast = decode_sharded = None
     if not args.no_decode:
         from asdsl_b200.inference.synthetic import PHI4_MINI, build_model_device
@@ -1400,6 +1460,7 @@ def main():
             "clocks": clocks,
             "c0_gemv": c0,
             "c4_multi": c4,
+            "q2_draft_gemv": q2,
             "decode": decode,
             "decode_fast": decode_fast,
             "decode_sharded": decode_sharded,
