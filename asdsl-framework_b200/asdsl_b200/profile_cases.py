@@ -16,6 +16,7 @@ Cases (kernels they launch):
   weight_prep      k_quantize_groups, k_pack_preq2, k_q4_128_from_f32 on 8192x3072 fp32
   exact_gemv       k_stream_gemv<preq2 exact> (RMSNorm + A8 prologue), 16384x3072, the gate_up
                    + SiLU form (8192 pairs), then 5120x3072 (qkv) and 3072x3072 (o) without RMSNorm
+  q2               k_gemv_q2<packed> (the QCSD draft bank's 2-bit GEMV), 8192x3072
   xchg1            k_allreduce_peer and the lm_head argmax exchange with a world of one GPU
                    (the peer stores go to this GPU's own buffers)
 """
@@ -164,6 +165,18 @@ def case_packed(reps):
     for _ in range(reps):
         _lib.call("asdsl_b200_gemv_q4_packed", w.data_ptr(), x.data_ptr(), sc.data_ptr(), bi.data_ptr(), y.data_ptr(),
                   M, K, gs, 1, s)
+
+
+def case_q2(reps):
+    M, K = 8192, 3072
+    w = _bytes(M * K // 4, 1)
+    sc = _fp16_scales(M * (K // 32), 0.01, 0.03, 2).float()
+    bi = -_fp16_scales(M * (K // 32), 0.01, 0.05, 3).float()
+    x, y = _x(K, 4), torch.empty(M, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(reps):
+        _lib.call("asdsl_b200_gemv_q2_packed", w.data_ptr(), x.data_ptr(), sc.data_ptr(), bi.data_ptr(), y.data_ptr(),
+                  M, K, 32, s)
 
 
 def case_weight_prep(reps):

@@ -378,7 +378,7 @@ int gemv_q2_impl(bool packed, const uint8_t* w, const float* x, const float* sca
     if (smem > 48 * 1024)
         ASDSL_CUDA(cudaFuncSetAttribute(fnp, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     const unsigned grid = static_cast<unsigned>(
-        std::min<long long>((M + asdsl::kQ2Warps - 1) / asdsl::kQ2Warps, sm_count() * 8ll));
+        std::min<long long>((M + asdsl::kQ2Warps - 1) / asdsl::kQ2Warps, sm_count() * 2ll));  // x staged once per CTA
     if (packed)
         asdsl::k_gemv_q2<true><<<grid, asdsl::kQ2Warps * 32, smem, as_stream(stream)>>>(w, x, scales, biases, y, M, K, gs,
                                                                                       0);
@@ -900,7 +900,10 @@ int asdsl_b200_selftest_bounded_wait(int which, void* stream) {
 // call on a device get distinct slots.  Later streams share slots (assigned in turn), so
 // multi-token calls on more than kTokSlots streams of one device must not overlap.
 constexpr int kTokSlots = 8;
-constexpr size_t kTokSlotBytes = kSmemBudget / 2;
+// a slot holds the A8 areas of one pass; the pipeline keeps the rest of the shared-memory budget,
+// at least kMtMinRing bytes (two 20 KB stages at K = 8192), so 16 tokens of K = 8192 take one pass
+constexpr size_t kMtMinRing = 40 * 1024;
+constexpr size_t kTokSlotBytes = kSmemBudget - kBarBytes - kMtMinRing;
 static __device__ __align__(128) unsigned char g_tok_scratch[kTokSlots * kTokSlotBytes];
 
 namespace {
@@ -1017,9 +1020,10 @@ int asdsl_b200_gemv_multi(int fmt, const uint8_t* w0, const uint8_t* w1, const f
     } else {
         return set_error(kEinval, "gemv_multi: unsupported weight format");
     }
-    // tokens per pass: 16 at most, and their A8 areas within half of the shared-memory budget
+    // tokens per pass: 16 at most, and their A8 areas within a token-scratch slot (the pipeline
+    // keeps the rest of the shared memory)
     const uint32_t xa = xarea_layout_bytes(K, gs, false);
-    int per_pass = static_cast<int>((kSmemBudget / 2) / xa);
+    int per_pass = static_cast<int>(kTokSlotBytes / xa);
     if (per_pass > 16) per_pass = 16;
     if (per_pass < 1) per_pass = 1;
     const long long nb = (static_cast<long long>(M) + 3) / 4;

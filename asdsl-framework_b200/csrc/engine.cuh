@@ -445,7 +445,7 @@ int eng_launch_program(asdsl_b200_engine* e, bool with_lm) {
 int eng_q2_gemv(const Q2Proj& q, const float* x, float* y, int M, int K, bool accumulate, cudaStream_t s) {
     const size_t smem = 4ull * (K + K / 32);
     const unsigned grid = static_cast<unsigned>(std::min<long long>((M + asdsl::kQ2Warps - 1) / asdsl::kQ2Warps,
-                                                                    sm_count() * 8ll));
+                                                                    sm_count() * 2ll));
     asdsl::k_gemv_q2<true><<<grid, asdsl::kQ2Warps * 32, smem, s>>>(q.w, x, q.s, q.b, y, M, K, 32, accumulate ? 1 : 0);
     ASDSL_CUDA(cudaGetLastError());
     return kOk;
