@@ -3,6 +3,8 @@
 on the device (seeded), runs `--reps` launches of its kernels on one stream and exits 0.
 
 Cases (kernels they launch):
+  decode_exact / decode_fast   the config-3 decode step (32-layer Phi-4-mini, seed 3, C0 weights
+                   quantized on the device), `--reps` graph replays from position 0
   attention        k_attention_split (decode at 1024 cached positions, Phi-4-mini heads; with
                    ASDSL_B200_ATTN_SPLIT=0 the one-CTA-per-head k_attention), and on the way
                    k_attention_rows / k_kv_write_rows / k_quant_tokens / k_stream_gemv<..,NT>
@@ -73,6 +75,27 @@ def _engine_case(numerics: str, reps: int):
             eng.forward_token_argmax(prompt[i % 7], 1024 + i)
     finally:
         eng.close()
+
+
+def _decode_case(numerics: str, reps: int):
+    from asdsl_b200.inference.synthetic import PHI4_MINI, build_model_device
+    from asdsl_b200.kernels._native_unified import engine_from_model
+
+    model = build_model_device(PHI4_MINI, seed=3, quantized=True)
+    eng = engine_from_model(model, numerics=numerics)
+    try:
+        eng.set_position(0, 1)
+        eng.replay(reps)
+    finally:
+        eng.close()
+
+
+def case_decode_exact(reps):
+    _decode_case("reference_exact", reps)
+
+
+def case_decode_fast(reps):
+    _decode_case("fast", reps)
 
 
 def case_attention(reps):
