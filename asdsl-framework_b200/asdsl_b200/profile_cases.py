@@ -11,6 +11,7 @@ Cases (kernels they launch):
                    (the batched prefill of those positions)
   attention_exact  k_attention_exact (reference-exact mode, positions < 256) and, from position 256,
                    k_attention_exact_scores + k_attention_exact_sums (1024 cached positions)
+  attention_exact_short  k_attention_exact at 64 cached positions (the short-cache form)
   multi            k_stream_gemv<preq, .., NT=8> (dp4a lanes) at 3072x8192, 16 tokens
   multi_mma        k_stream_gemv_mma (int8 mma.sync, selected from 5 tokens) at 8192x3072, 16 tokens
   gemm128          k_gemm_q4_128 (prompt GEMM), 16384x3072, 8 rows
@@ -61,7 +62,7 @@ def _x(K: int, seed: int, rows: int = 1) -> torch.Tensor:
     return torch.randn(rows * K, device="cuda", generator=g)
 
 
-def _engine_case(numerics: str, reps: int):
+def _engine_case(numerics: str, reps: int, cached: int = 1024):
     from asdsl_b200.inference.synthetic import PHI4_MINI, build_model_device
     from asdsl_b200.kernels._native_unified import engine_from_model
 
@@ -69,12 +70,16 @@ def _engine_case(numerics: str, reps: int):
     model = build_model_device(cfg, seed=5, norms_one=False)
     eng = engine_from_model(model, numerics=numerics)
     try:
-        prompt = np.random.default_rng(5).integers(0, cfg["vocab"], size=1024).tolist()
+        prompt = np.random.default_rng(5).integers(0, cfg["vocab"], size=cached).tolist()
         eng.forward_batch(prompt, 0)
         for i in range(reps):
-            eng.forward_token_argmax(prompt[i % 7], 1024 + i)
+            eng.forward_token_argmax(prompt[i % 7], cached + i)
     finally:
         eng.close()
+
+
+def case_attention_exact_short(reps):
+    _engine_case("reference_exact", reps, cached=64)
 
 
 def _decode_case(numerics: str, reps: int):
