@@ -34,6 +34,8 @@ _SIGS = {
     "asdsl_b200_version": [],
     "asdsl_b200_last_error": [],
     "asdsl_b200_device_status": [_P, _I],
+    "asdsl_b200_timeline_set": [_P, ctypes.c_uint],
+    "asdsl_b200_timeline_count": [_P],
     "asdsl_b200_selftest_bounded_wait": [_I, _P],
     "asdsl_b200_set_launch_policy": [_I, _I],
     "asdsl_b200_set_mma_min_tokens": [_I],

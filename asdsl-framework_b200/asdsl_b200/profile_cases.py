@@ -20,6 +20,8 @@ Cases (kernels they launch):
   exact_gemv       k_stream_gemv<preq2 exact> (RMSNorm + A8 prologue), 16384x3072, the gate_up
                    + SiLU form (8192 pairs), then 5120x3072 (qkv) and 3072x3072 (o) without RMSNorm
   q2               k_gemv_q2<packed> (the QCSD draft bank's 2-bit GEMV), 8192x3072
+  timeline         per-CTA phase timelines (asdsl_b200.timeline) of back-to-back config-0 GEMVs
+                   and of the decode graphs in both numerics modes
   xchg1            k_allreduce_peer and the lm_head argmax exchange with a world of one GPU
                    (the peer stores go to this GPU's own buffers)
 """
@@ -260,6 +262,62 @@ def case_xchg1(reps):
     finally:
         torch.cuda.synchronize()
         head.close()
+
+
+def case_timeline(reps):
+    """Per-CTA timelines (asdsl_b200.timeline): 16 back-to-back config-0 GEMVs (preq2 gs32
+    16384x3072, random bytes, 6 copies rotated past the L2) in a CUDA graph, then `reps` decode
+    graph replays of the 32-layer Phi-4-mini shape in both numerics modes; prints the per-kernel
+    means of each phase."""
+    from asdsl_b200.inference.synthetic import PHI4_MINI, build_model_device
+    from asdsl_b200.kernels._native_unified import engine_from_model
+    from asdsl_b200.timeline import Timeline, format_chain
+
+    M, K = 16384, 3072
+    copies = [_preq2(M, K, 10 + 3 * i) for i in range(6)]
+    x, y = _x(K, 3), torch.empty(M, device="cuda")
+    st = torch.cuda.Stream()
+
+    def run(c):
+        _lib.call("asdsl_b200_gemv_preq2_fused", c[0].data_ptr(), c[1].data_ptr(), x.data_ptr(), y.data_ptr(), M, K,
+                  32, st.cuda_stream)
+
+    with torch.cuda.stream(st):
+        for c in copies:
+            run(c)
+    st.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for i in range(16):
+            run(copies[i % len(copies)])
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    with Timeline() as tl:
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+    print(f"config-0 GEMV, 32 launches in graphs ({len(tl.recs)} records, {tl.dropped} dropped)")
+    print(format_chain(tl.launches()))
+    del g, copies
+    torch.cuda.empty_cache()
+    for numerics in ("fast", "reference_exact"):
+        model = build_model_device(PHI4_MINI, seed=3, quantized=True)
+        eng = engine_from_model(model, numerics=numerics)
+        try:
+            eng.set_position(0, 1)
+            eng.replay(3)
+            torch.cuda.synchronize()
+            with Timeline() as tl:
+                eng.replay(max(reps, 1))
+                torch.cuda.synchronize()
+        finally:
+            eng.close()
+            del model
+            torch.cuda.empty_cache()
+        print(f"decode {numerics}, {max(reps, 1)} graph replays ({len(tl.recs)} records, {tl.dropped} dropped); "
+              "[0..3] = qkv, o, gate_up, down")
+        print(format_chain(tl.launches(), period=4))
 
 
 CASES = {name[5:]: fn for name, fn in globals().items() if name.startswith("case_")}

@@ -164,6 +164,26 @@ int asdsl_b200_device_status(unsigned int* status, int clear) {
     return kOk;
 }
 
+int asdsl_b200_timeline_set(void* buf, unsigned int capacity) {
+    if (buf == nullptr) capacity = 0;
+    if (buf != nullptr && (capacity == 0 || (reinterpret_cast<uintptr_t>(buf) & 15u)))
+        return set_error(kEinval, "timeline_set: need a 16-byte aligned device buffer and a capacity");
+    ASDSL_CUDA(cudaDeviceSynchronize());
+    TlRec* b = static_cast<TlRec*>(buf);
+    const uint32_t cap = capacity, zero = 0;
+    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_buf, &b, sizeof(b)));
+    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_cap, &cap, sizeof(cap)));
+    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_n, &zero, sizeof(zero)));
+    return kOk;
+}
+
+int asdsl_b200_timeline_count(unsigned int* n) {
+    if (!n) return set_error(kEinval, "timeline_count: null pointer");
+    ASDSL_CUDA(cudaDeviceSynchronize());
+    ASDSL_CUDA(cudaMemcpyFromSymbol(n, g_tl_n, sizeof(*n)));
+    return kOk;
+}
+
 int asdsl_b200_quantize_activation(const float* x, int8_t* xq, float* xs, int32_t* xsum, int K, int gs,
                                    void* stream) {
     if (!x || !xq || !xs) return set_error(kEinval, "quantize_activation: null pointer");

@@ -165,7 +165,49 @@ struct GemvArgs {
     // reference-exact mode (kProRmsA8X, kEpiSiluX): the host CPU's RSQRTSS / RCPPS tables
     ExactTabs ex;
     int exact_inter;  // kFmtPreq2X*: the weights are in the exact (group-interleaved) layout
+    unsigned int tl_id;  // host-side launch number, carried into the timeline records
 };
+
+// ---------------------------------------------------------------------------
+// Optional per-CTA timeline of the streaming GEMVs (asdsl_b200_timeline_set): while a buffer is
+// set, one thread per event appends {event | kernel template << 4, launch number, block | SM << 20,
+// %globaltimer} at an atomic cursor.  The counterpart of the reference's ASDSL_ENGINE_PROFILE
+// breakdown for the per-op chain; off (null buffer) by default.
+// ---------------------------------------------------------------------------
+struct TlRec {
+    uint32_t code, id, where, pad;
+    unsigned long long t, pad2;
+};
+__device__ TlRec* g_tl_buf = nullptr;
+__device__ uint32_t g_tl_cap = 0;
+__device__ uint32_t g_tl_n = 0;
+enum TlEvent : uint32_t {
+    kTlStart = 1,     // CTA initialized (barriers set up)
+    kTlWaited = 2,    // consumers past the dependency wait (previous kernel complete)
+    kTlPrologue = 3,  // activation prologue done
+    kTlConsumed = 4,  // consumer warp 0 through its last work item
+    kTlEnd = 5,       // every consumer warp done
+    kTlProduced = 6,  // producer issued its last copy
+};
+
+template <int FMT, int PRO, int EPI, int NT>
+__device__ __forceinline__ void tl_rec(uint32_t ev, uint32_t id) {
+    TlRec* b = g_tl_buf;
+    if (b == nullptr) return;
+    const uint32_t i = atomicAdd(&g_tl_n, 1u);
+    if (i >= g_tl_cap) return;
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    TlRec r;
+    r.code = ev | (static_cast<uint32_t>(FMT) << 4) | (static_cast<uint32_t>(PRO) << 8) |
+             (static_cast<uint32_t>(EPI) << 12) | (static_cast<uint32_t>(NT) << 16);
+    r.id = id;
+    r.where = blockIdx.x | (smid << 20);
+    r.pad = 0;
+    r.t = globaltimer_ns();
+    r.pad2 = 0;
+    b[i] = r;
+}
 
 // ---------------------------------------------------------------------------
 // chunk geometry (shared by producer and consumers)
@@ -1343,6 +1385,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     __syncthreads();
     // let a dependent kernel launch now; it touches our outputs only after its own wait
     grid_launch_dependents();
+    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlStart, ga.tl_id);
 
     if (warp == kProducerWarp) {
         if (lane != 0) return;
@@ -1350,6 +1393,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
         const uint64_t pol = l2_policy_evict_first();
         int jg = 0;
         produce_chunks<NS, NSEG>(pa, u0, u1, stages, pa.stage_bytes, S, full, empty, jg, ga.status, pol);
+        tl_rec<FMT, PRO, EPI, NT>(kTlProduced, ga.tl_id);
         drain_ring(full, S, jg, ga.status);
         return;
     }
@@ -1357,6 +1401,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     // ---------------- consumer warps: every warp takes part of every stage ----------------
     const int cw = warp;
     grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
+    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlWaited, ga.tl_id);
     if constexpr (EPI == kEpiArgmax) {
         if (ga.xchg_stamps != nullptr && blockIdx.x == 0 && threadIdx.x == 0)
             ga.xchg_stamps[((*ga.xchg_epoch + 1) & ga.xchg_stamp_mask) * 4] = globaltimer_ns();
@@ -1368,6 +1413,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     } else {
         token_prologue<PRO>(ga, smem + pa.xarea_off, xa_stride);
     }
+    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlPrologue, ga.tl_id);
 
     XAddr xad;
     xad.x8 = kF32 ? 0u : smem_u32(xa.x8);
@@ -1388,6 +1434,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
         } else
             consume_chunks<FMT, PRO, EPI, NT>(pa, ga, xa, xad, xa_stride, u0, u1, stages, pa.stage_bytes, S, full,
                                               empty, s_part, s_cnt, jg, best_v, best_i);
+    }
+    if (g_tl_buf != nullptr) {
+        if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlConsumed, ga.tl_id);
+        consumer_sync();
+        if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlEnd, ga.tl_id);
     }
 
     if constexpr (EPI == kEpiArgmax) {

@@ -1,6 +1,7 @@
 // launch.cuh -- host-side planning and launch of the streaming GEMV family.
 #pragma once
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -290,6 +291,10 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
 
     ga.status = device_status_ptr();
     if (!ga.status) return set_error(kEcuda, "cannot resolve the device status word");
+    {
+        static std::atomic<unsigned int> launches{0};
+        ga.tl_id = launches.fetch_add(1u, std::memory_order_relaxed);
+    }
 
     auto kern = k_stream_gemv<FMT, PRO, EPI, NT>;
     {

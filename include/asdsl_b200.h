@@ -59,6 +59,15 @@ int asdsl_b200_set_mma_min_tokens(int n_tokens);
  * set by kernels whose bounded waits gave up.  Synchronizes the device. */
 int asdsl_b200_device_status(unsigned int* status, int clear);
 
+/* Per-CTA timeline of the streaming GEMVs, the counterpart of the reference's ASDSL_ENGINE_PROFILE
+ * stage breakdown (asdsl/kernels/native/unified_engine.cpp:74-90, :1675): while
+ * buf (device memory, 16-byte aligned, capacity records of 32 bytes) is set, every CTA appends
+ * {event | template << 4, launch number, block | SM << 20, pad, %globaltimer ns, pad} records for
+ * its start, dependency wait, prologue, consumers' end and producer's last copy (events 1-6).
+ * buf = NULL turns it off.  timeline_count gives the records appended (may exceed capacity). */
+int asdsl_b200_timeline_set(void* buf, unsigned int capacity);
+int asdsl_b200_timeline_count(unsigned int* n);
+
 /* Self-test of the failure detection (no reference counterpart): runs one wait that nothing
  * ever completes -- which 0: an mbarrier of the streaming pipeline, 1: a cross-GPU exchange
  * word -- and returns ASDSL_B200_ETIMEOUT once the 2 s limit made it give up and set its

@@ -1,0 +1,77 @@
+"""Host logic of the per-CTA GEMV timeline (asdsl_b200.timeline): grouping records into launch
+instances (graph replays reuse launch numbers) and the chain figures.  CPU only; the device side
+is exercised by the GPU test below."""
+
+import numpy as np
+import pytest
+
+from asdsl_b200.timeline import (END, PROLOGUE, PRODUCED, REC, START, WAITED, CONSUMED, chain_rows,
+                                 group_launches, summarize)
+
+
+def _recs(launches):
+    """launches: [(launch number, t0 ns)] each with 3 CTAs and fixed phase offsets"""
+    out = []
+    for lid, t0 in launches:
+        for b in range(3):
+            for ev, dt in ((START, 0), (WAITED, 500), (PROLOGUE, 800), (CONSUMED, 4000 + 10 * b),
+                           (END, 4100 + 10 * b), (PRODUCED, 3000)):
+                out.append((ev | (0 << 4) | (2 << 8) | (1 << 12) | (1 << 16), lid, b | (b << 20), 0, t0 + dt + b, 0))
+    r = np.array(out, dtype=REC)
+    return r[np.random.default_rng(0).permutation(len(r))]  # atomic order is not time order
+
+
+def test_group_launches_replays_and_chain():
+    # a graph of launches 7, 8 replayed twice: four instances
+    recs = _recs([(7, 0), (8, 5000), (7, 10000), (8, 15000)])
+    ls = group_launches(recs)
+    assert [(d["id"], d["instance"]) for d in ls] == [(7, 0), (8, 0), (7, 1), (8, 1)]
+    assert all(d["ctas"] == 3 for d in ls)
+    assert ls[0]["kernel"] == "k_stream_gemv<0,2,1,1>"
+    rows = chain_rows(ls)
+    assert rows[0]["span"] == pytest.approx((4100 + 20 + 2) / 1e3)
+    assert rows[1]["start_after_prev_end"] == pytest.approx((5000 - 4122) / 1e3)
+    assert rows[1]["waited_after_prev_end"] == pytest.approx((5500 - 4122) / 1e3)
+    assert rows[0]["prologue"] == pytest.approx(0.3)
+    s = summarize(rows)
+    assert s["k_stream_gemv<0,2,1,1>"]["launches"] == 4
+
+
+def test_timeline_exports():
+    from asdsl_b200 import _lib
+
+    for name in ("asdsl_b200_timeline_set", "asdsl_b200_timeline_count"):
+        assert name in _lib._SIGS
+
+
+@pytest.mark.gpu
+def test_timeline_records_every_cta(native):
+    import ctypes
+
+    import torch
+
+    from asdsl_b200 import _lib
+    from asdsl_b200.timeline import Timeline
+
+    M, K = 4096, 3072
+    meta = torch.randint(0, 256, (M * (K // 32) * 4,), dtype=torch.uint8, device="cuda")
+    meta.view(torch.float16)[:] = 0.01
+    quant = torch.randint(0, 256, ((M // 4) * (K // 32) * 64,), dtype=torch.uint8, device="cuda")
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(M, device="cuda")
+    with Timeline(capacity=1 << 16) as tl:
+        for _ in range(3):
+            _lib.call("asdsl_b200_gemv_preq2_fused", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), y.data_ptr(),
+                      M, K, 32, None)
+        torch.cuda.synchronize()
+    ls = tl.launches()
+    assert tl.dropped == 0 and len(ls) == 3
+    for d in ls:
+        assert d["start_min"] <= d["waited_min"] <= d["prologue_max"] <= d["end_max"]
+        assert d["ctas"] == min(torch.cuda.get_device_properties(0).multi_processor_count, M // 4)
+    # off again: no records
+    n = ctypes.c_uint(0)
+    _lib.call("asdsl_b200_gemv_preq2_fused", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), y.data_ptr(), M, K, 32,
+              None)
+    _lib.call("asdsl_b200_timeline_count", ctypes.byref(n))
+    assert n.value == 0
