@@ -35,7 +35,7 @@ _SIGS = {
     "asdsl_b200_last_error": [],
     "asdsl_b200_device_status": [_P, _I],
     "asdsl_b200_timeline_set": [_P, ctypes.c_uint],
-    "asdsl_b200_timeline_count": [_P],
+    "asdsl_b200_timeline_bytes": [ctypes.c_uint],
     "asdsl_b200_selftest_bounded_wait": [_I, _P],
     "asdsl_b200_set_launch_policy": [_I, _I],
     "asdsl_b200_set_mma_min_tokens": [_I],
@@ -126,6 +126,7 @@ class EngineConfigC(ctypes.Structure):
     ]
 _RESTYPES = {
     "asdsl_b200_version": ctypes.c_char_p,
+    "asdsl_b200_timeline_bytes": _SZ,
     "asdsl_b200_last_error": ctypes.c_char_p,
     "asdsl_b200_argmax_scratch_bytes": _SZ,
     "asdsl_b200_xchg_handle_bytes": _SZ,

@@ -299,7 +299,56 @@ def case_timeline(reps):
         torch.cuda.synchronize()
     print(f"config-0 GEMV, 32 launches in graphs ({len(tl.recs)} records, {tl.dropped} dropped)")
     print(format_chain(tl.launches()))
-    del g, copies
+    # two kernel templates alternating in one graph: the config-0 GEMV and the same weights in the
+    # reference-exact form (another function, same shape)
+    nw = torch.ones(K, device="cuda")
+
+    def run_x(c):
+        _lib.call("asdsl_b200_gemv_preq2_fused_exact", c[0].data_ptr(), c[1].data_ptr(), x.data_ptr(), None,
+                  ctypes.c_float(0.0), y.data_ptr(), M, K, st.cuda_stream)
+
+    with torch.cuda.stream(st):
+        for c in copies:
+            run_x(c)
+    st.synchronize()
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=st):
+        for i in range(16):
+            (run if i % 2 == 0 else run_x)(copies[i % len(copies)])
+    for _ in range(3):
+        g2.replay()
+    torch.cuda.synchronize()
+    with Timeline() as tl:
+        for _ in range(2):
+            g2.replay()
+        torch.cuda.synchronize()
+    print("config-0 GEMV alternating with its reference-exact form, in graphs")
+    print(format_chain(tl.launches()))
+    # the config-1 layer chain (qkv, o, gate_up + SiLU, down) captured by torch
+    from asdsl_b200.layer import build_c1_device, from_host
+
+    host = build_c1_device(1)
+    base = from_host(host)
+    layers = [base] + [base.clone() for _ in range(5)]
+    xl = torch.from_numpy(host["x"]).cuda()
+    for L in layers:
+        with torch.cuda.stream(st):
+            L.step(xl)
+    st.synchronize()
+    g3 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g3, stream=st):
+        for L in layers:
+            L.step(xl)
+    for _ in range(3):
+        g3.replay()
+    torch.cuda.synchronize()
+    with Timeline() as tl:
+        for _ in range(2):
+            g3.replay()
+        torch.cuda.synchronize()
+    print("config-1 layer chain (torch graph); [0..3] = qkv, o, gate_up, down")
+    print(format_chain(tl.launches(), period=4))
+    del g, g2, g3, copies, layers, base
     torch.cuda.empty_cache()
     for numerics in ("fast", "reference_exact"):
         model = build_model_device(PHI4_MINI, seed=3, quantized=True)

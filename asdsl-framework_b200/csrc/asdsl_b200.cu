@@ -164,24 +164,23 @@ int asdsl_b200_device_status(unsigned int* status, int clear) {
     return kOk;
 }
 
-int asdsl_b200_timeline_set(void* buf, unsigned int capacity) {
-    if (buf == nullptr) capacity = 0;
-    if (buf != nullptr && (capacity == 0 || (reinterpret_cast<uintptr_t>(buf) & 15u)))
-        return set_error(kEinval, "timeline_set: need a 16-byte aligned device buffer and a capacity");
+int asdsl_b200_timeline_set(void* buf, unsigned int slots_per_block) {
+    if (buf != nullptr && (slots_per_block == 0 || (reinterpret_cast<uintptr_t>(buf) & 15u)))
+        return set_error(kEinval, "timeline_set: need a 16-byte aligned device buffer and a slot count");
     ASDSL_CUDA(cudaDeviceSynchronize());
-    TlRec* b = static_cast<TlRec*>(buf);
-    const uint32_t cap = capacity, zero = 0;
-    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_buf, &b, sizeof(b)));
-    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_cap, &cap, sizeof(cap)));
-    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_n, &zero, sizeof(zero)));
+    // buffer: [kTlMaxBlocks] uint32 slot counters, then the records [kTlMaxBlocks][slots][kTlEvents]
+    uint32_t* cnt = static_cast<uint32_t*>(buf);
+    TlRec* recs = buf ? reinterpret_cast<TlRec*>(static_cast<uint8_t*>(buf) + 4 * kTlMaxBlocks) : nullptr;
+    const uint32_t slots = buf ? slots_per_block : 0u;
+    if (buf) ASDSL_CUDA(cudaMemset(buf, 0, 4 * kTlMaxBlocks));
+    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_cnt, &cnt, sizeof(cnt)));
+    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_slots, &slots, sizeof(slots)));
+    ASDSL_CUDA(cudaMemcpyToSymbol(g_tl_buf, &recs, sizeof(recs)));
     return kOk;
 }
 
-int asdsl_b200_timeline_count(unsigned int* n) {
-    if (!n) return set_error(kEinval, "timeline_count: null pointer");
-    ASDSL_CUDA(cudaDeviceSynchronize());
-    ASDSL_CUDA(cudaMemcpyFromSymbol(n, g_tl_n, sizeof(*n)));
-    return kOk;
+size_t asdsl_b200_timeline_bytes(unsigned int slots_per_block) {
+    return 4ull * kTlMaxBlocks + sizeof(TlRec) * kTlEvents * static_cast<size_t>(kTlMaxBlocks) * slots_per_block;
 }
 
 int asdsl_b200_quantize_activation(const float* x, int8_t* xq, float* xs, int32_t* xsum, int K, int gs,

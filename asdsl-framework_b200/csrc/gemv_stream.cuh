@@ -170,43 +170,61 @@ struct GemvArgs {
 
 // ---------------------------------------------------------------------------
 // Optional per-CTA timeline of the streaming GEMVs (asdsl_b200_timeline_set): while a buffer is
-// set, one thread per event appends {event | kernel template << 4, launch number, block | SM << 20,
-// %globaltimer} at an atomic cursor.  The counterpart of the reference's ASDSL_ENGINE_PROFILE
-// breakdown for the per-op chain; off (null buffer) by default.
+// set, every CTA takes the next slot of its block (one atomic on a per-block counter, so CTAs do
+// not contend) and one thread per event writes {%globaltimer, event | kernel template << 4,
+// launch number} into record [block][slot][event].  The counterpart of the reference's
+// ASDSL_ENGINE_PROFILE breakdown for the per-op chain; off (null buffer) by default.
 // ---------------------------------------------------------------------------
 struct TlRec {
-    uint32_t code, id, where, pad;
-    unsigned long long t, pad2;
+    unsigned long long t;
+    uint32_t code, id;
 };
-__device__ TlRec* g_tl_buf = nullptr;
-__device__ uint32_t g_tl_cap = 0;
-__device__ uint32_t g_tl_n = 0;
+constexpr int kTlEvents = 16;     // record slots per CTA (events 0..9 used)
+constexpr int kTlMaxBlocks = 1024;
+__device__ TlRec* g_tl_buf = nullptr;  // [kTlMaxBlocks][slots][kTlEvents]
+__device__ uint32_t* g_tl_cnt = nullptr;  // [kTlMaxBlocks] slots taken per block
+__device__ uint32_t g_tl_slots = 0;
 enum TlEvent : uint32_t {
+    kTlReduced = 0,   // RMSNorm prologues: the sum of squares reduced (thread 0)
     kTlStart = 1,     // CTA initialized (barriers set up)
     kTlWaited = 2,    // consumers past the dependency wait (previous kernel complete)
     kTlPrologue = 3,  // activation prologue done
     kTlConsumed = 4,  // consumer warp 0 through its last work item
     kTlEnd = 5,       // every consumer warp done
     kTlProduced = 6,  // producer issued its last copy
+    kTlXLoaded = 7,   // thread 0's first activation values arrived (prologue)
+    kTlFirstFull = 8, // consumer thread 0 past the full barrier of the CTA's first chunk
+    kTlLastFull = 9,  // ... and of its last chunk (all of the CTA's weights landed)
 };
 
-template <int FMT, int PRO, int EPI, int NT>
-__device__ __forceinline__ void tl_rec(uint32_t ev, uint32_t id) {
-    TlRec* b = g_tl_buf;
-    if (b == nullptr) return;
-    const uint32_t i = atomicAdd(&g_tl_n, 1u);
-    if (i >= g_tl_cap) return;
+// a CTA's timeline slot with its record code and launch number (slot ~0u: off)
+struct TlCtx {
+    uint32_t slot, code, id;
+};
+
+// the CTA's slot (thread 0, before the CTA's first barrier), or ~0u when off / full
+__device__ __forceinline__ uint32_t tl_slot() {
+    if (g_tl_buf == nullptr || blockIdx.x >= static_cast<unsigned>(kTlMaxBlocks)) return ~0u;
+    const uint32_t k = atomicAdd(g_tl_cnt + blockIdx.x, 1u);
+    return k < g_tl_slots ? k : ~0u;
+}
+
+__device__ __forceinline__ void tl_put(const TlCtx& c, uint32_t ev) {
+    if (c.slot == ~0u) return;
     uint32_t smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     TlRec r;
-    r.code = ev | (static_cast<uint32_t>(FMT) << 4) | (static_cast<uint32_t>(PRO) << 8) |
-             (static_cast<uint32_t>(EPI) << 12) | (static_cast<uint32_t>(NT) << 16);
-    r.id = id;
-    r.where = blockIdx.x | (smid << 20);
-    r.pad = 0;
     r.t = globaltimer_ns();
-    r.pad2 = 0;
-    b[i] = r;
+    r.code = ev | c.code | (smid << 24);
+    r.id = c.id;
+    g_tl_buf[(static_cast<size_t>(blockIdx.x) * g_tl_slots + c.slot) * kTlEvents + ev] = r;
+}
+
+template <int FMT, int PRO, int EPI, int NT>
+__device__ __forceinline__ void tl_rec(uint32_t slot, uint32_t ev, uint32_t id) {
+    constexpr uint32_t code = (static_cast<uint32_t>(FMT) << 4) | (static_cast<uint32_t>(PRO) << 8) |
+                              (static_cast<uint32_t>(EPI) << 12) | (static_cast<uint32_t>(NT) << 16);
+    tl_put(TlCtx{slot, code, id}, ev);
 }
 
 // ---------------------------------------------------------------------------
@@ -325,8 +343,14 @@ __device__ __forceinline__ float load_x1(const float* p) {
     else return __ldg(p);
 }
 
+// quads of the activation per consumer thread held in registers by the prologue (up to K = 8192)
+constexpr int kRegIters = 4;
+
+// nw_pre: the RMSNorm weights of this thread's quads (k * kConsumerThreads + ctid), already
+// loaded, or null (then they are loaded here)
 template <int PRO, bool kCoherent = false>
-__device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
+__device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid, const float4* nw_pre = nullptr,
+                             TlCtx tl = TlCtx{~0u, 0u, 0u}) {
     const int K = ga.K;
     const int lane = ctid & 31;
 
@@ -355,7 +379,6 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
         const int tpg = gs >> 2;  // threads per A8 group: 8 or 32
         // up to K = 8192 every thread's quads are loaded once, into registers: the RMSNorm sum of
         // squares and the quantization then share one round trip to memory
-        constexpr int kRegIters = 4;
         const bool in_regs = (PRO != kProQ8) && nquads <= kRegIters * kConsumerThreads;
         float4 xr[kRegIters];
         if (in_regs) {
@@ -364,6 +387,10 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
                 const int t = k * kConsumerThreads + ctid;
                 xr[k] = (t < nquads) ? load_x4<kCoherent>(reinterpret_cast<const float4*>(ga.x) + t)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (tl.slot != ~0u && ctid == 0) {
+                asm volatile("" ::"f"(xr[0].x));  // the record waits for the load
+                tl_put(tl, kTlXLoaded);
             }
         }
         float inv_rms = 1.0f;
@@ -400,6 +427,7 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
             }
             consumer_sync();
             inv_rms = xa.red[0];
+            if (ctid == 0) tl_put(tl, kTlReduced);
         } else if constexpr (PRO == kProRmsA8) {
             // inv = 1/sqrt(sum(x^2)/n + eps)  (unified_engine.cpp:499-513)
             float ss = 0.0f;
@@ -423,10 +451,11 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) tot = __fadd_rn(tot, xa.red[w]);
             inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), ga.eps)));
+            if (ctid == 0) tl_put(tl, kTlReduced);
         }
         // one quad (4 consecutive elements) of thread t: A8 codes into the permuted x8 area and,
         // from the lane holding a 32-slice's first quad, its scale and code sums
-        auto quad = [&](int t, const float4* preloaded) {
+        auto quad = [&](int t, const float4* preloaded, const float4* nw_loaded) {
             const bool live = t < nquads;
             const int e0 = t * 4;
             float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -451,13 +480,13 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
                     v[3] = f.w;
                     if constexpr (PRO == kProRmsA8X) {
                         // compiled order: (x * w) * inv
-                        const float4 w = __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
+                        const float4 w = nw_loaded ? *nw_loaded : __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
                         v[0] = __fmul_rn(__fmul_rn(v[0], w.x), inv_rms);
                         v[1] = __fmul_rn(__fmul_rn(v[1], w.y), inv_rms);
                         v[2] = __fmul_rn(__fmul_rn(v[2], w.z), inv_rms);
                         v[3] = __fmul_rn(__fmul_rn(v[3], w.w), inv_rms);
                     } else if constexpr (PRO == kProRmsA8) {
-                        const float4 w = __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
+                        const float4 w = nw_loaded ? *nw_loaded : __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
                         v[0] = __fmul_rn(__fmul_rn(v[0], inv_rms), w.x);
                         v[1] = __fmul_rn(__fmul_rn(v[1], inv_rms), w.y);
                         v[2] = __fmul_rn(__fmul_rn(v[2], inv_rms), w.z);
@@ -528,11 +557,11 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid) {
 #pragma unroll
             for (int k = 0; k < kRegIters; ++k) {
                 if (k * kConsumerThreads >= nquads) break;  // uniform across the CTA
-                quad(k * kConsumerThreads + ctid, &xr[k]);
+                quad(k * kConsumerThreads + ctid, &xr[k], nw_pre ? &nw_pre[k] : nullptr);
             }
         } else {
 #pragma unroll 2
-            for (int base = 0; base < nquads; base += kConsumerThreads) quad(base + ctid, nullptr);
+            for (int base = 0; base < nquads; base += kConsumerThreads) quad(base + ctid, nullptr, nullptr);
         }
         consumer_sync();
     }
@@ -1045,7 +1074,7 @@ template <int FMT, int PRO, int EPI, int NT>
 __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XArea& xa, const XAddr& xad,
                                uint32_t xa_stride, long long u0, long long u1, uint8_t* ring, uint32_t slot_bytes,
                                int S, uint64_t* full, uint64_t* empty, float* s_part, int* s_cnt, int& jg,
-                               float& best_v, int& best_i) {
+                               float& best_v, int& best_i, TlCtx tl = TlCtx{~0u, 0u, 0u}) {
     using T = FmtTraits<FMT>;
     constexpr int NS = T::kStreams;
     constexpr int NSEG = epi_is_silu(EPI) ? 2 : 1;
@@ -1072,6 +1101,10 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
             if (lane == 0) atomicOr(ga.status, kStatusWaitFull);
             jg += n_chunks;
             return;
+        }
+        if (tl.slot != ~0u && threadIdx.x == 0) {
+            if (j == 0) tl_put(tl, kTlFirstFull);
+            if (j == n_chunks - 1) tl_put(tl, kTlLastFull);
         }
         const long long cb = u0 + static_cast<long long>(j) * CU;
         const int n_units_here = static_cast<int>(((cb + CU < u1) ? cb + CU : u1) - cb);
@@ -1380,12 +1413,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
         }
         fence_mbar_init();
     }
+    __shared__ uint32_t s_tl;
+    if (threadIdx.x == 0) s_tl = tl_slot();
     if (IPU > 1)
         for (int i = threadIdx.x; i < S * CU; i += blockDim.x) s_cnt[i] = 0;
     __syncthreads();
     // let a dependent kernel launch now; it touches our outputs only after its own wait
     grid_launch_dependents();
-    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlStart, ga.tl_id);
+    const uint32_t tl = s_tl;
+    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(tl, kTlStart, ga.tl_id);
 
     if (warp == kProducerWarp) {
         if (lane != 0) return;
@@ -1393,27 +1429,40 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
         const uint64_t pol = l2_policy_evict_first();
         int jg = 0;
         produce_chunks<NS, NSEG>(pa, u0, u1, stages, pa.stage_bytes, S, full, empty, jg, ga.status, pol);
-        tl_rec<FMT, PRO, EPI, NT>(kTlProduced, ga.tl_id);
+        tl_rec<FMT, PRO, EPI, NT>(tl, kTlProduced, ga.tl_id);
         drain_ring(full, S, jg, ga.status);
         return;
     }
 
     // ---------------- consumer warps: every warp takes part of every stage ----------------
     const int cw = warp;
+    // RMSNorm weights never depend on the previous kernel: load this thread's quads before the wait
+    float4 nw[kRegIters];
+    const bool nw_pre = pro_is_rms(PRO) && NT == 1 && (ga.K >> 2) <= kRegIters * kConsumerThreads;
+    if (nw_pre) {
+#pragma unroll
+        for (int k = 0; k < kRegIters; ++k) {
+            const int t = k * kConsumerThreads + threadIdx.x;
+            nw[k] = (t < (ga.K >> 2)) ? __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
-    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlWaited, ga.tl_id);
+    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(tl, kTlWaited, ga.tl_id);
     if constexpr (EPI == kEpiArgmax) {
         if (ga.xchg_stamps != nullptr && blockIdx.x == 0 && threadIdx.x == 0)
             ga.xchg_stamps[((*ga.xchg_epoch + 1) & ga.xchg_stamp_mask) * 4] = globaltimer_ns();
     }
+    constexpr uint32_t tl_code = (static_cast<uint32_t>(FMT) << 4) | (static_cast<uint32_t>(PRO) << 8) |
+                                 (static_cast<uint32_t>(EPI) << 12) | (static_cast<uint32_t>(NT) << 16);
     // multi-token: one A8 area per activation row, xa_stride bytes apart
     const uint32_t xa_stride = (NT > 1) ? xarea_layout_bytes(ga.K, ga.gs, false) : 0u;
     if constexpr (NT == 1) {
-        run_prologue<PRO>(ga, xa, threadIdx.x);
+        run_prologue<PRO>(ga, xa, threadIdx.x, nw_pre ? nw : nullptr, TlCtx{tl, tl_code, ga.tl_id});
     } else {
         token_prologue<PRO>(ga, smem + pa.xarea_off, xa_stride);
     }
-    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlPrologue, ga.tl_id);
+    if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(tl, kTlPrologue, ga.tl_id);
 
     XAddr xad;
     xad.x8 = kF32 ? 0u : smem_u32(xa.x8);
@@ -1433,12 +1482,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
                 consume_chunks_x<FMT, PRO, EPI, false>(pa, ga, xa, u0, u1, stages, S, full, empty, jg, best_v, best_i);
         } else
             consume_chunks<FMT, PRO, EPI, NT>(pa, ga, xa, xad, xa_stride, u0, u1, stages, pa.stage_bytes, S, full,
-                                              empty, s_part, s_cnt, jg, best_v, best_i);
+                                              empty, s_part, s_cnt, jg, best_v, best_i, TlCtx{tl, tl_code, ga.tl_id});
     }
-    if (g_tl_buf != nullptr) {
-        if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlConsumed, ga.tl_id);
+    if (tl != ~0u) {
+        if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(tl, kTlConsumed, ga.tl_id);
         consumer_sync();
-        if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(kTlEnd, ga.tl_id);
+        if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(tl, kTlEnd, ga.tl_id);
     }
 
     if constexpr (EPI == kEpiArgmax) {

@@ -80,6 +80,13 @@ static_assert(kBarBytes >= 2 * kMaxStages * 8, "barrier area too small");
 
 inline uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
+// process-wide number of the next streaming-GEMV launch (one counter for every template
+// instantiation), carried into the timeline records
+inline unsigned int next_launch_number() {
+    static std::atomic<unsigned int> n{0};
+    return n.fetch_add(1u, std::memory_order_relaxed);
+}
+
 // process-wide launch policy (asdsl_b200_set_launch_policy)
 struct LaunchPolicy {
     int ctas_per_sm = kCtasPerSm;  // 1 leaves an SM slot free for the next kernel of a chain
@@ -132,7 +139,9 @@ inline PlanSplit plan_split(long long n_units, long long unit_stage, int nseg, i
     const int nq = K / 32;
     if (rows_per_unit == 4 && nq % 32 == 0 && ps.cu * nseg < kConsumerWarps) {
         // split K only when each part keeps >= 2 whole lane iterations (two slices in
-        // flight); short rows are cheaper unsplit than merged through shared memory
+        // flight); short rows are cheaper unsplit than merged through shared memory, even when
+        // the CTA's whole share has fewer units than warps: measured on B200, parts of one lane
+        // iteration for the 3072-row projections (3 x the items) made a decode step 6 % slower
         const int li = nq / 32;
         for (int d = 2; d <= 8 && d <= li; ++d) {
             if (li % d || li / d < 2) continue;
@@ -291,10 +300,7 @@ int launch_stream_gemv(const StreamIn* in, int n_streams, long long n_units, lon
 
     ga.status = device_status_ptr();
     if (!ga.status) return set_error(kEcuda, "cannot resolve the device status word");
-    {
-        static std::atomic<unsigned int> launches{0};
-        ga.tl_id = launches.fetch_add(1u, std::memory_order_relaxed);
-    }
+    ga.tl_id = next_launch_number();
 
     auto kern = k_stream_gemv<FMT, PRO, EPI, NT>;
     {

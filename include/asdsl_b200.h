@@ -60,13 +60,15 @@ int asdsl_b200_set_mma_min_tokens(int n_tokens);
 int asdsl_b200_device_status(unsigned int* status, int clear);
 
 /* Per-CTA timeline of the streaming GEMVs, the counterpart of the reference's ASDSL_ENGINE_PROFILE
- * stage breakdown (asdsl/kernels/native/unified_engine.cpp:74-90, :1675): while
- * buf (device memory, 16-byte aligned, capacity records of 32 bytes) is set, every CTA appends
- * {event | template << 4, launch number, block | SM << 20, pad, %globaltimer ns, pad} records for
- * its start, dependency wait, prologue, consumers' end and producer's last copy (events 1-6).
- * buf = NULL turns it off.  timeline_count gives the records appended (may exceed capacity). */
-int asdsl_b200_timeline_set(void* buf, unsigned int capacity);
-int asdsl_b200_timeline_count(unsigned int* n);
+ * stage breakdown (asdsl/kernels/native/unified_engine.cpp:74-90, :1675).  buf: device memory of
+ * asdsl_b200_timeline_bytes(slots_per_block) bytes, 16-byte aligned: 1024 uint32 per-block slot
+ * counters, then records [1024 blocks][slots_per_block][16 events] of 16 bytes {%globaltimer ns,
+ * event | template << 4 | SM << 24, launch number}.  Every CTA takes its block's next slot and
+ * writes its start (1), dependency wait (2), activation arrival (7), RMSNorm reduction (0),
+ * prologue end (3), first and last chunk landed (8, 9), consumers' end (4: warp 0, 5: all) and the
+ * producer's last copy (6).  buf = NULL turns it off. */
+int asdsl_b200_timeline_set(void* buf, unsigned int slots_per_block);
+size_t asdsl_b200_timeline_bytes(unsigned int slots_per_block);
 
 /* Self-test of the failure detection (no reference counterpart): runs one wait that nothing
  * ever completes -- which 0: an mbarrier of the streaming pipeline, 1: a cross-GPU exchange
