@@ -360,13 +360,27 @@ def case_timeline(reps):
             with Timeline() as tl:
                 eng.replay(max(reps, 1))
                 torch.cuda.synchronize()
+            tl_long = None
+            if numerics == "reference_exact":
+                # the same at 200 cached positions (the cache filled by a forward over a prompt)
+                prompt = np.random.default_rng(7).integers(0, PHI4_MINI["vocab"], size=200).tolist()
+                eng.forward_batch(prompt, 0)
+                eng.set_position(200, prompt[-1])
+                eng.replay(1)
+                torch.cuda.synchronize()
+                with Timeline() as tl_long:
+                    eng.replay(max(reps, 1))
+                    torch.cuda.synchronize()
         finally:
             eng.close()
             del model
             torch.cuda.empty_cache()
-        print(f"decode {numerics}, {max(reps, 1)} graph replays ({len(tl.recs)} records, {tl.dropped} dropped); "
-              "[0..3] = qkv, o, gate_up, down")
+        print(f"decode {numerics}, {max(reps, 1)} graph replays from position 3 ({len(tl.recs)} records, "
+              f"{tl.dropped} dropped); [0..3] = qkv, o, gate_up, down")
         print(format_chain(tl.launches(), period=4))
+        if tl_long is not None:
+            print(f"decode {numerics}, {max(reps, 1)} graph replays from position 201")
+            print(format_chain(tl_long.launches(), period=4))
 
 
 CASES = {name[5:]: fn for name, fn in globals().items() if name.startswith("case_")}

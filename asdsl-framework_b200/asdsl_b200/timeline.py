@@ -25,10 +25,14 @@ from . import _lib
 REC = np.dtype([("t", "<u8"), ("code", "<u4"), ("id", "<u4")])
 # records as read back: the device record plus its block (from its place in the buffer)
 ROW = np.dtype([("t", "<u8"), ("code", "<u4"), ("id", "<u4"), ("block", "<u4")])
-REDUCED, START, WAITED, PROLOGUE, CONSUMED, END, PRODUCED, XLOADED, FIRST_FULL, LAST_FULL = range(10)
+REDUCED, START, WAITED, PROLOGUE, CONSUMED, END, PRODUCED, XLOADED, FIRST_FULL, LAST_FULL, XALL = range(11)
+# k_attention_exact's phases (its records carry template code 15)
+A_ROPE, A_SCORES, A_MAXIMA, A_WEIGHTS, A_SUMS = range(11, 16)
 _EVENTS = {START: "start", WAITED: "waited", PROLOGUE: "prologue", CONSUMED: "consumed", END: "end",
            PRODUCED: "produced", XLOADED: "xloaded", REDUCED: "reduced", FIRST_FULL: "first_full",
-           LAST_FULL: "last_full"}
+           LAST_FULL: "last_full", XALL: "xall", A_ROPE: "rope", A_SCORES: "scores", A_MAXIMA: "maxima",
+           A_WEIGHTS: "weights", A_SUMS: "sums"}
+ATTN_PHASES = ["start", "waited", "rope", "scores", "maxima", "weights", "sums", "end"]
 MAX_BLOCKS, EVENTS = 1024, 16
 
 
@@ -73,6 +77,8 @@ class Timeline:
 
 def kernel_name(code: int) -> str:
     fmt, pro, epi, nt = (code >> 4) & 15, (code >> 8) & 15, (code >> 12) & 15, (code >> 16) & 255  # SM in bits 24+
+    if fmt == 15:
+        return "k_attention_exact"
     return f"k_stream_gemv<{fmt},{pro},{epi},{nt}>"
 
 
@@ -123,12 +129,20 @@ def chain_rows(launches: list[dict]) -> list[dict]:
             "prologue": us("prologue_max", "waited_max") if "prologue_max" in d else None,
             # inside the prologue: activation arrival after the wait, and the RMSNorm reduction
             "x_latency": us("xloaded_max", "waited_max") if "xloaded_max" in d else None,
-            "reduce": us("reduced_max", "xloaded_max") if "reduced_max" in d and "xloaded_max" in d else None,
+            "reduce": us("reduced_max", "xall_max") if "reduced_max" in d and "xall_max" in d else None,
             "end_spread": us("end_max", "end_min"),
             "produced_before_end": us("end_max", "produced_max") if "produced_max" in d else None,
         }
         ctas = d.get("per_cta", {})
         if ctas:
+            xs = [(c["xall"] - c["waited"]) / 1e3 for c in ctas.values() if "xall" in c and "waited" in c]
+            if xs:
+                row["mean_x_all_warps"] = float(np.mean(xs))
+                row["max_x_all_warps"] = float(np.max(xs))
+            qs = [(c["prologue"] - c.get("reduced", c["xall"])) / 1e3 for c in ctas.values()
+                  if "xall" in c and "prologue" in c]
+            if qs:
+                row["mean_quantize"] = float(np.mean(qs))
             last = max(ctas.values(), key=lambda c: c["end"])
             if "prologue" in last and "last_full" in last:
                 row["crit_data_after_prologue"] = (last["last_full"] - last["prologue"]) / 1e3
@@ -140,6 +154,12 @@ def chain_rows(launches: list[dict]) -> list[dict]:
             prod = [(c["produced"] - c["start"]) / 1e3 for c in ctas.values() if "produced" in c]
             if prod:
                 row["mean_producer_issue"] = float(np.mean(prod))
+        if d["kernel"] == "k_attention_exact" and ctas:
+            # mean duration of each phase over the heads' CTAs
+            for a, b in zip(ATTN_PHASES, ATTN_PHASES[1:]):
+                v = [(c[b] - c[a]) / 1e3 for c in ctas.values() if a in c and b in c]
+                if v:
+                    row["phase_" + b] = float(np.mean(v))
         if prev is not None:
             row["start_after_prev_end"] = (d["start_min"] - prev["end_max"]) / 1e3
             row["waited_after_prev_end"] = (d["waited_min"] - prev["end_max"]) / 1e3
@@ -169,11 +189,18 @@ def format_chain(launches: list[dict], period: int | None = None) -> str:
     summ = summarize(rows, period)
     cols = ["launches", "span", "end_after_prev_end", "start_after_prev_end", "waited_after_prev_end", "prologue",
             "x_latency", "reduce", "start_spread", "end_spread", "produced_before_end", "crit_data_after_prologue",
-            "crit_compute_after_data", "crit_start_to_end", "mean_data_after_prologue", "mean_producer_issue"]
+            "crit_compute_after_data", "crit_start_to_end", "mean_data_after_prologue", "mean_producer_issue",
+            "mean_x_all_warps", "max_x_all_warps", "mean_quantize"]
     short = ["launches", "span", "end_after_prev", "start_after_prev", "waited_after_prev", "prologue", "x_latency",
              "reduce", "start_spread", "end_spread", "produced<end", "crit_data", "crit_compute", "crit_span",
-             "mean_data", "prod_issue"]
+             "mean_data", "prod_issue", "x_all_mean", "x_all_max", "quantize"]
     lines = ["kernel                              " + " ".join(f"{c:>12}" for c in short)]
     for kern, f in summ.items():
         lines.append(f"{kern:36}" + " ".join(f"{f.get(c, float('nan')):12.3f}" for c in cols))
+    attn = {k: f for k, f in summ.items() if k.startswith("k_attention_exact")}
+    if attn:
+        ph = ["phase_" + p for p in ATTN_PHASES[1:]]
+        lines.append("attention phases (mean over heads, us): " + " ".join(f"{p[6:]:>9}" for p in ph))
+        for kern, f in attn.items():
+            lines.append(f"{kern:40}" + " ".join(f"{f.get(p, float('nan')):9.3f}" for p in ph))
     return "\n".join(lines)

@@ -1263,13 +1263,27 @@ int exact_tabs_device(ExactTabs* out) {
     if (dev < 0 || dev >= 64) return set_error(kErange, "reference-exact numerics: device ordinal beyond 63");
     std::lock_guard<std::mutex> lk(g_exact_mu);
     if (!g_exact_ready[dev]) {
-        const size_t n = kRcpTabSize + kRsqrtTabSize + T.exp_exc.size();
-        uint32_t* d = nullptr;
-        ASDSL_CUDA(cudaMalloc(&d, 4 * n));
-        std::vector<uint32_t> h(n);
+        // expf exceptions -> open-addressing hash table with at least 4 slots per entry
+        const size_t n_exc = T.exp_exc.size() / 2;
+        int bits = 4;
+        while ((size_t{1} << bits) < 4 * n_exc) ++bits;
+        const size_t slots = size_t{1} << bits;
+        const uint32_t mask = static_cast<uint32_t>(slots - 1);
+        const int shift = 32 - bits;
+        const size_t n = kRcpTabSize + kRsqrtTabSize + 2 * slots;
+        std::vector<uint32_t> h(n, kExpHashEmpty);
         std::memcpy(h.data(), T.rcp, 4 * kRcpTabSize);
         std::memcpy(h.data() + kRcpTabSize, T.rsqrt, 4 * kRsqrtTabSize);
-        std::memcpy(h.data() + kRcpTabSize + kRsqrtTabSize, T.exp_exc.data(), 4 * T.exp_exc.size());
+        uint32_t* hash = h.data() + kRcpTabSize + kRsqrtTabSize;
+        for (size_t e = 0; e < n_exc; ++e) {
+            const uint32_t key = T.exp_exc[2 * e];
+            uint32_t i = exp_hash_slot(key, shift);
+            while (hash[2 * i] != kExpHashEmpty) i = (i + 1u) & mask;
+            hash[2 * i] = key;
+            hash[2 * i + 1] = T.exp_exc[2 * e + 1];
+        }
+        uint32_t* d = nullptr;
+        ASDSL_CUDA(cudaMalloc(&d, 4 * n));
         const cudaError_t ec = cudaMemcpy(d, h.data(), 4 * n, cudaMemcpyHostToDevice);
         if (ec != cudaSuccess) {
             cudaFree(d);
@@ -1277,8 +1291,11 @@ int exact_tabs_device(ExactTabs* out) {
         }
         g_exact_dev[dev].rcp = d;
         g_exact_dev[dev].rsqrt = d + kRcpTabSize;
-        g_exact_dev[dev].exp_exc = d + kRcpTabSize + kRsqrtTabSize;
-        g_exact_dev[dev].n_exp_exc = static_cast<int>(T.exp_exc.size() / 2);
+        // 8-byte aligned: the rcp and rsqrt tables are 16 KB
+        g_exact_dev[dev].exp_hash = reinterpret_cast<const uint2*>(d + kRcpTabSize + kRsqrtTabSize);
+        g_exact_dev[dev].exp_hash_mask = mask;
+        g_exact_dev[dev].exp_hash_shift = shift;
+        g_exact_dev[dev].n_exp_exc = static_cast<int>(n_exc);
         g_exact_ready[dev] = true;
     }
     *out = g_exact_dev[dev];

@@ -24,6 +24,7 @@
 
 #include "engine_ops.cuh"
 #include "exact_math.cuh"
+#include "gemv_stream.cuh"  // the optional per-CTA timeline (tl_slot / tl_put)
 
 namespace asdsl {
 
@@ -79,6 +80,12 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
     float* ksc_s = reinterpret_cast<float*>(dsm + L.ksc);
     float* vsc_s = reinterpret_cast<float*>(dsm + L.vsc);
 
+    // optional timeline records (template code 15 = this kernel; phases 11..15 below)
+    __shared__ uint32_t s_tl;
+    if (tid == 0) s_tl = tl_slot();
+    __syncthreads();
+    const TlCtx tlc{s_tl, 15u << 4, 0xFFFF0000u};
+    if (tid == 0) tl_put(tlc, kTlStart);
     // the position is final here: the embedding kernel of this step ran to completion first
     const int pos = a.st->pos;
     const bool ok = pos >= 0 && pos < a.max_seq && pos < kAttnXMaxSeq;
@@ -102,6 +109,7 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
     }
     grid_dependency_wait();
     grid_launch_dependents();
+    if (tid == 0) tl_put(tlc, kTlWaited);
     if (!ok) return;
     const int q_dim = a.n_heads * hd, kv_dim = a.n_kv * hd;
 
@@ -148,6 +156,16 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
         qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
         k_s[tid] = __fmul_rn(static_cast<float>(qk), ksc);
         v_s[tid] = __fmul_rn(static_cast<float>(qv), vsc);
+        if (pos < kAttnXPrefetch) {
+            // this position's codes and scales join the staged rows: code * scale there is the
+            // same product as k_s / v_s, so the loops below need no case for it
+            kc_s[pos * kAttnXRow + tid] = static_cast<int8_t>(qk);
+            vc_s[pos * hd + tid] = static_cast<int8_t>(qv);
+            if ((tid & 63) == 0) {
+                ksc_s[2 * pos + b] = ksc;
+                vsc_s[2 * pos + b] = vsc;
+            }
+        }
         if (h % groups == 0) {
             const long long kb = (static_cast<long long>(pos) * a.n_kv + g) * hd;
             a.kq[kb + tid] = static_cast<int8_t>(qk);
@@ -160,14 +178,41 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
         }
     }
     __syncthreads();
+    if (tid == 0) tl_put(tlc, kTlAttnRope);
 
-    // ---- scores: one thread per position ----
-    for (int p = tid; p <= pos; p += kAttnXThreads) {
+    // ---- scores ----
+    // short caches (every row staged, one pass): 8 threads per position, thread l running dot
+    // lane l of both 64-dim blocks (the FMA chains below), folded by shuffles in the same order;
+    // longer ones: one thread per position, its eight lanes in registers
+    constexpr int kScoreGroupMaxPos = kAttnXThreads / 8 - 1;
+    if (pos <= kScoreGroupMaxPos) {
+        const int l = tid & 7;
+        const unsigned m = 0xFFu << (tid & 24);  // this group of 8 lanes (one position)
+        for (int p = tid >> 3; p <= pos; p += kAttnXThreads / 8) {
+            const float sc0 = ksc_s[2 * p], sc1 = ksc_s[2 * p + 1];
+            const int8_t* kr = kc_s + p * kAttnXRow + l;
+            float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                acc0 = __fmaf_rn(q_s[i * 8 + l], __fmul_rn(small_int_to_float(kr[i * 8]), sc0), i == 0 ? 0.0f : acc0);
+                acc1 = __fmaf_rn(q_s[64 + i * 8 + l], __fmul_rn(small_int_to_float(kr[64 + i * 8]), sc1),
+                                 i == 0 ? 0.0f : acc1);
+            }
+            float a0 = __fadd_rn(acc0, __shfl_xor_sync(m, acc0, 4));  // l < 4: v_l + v_{l+4}
+            float a1 = __fadd_rn(acc1, __shfl_xor_sync(m, acc1, 4));
+            a0 = __fadd_rn(a0, __shfl_xor_sync(m, a0, 1));  // (a0 + a1), (a2 + a3)
+            a1 = __fadd_rn(a1, __shfl_xor_sync(m, a1, 1));
+            a0 = __fadd_rn(a0, __shfl_xor_sync(m, a0, 2));  // (a0 + a1) + (a2 + a3)
+            a1 = __fadd_rn(a1, __shfl_xor_sync(m, a1, 2));
+            if (l == 0) s_s[p] = __fmul_rn(__fadd_rn(__fadd_rn(0.0f, a0), a1), inv_sqrt_d);
+        }
+    }
+    for (int p = (pos <= kScoreGroupMaxPos) ? pos + 1 : tid; p <= pos; p += kAttnXThreads) {
         float dot = 0.0f;
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
             float ln[8];
-            if (p == pos) {
+            if (p == pos && pos >= kAttnXPrefetch) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -200,6 +245,7 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
         s_s[p] = __fmul_rn(dot, inv_sqrt_d);
     }
     __syncthreads();
+    if (tid == 0) tl_put(tlc, kTlAttnScores);
 
     // ---- tile maxima (one warp per tile), then the running maxima and old scales in order ----
     const int nt = (pos + kAttnXTile) / kAttnXTile;  // tiles covering positions 0..pos
@@ -241,15 +287,47 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
         }
     }
     __syncthreads();
+    if (tid == 0) tl_put(tlc, kTlAttnMaxima);
     // ---- weights of every position ----
     for (int p = tid; p <= pos; p += kAttnXThreads)
         w_s[p] = exact_expf(__fsub_rn(s_s[p], tile_s[4 * (p / kAttnXTile)]), ex);
     __syncthreads();
+    if (tid == 0) tl_put(tlc, kTlAttnWeights);
     // ---- every tile's tile_l and tile_num (thread per (tile, dim)), in position order ----
     for (int i = tid; i < nt * hd; i += kAttnXThreads) {
         const int t = i / hd, d = i % hd;
         const int tk = t * kAttnXTile, span = min(kAttnXTile, pos + 1 - tk);
         float tl = 0.0f, tn = 0.0f;
+        if (tk + span <= kAttnXPrefetch) {
+            // every position of the tile is staged: one uniform loop whose loads run ahead of
+            // the two sequential sums
+            const int8_t* vr = vc_s + tk * hd + d;
+            const float* sr = vsc_s + 2 * tk + (d >> 6);
+            const float* wr = w_s + tk;
+            int pp = 0;
+            for (; pp + 8 <= span; pp += 8) {
+                // eight positions' operands first, then the two sums in position order
+                float wv[8], vv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    wv[u] = wr[pp + u];
+                    vv[u] = __fmul_rn(small_int_to_float(vr[(pp + u) * hd]), sr[2 * (pp + u)]);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    tl = __fadd_rn(tl, wv[u]);
+                    tn = __fmaf_rn(wv[u], vv[u], tn);
+                }
+            }
+            for (; pp < span; ++pp) {
+                const float wp = wr[pp];
+                tl = __fadd_rn(tl, wp);
+                tn = __fmaf_rn(wp, __fmul_rn(small_int_to_float(vr[pp * hd]), sr[2 * pp]), tn);
+            }
+            tn_s[t * hd + d] = tn;
+            if (d == 0) tile_s[4 * t + 2] = tl;
+            continue;
+        }
         for (int pp = 0; pp < span; ++pp) {
             const int p = tk + pp;
             const float wp = w_s[p];
@@ -269,6 +347,7 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
         if (d == 0) tile_s[4 * t + 2] = tl;
     }
     __syncthreads();
+    if (tid == 0) tl_put(tlc, kTlAttnSums);
     // ---- merge the tiles in order ----
     if (tid < hd) {
         float l = 0.0f, num = 0.0f;
@@ -279,6 +358,7 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
         }
         a.out[h * hd + tid] = __fmul_rn(num, __fdiv_rn(1.0f, l));
     }
+    if (tid == 0) tl_put(tlc, kTlEnd);
 }
 
 // ---------------------------------------------------------------------------
@@ -523,12 +603,27 @@ __global__ void __launch_bounds__(kAttnXThreads)
             const int tt = i / hd, d = i % hd;
             const int tk = tt * kAttnXTile, span = min(kAttnXTile, p1 - p0 - tk);
             float tl = 0.0f, tn = 0.0f;
-            for (int pp = 0; pp < span; ++pp) {
+            int pp = 0;
+            for (; pp + 8 <= span; pp += 8) {
+                // eight positions' operands first, then the two sums in position order
+                float wv[8], vv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int q = tk + pp + u;
+                    wv[u] = w_s[q];
+                    vv[u] = __fmul_rn(small_int_to_float(vc_s[q * hd + d]), vsc_s[2 * q + (d >> 6)]);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    tl = __fadd_rn(tl, wv[u]);
+                    tn = __fmaf_rn(wv[u], vv[u], tn);
+                }
+            }
+            for (; pp < span; ++pp) {
                 const int q = tk + pp;
                 const float wp = w_s[q];
                 tl = __fadd_rn(tl, wp);
-                const float vf = __fmul_rn(static_cast<float>(vc_s[q * hd + d]), vsc_s[2 * q + (d >> 6)]);
-                tn = __fmaf_rn(wp, vf, tn);
+                tn = __fmaf_rn(wp, __fmul_rn(small_int_to_float(vc_s[q * hd + d]), vsc_s[2 * q + (d >> 6)]), tn);
             }
             float* r = tres + static_cast<long long>(t0 + tt) * kAttnXResStride;
             r[4 + d] = tn;

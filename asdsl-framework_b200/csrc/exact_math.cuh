@@ -31,9 +31,19 @@ constexpr int kRsqrtTabSize = 2048;  // RSQRTSS: exponent parity x top 10 mantis
 struct ExactTabs {
     const uint32_t* rcp;      // [2048] RCPSS output bits for inputs 1 + i/2048 (exponent 127)
     const uint32_t* rsqrt;    // [2048] RSQRTSS output bits: [0,1024) inputs in [1,2), [1024,2048) in [2,4)
-    const uint32_t* exp_exc;  // [2 * n_exp_exc] (input bits, libm expf output bits), input bits ascending
-    int n_exp_exc;
+    // the expf exceptions as an open-addressing hash table: slots of (input bits, libm expf
+    // output bits), empty slots keyed kExpHashEmpty, linear probing from exp_hash_slot(key)
+    const uint2* exp_hash;
+    uint32_t exp_hash_mask;   // slots - 1 (a power of two)
+    int exp_hash_shift;       // 32 - log2(slots)
+    int n_exp_exc;            // exceptions listed
 };
+
+constexpr uint32_t kExpHashEmpty = 0xFFFFFFFFu;  // a NaN pattern: never an input of the attention's expf
+
+__host__ __device__ __forceinline__ uint32_t exp_hash_slot(uint32_t key, int shift) {
+    return (key * 0x9E3779B1u) >> shift;  // multiplicative hashing spreads runs of adjacent keys
+}
 
 // RCPSS on a positive or negative normal input: the table entry of its mantissa, its exponent
 // moved by the input's; results below the normal range are flushed to a signed zero (as the
@@ -103,20 +113,20 @@ __device__ __forceinline__ float exact_expf(float x, const ExactTabs& t) {
         const double fd = static_cast<double>(f);
         const double up = static_cast<double>(__uint_as_float(__float_as_uint(f) + 1u));
         const double dn = static_cast<double>(__uint_as_float(__float_as_uint(f) - 1u));
-        // distance to the nearer rounding midpoint, in units of the spacing on that side
-        const double dup = ((fd + up) * 0.5 - y) / (up - fd);
-        const double ddn = (y - (fd + dn) * 0.5) / (fd - dn);
-        hard = (dup < 0.01) || (ddn < 0.01);
+        // within 1/100 of the spacing of a rounding midpoint on either side (the spacings are
+        // positive: compared by multiplication, no double division)
+        hard = (((fd + up) * 0.5 - y) < 0.01 * (up - fd)) || ((y - (fd + dn) * 0.5) < 0.01 * (fd - dn));
     }
     if (hard) {
+        // the table is at most a quarter full, so a probe run ends at an empty slot within a slot
+        // or two (one cache line); the loop bound only guards a malformed table
         const uint32_t key = __float_as_uint(x);
-        int lo = 0, hi = t.n_exp_exc - 1;
-        while (lo <= hi) {
-            const int mid = (lo + hi) >> 1;
-            const uint32_t k = __ldg(t.exp_exc + 2 * mid);
-            if (k == key) return __uint_as_float(__ldg(t.exp_exc + 2 * mid + 1));
-            if (k < key) lo = mid + 1;
-            else hi = mid - 1;
+        uint32_t i = exp_hash_slot(key, t.exp_hash_shift);
+        for (uint32_t probe = 0; probe <= t.exp_hash_mask; ++probe) {
+            const uint2 e = __ldg(t.exp_hash + i);
+            if (e.x == key) return __uint_as_float(e.y);
+            if (e.x == kExpHashEmpty) break;
+            i = (i + 1u) & t.exp_hash_mask;
         }
     }
     return f;

@@ -195,6 +195,13 @@ enum TlEvent : uint32_t {
     kTlXLoaded = 7,   // thread 0's first activation values arrived (prologue)
     kTlFirstFull = 8, // consumer thread 0 past the full barrier of the CTA's first chunk
     kTlLastFull = 9,  // ... and of its last chunk (all of the CTA's weights landed)
+    kTlXAll = 10,     // the latest consumer warp's first activation values arrived (prologue)
+    // k_attention_exact (template code 15): RoPE + KV quantization, scores, maxima, weights, tile sums
+    kTlAttnRope = 11,
+    kTlAttnScores = 12,
+    kTlAttnMaxima = 13,
+    kTlAttnWeights = 14,
+    kTlAttnSums = 15,
 };
 
 // a CTA's timeline slot with its record code and launch number (slot ~0u: off)
@@ -209,12 +216,12 @@ __device__ __forceinline__ uint32_t tl_slot() {
     return k < g_tl_slots ? k : ~0u;
 }
 
-__device__ __forceinline__ void tl_put(const TlCtx& c, uint32_t ev) {
+__device__ __forceinline__ void tl_put(const TlCtx& c, uint32_t ev, unsigned long long t = 0) {
     if (c.slot == ~0u) return;
     uint32_t smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     TlRec r;
-    r.t = globaltimer_ns();
+    r.t = t ? t : globaltimer_ns();
     r.code = ev | c.code | (smid << 24);
     r.id = c.id;
     g_tl_buf[(static_cast<size_t>(blockIdx.x) * g_tl_slots + c.slot) * kTlEvents + ev] = r;
@@ -388,9 +395,17 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid, const float
                 xr[k] = (t < nquads) ? load_x4<kCoherent>(reinterpret_cast<const float4*>(ga.x) + t)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (tl.slot != ~0u && ctid == 0) {
-                asm volatile("" ::"f"(xr[0].x));  // the record waits for the load
-                tl_put(tl, kTlXLoaded);
+            if (tl.slot != ~0u) {
+                // the records wait for the loads: thread 0's arrival, and the latest warp's
+                __shared__ unsigned long long s_xall;
+                if (ctid == 0) s_xall = 0ull;
+                consumer_sync();
+                asm volatile("" ::"f"(xr[0].x), "f"(xr[1].x), "f"(xr[2].x), "f"(xr[3].x));
+                const unsigned long long tx = globaltimer_ns();
+                if (ctid == 0) tl_put(tl, kTlXLoaded, tx);
+                if ((ctid & 31) == 0) atomicMax(&s_xall, tx);
+                consumer_sync();
+                if (ctid == 0) tl_put(tl, kTlXAll, s_xall);
             }
         }
         float inv_rms = 1.0f;
@@ -1235,6 +1250,14 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
             } else {
                 const int q0 = (P == 1) ? 0 : pa.q_bounds[part];
                 const int q1 = (P == 1) ? nq : pa.q_bounds[part + 1];
+                // the residual row is read before the band math (only this unit writes it), so
+                // its L2 round trip overlaps the math; every part of a split reads it, the one
+                // that finishes the unit uses it
+                float res = 0.0f;
+                if constexpr (EPI == kEpiResid) {
+                    const int rrow = static_cast<int>(unit) * 4 + (lane >> 3);
+                    if ((lane & 7) == 0 && rrow < M) res = __ldcg(ga.resid + rrow);
+                }
                 float a[4];
                 // 32-bit offsets: a stage is far below 4 GB
                 const uint32_t p0 = (seg == 0 ? ub[0][0] : ub[NSEG - 1][0]) +
@@ -1279,8 +1302,9 @@ __device__ void consume_chunks(const PipeArgs& pa, const GemvArgs& ga, const XAr
                     if constexpr (EPI == kEpiStore) {
                         ga.y[row] = vrow[0];
                     } else if constexpr (EPI == kEpiResid) {
-                        // L2 read: in a persistent kernel other CTAs wrote neighbouring rows of this line
-                        ga.resid[row] = __fadd_rn(vrow[0], __ldcg(ga.resid + row));
+                        // L2 read (res, above): in a persistent kernel other CTAs wrote neighbouring
+                        // rows of this line
+                        ga.resid[row] = __fadd_rn(vrow[0], res);
                     } else if constexpr (EPI == kEpiSilu) {
                         ga.h[row] = ref_silu_mul(vrow[0], vrow[NSEG - 1]);
 
@@ -1348,8 +1372,13 @@ __device__ void consume_chunks_x(const PipeArgs& pa, const GemvArgs& ga, const X
             const int un = it >> 1, half = it & 1;
             const long long o0 = static_cast<long long>(un) * pa.s[0].unit_bytes;
             const long long o1 = static_cast<long long>(un) * pa.s[1].unit_bytes;
-            const float v = rows_exact<LPT, kInter>(ub[0][0] + o0, ub[0][1] + o1, K, x8, xz, lane, half);
             const int row = static_cast<int>(cb + un) * (4 * LPT) + half * (2 * LPT) + lane / TPR;
+            // the residual row is read before the row math (only this item writes it), so its
+            // L2 round trip overlaps the math instead of following it
+            float res = 0.0f;
+            if constexpr (EPI == kEpiResid)
+                if (writer && row < M) res = __ldcg(ga.resid + row);
+            const float v = rows_exact<LPT, kInter>(ub[0][0] + o0, ub[0][1] + o1, K, x8, xz, lane, half);
             if constexpr (EPI == kEpiSiluX) {
                 const float u =
                     rows_exact<LPT, kInter>(ub[NSEG - 1][0] + o0, ub[NSEG - 1][1] + o1, K, x8, xz, lane, half);
@@ -1358,7 +1387,7 @@ __device__ void consume_chunks_x(const PipeArgs& pa, const GemvArgs& ga, const X
                 if constexpr (EPI == kEpiStore) {
                     ga.y[row] = v;
                 } else if constexpr (EPI == kEpiResid) {
-                    ga.resid[row] = __fadd_rn(v, __ldcg(ga.resid + row));
+                    ga.resid[row] = __fadd_rn(v, res);
                 } else if constexpr (EPI == kEpiArgmax) {
                     if (ga.y) ga.y[row] = v;
                     argmax_take(best_v, best_i, v, ga.row_base + row);
