@@ -18,7 +18,10 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libasdsl_b200.so")
+# ASDSL_B200_TIMELINE=1 loads the timeline build (per-CTA records compiled into the kernels)
+TIMELINE_LIB_PATH = os.path.join(_HERE, "libasdsl_b200_timeline.so")
+LIB_PATH = (TIMELINE_LIB_PATH if os.environ.get("ASDSL_B200_TIMELINE", "0") not in ("", "0")
+            else os.path.join(_HERE, "libasdsl_b200.so"))
 
 OK, EINVAL, ERANGE, ECUDA, ENCCL, ETIMEOUT, ENOMEM = range(7)
 

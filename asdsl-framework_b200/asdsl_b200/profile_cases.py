@@ -20,8 +20,8 @@ Cases (kernels they launch):
   exact_gemv       k_stream_gemv<preq2 exact> (RMSNorm + A8 prologue), 16384x3072, the gate_up
                    + SiLU form (8192 pairs), then 5120x3072 (qkv) and 3072x3072 (o) without RMSNorm
   q2               k_gemv_q2<packed> (the QCSD draft bank's 2-bit GEMV), 8192x3072
-  timeline         per-CTA phase timelines (asdsl_b200.timeline) of back-to-back config-0 GEMVs
-                   and of the decode graphs in both numerics modes
+  timeline         per-CTA phase timelines (asdsl_b200.timeline, loads libasdsl_b200_timeline.so) of
+                   back-to-back config-0 GEMVs and of the decode graphs in both numerics modes
   xchg1            k_allreduce_peer and the lm_head argmax exchange with a world of one GPU
                    (the peer stores go to this GPU's own buffers)
 """
@@ -391,7 +391,8 @@ def main():
     ap.add_argument("case", choices=sorted(CASES))
     ap.add_argument("--reps", type=int, default=4)
     a = ap.parse_args()
-    _lib.load()
+    # the timeline case needs the build with the per-CTA records compiled in
+    _lib.load(_lib.TIMELINE_LIB_PATH if a.case == "timeline" else None)
     CASES[a.case](a.reps)
     torch.cuda.synchronize()
     if _lib.device_status(clear=True) != 0:

@@ -11,6 +11,10 @@ its consumers and the producer's last copy.
         ...  # launches (eager or graph replays)
     launches = tl.launches()          # one dict per launch instance, in start order
     print(format_chain(launches))
+
+The records are compiled only into libasdsl_b200_timeline.so (the default library's kernels carry
+no hooks): set ASDSL_B200_TIMELINE=1 before asdsl_b200 loads its library, or load it explicitly
+with ``_lib.load(_lib.TIMELINE_LIB_PATH)``.
 """
 
 from __future__ import annotations

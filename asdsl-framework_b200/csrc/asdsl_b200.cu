@@ -165,6 +165,9 @@ int asdsl_b200_device_status(unsigned int* status, int clear) {
 }
 
 int asdsl_b200_timeline_set(void* buf, unsigned int slots_per_block) {
+    if (!kTimeline && buf != nullptr)
+        return set_error(kEinval, "timeline_set: this library was built without timeline records; load "
+                                  "libasdsl_b200_timeline.so (set ASDSL_B200_TIMELINE=1 before loading asdsl_b200)");
     if (buf != nullptr && (slots_per_block == 0 || (reinterpret_cast<uintptr_t>(buf) & 15u)))
         return set_error(kEinval, "timeline_set: need a 16-byte aligned device buffer and a slot count");
     ASDSL_CUDA(cudaDeviceSynchronize());

@@ -82,9 +82,11 @@ __global__ void __launch_bounds__(kAttnXThreads) k_attention_exact(AttnArgs a, E
 
     // optional timeline records (template code 15 = this kernel; phases 11..15 below)
     __shared__ uint32_t s_tl;
-    if (tid == 0) s_tl = tl_slot();
-    __syncthreads();
-    const TlCtx tlc{s_tl, 15u << 4, 0xFFFF0000u};
+    if constexpr (kTimeline) {
+        if (tid == 0) s_tl = tl_slot();
+        __syncthreads();
+    }
+    const TlCtx tlc{kTimeline ? s_tl : ~0u, 15u << 4, 0xFFFF0000u};
     if (tid == 0) tl_put(tlc, kTlStart);
     // the position is final here: the embedding kernel of this step ran to completion first
     const int pos = a.st->pos;

@@ -175,15 +175,25 @@ struct GemvArgs {
 // launch number} into record [block][slot][event].  The counterpart of the reference's
 // ASDSL_ENGINE_PROFILE breakdown for the per-op chain; off (null buffer) by default.
 // ---------------------------------------------------------------------------
+#ifndef ASDSL_B200_TIMELINE
+#define ASDSL_B200_TIMELINE 0  // the timeline build (libasdsl_b200_timeline.so) defines it as 1
+#endif
+// the records exist only in the timeline build: with them compiled in but switched off, the hot
+// kernels still lost ~3 % (config-1 layer step, B200) to the extra registers and branches
+constexpr bool kTimeline = ASDSL_B200_TIMELINE != 0;
+
 struct TlRec {
     unsigned long long t;
     uint32_t code, id;
 };
 constexpr int kTlEvents = 16;     // record slots per CTA (events 0..9 used)
 constexpr int kTlMaxBlocks = 1024;
-__device__ TlRec* g_tl_buf = nullptr;  // [kTlMaxBlocks][slots][kTlEvents]
-__device__ uint32_t* g_tl_cnt = nullptr;  // [kTlMaxBlocks] slots taken per block
-__device__ uint32_t g_tl_slots = 0;
+// constant memory: every CTA reads these at its start, before its first barrier; the per-SM
+// constant cache keeps that read off the memory system once a kernel has run (a global variable
+// cost every CTA an L2 round trip before its producer could start streaming)
+__constant__ TlRec* g_tl_buf;     // [kTlMaxBlocks][slots][kTlEvents], null = off
+__constant__ uint32_t* g_tl_cnt;  // [kTlMaxBlocks] slots taken per block
+__constant__ uint32_t g_tl_slots;
 enum TlEvent : uint32_t {
     kTlReduced = 0,   // RMSNorm prologues: the sum of squares reduced (thread 0)
     kTlStart = 1,     // CTA initialized (barriers set up)
@@ -211,13 +221,13 @@ struct TlCtx {
 
 // the CTA's slot (thread 0, before the CTA's first barrier), or ~0u when off / full
 __device__ __forceinline__ uint32_t tl_slot() {
-    if (g_tl_buf == nullptr || blockIdx.x >= static_cast<unsigned>(kTlMaxBlocks)) return ~0u;
+    if (!kTimeline || g_tl_buf == nullptr || blockIdx.x >= static_cast<unsigned>(kTlMaxBlocks)) return ~0u;
     const uint32_t k = atomicAdd(g_tl_cnt + blockIdx.x, 1u);
     return k < g_tl_slots ? k : ~0u;
 }
 
 __device__ __forceinline__ void tl_put(const TlCtx& c, uint32_t ev, unsigned long long t = 0) {
-    if (c.slot == ~0u) return;
+    if (!kTimeline || c.slot == ~0u) return;
     uint32_t smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     TlRec r;
@@ -1443,13 +1453,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
         fence_mbar_init();
     }
     __shared__ uint32_t s_tl;
-    if (threadIdx.x == 0) s_tl = tl_slot();
+    if constexpr (kTimeline)
+        if (threadIdx.x == 0) s_tl = tl_slot();
     if (IPU > 1)
         for (int i = threadIdx.x; i < S * CU; i += blockDim.x) s_cnt[i] = 0;
     __syncthreads();
     // let a dependent kernel launch now; it touches our outputs only after its own wait
     grid_launch_dependents();
-    const uint32_t tl = s_tl;
+    const uint32_t tl = kTimeline ? s_tl : ~0u;  // a constant outside the timeline build
     if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(tl, kTlStart, ga.tl_id);
 
     if (warp == kProducerWarp) {

@@ -66,7 +66,9 @@ int asdsl_b200_device_status(unsigned int* status, int clear);
  * event | template << 4 | SM << 24, launch number}.  Every CTA takes its block's next slot and
  * writes its start (1), dependency wait (2), activation arrival (7), RMSNorm reduction (0),
  * prologue end (3), first and last chunk landed (8, 9), consumers' end (4: warp 0, 5: all) and the
- * producer's last copy (6).  buf = NULL turns it off. */
+ * producer's last copy (6).  buf = NULL turns it off.  Records exist only in the timeline build,
+ * libasdsl_b200_timeline.so (compiled with ASDSL_B200_TIMELINE=1); the default library keeps
+ * its kernels free of the hooks and returns ASDSL_B200_EINVAL for a non-NULL buf. */
 int asdsl_b200_timeline_set(void* buf, unsigned int slots_per_block);
 size_t asdsl_b200_timeline_bytes(unsigned int slots_per_block);
 

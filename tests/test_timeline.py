@@ -44,32 +44,64 @@ def test_timeline_exports():
         assert name in _lib._SIGS
 
 
+_CHILD = r"""
+import sys
+import torch
+from asdsl_b200 import _lib
+from asdsl_b200.timeline import Timeline
+
+_lib.load(_lib.TIMELINE_LIB_PATH)
+M, K = 4096, 3072
+meta = torch.randint(0, 256, (M * (K // 32) * 4,), dtype=torch.uint8, device="cuda")
+meta.view(torch.float16)[:] = 0.01
+quant = torch.randint(0, 256, ((M // 4) * (K // 32) * 64,), dtype=torch.uint8, device="cuda")
+x = torch.randn(K, device="cuda")
+y = torch.empty(M, device="cuda")
+with Timeline(slots=8) as tl:
+    for _ in range(3):
+        _lib.call("asdsl_b200_gemv_preq2_fused", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), y.data_ptr(),
+                  M, K, 32, None)
+    torch.cuda.synchronize()
+ls = tl.launches()
+assert tl.dropped == 0 and len(ls) == 3, (tl.dropped, len(ls))
+for d in ls:
+    assert d["start_min"] <= d["waited_min"] <= d["prologue_max"] <= d["end_max"]
+    assert d["ctas"] == min(torch.cuda.get_device_properties(0).multi_processor_count, M // 4)
+# off again: no records
+before = tl.buf.clone()
+_lib.call("asdsl_b200_gemv_preq2_fused", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), y.data_ptr(), M, K, 32,
+          None)
+torch.cuda.synchronize()
+assert torch.equal(before, tl.buf)
+print("timeline ok")
+"""
+
+
 @pytest.mark.gpu
 def test_timeline_records_every_cta(native):
+    """The timeline build (libasdsl_b200_timeline.so, in a child process: this process has the
+    default library loaded) records every CTA of three launches, in phase order."""
+    import os
+    import subprocess
+    import sys
+
+    from asdsl_b200.build import build_library
+
+    build_library(timeline=True)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([os.path.join(root, "asdsl-framework_b200"), root, env.get("PYTHONPATH", "")])
+    r = subprocess.run(["timeout", "-k", "10", "300", sys.executable, "-c", _CHILD], cwd=root, env=env,
+                       capture_output=True, text=True)
+    assert r.returncode == 0 and "timeline ok" in r.stdout, (r.stdout + r.stderr)[-3000:]
+
+
+@pytest.mark.gpu
+def test_default_library_has_no_timeline(native):
+    """The default library's kernels carry no timeline hooks: asking it for records is an error."""
     import torch
 
-    from asdsl_b200 import _lib
-    from asdsl_b200.timeline import Timeline
-
-    M, K = 4096, 3072
-    meta = torch.randint(0, 256, (M * (K // 32) * 4,), dtype=torch.uint8, device="cuda")
-    meta.view(torch.float16)[:] = 0.01
-    quant = torch.randint(0, 256, ((M // 4) * (K // 32) * 64,), dtype=torch.uint8, device="cuda")
-    x = torch.randn(K, device="cuda")
-    y = torch.empty(M, device="cuda")
-    with Timeline(slots=8) as tl:
-        for _ in range(3):
-            _lib.call("asdsl_b200_gemv_preq2_fused", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), y.data_ptr(),
-                      M, K, 32, None)
-        torch.cuda.synchronize()
-    ls = tl.launches()
-    assert tl.dropped == 0 and len(ls) == 3
-    for d in ls:
-        assert d["start_min"] <= d["waited_min"] <= d["prologue_max"] <= d["end_max"]
-        assert d["ctas"] == min(torch.cuda.get_device_properties(0).multi_processor_count, M // 4)
-    # off again: no records
-    before = tl.buf.clone()
-    _lib.call("asdsl_b200_gemv_preq2_fused", meta.data_ptr(), quant.data_ptr(), x.data_ptr(), y.data_ptr(), M, K, 32,
-              None)
-    torch.cuda.synchronize()
-    assert torch.equal(before, tl.buf)
+    buf = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError):
+        native.call("asdsl_b200_timeline_set", buf.data_ptr(), 1)
+    native.call("asdsl_b200_timeline_set", None, 0)
