@@ -363,11 +363,8 @@ __device__ __forceinline__ float load_x1(const float* p) {
 // quads of the activation per consumer thread held in registers by the prologue (up to K = 8192)
 constexpr int kRegIters = 4;
 
-// nw_pre: the RMSNorm weights of this thread's quads (k * kConsumerThreads + ctid), already
-// loaded, or null (then they are loaded here)
 template <int PRO, bool kCoherent = false>
-__device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid, const float4* nw_pre = nullptr,
-                             TlCtx tl = TlCtx{~0u, 0u, 0u}) {
+__device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid, TlCtx tl = TlCtx{~0u, 0u, 0u}) {
     const int K = ga.K;
     const int lane = ctid & 31;
 
@@ -480,7 +477,7 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid, const float
         }
         // one quad (4 consecutive elements) of thread t: A8 codes into the permuted x8 area and,
         // from the lane holding a 32-slice's first quad, its scale and code sums
-        auto quad = [&](int t, const float4* preloaded, const float4* nw_loaded) {
+        auto quad = [&](int t, const float4* preloaded) {
             const bool live = t < nquads;
             const int e0 = t * 4;
             float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -505,13 +502,13 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid, const float
                     v[3] = f.w;
                     if constexpr (PRO == kProRmsA8X) {
                         // compiled order: (x * w) * inv
-                        const float4 w = nw_loaded ? *nw_loaded : __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
+                        const float4 w = __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
                         v[0] = __fmul_rn(__fmul_rn(v[0], w.x), inv_rms);
                         v[1] = __fmul_rn(__fmul_rn(v[1], w.y), inv_rms);
                         v[2] = __fmul_rn(__fmul_rn(v[2], w.z), inv_rms);
                         v[3] = __fmul_rn(__fmul_rn(v[3], w.w), inv_rms);
                     } else if constexpr (PRO == kProRmsA8) {
-                        const float4 w = nw_loaded ? *nw_loaded : __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
+                        const float4 w = __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t);
                         v[0] = __fmul_rn(__fmul_rn(v[0], inv_rms), w.x);
                         v[1] = __fmul_rn(__fmul_rn(v[1], inv_rms), w.y);
                         v[2] = __fmul_rn(__fmul_rn(v[2], inv_rms), w.z);
@@ -582,11 +579,11 @@ __device__ void run_prologue(const GemvArgs& ga, XArea xa, int ctid, const float
 #pragma unroll
             for (int k = 0; k < kRegIters; ++k) {
                 if (k * kConsumerThreads >= nquads) break;  // uniform across the CTA
-                quad(k * kConsumerThreads + ctid, &xr[k], nw_pre ? &nw_pre[k] : nullptr);
+                quad(k * kConsumerThreads + ctid, &xr[k]);
             }
         } else {
 #pragma unroll 2
-            for (int base = 0; base < nquads; base += kConsumerThreads) quad(base + ctid, nullptr, nullptr);
+            for (int base = 0; base < nquads; base += kConsumerThreads) quad(base + ctid, nullptr);
         }
         consumer_sync();
     }
@@ -1476,17 +1473,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
 
     // ---------------- consumer warps: every warp takes part of every stage ----------------
     const int cw = warp;
-    // RMSNorm weights never depend on the previous kernel: load this thread's quads before the wait
-    float4 nw[kRegIters];
-    const bool nw_pre = pro_is_rms(PRO) && NT == 1 && (ga.K >> 2) <= kRegIters * kConsumerThreads;
-    if (nw_pre) {
-#pragma unroll
-        for (int k = 0; k < kRegIters; ++k) {
-            const int t = k * kConsumerThreads + threadIdx.x;
-            nw[k] = (t < (ga.K >> 2)) ? __ldg(reinterpret_cast<const float4*>(ga.norm_w) + t)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    }
+    // (loading the RMSNorm weights into registers before the wait was measured: the decode step
+    // got 4 % slower, the registers held across the wait costing more than the load it hid)
     grid_dependency_wait();  // activations / residual written by the previous kernel are visible now
     if (threadIdx.x == 0) tl_rec<FMT, PRO, EPI, NT>(tl, kTlWaited, ga.tl_id);
     if constexpr (EPI == kEpiArgmax) {
@@ -1498,7 +1486,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stream_gemv(const Pipe
     // multi-token: one A8 area per activation row, xa_stride bytes apart
     const uint32_t xa_stride = (NT > 1) ? xarea_layout_bytes(ga.K, ga.gs, false) : 0u;
     if constexpr (NT == 1) {
-        run_prologue<PRO>(ga, xa, threadIdx.x, nw_pre ? nw : nullptr, TlCtx{tl, tl_code, ga.tl_id});
+        run_prologue<PRO>(ga, xa, threadIdx.x, TlCtx{tl, tl_code, ga.tl_id});
     } else {
         token_prologue<PRO>(ga, smem + pa.xarea_off, xa_stride);
     }
