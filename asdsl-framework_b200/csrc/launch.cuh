@@ -339,7 +339,10 @@ inline int exact_lpt_for(long long m_seg, bool pair) {
     const long long nb_seg = (m_seg + 3) / 4;
     // a paired (gate/up) unit is computed by one warp in two passes: rank it by one half's rows
     const long long work_rows = m_seg;
-    int lpt = work_rows >= 28416 ? 8 : (work_rows >= 14208 ? 4 : (work_rows >= 7104 ? 2 : 1));
+    // measured in the config-3 exact decode chain (B200): 3072- and 5120-row matrices run 1.5 %
+    // faster per token with 2 lanes per thread than with 1, the 200064-row lm_head 0.7 % faster
+    // with 4 than with 8; 16384-row matrices are fastest with 4 (back-to-back launches)
+    int lpt = work_rows >= 14208 ? 4 : (work_rows >= 3072 ? 2 : 1);
     static const int forced = [] {
         const char* v = std::getenv("ASDSL_EXACT_LPT");
         const int f = v ? std::atoi(v) : 0;
