@@ -38,6 +38,9 @@ _SIGS = {
     "asdsl_b200_last_error": [],
     "asdsl_b200_device_status": [_P, _I],
     "asdsl_b200_timeline_set": [_P, ctypes.c_uint],
+    "asdsl_b200_layer_create": [_P] * 11 + [_I] * 4 + [_P],
+    "asdsl_b200_layer_forward": [_P, _P, _P],
+    "asdsl_b200_layer_destroy": [_P],
     "asdsl_b200_timeline_bytes": [ctypes.c_uint],
     "asdsl_b200_selftest_bounded_wait": [_I, _P],
     "asdsl_b200_set_launch_policy": [_I, _I],

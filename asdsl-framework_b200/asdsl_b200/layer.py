@@ -9,7 +9,8 @@ the dependent chain a decode step runs:
 
 Weights live in HBM for the object's lifetime; ``step`` enqueues the four
 kernels on torch's current stream (capturable in a CUDA graph), ``forward``
-is the host-buffer call a user makes (x in, outputs out, copies included).
+is the host-buffer call a user makes (x in, outputs out, copies included),
+one native call (asdsl_b200_layer_forward).
 ``build_c1_host`` reproduces the reference's C0.1 weight pipeline for the
 benchmark: gs-32 asymmetric quantization with the clip search, then
 dequantize and requantize to Q4_128 for gate_up/down
@@ -63,9 +64,7 @@ class LayerProjections:
         self.y = self._out_cat[qkv_rows + hidden :]
         self.h = torch.empty(inter, dtype=torch.float32, device=dev)
         self._x = torch.empty(hidden, dtype=torch.float32, device=dev)
-        self._pin_x = torch.empty(hidden, dtype=torch.float32, pin_memory=True)
-        self._pin_out = torch.empty(n_out, dtype=torch.float32, pin_memory=True)
-        self._graph = None  # forward(): H2D + the 4 kernels + D2H, captured on first use
+        self._native = None  # forward(): asdsl_b200_layer handle, created on first use
 
     @property
     def weight_bytes(self) -> int:
@@ -94,28 +93,39 @@ class LayerProjections:
                                                    self.y.data_ptr(), self.H, self.I, s))
         return 4
 
-    def _enqueue_io_step(self):
-        self._x.copy_(self._pin_x, non_blocking=True)
-        self.step(self._x)
-        self._pin_out.copy_(self._out_cat, non_blocking=True)
-
     def forward(self, x_host: np.ndarray) -> dict:
-        """Host buffers in and out: pinned H2D of x, the step, one D2H of the results -- replayed
-        as one CUDA graph (captured on the first call, after one eager run)."""
-        self._pin_x.numpy()[:] = x_host
-        stream = torch.cuda.current_stream()
-        if self._graph is None:
-            self._enqueue_io_step()  # eager: kernel attributes and modules before the capture
-            stream.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                self._enqueue_io_step()
-            self._graph = g
-        self._graph.replay()
-        stream.synchronize()
-        o = self._pin_out.numpy()
+        """Host buffers in and out: x[hidden] in, {"qkv", "o", "y"} out, synchronous.  One native
+        call (asdsl_b200_layer_forward): x into pinned staging, one replay of a CUDA graph holding
+        the H2D copy, the four kernels and the D2H copy on the layer's own stream, then the results
+        out of pinned staging.  The graph is captured on the first call."""
+        import ctypes
+
+        lib = _lib.load()
+        if self._native is None:
+            h = ctypes.c_void_p()
+            ptrs = [t.data_ptr() for t in (self.qkv_meta, self.qkv_quant, self.o_meta, self.o_quant, self.gu_q,
+                                           self.gu_s, self.dn_q, self.dn_s, self._x, self.h, self._out_cat)]
+            _lib.check(lib.asdsl_b200_layer_create(*ptrs, self.H, self.QKV, self.QD, self.I, ctypes.byref(h)),
+                       "layer_create")
+            self._native = h
+        x = np.ascontiguousarray(x_host, dtype=np.float32)
+        if x.size != self.H:
+            raise ValueError(f"forward: x has {x.size} elements, the layer takes {self.H}")
+        out = np.empty(self.QKV + 2 * self.H, dtype=np.float32)
+        _lib.check(lib.asdsl_b200_layer_forward(self._native, x.ctypes.data, out.ctypes.data), "layer_forward")
         n1, n2 = self.QKV, self.QKV + self.H
-        return {"qkv": o[:n1].copy(), "o": o[n1:n2].copy(), "y": o[n2:].copy()}
+        return {"qkv": out[:n1], "o": out[n1:n2], "y": out[n2:]}
+
+    def close(self) -> None:
+        if self._native is not None:
+            _lib.load().asdsl_b200_layer_destroy(self._native)
+            self._native = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def clone(self) -> "LayerProjections":
         """Same weights at new device addresses (L2-rotation copies for benchmarking)."""

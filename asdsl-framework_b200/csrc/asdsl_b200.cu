@@ -1382,5 +1382,164 @@ int asdsl_b200_gateup_silu_exact(const uint8_t* meta, const uint8_t* quant, cons
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// one layer's projection set behind a synchronous host-buffer call (asdsl_b200_layer_*): the
+// H2D copy of x, the four GEMVs and the D2H copy of the three results replay as one CUDA graph
+// on the object's own stream, so a call costs one graph launch and one stream synchronization
+// ---------------------------------------------------------------------------
+struct asdsl_b200_layer {
+    const uint8_t* w[8] = {};  // qkv meta, quant; o meta, quant; gate_up quant, scales; down quant, scales
+    float* x_dev = nullptr;
+    float* h_dev = nullptr;
+    float* out_dev = nullptr;  // [qkv_rows | hidden | hidden]
+    int H = 0, QKV = 0, QD = 0, I = 0;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    float* x_pin = nullptr;
+    float* out_pin = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+namespace {
+// the layer step's host transfers as kernels reading / writing the pinned staging through its
+// mapped address (UVA): in a graph, a copy-engine node of a few KB cost ~10 us each, a kernel ~1 us,
+// and kernels chain with programmatic dependent launch
+__global__ void k_host_in(const float* __restrict__ src, float* __restrict__ dst, int n) {
+    grid_launch_dependents();  // the next GEMV's producer may stream its weights already
+    const int n4 = n >> 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n4) reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+    if (i < (n & 3)) dst[4 * n4 + i] = src[4 * n4 + i];
+}
+
+__global__ void k_host_out(const float* __restrict__ src, float* __restrict__ dst, int n) {
+    grid_dependency_wait();  // the last GEMV's results are complete and visible
+    const int n4 = n >> 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n4) reinterpret_cast<float4*>(dst)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+    if (i < (n & 3)) dst[4 * n4 + i] = __ldcg(src + 4 * n4 + i);
+}
+
+int layer_enqueue(asdsl_b200_layer* L) {
+    {
+        const int n = L->H;
+        k_host_in<<<(n / 4 + 255) / 256 + 1, 256, 0, L->stream>>>(L->x_pin, L->x_dev, n);
+        ASDSL_CUDA(cudaGetLastError());
+    }
+    float* qkv = L->out_dev;
+    float* o = L->out_dev + L->QKV;
+    float* y = L->out_dev + L->QKV + L->H;
+    if (int rc = asdsl_b200_gemv_preq2_fused(L->w[0], L->w[1], L->x_dev, qkv, L->QKV, L->H, 32, L->stream)) return rc;
+    if (int rc = asdsl_b200_gemv_preq2_fused(L->w[2], L->w[3], qkv, o, L->H, L->QD, 32, L->stream)) return rc;
+    if (int rc = asdsl_b200_gateup_silu(ASDSL_B200_FMT_Q4_128_BANDED, L->w[4], L->w[5], o, L->h_dev, L->I, L->H,
+                                        L->stream))
+        return rc;
+    if (int rc = asdsl_b200_gemv_q4_128_banded(L->w[6], L->w[7], L->h_dev, y, L->H, L->I, L->stream)) return rc;
+    {
+        const int n = L->QKV + 2 * L->H;
+        cudaLaunchConfig_t cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3((n / 4 + 255) / 256 + 1);
+        cfg.blockDim = dim3(256);
+        cfg.stream = L->stream;
+        cudaLaunchAttribute attr[1];
+        if (launch_policy().pdl) {
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+        }
+        ASDSL_CUDA(cudaLaunchKernelEx(&cfg, k_host_out, static_cast<const float*>(L->out_dev), L->out_pin, n));
+    }
+    return kOk;
+}
+
+void layer_free(asdsl_b200_layer* L) {
+    if (!L) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(L->device);
+    if (L->exec) cudaGraphExecDestroy(L->exec);
+    if (L->graph) cudaGraphDestroy(L->graph);
+    if (L->stream) {
+        cudaStreamSynchronize(L->stream);
+        cudaStreamDestroy(L->stream);
+    }
+    if (L->x_pin) cudaFreeHost(L->x_pin);
+    if (L->out_pin) cudaFreeHost(L->out_pin);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete L;
+}
+}  // namespace
+
+extern "C" {
+
+int asdsl_b200_layer_create(const uint8_t* qkv_meta, const uint8_t* qkv_quant, const uint8_t* o_meta,
+                            const uint8_t* o_quant, const uint8_t* gu_quant, const uint8_t* gu_scales,
+                            const uint8_t* dn_quant, const uint8_t* dn_scales, float* x_dev, float* h_dev,
+                            float* out_dev, int hidden, int qkv_rows, int q_dim, int inter, asdsl_b200_layer** out) {
+    if (!out) return set_error(kEinval, "layer_create: null handle pointer");
+    *out = nullptr;
+    if (!qkv_meta || !qkv_quant || !o_meta || !o_quant || !gu_quant || !gu_scales || !dn_quant || !dn_scales ||
+        !x_dev || !h_dev || !out_dev)
+        return set_error(kEinval, "layer_create: null pointer");
+    if (hidden <= 0 || qkv_rows <= 0 || q_dim <= 0 || inter <= 0 || q_dim > qkv_rows)
+        return set_error(kEinval, "layer_create: invalid dimensions");
+    auto* L = new asdsl_b200_layer();
+    const uint8_t* w[8] = {qkv_meta, qkv_quant, o_meta, o_quant, gu_quant, gu_scales, dn_quant, dn_scales};
+    for (int i = 0; i < 8; ++i) L->w[i] = w[i];
+    L->x_dev = x_dev;
+    L->h_dev = h_dev;
+    L->out_dev = out_dev;
+    L->H = hidden;
+    L->QKV = qkv_rows;
+    L->QD = q_dim;
+    L->I = inter;
+    auto fail = [&](int rc) {
+        layer_free(L);
+        return rc;
+    };
+    if (cudaGetDevice(&L->device) != cudaSuccess) return fail(set_error(kEcuda, "layer_create: no CUDA device"));
+    if (cudaStreamCreateWithFlags(&L->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMallocHost(&L->x_pin, 4ull * hidden) != cudaSuccess ||
+        cudaMallocHost(&L->out_pin, 4ull * (qkv_rows + 2ll * hidden)) != cudaSuccess)
+        return fail(set_error(kEnomem, "layer_create: stream or pinned staging"));
+    std::memset(L->x_pin, 0, 4ull * hidden);
+    // one eager step (kernel attributes are set on first use, outside any capture), then the graph
+    if (int rc = layer_enqueue(L)) return fail(rc);
+    if (cudaStreamSynchronize(L->stream) != cudaSuccess) return fail(set_error(kEcuda, "layer_create: first step"));
+    if (cudaStreamBeginCapture(L->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return fail(set_error(kEcuda, "layer_create: capture"));
+    const int rc = layer_enqueue(L);
+    const cudaError_t ec = cudaStreamEndCapture(L->stream, &L->graph);
+    if (rc) return fail(rc);
+    if (ec != cudaSuccess || cudaGraphInstantiate(&L->exec, L->graph, 0) != cudaSuccess)
+        return fail(set_error(kEcuda, "layer_create: graph"));
+    *out = L;
+    return kOk;
+}
+
+int asdsl_b200_layer_forward(asdsl_b200_layer* L, const float* x_host, float* out_host) {
+    if (!L || !x_host || !out_host) return set_error(kEinval, "layer_forward: null pointer");
+    int cur = 0;
+    ASDSL_CUDA(cudaGetDevice(&cur));
+    if (cur != L->device) ASDSL_CUDA(cudaSetDevice(L->device));
+    std::memcpy(L->x_pin, x_host, 4ull * L->H);
+    cudaError_t ec = cudaGraphLaunch(L->exec, L->stream);
+    if (ec == cudaSuccess) ec = cudaStreamSynchronize(L->stream);
+    if (cur != L->device) cudaSetDevice(cur);
+    ASDSL_CUDA(ec);
+    std::memcpy(out_host, L->out_pin, 4ull * (L->QKV + 2ll * L->H));
+    return kOk;
+}
+
+int asdsl_b200_layer_destroy(asdsl_b200_layer* L) {
+    layer_free(L);
+    return kOk;
+}
+
+}  // extern "C"
+
 // device-resident decode engine (asdsl_b200_engine_*)
 #include "engine.cuh"

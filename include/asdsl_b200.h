@@ -300,6 +300,26 @@ int asdsl_b200_gateup_silu(int fmt, const uint8_t* w0, const uint8_t* w1, const 
 int asdsl_b200_gemv_multi(int fmt, const uint8_t* w0, const uint8_t* w1, const float* X, float* Y,
                           int out_features, int in_features, int n_tokens, void* stream);
 
+/* One decoder layer's projection set (the config-1 workload) behind a synchronous host-buffer
+ * call: qkv = W_qkv x and o = W_o qkv[:q_dim] (preq2 gs 32), h = SiLU(W_gate o) * (W_up o) and
+ * y = W_down h (banded Q4_128) -- the reference runs these as the projections of
+ * UnifiedEngine::forward_token (asdsl/kernels/native/unified_engine.cpp:1411-1413, :1487-1489,
+ * :1532-1538, :1592-1598), each a call of its native GEMV from the host.
+ * layer_create borrows the device weights and the device buffers x_dev[hidden], h_dev[inter] and
+ * out_dev[qkv_rows + 2 * hidden] (qkv | o | y), which must outlive the handle; it makes its own
+ * stream and pinned staging, runs one step and captures the step as one CUDA graph: a kernel
+ * reading x from the pinned staging (mapped host memory), the four GEMVs, a kernel writing
+ * out_dev to the pinned staging.  layer_forward copies x_host[hidden] in, replays the graph,
+ * waits, and copies the results to out_host[qkv_rows + 2 * hidden]; one call at a time per
+ * handle. */
+typedef struct asdsl_b200_layer asdsl_b200_layer;
+int asdsl_b200_layer_create(const uint8_t* qkv_meta, const uint8_t* qkv_quant, const uint8_t* o_meta,
+                            const uint8_t* o_quant, const uint8_t* gu_quant, const uint8_t* gu_scales,
+                            const uint8_t* dn_quant, const uint8_t* dn_scales, float* x_dev, float* h_dev,
+                            float* out_dev, int hidden, int qkv_rows, int q_dim, int inter, asdsl_b200_layer** out);
+int asdsl_b200_layer_forward(asdsl_b200_layer* layer, const float* x_host, float* out_host);
+int asdsl_b200_layer_destroy(asdsl_b200_layer* layer);
+
 /* Reference-exact GEMVs (see ASDSL_B200_NUMERICS_REFERENCE_EXACT): gemv_preq2_fused_avx2
  * (gemv_preq2_avx2.cpp:301-319) with every row summed as the compiled process_one_row does
  * (:216-253), bit-identical to the reference kernel.  norm_w non-null folds the engine's

@@ -398,11 +398,25 @@ def test_layer_projection_set_matches_oracle(native, oracle):
     """Config-1-shaped layer chain (small seeded weights through the same pipeline) vs the oracle."""
     from asdsl_b200.layer import build_c1_host, from_host, layer_reference
 
+    import torch
+
     cfg = dict(hidden=512, qkv_rows=768, q_dim=512, inter=1024)
     host = build_c1_host(7, cfg)
     L = from_host(host)
-    out = L.forward(host["x"])
     ref = layer_reference(oracle, host)
-    for k in ("qkv", "o", "y"):
-        assert rel_err(out[k], ref[k]) < TOL, k
+    x2 = (np.random.default_rng(3).standard_normal(cfg["hidden"]) * 0.5).astype(np.float32)
+    for rep in range(2):  # the native host-buffer call twice (graph captured on the first)
+        out = L.forward(host["x"])
+        for k in ("qkv", "o", "y"):
+            assert rel_err(out[k], ref[k]) < TOL, k
+        # another input in between: the staging carries nothing over from call to call
+        out2 = L.forward(x2)
+        # the same kernels enqueued from Python on torch's stream give the same bits
+        L.step(torch.from_numpy(x2).cuda())
+        torch.cuda.synchronize()
+        for k, t in (("qkv", L.qkv_out), ("o", L.o_out), ("y", L.y)):
+            assert np.array_equal(out2[k].view(np.uint32), t.cpu().numpy().view(np.uint32)), k
+    with pytest.raises(ValueError):
+        L.forward(np.zeros(3, np.float32))
+    L.close()
     _status_clean(native)
