@@ -41,6 +41,8 @@ _SIGS = {
     "asdsl_b200_layer_create": [_P] * 11 + [_I] * 4 + [_P],
     "asdsl_b200_layer_forward": [_P, _P, _P],
     "asdsl_b200_layer_destroy": [_P],
+    "asdsl_b200_host_to_device": [_P, _P, ctypes.c_longlong, _P],
+    "asdsl_b200_device_to_host": [_P, _P, ctypes.c_longlong, _P],
     "asdsl_b200_timeline_bytes": [ctypes.c_uint],
     "asdsl_b200_selftest_bounded_wait": [_I, _P],
     "asdsl_b200_set_launch_policy": [_I, _I],

@@ -1397,6 +1397,8 @@ struct asdsl_b200_layer {
     cudaStream_t stream = nullptr;
     float* x_pin = nullptr;
     float* out_pin = nullptr;
+    float* x_map = nullptr;    // the staging's device-side (mapped) addresses
+    float* out_map = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
 };
@@ -1421,10 +1423,24 @@ __global__ void k_host_out(const float* __restrict__ src, float* __restrict__ ds
     if (i < (n & 3)) dst[4 * n4 + i] = __ldcg(src + 4 * n4 + i);
 }
 
+// the device-side address of a pinned host buffer (mapped into the device's address space), or
+// an error: pageable or unmapped memory is refused before any kernel could touch it
+int mapped_address(const void* host, const char* fn, void** dev_addr) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, host) != cudaSuccess || at.type != cudaMemoryTypeHost ||
+        at.devicePointer == nullptr) {
+        cudaGetLastError();
+        return set_error(kEinval, std::string(fn) + ": the host buffer must be pinned and mapped (cudaMallocHost "
+                                                    "/ cudaHostAlloc / torch pin_memory)");
+    }
+    *dev_addr = at.devicePointer;
+    return kOk;
+}
+
 int layer_enqueue(asdsl_b200_layer* L) {
     {
         const int n = L->H;
-        k_host_in<<<(n / 4 + 255) / 256 + 1, 256, 0, L->stream>>>(L->x_pin, L->x_dev, n);
+        k_host_in<<<(n / 4 + 255) / 256 + 1, 256, 0, L->stream>>>(L->x_map, L->x_dev, n);
         ASDSL_CUDA(cudaGetLastError());
     }
     float* qkv = L->out_dev;
@@ -1450,7 +1466,7 @@ int layer_enqueue(asdsl_b200_layer* L) {
             cfg.attrs = attr;
             cfg.numAttrs = 1;
         }
-        ASDSL_CUDA(cudaLaunchKernelEx(&cfg, k_host_out, static_cast<const float*>(L->out_dev), L->out_pin, n));
+        ASDSL_CUDA(cudaLaunchKernelEx(&cfg, k_host_out, static_cast<const float*>(L->out_dev), L->out_map, n));
     }
     return kOk;
 }
@@ -1506,6 +1522,14 @@ int asdsl_b200_layer_create(const uint8_t* qkv_meta, const uint8_t* qkv_quant, c
         cudaMallocHost(&L->out_pin, 4ull * (qkv_rows + 2ll * hidden)) != cudaSuccess)
         return fail(set_error(kEnomem, "layer_create: stream or pinned staging"));
     std::memset(L->x_pin, 0, 4ull * hidden);
+    {
+        void* dx = nullptr;
+        void* dout = nullptr;
+        if (int rc = mapped_address(L->x_pin, "layer_create", &dx)) return fail(rc);
+        if (int rc = mapped_address(L->out_pin, "layer_create", &dout)) return fail(rc);
+        L->x_map = static_cast<float*>(dx);
+        L->out_map = static_cast<float*>(dout);
+    }
     // one eager step (kernel attributes are set on first use, outside any capture), then the graph
     if (int rc = layer_enqueue(L)) return fail(rc);
     if (cudaStreamSynchronize(L->stream) != cudaSuccess) return fail(set_error(kEcuda, "layer_create: first step"));
@@ -1536,6 +1560,41 @@ int asdsl_b200_layer_forward(asdsl_b200_layer* L, const float* x_host, float* ou
 
 int asdsl_b200_layer_destroy(asdsl_b200_layer* L) {
     layer_free(L);
+    return kOk;
+}
+
+
+int asdsl_b200_host_to_device(const float* host_pinned, float* dev, long long n, void* stream) {
+    if (!host_pinned || !dev || n < 0 || n > 0x7fffffffLL) return set_error(kEinval, "host_to_device: invalid arguments");
+    if (n == 0) return kOk;
+    void* src = nullptr;
+    if (int rc = mapped_address(host_pinned, "host_to_device", &src)) return rc;
+    const int ni = static_cast<int>(n);
+    k_host_in<<<static_cast<unsigned>((n / 4 + 255) / 256 + 1), 256, 0, as_stream(stream)>>>(
+        static_cast<const float*>(src), dev, ni);
+    ASDSL_CUDA(cudaGetLastError());
+    return kOk;
+}
+
+int asdsl_b200_device_to_host(const float* dev, float* host_pinned, long long n, void* stream) {
+    if (!host_pinned || !dev || n < 0 || n > 0x7fffffffLL) return set_error(kEinval, "device_to_host: invalid arguments");
+    if (n == 0) return kOk;
+    void* dst = nullptr;
+    if (int rc = mapped_address(host_pinned, "device_to_host", &dst)) return rc;
+    const int ni = static_cast<int>(n);
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>((n / 4 + 255) / 256 + 1));
+    cfg.blockDim = dim3(256);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    if (launch_policy().pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    ASDSL_CUDA(cudaLaunchKernelEx(&cfg, k_host_out, dev, static_cast<float*>(dst), ni));
     return kOk;
 }
 

@@ -615,17 +615,34 @@ def c0_bench(world: int, rank: int, steps: int = 320) -> dict:
     e1.record(s)
     e1.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / (reps * n)
-    # e2e: pinned x in, y out, every call
+    # e2e: pinned x in, y out, every call (asdsl_b200_host_to_device / _device_to_host: kernels that
+    # read and write the pinned buffers through their mapped address); each call's three launches
+    # replay as one CUDA graph (one per weight copy), as a host-buffer call would issue them
     hx = torch.from_numpy(x).pin_memory()
     hy = torch.empty(M, dtype=torch.float32).pin_memory()
-    n_e2e = 100
+
+    def call_io(c):
+        _lib.check(lib.asdsl_b200_host_to_device(hx.data_ptr(), xd.data_ptr(), K, s.cuda_stream), "host_to_device")
+        run(c)
+        _lib.check(lib.asdsl_b200_device_to_host(yd.data_ptr(), hy.data_ptr(), M, s.cuda_stream), "device_to_host")
+
+    with torch.cuda.stream(s):
+        call_io(copies[0])
+    s.synchronize()
+    gi = torch.cuda.CUDAGraph()  # one call per weight copy, back to back (as a decode graph chains them)
+    with torch.cuda.graph(gi, stream=s):
+        for c in copies:
+            call_io(c)
+    with torch.cuda.stream(s):
+        gi.replay()
+    s.synchronize()
+    n_rep = max(1, 100 // len(copies))
+    n_e2e = n_rep * len(copies)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(s)
     with torch.cuda.stream(s):
-        for i in range(n_e2e):
-            xd.copy_(hx, non_blocking=True)
-            run(copies[i % len(copies)])
-            hy.copy_(yd, non_blocking=True)
+        for _ in range(n_rep):
+            gi.replay()
     f1.record(s)
     f1.synchronize()
     e2e_us = f0.elapsed_time(f1) * 1e3 / n_e2e

@@ -320,6 +320,15 @@ int asdsl_b200_layer_create(const uint8_t* qkv_meta, const uint8_t* qkv_quant, c
 int asdsl_b200_layer_forward(asdsl_b200_layer* layer, const float* x_host, float* out_host);
 int asdsl_b200_layer_destroy(asdsl_b200_layer* layer);
 
+/* Small host <-> device transfers as kernels (no counterpart in the reference, whose kernels take
+ * host arrays directly): host_pinned must be pinned host memory (cudaMallocHost, cudaHostAlloc,
+ * torch's pin_memory), which the kernel reads or writes through its mapped address.  For a few
+ * KB this costs ~1 us where a copy-engine transfer costs ~10 us; device_to_host launches with
+ * programmatic dependent launch and waits for the previous kernel on the stream.  Stream-ordered;
+ * the host sees device_to_host's data after synchronizing the stream. */
+int asdsl_b200_host_to_device(const float* host_pinned, float* dev, long long n, void* stream);
+int asdsl_b200_device_to_host(const float* dev, float* host_pinned, long long n, void* stream);
+
 /* Reference-exact GEMVs (see ASDSL_B200_NUMERICS_REFERENCE_EXACT): gemv_preq2_fused_avx2
  * (gemv_preq2_avx2.cpp:301-319) with every row summed as the compiled process_one_row does
  * (:216-253), bit-identical to the reference kernel.  norm_w non-null folds the engine's

@@ -420,3 +420,27 @@ def test_layer_projection_set_matches_oracle(native, oracle):
         L.forward(np.zeros(3, np.float32))
     L.close()
     _status_clean(native)
+
+
+def test_zero_copy_transfers(native):
+    """asdsl_b200_host_to_device / _device_to_host: exact round trips through pinned host memory
+    for sizes with and without a 4-float tail, twice in a row; pageable host memory is refused."""
+    import torch
+
+    lib = native.load()
+    s = torch.cuda.Stream()
+    for n in (1, 7, 3072, 11264 + 3):
+        src = torch.from_numpy(np.random.default_rng(n).standard_normal(n).astype(np.float32)).pin_memory()
+        back = torch.zeros(n, dtype=torch.float32).pin_memory()
+        dev = torch.empty(n, dtype=torch.float32, device="cuda")
+        for _ in range(2):
+            native.check(lib.asdsl_b200_host_to_device(src.data_ptr(), dev.data_ptr(), n, s.cuda_stream), "h2d")
+            native.check(lib.asdsl_b200_device_to_host(dev.data_ptr(), back.data_ptr(), n, s.cuda_stream), "d2h")
+            s.synchronize()
+            assert np.array_equal(back.numpy().view(np.uint32), src.numpy().view(np.uint32)), n
+            src.mul_(-1.0)
+    pageable = np.zeros(16, np.float32)
+    dev = torch.empty(16, dtype=torch.float32, device="cuda")
+    with pytest.raises(ValueError):
+        native.call("asdsl_b200_host_to_device", pageable.ctypes.data, dev.data_ptr(), 16, None)
+    _status_clean(native)
