@@ -84,6 +84,22 @@ def test_argument_errors_map_to_reference_exceptions(lib):
         _lib.call("asdsl_b200_gemv_preq2_fused_exact", None, None, None, None, 0.0, None, 16, 64, None)
     with pytest.raises(ValueError, match="positive multiple of 4"):
         _lib.call("asdsl_b200_gateup_silu_exact", 16, 16, 16, None, 0.0, 16, 6, 64, None)
+    # the layer step and the zero-copy transfers: argument checks before any CUDA call
+    import ctypes
+
+    h = ctypes.c_void_p()
+    with pytest.raises(ValueError, match="layer_create: null pointer"):
+        _lib.call("asdsl_b200_layer_create", *([None] * 11), 3072, 5120, 3072, 8192, ctypes.byref(h))
+    with pytest.raises(ValueError, match="layer_create: invalid dimensions"):
+        _lib.call("asdsl_b200_layer_create", *([16] * 11), 3072, 5120, 6144, 8192, ctypes.byref(h))
+    with pytest.raises(ValueError, match="layer_forward: null pointer"):
+        _lib.call("asdsl_b200_layer_forward", None, None, None)
+    assert _lib.call("asdsl_b200_layer_destroy", None) == 0
+    with pytest.raises(ValueError, match="host_to_device: invalid arguments"):
+        _lib.call("asdsl_b200_host_to_device", None, 16, 4, None)
+    with pytest.raises(ValueError, match="device_to_host: invalid arguments"):
+        _lib.call("asdsl_b200_device_to_host", 16, 16, -1, None)
+    assert _lib.call("asdsl_b200_host_to_device", 16, 16, 0, None) == 0
 
 
 def test_python_api_fails_loudly_without_gpu():
