@@ -82,8 +82,9 @@ struct asdsl_b200_engine {
     // pinned host staging
     int* h_stage = nullptr;  // [4]: pos, token, argmax, status
     cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
-    // long-cache variants (max_seq_len > 256): attention split over 256-position chunks; replayed
-    // for steps at positions >= 256, where the host-side position mirror says the cache is long
+    // long-cache variants (max_seq_len > 256): attention split over position chunks (256 fast, 128
+    // reference-exact); replayed for steps at positions >= 256, where the host-side position
+    // mirror says the cache is long
     cudaGraphExec_t g_decode_long = nullptr, g_prefill_long = nullptr;
     bool capture_long = false;
     int host_pos = 0;  // the device position as the host last set and advanced it

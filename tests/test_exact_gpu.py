@@ -229,7 +229,7 @@ def test_engine_exact_config3_greedy_trajectory(native, oracle):
 
 def test_engine_exact_generate_across_long_cache_boundary(native, oracle):
     """generate() across position 256, where the engine switches from the single-CTA attention
-    graph to the split (head x 256-position chunk) one: 300 greedy tokens on a TINY-shaped model
+    graph to the split (head x 128-position chunk) one: 300 greedy tokens on a TINY-shaped model
     with a 512-position cache equal the oracle engine's, and so do the logits at positions 255,
     256 and 299 (teacher-forced on those tokens)."""
     from asdsl_b200.inference.synthetic import TINY, build_model
