@@ -1502,6 +1502,8 @@ int asdsl_b200_layer_create(const uint8_t* qkv_meta, const uint8_t* qkv_quant, c
         return set_error(kEinval, "layer_create: null pointer");
     if (hidden <= 0 || qkv_rows <= 0 || q_dim <= 0 || inter <= 0 || q_dim > qkv_rows)
         return set_error(kEinval, "layer_create: invalid dimensions");
+    if ((reinterpret_cast<uintptr_t>(x_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15u)
+        return set_error(kEinval, "layer_create: x_dev and out_dev must be 16-byte aligned");
     auto* L = new asdsl_b200_layer();
     const uint8_t* w[8] = {qkv_meta, qkv_quant, o_meta, o_quant, gu_quant, gu_scales, dn_quant, dn_scales};
     for (int i = 0; i < 8; ++i) L->w[i] = w[i];
@@ -1569,6 +1571,8 @@ int asdsl_b200_host_to_device(const float* host_pinned, float* dev, long long n,
     if (n == 0) return kOk;
     void* src = nullptr;
     if (int rc = mapped_address(host_pinned, "host_to_device", &src)) return rc;
+    if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dev)) & 15u)
+        return set_error(kEinval, "host_to_device: both buffers must be 16-byte aligned");
     const int ni = static_cast<int>(n);
     k_host_in<<<static_cast<unsigned>((n / 4 + 255) / 256 + 1), 256, 0, as_stream(stream)>>>(
         static_cast<const float*>(src), dev, ni);
@@ -1581,6 +1585,8 @@ int asdsl_b200_device_to_host(const float* dev, float* host_pinned, long long n,
     if (n == 0) return kOk;
     void* dst = nullptr;
     if (int rc = mapped_address(host_pinned, "device_to_host", &dst)) return rc;
+    if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(dev)) & 15u)
+        return set_error(kEinval, "device_to_host: both buffers must be 16-byte aligned");
     const int ni = static_cast<int>(n);
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));

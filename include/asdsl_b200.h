@@ -322,7 +322,8 @@ int asdsl_b200_layer_destroy(asdsl_b200_layer* layer);
 
 /* Small host <-> device transfers as kernels (no counterpart in the reference, whose kernels take
  * host arrays directly): host_pinned must be pinned host memory (cudaMallocHost, cudaHostAlloc,
- * torch's pin_memory), which the kernel reads or writes through its mapped address.  For a few
+ * torch's pin_memory), which the kernel reads or writes through its mapped address; both buffers
+ * 16-byte aligned (others are rejected with ASDSL_B200_EINVAL).  For a few
  * KB this costs ~1 us where a copy-engine transfer costs ~10 us; device_to_host launches with
  * programmatic dependent launch and waits for the previous kernel on the stream.  Stream-ordered;
  * the host sees device_to_host's data after synchronizing the stream. */

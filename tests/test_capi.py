@@ -100,6 +100,8 @@ def test_argument_errors_map_to_reference_exceptions(lib):
     with pytest.raises(ValueError, match="device_to_host: invalid arguments"):
         _lib.call("asdsl_b200_device_to_host", 16, 16, -1, None)
     assert _lib.call("asdsl_b200_host_to_device", 16, 16, 0, None) == 0
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        _lib.call("asdsl_b200_layer_create", *([16] * 8), 20, 16, 16, 3072, 5120, 3072, 8192, ctypes.byref(h))
 
 
 def test_python_api_fails_loudly_without_gpu():

@@ -443,4 +443,8 @@ def test_zero_copy_transfers(native):
     dev = torch.empty(16, dtype=torch.float32, device="cuda")
     with pytest.raises(ValueError):
         native.call("asdsl_b200_host_to_device", pageable.ctypes.data, dev.data_ptr(), 16, None)
+    # a buffer off the 16-byte grid is refused before any launch (the kernels move float4s)
+    pinned = torch.zeros(16, dtype=torch.float32).pin_memory()
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        native.call("asdsl_b200_host_to_device", pinned.data_ptr(), dev.data_ptr() + 4, 8, None)
     _status_clean(native)
