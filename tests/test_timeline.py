@@ -37,6 +37,19 @@ def test_group_launches_replays_and_chain():
     assert s["k_stream_gemv<0,2,1,1>"]["launches"] == 4
 
 
+def test_two_library_builds():
+    """The default library is compiled without the timeline records, the profiling one with them;
+    both from the same single translation unit, for sm_100a."""
+    from asdsl_b200 import build
+
+    d = build._command(build.LIB, False)
+    t = build._command(build.LIB_TIMELINE, False)
+    assert "-DASDSL_B200_TIMELINE=1" not in d and "-DASDSL_B200_TIMELINE=1" in t
+    for cmd, lib in ((d, build.LIB), (t, build.LIB_TIMELINE)):
+        assert "arch=compute_100a,code=sm_100a" in cmd and cmd[cmd.index("-o") + 1] == lib + ".tmp"
+        assert cmd[-1].endswith("asdsl_b200.cu")
+
+
 def test_timeline_exports():
     from asdsl_b200 import _lib
 
